@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 embedding hot path (one JSON line on rank 0).
+
+Default workload: corpus embedding with the all-MiniLM-L6-v2 shape (6 layers,
+hidden 384, 12 heads x 32, FFN 1536, seed-0 random F32 weights run on the
+BF16 tensor-core path), 1024 sequences of uniform length 16..256 with
+[CLS]/[SEP], mean pooling + L2.  A step is one forward over the whole batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload minilm|bert-base|mpnet|qwen3]
+
+N > 1 is launched by torch.distributed.run, one process per GPU: every rank
+embeds its own 1024-sequence shard (weak scaling, no data-path collective);
+`value` is all ranks' sequences / the slowest rank's time.
+
+--impl reference times the reference algorithm on the host cores (the Lisp
+cannot run here, so its CPU restatement in oracle/ stands in, threads = all
+host cores, one sequence per thread as embed.lisp does).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "lisp-embed_b200"))
+
+import numpy as np  # noqa: E402
+
+WORKLOADS = {
+    # name: (shape name, seed, sequences per rank, description)
+    "minilm": ("minilm-l6", 0, 1024, "MiniLM-L6 shape, 1024 seqs len U[16,256], mean pool"),
+    "bert-base": ("bert-base", 1, 8192, "BERT-base shape BF16, 8192 seqs log-U[32,512], CLS"),
+    "mpnet": ("mpnet-base", 2, 4096, "MPNet-base shape, 4096 seqs len U[64,384], mean pool"),
+    "qwen3": ("qwen3-0.6b", 3, 2048, "Qwen3-0.6B shape BF16, 2048 seqs len U[128,512]+EOS, last"),
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="minilm")
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="bounded CPU-baseline sample length")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def algorithmic_flops(shape, offsets):
+    """Encoder FLOPs on true lengths: layers * [2 L (4H^2 + 2HF) + 4 L^2 H]
+    (BERT family); Qwen3: layers * [2 L (qkv+o+3HF) + 2 * 2 L(L+1)/2 * heads*hd]."""
+    lens = np.diff(offsets).astype(np.float64)
+    H, F, Lr = shape.hidden, shape.inter, shape.layers
+    if shape.model_type == "qwen3":
+        hd, nh, kv = shape.head_dim, shape.heads, shape.kv_heads
+        lin = H * (nh * hd + 2 * kv * hd) + nh * hd * H + 3 * H * F
+        return float(Lr * np.sum(2 * lens * lin + 2 * nh * hd * lens * (lens + 1)))
+    return float(Lr * np.sum(2 * lens * (4 * H * H + 2 * H * F) + 4 * lens * lens * H))
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            j = json.load(f)
+        return j, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, \
+            "fallback"
+
+
+def profile_traffic(kind):
+    """DRAM bytes per GEMM launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", f"{kind}.txt")
+    try:
+        with open(path) as f:
+            for ln in f:
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock / throttle reasons during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            with open(self.tmp.name) as f:
+                rows = [ln.strip().split(", ") for ln in f if ln.strip()]
+            os.unlink(self.tmp.name)
+        except OSError:
+            return None
+        rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(model_dir, ids, offsets, seconds):
+    """The oracle (CPU restatement of the reference) on all host cores, one
+    sequence per thread in batches (embed.lisp:88-105); bounded sample."""
+    from oracle import oracle
+    om = oracle.OracleModel(model_dir)
+    threads = os.cpu_count() or 1
+    nseq = len(offsets) - 1
+    done = 0
+    t0 = time.perf_counter()
+    s = 0
+    while True:
+        b = list(range(s, min(nseq, s + threads)))
+        if not b:
+            s = 0
+            continue
+        sub_off = offsets[b[0]:b[-1] + 2] - offsets[b[0]]
+        om.embed_batch(ids[offsets[b[0]]:offsets[b[-1] + 1]], sub_off, threads=threads)
+        done += len(b)
+        s = b[-1] + 1 if b[-1] + 1 < nseq else 0
+        if time.perf_counter() - t0 >= seconds:
+            break
+    el = time.perf_counter() - t0
+    return {"value": done / el, "unit": "embeddings/s", "cores": threads, "kind": "port",
+            "sample": f"{done} of the workload's sequences in {el:.1f} s "
+                      f"({threads} threads, one sequence per thread)"}
+
+
+def run_reference(args, rank):
+    """--impl reference: the oracle port of the reference's CPU path."""
+    if rank != 0:
+        return 0
+    from embedcuda import synth
+    shape_name, seed, nseq, desc = WORKLOADS[args.workload]
+    shape = synth.SHAPES[shape_name]
+    root = os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth")
+    d = synth.build_model_dir(shape, seed, root)
+    ids, offsets = synth.make_inputs(shape_name, nseq, seed)
+    from oracle import oracle
+    om = oracle.OracleModel(d)
+    threads = os.cpu_count() or 1
+    times, counts = [], []
+    pos = 0
+
+    def one_step():
+        nonlocal pos
+        b0 = pos
+        b1 = min(nseq, pos + threads)
+        sub_off = offsets[b0:b1 + 1] - offsets[b0]
+        t = time.perf_counter()
+        om.embed_batch(ids[offsets[b0]:offsets[b1]], sub_off, threads=threads)
+        el = time.perf_counter() - t
+        pos = b1 if b1 < nseq else 0
+        return el, b1 - b0
+
+    for _ in range(args.warmup):
+        one_step()
+    for _ in range(args.steps):
+        el, c = one_step()
+        times.append(el)
+        counts.append(c)
+    tot = sum(times)
+    value = sum(counts) / tot
+    line = {
+        "impl": "reference", "metric": "embeddings/sec", "value": value, "unit": "embeddings/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": shape_name, "description": desc, "sequences_per_step": threads,
+                   "note": "each step embeds `threads` sequences of the workload"},
+        "cpu_baseline": {"value": value, "unit": "embeddings/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x {threads} sequences; SBCL absent, the "
+                                   "C restatement of bert.lisp/llama.lisp stands in"},
+        "e2e": {"value": value, "unit": "embeddings/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    from embedcuda import _lib, model, synth
+    shape_name, seed, nseq, desc = WORKLOADS[args.workload]
+    shape = synth.SHAPES[shape_name]
+    root = os.path.join(os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth"), f"r{rank}")
+    mdir = synth.build_model_dir(shape, seed, root)
+    _lib.init([local_rank])
+    model.load_model(mdir)
+    dim = model.dim()
+    rseed = seed if rank == 0 else seed * 100003 + 7919 * rank
+    ids, offsets = synth.make_inputs(shape_name, nseq, rseed)
+    T = int(offsets[-1])
+    flops_step = algorithmic_flops(shape, offsets)
+
+    d_ids = torch.from_numpy(ids).cuda()
+    d_out = torch.empty((nseq, dim), dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    L = _lib.lib()
+
+    def step_device():
+        model.embed_batch_device(d_ids.data_ptr(), offsets, nseq, d_out.data_ptr(), dim, sptr)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step_device()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    # timed region: K steps, L2 flushed (256 MB write) between them, CUDA
+    # events around each step on the stream the library launches on
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    smi_index = phys[local_rank] if len(phys) > local_rank and phys[local_rank] else local_rank
+    L.ecdbg_profile(1)
+    with ClockSampler(smi_index) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step_device()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    launches = int(L.ecdbg_launches())
+    L.ecdbg_profile(0)
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    prof = {}
+    import ctypes as C
+    for cls in ("gemm", "attention", "rows"):
+        v = [C.c_double(), C.c_double(), C.c_double(), C.c_longlong()]
+        L.ecdbg_profile_read(cls.encode(), *[C.byref(x) for x in v])
+        prof[cls] = {"ms": v[0].value, "flops": v[1].value, "bytes": v[2].value,
+                     "launches": v[3].value}
+    clocks = clk.summary()
+
+    # end to end through the host API (ec_embed_batch): ids from pinned host
+    # memory in, embeddings back to host memory, each step
+    h_ids = torch.from_numpy(ids).pin_memory().numpy()
+    h_out = np.empty((nseq, dim), np.float32)
+    for _ in range(2):
+        model.embed_batch(h_ids, offsets, out=h_out)
+    e2e_s = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.embed_batch(h_ids, offsets, out=h_out)
+        e2e_s += time.perf_counter() - t0
+    nblk = int(np.sum((np.diff(offsets) + 63) // 64))
+    h2d = T * 4 + (nseq + 1) * 4 + nblk * 8
+    d2h = nseq * dim * 4
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_s = float(t[0]), float(t[1])
+        dist.barrier()
+
+    out = None
+    if rank == 0:
+        peaks, src = measured_peaks()
+        g = prof["gemm"]
+        achieved = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else None
+        peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+        traffic = profile_traffic(f"gemm_{args.workload}")
+        value = world * nseq * args.steps / (ms * 1e-3)
+        step_tflops = flops_step * args.steps / (ms * 1e-3) / 1e12
+        out = {
+            "metric": "embeddings/sec", "value": value, "unit": "embeddings/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded ids and N(0,0.02) weights of the named shape)",
+            "config": {"workload": shape_name, "description": desc, "sequences_per_rank": nseq,
+                       "tokens_per_rank": T, "parallelism": f"dp{world} (sequence shards)",
+                       "l2": "flushed (256 MB write) between timed steps",
+                       "precision": "bf16 tensor-core GEMM/attention, fp32 accumulate, "
+                                    "fp32 norms and residual stream"},
+            "e2e": {"value": world * nseq * args.steps / e2e_s, "unit": "embeddings/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "timing": "host wall clock around the synchronous ec_embed_batch call"},
+            "roofline": {"bound": "tensor", "kernel": "gemm_tn_bf16 (all GEMM launches)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved and peak else None,
+                         "traffic": traffic,
+                         "peak_source": f"{src} bf16_tflops_sustained (dense cuBLAS, "
+                                        "seconds-long loop)",
+                         "step_tflops": step_tflops,
+                         "step_frac_of_peak": step_tflops / peak if peak else None},
+            "kernel_classes": prof,
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline(mdir, ids, offsets, args.cpu_seconds)
+        except Exception as e:  # the baseline must not sink the GPU number
+            out["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    _lib.shutdown()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,154 @@
+/* embedcuda.h -- C ABI of libembedcuda.so, the B200 (sm_100a) backend of
+ * lisp-embed's embedding hot path.
+ *
+ * Every entry point takes plain C types (pointers + sizes), returns an int
+ * status (EC_OK or a negative EC_E* code) and never exits the process; the
+ * message of the last failure on the calling thread is ec_last_error().
+ * Host buffers belong to the caller and are only read or written during the
+ * call; device memory belongs to the library.  Calls are serialised by an
+ * internal mutex, so the many sb-thread workers of embed.lisp may call in
+ * concurrently.
+ *
+ * Each declaration cites the reference function it stands in for
+ * (file:line in drvova/lisp-embed).
+ */
+#ifndef EMBEDCUDA_H
+#define EMBEDCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define EC_OK 0
+#define EC_EINVAL (-1)    /* bad argument, shape or dtype                      */
+#define EC_ESTATE (-2)    /* call out of order (no ec_init / no model / index) */
+#define EC_ECUDA (-3)     /* CUDA runtime or driver error                      */
+#define EC_ENOMEM (-4)    /* device allocation failed or over EC_MAX_BYTES     */
+#define EC_ETIMEOUT (-5)  /* a kernel's bounded wait ran out (kernel aborted)  */
+#define EC_ENCCL (-6)     /* NCCL missing or a collective failed               */
+#define EC_EUNSUPPORTED (-7) /* model family / config outside this build      */
+
+/* ---- dtypes of ec_upload_tensor (safetensors "dtype") ----------------------- */
+#define EC_F32 0
+#define EC_BF16 1
+#define EC_F16 2
+
+/* ---- model families returned by ec_load_model (model.lisp:11) -------------- */
+#define EC_FAMILY_BERT 1   /* bert / roberta / distilbert (bert.lisp)        */
+#define EC_FAMILY_MPNET 2  /* mpnet (bert.lisp:322-499)                      */
+#define EC_FAMILY_LLAMA 3  /* llama / qwen2 / qwen3 / mistral (llama.lisp)    */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *ec_last_error(void);
+
+/* Bring up the library on `ndev` CUDA devices listed in `devices` (NULL or
+ * ndev <= 0: the devices named by EC_DEVICES, else every visible device).
+ * Replaces nothing in the reference: it is the GPU context that the Lisp
+ * globals of model.lisp:11-12 and bert.lisp:10-27 stand for. */
+int ec_init(const int *devices, int ndev);
+
+/* Number of devices the library drives (after ec_init). */
+int ec_device_count(void);
+
+/* Release every device buffer, stream and communicator. */
+int ec_shutdown(void);
+
+/* Upload one safetensors tensor with its raw bytes (no host widening) to every
+ * device.  Replaces st:get-tensor (st.lisp:32-86): F32 is kept bit-exact,
+ * BF16 and F16 are widened on the device with st.lisp's rules (BF16 << 16;
+ * F16 exponent 31 -> +-most-positive-single-float, st.lisp:29). */
+int ec_upload_tensor(const char *name, int dtype, const int64_t *shape, int ndim,
+                     const void *data, size_t nbytes);
+
+/* Build the model from the uploaded tensors.  `config_json` is config.json,
+ * `pooling_json` is 1_Pooling/config.json or NULL.  Replaces
+ * model:load-model's dispatch (model.lisp:28-46) plus bert:load-model
+ * (bert.lisp:55-129, 343-389) and llama:load-model (llama.lisp:172-220).
+ * Writes the family (EC_FAMILY_*) and the embedding dimension. */
+int ec_load_model(const char *config_json, const char *pooling_json, int *family,
+                  int *dim);
+
+/* Embedding dimension of the loaded model; replaces model:dim (model.lisp:56-62).
+ * Returns the dimension (> 0) or a negative status. */
+int ec_dim(void);
+
+/* Embed `nseq` token-id sequences.  Sequence s is ids[offsets[s] ..
+ * offsets[s+1]); `out` receives nseq rows of ec_dim() floats at a stride of
+ * `out_stride` floats, L2-normalised, in input order.  Replaces model:embed
+ * (model.lisp:48-54) -> bert::embed-bert (bert.lisp:275-320),
+ * bert::embed-mpnet (:455-499) and llama:embed (llama.lisp:296-344) for a
+ * whole batch, the way embed:run batches chunks (embed.lisp:88-105). */
+int ec_embed_batch(const int32_t *ids, const int64_t *offsets, int nseq, float *out,
+                   int out_stride);
+
+/* Device-resident variant for callers that keep ids and outputs in HBM
+ * (single device only): `d_ids` and `d_out` are device pointers on the
+ * library's device 0; `offsets` stays on the host.  The work is enqueued on
+ * `stream` (a cudaStream_t; NULL = the library's own stream) after the work
+ * already queued there, and the call returns once it has finished.  Same
+ * semantics as ec_embed_batch. */
+int ec_embed_batch_device(const int32_t *d_ids, const int64_t *offsets, int nseq,
+                          float *d_out, int out_stride, void *stream);
+
+/* ---- IVF (ann.lisp, kb.lisp) ------------------------------------------------- */
+
+/* Lloyd k-means over the rows of x (n x d, row-major f32).  The training set
+ * is x[sample[0..nsample)] in that order and centroid c starts as
+ * x[sample[c]] (ann.lisp:83-86), or as init[c] when `init` is not NULL.  Each iteration assigns every training row
+ * to its nearest centroid by inner product (ties -> lowest index,
+ * ann.lisp:69-77) and replaces each non-empty centroid by the mean of its
+ * rows (ann.lisp:107-122).  Rows are sharded across the library's devices and
+ * the per-device sums and counts are combined with an NCCL all-reduce.
+ * `centroids` receives k x d floats.  Replaces ann::kmeans (ann.lisp:79-125). */
+int ec_kmeans(const float *x, int64_t n, int d, const int64_t *sample, int64_t nsample,
+              int k, int iters, const float *init, float *centroids);
+
+/* Assign every row of x to its nearest centroid and build the inverted lists:
+ * counts[k] and lists[n] (row ids grouped by centroid, ascending within each
+ * list).  Replaces ann::assign-all (ann.lisp:127-158). */
+int ec_assign_all(const float *x, int64_t n, int d, const float *centroids, int k,
+                  uint32_t *counts, uint32_t *lists);
+
+/* One assignment pass with explicit centroids: assign[i] = nearest centroid
+ * of x[rows[i]] (rows NULL: row i).  Replaces the assign step of ann::kmeans
+ * (ann.lisp:90-105). */
+int ec_assign(const float *x, int64_t n, int d, const int64_t *rows, int64_t nrows,
+              const float *centroids, int k, int32_t *assign);
+
+/* Keep an index resident on the devices: vectors (n x d), centroids (k x d),
+ * counts[k], lists[n] -- the contents of index.bin and ann.bin.  Replaces
+ * kb::load-index's vector part (kb.lisp:84-129) and kb::load-ann
+ * (kb.lisp:283-314).  k = 0 loads vectors only (flat search). */
+int ec_index_load(const float *x, int64_t n, int d, const float *centroids, int k,
+                  const uint32_t *counts, const uint32_t *lists);
+
+/* IVF search of nq queries (nq x d): the nprobe best centroids by inner
+ * product, exact scan of their lists, top `topk` by score (descending).
+ * ids[nq x topk] / scores[nq x topk]; unused slots get id -1.  Results equal
+ * kb::top-k-ivf (kb.lisp:348-364), ties broken as its stable sorts do. */
+int ec_ivf_search(const float *q, int nq, int nprobe, int topk, int64_t *ids,
+                  float *scores);
+
+/* Exact flat search over all resident vectors; replaces kb::top-k-brute
+ * (kb.lisp:186-200).  Ties -> lower row id first. */
+int ec_flat_search(const float *q, int nq, int topk, int64_t *ids, float *scores);
+
+/* ---- multi-process (one process per GPU) ------------------------------------ */
+
+/* Size of the opaque NCCL unique id (128 bytes). */
+int ec_comm_id_size(void);
+/* Rank 0 creates the id; the caller ships it to the other ranks. */
+int ec_comm_get_id(void *id_out);
+/* Join a `world`-rank communicator as `rank` (after ec_init on one device).
+ * ec_kmeans then all-reduces across processes instead of local devices: each
+ * rank passes its own shard of training rows and the same `init`. */
+int ec_comm_init(int rank, int world, const void *id);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EMBEDCUDA_H */

@@ -1,0 +1,43 @@
+/* embedcuda_debug.h -- kernel-level test hooks of libembedcuda.so.
+ *
+ * Not part of the reference-facing interface (no reference counterpart):
+ * they let the test suite check a single kernel against a PyTorch fp32
+ * reference.  All pointers are device pointers on the library's device 0.
+ */
+#ifndef EMBEDCUDA_DEBUG_H
+#define EMBEDCUDA_DEBUG_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out = epilogue(A[M, K] . W[N, K]^T), A and W bf16 row-major.
+ * epi: 0 bf16 (+bias), 1 bf16 gelu(+bias), 2 f32 (+bias) + resid,
+ *      3 bf16 swiglu over 2 x (bn/2)-column gate/up blocks, 4 f32 (+bias).
+ * bn: tile width (64, 128, 192, 256) or 0 for automatic. */
+int ecdbg_gemm(const void *A, const void *W, int M, int N, int K, const float *bias,
+               const float *resid, void *out, int epi, int bn);
+
+/* Varlen attention over packed bf16 rows qkv[T, ld]; cu[nseq + 1] (device,
+ * int32) token offsets; lens on the host.  out[T, heads * head_dim] bf16. */
+int ecdbg_attention(const void *qkv, int ld, int q_off, int k_off, int v_off, void *out,
+                    const int32_t *cu_dev, const int32_t *lens_host, int nseq, int heads,
+                    int kv_heads, int head_dim, int causal);
+
+/* Per-kernel-class device timing of the embedding forward, for the
+ * benchmark's roofline figures.  ecdbg_profile(1) clears the counters and
+ * brackets every later launch with CUDA events on its stream; (0) stops.
+ * ecdbg_profile_read fills the summed event time (ms), algorithmic FLOPs and
+ * bytes and the launch count of class `cls` ("gemm", "attention", "rows"). */
+int ecdbg_profile(int enable);
+int ecdbg_profile_read(const char *cls, double *ms, double *flops, double *bytes,
+                       long long *launches);
+/* Kernel launches issued by the library since the last ecdbg_profile(1). */
+long long ecdbg_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

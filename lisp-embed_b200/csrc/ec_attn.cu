@@ -1,0 +1,57 @@
+// ec_attn.cu -- instantiations and host launcher of the varlen attention.
+#include <mutex>
+
+#include "ec_attn.cuh"
+#include "ec_kernels.h"
+
+namespace ec {
+
+template <int HD>
+static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
+  static std::mutex mu;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<HD>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(AttnSmem<HD>::BYTES));
+      if (e != cudaSuccess) return e;
+      set[dev] = true;
+    }
+  }
+  AttnArgs a;
+  a.qkv = l.qkv;
+  a.ld = l.ld;
+  a.q_off = l.q_off;
+  a.k_off = l.k_off;
+  a.v_off = l.v_off;
+  a.out = l.out;
+  a.ldo = l.ldo;
+  a.cu = l.cu;
+  a.blocks = l.blocks;
+  a.heads = l.heads;
+  a.kv_group = l.kv_group;
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  a.causal = l.causal;
+  a.relbias = l.relbias;
+  a.rel_max = l.rel_max;
+  dim3 grid(l.nblocks, l.heads);
+  attn_fwd_kernel<HD><<<grid, kAttnThreads, AttnSmem<HD>::BYTES, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
+  if (l.nblocks <= 0) return cudaSuccess;
+  switch (l.head_dim) {
+    case 32: return run_attn<32>(l, st);
+    case 64: return run_attn<64>(l, st);
+    case 128: return run_attn<128>(l, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ec

@@ -1,0 +1,117 @@
+// ec_debug.cu -- kernel-level test hooks (include/embedcuda_debug.h).
+#include <algorithm>
+#include <numeric>
+#include <vector>
+
+#include "../../include/embedcuda_debug.h"
+#include "ec_state.h"
+
+using namespace ec;
+
+extern "C" {
+
+int ecdbg_gemm(const void* A, const void* W, int M, int N, int K, const float* bias,
+               const float* resid, void* out, int epi, int bn) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  GemmLaunch g;
+  g.A = static_cast<const bf16*>(A);
+  g.lda = K;
+  g.W = static_cast<const bf16*>(W);
+  g.ldw = K;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.bias = bias;
+  g.resid = resid;
+  g.ldr = N;
+  g.out = out;
+  g.ldo = epi == 3 ? N / 2 : N;
+  g.epi = epi;
+  g.bn = bn;
+  g.status = d.status;
+  rc = check_cuda(launch_gemm(g, d.stream, d.num_sms), "gemm");
+  if (rc) return rc;
+  return sync_and_check(d, "gemm");
+}
+
+int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, void* out,
+                    const int32_t* cu_dev, const int32_t* lens_host, int nseq, int heads,
+                    int kv_heads, int head_dim, int causal) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  std::vector<int2> blk;
+  std::vector<int> order(nseq);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens_host[a] > lens_host[b]; });
+  for (int s : order)
+    for (int q0 = 0; q0 < lens_host[s]; q0 += 64) blk.push_back(make_int2(s, q0));
+  void* dblk = nullptr;
+  rc = dev_alloc(d, &dblk, blk.size() * 8 + 8, "blocks");
+  if (rc) return rc;
+  rc = check_cuda(cudaMemcpy(dblk, blk.data(), blk.size() * 8, cudaMemcpyHostToDevice), "blocks");
+  AttnLaunch a;
+  a.qkv = static_cast<const bf16*>(qkv);
+  a.ld = ld;
+  a.q_off = q_off;
+  a.k_off = k_off;
+  a.v_off = v_off;
+  a.out = static_cast<bf16*>(out);
+  a.ldo = heads * head_dim;
+  a.cu = cu_dev;
+  a.blocks = static_cast<const int2*>(dblk);
+  a.nblocks = static_cast<int>(blk.size());
+  a.heads = heads;
+  a.kv_group = heads / kv_heads;
+  a.head_dim = head_dim;
+  a.causal = causal;
+  a.relbias = nullptr;
+  a.rel_max = 0;
+  if (!rc) rc = check_cuda(launch_attention(a, d.stream), "attention");
+  if (!rc) rc = sync_and_check(d, "attention");
+  dev_free(d, dblk, blk.size() * 8 + 8);
+  return rc;
+}
+
+int ecdbg_profile(int enable) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (enable) {
+    for (auto& a : G().prof) a = ProfAcc();
+    G().launches = 0;
+    for (Device* d : G().devs) d->pend.clear();
+  }
+  G().profile = enable != 0;
+  return EC_OK;
+}
+
+int ecdbg_profile_read(const char* cls, double* ms, double* flops, double* bytes,
+                       long long* launches) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!cls) return set_error(EC_EINVAL, "class is NULL");
+  const std::string c(cls);
+  const int i = c == "gemm" ? 0 : c == "attention" ? 1 : c == "rows" ? 2 : -1;
+  if (i < 0) return set_error(EC_EINVAL, "unknown class %s", cls);
+  const ProfAcc& a = G().prof[i];
+  if (ms) *ms = a.ms;
+  if (flops) *flops = a.flops;
+  if (bytes) *bytes = a.bytes;
+  if (launches) *launches = a.launches;
+  return EC_OK;
+}
+
+long long ecdbg_launches(void) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  return G().launches;
+}
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// ec_gemm.cuh -- persistent tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = A[M, K] . W[N, K]^T  (+ fused epilogue)
+//
+// A (activations, bf16, row-major, K contiguous) and W (weights, bf16,
+// PyTorch Linear layout [out, in]) are both K-major.  This is the product
+// `linear` computes one token at a time in the reference (bert.lisp:145-153,
+// llama.lisp:97-104); here one launch covers every token of the batch.
+//
+// Structure (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      : TMA producer (one elected lane) -- A tile 128x64 and W tile
+//                 BNx64 per stage, 128-byte swizzle, STAGES-deep ring.
+//   warp 1      : TMEM allocator + UMMA issuer (one elected lane):
+//                 tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN, K=16,
+//                 fp32 accumulators in TMEM, double-buffered (2 x BN columns)
+//                 so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 2..5  : epilogue; warp w owns TMEM lanes 32*(w%4).. (= tile rows),
+//                 reads 32 columns at a time with tcgen05.ld, applies the
+//                 epilogue in fp32 and stores with 16-byte vector stores.
+// All waits are bounded (ec_ptx.cuh); a timeout records a status code,
+// raises the CTA abort flag and every role unwinds, then TMEM is freed.
+#pragma once
+
+#include "ec_ptx.cuh"
+
+namespace ec {
+
+enum GemmEpi : int {
+  kEpiBf16 = 0,        // out bf16 = acc + bias
+  kEpiBf16Gelu = 1,    // out bf16 = gelu(acc + bias)           (bert.lisp:263-264)
+  kEpiF32Resid = 2,    // out f32  = (acc + bias) + resid       (bert.lisp:250-256)
+  kEpiBf16Swiglu = 3,  // out bf16 = silu(gate) * up, N/2 wide  (llama.lisp:284-290)
+  kEpiF32 = 4,         // out f32  = acc + bias
+};
+
+struct GemmArgs {
+  int M, N, K;
+  const float* bias;   // [N] or nullptr
+  const float* resid;  // [M, ldr] fp32 (kEpiF32Resid); may alias out
+  int ldr;
+  void* out;           // bf16 or fp32, row stride ldo elements
+  int ldo;
+  int n_tiles_n;       // N / BN
+  int num_tiles;       // ceil(M / 128) * n_tiles_n
+  unsigned* status;    // device status word
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 192 ? 5 : 6);
+  static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
+  static constexpr uint32_t B_BYTES = BN * kGemmBK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS =
+      2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
+  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+};
+
+// GELU with the erf of Abramowitz-Stegun 7.1.26, the form bert::gelu uses
+// (bert.lisp:176-192).
+__device__ __forceinline__ float gelu_as(float x) {
+  const float z = x * 0.70710678118654752f;
+  const float az = fabsf(z);
+  const float t = 1.0f / (1.0f + 0.3275911f * az);
+  const float poly =
+      t * (0.254829592f +
+           t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
+  float e = 1.0f - poly * __expf(-az * az);
+  e = z < 0.0f ? -e : e;
+  return 0.5f * x * (1.0f + e);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int EPI>
+__device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int col0,
+                                                const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (a.bias) {
+    const float4* b4 = reinterpret_cast<const float4*>(a.bias + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 b = __ldg(b4 + j);
+      v[4 * j] += b.x;
+      v[4 * j + 1] += b.y;
+      v[4 * j + 2] += b.z;
+      v[4 * j + 3] += b.w;
+    }
+  }
+  if (row >= a.M) return;
+  if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu) {
+    uint32_t p[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float x0 = v[2 * j], x1 = v[2 * j + 1];
+      if constexpr (EPI == kEpiBf16Gelu) {
+        x0 = gelu_as(x0);
+        x1 = gelu_as(x1);
+      }
+      p[j] = pack_bf16(x0, x1);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
+                                          static_cast<size_t>(row) * a.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  } else if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                            static_cast<size_t>(row) * a.ldo + col0);
+    if constexpr (EPI == kEpiF32Resid) {
+      const float4* rs =
+          reinterpret_cast<const float4*>(a.resid + static_cast<size_t>(row) * a.ldr + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 q = rs[j];
+        v[4 * j] += q.x;
+        v[4 * j + 1] += q.y;
+        v[4 * j + 2] += q.z;
+        v[4 * j + 3] += q.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tn_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(EPI != kEpiBf16Swiglu || BN % 64 == 0, "swiglu BN");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int k_blocks = args.K / kGemmBK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const uint64_t pol_w = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+        const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            report(args.status, kDevTimeoutProducer);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(smA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * kGemmBK,
+                      mb * kGemmBM);
+          tma_load_2d_hint(smB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * kGemmBK,
+                           nb * BN, pol_w);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          report(args.status, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            report(args.status, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(smB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_f16(d_tmem, desc_sw128_kmajor(a_addr + k * 32),
+                     desc_sw128_kmajor(b_addr + k * 32), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // epilogue warps 2..5
+    const int quad = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+      const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+        report(args.status, kDevTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * kGemmBM + quad * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+      if constexpr (EPI == kEpiBf16Swiglu) {
+        // gate columns [0, BN/2), up columns [BN/2, BN) of this tile
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, g);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, u);
+          tmem_wait_ld();
+          if (row < args.M) {
+            uint32_t p[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float a0 = silu_f(__uint_as_float(g[2 * j])) * __uint_as_float(u[2 * j]);
+              const float a1 =
+                  silu_f(__uint_as_float(g[2 * j + 1])) * __uint_as_float(u[2 * j + 1]);
+              p[j] = pack_bf16(a0, a1);
+            }
+            const int col0 = nb * (BN / 2) + c * 32;
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.out) +
+                                                  static_cast<size_t>(row) * args.ldo + col0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_wait_ld();
+          epi_store_chunk<EPI>(args, row, nb * BN + c * 32, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // let copies and MMAs already in flight land before the CTA exits
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace ec

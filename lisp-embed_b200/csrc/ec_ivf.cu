@@ -1,0 +1,418 @@
+// ec_ivf.cu -- C ABI of the IVF path: k-means (ann::kmeans), assignment
+// (ann::assign-all), resident index, IVF and flat search (kb::top-k-ivf,
+// kb::top-k-brute).  Rows are sharded over the library's devices (or over
+// processes after ec_comm_init); only k-means exchanges data, with one NCCL
+// all-reduce of the centroid sums + counts per Lloyd iteration.
+#include <algorithm>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "ec_comm.h"
+#include "ec_ivf.h"
+#include "ec_state.h"
+
+namespace ec {
+
+#define EC_TRY(expr)              \
+  do {                            \
+    int rc_ = (expr);             \
+    if (rc_ != EC_OK) return rc_; \
+  } while (0)
+
+// scoped device buffer
+struct DBuf {
+  Device* d = nullptr;
+  void* p = nullptr;
+  size_t n = 0;
+  int alloc(Device& dev, size_t bytes, const char* what) {
+    d = &dev;
+    n = bytes;
+    return dev_alloc(dev, &p, bytes, what);
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+  ~DBuf() {
+    if (p) dev_free(*d, p, n);
+  }
+};
+
+// run fn(k) on every device, one host thread each; first error wins
+template <class F>
+static int on_devices(int nd, F fn) {
+  if (nd == 1) return fn(0);
+  std::vector<int> rc(nd, EC_OK);
+  std::vector<std::string> msg(nd);
+  std::vector<std::thread> th;
+  for (int k = 0; k < nd; ++k)
+    th.emplace_back([&, k] {
+      rc[k] = fn(k);
+      if (rc[k]) msg[k] = ec_last_error();
+    });
+  for (auto& t : th) t.join();
+  for (int k = 0; k < nd; ++k)
+    if (rc[k]) return set_error(rc[k], "device %d: %s", G().devs[k]->ordinal, msg[k].c_str());
+  return EC_OK;
+}
+
+static void split(int64_t n, int parts, int k, int64_t* b, int64_t* e) {
+  const int64_t per = (n + parts - 1) / parts;
+  *b = std::min<int64_t>(n, per * k);
+  *e = std::min<int64_t>(n, per * (k + 1));
+}
+
+// ------------------------------------------------------------------ kmeans --
+static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t* sample,
+                         int64_t j0, int64_t j1, int k, int iters, const float* cent0,
+                         float* cent_out, bool reduce) {
+  Device& dv = *G().devs[li];
+  EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
+  const int64_t ns = j1 - j0;
+  // training rows of this shard, in sample order (ann.lisp:99-103)
+  std::vector<float> xs(static_cast<size_t>(std::max<int64_t>(ns, 1)) * d);
+  for (int64_t j = 0; j < ns; ++j)
+    std::memcpy(&xs[static_cast<size_t>(j) * d], x + sample[j0 + j] * d, static_cast<size_t>(d) * 4);
+  (void)n;
+  DBuf bx, bc, ba, bh, bcnt, boffs, bl, bs;
+  const int64_t nt = sort_tiles(ns);
+  EC_TRY(bx.alloc(dv, xs.size() * 4, "kmeans rows"));
+  EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
+  EC_TRY(ba.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "assignments"));
+  EC_TRY(bh.alloc(dv, static_cast<size_t>(std::max<int64_t>(nt, 1)) * k * 4, "sort scratch"));
+  EC_TRY(bcnt.alloc(dv, static_cast<size_t>(k) * 4, "counts"));
+  EC_TRY(boffs.alloc(dv, static_cast<size_t>(k + 1) * 8, "offsets"));
+  EC_TRY(bl.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "lists"));
+  EC_TRY(bs.alloc(dv, static_cast<size_t>(k) * (d + 1) * 4, "sums"));
+  cudaStream_t st = dv.stream;
+  EC_TRY(check_cuda(cudaMemcpyAsync(bx.p, xs.data(), static_cast<size_t>(ns) * d * 4,
+                                    cudaMemcpyHostToDevice, st), "rows upload"));
+  EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent0, static_cast<size_t>(k) * d * 4,
+                                    cudaMemcpyHostToDevice, st), "centroid upload"));
+  for (int it = 0; it < iters; ++it) {
+    EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, ns, bc.as<float>(), k, d,
+                                    ba.as<int32_t>(), st), "assign"));
+    EC_TRY(check_cuda(launch_lists(ba.as<int32_t>(), ns, k, bh.as<uint32_t>(), bcnt.as<uint32_t>(),
+                                   boffs.as<int64_t>(), 0u, bl.as<uint32_t>(), st), "lists"));
+    EC_TRY(check_cuda(launch_segsum(bx.as<float>(), bl.as<uint32_t>(), boffs.as<int64_t>(), k, d,
+                                    bs.as<float>(), st), "sums"));
+    if (reduce)
+      EC_TRY(comm_allreduce_sum_f32(li, bs.as<float>(), static_cast<size_t>(k) * (d + 1), st));
+    EC_TRY(check_cuda(launch_update(bs.as<float>(), k, d, bc.as<float>(), st), "update"));
+  }
+  if (cent_out)
+    EC_TRY(check_cuda(cudaMemcpyAsync(cent_out, bc.p, static_cast<size_t>(k) * d * 4,
+                                      cudaMemcpyDeviceToHost, st), "centroid download"));
+  return sync_and_check(dv, "kmeans");
+}
+
+// ---------------------------------------------------------------- assign --
+static int assign_device(int li, const float* x, int64_t r0, int64_t r1, int d, const int64_t* rows,
+                         const float* cent, int k, int32_t* assign_out, uint32_t* counts_out,
+                         int64_t* offs_out, uint32_t* lists_out) {
+  Device& dv = *G().devs[li];
+  EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
+  const int64_t m = r1 - r0;
+  if (m <= 0) {
+    if (counts_out) std::fill(counts_out, counts_out + k, 0u);
+    if (offs_out) std::fill(offs_out, offs_out + k + 1, 0);
+    return EC_OK;
+  }
+  std::vector<float> xs;
+  const float* src = x + r0 * d;
+  if (rows) {
+    xs.resize(static_cast<size_t>(m) * d);
+    for (int64_t j = 0; j < m; ++j)
+      std::memcpy(&xs[static_cast<size_t>(j) * d], x + rows[r0 + j] * d, static_cast<size_t>(d) * 4);
+    src = xs.data();
+  }
+  DBuf bx, bc, ba;
+  EC_TRY(bx.alloc(dv, static_cast<size_t>(m) * d * 4, "rows"));
+  EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
+  EC_TRY(ba.alloc(dv, static_cast<size_t>(m) * 4, "assignments"));
+  cudaStream_t st = dv.stream;
+  EC_TRY(check_cuda(cudaMemcpyAsync(bx.p, src, static_cast<size_t>(m) * d * 4, cudaMemcpyHostToDevice, st),
+                    "rows upload"));
+  EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice, st),
+                    "centroid upload"));
+  EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, m, bc.as<float>(), k, d, ba.as<int32_t>(), st),
+                    "assign"));
+  if (assign_out)
+    EC_TRY(check_cuda(cudaMemcpyAsync(assign_out + r0, ba.p, static_cast<size_t>(m) * 4,
+                                      cudaMemcpyDeviceToHost, st), "assign download"));
+  if (lists_out) {
+    DBuf bh, bcnt, boffs, bl;
+    const int64_t nt = sort_tiles(m);
+    EC_TRY(bh.alloc(dv, static_cast<size_t>(nt) * k * 4, "sort scratch"));
+    EC_TRY(bcnt.alloc(dv, static_cast<size_t>(k) * 4, "counts"));
+    EC_TRY(boffs.alloc(dv, static_cast<size_t>(k + 1) * 8, "offsets"));
+    EC_TRY(bl.alloc(dv, static_cast<size_t>(m) * 4, "lists"));
+    EC_TRY(check_cuda(launch_lists(ba.as<int32_t>(), m, k, bh.as<uint32_t>(), bcnt.as<uint32_t>(),
+                                   boffs.as<int64_t>(), static_cast<uint32_t>(r0), bl.as<uint32_t>(), st),
+                      "lists"));
+    EC_TRY(check_cuda(cudaMemcpyAsync(counts_out, bcnt.p, static_cast<size_t>(k) * 4,
+                                      cudaMemcpyDeviceToHost, st), "counts download"));
+    EC_TRY(check_cuda(cudaMemcpyAsync(offs_out, boffs.p, static_cast<size_t>(k + 1) * 8,
+                                      cudaMemcpyDeviceToHost, st), "offsets download"));
+    EC_TRY(check_cuda(cudaMemcpyAsync(lists_out, bl.p, static_cast<size_t>(m) * 4,
+                                      cudaMemcpyDeviceToHost, st), "lists download"));
+    return sync_and_check(dv, "assign-all");
+  }
+  return sync_and_check(dv, "assign");
+}
+
+static int check_common(int64_t n, int d, int k) {
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (n < 0 || d <= 0 || d % 4 || d > 8192) return set_error(EC_EINVAL, "dim %d must be a positive multiple of 4 (<= 8192)", d);
+  if (k <= 0 || k > 32768) return set_error(EC_EINVAL, "k %d outside 1..32768", k);
+  if (n > 0xffffffffLL) return set_error(EC_EINVAL, "more than 2^32 rows");
+  return EC_OK;
+}
+
+// --------------------------------------------------------------- search --
+static int ensure_search_ws(Device& dv, size_t bytes, void** out) {
+  IndexW& ix = dv.index;
+  if (ix.sws && ix.sws_bytes >= bytes) {
+    *out = ix.sws;
+    return EC_OK;
+  }
+  if (ix.sws) {
+    dev_free(dv, ix.sws, ix.sws_bytes);
+    ix.sws = nullptr;
+    ix.sws_bytes = 0;
+  }
+  EC_TRY(dev_alloc(dv, &ix.sws, bytes, "search workspace"));
+  ix.sws_bytes = bytes;
+  *out = ix.sws;
+  return EC_OK;
+}
+
+static size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static int search_device(int li, const float* q, int64_t q0, int64_t q1, int nprobe, int topk, bool ivf,
+                         int64_t* ids, float* scores) {
+  Device& dv = *G().devs[li];
+  IndexW& ix = dv.index;
+  EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
+  const int d = ix.d;
+  cudaStream_t st = dv.stream;
+  const int64_t QB = 8192;
+  for (int64_t a = q0; a < q1; a += QB) {
+    const int64_t nq = std::min(QB, q1 - a);
+    const int nchunks = ivf ? 0 : static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(1, (ix.n + 8191) / 8192)));
+    const int ngroups = ivf ? nprobe : nchunks;
+    const size_t s_q = a256(static_cast<size_t>(nq) * d * 4);
+    const size_t s_s = ivf ? a256(static_cast<size_t>(nq) * ix.k * 4) : 0;
+    const size_t s_p = ivf ? a256(static_cast<size_t>(nq) * nprobe * 4) : 0;
+    const size_t s_c = a256(static_cast<size_t>(nq) * ngroups * topk * 8);
+    const size_t s_i = a256(static_cast<size_t>(nq) * topk * 8);
+    const size_t s_f = a256(static_cast<size_t>(nq) * topk * 4);
+    void* ws;
+    EC_TRY(ensure_search_ws(dv, s_q + s_s + s_p + s_c + s_i + s_f, &ws));
+    char* w = static_cast<char*>(ws);
+    float* dq = reinterpret_cast<float*>(w);
+    float* dS = reinterpret_cast<float*>(w + s_q);
+    int32_t* dp = reinterpret_cast<int32_t*>(w + s_q + s_s);
+    unsigned long long* dc = reinterpret_cast<unsigned long long*>(w + s_q + s_s + s_p);
+    int64_t* di = reinterpret_cast<int64_t*>(w + s_q + s_s + s_p + s_c);
+    float* df = reinterpret_cast<float*>(w + s_q + s_s + s_p + s_c + s_i);
+    EC_TRY(check_cuda(cudaMemcpyAsync(dq, q + a * d, static_cast<size_t>(nq) * d * 4,
+                                      cudaMemcpyHostToDevice, st), "query upload"));
+    if (ivf) {
+      EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st), "probe scores"));
+      EC_TRY(check_cuda(launch_probe_select(dS, nq, ix.k, nprobe, dp, st), "probe select"));
+      EC_TRY(check_cuda(launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, dc, st),
+                        "list scan"));
+    } else {
+      EC_TRY(check_cuda(launch_flat_scan(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st), "flat scan"));
+    }
+    EC_TRY(check_cuda(launch_merge(dc, nq, ngroups, topk, di, df, st), "merge"));
+    EC_TRY(check_cuda(cudaMemcpyAsync(ids + a * topk, di, static_cast<size_t>(nq) * topk * 8,
+                                      cudaMemcpyDeviceToHost, st), "ids download"));
+    EC_TRY(check_cuda(cudaMemcpyAsync(scores + a * topk, df, static_cast<size_t>(nq) * topk * 4,
+                                      cudaMemcpyDeviceToHost, st), "scores download"));
+    EC_TRY(sync_and_check(dv, "search"));
+  }
+  return EC_OK;
+}
+
+}  // namespace ec
+
+using namespace ec;
+
+extern "C" {
+
+int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t nsample, int k,
+              int iters, const float* init, float* centroids) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  if (!x || !sample || !centroids || iters < 0 || nsample < 0)
+    return set_error(EC_EINVAL, "bad kmeans arguments");
+  for (int64_t j = 0; j < nsample; ++j)
+    if (sample[j] < 0 || sample[j] >= n) return set_error(EC_EINVAL, "sample[%lld] out of range", (long long)j);
+  std::vector<float> c0(static_cast<size_t>(k) * d);
+  if (init) {
+    std::memcpy(c0.data(), init, c0.size() * 4);
+  } else {
+    // init: copy k sample rows (ann.lisp:83-86)
+    if (nsample < k) return set_error(EC_EINVAL, "sample of %lld rows < k %d", (long long)nsample, k);
+    for (int c = 0; c < k; ++c)
+      std::memcpy(&c0[static_cast<size_t>(c) * d], x + sample[c] * d, static_cast<size_t>(d) * 4);
+  }
+  const bool proc = comm_process_mode();
+  const int nd = static_cast<int>(G().devs.size());
+  if (!proc && nd > 1) EC_TRY(comm_ensure_local());
+  const bool reduce = proc ? G().world > 1 : nd > 1;
+  return on_devices(nd, [&](int li) {
+    int64_t j0, j1;
+    split(nsample, nd, li, &j0, &j1);
+    return kmeans_device(li, x, n, d, sample, j0, j1, k, iters, c0.data(), li == 0 ? centroids : nullptr,
+                         reduce);
+  });
+}
+
+int ec_assign(const float* x, int64_t n, int d, const int64_t* rows, int64_t nrows,
+              const float* centroids, int k, int32_t* assign) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  if (!x || !centroids || !assign) return set_error(EC_EINVAL, "bad assign arguments");
+  const int64_t m = rows ? nrows : n;
+  if (rows)
+    for (int64_t j = 0; j < nrows; ++j)
+      if (rows[j] < 0 || rows[j] >= n) return set_error(EC_EINVAL, "rows[%lld] out of range", (long long)j);
+  const int nd = static_cast<int>(G().devs.size());
+  return on_devices(nd, [&](int li) {
+    int64_t r0, r1;
+    split(m, nd, li, &r0, &r1);
+    return assign_device(li, x, r0, r1, d, rows, centroids, k, assign, nullptr, nullptr, nullptr);
+  });
+}
+
+int ec_assign_all(const float* x, int64_t n, int d, const float* centroids, int k, uint32_t* counts,
+                  uint32_t* lists) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  if (!x || !centroids || !counts || !lists) return set_error(EC_EINVAL, "bad assign-all arguments");
+  const int nd = static_cast<int>(G().devs.size());
+  if (nd == 1) {
+    std::vector<int64_t> offs(k + 1);
+    return assign_device(0, x, 0, n, d, nullptr, centroids, k, nullptr, counts, offs.data(), lists);
+  }
+  std::vector<std::vector<uint32_t>> cnt(nd, std::vector<uint32_t>(k)), lst(nd);
+  std::vector<std::vector<int64_t>> offs(nd, std::vector<int64_t>(k + 1));
+  for (int li = 0; li < nd; ++li) {
+    int64_t r0, r1;
+    split(n, nd, li, &r0, &r1);
+    lst[li].resize(static_cast<size_t>(std::max<int64_t>(r1 - r0, 1)));
+  }
+  EC_TRY(on_devices(nd, [&](int li) {
+    int64_t r0, r1;
+    split(n, nd, li, &r0, &r1);
+    return assign_device(li, x, r0, r1, d, nullptr, centroids, k, nullptr, cnt[li].data(), offs[li].data(),
+                         lst[li].data());
+  }));
+  // concatenate the per-device runs of each list in device order: shards are
+  // ascending row ranges, so ids stay ascending within a list (ann.lisp:153-157)
+  int64_t pos = 0;
+  for (int c = 0; c < k; ++c) {
+    uint32_t tot = 0;
+    for (int li = 0; li < nd; ++li) {
+      const int64_t b = offs[li][c], e = offs[li][c + 1];
+      std::memcpy(lists + pos, lst[li].data() + b, static_cast<size_t>(e - b) * 4);
+      pos += e - b;
+      tot += cnt[li][c];
+    }
+    counts[c] = tot;
+  }
+  return EC_OK;
+}
+
+int ec_index_load(const float* x, int64_t n, int d, const float* centroids, int k,
+                  const uint32_t* counts, const uint32_t* lists) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!x || n <= 0 || d <= 0 || d % 4 || d > 8192) return set_error(EC_EINVAL, "bad index arguments");
+  if (k < 0 || (k > 0 && (!centroids || !counts || !lists)) || k > 8192)
+    return set_error(EC_EINVAL, "bad ivf arguments (k <= 8192)");
+  std::vector<int64_t> offs(k + 1, 0);
+  for (int c = 0; c < k; ++c) offs[c + 1] = offs[c] + counts[c];
+  if (k > 0 && offs[k] != n) return set_error(EC_EINVAL, "counts sum to %lld, not n", (long long)offs[k]);
+  if (k > 0)
+    for (int64_t i = 0; i < n; ++i)
+      if (lists[i] >= n) return set_error(EC_EINVAL, "list entry %lld out of range", (long long)i);
+  for (Device* dv : G().devs) {
+    EC_TRY(check_cuda(cudaSetDevice(dv->ordinal), "cudaSetDevice"));
+    if (dv->index.sws) dev_free(*dv, dv->index.sws, dv->index.sws_bytes);
+    for (void* p : dv->index.owned) cudaFree(p);
+    dv->index = IndexW();
+    IndexW& ix = dv->index;
+    auto take = [&](void** p, size_t bytes, const char* what) -> int {
+      int rc = dev_alloc(*dv, p, bytes, what);
+      if (!rc) ix.owned.push_back(*p);
+      return rc;
+    };
+    EC_TRY(take(reinterpret_cast<void**>(&ix.x), static_cast<size_t>(n) * d * 4, "index vectors"));
+    EC_TRY(check_cuda(cudaMemcpy(ix.x, x, static_cast<size_t>(n) * d * 4, cudaMemcpyHostToDevice),
+                      "vectors upload"));
+    if (k > 0) {
+      EC_TRY(take(reinterpret_cast<void**>(&ix.cent), static_cast<size_t>(k) * d * 4, "centroids"));
+      EC_TRY(take(reinterpret_cast<void**>(&ix.lists), static_cast<size_t>(n) * 4, "lists"));
+      EC_TRY(take(reinterpret_cast<void**>(&ix.offs), static_cast<size_t>(k + 1) * 8, "offsets"));
+      EC_TRY(check_cuda(cudaMemcpy(ix.cent, centroids, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice),
+                        "centroids upload"));
+      EC_TRY(check_cuda(cudaMemcpy(ix.lists, lists, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice),
+                        "lists upload"));
+      EC_TRY(check_cuda(cudaMemcpy(ix.offs, offs.data(), static_cast<size_t>(k + 1) * 8, cudaMemcpyHostToDevice),
+                        "offsets upload"));
+    }
+    ix.n = n;
+    ix.d = d;
+    ix.k = k;
+    ix.h_offs = offs;
+  }
+  return EC_OK;
+}
+
+int ec_ivf_search(const float* q, int nq, int nprobe, int topk, int64_t* ids, float* scores) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  const IndexW& ix = G().devs[0]->index;
+  if (!ix.x || ix.k <= 0) return set_error(EC_ESTATE, "no IVF index loaded");
+  if (nq == 0) return EC_OK;
+  if (!q || nq < 0 || !ids || !scores || topk < 1 || topk > 64 || nprobe < 1)
+    return set_error(EC_EINVAL, "bad search arguments (1 <= topk <= 64, nprobe >= 1)");
+  nprobe = std::min(nprobe, ix.k);  // (min *ann-nprobe* *ann-k*) kb.lisp:350
+  if (static_cast<size_t>(nprobe) * topk * 8 + 256 > 200 * 1024)
+    return set_error(EC_EINVAL, "nprobe * topk too large");
+  const int nd = static_cast<int>(G().devs.size());
+  return on_devices(nd, [&](int li) {
+    int64_t a, b;
+    split(nq, nd, li, &a, &b);
+    return a < b ? search_device(li, q, a, b, nprobe, topk, true, ids, scores) : EC_OK;
+  });
+}
+
+int ec_flat_search(const float* q, int nq, int topk, int64_t* ids, float* scores) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  const IndexW& ix = G().devs[0]->index;
+  if (!ix.x) return set_error(EC_ESTATE, "no index loaded");
+  if (nq == 0) return EC_OK;
+  if (!q || nq < 0 || !ids || !scores || topk < 1 || topk > 64)
+    return set_error(EC_EINVAL, "bad search arguments (1 <= topk <= 64)");
+  const int nd = static_cast<int>(G().devs.size());
+  return on_devices(nd, [&](int li) {
+    int64_t a, b;
+    split(nq, nd, li, &a, &b);
+    return a < b ? search_device(li, q, a, b, 0, topk, false, ids, scores) : EC_OK;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,36 @@
+// ec_ivf.h -- launchers of the IVF kernels (ec_ivf_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ec {
+
+// assign[i] = argmax_c <X[rows ? rows[i] : i], C[c]>, ties -> lowest c
+cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const float* C, int k,
+                          int d, int32_t* out, cudaStream_t st);
+// S[q, c] = <Q[q], C[c]> (sequential single-float order)
+cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
+                          cudaStream_t st);
+// stable counting sort of assignments into inverted lists:
+// counts[k], offs[k + 1], lists[n] (base + row id, ascending within a list);
+// tile_hist needs sort_tiles(n) * k words of scratch
+int64_t sort_tiles(int64_t n);
+cudaError_t launch_lists(const int32_t* a, int64_t n, int k, uint32_t* tile_hist,
+                         uint32_t* counts, int64_t* offs, uint32_t base, uint32_t* lists,
+                         cudaStream_t st);
+// out[c * (d + 1) + j] = sum of X[list c][j] in list order; [.. + d] = count
+cudaError_t launch_segsum(const float* X, const uint32_t* lists, const int64_t* offs, int k,
+                          int d, float* out, cudaStream_t st);
+cudaError_t launch_update(const float* sums, int k, int d, float* cent, cudaStream_t st);
+cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, int32_t* probes,
+                                cudaStream_t st);
+cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
+                             const int32_t* probes, int nprobe, const float* Q, int64_t nq,
+                             int topk, unsigned long long* cand, cudaStream_t st);
+cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, const float* Q,
+                             int64_t nq, int topk, unsigned long long* cand, cudaStream_t st);
+cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk,
+                         int64_t* ids, float* scores, cudaStream_t st);
+
+}  // namespace ec

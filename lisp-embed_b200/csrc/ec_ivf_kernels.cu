@@ -1,0 +1,564 @@
+// ec_ivf_kernels.cu -- IVF kernels: k-means assignment, stable inverted-list
+// build, per-cluster sums, IVF probe and list scan, flat scan.
+//
+// Scores are computed with the reference's exact arithmetic: a sequential
+// single-float sum over k of separately rounded products (ann.lisp:25-35,
+// kb.lisp:153-162), written with __fmul_rn / __fadd_rn so the compiler
+// cannot contract them into FMAs.  Every score is therefore bit-identical to
+// the Lisp's, and argmax / top-k decisions (ties included) match exactly.
+// The score kernel is a register-tiled SIMT GEMM: a 128 x 128 output tile
+// per CTA, an 8 x 8 micro-tile per thread, k staged through shared memory
+// in chunks of 32 -- each thread still walks k in order for each of its
+// outputs.
+#include <cfloat>
+#include <cstdint>
+
+#include "ec_ivf.h"
+
+namespace ec {
+
+constexpr int SB = 128;   // rows / centroids per tile
+constexpr int SK = 32;    // k chunk
+constexpr int SPAD = 4;
+
+// ordered key: ascending key == descending score, then ascending tiebreak
+__device__ __forceinline__ unsigned long long desc_key(float s, uint32_t tie) {
+  s = s + 0.0f;  // -0.0 -> +0.0 (they compare equal in the reference)
+  uint32_t u = __float_as_uint(s);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // ascending float order
+  return (static_cast<unsigned long long>(~u) << 32) | tie;
+}
+__device__ __forceinline__ float key_score(unsigned long long k) {
+  uint32_t u = ~static_cast<uint32_t>(k >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+  return __uint_as_float(u);
+}
+
+// Load a SB x SK chunk (rows r0.., cols k0..) of a row-major [n, d] matrix
+// transposed into smem T[SK][SB + SPAD]; rows past n read as 0.
+__device__ __forceinline__ void load_chunk_t(float (*T)[SB + SPAD], const float* X, const int64_t* rows,
+                                             int64_t r0, int64_t n, int d, int k0) {
+  // 128 rows x 32 cols = 1024 float4; 256 threads x 4
+  for (int i = threadIdx.x; i < SB * (SK / 4); i += blockDim.x) {
+    const int r = i / (SK / 4), c4 = i % (SK / 4);
+    const int64_t gr = r0 + r;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (gr < n && k0 + c4 * 4 < d) {
+      const int64_t src = rows ? rows[gr] : gr;
+      v = *reinterpret_cast<const float4*>(X + src * d + k0 + c4 * 4);
+    }
+    T[c4 * 4 + 0][r] = v.x;
+    T[c4 * 4 + 1][r] = v.y;
+    T[c4 * 4 + 2][r] = v.z;
+    T[c4 * 4 + 3][r] = v.w;
+  }
+}
+
+// acc[i][j] = sum_k A[row i][k] * B[col j][k], k ascending, no FMA.
+// Thread (ty, tx) of a 16 x 16 grid owns rows ty + 16 i and cols tx + 16 j.
+__device__ __forceinline__ void exact_tile(float (&acc)[8][8], float (*As)[SB + SPAD],
+                                           float (*Bs)[SB + SPAD], const float* X,
+                                           const int64_t* xrows, int64_t r0, int64_t n,
+                                           const float* C, int64_t c0, int64_t kc, int d) {
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < d; k0 += SK) {
+    __syncthreads();
+    load_chunk_t(As, X, xrows, r0, n, d, k0);
+    load_chunk_t(Bs, C, nullptr, c0, kc, d, k0);
+    __syncthreads();
+    const int kend = d - k0 < SK ? d - k0 : SK;
+    for (int k = 0; k < kend; ++k) {
+      float a[8], b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = As[k][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = Bs[k][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+    }
+  }
+}
+
+// ann::nearest-centroid for every row: strict > over ascending centroid
+// index, i.e. the highest score with the lowest index among equals.
+__global__ void __launch_bounds__(256) assign_kernel(const float* X, const int64_t* xrows, int64_t n,
+                                                     const float* C, int k, int d, int32_t* out) {
+  __shared__ float As[SK][SB + SPAD];
+  __shared__ float Bs[SK][SB + SPAD];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * SB;
+  float best[8];
+  int bidx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    best[i] = -FLT_MAX;
+    bidx[i] = 0x7fffffff;
+  }
+  for (int c0 = 0; c0 < k; c0 += SB) {
+    float acc[8][8];
+    exact_tile(acc, As, Bs, X, xrows, r0, n, C, c0, k, d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + tx + 16 * j;
+        if (c < k) {
+          const float s = acc[i][j];
+          if (s > best[i] || (s == best[i] && c < bidx[i])) {
+            best[i] = s;
+            bidx[i] = c;
+          }
+        }
+      }
+  }
+  // combine the 16 threads (tx) of each row: lanes differ in bits 0..3
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float s = best[i];
+    int c = bidx[i];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const int c2 = __shfl_xor_sync(0xffffffffu, c, o);
+      if (s2 > s || (s2 == s && c2 < c)) {
+        s = s2;
+        c = c2;
+      }
+    }
+    const int64_t row = r0 + ty + 16 * i;
+    // no score above most-negative-single-float: the Lisp keeps best = 0
+    if (tx == 0 && row < n) out[row] = (c == 0x7fffffff || !(s > -FLT_MAX)) ? 0 : c;
+  }
+}
+
+// full score matrix S[q, c] (IVF probe, kb.lisp:351-352)
+__global__ void __launch_bounds__(256) scores_kernel(const float* Q, int64_t nq, const float* C, int k,
+                                                     int d, float* S) {
+  __shared__ float As[SK][SB + SPAD];
+  __shared__ float Bs[SK][SB + SPAD];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * SB;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * SB;
+  float acc[8][8];
+  exact_tile(acc, As, Bs, Q, nullptr, r0, nq, C, c0, k, d);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = r0 + ty + 16 * i;
+    if (r >= nq) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t c = c0 + tx + 16 * j;
+      if (c < k) S[r * k + c] = acc[i][j];
+    }
+  }
+}
+
+// ---------------------------------------------------- stable counting sort --
+constexpr int kSortTile = 4096;
+
+__global__ void hist_kernel(const int32_t* a, int64_t n, int k, uint32_t* tile_hist) {
+  extern __shared__ uint32_t h[];
+  for (int c = threadIdx.x; c < k; c += blockDim.x) h[c] = 0;
+  __syncthreads();
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSortTile;
+  for (int64_t i = t0 + threadIdx.x; i < t0 + kSortTile && i < n; i += blockDim.x)
+    atomicAdd(&h[a[i]], 1u);
+  __syncthreads();
+  for (int c = threadIdx.x; c < k; c += blockDim.x)
+    tile_hist[static_cast<int64_t>(blockIdx.x) * k + c] = h[c];
+}
+
+// counts[c] = sum over tiles
+__global__ void colsum_kernel(const uint32_t* tile_hist, int ntiles, int k, uint32_t* counts) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= k) return;
+  uint32_t s = 0;
+  for (int t = 0; t < ntiles; ++t) s += tile_hist[static_cast<int64_t>(t) * k + c];
+  counts[c] = s;
+}
+
+// single-block exclusive scan of counts -> offs[0..k], k <= 32 * 1024
+__global__ void scan_kernel(const uint32_t* counts, int k, int64_t* offs) {
+  __shared__ int64_t part[1024];
+  const int per = (k + blockDim.x - 1) / blockDim.x;
+  const int b = threadIdx.x * per;
+  int64_t s = 0;
+  for (int i = 0; i < per && b + i < k; ++i) s += counts[b + i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    for (int t = 0; t < static_cast<int>(blockDim.x); ++t) {
+      const int64_t v = part[t];
+      part[t] = acc;
+      acc += v;
+    }
+    offs[k] = acc;
+  }
+  __syncthreads();
+  int64_t acc = part[threadIdx.x];
+  for (int i = 0; i < per && b + i < k; ++i) {
+    offs[b + i] = acc;
+    acc += counts[b + i];
+  }
+}
+
+// tile_hist[t][c] <- start of tile t's run inside list c
+__global__ void tile_offsets_kernel(uint32_t* tile_hist, int ntiles, int k, const int64_t* offs) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= k) return;
+  uint32_t run = static_cast<uint32_t>(offs[c]);
+  for (int t = 0; t < ntiles; ++t) {
+    const uint32_t v = tile_hist[static_cast<int64_t>(t) * k + c];
+    tile_hist[static_cast<int64_t>(t) * k + c] = run;
+    run += v;
+  }
+}
+
+// one warp per tile, rows in ascending order: lists[pos] = base + row
+__global__ void scatter_kernel(const int32_t* a, int64_t n, int k, const uint32_t* tile_off,
+                               uint32_t base, uint32_t* lists) {
+  extern __shared__ uint32_t cur[];
+  for (int c = threadIdx.x; c < k; c += blockDim.x)
+    cur[c] = tile_off[static_cast<int64_t>(blockIdx.x) * k + c];
+  __syncwarp();
+  const int lane = threadIdx.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSortTile;
+  for (int64_t i0 = t0; i0 < t0 + kSortTile && i0 < n; i0 += 32) {
+    const int64_t i = i0 + lane;
+    const bool valid = i < n && i < t0 + kSortTile;
+    const int c = valid ? a[i] : -1 - lane;  // invalid lanes never match
+    const unsigned peers = __match_any_sync(0xffffffffu, c);
+    if (valid) {
+      const unsigned lower = peers & ((1u << lane) - 1u);
+      const uint32_t pos = cur[c] + __popc(lower);
+      lists[pos] = base + static_cast<uint32_t>(i);
+      __syncwarp(peers);
+      if (lower == 0) cur[c] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+// sums[c] = x[rows of list c] summed in list order (ann.lisp:109-115) as
+// float4 columns; out[c * (d + 1) + d] = count.
+__global__ void segsum_kernel(const float* X, const uint32_t* lists, const int64_t* offs, int k,
+                              int d, float* out) {
+  const int c = blockIdx.x;
+  if (c >= k) return;
+  const int64_t b = offs[c], e = offs[c + 1];
+  for (int c4 = threadIdx.x; c4 < d / 4; c4 += blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t j = b; j < e; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(X + static_cast<int64_t>(lists[j]) * d + c4 * 4);
+      s.x = __fadd_rn(s.x, v.x);
+      s.y = __fadd_rn(s.y, v.y);
+      s.z = __fadd_rn(s.z, v.z);
+      s.w = __fadd_rn(s.w, v.w);
+    }
+    float* o = out + static_cast<int64_t>(c) * (d + 1) + c4 * 4;
+    o[0] = s.x;
+    o[1] = s.y;
+    o[2] = s.z;
+    o[3] = s.w;
+  }
+  if (threadIdx.x == 0) out[static_cast<int64_t>(c) * (d + 1) + d] = static_cast<float>(e - b);
+}
+
+// centroid = sum / count for non-empty clusters (ann.lisp:116-122)
+__global__ void update_kernel(const float* sums, int k, int d, float* cent) {
+  const int c = blockIdx.x;
+  if (c >= k) return;
+  const float cnt = sums[static_cast<int64_t>(c) * (d + 1) + d];
+  if (!(cnt > 0.f)) return;
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    cent[static_cast<int64_t>(c) * d + i] = __fdiv_rn(sums[static_cast<int64_t>(c) * (d + 1) + i], cnt);
+}
+
+// --------------------------------------------------------------- search --
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w < v ? w : v;
+  }
+  return v;
+}
+
+// block-wide min of one key per thread (blockDim multiple of 32, <= 1024)
+__device__ unsigned long long block_min_u64(unsigned long long v, unsigned long long* red) {
+  v = warp_min_u64(v);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : ~0ull;
+    v = warp_min_u64(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// top nprobe centroids of each query: score desc, index asc (stable sort of
+// kb.lisp:353).  One block per query, bitonic sort of k <= 8192 keys.
+__global__ void probe_select_kernel(const float* S, int k, int nprobe, int32_t* probes) {
+  extern __shared__ unsigned long long keys[];
+  const int64_t q = blockIdx.x;
+  int P = 1;
+  while (P < k) P <<= 1;
+  for (int i = threadIdx.x; i < P; i += blockDim.x)
+    keys[i] = i < k ? desc_key(S[q * k + i], static_cast<uint32_t>(i)) : ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = keys[i], b = keys[j];
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  for (int i = threadIdx.x; i < nprobe; i += blockDim.x)
+    probes[q * nprobe + i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
+}
+
+// Exact scores of `cnt` rows against one query, top `topk` by (score desc,
+// position asc), merged into a running list in smem.  rows_of(pos) maps a
+// position to a row id.  Shared by the list scan and the flat scan.
+template <bool kIndirect>
+__device__ void scan_rows(const float* X, int d, const uint32_t* lists, int64_t start, int64_t cnt,
+                          const float* qs, int topk, unsigned long long* best,
+                          unsigned long long* tile, unsigned long long* red) {
+  constexpr int TILE = 2048;
+  for (int64_t t0 = 0; t0 < cnt; t0 += TILE) {
+    const int m = static_cast<int>(cnt - t0 < TILE ? cnt - t0 : TILE);
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const int64_t p = t0 + i;
+      const int64_t row = kIndirect ? static_cast<int64_t>(lists[start + p]) : start + p;
+      const float4* xr = reinterpret_cast<const float4*>(X + row * d);
+      float s = 0.f;
+      for (int c4 = 0; c4 < d / 4; ++c4) {
+        const float4 v = xr[c4];
+        s = __fadd_rn(s, __fmul_rn(v.x, qs[4 * c4]));
+        s = __fadd_rn(s, __fmul_rn(v.y, qs[4 * c4 + 1]));
+        s = __fadd_rn(s, __fmul_rn(v.z, qs[4 * c4 + 2]));
+        s = __fadd_rn(s, __fmul_rn(v.w, qs[4 * c4 + 3]));
+      }
+      tile[i] = desc_key(s, static_cast<uint32_t>(p));
+    }
+    // append the running best as candidates (their positions are smaller)
+    for (int i = threadIdx.x; i < topk; i += blockDim.x) tile[m + i] = best[i];
+    __syncthreads();
+    const int tot = m + topk;
+    for (int r = 0; r < topk; ++r) {
+      unsigned long long mine = ~0ull;
+      int at = -1;
+      for (int i = threadIdx.x; i < tot; i += blockDim.x)
+        if (tile[i] < mine) {
+          mine = tile[i];
+          at = i;
+        }
+      const unsigned long long w = block_min_u64(mine, red);
+      if (w == mine && at >= 0 && w != ~0ull) tile[at] = ~0ull;  // keys are unique
+      if (threadIdx.x == 0) best[r] = w;
+      __syncthreads();
+    }
+  }
+}
+
+// grid (nprobe, nq): top-k of list probes[q][p] for query q.
+// cand[(q * nprobe + p) * topk + r] = key with tiebreak = position in list.
+__global__ void list_scan_kernel(const float* X, int d, const uint32_t* lists, const int64_t* offs,
+                                 const int32_t* probes, int nprobe, const float* Q, int topk,
+                                 unsigned long long* cand) {
+  extern __shared__ unsigned long long sm[];
+  unsigned long long* best = sm;              // [topk]
+  unsigned long long* red = best + 64;        // [32]
+  unsigned long long* tile = red + 32;        // [2048 + topk]
+  float* qs = reinterpret_cast<float*>(tile + 2048 + 64);
+  const int p = blockIdx.x;
+  const int64_t q = blockIdx.y;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) qs[i] = Q[q * d + i];
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) best[i] = ~0ull;
+  __syncthreads();
+  const int c = probes[q * nprobe + p];
+  scan_rows<true>(X, d, lists, offs[c], offs[c + 1] - offs[c], qs, topk, best, tile, red);
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) {
+    const unsigned long long kk = best[i];
+    // replace the list position by the row id (kept for the merge)
+    cand[(q * nprobe + p) * topk + i] =
+        kk == ~0ull ? ~0ull
+                    : (kk & 0xffffffff00000000ull) |
+                          lists[offs[c] + static_cast<int64_t>(kk & 0xffffffffu)];
+  }
+}
+
+// grid (nchunks, nq): top-k of rows [chunk * rows_per, ...) for query q
+__global__ void flat_scan_kernel(const float* X, int64_t n, int d, int64_t rows_per, const float* Q,
+                                 int topk, unsigned long long* cand) {
+  extern __shared__ unsigned long long sm[];
+  unsigned long long* best = sm;
+  unsigned long long* red = best + 64;
+  unsigned long long* tile = red + 32;
+  float* qs = reinterpret_cast<float*>(tile + 2048 + 64);
+  const int64_t ch = blockIdx.x;
+  const int64_t q = blockIdx.y;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) qs[i] = Q[q * d + i];
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) best[i] = ~0ull;
+  __syncthreads();
+  const int64_t s = ch * rows_per;
+  const int64_t cnt = s >= n ? 0 : (n - s < rows_per ? n - s : rows_per);
+  scan_rows<false>(X, d, nullptr, s, cnt, qs, topk, best, tile, red);
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) {
+    const unsigned long long kk = best[i];
+    cand[(q * gridDim.x + ch) * topk + i] =
+        kk == ~0ull ? ~0ull : (kk & 0xffffffff00000000ull) | static_cast<uint32_t>(s + (kk & 0xffffffffu));
+  }
+}
+
+// Final top-k per query over ngroups x topk candidates.  Order: score desc,
+// then group (probe rank / chunk) asc, then the candidate's rank inside its
+// group -- the stable merge of kb.lisp:363 and :199.
+__global__ void merge_kernel(const unsigned long long* cand, int ngroups, int topk, int64_t* ids,
+                             float* scores) {
+  extern __shared__ unsigned long long mk[];
+  unsigned long long* red = mk;
+  unsigned long long* keys = mk + 32;
+  const int64_t q = blockIdx.x;
+  const int tot = ngroups * topk;
+  for (int i = threadIdx.x; i < tot; i += blockDim.x) {
+    const unsigned long long c = cand[q * tot + i];
+    // re-key: score bits high, then flat index (group * topk + rank) low
+    keys[i] = c == ~0ull ? ~0ull : ((c & 0xffffffff00000000ull) | static_cast<uint32_t>(i));
+  }
+  __syncthreads();
+  for (int r = 0; r < topk; ++r) {
+    unsigned long long mine = ~0ull;
+    int at = -1;
+    for (int i = threadIdx.x; i < tot; i += blockDim.x)
+      if (keys[i] < mine) {
+        mine = keys[i];
+        at = i;
+      }
+    const unsigned long long w = block_min_u64(mine, red);
+    if (w == mine && at >= 0 && w != ~0ull) keys[at] = ~0ull;
+    if (threadIdx.x == 0) {
+      if (w == ~0ull) {
+        ids[q * topk + r] = -1;
+        scores[q * topk + r] = -FLT_MAX;
+      } else {
+        const unsigned long long c = cand[q * tot + static_cast<int>(w & 0xffffffffu)];
+        ids[q * topk + r] = static_cast<int64_t>(c & 0xffffffffu);
+        scores[q * topk + r] = key_score(c);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------- launchers --
+cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const float* C, int k, int d,
+                          int32_t* out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t grid = (n + SB - 1) / SB;
+  assign_kernel<<<static_cast<unsigned>(grid), 256, 0, st>>>(X, rows, n, C, k, d, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
+                          cudaStream_t st) {
+  if (nq <= 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((nq + SB - 1) / SB), static_cast<unsigned>((k + SB - 1) / SB));
+  scores_kernel<<<grid, 256, 0, st>>>(Q, nq, C, k, d, S);
+  return cudaGetLastError();
+}
+
+int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+cudaError_t launch_lists(const int32_t* a, int64_t n, int k, uint32_t* tile_hist, uint32_t* counts,
+                         int64_t* offs, uint32_t base, uint32_t* lists, cudaStream_t st) {
+  const int64_t nt = sort_tiles(n);
+  const size_t hsm = static_cast<size_t>(k) * 4;
+  if (hsm > 200 * 1024) return cudaErrorInvalidValue;
+  if (hsm > 48 * 1024) {
+    cudaFuncSetAttribute(hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(hsm));
+    cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(hsm));
+  }
+  if (nt > 0) hist_kernel<<<static_cast<unsigned>(nt), 256, hsm, st>>>(a, n, k, tile_hist);
+  colsum_kernel<<<(k + 255) / 256, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, counts);
+  scan_kernel<<<1, 1024, 0, st>>>(counts, k, offs);
+  tile_offsets_kernel<<<(k + 255) / 256, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, offs);
+  if (nt > 0) scatter_kernel<<<static_cast<unsigned>(nt), 32, hsm, st>>>(a, n, k, tile_hist, base, lists);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_segsum(const float* X, const uint32_t* lists, const int64_t* offs, int k, int d,
+                          float* out, cudaStream_t st) {
+  int th = d / 4;
+  th = th < 32 ? 32 : (th > 256 ? 256 : ((th + 31) / 32) * 32);
+  segsum_kernel<<<k, th, 0, st>>>(X, lists, offs, k, d, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_update(const float* sums, int k, int d, float* cent, cudaStream_t st) {
+  update_kernel<<<k, 128, 0, st>>>(sums, k, d, cent);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, int32_t* probes,
+                                cudaStream_t st) {
+  int P = 1;
+  while (P < k) P <<= 1;
+  const size_t sm = static_cast<size_t>(P) * 8;
+  if (sm > 64 * 1024) return cudaErrorInvalidValue;
+  cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  probe_select_kernel<<<static_cast<unsigned>(nq), 512, sm, st>>>(S, k, nprobe, probes);
+  return cudaGetLastError();
+}
+
+static size_t scan_smem(int d) { return (64 + 32 + 2048 + 64) * 8 + static_cast<size_t>(d) * 4; }
+
+cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
+                             const int32_t* probes, int nprobe, const float* Q, int64_t nq, int topk,
+                             unsigned long long* cand, cudaStream_t st) {
+  const size_t sm = scan_smem(d);
+  cudaFuncSetAttribute(list_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  dim3 grid(nprobe, static_cast<unsigned>(nq));
+  list_scan_kernel<<<grid, 256, sm, st>>>(X, d, lists, offs, probes, nprobe, Q, topk, cand);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, const float* Q, int64_t nq,
+                             int topk, unsigned long long* cand, cudaStream_t st) {
+  const size_t sm = scan_smem(d);
+  cudaFuncSetAttribute(flat_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  const int64_t rows_per = (n + nchunks - 1) / nchunks;
+  dim3 grid(nchunks, static_cast<unsigned>(nq));
+  flat_scan_kernel<<<grid, 256, sm, st>>>(X, n, d, rows_per, Q, topk, cand);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk, int64_t* ids,
+                         float* scores, cudaStream_t st) {
+  const size_t sm = (32 + static_cast<size_t>(ngroups) * topk) * 8;
+  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  merge_kernel<<<static_cast<unsigned>(nq), 256, sm, st>>>(cand, ngroups, topk, ids, scores);
+  return cudaGetLastError();
+}
+
+}  // namespace ec

@@ -1,0 +1,242 @@
+// ec_json.h -- minimal JSON reader for config.json / 1_Pooling/config.json.
+//
+// Numbers with '.', 'e' or 'E' are converted exactly the way json.lisp's
+// parse-number does (json.lisp:79-113): integer digits accumulated in a
+// double, fraction digits added as digit * scale with scale starting at 0.1
+// and divided by 10 per digit, then multiplied by 10^exp computed by
+// repeated multiplication; so rms_norm_eps / rope_theta come out as the same
+// doubles the Lisp loaders see.  Other numbers are integers.
+#pragma once
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace ec {
+
+struct JVal {
+  enum Kind { Null, Bool, Int, Num, Str, Arr, Obj } kind = Null;
+  bool b = false;
+  int64_t i = 0;
+  double d = 0.0;
+  std::string s;
+  std::vector<JVal> a;
+  std::map<std::string, JVal> o;
+
+  const JVal* get(const std::string& k) const {
+    if (kind != Obj) return nullptr;
+    auto it = o.find(k);
+    return it == o.end() ? nullptr : &it->second;
+  }
+  bool is_num() const { return kind == Int || kind == Num; }
+  double num() const { return kind == Int ? static_cast<double>(i) : d; }
+  bool truthy() const {  // Lisp truthiness of gethash: anything but false/null
+    return !(kind == Null || (kind == Bool && !b));
+  }
+};
+
+class JParser {
+ public:
+  explicit JParser(const std::string& s) : s_(s) {}
+  bool parse(JVal& out, std::string& err) {
+    try {
+      ws();
+      value(out);
+      return true;
+    } catch (const std::string& e) {
+      err = e;
+      return false;
+    }
+  }
+
+ private:
+  const std::string& s_;
+  size_t p_ = 0;
+
+  char peek() const { return p_ < s_.size() ? s_[p_] : '\0'; }
+  char next() {
+    if (p_ >= s_.size()) throw std::string("json: unexpected end");
+    return s_[p_++];
+  }
+  void ws() {
+    while (p_ < s_.size() && (s_[p_] == ' ' || s_[p_] == '\n' || s_[p_] == '\r' || s_[p_] == '\t'))
+      ++p_;
+  }
+  void value(JVal& v) {
+    ws();
+    char c = peek();
+    if (c == '{') {
+      obj(v);
+    } else if (c == '[') {
+      arr(v);
+    } else if (c == '"') {
+      v.kind = JVal::Str;
+      str(v.s);
+    } else if (c == 't') {
+      word("true");
+      v.kind = JVal::Bool;
+      v.b = true;
+    } else if (c == 'f') {
+      word("false");
+      v.kind = JVal::Bool;
+      v.b = false;
+    } else if (c == 'n') {
+      word("null");
+      v.kind = JVal::Null;
+    } else {
+      num(v);
+    }
+  }
+  void word(const char* w) {
+    for (const char* q = w; *q; ++q)
+      if (next() != *q) throw std::string("json: bad literal");
+  }
+  void obj(JVal& v) {
+    v.kind = JVal::Obj;
+    next();
+    ws();
+    if (peek() == '}') {
+      next();
+      return;
+    }
+    while (true) {
+      ws();
+      std::string k;
+      str(k);
+      ws();
+      if (next() != ':') throw std::string("json: expected ':'");
+      JVal x;
+      value(x);
+      v.o[k] = std::move(x);
+      ws();
+      char c = next();
+      if (c == '}') return;
+      if (c != ',') throw std::string("json: expected ',' or '}'");
+    }
+  }
+  void arr(JVal& v) {
+    v.kind = JVal::Arr;
+    next();
+    ws();
+    if (peek() == ']') {
+      next();
+      return;
+    }
+    while (true) {
+      JVal x;
+      value(x);
+      v.a.push_back(std::move(x));
+      ws();
+      char c = next();
+      if (c == ']') return;
+      if (c != ',') throw std::string("json: expected ',' or ']'");
+    }
+  }
+  void str(std::string& out) {
+    if (next() != '"') throw std::string("json: expected string");
+    while (true) {
+      char c = next();
+      if (c == '"') return;
+      if (c == '\\') {
+        char e = next();
+        switch (e) {
+          case 'n': out += '\n'; break;
+          case 't': out += '\t'; break;
+          case 'r': out += '\r'; break;
+          case 'b': out += '\b'; break;
+          case 'f': out += '\f'; break;
+          case 'u': {
+            unsigned cp = 0;
+            for (int k = 0; k < 4; ++k) {
+              char h = next();
+              cp <<= 4;
+              if (h >= '0' && h <= '9') cp |= h - '0';
+              else if (h >= 'a' && h <= 'f') cp |= h - 'a' + 10;
+              else if (h >= 'A' && h <= 'F') cp |= h - 'A' + 10;
+              else throw std::string("json: bad \\u escape");
+            }
+            if (cp < 0x80) out += static_cast<char>(cp);
+            else if (cp < 0x800) {
+              out += static_cast<char>(0xC0 | (cp >> 6));
+              out += static_cast<char>(0x80 | (cp & 0x3F));
+            } else {
+              out += static_cast<char>(0xE0 | (cp >> 12));
+              out += static_cast<char>(0x80 | ((cp >> 6) & 0x3F));
+              out += static_cast<char>(0x80 | (cp & 0x3F));
+            }
+            break;
+          }
+          default: out += e;
+        }
+      } else {
+        out += c;
+      }
+    }
+  }
+  void num(JVal& v) {
+    size_t st = p_;
+    while (p_ < s_.size()) {
+      char c = s_[p_];
+      if ((c >= '0' && c <= '9') || c == '-' || c == '+' || c == '.' || c == 'e' || c == 'E')
+        ++p_;
+      else
+        break;
+    }
+    std::string t = s_.substr(st, p_ - st);
+    if (t.empty()) throw std::string("json: bad value");
+    if (t.find_first_of(".eE") == std::string::npos) {
+      v.kind = JVal::Int;
+      v.i = std::stoll(t);
+      return;
+    }
+    // json.lisp:85-113
+    double mant = 0.0, sign = 1.0;
+    size_t i = 0, n = t.size();
+    if (t[0] == '-') {
+      sign = -1.0;
+      i = 1;
+    }
+    while (i < n && t[i] >= '0' && t[i] <= '9') {
+      mant = mant * 10 + (t[i] - '0');
+      ++i;
+    }
+    if (i < n && t[i] == '.') {
+      ++i;
+      double scale = 0.1;
+      while (i < n && t[i] >= '0' && t[i] <= '9') {
+        mant = mant + scale * (t[i] - '0');
+        scale = scale / 10.0;
+        ++i;
+      }
+    }
+    if (i < n && (t[i] == 'e' || t[i] == 'E')) {
+      ++i;
+      int esign = 1;
+      long e = 0;
+      if (i < n && t[i] == '-') {
+        esign = -1;
+        ++i;
+      }
+      if (i < n && t[i] == '+') ++i;
+      while (i < n && t[i] >= '0' && t[i] <= '9') {
+        e = e * 10 + (t[i] - '0');
+        ++i;
+      }
+      // (expt 10d0 k) for integer k: repeated squaring; 1/10^|k| for k < 0
+      double base = 10.0, r = 1.0;
+      long k = e;
+      while (k > 0) {
+        if (k & 1) r *= base;
+        base *= base;
+        k >>= 1;
+      }
+      mant = esign > 0 ? mant * r : mant * (1.0 / r);
+    }
+    v.kind = JVal::Num;
+    v.d = sign * mant;
+  }
+};
+
+}  // namespace ec

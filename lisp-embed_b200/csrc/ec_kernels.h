@@ -1,0 +1,130 @@
+// ec_kernels.h -- host-side launchers of the sm_100a kernels and their
+// argument blocks.  Each .cu file instantiates its kernels and exposes only
+// these plain functions, so the host code (ec_api.cu) never sees a template.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ec {
+
+enum DtKind : int { kDtF32 = 0, kDtBf16 = 1 };
+enum ConvKind : int { kConvF16ToF32 = 0, kConvBf16ToF32 = 1, kConvF32ToBf16 = 2 };
+
+struct EmbedLnArgs {
+  const int* ids;
+  const int* pos;       // position of each token inside its sequence
+  int pos_offset;       // 2 for roberta and mpnet, else 0
+  const void* word;     // [vocab, H]
+  int word_dtype;
+  const void* posemb;   // [max_pos, H]
+  int pos_dtype;
+  const void* type0;    // row 0 of token_type_embeddings or nullptr
+  int type_dtype;
+  const float* g;
+  const float* b;
+  float* out32;         // [T, H]
+  __nv_bfloat16* outb;  // [T, H]
+  int T, H;
+};
+
+struct LnArgs {
+  const float* x;       // [T, H]
+  const float* g;
+  const float* b;
+  float* out32;         // may alias x
+  __nv_bfloat16* outb;
+  int T, H;
+};
+
+struct RmsArgs {
+  const float* x;       // [*, H]
+  const int* rows;      // optional row gather (nullptr = identity)
+  const float* g;
+  double eps;
+  __nv_bfloat16* outb;  // [T, H] or nullptr
+  float* out32;         // [T, H] or nullptr
+  int T, H;
+};
+
+struct QkRopeArgs {
+  __nv_bfloat16* qkv;
+  int ld;
+  int q_off, k_off;
+  int q_heads, k_heads;  // head_dim is 128
+  const float* q_norm;   // [128] or nullptr
+  const float* k_norm;
+  double eps;
+  const int* pos;
+  const float* cos_t;    // [max_pos, 64]
+  const float* sin_t;
+  int T;
+};
+
+struct PoolArgs {
+  const float* h;       // [T, H] fp32
+  const int* cu;        // [nseq + 1]
+  int mode;             // 0 first, 1 mean, 2 last
+  int final_norm;       // llama final RMSNorm on pooled tokens
+  const float* norm_w;
+  double eps;
+  float* out;
+  int out_stride;
+  int H;
+};
+
+cudaError_t launch_embed_ln(const EmbedLnArgs& a, cudaStream_t st);
+cudaError_t launch_ln(const LnArgs& a, cudaStream_t st);
+cudaError_t launch_rmsnorm(const RmsArgs& a, cudaStream_t st);
+cudaError_t launch_qk_norm_rope(const QkRopeArgs& a, cudaStream_t st);
+cudaError_t launch_pool_l2(const PoolArgs& a, int nseq, cudaStream_t st);
+cudaError_t launch_gather_rows(const void* table, int dtype, const int* ids, float* out, int T,
+                               int H, cudaStream_t st);
+cudaError_t launch_positions(const int* cu, int nseq, int* pos, cudaStream_t st);
+cudaError_t launch_convert(int kind, const void* src, void* dst, size_t n, cudaStream_t st);
+
+// ---- GEMM (ec_gemm.cu) -------------------------------------------------------
+// C[M, N] = A[M, K] . W[N, K]^T with epilogue `epi` (GemmEpi in ec_gemm.cuh:
+// 0 bf16, 1 bf16+gelu, 2 f32+resid, 3 bf16 swiglu, 4 f32).  A and W bf16,
+// K-major; K % 64 == 0; N % bn == 0.  `bn` 0 = pick automatically.
+struct GemmLaunch {
+  const __nv_bfloat16* A;
+  int lda;              // elements
+  const __nv_bfloat16* W;
+  int ldw;
+  int M, N, K;
+  const float* bias;
+  const float* resid;
+  int ldr;
+  void* out;
+  int ldo;
+  int epi;
+  int bn;
+  unsigned* status;
+};
+int gemm_pick_bn(int M, int N, int epi, int num_sms);
+cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms);
+// encode function for TMA descriptors (driver entry point), set once
+bool gemm_init_driver();
+
+// ---- attention (ec_attn.cu) --------------------------------------------------
+struct AttnLaunch {
+  const __nv_bfloat16* qkv;
+  int ld;
+  int q_off, k_off, v_off;
+  __nv_bfloat16* out;
+  int ldo;
+  const int* cu;
+  const int2* blocks;
+  int nblocks;
+  int heads, kv_group, head_dim;
+  int causal;
+  const float* relbias;  // [heads][2 * rel_max - 1], pre-scaled by log2(e)
+  int rel_max;
+};
+cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t st);
+
+}  // namespace ec

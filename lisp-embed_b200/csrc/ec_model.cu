@@ -1,0 +1,788 @@
+// ec_model.cu -- model assembly from uploaded safetensors and the batched
+// encoder forward on one device.
+//
+// Assembly replaces the per-tensor st:get-tensor calls of bert:load-model
+// (bert.lisp:83-127), bert::load-mpnet-weights (bert.lisp:343-389) and
+// llama:load-model (llama.lisp:189-218): Q/K/V weights are fused into one
+// [3H, H] (or [(heads + 2 kv) * hd, H]) bf16 matrix, gate/up into one
+// block-interleaved [2F, H] matrix, vectors stay fp32.
+//
+// The forward replaces embed-bert / embed-mpnet / llama:embed for a whole
+// batch of packed sequences: every linear of every token of every sequence of
+// a layer is one tcgen05 GEMM launch.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+
+#include "ec_gemm.cuh"
+#include "ec_json.h"
+#include "ec_state.h"
+
+namespace ec {
+
+// ----------------------------------------------------------------- helpers --
+static const Tensor* find_t(Device& d, const std::string& name) {
+  auto it = d.uploads.find(name);
+  return it == d.uploads.end() ? nullptr : &it->second;
+}
+
+static int need_t(Device& d, const std::string& name, const Tensor** out,
+                  std::initializer_list<int64_t> shape) {
+  const Tensor* t = find_t(d, name);
+  if (!t) return set_error(EC_EINVAL, "missing tensor %s", name.c_str());
+  if (shape.size()) {
+    std::vector<int64_t> want(shape);
+    if (t->shape != want) {
+      std::string got, exp;
+      for (auto v : t->shape) got += std::to_string(v) + ",";
+      for (auto v : want) exp += std::to_string(v) + ",";
+      return set_error(EC_EINVAL, "tensor %s has shape [%s], expected [%s]", name.c_str(),
+                       got.c_str(), exp.c_str());
+    }
+  }
+  *out = t;
+  return EC_OK;
+}
+
+static int model_alloc(Device& d, void** p, size_t bytes, const char* what) {
+  int rc = dev_alloc(d, p, bytes, what);
+  if (rc == EC_OK) d.model.owned.push_back(*p);
+  return rc;
+}
+
+// fp32 copy of a vector tensor (LayerNorm / RMSNorm weights, biases)
+static int as_f32(Device& d, const Tensor* t, float** out) {
+  if (t->dtype == kDtF32) {
+    *out = static_cast<float*>(t->p);
+    return EC_OK;
+  }
+  void* p;
+  int rc = model_alloc(d, &p, t->numel * 4, "f32 vector");
+  if (rc) return rc;
+  rc = check_cuda(launch_convert(kConvBf16ToF32, t->p, p, t->numel, d.stream), "convert");
+  *out = static_cast<float*>(p);
+  return rc;
+}
+
+// copy `rows` rows of a [*, cols] tensor starting at row r0 into dst (bf16)
+static int rows_to_bf16(Device& d, const Tensor* t, int64_t r0, int64_t rows, int64_t cols,
+                        bf16* dst) {
+  const size_t n = static_cast<size_t>(rows * cols);
+  if (t->dtype == kDtBf16) {
+    return check_cuda(cudaMemcpyAsync(dst, static_cast<const bf16*>(t->p) + r0 * cols,
+                                      n * 2, cudaMemcpyDeviceToDevice, d.stream),
+                      "weight copy");
+  }
+  return check_cuda(launch_convert(kConvF32ToBf16, static_cast<const float*>(t->p) + r0 * cols,
+                                   dst, n, d.stream),
+                    "weight convert");
+}
+
+// vertical concatenation of [rows_i, cols] matrices into one bf16 matrix
+static int concat_bf16(Device& d, const std::vector<const Tensor*>& parts, int64_t cols,
+                       bf16** out) {
+  int64_t rows = 0;
+  for (auto* t : parts) rows += t->shape[0];
+  void* p;
+  int rc = model_alloc(d, &p, static_cast<size_t>(rows * cols) * 2, "bf16 weight");
+  if (rc) return rc;
+  int64_t r = 0;
+  for (auto* t : parts) {
+    rc = rows_to_bf16(d, t, 0, t->shape[0], cols, static_cast<bf16*>(p) + r * cols);
+    if (rc) return rc;
+    r += t->shape[0];
+  }
+  *out = static_cast<bf16*>(p);
+  return EC_OK;
+}
+
+static int concat_f32(Device& d, const std::vector<const Tensor*>& parts, float** out) {
+  size_t n = 0;
+  for (auto* t : parts) n += t->numel;
+  void* p;
+  int rc = model_alloc(d, &p, n * 4, "f32 vector");
+  if (rc) return rc;
+  size_t o = 0;
+  for (auto* t : parts) {
+    if (t->dtype == kDtF32)
+      rc = check_cuda(cudaMemcpyAsync(static_cast<float*>(p) + o, t->p, t->numel * 4,
+                                      cudaMemcpyDeviceToDevice, d.stream),
+                      "vector copy");
+    else
+      rc = check_cuda(
+          launch_convert(kConvBf16ToF32, t->p, static_cast<float*>(p) + o, t->numel, d.stream),
+          "vector convert");
+    if (rc) return rc;
+    o += t->numel;
+  }
+  *out = static_cast<float*>(p);
+  return EC_OK;
+}
+
+void free_model(Device& d) {
+  for (void* p : d.model.owned) cudaFree(p);
+  d.model = ModelW();
+}
+
+// bert::mpnet-bucket (bert.lisp:324-331); single-float log computed in double
+// and rounded, as SBCL does for (log single-float).
+static int mpnet_bucket(int i, int j) {
+  const int n = i - j;
+  const int an = n < 0 ? -n : n;
+  const int ret = n < 0 ? 16 : 0;
+  if (an < 8) return ret + an;
+  const float a = static_cast<float>(std::log(static_cast<double>(static_cast<float>(an) / 8.0f)));
+  const float b = static_cast<float>(std::log(16.0));
+  const float v = 8.0f + 8.0f * (a / b);
+  const int f = static_cast<int>(std::floor(v));
+  return ret + (f < 15 ? f : 15);
+}
+
+// ------------------------------------------------------------ load model --
+static int cfg_int(const JVal& c, const char* k, int* out, bool required = true, int def = 0) {
+  const JVal* v = c.get(k);
+  if (!v || !v->is_num()) {
+    if (required) return set_error(EC_EINVAL, "config.json lacks %s", k);
+    *out = def;
+    return EC_OK;
+  }
+  *out = static_cast<int>(v->num());
+  return EC_OK;
+}
+
+static int load_bert(Device& d, const JVal& cfg, const std::string& mt, int pooling) {
+  ModelW& m = d.model;
+  int rc;
+  if ((rc = cfg_int(cfg, "hidden_size", &m.H)) || (rc = cfg_int(cfg, "num_hidden_layers", &m.layers)) ||
+      (rc = cfg_int(cfg, "num_attention_heads", &m.heads)) ||
+      (rc = cfg_int(cfg, "intermediate_size", &m.F)))
+    return rc;
+  if (m.heads <= 0 || m.H % m.heads) return set_error(EC_EINVAL, "hidden %% heads != 0");
+  m.hd = m.H / m.heads;  // bert.lisp:75
+  m.kv_heads = m.heads;
+  m.pooling = pooling;
+  const bool mpnet = mt == "mpnet";
+  m.family = mpnet ? EC_FAMILY_MPNET : EC_FAMILY_BERT;
+  m.pos_offset = (mpnet || mt == "roberta") ? 2 : 0;  // bert.lisp:294, :477
+  if (m.hd != 32 && m.hd != 64 && m.hd != 128)
+    return set_error(EC_EUNSUPPORTED, "head dim %d (supported: 32, 64, 128)", m.hd);
+  if (m.H % 128 || m.H > 1024 || m.F % 64)
+    return set_error(EC_EUNSUPPORTED, "hidden %d / ffn %d outside this build", m.H, m.F);
+  const int H = m.H, F = m.F;
+  const Tensor *w, *p, *ty = nullptr, *g, *b;
+  if ((rc = need_t(d, "embeddings.word_embeddings.weight", &w, {})) ||
+      (rc = need_t(d, "embeddings.position_embeddings.weight", &p, {})) ||
+      (rc = need_t(d, "embeddings.LayerNorm.weight", &g, {H})) ||
+      (rc = need_t(d, "embeddings.LayerNorm.bias", &b, {H})))
+    return rc;
+  if (w->shape.size() != 2 || w->shape[1] != H || p->shape.size() != 2 || p->shape[1] != H)
+    return set_error(EC_EINVAL, "embedding tables must be [*, %d]", H);
+  m.word = w->p;
+  m.word_dt = w->dtype;
+  m.vocab = static_cast<int>(w->shape[0]);
+  m.pos = p->p;
+  m.pos_dt = p->dtype;
+  m.max_pos = static_cast<int>(p->shape[0]);
+  if (!mpnet) {
+    ty = find_t(d, "embeddings.token_type_embeddings.weight");  // bert.lisp:87-89
+    if (ty) {
+      m.type0 = ty->p;
+      m.type_dt = ty->dtype;
+    }
+  }
+  if ((rc = as_f32(d, g, &m.emb_g)) || (rc = as_f32(d, b, &m.emb_b))) return rc;
+  if (mpnet) {
+    const Tensor* rb;
+    if ((rc = need_t(d, "encoder.relative_attention_bias.weight", &rb, {32, m.heads}))) return rc;
+    // table over i - j in [-(rel_max-1), rel_max-1], pre-multiplied by log2(e)
+    m.rel_max = 1024;
+    const int nb = 2 * m.rel_max - 1;
+    std::vector<float> rbh(rb->numel);
+    if (rb->dtype == kDtF32) {
+      if ((rc = check_cuda(cudaMemcpy(rbh.data(), rb->p, rb->numel * 4, cudaMemcpyDeviceToHost),
+                           "rel bias read")))
+        return rc;
+    } else {
+      std::vector<uint16_t> raw(rb->numel);
+      if ((rc = check_cuda(cudaMemcpy(raw.data(), rb->p, rb->numel * 2, cudaMemcpyDeviceToHost),
+                           "rel bias read")))
+        return rc;
+      for (size_t i = 0; i < raw.size(); ++i) {
+        uint32_t u = static_cast<uint32_t>(raw[i]) << 16;
+        std::memcpy(&rbh[i], &u, 4);
+      }
+    }
+    std::vector<float> tab(static_cast<size_t>(m.heads) * nb);
+    for (int dlt = -(m.rel_max - 1); dlt <= m.rel_max - 1; ++dlt) {
+      const int bk = mpnet_bucket(dlt, 0);
+      for (int h = 0; h < m.heads; ++h)
+        tab[static_cast<size_t>(h) * nb + dlt + m.rel_max - 1] =
+            rbh[static_cast<size_t>(bk) * m.heads + h] * 1.4426950408889634f;
+    }
+    void* dp;
+    if ((rc = model_alloc(d, &dp, tab.size() * 4, "rel bias table"))) return rc;
+    if ((rc = check_cuda(cudaMemcpyAsync(dp, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice,
+                                         d.stream),
+                         "rel bias upload")))
+      return rc;
+    m.relbias = static_cast<float*>(dp);
+    // the table must outlive the async copy of `tab`
+    if ((rc = check_cuda(cudaStreamSynchronize(d.stream), "rel bias sync"))) return rc;
+  }
+  m.bl.resize(m.layers);
+  for (int li = 0; li < m.layers; ++li) {
+    const std::string pf = "encoder.layer." + std::to_string(li) + ".";
+    BertLayerW& L = m.bl[li];
+    const Tensor *qw, *qb, *kw, *kb, *vw, *vb, *ow, *ob, *l1g, *l1b, *fw, *fb, *dw, *db, *l2g,
+        *l2b;
+    const std::string a = mpnet ? "attention.attn." : "attention.self.";
+    const std::string qn = mpnet ? "q" : "query", kn = mpnet ? "k" : "key",
+                      vn = mpnet ? "v" : "value";
+    const std::string on = mpnet ? "attention.attn.o." : "attention.output.dense.";
+    const std::string l1 = mpnet ? "attention.LayerNorm." : "attention.output.LayerNorm.";
+    if ((rc = need_t(d, pf + a + qn + ".weight", &qw, {H, H})) ||
+        (rc = need_t(d, pf + a + qn + ".bias", &qb, {H})) ||
+        (rc = need_t(d, pf + a + kn + ".weight", &kw, {H, H})) ||
+        (rc = need_t(d, pf + a + kn + ".bias", &kb, {H})) ||
+        (rc = need_t(d, pf + a + vn + ".weight", &vw, {H, H})) ||
+        (rc = need_t(d, pf + a + vn + ".bias", &vb, {H})) ||
+        (rc = need_t(d, pf + on + "weight", &ow, {H, H})) ||
+        (rc = need_t(d, pf + on + "bias", &ob, {H})) ||
+        (rc = need_t(d, pf + l1 + "weight", &l1g, {H})) ||
+        (rc = need_t(d, pf + l1 + "bias", &l1b, {H})) ||
+        (rc = need_t(d, pf + "intermediate.dense.weight", &fw, {F, H})) ||
+        (rc = need_t(d, pf + "intermediate.dense.bias", &fb, {F})) ||
+        (rc = need_t(d, pf + "output.dense.weight", &dw, {H, F})) ||
+        (rc = need_t(d, pf + "output.dense.bias", &db, {H})) ||
+        (rc = need_t(d, pf + "output.LayerNorm.weight", &l2g, {H})) ||
+        (rc = need_t(d, pf + "output.LayerNorm.bias", &l2b, {H})))
+      return rc;
+    if ((rc = concat_bf16(d, {qw, kw, vw}, H, &L.wqkv)) ||
+        (rc = concat_f32(d, {qb, kb, vb}, &L.bqkv)) || (rc = concat_bf16(d, {ow}, H, &L.wo)) ||
+        (rc = as_f32(d, ob, &L.bo)) || (rc = as_f32(d, l1g, &L.ln1g)) ||
+        (rc = as_f32(d, l1b, &L.ln1b)) || (rc = concat_bf16(d, {fw}, H, &L.wff)) ||
+        (rc = as_f32(d, fb, &L.bff)) || (rc = concat_bf16(d, {dw}, F, &L.wout)) ||
+        (rc = as_f32(d, db, &L.bout)) || (rc = as_f32(d, l2g, &L.ln2g)) ||
+        (rc = as_f32(d, l2b, &L.ln2b)))
+      return rc;
+  }
+  return EC_OK;
+}
+
+static int load_llama(Device& d, const JVal& cfg) {
+  ModelW& m = d.model;
+  int rc;
+  if ((rc = cfg_int(cfg, "hidden_size", &m.H)) || (rc = cfg_int(cfg, "num_hidden_layers", &m.layers)) ||
+      (rc = cfg_int(cfg, "num_attention_heads", &m.heads)) ||
+      (rc = cfg_int(cfg, "intermediate_size", &m.F)))
+    return rc;
+  if ((rc = cfg_int(cfg, "num_key_value_heads", &m.kv_heads, false, m.heads))) return rc;
+  if ((rc = cfg_int(cfg, "head_dim", &m.hd, false, m.heads ? m.H / m.heads : 0))) return rc;
+  const JVal* th = cfg.get("rope_theta");
+  m.theta = (th && th->is_num()) ? th->num() : 10000.0;   // llama.lisp:184
+  const JVal* ep = cfg.get("rms_norm_eps");
+  m.eps = (ep && ep->is_num()) ? ep->num() : 1e-6;        // llama.lisp:185
+  m.family = EC_FAMILY_LLAMA;
+  m.pooling = 2;      // llama::*pooling* :last (llama.lisp:19)
+  m.max_pos = 1024;   // llama::*max-pos* (llama.lisp:21)
+  if (m.hd != 128) return set_error(EC_EUNSUPPORTED, "llama head_dim %d (supported: 128)", m.hd);
+  if (m.kv_heads <= 0 || m.heads % m.kv_heads)
+    return set_error(EC_EINVAL, "heads %d not a multiple of kv heads %d", m.heads, m.kv_heads);
+  if (m.H % 128 || m.H > 2048 || m.F % 128)
+    return set_error(EC_EUNSUPPORTED, "hidden %d / ffn %d outside this build", m.H, m.F);
+  const int H = m.H, F = m.F, qd = m.heads * m.hd, kvd = m.kv_heads * m.hd;
+  const Tensor *emb, *nw;
+  if ((rc = need_t(d, "embed_tokens.weight", &emb, {})) || (rc = need_t(d, "norm.weight", &nw, {H})))
+    return rc;
+  if (emb->shape.size() != 2 || emb->shape[1] != H)
+    return set_error(EC_EINVAL, "embed_tokens must be [*, %d]", H);
+  m.word = emb->p;
+  m.word_dt = emb->dtype;
+  m.vocab = static_cast<int>(emb->shape[0]);
+  if ((rc = as_f32(d, nw, &m.final_norm))) return rc;
+  // init-rope (llama.lisp:124-135): double table rounded to single
+  const int half = m.hd / 2;
+  std::vector<float> cs(static_cast<size_t>(m.max_pos) * half), sn(cs.size());
+  for (int p = 0; p < m.max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double freq = 1.0 / std::pow(m.theta, (2.0 * i) / m.hd);
+      const double ang = p * freq;
+      cs[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(ang));
+      sn[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(ang));
+    }
+  void *dc, *ds;
+  if ((rc = model_alloc(d, &dc, cs.size() * 4, "rope cos")) ||
+      (rc = model_alloc(d, &ds, sn.size() * 4, "rope sin")))
+    return rc;
+  if ((rc = check_cuda(cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope")) ||
+      (rc = check_cuda(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope")))
+    return rc;
+  m.cos_t = static_cast<float*>(dc);
+  m.sin_t = static_cast<float*>(ds);
+  m.ll.resize(m.layers);
+  for (int li = 0; li < m.layers; ++li) {
+    const std::string pf = "layers." + std::to_string(li) + ".";
+    LlamaLayerW& L = m.ll[li];
+    const Tensor *in, *post, *qw, *kw, *vw, *ow, *gw, *uw, *dw;
+    if ((rc = need_t(d, pf + "input_layernorm.weight", &in, {H})) ||
+        (rc = need_t(d, pf + "post_attention_layernorm.weight", &post, {H})) ||
+        (rc = need_t(d, pf + "self_attn.q_proj.weight", &qw, {qd, H})) ||
+        (rc = need_t(d, pf + "self_attn.k_proj.weight", &kw, {kvd, H})) ||
+        (rc = need_t(d, pf + "self_attn.v_proj.weight", &vw, {kvd, H})) ||
+        (rc = need_t(d, pf + "self_attn.o_proj.weight", &ow, {H, qd})) ||
+        (rc = need_t(d, pf + "mlp.gate_proj.weight", &gw, {F, H})) ||
+        (rc = need_t(d, pf + "mlp.up_proj.weight", &uw, {F, H})) ||
+        (rc = need_t(d, pf + "mlp.down_proj.weight", &dw, {H, F})))
+      return rc;
+    const Tensor* qn = find_t(d, pf + "self_attn.q_norm.weight");  // get-tensor-opt
+    const Tensor* kn = find_t(d, pf + "self_attn.k_norm.weight");
+    if ((rc = as_f32(d, in, &L.in_ln)) || (rc = as_f32(d, post, &L.post_ln)) ||
+        (rc = concat_bf16(d, {qw, kw, vw}, H, &L.wqkv)) || (rc = concat_bf16(d, {ow}, qd, &L.wo)) ||
+        (rc = concat_bf16(d, {dw}, F, &L.wdown)))
+      return rc;
+    if (qn && (rc = as_f32(d, qn, &L.q_norm))) return rc;
+    if (kn && (rc = as_f32(d, kn, &L.k_norm))) return rc;
+    // gate/up interleaved in blocks of 128 rows: [g0 u0 g1 u1 ...], the
+    // layout the SwiGLU epilogue of a 256-wide tile expects
+    void* p;
+    if ((rc = model_alloc(d, &p, static_cast<size_t>(2) * F * H * 2, "gate/up"))) return rc;
+    bf16* gu = static_cast<bf16*>(p);
+    for (int b = 0; b < F / 128; ++b) {
+      if ((rc = rows_to_bf16(d, gw, b * 128, 128, H, gu + static_cast<size_t>(2 * b) * 128 * H)) ||
+          (rc = rows_to_bf16(d, uw, b * 128, 128, H,
+                             gu + static_cast<size_t>(2 * b + 1) * 128 * H)))
+        return rc;
+    }
+    L.wgu = gu;
+  }
+  return EC_OK;
+}
+
+int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
+  free_model(d);
+  // the workspace is laid out for a model; a new model starts from scratch
+  if (d.ws) {
+    cudaStreamSynchronize(d.stream);
+    dev_free(d, d.ws, d.ws_bytes);
+    d.ws = nullptr;
+  }
+  d.ws_bytes = 0;
+  d.ws_tokens = 0;
+  d.ws_seqs = 0;
+  const JVal* tc = cfg.get("text_config");
+  std::string mt;
+  if (tc && tc->kind == JVal::Obj && tc->get("model_type") && tc->get("model_type")->kind == JVal::Str)
+    mt = tc->get("model_type")->s;  // model.lisp:20-26
+  else if (cfg.get("model_type") && cfg.get("model_type")->kind == JVal::Str)
+    mt = cfg.get("model_type")->s;
+  if (mt.empty()) return set_error(EC_EINVAL, "no config.json model_type");
+  int rc;
+  if (mt == "bert" || mt == "roberta" || mt == "distilbert" || mt == "mpnet") {
+    int pooling = 0;  // :cls unless pooling_mode_mean_tokens (bert.lisp:76-78)
+    if (pool && pool->get("pooling_mode_mean_tokens") &&
+        pool->get("pooling_mode_mean_tokens")->truthy())
+      pooling = 1;
+    rc = load_bert(d, cfg, mt, pooling);
+  } else if (mt == "llama" || mt == "qwen2" || mt == "qwen3" || mt == "mistral" || mt == "gemma" ||
+             mt == "gemma2") {
+    rc = load_llama(d, cfg);
+  } else if (mt == "embedding_gemma2" || mt == "embedding_gemma2_text") {
+    rc = set_error(EC_EUNSUPPORTED, "model_type %s is not built in this library", mt.c_str());
+  } else {
+    rc = set_error(EC_EUNSUPPORTED, "unsupported model_type %s", mt.c_str());
+  }
+  if (rc == EC_OK) rc = sync_and_check(d, "model assembly");
+  if (rc != EC_OK) free_model(d);
+  return rc;
+}
+
+// --------------------------------------------------------------- forward --
+struct WsLayout {
+  size_t ids, pos, cu, blocks, h32, tmp, hb, qkv, ctx, ff, out, total;
+};
+
+static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
+  WsLayout L;
+  const size_t nqkv = static_cast<size_t>(m.heads + 2 * m.kv_heads) * m.hd;
+  const size_t nctx = static_cast<size_t>(m.heads) * m.hd;
+  const size_t nblk = T / 64 + nseq + 1;
+  size_t o = 0;
+  L.ids = o; o += al256(T * 4);
+  L.pos = o; o += al256(T * 4);
+  L.cu = o; o += al256((nseq + 1) * 4);
+  L.blocks = o; o += al256(nblk * 8);
+  L.h32 = o; o += al256(T * m.H * 4);
+  L.tmp = o; o += al256(T * m.H * 4);
+  L.hb = o; o += al256(T * m.H * 2);
+  L.qkv = o; o += al256(T * nqkv * 2);
+  L.ctx = o; o += al256(T * nctx * 2);
+  L.ff = o; o += al256(T * m.F * 2);
+  L.out = o; o += al256(nseq * m.H * 4);
+  L.total = o;
+  return L;
+}
+
+static int ensure_ws(Device& d, int T, int nseq) {
+  // the layout depends on the model (hidden, qkv, ffn widths), so size by
+  // bytes, not only by token / sequence counts
+  const int t2 = std::max(T, d.ws_tokens), s2 = std::max(nseq, d.ws_seqs);
+  const WsLayout L = layout_for(d.model, t2, s2);
+  const size_t pin = static_cast<size_t>(t2) * 4 + (static_cast<size_t>(s2) + 1) * 4 +
+                     (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
+                     static_cast<size_t>(s2) * d.model.H * 4 + 1024;
+  if (!d.ws || L.total > d.ws_bytes) {
+    if (d.ws) {
+      cudaStreamSynchronize(d.stream);
+      dev_free(d, d.ws, d.ws_bytes);
+      d.ws = nullptr;
+      d.ws_bytes = 0;
+    }
+    int rc = dev_alloc(d, &d.ws, L.total, "forward workspace");
+    if (rc) return rc;
+    d.ws_bytes = L.total;
+  }
+  d.ws_tokens = t2;
+  d.ws_seqs = s2;
+  if (pin > d.pin_bytes) {
+    if (d.pin) {
+      cudaStreamSynchronize(d.stream);
+      cudaFreeHost(d.pin);
+    }
+    d.pin = nullptr;
+    d.pin_bytes = 0;
+    if (cudaHostAlloc(&d.pin, pin, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(EC_ENOMEM, "pinned staging of %zu bytes failed", pin);
+    }
+    d.pin_bytes = pin;
+  }
+  return EC_OK;
+}
+
+#define EC_TRY(expr)              \
+  do {                            \
+    int rc_ = (expr);             \
+    if (rc_ != EC_OK) return rc_; \
+  } while (0)
+
+// Run the forward for sequences seqs[s0..s1) (indices into offsets) that are
+// packed in `ids_dev` (already on the device) and write pooled rows to out.
+static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nblk,
+                          double attn_pairs, float* out, int out_stride) {
+  ModelW& m = d.model;
+  char* ws = static_cast<char*>(d.ws);
+  int* ids = reinterpret_cast<int*>(ws + L.ids);
+  int* pos = reinterpret_cast<int*>(ws + L.pos);
+  int* cu = reinterpret_cast<int*>(ws + L.cu);
+  int2* blocks = reinterpret_cast<int2*>(ws + L.blocks);
+  float* h32 = reinterpret_cast<float*>(ws + L.h32);
+  float* tmp = reinterpret_cast<float*>(ws + L.tmp);
+  bf16* hb = reinterpret_cast<bf16*>(ws + L.hb);
+  bf16* qkv = reinterpret_cast<bf16*>(ws + L.qkv);
+  bf16* ctx = reinterpret_cast<bf16*>(ws + L.ctx);
+  bf16* ff = reinterpret_cast<bf16*>(ws + L.ff);
+  cudaStream_t st = d.stream;
+  const int H = m.H, F = m.F;
+  const int nqkv = (m.heads + 2 * m.kv_heads) * m.hd, nctx = m.heads * m.hd;
+
+  // every launch is bracketed by prof_begin / prof_end (events only while
+  // profiling): class 0 gemm, 1 attention, 2 row kernels
+  auto rows = [&](cudaError_t e, const char* what, double bytes, int e0) -> int {
+    prof_end(d, 2, 0.0, bytes, e0);
+    return check_cuda(e, what);
+  };
+  const double TH = static_cast<double>(T) * H;
+  {
+    const int e0 = prof_begin(d);
+    EC_TRY(rows(launch_positions(cu, nseq, pos, st), "positions", T * 4.0, e0));
+  }
+
+  auto gemm = [&](const bf16* A, int lda, const bf16* W, int N, int K, const float* bias,
+                  const float* resid, void* o, int ldo, int epi) -> int {
+    GemmLaunch g;
+    g.A = A;
+    g.lda = lda;
+    g.W = W;
+    g.ldw = K;
+    g.M = T;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.resid = resid;
+    g.ldr = H;
+    g.out = o;
+    g.ldo = ldo;
+    g.epi = epi;
+    g.bn = 0;
+    g.status = d.status;
+    const double out_b = epi == kEpiF32Resid || epi == kEpiF32 ? 4.0 * T * N
+                         : epi == kEpiBf16Swiglu              ? 1.0 * T * N
+                                                              : 2.0 * T * N;
+    const double bytes = 2.0 * T * K + 2.0 * N * K + out_b + (resid ? 4.0 * T * N : 0.0);
+    const int e0 = prof_begin(d);
+    const cudaError_t e = launch_gemm(g, st, d.num_sms);
+    prof_end(d, 0, 2.0 * T * N * K, bytes, e0);
+    return check_cuda(e, "gemm");
+  };
+  AttnLaunch at;
+  at.qkv = qkv;
+  at.ld = nqkv;
+  at.q_off = 0;
+  at.k_off = m.heads * m.hd;
+  at.v_off = (m.heads + m.kv_heads) * m.hd;
+  at.out = ctx;
+  at.ldo = nctx;
+  at.cu = cu;
+  at.blocks = blocks;
+  at.nblocks = nblk;
+  at.heads = m.heads;
+  at.kv_group = m.heads / m.kv_heads;
+  at.head_dim = m.hd;
+  at.causal = m.family == EC_FAMILY_LLAMA ? 1 : 0;
+  at.relbias = m.relbias;
+  at.rel_max = m.rel_max;
+  auto attention = [&]() -> int {
+    const int e0 = prof_begin(d);
+    const cudaError_t e = launch_attention(at, st);
+    prof_end(d, 1, attn_pairs * 4.0 * m.heads * m.hd, 2.0 * T * (nqkv + nctx), e0);
+    return check_cuda(e, "attention");
+  };
+
+  if (m.family == EC_FAMILY_BERT || m.family == EC_FAMILY_MPNET) {
+    EmbedLnArgs e;
+    e.ids = ids;
+    e.pos = pos;
+    e.pos_offset = m.pos_offset;
+    e.word = m.word;
+    e.word_dtype = m.word_dt;
+    e.posemb = m.pos;
+    e.pos_dtype = m.pos_dt;
+    e.type0 = m.family == EC_FAMILY_BERT ? m.type0 : nullptr;
+    e.type_dtype = m.type_dt;
+    e.g = m.emb_g;
+    e.b = m.emb_b;
+    e.out32 = h32;
+    e.outb = hb;
+    e.T = T;
+    e.H = H;
+    {
+      const int e0 = prof_begin(d);
+      EC_TRY(rows(launch_embed_ln(e, st), "embed", TH * (8.0 + 6.0), e0));
+    }
+    for (int li = 0; li < m.layers; ++li) {
+      const BertLayerW& w = m.bl[li];
+      EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, w.bqkv, nullptr, qkv, nqkv, kEpiBf16));
+      EC_TRY(attention());
+      EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, w.bo, h32, tmp, H, kEpiF32Resid));
+      LnArgs l1{tmp, w.ln1g, w.ln1b, h32, hb, T, H};
+      {
+        const int e0 = prof_begin(d);
+        EC_TRY(rows(launch_ln(l1, st), "layernorm", TH * 10.0, e0));
+      }
+      EC_TRY(gemm(hb, H, w.wff, F, H, w.bff, nullptr, ff, F, kEpiBf16Gelu));
+      EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
+      LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};
+      {
+        const int e0 = prof_begin(d);
+        EC_TRY(rows(launch_ln(l2, st), "layernorm", TH * 10.0, e0));
+      }
+    }
+    PoolArgs pa;
+    pa.h = h32;
+    pa.cu = cu;
+    pa.mode = m.pooling;
+    pa.final_norm = 0;
+    pa.norm_w = nullptr;
+    pa.eps = 0.0;
+    pa.out = out;
+    pa.out_stride = out_stride;
+    pa.H = H;
+    {
+      const int e0 = prof_begin(d);
+      EC_TRY(rows(launch_pool_l2(pa, nseq, st), "pool",
+                  (m.pooling == 1 ? TH : static_cast<double>(nseq) * H) * 4.0, e0));
+    }
+    return EC_OK;
+  }
+  // llama family: h = embed_tokens[ids] (llama.lisp:316-320)
+  {
+    const int e0 = prof_begin(d);
+    EC_TRY(rows(launch_gather_rows(m.word, m.word_dt, ids, h32, T, H, st), "gather",
+                TH * (m.word_dt == kDtBf16 ? 6.0 : 8.0), e0));
+  }
+  for (int li = 0; li < m.layers; ++li) {
+    const LlamaLayerW& w = m.ll[li];
+    RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};
+    {
+      const int e0 = prof_begin(d);
+      EC_TRY(rows(launch_rmsnorm(r1, st), "rmsnorm", TH * 6.0, e0));
+    }
+    EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16));
+    QkRopeArgs q;
+    q.qkv = qkv;
+    q.ld = nqkv;
+    q.q_off = 0;
+    q.k_off = m.heads * m.hd;
+    q.q_heads = m.heads;
+    q.k_heads = m.kv_heads;
+    q.q_norm = w.q_norm;
+    q.k_norm = w.k_norm;
+    q.eps = m.eps;
+    q.pos = pos;
+    q.cos_t = m.cos_t;
+    q.sin_t = m.sin_t;
+    q.T = T;
+    {
+      const int e0 = prof_begin(d);
+      EC_TRY(rows(launch_qk_norm_rope(q, st), "qk norm rope",
+                  4.0 * T * (m.heads + m.kv_heads) * m.hd, e0));
+    }
+    EC_TRY(attention());
+    EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, h32, h32, H, kEpiF32Resid));
+    RmsArgs r2{h32, nullptr, w.post_ln, m.eps, hb, nullptr, T, H};
+    {
+      const int e0 = prof_begin(d);
+      EC_TRY(rows(launch_rmsnorm(r2, st), "rmsnorm", TH * 6.0, e0));
+    }
+    EC_TRY(gemm(hb, H, w.wgu, 2 * F, H, nullptr, nullptr, ff, F, kEpiBf16Swiglu));
+    EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, h32, h32, H, kEpiF32Resid));
+  }
+  PoolArgs pa;
+  pa.h = h32;
+  pa.cu = cu;
+  pa.mode = m.pooling;
+  pa.final_norm = 1;
+  pa.norm_w = m.final_norm;
+  pa.eps = m.eps;
+  pa.out = out;
+  pa.out_stride = out_stride;
+  pa.H = H;
+  {
+    const int e0 = prof_begin(d);
+    EC_TRY(rows(launch_pool_l2(pa, nseq, st), "pool", static_cast<double>(nseq) * H * 4.0, e0));
+  }
+  return EC_OK;
+}
+
+// Build the per-chunk host tables (cu offsets, attention blocks sorted by
+// descending length) into pinned staging and upload them.
+static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, int* nblk_out) {
+  const int nseq = static_cast<int>(lens.size());
+  char* pin = static_cast<char*>(d.pin);
+  int* hcu = reinterpret_cast<int*>(pin);
+  int2* hblk = reinterpret_cast<int2*>(pin + al256((nseq + 1) * 4));
+  hcu[0] = 0;
+  for (int i = 0; i < nseq; ++i) hcu[i + 1] = hcu[i] + lens[i];
+  std::vector<int> order(nseq);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens[a] > lens[b]; });
+  int nb = 0;
+  for (int s : order)
+    for (int q0 = 0; q0 < lens[s]; q0 += 64) hblk[nb++] = make_int2(s, q0);
+  char* ws = static_cast<char*>(d.ws);
+  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.cu, hcu, (nseq + 1) * 4, cudaMemcpyHostToDevice, d.stream),
+                    "cu upload"));
+  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks, hblk, static_cast<size_t>(nb) * 8,
+                                    cudaMemcpyHostToDevice, d.stream),
+                    "block upload"));
+  *nblk_out = nb;
+  return EC_OK;
+}
+
+int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
+                    const std::vector<int>& seqs, const int64_t* offsets, float* out_host,
+                    int out_stride, float* out_dev) {
+  ModelW& m = d.model;
+  if (!m.family) return set_error(EC_ESTATE, "no model loaded");
+  EC_TRY(check_cuda(cudaSetDevice(d.ordinal), "set device"));
+  // validate lengths and ids (host ids only; device ids are trusted)
+  const int maxlen = m.family == EC_FAMILY_LLAMA ? m.max_pos : m.max_pos - m.pos_offset;
+  for (int s : seqs) {
+    const int64_t L = offsets[s + 1] - offsets[s];
+    if (L <= 0) return set_error(EC_EINVAL, "sequence %d is empty", s);
+    if (L > maxlen)
+      return set_error(EC_EINVAL, "sequence %d has %lld tokens, above the %d positions of the model",
+                       s, static_cast<long long>(L), maxlen);
+    if (m.family == EC_FAMILY_MPNET && L > 512)
+      return set_error(EC_EUNSUPPORTED, "MPNet sequence %d longer than 512 tokens", s);
+    if (ids_host)
+      for (int64_t t = offsets[s]; t < offsets[s + 1]; ++t)
+        if (ids_host[t] < 0 || ids_host[t] >= m.vocab)
+          return set_error(EC_EINVAL, "token id %d of sequence %d outside vocab %d", ids_host[t],
+                           s, m.vocab);
+  }
+  size_t i = 0;
+  while (i < seqs.size()) {
+    // chunk: as many sequences as fit the token budget (at least one)
+    size_t j = i;
+    int64_t T = 0;
+    while (j < seqs.size()) {
+      const int64_t L = offsets[seqs[j] + 1] - offsets[seqs[j]];
+      if (j > i && T + L > G().max_tokens) break;
+      T += L;
+      ++j;
+    }
+    if (ids_dev) {
+      // device ids must be one contiguous range of consecutive sequences
+      for (size_t k = i + 1; k < j; ++k)
+        if (seqs[k] != seqs[k - 1] + 1) return set_error(EC_EINVAL, "non-contiguous device chunk");
+    }
+    const int nseq = static_cast<int>(j - i);
+    EC_TRY(ensure_ws(d, static_cast<int>(T), nseq));
+    WsLayout L = layout_for(m, d.ws_tokens, d.ws_seqs);
+    std::vector<int> lens(nseq);
+    for (int k = 0; k < nseq; ++k)
+      lens[k] = static_cast<int>(offsets[seqs[i + k] + 1] - offsets[seqs[i + k]]);
+    int nblk = 0;
+    EC_TRY(upload_tables(d, L, lens, &nblk));
+    char* ws = static_cast<char*>(d.ws);
+    if (ids_dev) {
+      EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, ids_dev + offsets[seqs[i]],
+                                        static_cast<size_t>(T) * 4, cudaMemcpyDeviceToDevice,
+                                        d.stream),
+                        "ids copy"));
+    } else {
+      int* hid = reinterpret_cast<int*>(static_cast<char*>(d.pin) + d.pin_bytes -
+                                        al256(static_cast<size_t>(T) * 4) - 256);
+      // pinned layout: tables at the front, ids at the back
+      int64_t o = 0;
+      for (int k = 0; k < nseq; ++k) {
+        const int s = seqs[i + k];
+        std::memcpy(hid + o, ids_host + offsets[s], static_cast<size_t>(lens[k]) * 4);
+        o += lens[k];
+      }
+      EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, hid, static_cast<size_t>(T) * 4,
+                                        cudaMemcpyHostToDevice, d.stream),
+                        "ids upload"));
+    }
+    float* dout = out_dev ? out_dev + static_cast<size_t>(seqs[i]) * out_stride
+                          : reinterpret_cast<float*>(ws + L.out);
+    const int ostride = out_dev ? out_stride : m.H;
+    double pairs = 0.0;  // (query, key) pairs that attention scores
+    for (int k = 0; k < nseq; ++k)
+      pairs += m.family == EC_FAMILY_LLAMA ? 0.5 * lens[k] * (lens[k] + 1.0)
+                                           : static_cast<double>(lens[k]) * lens[k];
+    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, nblk, pairs, dout, ostride));
+    if (!out_dev) {
+      std::vector<float> hout(static_cast<size_t>(nseq) * m.H);
+      EC_TRY(check_cuda(cudaMemcpyAsync(hout.data(), dout, hout.size() * 4,
+                                        cudaMemcpyDeviceToHost, d.stream),
+                        "output download"));
+      EC_TRY(sync_and_check(d, "forward"));
+      prof_collect(d);
+      for (int k = 0; k < nseq; ++k)
+        std::memcpy(out_host + static_cast<size_t>(seqs[i + k]) * out_stride,
+                    hout.data() + static_cast<size_t>(k) * m.H, static_cast<size_t>(m.H) * 4);
+    } else {
+      EC_TRY(sync_and_check(d, "forward"));
+      prof_collect(d);
+    }
+    i = j;
+  }
+  return EC_OK;
+}
+
+}  // namespace ec

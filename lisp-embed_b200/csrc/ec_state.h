@@ -1,0 +1,154 @@
+// ec_state.h -- library-internal state shared by the host translation units:
+// the per-device context (stream, uploaded tensors, packed model weights,
+// workspace, resident index), error reporting and checked allocation.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/embedcuda.h"
+#include "ec_kernels.h"
+
+namespace ec {
+
+using bf16 = __nv_bfloat16;
+
+struct Tensor {
+  void* p = nullptr;
+  int dtype = kDtF32;  // kDtF32 or kDtBf16 on the device (F16 is widened to F32)
+  std::vector<int64_t> shape;
+  size_t numel = 0;
+};
+
+struct BertLayerW {
+  bf16 *wqkv = nullptr, *wo = nullptr, *wff = nullptr, *wout = nullptr;
+  float *bqkv = nullptr, *bo = nullptr, *ln1g = nullptr, *ln1b = nullptr;
+  float *bff = nullptr, *bout = nullptr, *ln2g = nullptr, *ln2b = nullptr;
+};
+
+struct LlamaLayerW {
+  float *in_ln = nullptr, *post_ln = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  bf16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
+};
+
+struct ModelW {
+  int family = 0;  // EC_FAMILY_*
+  int H = 0, layers = 0, heads = 0, kv_heads = 0, hd = 0, F = 0;
+  int pooling = 0;  // 0 first token, 1 mean, 2 last token
+  int pos_offset = 0, vocab = 0, max_pos = 0;
+  double eps = 1e-6, theta = 10000.0;
+  const void* word = nullptr;
+  int word_dt = kDtF32;
+  const void* pos = nullptr;
+  int pos_dt = kDtF32;
+  const void* type0 = nullptr;
+  int type_dt = kDtF32;
+  float *emb_g = nullptr, *emb_b = nullptr;
+  float* relbias = nullptr;  // MPNet [heads][2 * rel_max - 1] * log2(e)
+  int rel_max = 0;
+  std::vector<BertLayerW> bl;
+  std::vector<LlamaLayerW> ll;
+  float *final_norm = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+  std::vector<void*> owned;
+};
+
+struct IndexW {
+  int64_t n = 0;
+  int d = 0, k = 0;
+  float* x = nullptr;          // [n, d]
+  float* cent = nullptr;       // [k, d]
+  uint32_t* lists = nullptr;   // [n]
+  int64_t* offs = nullptr;     // [k + 1]
+  std::vector<int64_t> h_offs; // host copy
+  std::vector<void*> owned;
+  void* sws = nullptr;         // search workspace
+  size_t sws_bytes = 0;
+};
+
+struct ProfAcc {
+  double ms = 0, flops = 0, bytes = 0;
+  long long launches = 0;
+};
+
+struct PendingEv {
+  int cls;  // 0 gemm, 1 attention, 2 rows
+  double flops, bytes;
+  int e0, e1;
+};
+
+struct Device {
+  int ordinal = 0;
+  std::vector<cudaEvent_t> evpool;  // profiling events, reused
+  std::vector<PendingEv> pend;      // launches awaiting their elapsed time
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  std::map<std::string, Tensor> uploads;
+  ModelW model;
+  IndexW index;
+  unsigned* status = nullptr;  // device status word of bounded waits
+  // forward workspace
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  int ws_tokens = 0, ws_seqs = 0;
+  // pinned host staging
+  void* pin = nullptr;
+  size_t pin_bytes = 0;
+  size_t allocated = 0;
+};
+
+struct Global {
+  std::mutex mu;
+  std::vector<Device*> devs;
+  bool inited = false;
+  size_t max_bytes = 0;  // EC_MAX_BYTES (0 = unlimited), per device
+  int max_tokens = 262144;
+  // profiling of the forward (ecdbg_profile)
+  bool profile = false;
+  ProfAcc prof[3];
+  long long launches = 0;
+  // multi-process communicator
+  void* comm = nullptr;
+  int rank = 0, world = 1;
+};
+
+Global& G();
+
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+
+// checked device allocation on the current device (honours EC_MAX_BYTES)
+int dev_alloc(Device& d, void** p, size_t bytes, const char* what);
+void dev_free(Device& d, void* p, size_t bytes);
+
+int check_cuda(cudaError_t e, const char* what);
+// synchronise d.stream and translate both CUDA errors and the device status
+// word (bounded-wait timeouts) into a status code
+int sync_and_check(Device& d, const char* what);
+
+struct JVal;
+// build the model of config.json (+ pooling config) from d.uploads
+int load_model_on(Device& d, const JVal& cfg, const JVal* pool);
+
+// forward entry used by ec_embed_batch / ec_embed_batch_device
+int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
+                    const std::vector<int>& seqs, const int64_t* offsets, float* out_host,
+                    int out_stride, float* out_dev);
+
+// profiling helpers: bracket one launch with events (no-op unless profiling)
+int prof_begin(Device& d);
+void prof_end(Device& d, int cls, double flops, double bytes, int e0);
+// fold finished events of d into G().prof (call after synchronising d.stream)
+void prof_collect(Device& d);
+
+// model teardown
+void free_model(Device& d);
+void free_index(Device& d);
+
+}  // namespace ec

@@ -1,0 +1,106 @@
+"""IVF index build -- the ann.lisp mirror (ann.lisp:1-200).
+
+``kmeans`` (ann::kmeans), ``assign_all`` (ann::assign-all), ``save_ann`` /
+``load_ann`` (the ann.bin format of ann.lisp:4-6, 165-187) and ``run``.
+The arithmetic runs in libembedcuda.so; ``sample`` is the explicit list of
+training rows whose first k rows initialise the centroids (ann.lisp:83-86).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+
+import numpy as np
+
+from . import _lib
+
+MAGIC = 0x414E4E31  # "ANN1"
+
+
+def kmeans(vecs, sample, k, iters, init=None):
+    """Train k centroids on vecs[sample] (float32[k, dim])."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    sample = np.ascontiguousarray(sample, np.int64)
+    n, d = vecs.shape
+    cent = np.empty((k, d), np.float32)
+    init_p = None
+    if init is not None:
+        init = np.ascontiguousarray(init, np.float32)
+        init_p = _lib.ptr(init, C.c_float)
+    _lib.check(_lib.lib().ec_kmeans(_lib.ptr(vecs, C.c_float), n, d, _lib.ptr(sample, C.c_int64),
+                                    sample.size, k, iters, init_p, _lib.ptr(cent, C.c_float)),
+               "kmeans")
+    return cent
+
+
+def assign(vecs, centroids, rows=None):
+    """Nearest centroid (argmax inner product, ties -> lowest index)."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    n, d = vecs.shape
+    k = centroids.shape[0]
+    rp = None
+    m = n
+    if rows is not None:
+        rows = np.ascontiguousarray(rows, np.int64)
+        rp = _lib.ptr(rows, C.c_int64)
+        m = rows.size
+    out = np.empty(m, np.int32)
+    _lib.check(_lib.lib().ec_assign(_lib.ptr(vecs, C.c_float), n, d, rp, m,
+                                    _lib.ptr(centroids, C.c_float), k, _lib.ptr(out, C.c_int32)),
+               "assign")
+    return out
+
+
+def assign_all(vecs, centroids):
+    """(counts uint32[k], lists uint32[n]) with ascending row ids per list."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    n, d = vecs.shape
+    k = centroids.shape[0]
+    counts = np.empty(k, np.uint32)
+    lists = np.empty(n, np.uint32)
+    _lib.check(_lib.lib().ec_assign_all(_lib.ptr(vecs, C.c_float), n, d,
+                                        _lib.ptr(centroids, C.c_float), k,
+                                        _lib.ptr(counts, C.c_uint32), _lib.ptr(lists, C.c_uint32)),
+               "assign_all")
+    return counts, lists
+
+
+def save_ann(path, centroids, counts, lists, n):
+    """ann.bin: u32 magic, k, dim, n; k*dim f32; k u32 counts; n u32 ids."""
+    k, d = centroids.shape
+    with open(path, "wb") as f:
+        f.write(struct.pack("<4I", MAGIC, k, d, n))
+        f.write(np.ascontiguousarray(centroids, "<f4").tobytes())
+        f.write(np.ascontiguousarray(counts, "<u4").tobytes())
+        f.write(np.ascontiguousarray(lists, "<u4").tobytes())
+
+
+def load_ann(path):
+    """(centroids, counts, lists) from ann.bin, or None when the magic differs
+    (kb::load-ann, kb.lisp:283-314)."""
+    with open(path, "rb") as f:
+        magic, k, d, n = struct.unpack("<4I", f.read(16))
+        if magic != MAGIC:
+            return None
+        cent = np.frombuffer(f.read(4 * k * d), "<f4").reshape(k, d).copy()
+        counts = np.frombuffer(f.read(4 * k), "<u4").copy()
+        lists = np.frombuffer(f.read(4 * n), "<u4").copy()
+    return cent, counts, lists
+
+
+def run(vecs, k=1024, iters=10, sample=None, seed=None, out_path=None):
+    """ann:run: k-means on a sample, then assign every row (ann.lisp:189-200).
+    The reference draws the sample with the global random state; here it is
+    explicit (or drawn from `seed`)."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    n = vecs.shape[0]
+    if sample is None:
+        rng = np.random.default_rng(seed)
+        sample = rng.choice(n, size=min(100000, n), replace=False)
+    cent = kmeans(vecs, sample, k, iters)
+    counts, lists = assign_all(vecs, cent)
+    if out_path:
+        save_ann(out_path, cent, counts, lists, n)
+    return cent, counts, lists

@@ -1,0 +1,61 @@
+"""The C ABI without a GPU: the library builds, loads and exports every
+symbol its public headers declare; calls fail cleanly (status + message)
+when no device is present."""
+import ctypes as C
+import os
+import subprocess
+
+import pytest
+
+from conftest import gpu_available
+from embedcuda import _lib
+
+REPO = _lib.REPO
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    declared = _lib.header_symbols(os.path.join(REPO, "include", "embedcuda.h"))
+    declared += _lib.header_symbols(os.path.join(REPO, "include", "embedcuda_debug.h"))
+    assert "ec_embed_batch" in declared and "ec_kmeans" in declared
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    for s in declared:
+        assert hasattr(lib, s)
+
+
+def test_library_is_sm100a_only():
+    out = subprocess.run(["cuobjdump", "--list-elf", _lib.LIB_PATH], capture_output=True,
+                         text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = {ln.split(".")[-2] for ln in out.stdout.splitlines() if ".cubin" in ln}
+    assert arches == {"sm_100a"}, arches
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks the no-device path")
+def test_calls_fail_cleanly_without_device():
+    lib = _lib.lib()
+    rc = lib.ec_init(None, 0)
+    assert rc in (_lib.EC_ECUDA, _lib.EC_EUNSUPPORTED)
+    assert _lib.last_error()
+    # everything else reports "ec_init first"
+    assert lib.ec_dim() == _lib.EC_ESTATE
+    assert lib.ec_embed_batch(None, None, 0, None, 0) == _lib.EC_ESTATE
+    assert "ec_init" in _lib.last_error()
+    shape = (C.c_int64 * 1)(4)
+    assert lib.ec_upload_tensor(b"x", _lib.EC_F32, shape, 1, None, 16) == _lib.EC_ESTATE
+    assert lib.ec_comm_id_size() == 128
+
+
+def test_header_declares_status_codes():
+    with open(os.path.join(REPO, "include", "embedcuda.h")) as f:
+        src = f.read()
+    for name, val in [("EC_OK", 0), ("EC_EINVAL", -1), ("EC_ESTATE", -2), ("EC_ECUDA", -3),
+                      ("EC_ENOMEM", -4), ("EC_ETIMEOUT", -5), ("EC_ENCCL", -6),
+                      ("EC_EUNSUPPORTED", -7)]:
+        assert f"#define {name} " in src
+        assert getattr(_lib, name) == val

@@ -1,0 +1,114 @@
+"""Kernel-level checks of the tcgen05 GEMM and the varlen attention against
+a plain PyTorch fp32 reference of the same op (bf16 inputs)."""
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _gemm(ec, A, W, bias, resid, epi, bn, out_cols, out_dtype):
+    M, K = A.shape
+    N = W.shape[0]
+    out = torch.empty((M, out_cols), dtype=out_dtype, device="cuda")
+    torch.cuda.synchronize()
+    ec.check(ec.lib().ecdbg_gemm(A.data_ptr(), W.data_ptr(), M, N, K,
+                                 bias.data_ptr() if bias is not None else None,
+                                 resid.data_ptr() if resid is not None else None,
+                                 out.data_ptr(), epi, bn), "gemm")
+    return out
+
+
+def _gelu_as(x):
+    # bert::gelu with the A&S erf (bert.lisp:176-192); |erf err| < 1.5e-7
+    return 0.5 * x * (1.0 + torch.erf(x / math.sqrt(2.0)))
+
+
+@pytest.mark.parametrize("M,N,K,bn", [
+    (1, 384, 384, 0), (127, 1152, 384, 192), (128, 1152, 384, 128), (300, 1536, 384, 256),
+    (4101, 384, 1536, 192), (777, 2304, 768, 256), (2048, 768, 3072, 0), (513, 1024, 2048, 128),
+    (64, 256, 64, 64),
+])
+@pytest.mark.parametrize("epi", [0, 1, 2, 4])
+def test_gemm_epilogues(ec, M, N, K, bn, epi):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    ref = A.float() @ W.float().t() + bias
+    if epi in (0, 1):
+        out = _gemm(ec, A, W, bias, None, epi, bn, N, torch.bfloat16).float()
+        if epi == 1:
+            ref = _gelu_as(ref)
+        tol = 1e-2
+    else:
+        resid = torch.randn(M, N, device="cuda", generator=g) if epi == 2 else None
+        if resid is not None:
+            ref = ref + resid
+        out = _gemm(ec, A, W, bias, resid, epi, bn, N, torch.float32)
+        tol = 1e-4
+    err = (out - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
+    assert err < tol, f"rel err {err}"
+
+
+@pytest.mark.parametrize("M,F", [(1, 3072), (300, 3072), (1029, 1536)])
+def test_gemm_swiglu(ec, M, F):
+    K = 1024
+    g = torch.Generator(device="cuda").manual_seed(M + F)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    Wg = (0.03 * torch.randn(F, K, device="cuda", generator=g)).bfloat16()
+    Wu = (0.03 * torch.randn(F, K, device="cuda", generator=g)).bfloat16()
+    # block-interleave 128 rows of gate, 128 rows of up (256-wide tiles)
+    W = torch.stack([Wg.view(F // 128, 128, K), Wu.view(F // 128, 128, K)], 1).reshape(2 * F, K)
+    out = _gemm(ec, A, W.contiguous(), None, None, 3, 256, F, torch.bfloat16).float()
+    gg = A.float() @ Wg.float().t()
+    uu = A.float() @ Wu.float().t()
+    ref = gg / (1 + torch.exp(-gg)) * uu
+    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+def _attn_ref(qkv, lens, heads, kv_heads, hd, q_off, k_off, v_off, causal):
+    outs = []
+    o = 0
+    group = heads // kv_heads
+    for L in lens:
+        x = qkv[o:o + L].float()
+        q = x[:, q_off:q_off + heads * hd].view(L, heads, hd).transpose(0, 1)
+        k = x[:, k_off:k_off + kv_heads * hd].view(L, kv_heads, hd).transpose(0, 1)
+        v = x[:, v_off:v_off + kv_heads * hd].view(L, kv_heads, hd).transpose(0, 1)
+        k = k.repeat_interleave(group, 0)
+        v = v.repeat_interleave(group, 0)
+        s = q @ k.transpose(1, 2) / math.sqrt(hd)
+        if causal:
+            s = s.masked_fill(torch.triu(torch.ones(L, L, device=s.device, dtype=torch.bool), 1),
+                              float("-inf"))
+        p = torch.softmax(s, -1)
+        outs.append((p @ v).transpose(0, 1).reshape(L, heads * hd))
+        o += L
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize("hd,heads,kv,causal", [(32, 12, 12, 0), (64, 12, 12, 0), (128, 16, 8, 1),
+                                                 (128, 4, 4, 0), (64, 2, 1, 1)])
+def test_attention(ec, hd, heads, kv, causal):
+    lens = [1, 5, 63, 64, 65, 200, 513, 17]
+    T = sum(lens)
+    ld = (heads + 2 * kv) * hd
+    g = torch.Generator(device="cuda").manual_seed(hd + heads)
+    qkv = torch.randn(T, ld, device="cuda", generator=g).bfloat16()
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device="cuda")
+    out = torch.zeros(T, heads * hd, dtype=torch.bfloat16, device="cuda")
+    lens_h = np.asarray(lens, np.int32)
+    torch.cuda.synchronize()
+    import ctypes as C
+    ec.check(ec.lib().ecdbg_attention(qkv.data_ptr(), ld, 0, heads * hd, (heads + kv) * hd,
+                                      out.data_ptr(), C.c_void_p(cu.data_ptr()),
+                                      lens_h.ctypes.data_as(C.POINTER(C.c_int32)), len(lens),
+                                      heads, kv, hd, causal), "attention")
+    ref = _attn_ref(qkv, lens, heads, kv, hd, 0, heads * hd, (heads + kv) * hd, causal)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
