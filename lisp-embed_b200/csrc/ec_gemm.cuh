@@ -7,16 +7,17 @@
 // `linear` computes one token at a time in the reference (bert.lisp:145-153,
 // llama.lisp:97-104); here one launch covers every token of the batch.
 //
-// Structure (192 threads, one CTA per SM, persistent over output tiles):
+// Structure (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      : TMA producer (one elected lane) -- A tile 128x64 and W tile
 //                 BNx64 per stage, 128-byte swizzle, STAGES-deep ring.
 //   warp 1      : TMEM allocator + UMMA issuer (one elected lane):
 //                 tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN, K=16,
 //                 fp32 accumulators in TMEM, double-buffered (2 x BN columns)
 //                 so the epilogue of tile i overlaps the MMAs of tile i+1.
-//   warps 2..5  : epilogue; warp w owns TMEM lanes 32*(w%4).. (= tile rows),
-//                 reads 32 columns at a time with tcgen05.ld, applies the
-//                 epilogue in fp32 and stores with 16-byte vector stores.
+//   warps 2..9  : epilogue; warp w owns TMEM lanes 32*(w%4).. (= tile rows),
+//                 two warps per lane quadrant take alternate 32-column chunks
+//                 (tcgen05.ld), apply the epilogue in fp32 and store with
+//                 16-byte vector stores.
 // All waits are bounded (ec_ptx.cuh); a timeout records a status code,
 // raises the CTA abort flag and every role unwinds, then TMEM is freed.
 #pragma once
@@ -47,7 +48,8 @@ struct GemmArgs {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // 2 control warps + 8 epilogue warps
+constexpr int kGemmEpiWarps = 8;
 
 template <int BN>
 struct GemmCfg {
@@ -60,21 +62,38 @@ struct GemmCfg {
   static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
 };
 
-// GELU with the erf of Abramowitz-Stegun 7.1.26, the form bert::gelu uses
-// (bert.lisp:176-192).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// GELU with the erf of Abramowitz-Stegun 7.1.26 (|error| <= 1.5e-7), the
+// form bert::gelu uses (bert.lisp:176-192).  Branch-free: one approximate
+// reciprocal and one exp2 per element (relative error ~1e-6, far below the
+// bf16 rounding of the result).
 __device__ __forceinline__ float gelu_as(float x) {
   const float z = x * 0.70710678118654752f;
   const float az = fabsf(z);
-  const float t = 1.0f / (1.0f + 0.3275911f * az);
+  const float t = rcp_approx(fmaf(0.3275911f, az, 1.0f));
   const float poly =
       t * (0.254829592f +
            t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
-  float e = 1.0f - poly * __expf(-az * az);
-  e = z < 0.0f ? -e : e;
-  return 0.5f * x * (1.0f + e);
+  const float e = fmaf(-poly, ex2_approx(-1.4426950408889634f * az * az), 1.0f);
+  const float se = copysignf(e, z);
+  const float hx = 0.5f * x;
+  return fmaf(hx, se, hx);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x) (llama::silu, llama.lisp:119-122)
+__device__ __forceinline__ float silu_f(float x) {
+  return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
+}
 
 template <int EPI>
 __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int col0,
@@ -162,7 +181,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kGemmEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -251,8 +270,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..5
+    // epilogue warps 2..9: lane quadrant warp % 4, chunk parity (warp - 2) / 4
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
@@ -269,7 +289,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (EPI == kEpiBf16Swiglu) {
         // gate columns [0, BN/2), up columns [BN/2, BN) of this tile
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(t_row + c * 32, g);
           tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, u);
@@ -293,7 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_wait_ld();
