@@ -1,0 +1,215 @@
+;;;; cuda.lisp -- SBCL bindings of libembedcuda.so (sb-alien only, no new
+;;;; dependencies).  Loaded after st/model/ann/kb, it lets the existing Lisp
+;;;; entry points run on B200s:
+;;;;
+;;;;   (cuda:init)                        ; once, before model:load-model
+;;;;   (cuda:load-model path)             ; instead of the weight reading of
+;;;;                                      ; bert:load-model / llama:load-model
+;;;;   (cuda:embed-ids ids)               ; one sequence of token ids
+;;;;   (cuda:embed-batch list-of-id-vectors)
+;;;;   (cuda:kmeans vecs sample k iters)  ; ann::kmeans
+;;;;   (cuda:assign-all vecs n centroids k)
+;;;;   (cuda:index-load vecs n centroids counts lists)
+;;;;   (cuda:top-k q k)                   ; kb::top-k
+;;;;
+;;;; Every foreign call returns an int status; a negative status becomes a
+;;;; Lisp ERROR carrying ec_last_error(), as st.lisp / model.lisp signal
+;;;; theirs.  Arrays cross the boundary pinned (sb-sys:with-pinned-objects +
+;;;; vector-sap); the library copies what it needs before returning.
+
+(defpackage :cuda
+  (:use :cl)
+  (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
+           #:kmeans #:assign-all #:index-load #:top-k #:top-k-brute #:*nprobe*))
+(in-package :cuda)
+
+(defparameter *library* (or (sb-ext:posix-getenv "EC_LIBRARY") "libembedcuda.so"))
+(defparameter *nprobe* 64)   ; kb::*ann-nprobe*
+(defvar *loaded* nil)
+(defvar *dim* 0)
+(defvar *ivf* nil)
+
+(defun available-p () *loaded*)
+
+;;; ---- raw routines (include/embedcuda.h) ----------------------------------
+
+(sb-alien:define-alien-routine ("ec_last_error" %last-error) sb-alien:c-string)
+(sb-alien:define-alien-routine ("ec_init" %init) sb-alien:int
+  (devices sb-sys:system-area-pointer) (ndev sb-alien:int))
+(sb-alien:define-alien-routine ("ec_upload_tensor" %upload-tensor) sb-alien:int
+  (name sb-alien:c-string) (dtype sb-alien:int) (shape sb-sys:system-area-pointer)
+  (ndim sb-alien:int) (data sb-sys:system-area-pointer) (nbytes sb-alien:unsigned-long))
+(sb-alien:define-alien-routine ("ec_load_model" %load-model) sb-alien:int
+  (config sb-alien:c-string) (pooling sb-alien:c-string)
+  (family sb-sys:system-area-pointer) (dim sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_embed_batch" %embed-batch) sb-alien:int
+  (ids sb-sys:system-area-pointer) (offsets sb-sys:system-area-pointer) (nseq sb-alien:int)
+  (out sb-sys:system-area-pointer) (out-stride sb-alien:int))
+(sb-alien:define-alien-routine ("ec_kmeans" %kmeans) sb-alien:int
+  (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
+  (sample sb-sys:system-area-pointer) (nsample (sb-alien:signed 64)) (k sb-alien:int)
+  (iters sb-alien:int) (init sb-sys:system-area-pointer) (centroids sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_assign_all" %assign-all) sb-alien:int
+  (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
+  (centroids sb-sys:system-area-pointer) (k sb-alien:int)
+  (counts sb-sys:system-area-pointer) (lists sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_index_load" %index-load) sb-alien:int
+  (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
+  (centroids sb-sys:system-area-pointer) (k sb-alien:int)
+  (counts sb-sys:system-area-pointer) (lists sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_ivf_search" %ivf-search) sb-alien:int
+  (q sb-sys:system-area-pointer) (nq sb-alien:int) (nprobe sb-alien:int) (topk sb-alien:int)
+  (ids sb-sys:system-area-pointer) (scores sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_flat_search" %flat-search) sb-alien:int
+  (q sb-sys:system-area-pointer) (nq sb-alien:int) (topk sb-alien:int)
+  (ids sb-sys:system-area-pointer) (scores sb-sys:system-area-pointer))
+
+(defun check (rc what)
+  (when (minusp rc)
+    (error "~A failed (status ~D): ~A" what rc (%last-error)))
+  rc)
+
+(defmacro with-saps (bindings &body body)
+  "Bind each VAR to the SAP of a pinned specialised vector (or a null SAP)."
+  `(sb-sys:with-pinned-objects ,(remove nil (mapcar #'second bindings))
+     (let ,(mapcar (lambda (b)
+                     `(,(first b) (if ,(second b)
+                                      (sb-sys:vector-sap ,(second b))
+                                      (sb-sys:int-sap 0))))
+                   bindings)
+       ,@body)))
+
+;;; ---- context ---------------------------------------------------------------
+
+(defun init (&optional devices)
+  "Load the library and bring up DEVICES (list of CUDA ordinals; NIL = all)."
+  (unless *loaded*
+    (sb-alien:load-shared-object *library*)
+    (let ((dv (and devices (coerce devices '(simple-array (signed-byte 32) (*))))))
+      (with-saps ((p dv))
+        (check (%init p (if dv (length dv) 0)) "ec_init")))
+    (setf *loaded* t))
+  t)
+
+;;; ---- st.lisp: raw tensors straight to the device ---------------------------
+
+(defun dtype-code (s)
+  (cond ((string= s "F32") 0) ((string= s "BF16") 1) ((string= s "F16") 2)
+        (t (error "unsupported dtype ~A" s))))
+
+(defun upload-safetensors (path)
+  "Hand every tensor's raw bytes to ec_upload_tensor (st:get-tensor without
+the host widening, st.lisp:32-86)."
+  (multiple-value-bind (header data-start) (st:parse-header path)
+    (with-open-file (in path :direction :input :element-type '(unsigned-byte 8))
+      (loop for name in (st:tensor-names header)
+            for info = (gethash name header)
+            unless (string= name "__metadata__")
+              do (let* ((offs (gethash "data_offsets" info))
+                        (nbytes (- (second offs) (first offs)))
+                        (buf (make-array nbytes :element-type '(unsigned-byte 8)))
+                        (shape (coerce (gethash "shape" info)
+                                       '(simple-array (signed-byte 64) (*)))))
+                   (file-position in (+ data-start (first offs)))
+                   (unless (= (read-sequence buf in) nbytes)
+                     (error "EOF in tensor ~A" name))
+                   (with-saps ((sp shape) (bp buf))
+                     (check (%upload-tensor name (dtype-code (gethash "dtype" info)) sp
+                                            (length shape) bp nbytes)
+                            (format nil "upload ~A" name))))))))
+
+;;; ---- model.lisp ------------------------------------------------------------
+
+(defun slurp (path)
+  (when (probe-file path)
+    (with-open-file (in path :direction :input :external-format :utf-8)
+      (let ((s (make-string (file-length in))))
+        (subseq s 0 (read-sequence s in))))))
+
+(defun load-model (path)
+  "Upload model.safetensors and build the model on the devices.  Returns the
+family keyword as model:load-model does (model.lisp:28-46)."
+  (init)
+  (let* ((dir (make-pathname :defaults path :name nil :type nil))
+         (cfg (slurp (merge-pathnames "config.json" dir)))
+         (pool (slurp (merge-pathnames "1_Pooling/config.json" dir)))
+         (fam (make-array 1 :element-type '(signed-byte 32)))
+         (dm (make-array 1 :element-type '(signed-byte 32))))
+    (upload-safetensors (merge-pathnames "model.safetensors" dir))
+    (with-saps ((fp fam) (dp dm))
+      (check (%load-model cfg pool fp dp) "ec_load_model"))
+    (setf *dim* (aref dm 0))
+    (ecase (aref fam 0) (1 :bert) (2 :mpnet) (3 :llama))))
+
+(defun dim () *dim*)
+
+(defun embed-batch (id-vectors)
+  "List of token-id vectors -> list of L2-normalised (simple-array
+single-float (dim)), in input order (model:embed for a whole batch)."
+  (let* ((n (length id-vectors))
+         (offsets (make-array (1+ n) :element-type '(signed-byte 64)))
+         (total (reduce #'+ id-vectors :key #'length))
+         (ids (make-array total :element-type '(signed-byte 32)))
+         (out (make-array (* n *dim*) :element-type 'single-float)))
+    (loop for v in id-vectors
+          for i from 0
+          with pos = 0
+          do (setf (aref offsets i) pos)
+             (loop for x across v do (setf (aref ids pos) x) (incf pos))
+          finally (setf (aref offsets n) pos))
+    (with-saps ((ip ids) (op offsets) (outp out))
+      (check (%embed-batch ip op n outp *dim*) "ec_embed_batch"))
+    (loop for i below n
+          collect (subseq out (* i *dim*) (* (1+ i) *dim*)))))
+
+(defun embed-ids (ids)
+  "One sequence of token ids (tokenizer:tk-encode's output) -> embedding."
+  (first (embed-batch (list ids))))
+
+;;; ---- ann.lisp ----------------------------------------------------------------
+
+(defun kmeans (vecs sample k iters &key (dim 384))
+  "ann::kmeans (ann.lisp:79-125) on the GPUs.  SAMPLE is the vector of
+training row indices; its first K rows initialise the centroids."
+  (let* ((n (floor (length vecs) dim))
+         (s (coerce sample '(simple-array (signed-byte 64) (*))))
+         (cent (make-array (* k dim) :element-type 'single-float)))
+    (with-saps ((xp vecs) (sp s) (cp cent) (np nil))
+      (check (%kmeans xp n dim sp (length s) k iters np cp) "ec_kmeans"))
+    cent))
+
+(defun assign-all (vecs n centroids k &key (dim 384))
+  "ann::assign-all (ann.lisp:127-158): (values counts lists)."
+  (let ((counts (make-array k :element-type '(unsigned-byte 32)))
+        (lists (make-array n :element-type '(unsigned-byte 32))))
+    (with-saps ((xp vecs) (cp centroids) (np counts) (lp lists))
+      (check (%assign-all xp n dim cp k np lp) "ec_assign_all"))
+    (values counts lists)))
+
+;;; ---- kb.lisp -------------------------------------------------------------------
+
+(defun index-load (vecs n &key centroids counts lists (dim 384))
+  "Keep index.bin (and ann.bin when CENTROIDS is given) resident on the GPUs."
+  (let ((k (if centroids (floor (length centroids) dim) 0)))
+    (with-saps ((xp vecs) (cp centroids) (np counts) (lp lists))
+      (check (%index-load xp n dim cp k np lp) "ec_index_load"))
+    (setf *ivf* (plusp k))))
+
+(defun %search (q k ivf)
+  (let ((ids (make-array k :element-type '(signed-byte 64)))
+        (sc (make-array k :element-type 'single-float))
+        (qv (coerce q '(simple-array single-float (*)))))
+    (with-saps ((qp qv) (ip ids) (sp sc))
+      (check (if ivf
+                 (%ivf-search qp 1 *nprobe* k ip sp)
+                 (%flat-search qp 1 k ip sp))
+             "search"))
+    (loop for i below k
+          when (>= (aref ids i) 0)
+            collect (cons (aref ids i) (aref sc i)))))
+
+(defun top-k-brute (q k) (%search q k nil))
+
+(defun top-k (q k)
+  "kb::top-k (kb.lisp:366-368): list of (row . score), descending."
+  (%search q k *ivf*))

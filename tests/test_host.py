@@ -1,0 +1,77 @@
+"""Host-side logic without a GPU: the seeded workload generator, the
+safetensors reader of the host mirror (st.lisp), the ann.bin format
+(ann.lisp:4-6, 165-187) and the benchmark's FLOP accounting."""
+import json
+import os
+import struct
+
+import numpy as np
+
+from embedcuda import ann, st, synth
+
+
+def test_inputs_match_the_workload_spec():
+    ids, offs = synth.make_inputs("minilm", 1024, 0)
+    lens = np.diff(offs)
+    assert len(lens) == 1024 and lens.min() >= 16 and lens.max() <= 256
+    first = ids[offs[:-1]]
+    last = ids[offs[1:] - 1]
+    assert np.all(first == 101) and np.all(last == 102)
+    body = np.concatenate([ids[offs[i] + 1:offs[i + 1] - 1] for i in range(1024)])
+    assert body.min() >= 1000 and body.max() <= 30521
+    ids2, offs2 = synth.make_inputs("minilm", 1024, 0)
+    assert np.array_equal(ids, ids2) and np.array_equal(offs, offs2)  # seeded
+    q, qo = synth.make_inputs("qwen3", 64, 3)
+    ql = np.diff(qo)
+    assert ql.min() >= 129 and ql.max() <= 513 and np.all(q[qo[1:] - 1] == 151643)
+    b, bo = synth.make_inputs("bert", 512, 1)
+    bl = np.diff(bo)
+    assert bl.min() >= 32 and bl.max() <= 512
+    m, mo = synth.make_inputs("mpnet", 256, 2)
+    ml = np.diff(mo)
+    assert ml.min() >= 64 and ml.max() <= 384 and np.all(m[mo[:-1]] == 0) and np.all(m[mo[1:] - 1] == 2)
+
+
+def test_safetensors_layout_and_bf16_rounding(tmp_path):
+    s = synth.with_layers(synth.BERT_BASE, 1, vocab=64)
+    d = synth.build_model_dir(s, 1, str(tmp_path))
+    header, start = st.parse_header(os.path.join(d, "model.safetensors"))
+    names = st.tensor_names(header)
+    assert "encoder.layer.0.attention.self.query.weight" in names
+    info = header["embeddings.word_embeddings.weight"]
+    assert info["dtype"] == "BF16" and info["shape"] == [64, 768]
+    with open(os.path.join(d, "config.json")) as f:
+        cfg = json.load(f)
+    assert cfg["model_type"] == "bert" and cfg["hidden_size"] == 768
+    assert not os.path.exists(os.path.join(d, "1_Pooling", "config.json")) or \
+        not json.load(open(os.path.join(d, "1_Pooling", "config.json")))["pooling_mode_mean_tokens"]
+    # round-to-nearest-even to bf16
+    a = np.array([1.0, 1.00390625, 1.01171875, -3.0e-39], np.float32)
+    bits = synth.f32_to_bf16_bits(a)
+    assert list(bits[:3]) == [0x3F80, 0x3F80, 0x3F82]
+
+
+def test_ann_bin_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    cent = rng.standard_normal((5, 384)).astype(np.float32)
+    counts = np.array([3, 0, 2, 1, 4], np.uint32)
+    lists = rng.permutation(10).astype(np.uint32)
+    p = str(tmp_path / "ann.bin")
+    ann.save_ann(p, cent, counts, lists, 10)
+    with open(p, "rb") as f:
+        assert struct.unpack("<4I", f.read(16)) == (0x414E4E31, 5, 384, 10)
+    assert os.path.getsize(p) == 4 * (4 + 5 * 384 + 5 + 10)
+    c2, n2, l2 = ann.load_ann(p)
+    assert np.array_equal(c2, cent) and np.array_equal(n2, counts) and np.array_equal(l2, lists)
+
+
+def test_bench_flop_accounting():
+    import bench
+    offs = np.array([0, 100, 300], np.int64)
+    f = bench.algorithmic_flops(synth.MINILM, offs)
+    H, F, L = 384, 1536, 6
+    want = L * sum(2 * n * (4 * H * H + 2 * H * F) + 4 * n * n * H for n in (100, 200))
+    assert f == want
+    ids, offsets = synth.make_inputs("minilm", 1024, 0)
+    total = bench.algorithmic_flops(synth.MINILM, offsets)
+    assert 3.0e12 < total < 3.4e12  # the ~3.18e12 of the workload spec
