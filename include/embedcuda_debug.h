@@ -37,6 +37,12 @@ int ecdbg_profile_read(const char *cls, double *ms, double *flops, double *bytes
 /* Kernel launches issued by the library since the last ecdbg_profile(1). */
 long long ecdbg_launches(void);
 
+/* Failure-path check of the bounded waits: launches one CTA that waits on an
+ * mbarrier no thread arrives on, with a limit of `limit_ms` milliseconds.
+ * The wait gives up, the kernel records a status and exits, and the call
+ * returns EC_ETIMEOUT with the context still usable. */
+int ecdbg_wait_timeout(int limit_ms);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,4 +1,5 @@
 // ec_attn.cu -- instantiations and host launcher of the varlen attention.
+#include <cstdlib>
 #include <mutex>
 
 #include "ec_attn.cuh"
@@ -39,7 +40,13 @@ static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
   a.causal = l.causal;
   a.relbias = l.relbias;
   a.rel_max = l.rel_max;
-  dim3 grid(l.nblocks, l.heads);
+  // heads per CTA: enough CTAs to fill the GPU several times over, else walk
+  // several heads per CTA to amortise the tile loads
+  int hpc = 1;
+  if (const char* e = getenv("EC_ATTN_HEADS_PER_CTA")) hpc = atoi(e);
+  if (hpc < 1 || l.heads % hpc) hpc = 1;
+  a.heads_per_cta = hpc;
+  dim3 grid(l.nblocks, l.heads / hpc);
   attn_fwd_kernel<HD><<<grid, kAttnThreads, AttnSmem<HD>::BYTES, st>>>(a);
   return cudaGetLastError();
 }

@@ -4,7 +4,7 @@
 // bert::encoder-layer (bert.lisp:226-248), bert::mpnet-layer (:408-423, with
 // the relative-position bias) and llama::layer-forward (llama.lisp:255-271,
 // causal grouped-query attention).  Sequences are packed back to back (no
-// padding); one CTA handles 64 query rows of one sequence and one head and
+// padding); one CTA handles 64 query rows of one sequence for every head and
 // streams the sequence's keys in blocks of 64 with an online softmax, so the
 // L x L score matrix never leaves registers.  Tensor-core math is
 // mma.sync.m16n8k16 bf16 -> fp32.
@@ -29,6 +29,7 @@ struct AttnArgs {
   int causal;
   const float* relbias;      // [heads][2 * rel_max - 1] (already * log2 e) or nullptr
   int rel_max;               // bias index = (i - j) + rel_max - 1
+  int heads_per_cta;         // heads walked by one CTA (grid.y = heads / heads_per_cta)
 };
 
 constexpr int kAttnBQ = 64;
@@ -71,6 +72,12 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ float fast_exp2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -80,7 +87,8 @@ template <int HD>
 struct AttnSmem {
   static constexpr int LDS = HD + 8;  // padded row (elements) -> conflict-free ldmatrix
   static constexpr int TILE = kAttnBK * LDS;
-  static constexpr size_t BYTES = static_cast<size_t>(5 * TILE) * 2 + 2048 * 4;
+  // Q, K, V double-buffered + relative-bias row
+  static constexpr size_t BYTES = static_cast<size_t>(6 * TILE) * 2 + 2048 * 4;
 };
 
 // Load a 64-row tile (rows r0.. of the sequence starting at token `base`,
@@ -99,6 +107,10 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat1
   }
 }
 
+// One CTA per (sequence, 64-query block, group of heads_per_cta heads).  The
+// work is the flattened sequence of (head, key block) items; the Q/K/V tiles
+// of item i+1 are fetched with cp.async while item i computes, across head
+// boundaries.
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_fwd_kernel(const AttnArgs a) {
@@ -107,172 +119,192 @@ __global__ void __launch_bounds__(kAttnThreads)
   constexpr int NT_D = HD / 8;    // n-tiles of the output
   constexpr int KS_D = HD / 16;   // k-steps over head dim
   extern __shared__ __align__(16) uint8_t attn_smem[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(attn_smem);
-  __nv_bfloat16* sK = sQ + TILE;       // 2 buffers
-  __nv_bfloat16* sV = sK + 2 * TILE;   // 2 buffers
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(attn_smem);  // 2 buffers
+  __nv_bfloat16* sK = sQ + 2 * TILE;                                   // 2 buffers
+  __nv_bfloat16* sV = sK + 2 * TILE;                                   // 2 buffers
   float* sBias = reinterpret_cast<float*>(sV + 2 * TILE);
 
   const int2 blk = a.blocks[blockIdx.x];
   const int seq = blk.x, q0 = blk.y;
-  const int h = blockIdx.y;
-  const int kvh = h / a.kv_group;
   const int base = a.cu[seq];
   const int L = a.cu[seq + 1] - base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int qcol = a.q_off + h * HD, kcol = a.k_off + kvh * HD, vcol = a.v_off + kvh * HD;
   int kv_end = L;
   if (a.causal) kv_end = min(L, q0 + kAttnBQ);
   const int nkb = (kv_end + kAttnBK - 1) / kAttnBK;
-
-  load_tile<HD>(sQ, a.qkv, a.ld, base, q0, L, qcol);
-  load_tile<HD>(sK, a.qkv, a.ld, base, 0, L, kcol);
-  load_tile<HD>(sV, a.qkv, a.ld, base, 0, L, vcol);
-  cp_async_commit();
-
+  const int h0 = blockIdx.y * a.heads_per_cta;
+  const int total = a.heads_per_cta * nkb;
   const bool use_bias = a.relbias != nullptr;
-  if (use_bias) {
-    const int nb = 2 * a.rel_max - 1;
-    const float* src = a.relbias + static_cast<size_t>(h) * nb;
-    // only offsets reachable inside this sequence: |i - j| < L
-    for (int i = threadIdx.x; i < 2 * L - 1 && i < 2048; i += kAttnThreads)
-      sBias[i] = src[i - (L - 1) + a.rel_max - 1];
-  }
+
+  auto issue = [&](int it) {
+    const int h = h0 + it / nkb, kb = it % nkb;
+    const int kvh = h / a.kv_group;
+    if (kb == 0) load_tile<HD>(sQ + (h & 1) * TILE, a.qkv, a.ld, base, q0, L, a.q_off + h * HD);
+    load_tile<HD>(sK + (it & 1) * TILE, a.qkv, a.ld, base, kb * kAttnBK, L, a.k_off + kvh * HD);
+    load_tile<HD>(sV + (it & 1) * TILE, a.qkv, a.ld, base, kb * kAttnBK, L, a.v_off + kvh * HD);
+    cp_async_commit();
+  };
 
   float o[NT_D][4];
-#pragma unroll
-  for (int n = 0; n < NT_D; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  float m_r[2], l_r[2];
   uint32_t qf[KS_D][4];
-
   const int row_a = q0 + warp * 16 + (lane >> 2);  // query row (within seq) of c0/c1
   const int row_b = row_a + 8;
 
-  for (int kb = 0; kb < nkb; ++kb) {
-    const int buf = kb & 1;
-    if (kb + 1 < nkb) {
-      load_tile<HD>(sK + (buf ^ 1) * TILE, a.qkv, a.ld, base, (kb + 1) * kAttnBK, L, kcol);
-      load_tile<HD>(sV + (buf ^ 1) * TILE, a.qkv, a.ld, base, (kb + 1) * kAttnBK, L, vcol);
-      cp_async_commit();
+  issue(0);
+  for (int it = 0; it < total; ++it) {
+    const int h = h0 + it / nkb, kb = it % nkb;
+    if (it + 1 < total) {
+      issue(it + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
     if (kb == 0) {
+      if (use_bias) {
+        // bias for i - j over this sequence: |i - j| < L
+        const int nb = 2 * a.rel_max - 1;
+        const float* src = a.relbias + static_cast<size_t>(h) * nb;
+        for (int i = threadIdx.x; i < 2 * L - 1 && i < 2048; i += kAttnThreads)
+          sBias[i] = src[i - (L - 1) + a.rel_max - 1];
+        __syncthreads();
+      }
+      const __nv_bfloat16* cQ = sQ + (h & 1) * TILE;
 #pragma unroll
       for (int ks = 0; ks < KS_D; ++ks)
-        ldsm_x4(qf[ks], sQ + (warp * 16 + (lane & 15)) * LDS + ks * 16 + (lane >> 4) * 8);
+        ldsm_x4(qf[ks], cQ + (warp * 16 + (lane & 15)) * LDS + ks * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      m_r[0] = m_r[1] = -INFINITY;
+      l_r[0] = l_r[1] = 0.f;
     }
-    const __nv_bfloat16* cK = sK + buf * TILE;
-    const __nv_bfloat16* cV = sV + buf * TILE;
-
-    // S = Q K^T : 16 x 64 per warp
-    float s[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < KS_D; ++ks) {
-#pragma unroll
-      for (int n = 0; n < 8; n += 2) {
-        uint32_t b[4];
-        const int mi = lane >> 3;  // matrix index
-        const int key = n * 8 + (mi >> 1) * 8 + (lane & 7);
-        ldsm_x4(b, cK + key * LDS + ks * 16 + (mi & 1) * 8);
-        mma_bf16_16816(s[n], qf[ks], b[0], b[1]);
-        mma_bf16_16816(s[n + 1], qf[ks], b[2], b[3]);
-      }
-    }
-    // scale, bias, masks
+    const __nv_bfloat16* cK = sK + (it & 1) * TILE;
+    const __nv_bfloat16* cV = sV + (it & 1) * TILE;
     const int k0 = kb * kAttnBK;
-    float mx[2] = {-INFINITY, -INFINITY};
+    // warps whose 16 query rows all lie past the sequence skip the math
+    const bool warp_live = q0 + warp * 16 < L;
+    // keys k0 + 8n .. for n < nt_live exist in this sequence
+    const int nt_live = min(8, (L - k0 + 7) >> 3);
+    // only the last block (or one touching the causal diagonal) needs masks
+    const bool need_mask = (k0 + kAttnBK > L) || (a.causal && k0 + kAttnBK - 1 > q0 + warp * 16);
+    if (warp_live) {
+      // S = Q K^T : 16 x 64 per warp
+      float s[8][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
-        const int qr = (e < 2) ? row_a : row_b;
-        float v = s[n][e] * a.scale_log2;
-        if (use_bias) v += sBias[qr - key + (L - 1) < 0 ? 0 : min(qr - key + (L - 1), 2046)];
-        const bool masked = key >= L || (a.causal && key > qr);
-        v = masked ? -INFINITY : v;
-        s[n][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      for (int ks = 0; ks < KS_D; ++ks) {
+#pragma unroll
+        for (int n = 0; n < 8; n += 2) {
+          if (n < nt_live) {
+            uint32_t b[4];
+            const int mi = lane >> 3;  // matrix index
+            const int key = n * 8 + (mi >> 1) * 8 + (lane & 7);
+            ldsm_x4(b, cK + key * LDS + ks * 16 + (mi & 1) * 8);
+            mma_bf16_16816(s[n], qf[ks], b[0], b[1]);
+            mma_bf16_16816(s[n + 1], qf[ks], b[2], b[3]);
+          }
+        }
+      }
+      // scale, bias, masks
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
+          const int qr = (e < 2) ? row_a : row_b;
+          float v = s[n][e] * a.scale_log2;
+          if (use_bias) {
+            const int bi = qr - key + (L - 1);
+            v += sBias[bi < 0 ? 0 : (bi > 2046 ? 2046 : bi)];
+          }
+          if (need_mask) {
+            const bool masked = key >= L || (a.causal && key > qr);
+            v = masked ? -INFINITY : v;
+          }
+          s[n][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      // Key 0 is visible to every query row (0 < L and 0 <= row), so after the
+      // first key block every running max is finite and the updates below
+      // never see -inf - -inf.
+      float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float mnew = fmaxf(m_r[r], mx[r]);
+        corr[r] = fast_exp2(m_r[r] - mnew);
+        m_r[r] = mnew;
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = e >> 1;
+          const float p = n < nt_live ? fast_exp2(s[n][e] - m_r[r]) : 0.f;
+          s[n][e] = p;
+          rs[r] += p;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_r[r] = l_r[r] * corr[r] + rs[r];
+      }
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
+      // O += P V over the live 16-key steps
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (2 * t < nt_live) {
+          uint32_t pa[4];
+          pa[0] = pack2_bf16(s[2 * t][0], s[2 * t][1]);
+          pa[1] = pack2_bf16(s[2 * t][2], s[2 * t][3]);
+          pa[2] = pack2_bf16(s[2 * t + 1][0], s[2 * t + 1][1]);
+          pa[3] = pack2_bf16(s[2 * t + 1][2], s[2 * t + 1][3]);
+#pragma unroll
+          for (int n = 0; n < NT_D; n += 2) {
+            uint32_t b[4];
+            const int mi = lane >> 3;
+            const int key = t * 16 + (mi & 1) * 8 + (lane & 7);
+            const int d = (n + (mi >> 1)) * 8;
+            ldsm_x4_t(b, cV + key * LDS + d);
+            mma_bf16_16816(o[n], pa, b[0], b[1]);
+            mma_bf16_16816(o[n + 1], pa, b[2], b[3]);
+          }
+        }
       }
     }
+    if (kb == nkb - 1 && warp_live) {
+      // normalise and store this head's rows
+      const float inv0 = l_r[0] > 0.f ? 1.f / l_r[0] : 0.f;
+      const float inv1 = l_r[1] > 0.f ? 1.f / l_r[1] : 0.f;
+      __nv_bfloat16* out_h = a.out + h * HD;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    // Key 0 is visible to every query row (0 < L and 0 <= row), so after the
-    // first key block every running max is finite and the updates below
-    // never see -inf - -inf.
-    float corr[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float mnew = fmaxf(m_r[r], mx[r]);
-      corr[r] = exp2f(m_r[r] - mnew);
-      m_r[r] = mnew;
-    }
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = e >> 1;
-        const float p = exp2f(s[n][e] - m_r[r]);
-        s[n][e] = p;
-        rs[r] += p;
+      for (int n = 0; n < NT_D; ++n) {
+        const int d = n * 8 + (lane & 3) * 2;
+        if (row_a < L)
+          *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_a) * a.ldo + d) =
+              pack2_bf16(o[n][0] * inv0, o[n][1] * inv0);
+        if (row_b < L)
+          *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_b) * a.ldo + d) =
+              pack2_bf16(o[n][2] * inv1, o[n][3] * inv1);
       }
     }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-      l_r[r] = l_r[r] * corr[r] + rs[r];
-    }
-#pragma unroll
-    for (int n = 0; n < NT_D; ++n) {
-      o[n][0] *= corr[0];
-      o[n][1] *= corr[0];
-      o[n][2] *= corr[1];
-      o[n][3] *= corr[1];
-    }
-    // O += P V
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {  // k-steps of 16 keys
-      uint32_t pa[4];
-      pa[0] = pack2_bf16(s[2 * t][0], s[2 * t][1]);
-      pa[1] = pack2_bf16(s[2 * t][2], s[2 * t][3]);
-      pa[2] = pack2_bf16(s[2 * t + 1][0], s[2 * t + 1][1]);
-      pa[3] = pack2_bf16(s[2 * t + 1][2], s[2 * t + 1][3]);
-#pragma unroll
-      for (int n = 0; n < NT_D; n += 2) {
-        uint32_t b[4];
-        const int mi = lane >> 3;
-        const int key = t * 16 + (mi & 1) * 8 + (lane & 7);
-        const int d = (n + (mi >> 1)) * 8;
-        ldsm_x4_t(b, cV + key * LDS + d);
-        mma_bf16_16816(o[n], pa, b[0], b[1]);
-        mma_bf16_16816(o[n + 1], pa, b[2], b[3]);
-      }
-    }
-    __syncthreads();  // buffer `buf` is refilled two iterations later
-  }
-
-  // normalise and store
-  const float inv0 = l_r[0] > 0.f ? 1.f / l_r[0] : 0.f;
-  const float inv1 = l_r[1] > 0.f ? 1.f / l_r[1] : 0.f;
-  __nv_bfloat16* out_h = a.out + h * HD;
-#pragma unroll
-  for (int n = 0; n < NT_D; ++n) {
-    const int d = n * 8 + (lane & 3) * 2;
-    if (row_a < L)
-      *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_a) * a.ldo + d) =
-          pack2_bf16(o[n][0] * inv0, o[n][1] * inv0);
-    if (row_b < L)
-      *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_b) * a.ldo + d) =
-          pack2_bf16(o[n][2] * inv1, o[n][3] * inv1);
+    __syncthreads();  // buffers of item `it` are refilled by issue(it + 2)
   }
 }
 

@@ -4,9 +4,35 @@
 #include <vector>
 
 #include "../../include/embedcuda_debug.h"
+#include "ec_ptx.cuh"
 #include "ec_state.h"
 
 using namespace ec;
+
+namespace {
+
+// Waits on a barrier that never completes; the bounded wait gives up after
+// limit_ns and the kernel reports kDevTimeoutOther.
+__global__ void wait_timeout_kernel(unsigned* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    bool done = false;
+    while (!done) {
+      done = mbar_try_wait(&bar, 0);
+      if (!done && globaltimer_ns() - t0 > limit_ns) break;
+    }
+    if (!done) report(status, kDevTimeoutOther);
+  }
+  __syncthreads();
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -107,6 +133,20 @@ int ecdbg_profile_read(const char* cls, double* ms, double* flops, double* bytes
   if (bytes) *bytes = a.bytes;
   if (launches) *launches = a.launches;
   return EC_OK;
+}
+
+int ecdbg_wait_timeout(int limit_ms) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (limit_ms < 1 || limit_ms > 1000) return set_error(EC_EINVAL, "limit_ms outside 1..1000");
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  wait_timeout_kernel<<<1, 32, 0, d.stream>>>(d.status, 1000000ull * limit_ms);
+  rc = check_cuda(cudaGetLastError(), "wait kernel");
+  if (rc) return rc;
+  return sync_and_check(d, "bounded wait");
 }
 
 long long ecdbg_launches(void) {

@@ -39,9 +39,27 @@ static bool encode_2d_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uin
   return r == CUDA_SUCCESS;
 }
 
+// Output map of the epilogue's bulk stores: 32 x 32 boxes, fp32 rows of
+// 128 B with 128-byte swizzle or bf16 rows of 64 B with 64-byte swizzle (the
+// layouts stage_off writes); rows past `rows` are not written.
+static bool encode_2d_out(CUtensorMap* map, void* ptr, bool f32, uint64_t rows, uint64_t cols,
+                          uint64_t ld_elems) {
+  if (!g_encode) return false;
+  const uint64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_elems * es};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI>
 static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, EPI>;
   // the shared-memory opt-in is a per-device function attribute
   static std::mutex attr_mu;
   static bool attr_set[64] = {};
@@ -58,9 +76,11 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
       attr_set[dev] = true;
     }
   }
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if (!encode_2d_bf16(&ta, g.A, g.M, g.K, g.lda, kGemmBM)) return cudaErrorInvalidValue;
   if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.ldw, BN)) return cudaErrorInvalidValue;
+  const uint64_t out_cols = EPI == kEpiBf16Swiglu ? g.N / 2 : g.N;
+  if (!encode_2d_out(&tc, g.out, Cfg::OUT_F32, g.M, out_cols, g.ldo)) return cudaErrorInvalidValue;
   GemmArgs a;
   a.M = g.M;
   a.N = g.N;
@@ -74,7 +94,7 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * a.n_tiles_n;
   a.status = g.status;
   const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
-  gemm_tn_bf16_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, a);
+  gemm_tn_bf16_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
   return cudaGetLastError();
 }
 
@@ -86,7 +106,7 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
     case kEpiF32Resid: return run<BN, kEpiF32Resid>(g, st, num_sms);
     case kEpiF32: return run<BN, kEpiF32>(g, st, num_sms);
     case kEpiBf16Swiglu:
-      if constexpr (BN % 64 == 0) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
+      if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }

@@ -16,8 +16,12 @@
 //                 so the epilogue of tile i overlaps the MMAs of tile i+1.
 //   warps 2..9  : epilogue; warp w owns TMEM lanes 32*(w%4).. (= tile rows),
 //                 two warps per lane quadrant take alternate 32-column chunks
-//                 (tcgen05.ld), apply the epilogue in fp32 and store with
-//                 16-byte vector stores.
+//                 (tcgen05.ld), apply the epilogue in fp32, stage the 32x32
+//                 chunk in swizzled shared memory (double-buffered) and write
+//                 it with a TMA bulk tensor store; rows past M are clipped by
+//                 the tensor map.  The fp32 residual of a chunk is read with
+//                 coalesced 16-byte loads issued before the TMEM read and
+//                 transposed to row-per-lane through the same staging buffer.
 // All waits are bounded (ec_ptx.cuh); a timeout records a status code,
 // raises the CTA abort flag and every role unwinds, then TMEM is freed.
 #pragma once
@@ -51,15 +55,23 @@ constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 320;  // 2 control warps + 8 epilogue warps
 constexpr int kGemmEpiWarps = 8;
 
-template <int BN>
+template <int BN, int EPI>
 struct GemmCfg {
-  static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 192 ? 5 : 6);
+  static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32;
+  // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
+  // rows of 64 B (64B swizzle); two per epilogue warp
+  static constexpr uint32_t CHUNK_BYTES = OUT_F32 ? 4096 : 2048;
+  static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t B_BYTES = BN * kGemmBK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int MAX_STAGES = (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES)) /
+                                    static_cast<int>(STAGE_BYTES);
+  static constexpr int STAGES = MAX_STAGES > 6 ? 6 : MAX_STAGES;
   static constexpr uint32_t TMEM_COLS =
       2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
-  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 512;
+  static_assert(STAGES >= 2, "shared memory budget");
 };
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -95,66 +107,23 @@ __device__ __forceinline__ float silu_f(float x) {
   return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
 }
 
-template <int EPI>
-__device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int col0,
-                                                const uint32_t (&r)[32]) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if (a.bias) {
-    const float4* b4 = reinterpret_cast<const float4*>(a.bias + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 b = __ldg(b4 + j);
-      v[4 * j] += b.x;
-      v[4 * j + 1] += b.y;
-      v[4 * j + 2] += b.z;
-      v[4 * j + 3] += b.w;
-    }
-  }
-  if (row >= a.M) return;
-  if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu) {
-    uint32_t p[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float x0 = v[2 * j], x1 = v[2 * j + 1];
-      if constexpr (EPI == kEpiBf16Gelu) {
-        x0 = gelu_as(x0);
-        x1 = gelu_as(x1);
-      }
-      p[j] = pack_bf16(x0, x1);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
-                                          static_cast<size_t>(row) * a.ldo + col0);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-  } else if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
-                                            static_cast<size_t>(row) * a.ldo + col0);
-    if constexpr (EPI == kEpiF32Resid) {
-      const float4* rs =
-          reinterpret_cast<const float4*>(a.resid + static_cast<size_t>(row) * a.ldr + col0);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 q = rs[j];
-        v[4 * j] += q.x;
-        v[4 * j + 1] += q.y;
-        v[4 * j + 2] += q.z;
-        v[4 * j + 3] += q.w;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  }
+// Byte offset of 16-byte column chunk c of row r in a swizzled staging chunk:
+// fp32 rows are 128 B (chunk c ^ (r & 7)), bf16 rows 64 B (c ^ ((r >> 1) & 3)),
+// the layouts TMA's 128B / 64B swizzle modes read.
+template <bool F32>
+__device__ __forceinline__ uint32_t stage_off(int r, int c) {
+  if constexpr (F32) return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+  return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using Cfg = GemmCfg<BN>;
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+  using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr bool F32 = Cfg::OUT_F32;
   constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(EPI != kEpiBf16Swiglu || BN % 64 == 0, "swiglu BN");
@@ -164,7 +133,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smB + STAGES * Cfg::B_BYTES);
+  uint8_t* smE = smB + STAGES * Cfg::B_BYTES;  // epilogue staging, 2 chunks per warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(smE + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -189,6 +159,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -271,61 +242,130 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // epilogue warps 2..9: lane quadrant warp % 4, chunk parity (warp - 2) / 4
+    const int ew = warp - 2;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = ew >> 2;
+    uint8_t* stage_base = smE + ew * 2 * Cfg::CHUNK_BYTES;
+    constexpr int NCH = EPI == kEpiBf16Swiglu ? BN / 64 : BN / 32;  // output chunks per tile
+    static_assert(NCH >= 2, "every epilogue warp needs a chunk per tile");
     int acc = 0;
     uint32_t acc_phase = 0;
+    int sbuf = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
       const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-        report(args.status, kDevTimeoutEpilogue);
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      const int row = mb * kGemmBM + quad * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
-      if constexpr (EPI == kEpiBf16Swiglu) {
-        // gate columns [0, BN/2), up columns [BN/2, BN) of this tile
+      const int row0 = mb * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1
-        for (int c = half; c < BN / 64; c += 2) {
+      for (int c = half; c < NCH; c += 2) {
+        const int col0 = (EPI == kEpiBf16Swiglu ? nb * (BN / 2) : nb * BN) + c * 32;
+        // residual rows row0 + 4k + lane/8, columns col0 + (lane%8)*4 .. +3:
+        // coalesced 128-byte rows, issued before the TMEM wait
+        float4 res[8];
+        if constexpr (EPI == kEpiF32Resid) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = row0 + 4 * k + (lane >> 3);
+            res[k] = r < args.M
+                         ? *reinterpret_cast<const float4*>(
+                               args.resid + static_cast<size_t>(r) * args.ldr + col0 + (lane & 7) * 4)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        if (c == half) {
+          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+            report(args.status, kDevTimeoutEpilogue);
+            *abort_flag = 1;
+            tile = args.num_tiles;  // leave both loops
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN);
+        float v[32];
+        if constexpr (EPI == kEpiBf16Swiglu) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(t_row + c * 32, g);
           tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, u);
           tmem_wait_ld();
-          if (row < args.M) {
-            uint32_t p[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float a0 = silu_f(__uint_as_float(g[2 * j])) * __uint_as_float(u[2 * j]);
-              const float a1 =
-                  silu_f(__uint_as_float(g[2 * j + 1])) * __uint_as_float(u[2 * j + 1]);
-              p[j] = pack_bf16(a0, a1);
-            }
-            const int col0 = nb * (BN / 2) + c * 32;
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.out) +
-                                                  static_cast<size_t>(row) * args.ldo + col0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += 2) {
+          for (int j = 0; j < 32; ++j)
+            v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+        } else {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_wait_ld();
-          epi_store_chunk<EPI>(args, row, nb * BN + c * 32, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (args.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 b = __ldg(b4 + j);
+              v[4 * j] += b.x;
+              v[4 * j + 1] += b.y;
+              v[4 * j + 2] += b.z;
+              v[4 * j + 3] += b.w;
+            }
+          }
+        }
+        // staging buffer sbuf: the bulk store issued from it two chunks ago
+        // must have finished reading it
+        uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        if constexpr (EPI == kEpiF32Resid) {
+          // transpose the residual to row-per-lane through the staging chunk
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(st + stage_off<true>(4 * k + (lane >> 3), lane & 7)) = res[k];
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 q = *reinterpret_cast<const float4*>(st + stage_off<true>(lane, j));
+            v[4 * j] += q.x;
+            v[4 * j + 1] += q.y;
+            v[4 * j + 2] += q.z;
+            v[4 * j + 3] += q.w;
+          }
+        }
+        if constexpr (F32) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              x[e] = v[8 * j + e];
+              if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_as(x[e]);
+            }
+            *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
+                make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
+                           pack_bf16(x[6], x[7]));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, st, col0, row0);
+          tma_store_commit();
+        }
+        sbuf ^= 1;
+        if (c + 2 >= NCH) {
+          // last chunk of this warp in the tile: hand the accumulator back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) tma_store_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -202,13 +202,29 @@ __global__ void pool_l2_kernel(PoolArgs a) {
   float acc[4] = {0.f, 0.f, 0.f, 0.f};  // H <= 4 * blockDim
   const int t_first = a.mode == 2 ? L - 1 : 0;
   const int t_last = a.mode == 1 ? L : t_first + 1;
-  for (int t = t_first; t < t_last; ++t) {
-    const float* x = a.h + static_cast<size_t>(base + t) * H;
-    float inv = 1.f;
-    if (a.final_norm) {
+  if (!a.final_norm) {
+    // sums in token order per dimension (bert.lisp:307-310); eight tokens'
+    // loads are issued ahead of their adds to hide memory latency
+    int j = 0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x, ++j) {
+      const float* x = a.h + static_cast<size_t>(base) * H + i;
+      float s0 = 0.f;
+      int t = t_first;
+      for (; t + 8 <= t_last; t += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = x[static_cast<size_t>(t + u) * H];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s0 = s0 + v[u];
+      }
+      for (; t < t_last; ++t) s0 = s0 + x[static_cast<size_t>(t) * H];
+      acc[j] = s0;
+    }
+  } else {
+    for (int t = t_first; t < t_last; ++t) {
+      const float* x = a.h + static_cast<size_t>(base + t) * H;
       double ss = 0.0;
-      for (int i = threadIdx.x; i < H; i += blockDim.x)
-        ss += static_cast<double>(x[i] * x[i]);
+      for (int i = threadIdx.x; i < H; i += blockDim.x) ss += static_cast<double>(x[i] * x[i]);
       ss = warp_sum_d(ss);
       if ((threadIdx.x & 31) == 0) redd[threadIdx.x >> 5] = ss;
       __syncthreads();
@@ -218,14 +234,11 @@ __global__ void pool_l2_kernel(PoolArgs a) {
         if (threadIdx.x == 0) redd[0] = v;
       }
       __syncthreads();
-      inv = static_cast<float>(1.0 / sqrt(redd[0] / H + a.eps));
+      const float inv = static_cast<float>(1.0 / sqrt(redd[0] / H + a.eps));
       __syncthreads();
-    }
-    int j = 0;
-    for (int i = threadIdx.x; i < H; i += blockDim.x, ++j) {
-      float v = x[i];
-      if (a.final_norm) v = (v * inv) * a.norm_w[i];
-      acc[j] = acc[j] + v;
+      int j = 0;
+      for (int i = threadIdx.x; i < H; i += blockDim.x, ++j)
+        acc[j] = acc[j] + (x[i] * inv) * a.norm_w[i];
     }
   }
   float sq = 0.f;
