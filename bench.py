@@ -230,6 +230,9 @@ def main():
     if args.impl == "reference":
         return run_reference(args, rank)
 
+    # NCCL's version banner goes to stdout; the benchmark prints one JSON line
+    if not os.environ.get("EC_KEEP_NCCL_DEBUG"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     import torch
     import torch.distributed as dist
     from datetime import timedelta

@@ -7,7 +7,7 @@
 
 namespace ec {
 
-template <int HD>
+template <int HD, int MODE>
 static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
   static std::mutex mu;
   static bool set[64] = {};
@@ -17,7 +17,7 @@ static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<HD>,
+      cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<HD, MODE>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(AttnSmem<HD>::BYTES));
       if (e != cudaSuccess) return e;
@@ -42,21 +42,29 @@ static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
   a.rel_max = l.rel_max;
   // heads per CTA: enough CTAs to fill the GPU several times over, else walk
   // several heads per CTA to amortise the tile loads
-  int hpc = 1;
+  int hpc = l.heads % 4 == 0 ? 4 : (l.heads % 2 == 0 ? 2 : 1);
   if (const char* e = getenv("EC_ATTN_HEADS_PER_CTA")) hpc = atoi(e);
   if (hpc < 1 || l.heads % hpc) hpc = 1;
   a.heads_per_cta = hpc;
   dim3 grid(l.nblocks, l.heads / hpc);
-  attn_fwd_kernel<HD><<<grid, kAttnThreads, AttnSmem<HD>::BYTES, st>>>(a);
+  attn_fwd_kernel<HD, MODE><<<grid, kAttnThreads, AttnSmem<HD>::BYTES, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int HD>
+static cudaError_t run_mode(const AttnLaunch& l, cudaStream_t st) {
+  if (l.causal) return run_attn<HD, 2>(l, st);
+  if (l.relbias) return run_attn<HD, 1>(l, st);
+  return run_attn<HD, 0>(l, st);
 }
 
 cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
   if (l.nblocks <= 0) return cudaSuccess;
+  if (l.causal && l.relbias) return cudaErrorInvalidValue;
   switch (l.head_dim) {
-    case 32: return run_attn<32>(l, st);
-    case 64: return run_attn<64>(l, st);
-    case 128: return run_attn<128>(l, st);
+    case 32: return run_mode<32>(l, st);
+    case 64: return run_mode<64>(l, st);
+    case 128: return run_mode<128>(l, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -111,9 +111,13 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat1
 // work is the flattened sequence of (head, key block) items; the Q/K/V tiles
 // of item i+1 are fetched with cp.async while item i computes, across head
 // boundaries.
-template <int HD>
+// MODE 0: bidirectional with padding (BERT); 1: + relative bias (MPNet);
+// 2: causal (Llama / Qwen3).
+template <int HD, int MODE>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_fwd_kernel(const AttnArgs a) {
+  constexpr bool kBias = MODE == 1;
+  constexpr bool kCausal = MODE == 2;
   constexpr int LDS = AttnSmem<HD>::LDS;
   constexpr int TILE = AttnSmem<HD>::TILE;
   constexpr int NT_D = HD / 8;    // n-tiles of the output
@@ -130,11 +134,10 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int L = a.cu[seq + 1] - base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int kv_end = L;
-  if (a.causal) kv_end = min(L, q0 + kAttnBQ);
+  if (kCausal) kv_end = min(L, q0 + kAttnBQ);
   const int nkb = (kv_end + kAttnBK - 1) / kAttnBK;
   const int h0 = blockIdx.y * a.heads_per_cta;
   const int total = a.heads_per_cta * nkb;
-  const bool use_bias = a.relbias != nullptr;
 
   auto issue = [&](int it) {
     const int h = h0 + it / nkb, kb = it % nkb;
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
     if (kb == 0) {
-      if (use_bias) {
+      if (kBias) {
         // bias for i - j over this sequence: |i - j| < L
         const int nb = 2 * a.rel_max - 1;
         const float* src = a.relbias + static_cast<size_t>(h) * nb;
@@ -187,9 +190,9 @@ __global__ void __launch_bounds__(kAttnThreads)
     // keys k0 + 8n .. for n < nt_live exist in this sequence
     const int nt_live = min(8, (L - k0 + 7) >> 3);
     // only the last block (or one touching the causal diagonal) needs masks
-    const bool need_mask = (k0 + kAttnBK > L) || (a.causal && k0 + kAttnBK - 1 > q0 + warp * 16);
+    const bool need_mask = (k0 + kAttnBK > L) || (kCausal && k0 + kAttnBK - 1 > q0 + warp * 16);
     if (warp_live) {
-      // S = Q K^T : 16 x 64 per warp
+      // S = Q K^T : 16 x 64 per warp (raw dot products)
       float s[8][4];
 #pragma unroll
       for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
@@ -207,26 +210,35 @@ __global__ void __launch_bounds__(kAttnThreads)
           }
         }
       }
-      // scale, bias, masks
+      // logits in log2 units are s * scale_log2 (+ bias); without a bias the
+      // scale is applied inside the exp (scale > 0 keeps the max)
+      if (kBias) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
+            const int qr = (e < 2) ? row_a : row_b;
+            const int bi = qr - key + (L - 1);
+            s[n][e] = fmaf(s[n][e], a.scale_log2, sBias[bi < 0 ? 0 : (bi > 2046 ? 2046 : bi)]);
+          }
+      }
+      if (need_mask) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
+            const int qr = (e < 2) ? row_a : row_b;
+            const bool masked = key >= L || (kCausal && key > qr);
+            s[n][e] = masked ? -INFINITY : s[n][e];
+          }
+      }
       float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
-          const int qr = (e < 2) ? row_a : row_b;
-          float v = s[n][e] * a.scale_log2;
-          if (use_bias) {
-            const int bi = qr - key + (L - 1);
-            v += sBias[bi < 0 ? 0 : (bi > 2046 ? 2046 : bi)];
-          }
-          if (need_mask) {
-            const bool masked = key >= L || (a.causal && key > qr);
-            v = masked ? -INFINITY : v;
-          }
-          s[n][e] = v;
-          mx[e >> 1] = fmaxf(mx[e >> 1], v);
-        }
+        mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
+        mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
       }
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
@@ -235,22 +247,28 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
       // Key 0 is visible to every query row (0 < L and 0 <= row), so after the
       // first key block every running max is finite and the updates below
-      // never see -inf - -inf.
-      float corr[2], rs[2] = {0.f, 0.f};
+      // never see -inf - -inf.  Running maxima are kept in log2 units.
+      const float sc = kBias ? 1.0f : a.scale_log2;
+      float corr[2], rs[2] = {0.f, 0.f}, nm[2];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const float mnew = fmaxf(m_r[r], mx[r]);
+        const float mnew = fmaxf(m_r[r], mx[r] * sc);
         corr[r] = fast_exp2(m_r[r] - mnew);
         m_r[r] = mnew;
+        nm[r] = -mnew;
       }
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
+        if (n < nt_live) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = e >> 1;
-          const float p = n < nt_live ? fast_exp2(s[n][e] - m_r[r]) : 0.f;
-          s[n][e] = p;
-          rs[r] += p;
+          for (int e = 0; e < 4; ++e) {
+            const int r = e >> 1;
+            const float p = fast_exp2(fmaf(s[n][e], sc, nm[r]));
+            s[n][e] = p;
+            rs[r] += p;
+          }
+        } else {
+          s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
         }
       }
 #pragma unroll

@@ -1,0 +1,66 @@
+"""Two-GPU paths (run only when two GPUs are visible): the in-process
+multi-device split of ec_embed_batch must give the same embeddings as one
+device, and k-means over two devices (NCCL all-reduce of sums + counts)
+must agree with the single-device result up to float32 summation order."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+pytestmark = pytest.mark.gpu
+
+CHILD = r"""
+import sys, os, json
+import numpy as np
+sys.path[:0] = [{repo!r}, os.path.join({repo!r}, "lisp-embed_b200")]
+from embedcuda import _lib, model, synth, ann
+from oracle import oracle
+_lib.init([0, 1])
+d = synth.build_model_dir(synth.with_layers(synth.MINILM, 2), 0, {root!r})
+model.load_model(d)
+ids, offs = synth.make_inputs("minilm", 256, 5)
+two = model.embed_batch(ids, offs)
+x, _ = synth.make_ivf_corpus(40000, 384, 64, seed=4)
+sample = synth.make_ivf_sample(len(x), 4)
+cent2 = ann.kmeans(x, sample, 64, 4)
+counts, lists = ann.assign_all(x, cent2)
+rc, rl = oracle.assign_all(x, cent2)
+np.save({out!r} + "_emb.npy", two)
+np.save({out!r} + "_cent.npy", cent2)
+print(json.dumps({{"lists_equal": bool(np.array_equal(counts, rc) and np.array_equal(lists, rl))}}))
+"""
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_two_device_embed_and_kmeans(tmp_path, synth_root):
+    out = str(tmp_path / "r")
+    p = subprocess.run([sys.executable, "-c", CHILD.format(repo=REPO, root=synth_root, out=out)],
+                       capture_output=True, text=True, timeout=900)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert '"lists_equal": true' in p.stdout
+    from embedcuda import _lib, ann, model, synth
+    from oracle import oracle
+    _lib.init([0])
+    d = synth.build_model_dir(synth.with_layers(synth.MINILM, 2), 0, synth_root)
+    model.load_model(d)
+    ids, offs = synth.make_inputs("minilm", 256, 5)
+    one = model.embed_batch(ids, offs)
+    two = np.load(out + "_emb.npy")
+    assert np.array_equal(one, two)  # no collective: per-sequence results are identical
+    x, _ = synth.make_ivf_corpus(40000, 384, 64, seed=4)
+    sample = synth.make_ivf_sample(len(x), 4)
+    ref = oracle.kmeans(x, sample, 64, 4)
+    cent2 = np.load(out + "_cent.npy")
+    assert np.allclose(cent2, ref, rtol=1e-5, atol=1e-6)
