@@ -20,6 +20,13 @@ extern "C" {
 int ecdbg_gemm(const void *A, const void *W, int M, int N, int K, const float *bias,
                const float *resid, void *out, int epi, int bn);
 
+/* Fused feed-forward block: out = LayerNorm(W2 . gelu(W1 . A + b1) + b2 +
+ * resid), A bf16 [M, H], W1 bf16 [F, H], W2 bf16 [H, F], vectors fp32;
+ * writes out32 fp32 [M, H] and outb bf16 [M, H].  H in {128, 256, 384}. */
+int ecdbg_mlp(const void *A, const void *W1, const void *W2, const float *b1, const float *b2,
+              const float *resid, const float *ln_g, const float *ln_b, float *out32,
+              void *outb, int M, int H, int F);
+
 /* Varlen attention over packed bf16 rows qkv[T, ld]; cu[nseq + 1] (device,
  * int32) token offsets; lens on the host.  out[T, heads * head_dim] bf16. */
 int ecdbg_attention(const void *qkv, int ld, int q_off, int k_off, int v_off, void *out,

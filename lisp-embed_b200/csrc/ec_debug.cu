@@ -65,6 +65,23 @@ int ecdbg_gemm(const void* A, const void* W, int M, int N, int K, const float* b
   return sync_and_check(d, "gemm");
 }
 
+int ecdbg_mlp(const void* A, const void* W1, const void* W2, const float* b1, const float* b2,
+              const float* resid, const float* ln_g, const float* ln_b, float* out32, void* outb,
+              int M, int H, int F) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!mlp_supported(H, F)) return set_error(EC_EUNSUPPORTED, "fused mlp H %d F %d", H, F);
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  MlpLaunch l{static_cast<const bf16*>(A), static_cast<const bf16*>(W1), static_cast<const bf16*>(W2),
+              b1, b2, resid, ln_g, ln_b, out32, static_cast<bf16*>(outb), M, H, F, d.status};
+  rc = check_cuda(launch_mlp(l, d.stream, d.num_sms), "fused mlp");
+  if (rc) return rc;
+  return sync_and_check(d, "fused mlp");
+}
+
 int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, void* out,
                     const int32_t* cu_dev, const int32_t* lens_host, int nseq, int heads,
                     int kv_heads, int head_dim, int causal) {

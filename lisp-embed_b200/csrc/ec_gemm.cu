@@ -11,6 +11,8 @@ namespace ec {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
+PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() { return g_encode; }
+
 bool gemm_init_driver() {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;

@@ -110,6 +110,27 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms);
 // encode function for TMA descriptors (driver entry point), set once
 bool gemm_init_driver();
 
+// ---- fused feed-forward block (ec_mlp.cu) -------------------------------------
+// out = LayerNorm(W2 . gelu(W1 . A + b1) + b2 + resid) for H in {128, 256, 384},
+// F % 128 == 0; writes the fp32 row (out32, may alias resid) and its bf16
+// copy (outb, may alias A).
+struct MlpLaunch {
+  const __nv_bfloat16* A;   // [M, H]
+  const __nv_bfloat16* W1;  // [F, H]
+  const __nv_bfloat16* W2;  // [H, F]
+  const float* b1;
+  const float* b2;
+  const float* resid;       // [M, H]
+  const float* ln_g;
+  const float* ln_b;
+  float* out32;
+  __nv_bfloat16* outb;
+  int M, H, F;
+  unsigned* status;
+};
+bool mlp_supported(int H, int F);
+cudaError_t launch_mlp(const MlpLaunch& l, cudaStream_t st, int num_sms);
+
 // ---- attention (ec_attn.cu) --------------------------------------------------
 struct AttnLaunch {
   const __nv_bfloat16* qkv;

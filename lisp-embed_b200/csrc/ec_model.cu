@@ -11,6 +11,7 @@
 // batch of packed sequences: every linear of every token of every sequence of
 // a layer is one tcgen05 GEMM launch.
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <numeric>
@@ -582,12 +583,25 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
         const int e0 = prof_begin(d);
         EC_TRY(rows(launch_ln(l1, st), "layernorm", TH * 10.0, e0));
       }
-      EC_TRY(gemm(hb, H, w.wff, F, H, w.bff, nullptr, ff, F, kEpiBf16Gelu));
-      EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
-      LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};
-      {
+      // the fused block is opt-in until it beats the unfused path (it is
+      // bound by streaming W1/W2 from L2 with 64 KB in flight per SM)
+      if (mlp_supported(H, F) && getenv("EC_FUSED_MLP")) {
+        // up + GELU + down + bias + residual + LayerNorm in one kernel
+        MlpLaunch ml{hb, w.wff, w.wout, w.bff, w.bout, h32, w.ln2g, w.ln2b, h32, hb, T, H, F,
+                     d.status};
         const int e0 = prof_begin(d);
-        EC_TRY(rows(launch_ln(l2, st), "layernorm", TH * 10.0, e0));
+        const cudaError_t e = launch_mlp(ml, st, d.num_sms);
+        prof_end(d, 0, 4.0 * T * H * F, 2.0 * T * H + 4.0 * H * F + 4.0 * T * H + 6.0 * T * H,
+                 e0);
+        EC_TRY(check_cuda(e, "fused mlp"));
+      } else {
+        EC_TRY(gemm(hb, H, w.wff, F, H, w.bff, nullptr, ff, F, kEpiBf16Gelu));
+        EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
+        LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};
+        {
+          const int e0 = prof_begin(d);
+          EC_TRY(rows(launch_ln(l2, st), "layernorm", TH * 10.0, e0));
+        }
       }
     }
     PoolArgs pa;

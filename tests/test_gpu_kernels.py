@@ -112,3 +112,37 @@ def test_attention(ec, hd, heads, kv, causal):
     ref = _attn_ref(qkv, lens, heads, kv, hd, 0, heads * hd, (heads + kv) * hd, causal)
     err = (out.float() - ref).abs().max().item()
     assert err < 2e-2, err
+
+
+def _ln_ref(x, g, b):
+    # bert::layernorm: (x - mean) / (sqrt(var) + 1e-12) * g + b
+    m = x.mean(-1, keepdim=True)
+    v = ((x - m) ** 2).mean(-1, keepdim=True)
+    return (x - m) / (v.sqrt() + 1e-12) * g + b
+
+
+@pytest.mark.parametrize("M,H,F", [(1, 384, 1536), (200, 384, 1536), (4097, 384, 1536),
+                                   (300, 256, 512), (129, 128, 256)])
+def test_fused_mlp(ec, M, H, F):
+    g = torch.Generator(device="cuda").manual_seed(M + H + F)
+    A = torch.randn(M, H, device="cuda", generator=g).bfloat16()
+    W1 = (0.05 * torch.randn(F, H, device="cuda", generator=g)).bfloat16()
+    W2 = (0.03 * torch.randn(H, F, device="cuda", generator=g)).bfloat16()
+    b1 = 0.1 * torch.randn(F, device="cuda", generator=g)
+    b2 = 0.1 * torch.randn(H, device="cuda", generator=g)
+    resid = torch.randn(M, H, device="cuda", generator=g)
+    lg = 1 + 0.1 * torch.randn(H, device="cuda", generator=g)
+    lb = 0.1 * torch.randn(H, device="cuda", generator=g)
+    out32 = torch.empty(M, H, device="cuda")
+    outb = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    ec.check(ec.lib().ecdbg_mlp(A.data_ptr(), W1.data_ptr(), W2.data_ptr(), b1.data_ptr(),
+                                b2.data_ptr(), resid.data_ptr(), lg.data_ptr(), lb.data_ptr(),
+                                out32.data_ptr(), outb.data_ptr(), M, H, F), "mlp")
+    u = _gelu_as(A.float() @ W1.float().t() + b1)
+    p = u.bfloat16().float()  # the intermediate is bf16 on chip
+    y = p @ W2.float().t() + b2 + resid
+    ref = _ln_ref(y, lg, lb)
+    err = (out32 - ref).abs().max().item()
+    assert err < 2e-2, err
+    assert (outb.float() - ref).abs().max().item() < 5e-2
