@@ -41,6 +41,7 @@ WORKLOADS = {
     "mpnet": ("mpnet-base", 2, 4096, "MPNet-base shape, 4096 seqs len U[64,384], mean pool"),
     "qwen3": ("qwen3-0.6b", 3, 2048, "Qwen3-0.6B shape BF16, 2048 seqs len U[128,512]+EOS, last"),
 }
+IVF_N, IVF_D, IVF_K, IVF_ITERS, IVF_SEED = 3_270_000, 384, 4096, 20, 4
 
 
 def parse_args():
@@ -49,7 +50,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="minilm")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["ivf", "query"], default="minilm")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -168,6 +169,133 @@ def cpu_baseline(model_dir, ids, offsets, seconds):
                       f"({threads} threads, one sequence per thread)"}
 
 
+def ivf_corpus_torch(n, d, k, seed, device):
+    """The IVF workload generated on the GPU: k centers uniform on the unit
+    sphere, x = normalize(center + 0.05 N(0, I)), fp32 (same distribution as
+    synth.make_ivf_corpus, drawn with torch's generator for speed)."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    centers = torch.randn(k, d, generator=g, device=device)
+    centers /= centers.norm(dim=1, keepdim=True)
+    labels = torch.randint(0, k, (n,), generator=g, device=device)
+    x = torch.empty(n, d, device=device)
+    step = 1 << 20
+    for s0 in range(0, n, step):
+        e = min(n, s0 + step)
+        blk = centers[labels[s0:e]] + 0.05 * torch.randn(e - s0, d, generator=g, device=device)
+        x[s0:e] = blk / blk.norm(dim=1, keepdim=True)
+    perm = torch.randperm(n, generator=g, device=device)
+    return x, perm
+
+
+def run_ivf(args, rank, world, local_rank):
+    """IVF build seconds: 20 Lloyd iterations over all 3.27M rows (k 4096,
+    init = first k rows of a seeded permutation, ann.lisp:83-86), rows
+    sharded over the ranks with one NCCL all-reduce of sums + counts per
+    iteration, then the inverted lists of each shard (ann::assign-all).
+    Inputs start in host memory; the timed region includes their upload."""
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from embedcuda import _lib, ann
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    x_dev, perm = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda")
+    j0 = (IVF_N + world - 1) // world * rank
+    j1 = min(IVF_N, j0 + (IVF_N + world - 1) // world)
+    mine = perm[j0:j1]
+    x_local = x_dev[mine].cpu().numpy()            # this rank's training rows, sample order
+    init = x_dev[perm[:IVF_K]].cpu().numpy()        # same on every rank
+    del x_dev
+    torch.cuda.empty_cache()
+    _lib.init([local_rank])
+    L = _lib.lib()
+    if world > 1:
+        idbuf = C.create_string_buffer(L.ec_comm_id_size())
+        if rank == 0:
+            _lib.check(L.ec_comm_get_id(idbuf), "comm id")
+        t = torch.frombuffer(bytearray(idbuf.raw), dtype=torch.uint8).cuda()
+        dist.broadcast(t, 0)
+        idbuf = C.create_string_buffer(bytes(t.cpu().numpy()), len(idbuf.raw))
+        _lib.check(L.ec_comm_init(rank, world, idbuf), "comm init")
+    local_sample = np.arange(len(x_local), dtype=np.int64)
+    # warm-up: one iteration (module load, NCCL channels)
+    ann.kmeans(x_local[:200000], local_sample[:200000], IVF_K, 1, init=init)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    cent = ann.kmeans(x_local, local_sample, IVF_K, IVF_ITERS, init=init)
+    t_km = time.perf_counter() - t0
+    counts, lists = ann.assign_all(x_local, cent)
+    t_all = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([t_km, t_all], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_km, t_all = float(tt[0]), float(tt[1])
+    if rank == 0:
+        flops = 2.0 * IVF_N * IVF_K * IVF_D * (IVF_ITERS + 1)
+        out = {"metric": "IVF build s", "value": t_all, "unit": "s", "n_gpus": world,
+               "steps": 1, "warmup": 1, "ms_per_step": 1000 * t_all, "higher_is_better": False,
+               "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+               "config": {"workload": "ivf-3.27Mx384", "n": IVF_N, "dim": IVF_D, "k": IVF_K,
+                          "iters": IVF_ITERS, "sample": "all rows, seeded permutation",
+                          "kmeans_s": t_km, "assign_all_s": t_all - t_km,
+                          "parallelism": f"rows sharded over {world} GPU(s), NCCL all-reduce"},
+               "achieved_tflops": flops / t_all / 1e12,
+               "note": "sequential single-float scores (bit-exact to ann.lisp on one GPU)"}
+        print(json.dumps(out), flush=True)
+    _lib.shutdown()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_query(args, rank, local_rank):
+    """p50 ms of one short MiniLM query end to end through the host API:
+    ec_embed_batch of ~10 token ids, then ec_ivf_search top-10 with nprobe 32
+    over the 3.27M x 384 IVF index (kb:kb-search without the text part)."""
+    if rank != 0:
+        return 0
+    import torch
+    from embedcuda import _lib, ann, kb, model, synth
+    torch.cuda.set_device(local_rank)
+    x_dev, perm = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda")
+    x = x_dev.cpu().numpy()
+    del x_dev
+    torch.cuda.empty_cache()
+    perm = perm.cpu().numpy().astype(np.int64)
+    _lib.init([local_rank])
+    cent = ann.kmeans(x, perm, IVF_K, IVF_ITERS)
+    counts, lists = ann.assign_all(x, cent)
+    kb.load_index(x, (cent, counts, lists))
+    d = synth.build_model_dir(synth.MINILM, 0, os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth"))
+    model.load_model(d)
+    rng = np.random.default_rng(7)
+    times = []
+    for i in range(101 + args.warmup):
+        ids = np.concatenate([[101], rng.integers(1000, 30522, 8), [102]]).astype(np.int32)
+        t0 = time.perf_counter()
+        q = model.embed(ids)
+        ids_, sc = kb.search_ivf(q, 10, nprobe=32)
+        el = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(el)
+    p50 = 1000 * float(np.median(times))
+    out = {"metric": "p50 query ms", "value": p50, "unit": "ms", "n_gpus": 1, "steps": 101,
+           "warmup": args.warmup, "ms_per_step": p50, "higher_is_better": False,
+           "scaling": "none", "vs_baseline": None, "dtype": "bf16+f32", "data": "synthetic",
+           "config": {"workload": "minilm-l6 query (10 ids) + ivf top-10 nprobe 32 over 3.27Mx384",
+                      "p90_ms": 1000 * float(np.percentile(times, 90)),
+                      "min_ms": 1000 * float(np.min(times))}}
+    print(json.dumps(out), flush=True)
+    _lib.shutdown()
+    return 0
+
+
 def run_reference(args, rank):
     """--impl reference: the oracle port of the reference's CPU path."""
     if rank != 0:
@@ -228,7 +356,18 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.workload in ("ivf", "query"):
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "reference arm is timed for the embedding workloads only"}))
+            return 0
         return run_reference(args, rank)
+    if not os.environ.get("EC_KEEP_NCCL_DEBUG"):
+        os.environ["NCCL_DEBUG"] = "WARN"
+    if args.workload == "ivf":
+        return run_ivf(args, rank, world, local_rank)
+    if args.workload == "query":
+        return run_query(args, rank, local_rank)
 
     # NCCL's version banner goes to stdout; the benchmark prints one JSON line
     if not os.environ.get("EC_KEEP_NCCL_DEBUG"):
