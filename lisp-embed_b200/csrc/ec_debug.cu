@@ -97,6 +97,11 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lens_host[a] > lens_host[b]; });
   for (int s : order)
     for (int q0 = 0; q0 < lens_host[s]; q0 += 64) blk.push_back(make_int2(s, q0));
+  const size_t n64 = blk.size();
+  int T = 0;
+  for (int s = 0; s < nseq; ++s) T += lens_host[s];
+  for (int s : order)
+    for (int q0 = 0; q0 < lens_host[s]; q0 += 128) blk.push_back(make_int2(s, q0));
   void* dblk = nullptr;
   rc = dev_alloc(d, &dblk, blk.size() * 8 + 8, "blocks");
   if (rc) return rc;
@@ -111,7 +116,12 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.ldo = heads * head_dim;
   a.cu = cu_dev;
   a.blocks = static_cast<const int2*>(dblk);
-  a.nblocks = static_cast<int>(blk.size());
+  a.nblocks = static_cast<int>(n64);
+  a.blocks128 = static_cast<const int2*>(dblk) + n64;
+  a.nblocks128 = static_cast<int>(blk.size() - n64);
+  a.rows = T;
+  a.status = d.status;
+  a.num_sms = d.num_sms;
   a.heads = heads;
   a.kv_group = heads / kv_heads;
   a.head_dim = head_dim;

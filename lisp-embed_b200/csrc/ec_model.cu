@@ -400,7 +400,7 @@ int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
 
 // --------------------------------------------------------------- forward --
 struct WsLayout {
-  size_t ids, pos, cu, blocks, h32, tmp, hb, qkv, ctx, ff, out, total;
+  size_t ids, pos, cu, blocks, blocks128, h32, tmp, hb, qkv, ctx, ff, out, total;
 };
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -415,6 +415,7 @@ static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
   L.pos = o; o += al256(T * 4);
   L.cu = o; o += al256((nseq + 1) * 4);
   L.blocks = o; o += al256(nblk * 8);
+  L.blocks128 = o; o += al256((T / 128 + nseq + 1) * 8);
   L.h32 = o; o += al256(T * m.H * 4);
   L.tmp = o; o += al256(T * m.H * 4);
   L.hb = o; o += al256(T * m.H * 2);
@@ -433,6 +434,7 @@ static int ensure_ws(Device& d, int T, int nseq) {
   const WsLayout L = layout_for(d.model, t2, s2);
   const size_t pin = static_cast<size_t>(t2) * 4 + (static_cast<size_t>(s2) + 1) * 4 +
                      (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
+                     (static_cast<size_t>(t2) / 128 + s2 + 1) * 8 + 512 +
                      static_cast<size_t>(s2) * d.model.H * 4 + 1024;
   if (!d.ws || L.total > d.ws_bytes) {
     if (d.ws) {
@@ -471,7 +473,7 @@ static int ensure_ws(Device& d, int T, int nseq) {
 
 // Run the forward for sequences seqs[s0..s1) (indices into offsets) that are
 // packed in `ids_dev` (already on the device) and write pooled rows to out.
-static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nblk,
+static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nblk, int nblk128,
                           double attn_pairs, float* out, int out_stride) {
   ModelW& m = d.model;
   char* ws = static_cast<char*>(d.ws);
@@ -545,6 +547,11 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
   at.causal = m.family == EC_FAMILY_LLAMA ? 1 : 0;
   at.relbias = m.relbias;
   at.rel_max = m.rel_max;
+  at.blocks128 = reinterpret_cast<const int2*>(ws + L.blocks128);
+  at.nblocks128 = nblk128;
+  at.rows = T;
+  at.status = d.status;
+  at.num_sms = d.num_sms;
   auto attention = [&]() -> int {
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_attention(at, st);
@@ -683,7 +690,8 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
 
 // Build the per-chunk host tables (cu offsets, attention blocks sorted by
 // descending length) into pinned staging and upload them.
-static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, int* nblk_out) {
+static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, int* nblk_out,
+                         int* nblk128_out) {
   const int nseq = static_cast<int>(lens.size());
   char* pin = static_cast<char*>(d.pin);
   int* hcu = reinterpret_cast<int*>(pin);
@@ -696,7 +704,15 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
   int nb = 0;
   for (int s : order)
     for (int q0 = 0; q0 < lens[s]; q0 += 64) hblk[nb++] = make_int2(s, q0);
+  int2* hblk128 = reinterpret_cast<int2*>(reinterpret_cast<char*>(hblk) + al256(static_cast<size_t>(nb) * 8));
+  int nb128 = 0;
+  for (int s : order)
+    for (int q0 = 0; q0 < lens[s]; q0 += 128) hblk128[nb128++] = make_int2(s, q0);
   char* ws = static_cast<char*>(d.ws);
+  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks128, hblk128, static_cast<size_t>(nb128) * 8,
+                                    cudaMemcpyHostToDevice, d.stream),
+                    "block upload"));
+  *nblk128_out = nb128;
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.cu, hcu, (nseq + 1) * 4, cudaMemcpyHostToDevice, d.stream),
                     "cu upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks, hblk, static_cast<size_t>(nb) * 8,
@@ -750,8 +766,8 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     std::vector<int> lens(nseq);
     for (int k = 0; k < nseq; ++k)
       lens[k] = static_cast<int>(offsets[seqs[i + k] + 1] - offsets[seqs[i + k]]);
-    int nblk = 0;
-    EC_TRY(upload_tables(d, L, lens, &nblk));
+    int nblk = 0, nblk128 = 0;
+    EC_TRY(upload_tables(d, L, lens, &nblk, &nblk128));
     char* ws = static_cast<char*>(d.ws);
     if (ids_dev) {
       EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, ids_dev + offsets[seqs[i]],
@@ -779,7 +795,7 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     for (int k = 0; k < nseq; ++k)
       pairs += m.family == EC_FAMILY_LLAMA ? 0.5 * lens[k] * (lens[k] + 1.0)
                                            : static_cast<double>(lens[k]) * lens[k];
-    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, nblk, pairs, dout, ostride));
+    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, nblk, nblk128, pairs, dout, ostride));
     if (!out_dev) {
       std::vector<float> hout(static_cast<size_t>(nseq) * m.H);
       EC_TRY(check_cuda(cudaMemcpyAsync(hout.data(), dout, hout.size() * 4,
