@@ -58,7 +58,7 @@ PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn();  // ec_gemm.cu
 
 template <int HD, int MODE>
 static cudaError_t run_fa(const AttnLaunch& l, cudaStream_t st) {
-  using Cfg = FaCfg<HD>;
+  using Cfg = FaCfg<HD, MODE>;
   static std::mutex mu;
   static bool set[64] = {};
   int dev = 0;
@@ -82,15 +82,16 @@ static cudaError_t run_fa(const AttnLaunch& l, cudaStream_t st) {
   CUtensorMap tm;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(l.ld), static_cast<cuuint64_t>(l.rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(l.ld) * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(Cfg::BOX_C), 128};
   cuuint32_t es[2] = {1, 1};
   if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(l.qkv), dims,
-          strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          Cfg::SW64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   FaArgs a;
   a.cu = l.cu;
-  a.qblocks = l.blocks128;
+  a.qinfo = l.blocks128;
   a.nqb = l.nblocks128;
   a.heads = l.heads;
   a.kv_group = l.kv_group;
@@ -112,7 +113,12 @@ static cudaError_t run_fa(const AttnLaunch& l, cudaStream_t st) {
 template <int HD>
 static cudaError_t run_fa_mode(const AttnLaunch& l, cudaStream_t st) {
   if (l.causal) return run_fa<HD, 2>(l, st);
-  if (l.relbias) return run_fa<HD, 1>(l, st);
+  if (l.relbias) {
+    // the relative-bias table does not fit beside double-buffered K/V and P
+    // at head dim 128; that combination uses the mma.sync kernel
+    if constexpr (HD == 128) return run_attn<HD, 1>(l, st);
+    else return run_fa<HD, 1>(l, st);
+  }
   return run_fa<HD, 0>(l, st);
 }
 
@@ -128,7 +134,8 @@ cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
   if (l.causal && l.relbias) return cudaErrorInvalidValue;
   const bool legacy = getenv("EC_LEGACY_ATTN") != nullptr || !l.blocks128 || l.rows <= 0;
   switch (l.head_dim) {
-    case 32: return run_mode<32>(l, st);
+    // head dim 32: the mma.sync kernel unless EC_TC_ATTN32 asks for tcgen05
+    case 32: return (legacy || !getenv("EC_TC_ATTN32")) ? run_mode<32>(l, st) : run_fa_mode<32>(l, st);
     case 64: return legacy ? run_mode<64>(l, st) : run_fa_mode<64>(l, st);
     case 128: return legacy ? run_mode<128>(l, st) : run_fa_mode<128>(l, st);
     default: return cudaErrorInvalidValue;

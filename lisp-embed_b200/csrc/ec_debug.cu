@@ -88,6 +88,12 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   std::lock_guard<std::mutex> lk(G().mu);
   clear_error();
   if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!qkv || !out || !cu_dev || !lens_host || nseq <= 0 || heads <= 0 || kv_heads <= 0 ||
+      heads % kv_heads || (head_dim != 32 && head_dim != 64 && head_dim != 128) ||
+      q_off + heads * head_dim > ld || k_off + kv_heads * head_dim > ld || v_off + kv_heads * head_dim > ld)
+    return set_error(EC_EINVAL, "bad attention arguments (heads %% kv_heads == 0, offsets inside ld)");
+  for (int s = 0; s < nseq; ++s)
+    if (lens_host[s] <= 0) return set_error(EC_EINVAL, "sequence %d is empty", s);
   Device& d = *G().devs[0];
   int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
   if (rc) return rc;
@@ -98,14 +104,22 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   for (int s : order)
     for (int q0 = 0; q0 < lens_host[s]; q0 += 64) blk.push_back(make_int2(s, q0));
   const size_t n64 = blk.size();
-  int T = 0;
-  for (int s = 0; s < nseq; ++s) T += lens_host[s];
+  std::vector<int> starts(nseq + 1, 0);
+  for (int s = 0; s < nseq; ++s) starts[s + 1] = starts[s] + lens_host[s];
+  const int T = starts[nseq];
+  std::vector<int4> blk128;
   for (int s : order)
-    for (int q0 = 0; q0 < lens_host[s]; q0 += 128) blk.push_back(make_int2(s, q0));
+    for (int q0 = 0; q0 < lens_host[s]; q0 += 128)
+      blk128.push_back(make_int4(starts[s], lens_host[s], q0, 0));
+  const size_t b64 = (n64 * 8 + 15) & ~static_cast<size_t>(15);
   void* dblk = nullptr;
-  rc = dev_alloc(d, &dblk, blk.size() * 8 + 8, "blocks");
+  rc = dev_alloc(d, &dblk, b64 + blk128.size() * 16 + 16, "blocks");
   if (rc) return rc;
-  rc = check_cuda(cudaMemcpy(dblk, blk.data(), blk.size() * 8, cudaMemcpyHostToDevice), "blocks");
+  rc = check_cuda(cudaMemcpy(dblk, blk.data(), n64 * 8, cudaMemcpyHostToDevice), "blocks");
+  if (!rc)
+    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64, blk128.data(), blk128.size() * 16,
+                               cudaMemcpyHostToDevice),
+                    "blocks");
   AttnLaunch a;
   a.qkv = static_cast<const bf16*>(qkv);
   a.ld = ld;
@@ -117,8 +131,8 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.cu = cu_dev;
   a.blocks = static_cast<const int2*>(dblk);
   a.nblocks = static_cast<int>(n64);
-  a.blocks128 = static_cast<const int2*>(dblk) + n64;
-  a.nblocks128 = static_cast<int>(blk.size() - n64);
+  a.blocks128 = reinterpret_cast<const int4*>(static_cast<char*>(dblk) + b64);
+  a.nblocks128 = static_cast<int>(blk128.size());
   a.rows = T;
   a.status = d.status;
   a.num_sms = d.num_sms;
@@ -130,7 +144,7 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.rel_max = 0;
   if (!rc) rc = check_cuda(launch_attention(a, d.stream), "attention");
   if (!rc) rc = sync_and_check(d, "attention");
-  dev_free(d, dblk, blk.size() * 8 + 8);
+  dev_free(d, dblk, b64 + blk128.size() * 16 + 16);
   return rc;
 }
 

@@ -7,8 +7,8 @@
 //   per 128-key block j:
 //     S_j = Q K_j^T          tcgen05.mma (A = Q, B = K, both K-major in smem)
 //                            -> TMEM, double-buffered (columns 0 / 128)
-//     softmax warps          one thread per query row reads its 128 scores
-//                            from TMEM twice (max, then exp), keeps the
+//     softmax warps          two threads per query row read its 128 scores
+//                            from TMEM twice (max, then exp), keep the
 //                            running max / sum, writes P_j (bf16) to a
 //                            128B-swizzled K-major shared-memory tile
 //     O += P_j V_j           tcgen05.mma (A = P, B = V read MN-major straight
@@ -18,7 +18,8 @@
 //
 // Persistent CTAs walk the work items (long sequences first); warp 0 issues
 // TMA loads (Q once per item, K/V per block, 2 stages, next item prefetched),
-// warp 1 issues the MMAs (S_{j+1} before PV_j), warps 2..5 run the softmax.
+// warp 1 issues the MMAs (S_{j+1} before PV_j), warps 2..9 run the softmax,
+// two per query row (one per 64-key half of each block).
 // All waits are bounded.
 #pragma once
 
@@ -28,7 +29,7 @@ namespace ec {
 
 struct FaArgs {
   const int* cu;        // [nseq + 1]
-  const int2* qblocks;  // (sequence, first query row), 128-row blocks, long first
+  const int4* qinfo;    // per 128-row query block: (first token, length, first row, 0), long first
   int nqb;
   int heads, kv_group;
   int q_off, k_off, v_off;
@@ -40,30 +41,55 @@ struct FaArgs {
   unsigned* status;
 };
 
-constexpr int kFaThreads = 192;  // producer, MMA, 4 softmax warps
+constexpr int kFaThreads = 320;  // producer, MMA, 8 softmax warps
 
-template <int HD>
+template <int HD, int MODE>
 struct FaCfg {
-  static_assert(HD == 64 || HD == 128, "head dim");
-  static constexpr int AT = HD / 64;                      // 128-byte atoms per row
-  static constexpr uint32_t TILE = AT * 16384;            // 128 rows x HD bf16
-  static constexpr uint32_t P_BYTES = 2 * 16384;          // 128 x 128 bf16, 2 K-atoms
-  static constexpr uint32_t BIAS_BYTES = 8192;
-  static constexpr size_t SMEM_BYTES = 1024 + TILE /*Q*/ + 4 * TILE /*K,V x2*/ + P_BYTES +
-                                       BIAS_BYTES + 512;
+  static_assert(HD == 32 || HD == 64 || HD == 128, "head dim");
+  // Q / K / V rows of HD bf16: 64-byte rows with 64-byte swizzle for HD 32,
+  // else 128-byte atoms with 128-byte swizzle (two atoms side by side for 128)
+  static constexpr bool SW64 = HD == 32;
+  static constexpr int AT = HD == 128 ? 2 : 1;             // atoms along the head dim
+  static constexpr uint32_t ATOM = SW64 ? 8192 : 16384;    // 128 rows of one atom
+  static constexpr uint32_t TILE = AT * ATOM;              // 128 rows x HD bf16
+  static constexpr uint32_t GROUP = SW64 ? 512 : 1024;     // 8-row group stride
+  static constexpr int BOX_C = SW64 ? 32 : 64;             // TMA box columns
+  static constexpr uint32_t P_BYTES = 2 * 2 * 16384;       // 2 buffers of 128 x 128 bf16
+  static constexpr uint32_t BIAS_BYTES = MODE == 1 ? 8192 : 0;  // bias of i - j + 127 + L
+  static constexpr uint32_t XCH_BYTES = 2 * 8 * 32 * 4;    // partner row max / sum slots
+  // no alignment slack: the kernel checks that dynamic shared memory starts
+  // on a 1024-byte boundary (it does when the kernel has no static smem)
+  static constexpr size_t SMEM_BYTES = TILE /*Q*/ + 4 * TILE /*K,V x2*/ + P_BYTES +
+                                       BIAS_BYTES + XCH_BYTES + 512;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
   static constexpr uint32_t O_COL = 256;
 };
 
-// MN-major operand, 128-byte swizzle: 64 elements contiguous along MN, rows
-// along K 128 B apart, 8-row K groups 1024 B apart (SBO), 64-element MN
-// blocks `lbo` bytes apart (LBO).
-__device__ __forceinline__ uint64_t desc_sw128_mnmajor(uint32_t smem_addr, uint32_t lbo) {
+// K-major operand tile: rows of 64 B (64-byte swizzle, 512 B groups) or
+// 128 B (128-byte swizzle, 1024 B groups)
+template <bool SW64>
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t smem_addr) {
+  if constexpr (!SW64) return desc_sw128_kmajor(smem_addr);
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
+  return d;
+}
+
+// MN-major operand (V read from its row-major tile): 64 (128-byte swizzle) or
+// 32 (64-byte swizzle) elements contiguous along MN, K rows one row apart,
+// 8-row K groups one group apart (SBO), MN blocks `lbo` bytes apart (LBO).
+template <bool SW64>
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t smem_addr, uint32_t lbo) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>((SW64 ? 512u : 1024u) >> 4) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(2u) << 61;
+  d |= static_cast<uint64_t>(SW64 ? 4u : 2u) << 61;
   return d;
 }
 
@@ -77,33 +103,39 @@ __device__ __forceinline__ float fa_exp2(float x) {
 template <int HD, int MODE>
 __global__ void __launch_bounds__(kFaThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQKV, const FaArgs a) {
-  using Cfg = FaCfg<HD>;
+  using Cfg = FaCfg<HD, MODE>;
   constexpr int AT = Cfg::AT;
   constexpr bool kBias = MODE == 1;
   constexpr bool kCausal = MODE == 2;
   constexpr uint32_t IDESC_S = make_idesc(1, 128, 128);
   constexpr uint32_t IDESC_PV = make_idesc(1, 128, HD) | (1u << 16);  // B MN-major
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // swizzled tiles need 1024-byte alignment
+    if (threadIdx.x == 0) report(a.status, kDevBadArg);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + Cfg::TILE;            // 2 stages
   uint8_t* sV = sK + 2 * Cfg::TILE;        // 2 stages
   uint8_t* sP = sV + 2 * Cfg::TILE;
   float* sBias = reinterpret_cast<float*>(sP + Cfg::P_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + Cfg::BIAS_BYTES);
+  float* sX = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sBias) + Cfg::BIAS_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sX) + Cfg::XCH_BYTES);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 1;
   uint64_t* kv_full = q_empty + 1;   // [2]
   uint64_t* kv_empty = kv_full + 2;  // [2]
   uint64_t* s_full = kv_empty + 2;   // [2]
   uint64_t* s_empty = s_full + 2;    // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* p_empty = p_full + 1;
-  uint64_t* o_full = p_empty + 1;
-  uint64_t* o_empty = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  uint64_t* p_full = s_empty + 2;    // [2]
+  uint64_t* p_empty = p_full + 2;    // [2]
+  uint64_t* o_full = p_empty + 2;    // [2]: PV of even / odd global block index
+  uint64_t* o_empty = o_full + 2;
+  uint64_t* xbar = o_empty + 1;  // [4 quads][2 slots] partner rendezvous, 64 threads
+  uint64_t* bbar = xbar + 8;     // bias table rendezvous, 256 threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -117,12 +149,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], 8);
     }
-    mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
-    mbar_init(o_full, 1);
-    mbar_init(o_empty, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 8);
+      mbar_init(&p_empty[i], 1);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(o_empty, 8);
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    mbar_init(bbar, 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -138,11 +174,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   // item -> (sequence base, length, first query row, head, key blocks)
   auto item_info = [&](int t, int& base, int& L, int& q0, int& h, int& nkb) {
-    const int2 qb = a.qblocks[t / a.heads];
+    const int4 qb = a.qinfo[t / a.heads];
     h = t % a.heads;
-    base = a.cu[qb.x];
-    L = a.cu[qb.x + 1] - base;
-    q0 = qb.y;
+    base = qb.x;
+    L = qb.y;
+    q0 = qb.z;
     const int kv_end = kCausal ? min(L, q0 + 128) : L;
     nkb = (kv_end + 127) >> 7;
   };
@@ -164,7 +200,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         q_ph ^= 1;
         mbar_arrive_expect_tx(q_full, Cfg::TILE);
         for (int at = 0; at < AT; ++at)
-          tma_load_2d(sQ + at * 16384, &tmQKV, q_full, a.q_off + h * HD + at * 64, base + q0);
+          tma_load_2d(sQ + at * Cfg::ATOM, &tmQKV, q_full, a.q_off + h * HD + at * 64, base + q0);
         for (int j = 0; j < nkb; ++j) {
           if (!mbar_wait(&kv_empty[st], kv_ph ^ 1, abort_flag)) {
             ok = false;
@@ -172,9 +208,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           }
           mbar_arrive_expect_tx(&kv_full[st], 2 * Cfg::TILE);
           for (int at = 0; at < AT; ++at) {
-            tma_load_2d(sK + st * Cfg::TILE + at * 16384, &tmQKV, &kv_full[st],
+            tma_load_2d(sK + st * Cfg::TILE + at * Cfg::ATOM, &tmQKV, &kv_full[st],
                         a.k_off + kvh * HD + at * 64, base + j * 128);
-            tma_load_2d(sV + st * Cfg::TILE + at * 16384, &tmQKV, &kv_full[st],
+            tma_load_2d(sV + st * Cfg::TILE + at * Cfg::ATOM, &tmQKV, &kv_full[st],
                         a.v_off + kvh * HD + at * 64, base + j * 128);
           }
           if (++st == 2) {
@@ -192,9 +228,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       int st = 0;
-      uint32_t kv_ph = 0, q_ph = 0, p_ph = 0, oe_ph = 0;
-      uint32_t se_ph[2] = {0, 0};
+      uint32_t kv_ph = 0, q_ph = 0, oe_ph = 0;
+      uint32_t se_ph[2] = {0, 0}, pf_ph[2] = {0, 0};
       int sbuf = 0;
+      long long pv_count = 0;  // global PV index: P buffer and o_full barrier parity
       bool ok = true;
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       auto mma_s = [&](int& used_st) -> bool {
@@ -205,9 +242,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const uint32_t k_addr = smem_u32(sK + st * Cfg::TILE);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16(tmem_base + sbuf * 128, desc_sw128_kmajor(q_addr + off),
-                   desc_sw128_kmajor(k_addr + off), IDESC_S, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * Cfg::ATOM + (kk & 3) * 32;
+          umma_f16(tmem_base + sbuf * 128, desc_kmajor<Cfg::SW64>(q_addr + off),
+                   desc_kmajor<Cfg::SW64>(k_addr + off), IDESC_S, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sbuf]);
         sbuf ^= 1;
@@ -223,19 +260,22 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           if (!mbar_wait(o_empty, oe_ph ^ 1, abort_flag)) return false;
           oe_ph ^= 1;
         }
-        if (!mbar_wait(p_full, p_ph, abort_flag)) return false;
-        p_ph ^= 1;
+        const int pb = static_cast<int>(pv_count & 1);
+        if (!mbar_wait(&p_full[pb], pf_ph[pb], abort_flag)) return false;
+        pf_ph[pb] ^= 1;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + used_st * Cfg::TILE);
+        const uint32_t pa = p_addr + pb * 32768;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_f16(tmem_base + Cfg::O_COL,
-                   desc_sw128_kmajor(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32),
-                   desc_sw128_mnmajor(v_addr + kk * 2048, 16384), IDESC_PV,
+                   desc_sw128_kmajor(pa + (kk >> 2) * 16384 + (kk & 3) * 32),
+                   desc_mnmajor<Cfg::SW64>(v_addr + kk * 2 * Cfg::GROUP, Cfg::ATOM), IDESC_PV,
                    (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&kv_empty[used_st]);
-        umma_commit(p_empty);
-        umma_commit(o_full);
+        umma_commit(&p_empty[pb]);
+        umma_commit(&o_full[pb]);
+        ++pv_count;
         return true;
       };
       for (int t = blockIdx.x; ok && t < nitems; t += gridDim.x) {
@@ -267,29 +307,63 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
   } else {
     // --------------------------------------------------------------- softmax
+    // warps 2..9: TMEM lane quadrant warp % 4 (query rows), key half
+    // (warp - 2) / 4: keys [64 * half, 64 * half + 64) of every block, which
+    // is exactly one K-atom of P; partners exchange row max / sum in smem.
+    const int sw = warp - 2;
     const int quad = warp & 3;
+    const int half = sw >> 2;
     const int r = quad * 32 + lane;  // query row in the block == TMEM lane
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    constexpr int OH = HD / 2;       // O columns handled by this warp
     int sbuf = 0;
     uint32_t sf_ph[2] = {0, 0};
-    uint32_t pe_ph = 0;
+    uint32_t pe_ph[2] = {0, 0};
     long long pv_done = 0;  // PVs of earlier items (global PV index base)
     bool ok = true;
-    uint8_t* p_row0 = sP + r * 128;          // K-atom 0 (keys 0..63)
-    uint8_t* p_row1 = sP + 16384 + r * 128;  // K-atom 1 (keys 64..127)
+    uint8_t* p_row = sP + half * 16384 + r * 128;  // this warp's K-atom of P buffer 0
+    // wait for PV with global index g: o_full[g & 1] completes once per PV of
+    // that parity, so its phase parity is (g >> 1) & 1.  Every PV up to g - 2
+    // is already known complete (the P-buffer waits), so the parity test is
+    // never two phases behind.
+    auto wait_pv = [&](long long g) -> bool {
+      return mbar_wait(&o_full[g & 1], static_cast<uint32_t>((g >> 1) & 1), abort_flag);
+    };
+    float* xch = sX;                               // [2 slots][8 warps][32]
+    int xslot = 0;
+    uint32_t xph[2] = {0, 0}, bph = 0;
+    // partner's value for this row; false if the rendezvous gave up
+    auto exchange = [&](float v, float& other) -> bool {
+      xch[(xslot * 8 + sw) * 32 + lane] = v;
+      const bool fine = mbar_sync(&xbar[quad * 2 + xslot], xph[xslot], abort_flag);
+      other = xch[(xslot * 8 + (sw ^ 4)) * 32 + lane];
+      xslot ^= 1;
+      return fine;
+    };
     for (int t = blockIdx.x; ok && t < nitems; t += gridDim.x) {
       int base, L, q0, h, nkb;
       item_info(t, base, L, q0, h, nkb);
       const int q = q0 + r;  // query position in the sequence
       if (kBias) {
-        named_bar(1, 128);  // previous item's readers are done
+        if (!mbar_sync(bbar, bph, abort_flag)) {  // previous item's readers are done
+          ok = false;
+          break;
+        }
+        // sBias[i - j + 127 + L] for every (query i, key j) a block can pair:
+        // i <= L + 126, j <= L + 126, so the index stays in [1, 2L + 253]
         const int nb = 2 * a.rel_max - 1;
         const float* src = a.relbias + static_cast<size_t>(h) * nb;
-        for (int i = threadIdx.x - 64; i < 2 * L - 1 && i < 2048; i += 128)
-          sBias[i] = src[i - (L - 1) + a.rel_max - 1];
-        named_bar(1, 128);
+        for (int i = threadIdx.x - 64; i < 2048; i += 256) {
+          const int dlt = i - 127 - L;  // i - j
+          sBias[i] = (dlt > -(a.rel_max) && dlt < a.rel_max) ? src[dlt + a.rel_max - 1] : 0.f;
+        }
+        if (!mbar_sync(bbar, bph, abort_flag)) {
+          ok = false;
+          break;
+        }
       }
-      float m_run = -INFINITY, l_run = 0.f;
+      const bool warp_live = q0 + quad * 32 < L;  // both partners agree
+      float m_run = -INFINITY, l_part = 0.f;
       for (int j = 0; j < nkb; ++j) {
         if (!mbar_wait(&s_full[sbuf], sf_ph[sbuf], abort_flag)) {
           ok = false;
@@ -297,122 +371,178 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
         sf_ph[sbuf] ^= 1;
         tc_fence_after();
-        const uint32_t s_addr = t_lane + sbuf * 128;
-        const int k0 = j * 128;
-        const bool need_mask = (k0 + 128 > L) || (kCausal && k0 + 127 > q0);
-        // pass 1: row max of the logits (log2 units)
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(s_addr + c * 32, v);
+        const int kh0 = j * 128 + half * 64;  // first key of this warp's half
+        const uint32_t s_addr = t_lane + sbuf * 128 + half * 64;
+        const bool need_mask = (kh0 + 64 > L) || (kCausal && kh0 + 63 > q0);
+        const int live_chunks = max(0, min(2, (L - kh0 + 31) >> 5));
+        if (warp_live) {
+          float mx = -INFINITY;
+          uint32_t v[2][32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            if (c < live_chunks) tmem_ld_32x32b_x32(s_addr + c * 32, v[c]);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float x = __uint_as_float(v[i]) * a.scale_log2;
-            const int key = k0 + c * 32 + i;
-            if (kBias) {
-              const int bi = q - key + (L - 1);
-              x += sBias[bi < 0 ? 0 : (bi > 2046 ? 2046 : bi)];
-            }
-            if (need_mask && (key >= L || (kCausal && key > q))) x = -INFINITY;
-            mx = fmaxf(mx, x);
-          }
-        }
-        // lazy rescale: keep the stale max unless the new one is 2^8 larger
-        if (mx > m_run + 8.0f) {
-          const float corr = fa_exp2(m_run - mx);
-          if (j > 0) {
-            // O holds PV of blocks < j: wait for PV(j-1), then scale it
-            const long long g = pv_done + j - 1;
-            if (!mbar_wait(o_full, static_cast<uint32_t>(g & 1), abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < HD / 32; ++c) {
-              uint32_t v[32];
-              tmem_ld_32x32b_x32(t_lane + Cfg::O_COL + c * 32, v);
-              tmem_wait_ld();
+          for (int c = 0; c < 2; ++c) {
+            if (c >= live_chunks) continue;
+            if (!need_mask && !kBias) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
-              tmem_st_32x32b_x32(t_lane + Cfg::O_COL + c * 32, v);
+              for (int i = 0; i < 32; i += 2)
+                mx = fmaxf(mx, fmaxf(__uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1])));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                float x = __uint_as_float(v[c][i]);
+                const int key = kh0 + c * 32 + i;
+                if (kBias) x = fmaf(x, a.scale_log2, sBias[q - key + 127 + L]);
+                if (need_mask && (key >= L || (kCausal && key > q))) x = -INFINITY;
+                mx = fmaxf(mx, x);
+              }
             }
-            tmem_wait_st();
           }
-          l_run *= corr;
-          m_run = mx;
+          if (!kBias) mx *= a.scale_log2;
+          float mo;
+          if (!exchange(mx, mo)) {
+            ok = false;
+            break;
+          }
+          mx = fmaxf(mx, mo);
+          // lazy rescale: keep the stale max unless the new one is 2^8 larger
+          if (mx > m_run + 8.0f) {
+            const float corr = fa_exp2(m_run - mx);
+            if (j > 0) {
+              // O holds PV of blocks < j: wait for PV(j-1), then scale our half
+              if (!wait_pv(pv_done + j - 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t o_addr = t_lane + Cfg::O_COL + half * OH;
+              if constexpr (OH >= 32) {
+#pragma unroll 1
+                for (int c = 0; c < OH / 32; ++c) {
+                  uint32_t v[32];
+                  tmem_ld_32x32b_x32(o_addr + c * 32, v);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
+                  tmem_st_32x32b_x32(o_addr + c * 32, v);
+                }
+              } else {
+                uint32_t v[16];
+                tmem_ld_32x32b_x16(o_addr, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
+                tmem_st_32x32b_x16(o_addr, v);
+              }
+              tmem_wait_st();
+            }
+            l_part *= corr;
+            m_run = mx;
+          }
         }
-        // pass 2: P = exp2(logit - m_run) to shared memory, row sum
-        if (!mbar_wait(p_empty, pe_ph ^ 1, abort_flag)) {
+        // pass 2: P = exp2(logit - m_run) into this warp's K-atom of P buffer
+        // pb (the PV two blocks back has released it), row sum
+        const int pb = static_cast<int>((pv_done + j) & 1);
+        if (!mbar_wait(&p_empty[pb], pe_ph[pb] ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        pe_ph ^= 1;
-        float sum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(s_addr + c * 32, v);
+        pe_ph[pb] ^= 1;
+        uint8_t* prow = p_row + pb * 32768;
+        if (warp_live) {
+          float sum = 0.f;
+          const float nm = -m_run;
+          uint32_t v[2][32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            if (c < live_chunks) tmem_ld_32x32b_x32(s_addr + c * 32, v[c]);
           tmem_wait_ld();
-          float p[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float x = __uint_as_float(v[i]) * a.scale_log2;
-            const int key = k0 + c * 32 + i;
-            if (kBias) {
-              const int bi = q - key + (L - 1);
-              x += sBias[bi < 0 ? 0 : (bi > 2046 ? 2046 : bi)];
+          for (int c = 0; c < 2; ++c) {
+            float p[32];
+            if (c < live_chunks) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int key = kh0 + c * 32 + i;
+                const float x = __uint_as_float(v[c][i]);
+                float e = kBias ? fa_exp2(fmaf(x, a.scale_log2, sBias[q - key + 127 + L]) + nm)
+                                : fa_exp2(fmaf(x, a.scale_log2, nm));
+                if (need_mask && (key >= L || (kCausal && key > q))) e = 0.f;
+                p[i] = e;
+                sum += e;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) p[i] = 0.f;  // keys past the sequence
             }
-            float e = fa_exp2(x - m_run);
-            if (need_mask && (key >= L || (kCausal && key > q))) e = 0.f;
-            p[i] = e;
-            sum += e;
-          }
-          uint8_t* prow = (c < 2) ? p_row0 : p_row1;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int c16 = (c & 1) * 4 + u;  // 16-byte chunk within the 128-byte row
-            *reinterpret_cast<uint4*>(prow + ((c16 ^ (r & 7)) << 4)) =
-                make_uint4(pack_bf16(p[8 * u], p[8 * u + 1]), pack_bf16(p[8 * u + 2], p[8 * u + 3]),
-                           pack_bf16(p[8 * u + 4], p[8 * u + 5]),
-                           pack_bf16(p[8 * u + 6], p[8 * u + 7]));
+            for (int u = 0; u < 4; ++u) {
+              const int c16 = c * 4 + u;  // 16-byte chunk within the 128-byte row
+              *reinterpret_cast<uint4*>(prow + ((c16 ^ (r & 7)) << 4)) =
+                  make_uint4(pack_bf16(p[8 * u], p[8 * u + 1]), pack_bf16(p[8 * u + 2], p[8 * u + 3]),
+                             pack_bf16(p[8 * u + 4], p[8 * u + 5]),
+                             pack_bf16(p[8 * u + 6], p[8 * u + 7]));
+            }
           }
+          l_part += sum;
         }
-        l_run += sum;
         tc_fence_before();
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&s_empty[sbuf]);
-          mbar_arrive(p_full);
+          mbar_arrive(&p_full[pb]);
         }
         sbuf ^= 1;
       }
       if (!ok) break;
-      // final: O / l for rows inside the sequence
-      const long long g = pv_done + nkb - 1;
-      if (!mbar_wait(o_full, static_cast<uint32_t>(g & 1), abort_flag)) {
+      // final: O / l for rows inside the sequence, this warp's column half
+      float l_other;
+      if (!exchange(l_part, l_other)) {
+        ok = false;
+        break;
+      }
+      const float l_run = l_part + l_other;
+      if (!wait_pv(pv_done + nkb - 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = a.out + static_cast<size_t>(base + q) * a.ldo + h * HD;
+      __nv_bfloat16* orow = a.out + static_cast<size_t>(base + q) * a.ldo + h * HD + half * OH;
+      const uint32_t o_addr = t_lane + Cfg::O_COL + half * OH;
+      if constexpr (OH >= 32) {
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_lane + Cfg::O_COL + c * 32, v);
+        for (int c = 0; c < OH / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(o_addr + c * 32, v);
+          tmem_wait_ld();
+          if (q < L) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              dst[u] = make_uint4(
+                  pack_bf16(__uint_as_float(v[8 * u]) * inv, __uint_as_float(v[8 * u + 1]) * inv),
+                  pack_bf16(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv),
+                  pack_bf16(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv),
+                  pack_bf16(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv));
+          }
+        }
+      } else {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(o_addr, v);
         tmem_wait_ld();
         if (q < L) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            dst[u] = make_uint4(pack_bf16(__uint_as_float(v[8 * u]) * inv, __uint_as_float(v[8 * u + 1]) * inv),
-                                pack_bf16(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv),
-                                pack_bf16(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv),
-                                pack_bf16(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv));
+          for (int u = 0; u < 2; ++u)
+            dst[u] = make_uint4(
+                pack_bf16(__uint_as_float(v[8 * u]) * inv, __uint_as_float(v[8 * u + 1]) * inv),
+                pack_bf16(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv),
+                pack_bf16(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv),
+                pack_bf16(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv));
         }
       }
       tc_fence_before();

@@ -145,14 +145,14 @@ struct AttnLaunch {
   int causal;
   const float* relbias;  // [heads][2 * rel_max - 1], pre-scaled by log2(e)
   int rel_max;
-  const int2* blocks128; // (sequence, first query row) per 128-row block, long first
+  const int4* blocks128; // (first token, length, first query row, 0) per 128-row block, long first
   int nblocks128;
   int rows;              // packed token rows in qkv (T)
   unsigned* status;
   int num_sms;
 };
-// head_dim 64 / 128: tcgen05 kernel (ec_fa.cuh) unless EC_LEGACY_ATTN is set;
-// head_dim 32: mma.sync kernel (ec_attn.cuh)
+// tcgen05 kernel (ec_fa.cuh) for head_dim 32 / 64 / 128; the mma.sync kernel
+// (ec_attn.cuh) when EC_LEGACY_ATTN is set
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t st);
 
 }  // namespace ec

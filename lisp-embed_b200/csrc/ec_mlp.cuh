@@ -81,7 +81,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint64_t* p_empty = p_full + 2;   // [2]
   uint64_t* y_full = p_empty + 2;
   uint64_t* y_empty = y_full + 1;
-  float* xsum = reinterpret_cast<float*>(y_empty + 1);  // [8 warps][32] partial row sums
+  uint64_t* xbar = y_empty + 1;  // [4 quads] partner rendezvous, 64 threads
+  float* xsum = reinterpret_cast<float*>(xbar + 4);  // [8 warps][32] partial row sums
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xsum + 8 * 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     }
     mbar_init(y_full, 1);
     mbar_init(y_empty, 8);
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     // (both buffers are idle once y_full has arrived)
     uint8_t* p_mine0 = smP + half * kMlpStage + quad * 4096;
     uint8_t* p_mine1 = p_mine0 + 2 * kMlpStage;
-    uint32_t u_phase = 0, y_phase = 0;
+    uint32_t u_phase = 0, y_phase = 0, x_phase = 0;
     uint32_t pe_phase[2] = {0, 0};
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
@@ -369,7 +371,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       tmem_wait_st();
       // mean over the full row: partner warp (other half) holds the rest
       xsum[ew * 32 + lane] = part;
-      named_bar(1 + (ew & 3), 64);
+      if (!mbar_sync(&xbar[ew & 3], x_phase, abort_flag)) {
+        ok = false;
+        break;
+      }
       const float mean = (part + xsum[(ew ^ 4) * 32 + lane]) / static_cast<float>(H);
       float q2 = 0.f;
       for (int c = 0; c < HC; ++c) {
@@ -382,9 +387,16 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           q2 += d * d;
         }
       }
-      named_bar(1 + (ew & 3), 64);  // both partners have read the mean slots
+      // both partners have read the mean slots before they are rewritten
+      if (!mbar_sync(&xbar[ew & 3], x_phase, abort_flag)) {
+        ok = false;
+        break;
+      }
       xsum[ew * 32 + lane] = q2;
-      named_bar(1 + (ew & 3), 64);
+      if (!mbar_sync(&xbar[ew & 3], x_phase, abort_flag)) {
+        ok = false;
+        break;
+      }
       const float var = (q2 + xsum[(ew ^ 4) * 32 + lane]) / static_cast<float>(H);
       const float stdv = sqrtf(var) + 1e-12f;  // bert.lisp:169
       for (int c = 0; c < HC; ++c) {

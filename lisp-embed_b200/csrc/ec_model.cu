@@ -415,7 +415,7 @@ static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
   L.pos = o; o += al256(T * 4);
   L.cu = o; o += al256((nseq + 1) * 4);
   L.blocks = o; o += al256(nblk * 8);
-  L.blocks128 = o; o += al256((T / 128 + nseq + 1) * 8);
+  L.blocks128 = o; o += al256((T / 128 + nseq + 1) * 16);
   L.h32 = o; o += al256(T * m.H * 4);
   L.tmp = o; o += al256(T * m.H * 4);
   L.hb = o; o += al256(T * m.H * 2);
@@ -434,7 +434,7 @@ static int ensure_ws(Device& d, int T, int nseq) {
   const WsLayout L = layout_for(d.model, t2, s2);
   const size_t pin = static_cast<size_t>(t2) * 4 + (static_cast<size_t>(s2) + 1) * 4 +
                      (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
-                     (static_cast<size_t>(t2) / 128 + s2 + 1) * 8 + 512 +
+                     (static_cast<size_t>(t2) / 128 + s2 + 1) * 16 + 512 +
                      static_cast<size_t>(s2) * d.model.H * 4 + 1024;
   if (!d.ws || L.total > d.ws_bytes) {
     if (d.ws) {
@@ -547,7 +547,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
   at.causal = m.family == EC_FAMILY_LLAMA ? 1 : 0;
   at.relbias = m.relbias;
   at.rel_max = m.rel_max;
-  at.blocks128 = reinterpret_cast<const int2*>(ws + L.blocks128);
+  at.blocks128 = reinterpret_cast<const int4*>(ws + L.blocks128);
   at.nblocks128 = nblk128;
   at.rows = T;
   at.status = d.status;
@@ -704,12 +704,12 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
   int nb = 0;
   for (int s : order)
     for (int q0 = 0; q0 < lens[s]; q0 += 64) hblk[nb++] = make_int2(s, q0);
-  int2* hblk128 = reinterpret_cast<int2*>(reinterpret_cast<char*>(hblk) + al256(static_cast<size_t>(nb) * 8));
+  int4* hblk128 = reinterpret_cast<int4*>(reinterpret_cast<char*>(hblk) + al256(static_cast<size_t>(nb) * 8));
   int nb128 = 0;
   for (int s : order)
-    for (int q0 = 0; q0 < lens[s]; q0 += 128) hblk128[nb128++] = make_int2(s, q0);
+    for (int q0 = 0; q0 < lens[s]; q0 += 128) hblk128[nb128++] = make_int4(hcu[s], lens[s], q0, 0);
   char* ws = static_cast<char*>(d.ws);
-  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks128, hblk128, static_cast<size_t>(nb128) * 8,
+  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks128, hblk128, static_cast<size_t>(nb128) * 16,
                                     cudaMemcpyHostToDevice, d.stream),
                     "block upload"));
   *nblk128_out = nb128;
