@@ -137,6 +137,27 @@ int ec_ivf_search(const float *q, int nq, int nprobe, int topk, int64_t *ids,
  * (kb.lisp:186-200).  Ties -> lower row id first. */
 int ec_flat_search(const float *q, int nq, int topk, int64_t *ids, float *scores);
 
+/* Flat search like ec_flat_search, over caller-owned DEVICE buffers on the
+ * current device, that allocates no device memory (no counterpart in the
+ * reference: kb::top-k-brute, kb.lisp:186-200, always allocates).  For hosts
+ * that cannot let the library allocate mid-request: an image that reserves
+ * its device arena up front (the allocation would fail once the arena is
+ * taken) or a request loop that cannot absorb the device-wide synchronisation
+ * cudaMalloc / cudaFree may cause.  d_x: n x d vectors, d_q: nq x d queries
+ * (both 16-byte aligned, d % 4 == 0, d <= 8192, 0 < n < 2^31), d_ids /
+ * d_scores: nq x topk (1 <= topk <= 64), same order and ties as
+ * ec_flat_search.  Enqueued on `stream` (a cudaStream_t, NULL = legacy
+ * default stream) and not synchronised.  The candidate lists live in one
+ * static 16 MiB device array per device: a call needs
+ * nq x min(256, ceil(n / 8192)) x topk x 8 bytes of it (nq <= 65535) and
+ * larger calls fail with EC_EINVAL before any launch.  Every call on a device
+ * shares that array, so calls whose kernels overlap in time race; calls in
+ * order on one stream do not.  The first call on each device looks up the
+ * array's address, so make it before any stream capture begins.  Needs no
+ * ec_init. */
+int ec_flat_search_noalloc(const float *d_x, int64_t n, int d, const float *d_q, int nq,
+                           int topk, int64_t *d_ids, float *d_scores, void *stream);
+
 /* ---- multi-process (one process per GPU) ------------------------------------ */
 
 /* Size of the opaque NCCL unique id (128 bytes). */

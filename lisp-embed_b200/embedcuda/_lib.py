@@ -60,6 +60,7 @@ _SIGS = {
     "ec_index_load": (C.c_int, [FP, C.c_int64, C.c_int, FP, C.c_int, U32P, U32P]),
     "ec_ivf_search": (C.c_int, [FP, C.c_int, C.c_int, C.c_int, I64P, FP]),
     "ec_flat_search": (C.c_int, [FP, C.c_int, C.c_int, I64P, FP]),
+    "ec_flat_search_noalloc": (C.c_int, [P, C.c_int64, C.c_int, P, C.c_int, C.c_int, P, P, P]),
     "ec_comm_id_size": (C.c_int, []),
     "ec_comm_get_id": (C.c_int, [P]),
     "ec_comm_init": (C.c_int, [C.c_int, C.c_int, P]),
