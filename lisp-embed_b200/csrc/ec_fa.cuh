@@ -41,7 +41,10 @@ struct FaArgs {
   unsigned* status;
 };
 
-constexpr int kFaThreads = 320;  // producer, MMA, 8 softmax warps
+// warps 0..7 softmax (two warpgroups), 8 TMA producer, 9 MMA issuer; with
+// ten warps a thread gets at most 168 registers (three warps share one SM
+// sub-partition's 16K registers), which the softmax code fits without spills
+constexpr int kFaThreads = 320;
 
 template <int HD, int MODE>
 struct FaCfg {
@@ -162,8 +165,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmQKV);
-  if (warp == 1) {
+  if (warp == 8 && lane == 0) tma_prefetch_desc(&tmQKV);
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     nkb = (kv_end + 127) >> 7;
   };
 
-  if (warp == 0) {
+  if (warp == 8) {
     // --------------------------------------------------------------- producer
     if (elect_one()) {
       int st = 0;
@@ -224,20 +227,22 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         *abort_flag = 1;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       int st = 0;
       uint32_t kv_ph = 0, q_ph = 0, oe_ph = 0;
-      uint32_t se_ph[2] = {0, 0}, pf_ph[2] = {0, 0};
+      // phase parities of the two-entry barrier pairs, one bit per entry
+      // (bit arrays, not indexed arrays, so they stay in registers)
+      uint32_t se_bits = 0, pf_bits = 0;
       int sbuf = 0;
       long long pv_count = 0;  // global PV index: P buffer and o_full barrier parity
       bool ok = true;
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       auto mma_s = [&](int& used_st) -> bool {
         if (!mbar_wait(&kv_full[st], kv_ph, abort_flag)) return false;
-        if (!mbar_wait(&s_empty[sbuf], se_ph[sbuf] ^ 1, abort_flag)) return false;
-        se_ph[sbuf] ^= 1;
+        if (!mbar_wait(&s_empty[sbuf], ((se_bits >> sbuf) & 1u) ^ 1u, abort_flag)) return false;
+        se_bits ^= 1u << sbuf;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sK + st * Cfg::TILE);
 #pragma unroll
@@ -261,8 +266,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           oe_ph ^= 1;
         }
         const int pb = static_cast<int>(pv_count & 1);
-        if (!mbar_wait(&p_full[pb], pf_ph[pb], abort_flag)) return false;
-        pf_ph[pb] ^= 1;
+        if (!mbar_wait(&p_full[pb], (pf_bits >> pb) & 1u, abort_flag)) return false;
+        pf_bits ^= 1u << pb;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + used_st * Cfg::TILE);
         const uint32_t pa = p_addr + pb * 32768;
@@ -305,20 +310,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         *abort_flag = 1;
       }
     }
-  } else {
+  } else if (warp < 8) {
     // --------------------------------------------------------------- softmax
-    // warps 2..9: TMEM lane quadrant warp % 4 (query rows), key half
-    // (warp - 2) / 4: keys [64 * half, 64 * half + 64) of every block, which
-    // is exactly one K-atom of P; partners exchange row max / sum in smem.
-    const int sw = warp - 2;
+    // warps 0..7: TMEM lane quadrant warp % 4 (query rows), key half
+    // warp / 4: keys [64 * half, 64 * half + 64) of every block, which is
+    // exactly one K-atom of P; partners exchange row max / sum in smem.
+    const int sw = warp;
     const int quad = warp & 3;
     const int half = sw >> 2;
     const int r = quad * 32 + lane;  // query row in the block == TMEM lane
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     constexpr int OH = HD / 2;       // O columns handled by this warp
     int sbuf = 0;
-    uint32_t sf_ph[2] = {0, 0};
-    uint32_t pe_ph[2] = {0, 0};
+    uint32_t sf_bits = 0, pe_bits = 0;  // phase parity per buffer, one bit each
     long long pv_done = 0;  // PVs of earlier items (global PV index base)
     bool ok = true;
     uint8_t* p_row = sP + half * 16384 + r * 128;  // this warp's K-atom of P buffer 0
@@ -331,11 +335,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     };
     float* xch = sX;                               // [2 slots][8 warps][32]
     int xslot = 0;
-    uint32_t xph[2] = {0, 0}, bph = 0;
+    uint32_t xbits = 0, bph = 0;
     // partner's value for this row; false if the rendezvous gave up
     auto exchange = [&](float v, float& other) -> bool {
       xch[(xslot * 8 + sw) * 32 + lane] = v;
-      const bool fine = mbar_sync(&xbar[quad * 2 + xslot], xph[xslot], abort_flag);
+      mbar_arrive(&xbar[quad * 2 + xslot]);
+      const bool fine = mbar_wait(&xbar[quad * 2 + xslot], (xbits >> xslot) & 1u, abort_flag);
+      xbits ^= 1u << xslot;
       other = xch[(xslot * 8 + (sw ^ 4)) * 32 + lane];
       xslot ^= 1;
       return fine;
@@ -353,7 +359,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // i <= L + 126, j <= L + 126, so the index stays in [1, 2L + 253]
         const int nb = 2 * a.rel_max - 1;
         const float* src = a.relbias + static_cast<size_t>(h) * nb;
-        for (int i = threadIdx.x - 64; i < 2048; i += 256) {
+        for (int i = threadIdx.x; i < 2048; i += 256) {
           const int dlt = i - 127 - L;  // i - j
           sBias[i] = (dlt > -(a.rel_max) && dlt < a.rel_max) ? src[dlt + a.rel_max - 1] : 0.f;
         }
@@ -365,11 +371,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const bool warp_live = q0 + quad * 32 < L;  // both partners agree
       float m_run = -INFINITY, l_part = 0.f;
       for (int j = 0; j < nkb; ++j) {
-        if (!mbar_wait(&s_full[sbuf], sf_ph[sbuf], abort_flag)) {
+        if (!mbar_wait(&s_full[sbuf], (sf_bits >> sbuf) & 1u, abort_flag)) {
           ok = false;
           break;
         }
-        sf_ph[sbuf] ^= 1;
+        sf_bits ^= 1u << sbuf;
         tc_fence_after();
         const int kh0 = j * 128 + half * 64;  // first key of this warp's half
         const uint32_t s_addr = t_lane + sbuf * 128 + half * 64;
@@ -377,22 +383,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const int live_chunks = max(0, min(2, (L - kh0 + 31) >> 5));
         if (warp_live) {
           float mx = -INFINITY;
-          uint32_t v[2][32];
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-            if (c < live_chunks) tmem_ld_32x32b_x32(s_addr + c * 32, v[c]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            if (c >= live_chunks) continue;
+#pragma unroll 1
+          for (int c = 0; c < live_chunks; ++c) {
+            uint32_t v[1][32];
+            tmem_ld_32x32b_x32(s_addr + c * 32, v[0]);
+            tmem_wait_ld();
             if (!need_mask && !kBias) {
 #pragma unroll
               for (int i = 0; i < 32; i += 2)
-                mx = fmaxf(mx, fmaxf(__uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1])));
+                mx = fmaxf(mx, fmaxf(__uint_as_float(v[0][i]), __uint_as_float(v[0][i + 1])));
             } else {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                float x = __uint_as_float(v[c][i]);
+                float x = __uint_as_float(v[0][i]);
                 const int key = kh0 + c * 32 + i;
                 if (kBias) x = fmaf(x, a.scale_log2, sBias[q - key + 127 + L]);
                 if (need_mask && (key >= L || (kCausal && key > q))) x = -INFINITY;
@@ -445,11 +448,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // pass 2: P = exp2(logit - m_run) into this warp's K-atom of P buffer
         // pb (the PV two blocks back has released it), row sum
         const int pb = static_cast<int>((pv_done + j) & 1);
-        if (!mbar_wait(&p_empty[pb], pe_ph[pb] ^ 1, abort_flag)) {
+        if (!mbar_wait(&p_empty[pb], ((pe_bits >> pb) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
-        pe_ph[pb] ^= 1;
+        pe_bits ^= 1u << pb;
         uint8_t* prow = p_row + pb * 32768;
         if (warp_live) {
           float sum = 0.f;
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     while (globaltimer_ns() - t0 < 2000000ull) {
     }
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
