@@ -27,6 +27,13 @@ int ecdbg_mlp(const void *A, const void *W1, const void *W2, const float *b1, co
               const float *resid, const float *ln_g, const float *ln_b, float *out32,
               void *outb, int M, int H, int F);
 
+/* GEMM + bias + residual + LayerNorm: out32 = LN(A . W^T + bias + resid) * g
+ * + b (fp32 [M, N], may alias resid) and outb = bf16 of it; A bf16 [M, K],
+ * W bf16 [N, K]; N in {384, 768, 1024} (one row per CTA cluster). */
+int ecdbg_gemm_ln(const void *A, const void *W, int M, int N, int K, const float *bias,
+                  const float *resid, const float *ln_g, const float *ln_b, float *out32,
+                  void *outb);
+
 /* Varlen attention over packed bf16 rows qkv[T, ld]; cu[nseq + 1] (device,
  * int32) token offsets; lens on the host.  out[T, heads * head_dim] bf16. */
 int ecdbg_attention(const void *qkv, int ld, int q_off, int k_off, int v_off, void *out,

@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include "ec_attn.cuh"
+#include "ec_attn_short.cuh"
 #include "ec_fa.cuh"
 #include "ec_kernels.h"
 
@@ -129,15 +130,90 @@ static cudaError_t run_mode(const AttnLaunch& l, cudaStream_t st) {
   return run_attn<HD, 0>(l, st);
 }
 
+// sequences [n_long, nseq) of the launch, one CTA per (sequence, head)
+template <int HD, int MODE, int BK, int MINB>
+static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
+  using S = ShortAttnSmem<HD, MODE>;
+  static_assert(kShortAttnMaxLen == kAttnShortCap, "short-kernel capacity");
+  static std::mutex mu;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_short_kernel<HD, MODE, BK, MINB>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(S::MAX_BYTES));
+      if (e != cudaSuccess) return e;
+      set[dev] = true;
+    }
+  }
+  if (l.max_short_len <= 0 || l.max_short_len > kShortAttnMaxLen) return cudaErrorInvalidValue;
+  ShortAttnArgs a;
+  a.qkv = l.qkv;
+  a.ld = l.ld;
+  a.q_off = l.q_off;
+  a.k_off = l.k_off;
+  a.v_off = l.v_off;
+  a.out = l.out;
+  a.ldo = l.ldo;
+  a.seqs = l.seqs;
+  a.first = l.n_long;
+  a.heads = l.heads;
+  a.kv_group = l.kv_group;
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  a.relbias = l.relbias;
+  a.rel_max = l.rel_max;
+  a.kcap = (l.max_short_len + 15) & ~15;
+  dim3 grid(l.nseq - l.n_long, l.heads);
+  attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int HD>
+static cudaError_t run_short_mode(const AttnLaunch& l, cudaStream_t st) {
+  // head dim 32 fits five CTAs per SM (94 registers, 40 KB of K/V); the
+  // register budget for that measured fastest among 64/128-key blocks and
+  // 4..6 CTAs per SM on MiniLM batches
+  constexpr int MINB = HD == 32 ? 5 : 1;
+  if (l.causal) return run_short<HD, 2, 64, MINB>(l, st);
+  if (l.relbias) return run_short<HD, 1, 64, MINB>(l, st);
+  return run_short<HD, 0, 64, MINB>(l, st);
+}
+
+// Sequences longer than kAttnShortCap go to the tcgen05 kernel (their
+// 128-row blocks are the prefix of the table), the rest to the short kernel.
+template <int HD>
+static cudaError_t run_split(const AttnLaunch& l, cudaStream_t st) {
+  if (l.n_long > 0) {
+    AttnLaunch lg = l;
+    lg.nblocks128 = l.nblocks128_long;
+    const cudaError_t e = run_fa_mode<HD>(lg, st);
+    if (e != cudaSuccess) return e;
+  }
+  return l.nseq > l.n_long ? run_short_mode<HD>(l, st) : cudaSuccess;
+}
+
 cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
   if (l.nblocks <= 0) return cudaSuccess;
   if (l.causal && l.relbias) return cudaErrorInvalidValue;
-  const bool legacy = getenv("EC_LEGACY_ATTN") != nullptr || !l.blocks128 || l.rows <= 0;
+  if (getenv("EC_LEGACY_ATTN") != nullptr || !l.blocks128 || l.rows <= 0) {
+    switch (l.head_dim) {
+      case 32: return run_mode<32>(l, st);
+      case 64: return run_mode<64>(l, st);
+      case 128: return run_mode<128>(l, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  // head dims 32 / 64: short sequences on the shared-memory kernel unless
+  // EC_NO_SHORT_ATTN; head dim 64 opts in with EC_SHORT_ATTN64
+  const bool split = l.seqs && getenv("EC_NO_SHORT_ATTN") == nullptr;
   switch (l.head_dim) {
-    // head dim 32: the mma.sync kernel unless EC_TC_ATTN32 asks for tcgen05
-    case 32: return (legacy || !getenv("EC_TC_ATTN32")) ? run_mode<32>(l, st) : run_fa_mode<32>(l, st);
-    case 64: return legacy ? run_mode<64>(l, st) : run_fa_mode<64>(l, st);
-    case 128: return legacy ? run_mode<128>(l, st) : run_fa_mode<128>(l, st);
+    case 32: return split ? run_split<32>(l, st) : run_fa_mode<32>(l, st);
+    case 64: return split && getenv("EC_SHORT_ATTN64") ? run_split<64>(l, st) : run_fa_mode<64>(l, st);
+    case 128: return run_fa_mode<128>(l, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -1,0 +1,244 @@
+// ec_attn_short.cuh -- attention for sequences of at most kShortAttnMaxLen
+// tokens, the common case of sentence embedding (MiniLM / BERT batches of
+// 16..256 tokens).
+//
+// Same arithmetic as ec_attn.cuh (softmax(Q K^T * scale + bias) V per
+// sequence and head: bert::encoder-layer bert.lisp:226-248, the MPNet bias of
+// bert::mpnet-layer :408-423, causal llama::layer-forward llama.lisp:255-271),
+// organised for short sequences: one CTA per (sequence, head) copies the
+// head's whole K and V into shared memory once, then each warp walks 16-row
+// query tiles on its own -- no block-wide barrier inside the loop, no 64-row
+// query padding, and K/V leave HBM once per (sequence, head).  Math is
+// mma.sync.m16n8k16 bf16 -> fp32 with the online softmax in registers over
+// 64-key blocks.
+#pragma once
+
+#include "ec_attn.cuh"
+
+namespace ec {
+
+constexpr int kShortAttnMaxLen = 256;  // keys resident in shared memory
+constexpr int kShortAttnThreads = 128;
+
+struct ShortAttnArgs {
+  const __nv_bfloat16* qkv;  // packed rows, row stride ld elements
+  int ld;
+  int q_off, k_off, v_off;
+  __nv_bfloat16* out;        // [T, heads * HD], row stride ldo
+  int ldo;
+  const int2* seqs;          // (first token, length) per sequence, longest first
+  int first;                 // index of the first sequence this launch handles
+  int heads, kv_group;
+  float scale_log2;          // log2(e) / sqrt(head_dim)
+  const float* relbias;      // MODE 1: [heads][2 * rel_max - 1] (* log2 e)
+  int rel_max;
+  int kcap;                  // K/V rows reserved in shared memory: the longest
+                             // sequence of the launch rounded up to 16
+};
+
+template <int HD, int MODE>
+struct ShortAttnSmem {
+  static constexpr int LDS = HD + 8;  // padded rows: conflict-free ldmatrix
+  static size_t bytes(int kcap) {
+    return static_cast<size_t>(2) * kcap * LDS * 2 + (MODE == 1 ? static_cast<size_t>(2) * kcap * 4 : 0);
+  }
+  static constexpr size_t MAX_BYTES =
+      static_cast<size_t>(2) * kShortAttnMaxLen * LDS * 2 + (MODE == 1 ? 2 * kShortAttnMaxLen * 4 : 0);
+};
+
+// BK: keys per online-softmax block (64 or 128); MINB: CTAs per SM the
+// register budget is sized for
+template <int HD, int MODE, int BK, int MINB>
+__global__ void __launch_bounds__(kShortAttnThreads, MINB)
+    attn_short_kernel(const ShortAttnArgs a) {
+  constexpr int NT = BK / 8;     // 8-key n-tiles per block
+  constexpr bool kBias = MODE == 1;
+  constexpr bool kCausal = MODE == 2;
+  constexpr int LDS = ShortAttnSmem<HD, MODE>::LDS;
+  constexpr int NT_D = HD / 8;   // n-tiles of the output
+  constexpr int KS_D = HD / 16;  // k-steps over the head dim
+  constexpr int CH = HD / 8;     // 16-byte chunks per row
+  extern __shared__ __align__(16) uint8_t short_smem[];
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(short_smem);
+  __nv_bfloat16* sV = sK + a.kcap * LDS;
+  float* sBias = reinterpret_cast<float*>(sV + a.kcap * LDS);
+
+  const int2 sq = a.seqs[a.first + blockIdx.x];
+  const int base = sq.x, L = sq.y;
+  const int h = blockIdx.y;
+  const int kvh = h / a.kv_group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Lr = (L + 15) & ~15;  // keys rounded up to whole 16-key MMA steps
+
+  // K and V of this head: rows [0, L) copied, rows [L, Lr) zeroed so that the
+  // masked tail of the last step multiplies zeros, never stale values
+  for (int i = threadIdx.x; i < Lr * CH; i += kShortAttnThreads) {
+    const int r = i / CH, c = i % CH;
+    const bool live = r < L;
+    const size_t g = static_cast<size_t>(base + (live ? r : 0)) * a.ld;
+    cp_async16(sK + r * LDS + c * 8, a.qkv + g + a.k_off + kvh * HD + c * 8, live);
+    cp_async16(sV + r * LDS + c * 8, a.qkv + g + a.v_off + kvh * HD + c * 8, live);
+  }
+  cp_async_commit();
+  if (kBias) {
+    // sBias[i - j + L - 1] for query i, key j < L
+    const int nb = 2 * a.rel_max - 1;
+    const float* src = a.relbias + static_cast<size_t>(h) * nb;
+    for (int i = threadIdx.x; i < 2 * L - 1; i += kShortAttnThreads) {
+      const int dlt = i - (L - 1);
+      sBias[i] = (dlt > -a.rel_max && dlt < a.rel_max) ? src[dlt + a.rel_max - 1] : 0.f;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  const float sc = kBias ? 1.0f : a.scale_log2;
+  for (int tile = warp; tile * 16 < L; tile += kShortAttnThreads / 32) {
+    const int q0 = tile * 16;
+    const int row_a = q0 + (lane >> 2), row_b = row_a + 8;
+    // Q fragments straight from global memory (rows past L read as zero)
+    uint32_t qf[KS_D][4];
+    {
+      const __nv_bfloat16* qa = a.qkv + static_cast<size_t>(base + row_a) * a.ld + a.q_off + h * HD;
+      const __nv_bfloat16* qb = qa + static_cast<size_t>(8) * a.ld;
+#pragma unroll
+      for (int ks = 0; ks < KS_D; ++ks) {
+        const int c = ks * 16 + (lane & 3) * 2;
+        qf[ks][0] = row_a < L ? *reinterpret_cast<const uint32_t*>(qa + c) : 0u;
+        qf[ks][1] = row_b < L ? *reinterpret_cast<const uint32_t*>(qb + c) : 0u;
+        qf[ks][2] = row_a < L ? *reinterpret_cast<const uint32_t*>(qa + c + 8) : 0u;
+        qf[ks][3] = row_b < L ? *reinterpret_cast<const uint32_t*>(qb + c + 8) : 0u;
+      }
+    }
+    float o[NT_D][4];
+#pragma unroll
+    for (int n = 0; n < NT_D; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+    const int kv_end = kCausal ? min(L, q0 + 16) : L;
+    for (int k0 = 0; k0 < kv_end; k0 += BK) {
+      const int nt_live = min(NT, (kv_end - k0 + 7) >> 3);  // live 8-key n-tiles
+      const bool need_mask = (k0 + BK > L) || (kCausal && k0 + BK - 1 > q0);
+      float s[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS_D; ++ks) {
+#pragma unroll
+        for (int n = 0; n < NT; n += 2) {
+          if (n < nt_live) {
+            uint32_t b[4];
+            const int mi = lane >> 3;
+            const int key = k0 + n * 8 + (mi >> 1) * 8 + (lane & 7);
+            ldsm_x4(b, sK + key * LDS + ks * 16 + (mi & 1) * 8);
+            mma_bf16_16816(s[n], qf[ks], b[0], b[1]);
+            mma_bf16_16816(s[n + 1], qf[ks], b[2], b[3]);
+          }
+        }
+      }
+      if (kBias) {
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
+            const int qr = (e < 2) ? row_a : row_b;
+            const int bi = qr - key + (L - 1);
+            s[n][e] = fmaf(s[n][e], a.scale_log2, sBias[bi < 0 ? 0 : (bi > 2 * L - 2 ? 2 * L - 2 : bi)]);
+          }
+      }
+      if (need_mask) {
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = k0 + n * 8 + (lane & 3) * 2 + (e & 1);
+            const int qr = (e < 2) ? row_a : row_b;
+            if (key >= L || (kCausal && key > qr)) s[n][e] = -INFINITY;
+          }
+      }
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
+        mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      // key 0 is visible to every row (0 < L, 0 <= row), so after the first
+      // block every running max is finite: no -inf - -inf below
+      float corr[2], rs[2] = {0.f, 0.f}, nm[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float mnew = fmaxf(m_r[r], mx[r] * sc);
+        corr[r] = fast_exp2(m_r[r] - mnew);
+        m_r[r] = mnew;
+        nm[r] = -mnew;
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        if (n < nt_live) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p = fast_exp2(fmaf(s[n][e], sc, nm[e >> 1]));
+            s[n][e] = p;
+            rs[e >> 1] += p;
+          }
+        } else {
+          s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_r[r] = l_r[r] * corr[r] + rs[r];
+      }
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
+      // O += P V over the live 16-key steps (rows past L of V are zero)
+#pragma unroll
+      for (int t = 0; t < NT / 2; ++t) {
+        if (2 * t < nt_live) {
+          uint32_t pa[4];
+          pa[0] = pack2_bf16(s[2 * t][0], s[2 * t][1]);
+          pa[1] = pack2_bf16(s[2 * t][2], s[2 * t][3]);
+          pa[2] = pack2_bf16(s[2 * t + 1][0], s[2 * t + 1][1]);
+          pa[3] = pack2_bf16(s[2 * t + 1][2], s[2 * t + 1][3]);
+#pragma unroll
+          for (int n = 0; n < NT_D; n += 2) {
+            uint32_t b[4];
+            const int mi = lane >> 3;
+            const int key = k0 + t * 16 + (mi & 1) * 8 + (lane & 7);
+            const int d = (n + (mi >> 1)) * 8;
+            ldsm_x4_t(b, sV + key * LDS + d);
+            mma_bf16_16816(o[n], pa, b[0], b[1]);
+            mma_bf16_16816(o[n + 1], pa, b[2], b[3]);
+          }
+        }
+      }
+    }
+    const float inv0 = l_r[0] > 0.f ? 1.f / l_r[0] : 0.f;
+    const float inv1 = l_r[1] > 0.f ? 1.f / l_r[1] : 0.f;
+    __nv_bfloat16* out_h = a.out + h * HD;
+#pragma unroll
+    for (int n = 0; n < NT_D; ++n) {
+      const int d = n * 8 + (lane & 3) * 2;
+      if (row_a < L)
+        *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_a) * a.ldo + d) =
+            pack2_bf16(o[n][0] * inv0, o[n][1] * inv0);
+      if (row_b < L)
+        *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_b) * a.ldo + d) =
+            pack2_bf16(o[n][2] * inv1, o[n][3] * inv1);
+    }
+  }
+}
+
+}  // namespace ec

@@ -82,6 +82,25 @@ int ecdbg_mlp(const void* A, const void* W1, const void* W2, const float* b1, co
   return sync_and_check(d, "fused mlp");
 }
 
+int ecdbg_gemm_ln(const void* A, const void* W, int M, int N, int K, const float* bias,
+                  const float* resid, const float* ln_g, const float* ln_b, float* out32,
+                  void* outb) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!gemm_ln_supported(N)) return set_error(EC_EUNSUPPORTED, "gemm+layernorm N %d", N);
+  if (!A || !W || !resid || !ln_g || !ln_b || !out32 || !outb || M <= 0 || K <= 0 || K % 64)
+    return set_error(EC_EINVAL, "bad gemm+layernorm arguments");
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  GemmLnLaunch g{static_cast<const bf16*>(A), K, static_cast<const bf16*>(W), M, N, K, bias, resid,
+                 ln_g, ln_b, out32, static_cast<bf16*>(outb), d.status};
+  rc = check_cuda(launch_gemm_ln(g, d.stream, d.num_sms), "gemm+layernorm");
+  if (rc) return rc;
+  return sync_and_check(d, "gemm+layernorm");
+}
+
 int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, void* out,
                     const int32_t* cu_dev, const int32_t* lens_host, int nseq, int heads,
                     int kv_heads, int head_dim, int causal) {
@@ -108,18 +127,33 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   for (int s = 0; s < nseq; ++s) starts[s + 1] = starts[s] + lens_host[s];
   const int T = starts[nseq];
   std::vector<int4> blk128;
-  for (int s : order)
+  std::vector<int2> seqs;
+  int n_long = 0, nblk128_long = 0, max_short = 0;
+  for (int s : order) {
     for (int q0 = 0; q0 < lens_host[s]; q0 += 128)
       blk128.push_back(make_int4(starts[s], lens_host[s], q0, 0));
+    seqs.push_back(make_int2(starts[s], lens_host[s]));
+    if (lens_host[s] > kAttnShortCap) {
+      ++n_long;
+      nblk128_long = static_cast<int>(blk128.size());
+    } else {
+      max_short = std::max(max_short, lens_host[s]);
+    }
+  }
   const size_t b64 = (n64 * 8 + 15) & ~static_cast<size_t>(15);
+  const size_t b128 = blk128.size() * 16;
+  const size_t tbytes = b64 + b128 + seqs.size() * 8 + 16;
   void* dblk = nullptr;
-  rc = dev_alloc(d, &dblk, b64 + blk128.size() * 16 + 16, "blocks");
+  rc = dev_alloc(d, &dblk, tbytes, "blocks");
   if (rc) return rc;
   rc = check_cuda(cudaMemcpy(dblk, blk.data(), n64 * 8, cudaMemcpyHostToDevice), "blocks");
   if (!rc)
-    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64, blk128.data(), blk128.size() * 16,
-                               cudaMemcpyHostToDevice),
+    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64, blk128.data(), b128, cudaMemcpyHostToDevice),
                     "blocks");
+  if (!rc)
+    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64 + b128, seqs.data(), seqs.size() * 8,
+                               cudaMemcpyHostToDevice),
+                    "sequences");
   AttnLaunch a;
   a.qkv = static_cast<const bf16*>(qkv);
   a.ld = ld;
@@ -136,6 +170,11 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.rows = T;
   a.status = d.status;
   a.num_sms = d.num_sms;
+  a.seqs = reinterpret_cast<const int2*>(static_cast<char*>(dblk) + b64 + b128);
+  a.nseq = nseq;
+  a.n_long = n_long;
+  a.nblocks128_long = nblk128_long;
+  a.max_short_len = max_short;
   a.heads = heads;
   a.kv_group = heads / kv_heads;
   a.head_dim = head_dim;
@@ -144,7 +183,7 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.rel_max = 0;
   if (!rc) rc = check_cuda(launch_attention(a, d.stream), "attention");
   if (!rc) rc = sync_and_check(d, "attention");
-  dev_free(d, dblk, b64 + blk128.size() * 16 + 16);
+  dev_free(d, dblk, tbytes);
   return rc;
 }
 

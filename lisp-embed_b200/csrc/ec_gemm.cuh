@@ -102,6 +102,28 @@ __device__ __forceinline__ float gelu_as(float x) {
   return fmaf(hx, se, hx);
 }
 
+// gelu_as on two values with the packed fp32 pipe (fma/mul .f32x2 issue two
+// lanes' worth of arithmetic per instruction); same formula, same constants.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 gelu_as2(float2 x) {
+  const float2 z = __fmul2_rn(x, f2(0.70710678118654752f));
+  const float2 az = make_float2(fabsf(z.x), fabsf(z.y));
+  const float2 den = __ffma2_rn(f2(0.3275911f), az, f2(1.0f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  // -poly(t), Horner with negated coefficients, so that 1 - poly * e is one fma
+  float2 p = __ffma2_rn(t, f2(-1.061405429f), f2(1.453152027f));
+  p = __ffma2_rn(t, p, f2(-1.421413741f));
+  p = __ffma2_rn(t, p, f2(0.284496736f));
+  p = __ffma2_rn(t, p, f2(-0.254829592f));
+  p = __fmul2_rn(t, p);
+  const float2 q = __fmul2_rn(__fmul2_rn(az, az), f2(-1.4426950408889634f));
+  const float2 e = make_float2(ex2_approx(q.x), ex2_approx(q.y));
+  const float2 r = __ffma2_rn(p, e, f2(1.0f));
+  const float2 se = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
+  const float2 hx = __fmul2_rn(x, f2(0.5f));
+  return __ffma2_rn(hx, se, hx);
+}
+
 // x * sigmoid(x) (llama::silu, llama.lisp:119-122)
 __device__ __forceinline__ float silu_f(float x) {
   return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
@@ -338,9 +360,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < 4; ++j) {
             float x[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              x[e] = v[8 * j + e];
-              if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_as(x[e]);
+            for (int e = 0; e < 8; e += 2) {
+              float2 xx = make_float2(v[8 * j + e], v[8 * j + e + 1]);
+              if constexpr (EPI == kEpiBf16Gelu) xx = gelu_as2(xx);
+              x[e] = xx.x;
+              x[e + 1] = xx.y;
             }
             *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
                 make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),

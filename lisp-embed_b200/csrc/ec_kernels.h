@@ -110,6 +110,25 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms);
 // encode function for TMA descriptors (driver entry point), set once
 bool gemm_init_driver();
 
+// ---- GEMM + bias + residual + LayerNorm (ec_gemm_ln.cuh) ---------------------
+// out32 = LN(A . W^T + bias + resid) * g + b (fp32, may alias resid) and
+// outb = bf16(out32); whole rows of N in {384, 768, 1024} per CTA cluster.
+struct GemmLnLaunch {
+  const __nv_bfloat16* A;
+  int lda;
+  const __nv_bfloat16* W;  // [N, K]
+  int M, N, K;
+  const float* bias;
+  const float* resid;      // [M, N]
+  const float* ln_g;
+  const float* ln_b;
+  float* out32;            // [M, N]
+  __nv_bfloat16* outb;     // [M, N]
+  unsigned* status;
+};
+bool gemm_ln_supported(int N);
+cudaError_t launch_gemm_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms);
+
 // ---- fused feed-forward block (ec_mlp.cu) -------------------------------------
 // out = LayerNorm(W2 . gelu(W1 . A + b1) + b2 + resid) for H in {128, 256, 384},
 // F % 128 == 0; writes the fp32 row (out32, may alias resid) and its bf16
@@ -150,7 +169,17 @@ struct AttnLaunch {
   int rows;              // packed token rows in qkv (T)
   unsigned* status;
   int num_sms;
+  // per sequence (first token, length), longest first; sequences [0, n_long)
+  // are longer than the short-sequence kernel's key capacity and own the
+  // first nblocks128_long entries of blocks128
+  const int2* seqs;
+  int nseq;
+  int n_long;
+  int nblocks128_long;
+  int max_short_len;     // longest sequence in [n_long, nseq)
 };
+// key capacity of the short-sequence attention kernel (ec_attn_short.cuh)
+constexpr int kAttnShortCap = 256;
 // tcgen05 kernel (ec_fa.cuh) for head_dim 32 / 64 / 128; the mma.sync kernel
 // (ec_attn.cuh) when EC_LEGACY_ATTN is set
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t st);

@@ -400,7 +400,7 @@ int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
 
 // --------------------------------------------------------------- forward --
 struct WsLayout {
-  size_t ids, pos, cu, blocks, blocks128, h32, tmp, hb, qkv, ctx, ff, out, total;
+  size_t ids, pos, cu, blocks, blocks128, seqs, h32, tmp, hb, qkv, ctx, ff, out, total;
 };
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -416,6 +416,7 @@ static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
   L.cu = o; o += al256((nseq + 1) * 4);
   L.blocks = o; o += al256(nblk * 8);
   L.blocks128 = o; o += al256((T / 128 + nseq + 1) * 16);
+  L.seqs = o; o += al256(nseq * 8);
   L.h32 = o; o += al256(T * m.H * 4);
   L.tmp = o; o += al256(T * m.H * 4);
   L.hb = o; o += al256(T * m.H * 2);
@@ -434,7 +435,7 @@ static int ensure_ws(Device& d, int T, int nseq) {
   const WsLayout L = layout_for(d.model, t2, s2);
   const size_t pin = static_cast<size_t>(t2) * 4 + (static_cast<size_t>(s2) + 1) * 4 +
                      (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
-                     (static_cast<size_t>(t2) / 128 + s2 + 1) * 16 + 512 +
+                     (static_cast<size_t>(t2) / 128 + s2 + 1) * 16 + static_cast<size_t>(s2) * 8 + 768 +
                      static_cast<size_t>(s2) * d.model.H * 4 + 1024;
   if (!d.ws || L.total > d.ws_bytes) {
     if (d.ws) {
@@ -473,8 +474,17 @@ static int ensure_ws(Device& d, int T, int nseq) {
 
 // Run the forward for sequences seqs[s0..s1) (indices into offsets) that are
 // packed in `ids_dev` (already on the device) and write pooled rows to out.
-static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nblk, int nblk128,
+// counts of the uploaded attention tables of one chunk
+struct AttnTables {
+  int nblk = 0, nblk128 = 0;     // 64-row and 128-row query blocks
+  int n_long = 0;                // sequences longer than kAttnShortCap (first in order)
+  int nblk128_long = 0;          // their 128-row blocks (a prefix of blocks128)
+  int max_short = 0;             // longest sequence of the rest
+};
+
+static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const AttnTables& tb,
                           double attn_pairs, float* out, int out_stride) {
+  const int nblk = tb.nblk, nblk128 = tb.nblk128;
   ModelW& m = d.model;
   char* ws = static_cast<char*>(d.ws);
   int* ids = reinterpret_cast<int*>(ws + L.ids);
@@ -530,6 +540,18 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
     prof_end(d, 0, 2.0 * T * N * K, bytes, e0);
     return check_cuda(e, "gemm");
   };
+  // h32 = LayerNorm(A . W^T + bias + h32), hb = bf16(h32) in one kernel
+  // (EC_NO_GEMM_LN keeps the GEMM + separate LayerNorm pair)
+  const bool fuse_ln = gemm_ln_supported(H) && getenv("EC_NO_GEMM_LN") == nullptr;
+  auto gemm_ln = [&](const bf16* A, int K, const bf16* W, const float* bias, const float* lg,
+                     const float* lb) -> int {
+    GemmLnLaunch g{A, K, W, T, H, K, bias, h32, lg, lb, h32, hb, d.status};
+    const double bytes = 2.0 * T * K + 2.0 * H * K + 4.0 * T * H + 6.0 * T * H;
+    const int e0 = prof_begin(d);
+    const cudaError_t e = launch_gemm_ln(g, st, d.num_sms);
+    prof_end(d, 0, 2.0 * T * H * K, bytes, e0);
+    return check_cuda(e, "gemm+layernorm");
+  };
   AttnLaunch at;
   at.qkv = qkv;
   at.ld = nqkv;
@@ -549,6 +571,11 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
   at.rel_max = m.rel_max;
   at.blocks128 = reinterpret_cast<const int4*>(ws + L.blocks128);
   at.nblocks128 = nblk128;
+  at.seqs = reinterpret_cast<const int2*>(ws + L.seqs);
+  at.nseq = nseq;
+  at.n_long = tb.n_long;
+  at.nblocks128_long = tb.nblk128_long;
+  at.max_short_len = tb.max_short;
   at.rows = T;
   at.status = d.status;
   at.num_sms = d.num_sms;
@@ -584,9 +611,11 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
       const BertLayerW& w = m.bl[li];
       EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, w.bqkv, nullptr, qkv, nqkv, kEpiBf16));
       EC_TRY(attention());
-      EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, w.bo, h32, tmp, H, kEpiF32Resid));
-      LnArgs l1{tmp, w.ln1g, w.ln1b, h32, hb, T, H};
-      {
+      if (fuse_ln) {
+        EC_TRY(gemm_ln(ctx, nctx, w.wo, w.bo, w.ln1g, w.ln1b));
+      } else {
+        EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, w.bo, h32, tmp, H, kEpiF32Resid));
+        LnArgs l1{tmp, w.ln1g, w.ln1b, h32, hb, T, H};
         const int e0 = prof_begin(d);
         EC_TRY(rows(launch_ln(l1, st), "layernorm", TH * 10.0, e0));
       }
@@ -603,9 +632,11 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
         EC_TRY(check_cuda(e, "fused mlp"));
       } else {
         EC_TRY(gemm(hb, H, w.wff, F, H, w.bff, nullptr, ff, F, kEpiBf16Gelu));
-        EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
-        LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};
-        {
+        if (fuse_ln) {
+          EC_TRY(gemm_ln(ff, F, w.wout, w.bout, w.ln2g, w.ln2b));
+        } else {
+          EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
+          LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};
           const int e0 = prof_begin(d);
           EC_TRY(rows(launch_ln(l2, st), "layernorm", TH * 10.0, e0));
         }
@@ -690,8 +721,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, int nbl
 
 // Build the per-chunk host tables (cu offsets, attention blocks sorted by
 // descending length) into pinned staging and upload them.
-static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, int* nblk_out,
-                         int* nblk128_out) {
+static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, AttnTables* tb) {
   const int nseq = static_cast<int>(lens.size());
   char* pin = static_cast<char*>(d.pin);
   int* hcu = reinterpret_cast<int*>(pin);
@@ -706,19 +736,31 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
     for (int q0 = 0; q0 < lens[s]; q0 += 64) hblk[nb++] = make_int2(s, q0);
   int4* hblk128 = reinterpret_cast<int4*>(reinterpret_cast<char*>(hblk) + al256(static_cast<size_t>(nb) * 8));
   int nb128 = 0;
-  for (int s : order)
+  for (int s : order) {
     for (int q0 = 0; q0 < lens[s]; q0 += 128) hblk128[nb128++] = make_int4(hcu[s], lens[s], q0, 0);
+    if (lens[s] > kAttnShortCap) {
+      ++tb->n_long;
+      tb->nblk128_long = nb128;
+    } else {
+      tb->max_short = std::max(tb->max_short, lens[s]);
+    }
+  }
+  int2* hseq = reinterpret_cast<int2*>(reinterpret_cast<char*>(hblk128) + al256(static_cast<size_t>(nb128) * 16));
+  for (int k = 0; k < nseq; ++k) hseq[k] = make_int2(hcu[order[k]], lens[order[k]]);
   char* ws = static_cast<char*>(d.ws);
+  EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.seqs, hseq, static_cast<size_t>(nseq) * 8,
+                                    cudaMemcpyHostToDevice, d.stream),
+                    "sequence upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks128, hblk128, static_cast<size_t>(nb128) * 16,
                                     cudaMemcpyHostToDevice, d.stream),
                     "block upload"));
-  *nblk128_out = nb128;
+  tb->nblk128 = nb128;
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.cu, hcu, (nseq + 1) * 4, cudaMemcpyHostToDevice, d.stream),
                     "cu upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks, hblk, static_cast<size_t>(nb) * 8,
                                     cudaMemcpyHostToDevice, d.stream),
                     "block upload"));
-  *nblk_out = nb;
+  tb->nblk = nb;
   return EC_OK;
 }
 
@@ -766,8 +808,8 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     std::vector<int> lens(nseq);
     for (int k = 0; k < nseq; ++k)
       lens[k] = static_cast<int>(offsets[seqs[i + k] + 1] - offsets[seqs[i + k]]);
-    int nblk = 0, nblk128 = 0;
-    EC_TRY(upload_tables(d, L, lens, &nblk, &nblk128));
+    AttnTables tb;
+    EC_TRY(upload_tables(d, L, lens, &tb));
     char* ws = static_cast<char*>(d.ws);
     if (ids_dev) {
       EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, ids_dev + offsets[seqs[i]],
@@ -795,7 +837,7 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     for (int k = 0; k < nseq; ++k)
       pairs += m.family == EC_FAMILY_LLAMA ? 0.5 * lens[k] * (lens[k] + 1.0)
                                            : static_cast<double>(lens[k]) * lens[k];
-    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, nblk, nblk128, pairs, dout, ostride));
+    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
     if (!out_dev) {
       std::vector<float> hout(static_cast<size_t>(nseq) * m.H);
       EC_TRY(check_cuda(cudaMemcpyAsync(hout.data(), dout, hout.size() * 4,

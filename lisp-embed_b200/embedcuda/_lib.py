@@ -66,6 +66,7 @@ _SIGS = {
     "ec_comm_init": (C.c_int, [C.c_int, C.c_int, P]),
     "ecdbg_gemm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P, P, C.c_int, C.c_int]),
     "ecdbg_mlp": (C.c_int, [P, P, P, P, P, P, P, P, P, P, C.c_int, C.c_int, C.c_int]),
+    "ecdbg_gemm_ln": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P]),
     "ecdbg_profile": (C.c_int, [C.c_int]),
     "ecdbg_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                      C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),

@@ -92,10 +92,7 @@ def _attn_ref(qkv, lens, heads, kv_heads, hd, q_off, k_off, v_off, causal):
     return torch.cat(outs)
 
 
-@pytest.mark.parametrize("hd,heads,kv,causal", [(32, 12, 12, 0), (64, 12, 12, 0), (128, 16, 8, 1),
-                                                 (128, 4, 4, 0), (64, 2, 1, 1)])
-def test_attention(ec, hd, heads, kv, causal):
-    lens = [1, 5, 63, 64, 65, 200, 513, 17]
+def _run_attention(ec, lens, hd, heads, kv, causal):
     T = sum(lens)
     ld = (heads + 2 * kv) * hd
     g = torch.Generator(device="cuda").manual_seed(hd + heads)
@@ -114,11 +111,57 @@ def test_attention(ec, hd, heads, kv, causal):
     assert err < 2e-2, err
 
 
+# mixed lengths: sequences above 256 tokens run on the tcgen05 kernel, the
+# others (head dims 32 / 64) on the short-sequence kernel
+@pytest.mark.parametrize("hd,heads,kv,causal", [(32, 12, 12, 0), (64, 12, 12, 0), (128, 16, 8, 1),
+                                                 (128, 4, 4, 0), (64, 2, 1, 1), (32, 4, 2, 1)])
+def test_attention(ec, hd, heads, kv, causal):
+    _run_attention(ec, [1, 5, 63, 64, 65, 200, 513, 17], hd, heads, kv, causal)
+
+
+# only short sequences (1..256 tokens, edges included); head dim 64 with and
+# without the short kernel
+@pytest.mark.parametrize("hd,heads,kv,causal,short64", [(32, 12, 12, 0, 0), (32, 4, 2, 1, 0),
+                                                         (64, 12, 12, 0, 1), (64, 4, 2, 1, 1),
+                                                         (64, 12, 12, 0, 0)])
+def test_attention_short_sequences(ec, monkeypatch, hd, heads, kv, causal, short64):
+    if short64:
+        monkeypatch.setenv("EC_SHORT_ATTN64", "1")
+    rng = np.random.default_rng(hd * 7 + heads)
+    lens = [int(x) for x in rng.integers(1, 257, 40)] + [256, 255, 16, 1]
+    _run_attention(ec, lens, hd, heads, kv, causal)
+
+
 def _ln_ref(x, g, b):
     # bert::layernorm: (x - mean) / (sqrt(var) + 1e-12) * g + b
     m = x.mean(-1, keepdim=True)
     v = ((x - m) ** 2).mean(-1, keepdim=True)
     return (x - m) / (v.sqrt() + 1e-12) * g + b
+
+
+# GEMM + residual + LayerNorm on CTA clusters: H 384 (2 CTAs), 768 (3), 1024 (4);
+# ragged M, K = H and K = 4H, output aliasing the residual as the model runs it
+@pytest.mark.parametrize("M,N,K,alias", [(1, 384, 384, False), (200, 384, 1536, True),
+                                         (4097, 384, 384, True), (999, 768, 768, False),
+                                         (3000, 768, 3072, True), (257, 1024, 1024, True)])
+def test_gemm_layernorm(ec, M, N, K, alias):
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    bias = 0.1 * torch.randn(N, device="cuda", generator=g)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    lg = 1 + 0.1 * torch.randn(N, device="cuda", generator=g)
+    lb = 0.1 * torch.randn(N, device="cuda", generator=g)
+    ref = _ln_ref(A.float() @ W.float().t() + bias + resid, lg, lb)
+    out32 = resid if alias else torch.empty(M, N, device="cuda")
+    outb = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    ec.check(ec.lib().ecdbg_gemm_ln(A.data_ptr(), W.data_ptr(), M, N, K, bias.data_ptr(),
+                                    resid.data_ptr(), lg.data_ptr(), lb.data_ptr(),
+                                    out32.data_ptr(), outb.data_ptr()), "gemm_ln")
+    err = (out32 - ref).abs().max().item()
+    assert err < 1e-2, err
+    assert (outb.float() - ref).abs().max().item() < 5e-2
 
 
 @pytest.mark.parametrize("M,H,F", [(1, 384, 1536), (200, 384, 1536), (4097, 384, 1536),
