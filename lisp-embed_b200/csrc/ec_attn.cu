@@ -207,12 +207,13 @@ cudaError_t launch_attention(const AttnLaunch& l, cudaStream_t st) {
       default: return cudaErrorInvalidValue;
     }
   }
-  // head dims 32 / 64: short sequences on the shared-memory kernel unless
-  // EC_NO_SHORT_ATTN; head dim 64 opts in with EC_SHORT_ATTN64
+  // head dims 32 / 64: sequences up to 256 tokens on the shared-memory
+  // kernel (measured faster than tcgen05 tiles of 128 padded rows for
+  // MiniLM / BERT-base / MPNet batches) unless EC_NO_SHORT_ATTN
   const bool split = l.seqs && getenv("EC_NO_SHORT_ATTN") == nullptr;
   switch (l.head_dim) {
     case 32: return split ? run_split<32>(l, st) : run_fa_mode<32>(l, st);
-    case 64: return split && getenv("EC_SHORT_ATTN64") ? run_split<64>(l, st) : run_fa_mode<64>(l, st);
+    case 64: return split ? run_split<64>(l, st) : run_fa_mode<64>(l, st);
     case 128: return run_fa_mode<128>(l, st);
     default: return cudaErrorInvalidValue;
   }

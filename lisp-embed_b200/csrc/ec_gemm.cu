@@ -1,6 +1,7 @@
 // ec_gemm.cu -- instantiations and host launcher of the tcgen05 GEMM.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "ec_gemm.cuh"
@@ -60,9 +61,9 @@ static bool encode_2d_out(CUtensorMap* map, void* ptr, bool f32, uint64_t rows, 
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int EW = 8>
 static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
-  using Cfg = GemmCfg<BN, EPI>;
+  using Cfg = GemmCfg<BN, EPI, EW>;
   // the shared-memory opt-in is a per-device function attribute
   static std::mutex attr_mu;
   static bool attr_set[64] = {};
@@ -72,7 +73,7 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
     std::lock_guard<std::mutex> lk(attr_mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI>,
+      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI, EW>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(Cfg::SMEM_BYTES));
       if (e != cudaSuccess) return e;
@@ -97,7 +98,7 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * a.n_tiles_n;
   a.status = g.status;
   const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
-  gemm_tn_bf16_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
+  gemm_tn_bf16_kernel<BN, EPI, EW><<<grid, gemm_threads(EW), Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
   return cudaGetLastError();
 }
 

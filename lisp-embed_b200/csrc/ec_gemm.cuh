@@ -54,14 +54,19 @@ constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 320;  // 2 control warps + 8 epilogue warps
 constexpr int kGemmEpiWarps = 8;
+// threads of a GEMM CTA with EW epilogue warps
+constexpr int gemm_threads(int ew) { return (2 + ew) * 32; }
 
-template <int BN, int EPI>
+// EW: epilogue warps (8, 12 or 16; four TMEM lane quadrants x EW / 4 column
+// parts).  More warps hide more of the TMEM-load / store latency of the
+// epilogue; with more than 8 a warp handles one 32-column chunk at a time.
+template <int BN, int EPI, int EW = 8>
 struct GemmCfg {
   static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32;
   // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
   // rows of 64 B (64B swizzle); two per epilogue warp
   static constexpr uint32_t CHUNK_BYTES = OUT_F32 ? 4096 : 2048;
-  static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * 2 * CHUNK_BYTES;
+  static constexpr uint32_t EPI_BYTES = EW * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t B_BYTES = BN * kGemmBK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -138,12 +143,13 @@ __device__ __forceinline__ uint32_t stage_off(int r, int c) {
   return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int EPI, int EW = 8>
+__global__ void __launch_bounds__(gemm_threads(EW), 1)
     gemm_tn_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, EPI>;
+  using Cfg = GemmCfg<BN, EPI, EW>;
+  static_assert(EW == 8 || EW == 12 || EW == 16, "epilogue warps");
   constexpr int STAGES = Cfg::STAGES;
   constexpr bool F32 = Cfg::OUT_F32;
   constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kGemmEpiWarps);
+      mbar_init(&tempty[b], EW);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -263,21 +269,108 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..9: lane quadrant warp % 4, chunk parity (warp - 2) / 4
+    // epilogue warps 2..EW+1: lane quadrant warp % 4, column part (warp - 2) / 4;
+    // part p takes chunks p, p + PARTS, ...
+    constexpr int PARTS = EW / 4;
     const int ew = warp - 2;
     const int quad = warp & 3;
-    const int half = ew >> 2;
+    const int half = ew >> 2;  // the column part
     uint8_t* stage_base = smE + ew * 2 * Cfg::CHUNK_BYTES;
     constexpr int NCH = EPI == kEpiBf16Swiglu ? BN / 64 : BN / 32;  // output chunks per tile
-    static_assert(NCH >= 2, "every epilogue warp needs a chunk per tile");
+    static_assert(NCH >= PARTS, "every epilogue warp needs a chunk per tile");
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+    // bias / GELU / fp32 epilogues: two chunks per step (two TMEM loads, one
+    // wait, 64 independent element chains), accumulator handed back as soon
+    // as the last TMEM read lands
+    constexpr bool kPaired = EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32;
+    for (int tile = blockIdx.x; kPaired && tile < args.num_tiles; tile += gridDim.x) {
+      const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+      const int row0 = mb * kGemmBM + quad * 32;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+      bool fine = true;
+      // eight warps: chunk pairs (c, c + 2); more warps: one chunk per step
+      constexpr bool PAIR = EW == 8;
+      constexpr int STEP = PAIR ? 4 : PARTS;
+#pragma unroll 1
+      for (int c0 = half; c0 < NCH; c0 += STEP) {
+        const bool two = PAIR && c0 + 2 < NCH;
+        if (c0 == half) {
+          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+            fine = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        uint32_t r[PAIR ? 2 : 1][32];
+        tmem_ld_32x32b_x32(t_row + c0 * 32, r[0]);
+        if constexpr (PAIR)
+          if (two) tmem_ld_32x32b_x32(t_row + (c0 + 2) * 32, r[PAIR ? 1 : 0]);
+        tmem_wait_ld();
+        if (c0 + STEP >= NCH) {
+          // every TMEM column of this warp is in registers: release the buffer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+#pragma unroll
+        for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
+          if (h == 1 && !two) break;
+          const int col0 = nb * BN + (c0 + 2 * h) * 32;
+          float4 bq[8];  // this chunk's bias (L1-resident after the first tile)
+          const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) bq[j] = args.bias ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
+          if (lane == 0) tma_store_wait_read<1>();
+          __syncwarp();
+          if constexpr (F32) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) = make_float4(
+                  __uint_as_float(r[h][4 * j]) + bq[j].x, __uint_as_float(r[h][4 * j + 1]) + bq[j].y,
+                  __uint_as_float(r[h][4 * j + 2]) + bq[j].z, __uint_as_float(r[h][4 * j + 3]) + bq[j].w);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float2 x[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float4 b = bq[2 * j + (e >> 1)];
+                x[e] = __fadd2_rn(make_float2(__uint_as_float(r[h][8 * j + 2 * e]),
+                                              __uint_as_float(r[h][8 * j + 2 * e + 1])),
+                                  (e & 1) ? make_float2(b.z, b.w) : make_float2(b.x, b.y));
+                if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_as2(x[e]);
+              }
+              *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
+                  make_uint4(pack_bf16(x[0].x, x[0].y), pack_bf16(x[1].x, x[1].y),
+                             pack_bf16(x[2].x, x[2].y), pack_bf16(x[3].x, x[3].y));
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, st, col0, row0);
+            tma_store_commit();
+          }
+          sbuf ^= 1;
+        }
+      }
+      if (!fine) {
+        report(args.status, kDevTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    for (int tile = blockIdx.x; !kPaired && tile < args.num_tiles; tile += gridDim.x) {
       const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
       const int row0 = mb * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1
-      for (int c = half; c < NCH; c += 2) {
+      for (int c = half; c < NCH; c += PARTS) {
         const int col0 = (EPI == kEpiBf16Swiglu ? nb * (BN / 2) : nb * BN) + c * 32;
         // residual rows row0 + 4k + lane/8, columns col0 + (lane%8)*4 .. +3:
         // coalesced 128-byte rows, issued before the TMEM wait
@@ -378,7 +471,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_store_commit();
         }
         sbuf ^= 1;
-        if (c + 2 >= NCH) {
+        if (c + PARTS >= NCH) {
           // last chunk of this warp in the tile: hand the accumulator back
           tc_fence_before();
           __syncwarp();

@@ -48,14 +48,18 @@ struct GemmLnCfg {
   static constexpr uint32_t BUF_BYTES = 4096;
   static constexpr uint32_t WARP_BYTES = 2 * BUF_BYTES + 2048;
   static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * WARP_BYTES;
-  // exchange slots: [2 values][2 tile parities][C ranks][2 halves][128 rows]
-  static constexpr uint32_t XS_FLOATS = 2 * 2 * C * 2 * 128;
-  static constexpr uint32_t XS_BYTES = XS_FLOATS * 4;
+  // exchange slots: float2 (sum, M2) [2 tile parities][C ranks][2 halves][128 rows]
+  static constexpr uint32_t XS_BYTES = 2 * C * 2 * 128 * 8;
+  static constexpr uint32_t XS_TX = C * kGemmEpiWarps * 32 * 8;  // bytes landing per tile
+  // bias, LayerNorm gain and shift of this CTA's column slice
+  static constexpr uint32_t VEC_BYTES = 3 * BN * 4;
   static constexpr int MAX_STAGES =
-      (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES + XS_BYTES)) / static_cast<int>(STAGE_BYTES);
+      (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES + XS_BYTES + VEC_BYTES)) /
+      static_cast<int>(STAGE_BYTES);
   static constexpr int STAGES = MAX_STAGES > 6 ? 6 : MAX_STAGES;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
-  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + XS_BYTES + 512;
+  static constexpr size_t SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES + EPI_BYTES + XS_BYTES + VEC_BYTES + 512;
   static_assert(STAGES >= 2, "shared memory budget");
   static_assert(NCH % 2 == 0, "both epilogue halves take whole chunks");
 };
@@ -79,12 +83,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * Cfg::A_BYTES;
   uint8_t* smE = smB + STAGES * Cfg::B_BYTES;  // epilogue buffers, WARP_BYTES per warp
-  float* xs = reinterpret_cast<float*>(smE + Cfg::EPI_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xs) + Cfg::XS_BYTES);
+  float2* xs = reinterpret_cast<float2*>(smE + Cfg::EPI_BYTES);
+  float* sVec = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + Cfg::XS_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sVec) + Cfg::VEC_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* xbar = tempty + 2;  // [2 tile parities], 8 * C warp arrivals
+  uint64_t* xbar = tempty + 2;  // [2 tile parities]: local expect_tx + C * 256 remote stores
   uint64_t* rbar = xbar + 2;    // [8 epilogue warps][2 buffers] residual loads
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kGemmEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kGemmEpiWarps);
     }
-    for (int i = 0; i < 2; ++i) mbar_init(&xbar[i], kGemmEpiWarps * C);
+    for (int i = 0; i < 2; ++i) mbar_init(&xbar[i], 1);
     for (int i = 0; i < 2 * kGemmEpiWarps; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -119,6 +124,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
+  }
+  if (warp >= 2) {
+    // bias (0 when absent), gain and shift of columns [rank * BN, +BN)
+    const int rk = static_cast<int>(cluster_rank());
+    for (int i = threadIdx.x - 64; i < BN; i += kGemmThreads - 64) {
+      sVec[i] = args.bias ? args.bias[rk * BN + i] : 0.f;
+      sVec[BN + i] = args.ln_g[rk * BN + i];
+      sVec[2 * BN + i] = args.ln_b[rk * BN + i];
+    }
   }
   tc_fence_before();
   cluster_sync_all();  // every CTA's barriers exist before any remote arrival
@@ -205,10 +219,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* rb = rbar + ew * 2;
     uint32_t rbits = 0;  // phase parity of rb[0], rb[1]
     const float inv_n = 1.0f / static_cast<float>(args.N);
-    const uint32_t xs_local = smem_u32(xs);
-    // slot [v][par][r][hf][row] (byte offset)
-    auto slot = [&](int v, int par, int r, int hf) -> uint32_t {
-      return static_cast<uint32_t>((((v * 2 + par) * C + r) * 2 + hf) * 128 + row) * 4u;
+    // xs[par][r][hf][row]
+    auto slot = [&](int par, int r, int hf) -> int { return ((par * C + r) * 2 + hf) * 128 + row; };
+    auto load_res = [&](int b, int c, int row0) {
+      mbar_arrive_expect_tx(&rb[b], Cfg::BUF_BYTES);
+      tma_load_2d(bufs + b * Cfg::BUF_BYTES, &tmR, &rb[b], rank * BN + c * 32, row0);
     };
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -223,11 +238,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // tile's bulk stores have finished reading them
       if (lane == 0) {
         tma_store_wait_read<0>();
-#pragma unroll
-        for (int b = 0; b < 2 && b < NLOC; ++b) {
-          mbar_arrive_expect_tx(&rb[b], Cfg::BUF_BYTES);
-          tma_load_2d(bufs + b * Cfg::BUF_BYTES, &tmR, &rb[b], rank * BN + (half + 2 * b) * 32, row0);
-        }
+        load_res(0, half, row0);
+        if (NLOC > 1) load_res(1, half + 2, row0);
+        // this tile's exchange: C * 256 partners' 8-byte stores land here
+        if (ew == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::XS_TX);
       }
       __syncwarp();
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
@@ -235,27 +249,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      // ---- pass A: x = acc + bias + resid, back into TMEM; partial sum
+      // ---- pass A: x = acc + bias + resid, back into TMEM; partial sum;
+      // chunk ci's residual is in buffer ci & 1
       float s_loc = 0.f;
 #pragma unroll 1
       for (int ci = 0; ci < NLOC; ++ci) {
         const int b = ci & 1;
-        const int c = half + 2 * ci;
-        const int col0 = rank * BN + c * 32;
-        uint8_t* buf = bufs + b * Cfg::BUF_BYTES;
+        const int cl = (half + 2 * ci) * 32;  // column within the slice
+        const uint8_t* buf = bufs + b * Cfg::BUF_BYTES;
         uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, v);
+        tmem_ld_32x32b_x32(t_row + cl, v);
         if (!mbar_wait(&rb[b], (rbits >> b) & 1u, abort_flag)) {
           ok = false;
           break;
         }
         rbits ^= 1u << b;
         tmem_wait_ld();
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 q = *reinterpret_cast<const float4*>(buf + stage_off<true>(lane, j));
-          const float4 bb = args.bias ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 bb = *reinterpret_cast<const float4*>(sVec + cl + 4 * j);
           const float x0 = (__uint_as_float(v[4 * j]) + bb.x) + q.x;
           const float x1 = (__uint_as_float(v[4 * j + 1]) + bb.y) + q.y;
           const float x2 = (__uint_as_float(v[4 * j + 2]) + bb.z) + q.z;
@@ -266,12 +279,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           v[4 * j + 2] = __float_as_uint(x2);
           v[4 * j + 3] = __float_as_uint(x3);
         }
-        tmem_st_32x32b_x32(t_row + c * 32, v);
+        tmem_st_32x32b_x32(t_row + cl, v);
         __syncwarp();  // every lane has read the buffer
-        if (lane == 0 && ci + 2 < NLOC) {
-          mbar_arrive_expect_tx(&rb[b], Cfg::BUF_BYTES);
-          tma_load_2d(buf, &tmR, &rb[b], rank * BN + (c + 4) * 32, row0);
-        }
+        if (lane == 0 && ci + 2 < NLOC) load_res(b, half + 2 * (ci + 2), row0);
       }
       if (!ok) break;
       tmem_wait_st();
@@ -289,18 +299,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           m2_loc += d0 * d0 + d1 * d1;
         }
       }
-      // ---- one exchange of (sum, M2) with every CTA of the cluster
-#pragma unroll
-      for (int r = 0; r < C; ++r) {
-        st_cluster_f32(cluster_map(xs_local + slot(0, par, rank, half), r), s_loc);
-        st_cluster_f32(cluster_map(xs_local + slot(1, par, rank, half), r), m2_loc);
-      }
-      fence_acq_rel_cluster();
-      __syncwarp();
-      if (lane == 0) {
+      // ---- one exchange of (sum, M2): an 8-byte asynchronous store into
+      // every CTA of the cluster, counted by that CTA's transaction barrier
+      {
+        const uint32_t dst = smem_u32(xs + slot(par, rank, half));
         const uint32_t bar = smem_u32(&xbar[par]);
 #pragma unroll
-        for (int r = 0; r < C; ++r) mbar_arrive_remote(cluster_map(bar, r));
+        for (int r = 0; r < C; ++r)
+          st_async_cluster_v2(cluster_map(dst, r), s_loc, m2_loc, cluster_map(bar, r));
       }
       if (!mbar_wait_cluster(&xbar[par], static_cast<uint32_t>((tcount >> 1) & 1), abort_flag)) {
         ok = false;
@@ -309,43 +315,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // merge in a fixed order, identical on every CTA of the cluster
       float sum = 0.f;
 #pragma unroll
-      for (int r = 0; r < C; ++r)
-        sum += xs[slot(0, par, r, 0) >> 2] + xs[slot(0, par, r, 1) >> 2];
+      for (int r = 0; r < C; ++r) sum += xs[slot(par, r, 0)].x + xs[slot(par, r, 1)].x;
       const float mean = sum * inv_n;
       float m2 = 0.f;
 #pragma unroll
       for (int r = 0; r < C; ++r)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const float dm = xs[slot(0, par, r, hf) >> 2] / kLocCols - mean;
-          m2 += xs[slot(1, par, r, hf) >> 2] + kLocCols * dm * dm;
+          const float2 p = xs[slot(par, r, hf)];
+          const float dm = p.x / kLocCols - mean;
+          m2 += p.y + kLocCols * dm * dm;
         }
       const float stdv = sqrtf(m2 * inv_n) + 1e-12f;
       const float inv = 1.0f / stdv;
       // ---- pass C: normalise, stage, bulk-store fp32 and bf16 rows
 #pragma unroll 1
       for (int ci = 0; ci < NLOC; ++ci) {
-        const int b = ci & 1;
-        const int c = half + 2 * ci;
-        const int col0 = rank * BN + c * 32;
-        uint8_t* st32 = bufs + b * Cfg::BUF_BYTES;
+        const int cl = (half + 2 * ci) * 32;  // column within the slice
         uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, v);
-        // the bf16 chunk and fp32 buffer b are free once earlier stores read them
+        tmem_ld_32x32b_x32(t_row + cl, v);
+        uint8_t* st32 = bufs + (ci & 1) * Cfg::BUF_BYTES;
+        // fp32 buffer and the bf16 chunk are free once earlier stores read them
         if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
         tmem_wait_ld();
-        const float4* g4 = reinterpret_cast<const float4*>(args.ln_g + col0);
-        const float4* bb4 = reinterpret_cast<const float4*>(args.ln_b + col0);
+        if (ci + 1 == NLOC) {
+          // last TMEM read of the tile: the accumulator goes back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float4 ga = __ldg(g4 + 2 * j), gb = __ldg(g4 + 2 * j + 1);
-          const float4 ba = __ldg(bb4 + 2 * j), bbv = __ldg(bb4 + 2 * j + 1);
-          const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-          const float bv[8] = {ba.x, ba.y, ba.z, ba.w, bbv.x, bbv.y, bbv.z, bbv.w};
           float y[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) y[e] = ((__uint_as_float(v[8 * j + e]) - mean) * inv) * gg[e] + bv[e];
+          for (int e = 0; e < 8; ++e)
+            y[e] = ((__uint_as_float(v[8 * j + e]) - mean) * inv) * sVec[BN + cl + 8 * j + e] +
+                   sVec[2 * BN + cl + 8 * j + e];
           *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j)) = make_float4(y[0], y[1], y[2], y[3]);
           *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j + 1)) =
               make_float4(y[4], y[5], y[6], y[7]);
@@ -356,15 +362,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmO32, st32, col0, row0);
-          tma_store_2d(&tmOb, stb, col0, row0);
+          tma_store_2d(&tmO32, st32, rank * BN + cl, row0);
+          tma_store_2d(&tmOb, stb, rank * BN + cl, row0);
           tma_store_commit();
         }
       }
-      // the accumulator buffer goes back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }

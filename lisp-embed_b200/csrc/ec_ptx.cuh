@@ -115,6 +115,16 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t ra
 __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// asynchronous 8-byte store into another CTA's shared memory that signals
+// that CTA's mbarrier (complete_tx of 8 bytes) when the data has landed
+__device__ __forceinline__ void st_async_cluster_v2(uint32_t cluster_addr, float a, float b,
+                                                    uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          cluster_addr),
+      "f"(a), "f"(b), "r"(cluster_bar)
+      : "memory");
+}
 __device__ __forceinline__ void fence_acq_rel_cluster() {
   asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }

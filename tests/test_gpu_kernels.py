@@ -119,14 +119,14 @@ def test_attention(ec, hd, heads, kv, causal):
     _run_attention(ec, [1, 5, 63, 64, 65, 200, 513, 17], hd, heads, kv, causal)
 
 
-# only short sequences (1..256 tokens, edges included); head dim 64 with and
-# without the short kernel
-@pytest.mark.parametrize("hd,heads,kv,causal,short64", [(32, 12, 12, 0, 0), (32, 4, 2, 1, 0),
-                                                         (64, 12, 12, 0, 1), (64, 4, 2, 1, 1),
-                                                         (64, 12, 12, 0, 0)])
-def test_attention_short_sequences(ec, monkeypatch, hd, heads, kv, causal, short64):
-    if short64:
-        monkeypatch.setenv("EC_SHORT_ATTN64", "1")
+# only short sequences (1..256 tokens, edges included), on the short kernel
+# and (EC_NO_SHORT_ATTN) on the tcgen05 kernel
+@pytest.mark.parametrize("hd,heads,kv,causal,tc", [(32, 12, 12, 0, 0), (32, 4, 2, 1, 0),
+                                                    (64, 12, 12, 0, 0), (64, 4, 2, 1, 0),
+                                                    (64, 12, 12, 0, 1), (32, 12, 12, 0, 1)])
+def test_attention_short_sequences(ec, monkeypatch, hd, heads, kv, causal, tc):
+    if tc:
+        monkeypatch.setenv("EC_NO_SHORT_ATTN", "1")
     rng = np.random.default_rng(hd * 7 + heads)
     lens = [int(x) for x in rng.integers(1, 257, 40)] + [256, 255, 16, 1]
     _run_attention(ec, lens, hd, heads, kv, causal)
