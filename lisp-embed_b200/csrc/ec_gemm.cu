@@ -61,28 +61,47 @@ static bool encode_2d_out(CUtensorMap* map, void* ptr, bool f32, uint64_t rows, 
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI, int EW = 8>
+template <int BN, int EPI, int CG = 1>
 static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
-  using Cfg = GemmCfg<BN, EPI, EW>;
-  // the shared-memory opt-in is a per-device function attribute
+  using Cfg = GemmCfg<BN, EPI, CG>;
+  // the shared-memory opt-in is a per-device function attribute; pairs also
+  // need the number of clusters that fit at once
   static std::mutex attr_mu;
-  static bool attr_set[64] = {};
+  static int max_clusters[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   {
     std::lock_guard<std::mutex> lk(attr_mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI, EW>,
+    if (!max_clusters[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI, CG>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(Cfg::SMEM_BYTES));
       if (e != cudaSuccess) return e;
-      attr_set[dev] = true;
+      int n = num_sms;
+      if constexpr (CG == 2) {
+        cfg.gridDim = dim3((num_sms / 2) * 2, 1, 1);
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_tn_bf16_kernel<BN, EPI, CG>, &cfg);
+        if (e != cudaSuccess) return e;
+        if (n <= 0) return cudaErrorInvalidConfiguration;
+      }
+      max_clusters[dev] = n;
     }
   }
   CUtensorMap ta, tb, tc;
   if (!encode_2d_bf16(&ta, g.A, g.M, g.K, g.lda, kGemmBM)) return cudaErrorInvalidValue;
-  if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.ldw, BN)) return cudaErrorInvalidValue;
+  if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.ldw, BN / CG)) return cudaErrorInvalidValue;
   const uint64_t out_cols = EPI == kEpiBf16Swiglu ? g.N / 2 : g.N;
   if (!encode_2d_out(&tc, g.out, Cfg::OUT_F32, g.M, out_cols, g.ldo)) return cudaErrorInvalidValue;
   GemmArgs a;
@@ -95,11 +114,22 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.out = g.out;
   a.ldo = g.ldo;
   a.n_tiles_n = g.N / BN;
-  a.num_tiles = ((g.M + kGemmBM - 1) / kGemmBM) * a.n_tiles_n;
+  a.num_tiles = ((g.M + kGemmBM * CG - 1) / (kGemmBM * CG)) * a.n_tiles_n;
   a.status = g.status;
-  const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
-  gemm_tn_bf16_kernel<BN, EPI, EW><<<grid, gemm_threads(EW), Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
-  return cudaGetLastError();
+  a.qk = QkRopeEpi{};
+  if constexpr (EPI == kEpiBf16QkRope) {
+    if (!g.qk) return cudaErrorInvalidValue;
+    a.qk = *g.qk;
+  }
+  if constexpr (CG == 1) {
+    const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
+    gemm_tn_bf16_kernel<BN, EPI, CG><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
+    return cudaGetLastError();
+  } else {
+    const int clusters = a.num_tiles < max_clusters[dev] ? a.num_tiles : max_clusters[dev];
+    cfg.gridDim = dim3(clusters * 2, 1, 1);
+    return cudaLaunchKernelEx(&cfg, gemm_tn_bf16_kernel<BN, EPI, CG>, ta, tb, tc, a);
+  }
 }
 
 template <int BN>
@@ -109,6 +139,9 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
     case kEpiBf16Gelu: return run<BN, kEpiBf16Gelu>(g, st, num_sms);
     case kEpiF32Resid: return run<BN, kEpiF32Resid>(g, st, num_sms);
     case kEpiF32: return run<BN, kEpiF32>(g, st, num_sms);
+    case kEpiBf16QkRope:
+      if constexpr (BN == 256) return run<BN, kEpiBf16QkRope>(g, st, num_sms);
+      return cudaErrorInvalidValue;
     case kEpiBf16Swiglu:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
       return cudaErrorInvalidValue;
@@ -118,6 +151,7 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
 
 int gemm_pick_bn(int M, int N, int epi, int num_sms) {
   if (epi == kEpiBf16Swiglu) return N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
+  if (epi == kEpiBf16QkRope) return N % 256 == 0 ? 256 : 0;
   const int mt = (M + kGemmBM - 1) / kGemmBM;
   int best = 0;
   double best_cost = 1e300;
@@ -140,6 +174,23 @@ int gemm_pick_bn(int M, int N, int epi, int num_sms) {
 
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   if (g.K % kGemmBK || g.M <= 0) return cudaErrorInvalidValue;
+  // CTA pairs (256 x 256 tiles, each CTA loads half of the W tile) where the
+  // mainloop dominates: K >= 768 and epilogues lighter than GELU (measured:
+  // 8-12% faster there, neutral or slower at K = 384 or with GELU).
+  // EC_GEMM_PAIR forces pairs for every eligible shape, EC_NO_GEMM_PAIR none.
+  const bool force_pair = getenv("EC_GEMM_PAIR") != nullptr;
+  if (!g.bn && g.N % 256 == 0 && getenv("EC_NO_GEMM_PAIR") == nullptr &&
+      (force_pair || (g.K >= 768 && g.epi != kEpiBf16Gelu))) {
+    switch (g.epi) {
+      case kEpiBf16: return run<256, kEpiBf16, 2>(g, st, num_sms);
+      case kEpiBf16Gelu: return run<256, kEpiBf16Gelu, 2>(g, st, num_sms);
+      case kEpiF32Resid: return run<256, kEpiF32Resid, 2>(g, st, num_sms);
+      case kEpiF32: return run<256, kEpiF32, 2>(g, st, num_sms);
+      case kEpiBf16Swiglu: return run<256, kEpiBf16Swiglu, 2>(g, st, num_sms);
+      case kEpiBf16QkRope: return run<256, kEpiBf16QkRope, 2>(g, st, num_sms);
+      default: break;
+    }
+  }
   const int bn = g.bn ? g.bn : gemm_pick_bn(g.M, g.N, g.epi, num_sms);
   if (!bn || g.N % bn) return cudaErrorInvalidValue;
   switch (bn) {

@@ -36,6 +36,19 @@ enum GemmEpi : int {
   kEpiF32Resid = 2,    // out f32  = (acc + bias) + resid       (bert.lisp:250-256)
   kEpiBf16Swiglu = 3,  // out bf16 = silu(gate) * up, N/2 wide  (llama.lisp:284-290)
   kEpiF32 = 4,         // out f32  = acc + bias
+  kEpiBf16QkRope = 5,  // out bf16 = acc, with per-head RMSNorm + RoPE on the
+                       // q/k heads (llama.lisp:244-253, 137-151), head dim 128
+};
+
+// per-head q/k RMSNorm + rotate-half RoPE applied in the QKV epilogue
+struct QkRopeEpi {
+  const float* q_norm;  // [128] or nullptr (no q/k norm)
+  const float* k_norm;
+  int q_heads, k_heads; // heads [0, q_heads) use q_norm, the next k_heads k_norm
+  double eps;
+  const int* pos;       // [M] position of each row
+  const float* cos_t;   // [max_pos, 64]
+  const float* sin_t;
 };
 
 struct GemmArgs {
@@ -48,6 +61,7 @@ struct GemmArgs {
   int n_tiles_n;       // N / BN
   int num_tiles;       // ceil(M / 128) * n_tiles_n
   unsigned* status;    // device status word
+  QkRopeEpi qk;        // kEpiBf16QkRope only
 };
 
 constexpr int kGemmBM = 128;
@@ -57,18 +71,18 @@ constexpr int kGemmEpiWarps = 8;
 // threads of a GEMM CTA with EW epilogue warps
 constexpr int gemm_threads(int ew) { return (2 + ew) * 32; }
 
-// EW: epilogue warps (8, 12 or 16; four TMEM lane quadrants x EW / 4 column
-// parts).  More warps hide more of the TMEM-load / store latency of the
-// epilogue; with more than 8 a warp handles one 32-column chunk at a time.
-template <int BN, int EPI, int EW = 8>
+// CG: CTAs per MMA (1, or 2 = a cluster pair issuing cta_group::2 MMAs of
+// M = 256: each CTA loads only half of the W tile, so the operand traffic per
+// output drops by a third -- the mainloop is bound by L2 -> SM bandwidth).
+template <int BN, int EPI, int CG = 1>
 struct GemmCfg {
   static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32;
   // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
   // rows of 64 B (64B swizzle); two per epilogue warp
   static constexpr uint32_t CHUNK_BYTES = OUT_F32 ? 4096 : 2048;
-  static constexpr uint32_t EPI_BYTES = EW * 2 * CHUNK_BYTES;
+  static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
-  static constexpr uint32_t B_BYTES = BN * kGemmBK * 2;
+  static constexpr uint32_t B_BYTES = (BN / CG) * kGemmBK * 2;  // this CTA's rows of W
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int MAX_STAGES = (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES)) /
                                     static_cast<int>(STAGE_BYTES);
@@ -143,16 +157,18 @@ __device__ __forceinline__ uint32_t stage_off(int r, int c) {
   return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-template <int BN, int EPI, int EW = 8>
-__global__ void __launch_bounds__(gemm_threads(EW), 1)
+template <int BN, int EPI, int CG = 1>
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, EPI, EW>;
-  static_assert(EW == 8 || EW == 12 || EW == 16, "epilogue warps");
+  using Cfg = GemmCfg<BN, EPI, CG>;
+  constexpr int EW = kGemmEpiWarps;
+  static_assert(CG == 1 || CG == 2, "CTA group");
   constexpr int STAGES = Cfg::STAGES;
   constexpr bool F32 = Cfg::OUT_F32;
-  constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
+  constexpr uint32_t IDESC = make_idesc(1, kGemmBM * CG, BN);
+  constexpr int TM = kGemmBM * CG;  // rows per tile
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(EPI != kEpiBf16Swiglu || BN % 64 == 0, "swiglu BN");
 
@@ -171,6 +187,11 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // pair: CTA `rank` owns rows rank * 128.. of each 256-row tile; the even
+  // CTA issues the MMAs; both walk the same tiles
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+  const int tile0 = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int tstep = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -179,7 +200,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], EW);
+      mbar_init(&tempty[b], EW * CG);  // the even CTA's counts both epilogues
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -190,14 +211,25 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // the partner's barriers exist
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int k_blocks = args.K / kGemmBK;
+  // hand accumulator buffer b back to the MMA issuer (the even CTA's barrier)
+  auto release_acc = [&](int b) {
+    if constexpr (CG == 2) mbar_arrive_remote(cluster_map(smem_u32(&tempty[b]), 0));
+    else mbar_arrive(&tempty[b]);
+  };
 
   if (warp == 0) {
     if (elect_one()) {
@@ -205,7 +237,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < args.num_tiles; tile += tstep) {
         const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
@@ -214,11 +246,21 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(smA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * kGemmBK,
-                      mb * kGemmBM);
-          tma_load_2d_hint(smB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * kGemmBK,
-                           nb * BN, pol_w);
+          if constexpr (CG == 2) {
+            // both CTAs' bytes land on the even CTA's barrier, which expects them
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            const uint32_t fb = cluster_map(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(smA + stage * Cfg::A_BYTES, &tmA, fb, kb * kGemmBK,
+                             mb * TM + static_cast<int>(rank) * kGemmBM);
+            tma_load_2d_pair(smB + stage * Cfg::B_BYTES, &tmB, fb, kb * kGemmBK,
+                             nb * BN + static_cast<int>(rank) * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+            tma_load_2d(smA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * kGemmBK,
+                        mb * kGemmBM);
+            tma_load_2d_hint(smB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * kGemmBK,
+                             nb * BN, pol_w);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -227,13 +269,13 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       }
     }
   } else if (warp == 1) {
-    if (elect_one()) {
+    if (rank == 0 && elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < args.num_tiles; tile += tstep) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
           report(args.status, kDevTimeoutMma);
           *abort_flag = 1;
@@ -253,17 +295,23 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           const uint32_t b_addr = smem_u32(smB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_f16(d_tmem, desc_sw128_kmajor(a_addr + k * 32),
-                     desc_sw128_kmajor(b_addr + k * 32), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              umma_f16_pair(d_tmem, desc_sw128_kmajor(a_addr + k * 32),
+                            desc_sw128_kmajor(b_addr + k * 32), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, desc_sw128_kmajor(a_addr + k * 32),
+                       desc_sw128_kmajor(b_addr + k * 32), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (CG == 2) umma_commit_pair(&empty[stage], 0x3);
+          else umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (CG == 2) umma_commit_pair(&tfull[acc], 0x3);
+        else umma_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -284,13 +332,113 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     // bias / GELU / fp32 epilogues: two chunks per step (two TMEM loads, one
     // wait, 64 independent element chains), accumulator handed back as soon
     // as the last TMEM read lands
-    constexpr bool kPaired = EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32;
-    for (int tile = blockIdx.x; kPaired && tile < args.num_tiles; tile += gridDim.x) {
+    constexpr bool kPaired =
+        EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiBf16QkRope;
+    for (int tile = tile0; kPaired && tile < args.num_tiles; tile += tstep) {
       const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
-      const int row0 = mb * kGemmBM + quad * 32;
+      const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
       bool fine = true;
+      if constexpr (EPI == kEpiBf16QkRope) {
+        static_assert(BN == 256 && EW == 8, "two 128-wide heads per tile, one per warp half");
+        if (nb * 2 < args.qk.q_heads + args.qk.k_heads) {
+          // this warp half owns head gh = 2 nb + half (chunks 4 half .. 4 half + 3);
+          // pass 1: the head's sum of squares (in double, as llama::rmsnorm),
+          // pass 2: scale by the norm weight, rotate pairs (i, i + 64), store
+          const int gh = nb * 2 + half;
+          const float* wn = gh < args.qk.q_heads ? args.qk.q_norm : args.qk.k_norm;
+          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+            report(args.status, kDevTimeoutEpilogue);
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t t_head = t_row + half * 128;
+          float inv = 1.f;
+          if (wn) {
+            double ss = 0.0;
+#pragma unroll 1
+            for (int c = 0; c < 4; c += 2) {
+              uint32_t r[2][32];
+              tmem_ld_32x32b_x32(t_head + c * 32, r[0]);
+              tmem_ld_32x32b_x32(t_head + (c + 1) * 32, r[1]);
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const float x = __uint_as_float(r[h][j]);
+                  ss += static_cast<double>(x * x);
+                }
+            }
+            inv = static_cast<float>(1.0 / sqrt(ss / 128.0 + args.qk.eps));
+          }
+          const int grow = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32 + lane;
+          const int p = grow < args.M ? args.qk.pos[grow] : 0;
+          const float* cs = args.qk.cos_t + static_cast<size_t>(p) * 64;
+          const float* sn = args.qk.sin_t + static_cast<size_t>(p) * 64;
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            // chunk c (columns 32c.. of the head) and its rotation partner c + 2
+            uint32_t r[2][32];
+            tmem_ld_32x32b_x32(t_head + c * 32, r[0]);
+            tmem_ld_32x32b_x32(t_head + (c + 2) * 32, r[1]);
+            tmem_wait_ld();
+            if (c == 1) {
+              // the head is in registers: hand the accumulator back
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) release_acc(acc);
+            }
+            float lo[32], hi[32];
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 c4 = *reinterpret_cast<const float4*>(cs + c * 32 + j);
+              const float4 s4 = *reinterpret_cast<const float4*>(sn + c * 32 + j);
+              float4 wl = make_float4(1.f, 1.f, 1.f, 1.f), wh = wl;
+              if (wn) {
+                wl = __ldg(reinterpret_cast<const float4*>(wn + c * 32 + j));
+                wh = __ldg(reinterpret_cast<const float4*>(wn + 64 + c * 32 + j));
+              }
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ssn[4] = {s4.x, s4.y, s4.z, s4.w};
+              const float gl[4] = {wl.x, wl.y, wl.z, wl.w}, gh4[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float x = __uint_as_float(r[0][j + e]), y = __uint_as_float(r[1][j + e]);
+                if (wn) {
+                  x = (x * inv) * gl[e];
+                  y = (y * inv) * gh4[e];
+                }
+                lo[j + e] = x * cc[e] - y * ssn[e];
+                hi[j + e] = x * ssn[e] + y * cc[e];
+              }
+            }
+            auto emit = [&](const float (&v)[32], int col0) {
+              uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
+              if (lane == 0) tma_store_wait_read<1>();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
+                    make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                               pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, st, col0, row0);
+                tma_store_commit();
+              }
+              sbuf ^= 1;
+            };
+            emit(lo, nb * BN + half * 128 + c * 32);
+            emit(hi, nb * BN + half * 128 + (c + 2) * 32);
+          }
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+          continue;
+        }
+      }
       // eight warps: chunk pairs (c, c + 2); more warps: one chunk per step
       constexpr bool PAIR = EW == 8;
       constexpr int STEP = PAIR ? 4 : PARTS;
@@ -313,7 +461,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           // every TMEM column of this warp is in registers: release the buffer
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (lane == 0) release_acc(acc);
         }
 #pragma unroll
         for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
@@ -366,9 +514,9 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    for (int tile = blockIdx.x; !kPaired && tile < args.num_tiles; tile += gridDim.x) {
+    for (int tile = tile0; !kPaired && tile < args.num_tiles; tile += tstep) {
       const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
-      const int row0 = mb * kGemmBM + quad * 32;  // first row of this warp's 32
+      const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1
       for (int c = half; c < NCH; c += PARTS) {
         const int col0 = (EPI == kEpiBf16Swiglu ? nb * (BN / 2) : nb * BN) + c * 32;
@@ -475,7 +623,7 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
           // last chunk of this warp in the tile: hand the accumulator back
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (lane == 0) release_acc(acc);
         }
       }
       acc ^= 1;
@@ -493,9 +641,11 @@ __global__ void __launch_bounds__(gemm_threads(EW), 1)
     while (globaltimer_ns() - t0 < 2000000ull) {
     }
   }
+  if constexpr (CG == 2) cluster_sync_all();  // neither CTA leaves while the pair MMAs run
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

@@ -90,6 +90,7 @@ cudaError_t launch_convert(int kind, const void* src, void* dst, size_t n, cudaS
 // C[M, N] = A[M, K] . W[N, K]^T with epilogue `epi` (GemmEpi in ec_gemm.cuh:
 // 0 bf16, 1 bf16+gelu, 2 f32+resid, 3 bf16 swiglu, 4 f32).  A and W bf16,
 // K-major; K % 64 == 0; N % bn == 0.  `bn` 0 = pick automatically.
+struct QkRopeEpi;  // ec_gemm.cuh
 struct GemmLaunch {
   const __nv_bfloat16* A;
   int lda;              // elements
@@ -104,6 +105,7 @@ struct GemmLaunch {
   int epi;
   int bn;
   unsigned* status;
+  const QkRopeEpi* qk = nullptr;  // kEpiBf16QkRope (5)
 };
 int gemm_pick_bn(int M, int N, int epi, int num_sms);
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms);

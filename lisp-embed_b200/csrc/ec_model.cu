@@ -514,8 +514,10 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   }
 
   auto gemm = [&](const bf16* A, int lda, const bf16* W, int N, int K, const float* bias,
-                  const float* resid, void* o, int ldo, int epi) -> int {
+                  const float* resid, void* o, int ldo, int epi,
+                  const QkRopeEpi* qk = nullptr) -> int {
     GemmLaunch g;
+    g.qk = qk;
     g.A = A;
     g.lda = lda;
     g.W = W;
@@ -665,12 +667,31 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     EC_TRY(rows(launch_gather_rows(m.word, m.word_dt, ids, h32, T, H, st), "gather",
                 TH * (m.word_dt == kDtBf16 ? 6.0 : 8.0), e0));
   }
+  // q/k norm + RoPE fused into the QKV GEMM (head dim 128, heads in 256-wide
+  // tiles); EC_NO_FUSED_ROPE keeps the separate row kernel
+  const bool fuse_rope = m.hd == 128 && nqkv % 256 == 0 && (m.heads + m.kv_heads) % 2 == 0 &&
+                         m.heads % 2 == 0 && getenv("EC_NO_FUSED_ROPE") == nullptr;
   for (int li = 0; li < m.layers; ++li) {
     const LlamaLayerW& w = m.ll[li];
     RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};
     {
       const int e0 = prof_begin(d);
       EC_TRY(rows(launch_rmsnorm(r1, st), "rmsnorm", TH * 6.0, e0));
+    }
+    if (fuse_rope) {
+      // QKV projection with the per-head q/k RMSNorm and RoPE in its epilogue
+      const QkRopeEpi qe{w.q_norm, w.k_norm, m.heads, m.kv_heads, m.eps, pos, m.cos_t, m.sin_t};
+      EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16QkRope, &qe));
+      EC_TRY(attention());
+      EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, h32, h32, H, kEpiF32Resid));
+      RmsArgs r2f{h32, nullptr, w.post_ln, m.eps, hb, nullptr, T, H};
+      {
+        const int e0 = prof_begin(d);
+        EC_TRY(rows(launch_rmsnorm(r2f, st), "rmsnorm", TH * 6.0, e0));
+      }
+      EC_TRY(gemm(hb, H, w.wgu, 2 * F, H, nullptr, nullptr, ff, F, kEpiBf16Swiglu));
+      EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, h32, h32, H, kEpiF32Resid));
+      continue;
     }
     EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16));
     QkRopeArgs q;

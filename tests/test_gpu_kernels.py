@@ -54,8 +54,38 @@ def test_gemm_epilogues(ec, M, N, K, bn, epi):
     assert err < tol, f"rel err {err}"
 
 
+# CTA-pair GEMM (cta_group::2, 256 x 256 tiles): ragged M (one or both
+# halves of the last tile past M), K down to one k-block
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (129, 512, 384), (300, 1536, 384),
+                                   (4097, 1536, 384), (2000, 768, 768), (513, 3072, 768)])
+@pytest.mark.parametrize("epi", [0, 1, 2, 4])
+def test_gemm_cta_pair(ec, monkeypatch, M, N, K, epi):
+    monkeypatch.setenv("EC_GEMM_PAIR", "1")
+    g = torch.Generator(device="cuda").manual_seed(M * 3 + N + K + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    ref = A.float() @ W.float().t() + bias
+    if epi == 1:
+        ref = _gelu_as(ref)
+    if epi in (0, 1):
+        out = _gemm(ec, A, W, bias, None, epi, 0, N, torch.bfloat16).float()
+        tol = 1e-2
+    else:
+        resid = torch.randn(M, N, device="cuda", generator=g) if epi == 2 else None
+        if resid is not None:
+            ref = ref + resid
+        out = _gemm(ec, A, W, bias, resid, epi, 0, N, torch.float32)
+        tol = 1e-4
+    err = (out - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
+    assert err < tol, f"rel err {err}"
+
+
 @pytest.mark.parametrize("M,F", [(1, 3072), (300, 3072), (1029, 1536)])
-def test_gemm_swiglu(ec, M, F):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_gemm_swiglu(ec, monkeypatch, M, F, pair):
+    if pair:
+        monkeypatch.setenv("EC_GEMM_PAIR", "1")
     K = 1024
     g = torch.Generator(device="cuda").manual_seed(M + F)
     A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
@@ -63,7 +93,7 @@ def test_gemm_swiglu(ec, M, F):
     Wu = (0.03 * torch.randn(F, K, device="cuda", generator=g)).bfloat16()
     # block-interleave 128 rows of gate, 128 rows of up (256-wide tiles)
     W = torch.stack([Wg.view(F // 128, 128, K), Wu.view(F // 128, 128, K)], 1).reshape(2 * F, K)
-    out = _gemm(ec, A, W.contiguous(), None, None, 3, 256, F, torch.bfloat16).float()
+    out = _gemm(ec, A, W.contiguous(), None, None, 3, 0 if pair else 256, F, torch.bfloat16).float()
     gg = A.float() @ Wg.float().t()
     uu = A.float() @ Wu.float().t()
     ref = gg / (1 + torch.exp(-gg)) * uu
