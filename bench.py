@@ -7,7 +7,7 @@ BF16 tensor-core path), 1024 sequences of uniform length 16..256 with
 [CLS]/[SEP], mean pooling + L2.  A step is one forward over the whole batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload minilm|bert-base|mpnet|qwen3]
+                    [--workload minilm|bert-base|mpnet|qwen3|gemma]
 
 N > 1 is launched by torch.distributed.run, one process per GPU: every rank
 embeds its own 1024-sequence shard (weak scaling, no data-path collective);
@@ -40,6 +40,9 @@ WORKLOADS = {
     "bert-base": ("bert-base", 1, 8192, "BERT-base shape BF16, 8192 seqs log-U[32,512], CLS"),
     "mpnet": ("mpnet-base", 2, 4096, "MPNet-base shape, 4096 seqs len U[64,384], mean pool"),
     "qwen3": ("qwen3-0.6b", 3, 2048, "Qwen3-0.6B shape BF16, 2048 seqs len U[128,512]+EOS, last"),
+    "gemma": ("embeddinggemma", 4, 2048,
+              "EmbeddingGemma shape (24 layers, H 512, PLE 512, out 768), 2048 seqs "
+              "len U[16,512], mean pool + projection"),
 }
 IVF_N, IVF_D, IVF_K, IVF_ITERS, IVF_SEED = 3_270_000, 384, 4096, 20, 4
 
@@ -59,13 +62,19 @@ def parse_args():
 
 def algorithmic_flops(shape, offsets):
     """Encoder FLOPs on true lengths: layers * [2 L (4H^2 + 2HF) + 4 L^2 H]
-    (BERT family); Qwen3: layers * [2 L (qkv+o+3HF) + 2 * 2 L(L+1)/2 * heads*hd]."""
+    (BERT family); Qwen3: layers * [2 L (qkv+o+3HF) + 2 * 2 L(L+1)/2 * heads*hd];
+    EmbeddingGemma: layers * [2 L (qkv+o+3HF + 3HP) + 4 L^2 heads*hd] (3HP: its
+    slice of the per-layer-embedding projection, the PLE gate and projection)."""
     lens = np.diff(offsets).astype(np.float64)
     H, F, Lr = shape.hidden, shape.inter, shape.layers
     if shape.model_type == "qwen3":
         hd, nh, kv = shape.head_dim, shape.heads, shape.kv_heads
         lin = H * (nh * hd + 2 * kv * hd) + nh * hd * H + 3 * H * F
         return float(Lr * np.sum(2 * lens * lin + 2 * nh * hd * lens * (lens + 1)))
+    if shape.model_type == "embedding_gemma2":
+        hd, nh, kv, P = shape.head_dim, shape.heads, shape.kv_heads, shape.extra["ple_dim"]
+        lin = H * (nh * hd + 2 * kv * hd) + nh * hd * H + 3 * H * F + 3 * H * P
+        return float(Lr * np.sum(2 * lens * lin + 4 * nh * hd * lens * lens))
     return float(Lr * np.sum(2 * lens * (4 * H * H + 2 * H * F) + 4 * lens * lens * H))
 
 

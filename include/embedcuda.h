@@ -41,6 +41,7 @@ extern "C" {
 #define EC_FAMILY_BERT 1   /* bert / roberta / distilbert (bert.lisp)        */
 #define EC_FAMILY_MPNET 2  /* mpnet (bert.lisp:322-499)                      */
 #define EC_FAMILY_LLAMA 3  /* llama / qwen2 / qwen3 / mistral (llama.lisp)    */
+#define EC_FAMILY_GEMMA 4  /* embedding_gemma2 (gemma.lisp)                    */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char *ec_last_error(void);

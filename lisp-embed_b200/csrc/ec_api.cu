@@ -1,6 +1,7 @@
 // ec_api.cu -- the C ABI of libembedcuda.so: context, errors, safetensors
 // upload, model load and batched embedding across the library's devices.
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -137,6 +138,25 @@ void prof_end(Device& d, int cls, double flops, double bytes, int e0) {
   d.pend.push_back(PendingEv{cls, flops, bytes, e0, e1});
 }
 
+void trace_launch(Device& d, const char* what) {
+  if (!G().sync_each) return;
+  const auto t0 = std::chrono::steady_clock::now();
+  auto ms = [&] {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  };
+  cudaError_t e;
+  while ((e = cudaStreamQuery(d.stream)) == cudaErrorNotReady) {
+    if (ms() > 60000.0) {
+      fprintf(stderr, "[ec] %s: still running after 60 s\n", what);
+      return;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+  unsigned st = 0;
+  if (e == cudaSuccess) cudaMemcpy(&st, d.status, 4, cudaMemcpyDeviceToHost);
+  fprintf(stderr, "[ec] %s: %s, status %u, %.3f ms\n", what, cudaGetErrorString(e), st, ms());
+}
+
 void prof_collect(Device& d) {
   for (const PendingEv& p : d.pend) {
     float ms = 0.f;
@@ -198,6 +218,7 @@ int ec_init(const int* devices, int ndev) {
     if (o < 0 || o >= count) return set_error(EC_EINVAL, "device %d not visible (%d devices)", o, count);
   G().max_bytes = env_size("EC_MAX_BYTES", 0);
   G().max_tokens = static_cast<int>(env_size("EC_MAX_TOKENS_PER_BATCH", 262144));
+  G().sync_each = getenv("EC_SYNC_EACH_LAUNCH") != nullptr;
   if (G().max_tokens < 1024) G().max_tokens = 1024;
   if (!gemm_init_driver()) return set_error(EC_ECUDA, "cuTensorMapEncodeTiled unavailable");
   std::vector<Device*> made;
@@ -325,7 +346,7 @@ int ec_load_model(const char* config_json, const char* pooling_json, int* family
   }
   const ModelW& m = G().devs[0]->model;
   if (family) *family = m.family;
-  if (dim) *dim = m.H;
+  if (dim) *dim = m.out_dim;
   return EC_OK;
 }
 
@@ -333,7 +354,7 @@ int ec_dim(void) {
   std::lock_guard<std::mutex> lk(G().mu);
   clear_error();
   if (!G().inited || !G().devs[0]->model.family) return set_error(EC_ESTATE, "no model loaded");
-  return G().devs[0]->model.H;
+  return G().devs[0]->model.out_dim;
 }
 
 int ec_embed_batch(const int32_t* ids, const int64_t* offsets, int nseq, float* out,
@@ -346,7 +367,8 @@ int ec_embed_batch(const int32_t* ids, const int64_t* offsets, int nseq, float* 
     return set_error(EC_EINVAL, "bad batch arguments");
   const ModelW& m = G().devs[0]->model;
   if (!m.family) return set_error(EC_ESTATE, "no model loaded");
-  if (out_stride < m.H) return set_error(EC_EINVAL, "out_stride %d < dim %d", out_stride, m.H);
+  if (out_stride < m.out_dim)
+    return set_error(EC_EINVAL, "out_stride %d < dim %d", out_stride, m.out_dim);
   for (int s = 0; s < nseq; ++s)
     if (offsets[s + 1] < offsets[s]) return set_error(EC_EINVAL, "offsets not ascending at %d", s);
   const int nd = static_cast<int>(G().devs.size());
@@ -394,7 +416,8 @@ int ec_embed_batch_device(const int32_t* d_ids, const int64_t* offsets, int nseq
   if (nseq < 0 || !offsets || !d_out || !d_ids) return set_error(EC_EINVAL, "bad batch arguments");
   const ModelW& m = G().devs[0]->model;
   if (!m.family) return set_error(EC_ESTATE, "no model loaded");
-  if (out_stride < m.H) return set_error(EC_EINVAL, "out_stride %d < dim %d", out_stride, m.H);
+  if (out_stride < m.out_dim)
+    return set_error(EC_EINVAL, "out_stride %d < dim %d", out_stride, m.out_dim);
   std::vector<int> all(nseq);
   std::iota(all.begin(), all.end(), 0);
   Device& d = *G().devs[0];

@@ -40,7 +40,7 @@ static cudaError_t run_attn(const AttnLaunch& l, cudaStream_t st) {
   a.blocks = l.blocks;
   a.heads = l.heads;
   a.kv_group = l.kv_group;
-  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(static_cast<float>(HD)));
   a.causal = l.causal;
   a.relbias = l.relbias;
   a.rel_max = l.rel_max;
@@ -101,7 +101,7 @@ static cudaError_t run_fa(const AttnLaunch& l, cudaStream_t st) {
   a.v_off = l.v_off;
   a.out = l.out;
   a.ldo = l.ldo;
-  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(static_cast<float>(HD)));
   a.relbias = l.relbias;
   a.rel_max = l.rel_max;
   a.status = l.status;
@@ -163,7 +163,7 @@ static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
   a.first = l.n_long;
   a.heads = l.heads;
   a.kv_group = l.kv_group;
-  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+  a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(static_cast<float>(HD)));
   a.relbias = l.relbias;
   a.rel_max = l.rel_max;
   a.kcap = (l.max_short_len + 15) & ~15;

@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // is already known complete (the P-buffer waits), so the parity test is
     // never two phases behind.
     auto wait_pv = [&](long long g) -> bool {
-      return mbar_wait(&o_full[g & 1], static_cast<uint32_t>((g >> 1) & 1), abort_flag);
+      return mbar_wait_warp(&o_full[g & 1], static_cast<uint32_t>((g >> 1) & 1), abort_flag);
     };
     float* xch = sX;                               // [2 slots][8 warps][32]
     int xslot = 0;
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     auto exchange = [&](float v, float& other) -> bool {
       xch[(xslot * 8 + sw) * 32 + lane] = v;
       mbar_arrive(&xbar[quad * 2 + xslot]);
-      const bool fine = mbar_wait(&xbar[quad * 2 + xslot], (xbits >> xslot) & 1u, abort_flag);
+      const bool fine = mbar_wait_warp(&xbar[quad * 2 + xslot], (xbits >> xslot) & 1u, abort_flag);
       xbits ^= 1u << xslot;
       other = xch[(xslot * 8 + (sw ^ 4)) * 32 + lane];
       xslot ^= 1;
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const bool warp_live = q0 + quad * 32 < L;  // both partners agree
       float m_run = -INFINITY, l_part = 0.f;
       for (int j = 0; j < nkb; ++j) {
-        if (!mbar_wait(&s_full[sbuf], (sf_bits >> sbuf) & 1u, abort_flag)) {
+        if (!mbar_wait_warp(&s_full[sbuf], (sf_bits >> sbuf) & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -410,9 +410,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             break;
           }
           mx = fmaxf(mx, mo);
-          // lazy rescale: keep the stale max unless the new one is 2^8 larger
-          if (mx > m_run + 8.0f) {
-            const float corr = fa_exp2(m_run - mx);
+          // lazy rescale: keep the stale max unless the new one is 2^8 larger.
+          // The decision is per row (lane) but the TMEM loads / stores below
+          // are warp-collective (.sync.aligned), so the whole warp rescales
+          // when any row needs it, each row by its own factor (1 where its
+          // max did not grow).  The partner warp sees the same row maxima
+          // and takes the same branch.
+          if (__any_sync(0xffffffffu, mx > m_run + 8.0f)) {
+            const float m_new = fmaxf(m_run, mx);
+            const float corr = m_new == -INFINITY ? 1.f : fa_exp2(m_run - m_new);
+            mx = m_new;
             if (j > 0) {
               // O holds PV of blocks < j: wait for PV(j-1), then scale our half
               if (!wait_pv(pv_done + j - 1)) {
@@ -448,7 +455,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // pass 2: P = exp2(logit - m_run) into this warp's K-atom of P buffer
         // pb (the PV two blocks back has released it), row sum
         const int pb = static_cast<int>((pv_done + j) & 1);
-        if (!mbar_wait(&p_empty[pb], ((pe_bits >> pb) & 1u) ^ 1u, abort_flag)) {
+        if (!mbar_wait_warp(&p_empty[pb], ((pe_bits >> pb) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }

@@ -102,7 +102,7 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   CUtensorMap ta, tb, tc;
   if (!encode_2d_bf16(&ta, g.A, g.M, g.K, g.lda, kGemmBM)) return cudaErrorInvalidValue;
   if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.ldw, BN / CG)) return cudaErrorInvalidValue;
-  const uint64_t out_cols = EPI == kEpiBf16Swiglu ? g.N / 2 : g.N;
+  const uint64_t out_cols = (EPI == kEpiBf16Swiglu || EPI == kEpiBf16GeluTanhGate) ? g.N / 2 : g.N;
   if (!encode_2d_out(&tc, g.out, Cfg::OUT_F32, g.M, out_cols, g.ldo)) return cudaErrorInvalidValue;
   GemmArgs a;
   a.M = g.M;
@@ -142,6 +142,9 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
     case kEpiBf16QkRope:
       if constexpr (BN == 256) return run<BN, kEpiBf16QkRope>(g, st, num_sms);
       return cudaErrorInvalidValue;
+    case kEpiBf16GeluTanhGate:
+      if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16GeluTanhGate>(g, st, num_sms);
+      return cudaErrorInvalidValue;
     case kEpiBf16Swiglu:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
       return cudaErrorInvalidValue;
@@ -150,7 +153,8 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
 }
 
 int gemm_pick_bn(int M, int N, int epi, int num_sms) {
-  if (epi == kEpiBf16Swiglu) return N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
+  if (epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate)
+    return N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
   if (epi == kEpiBf16QkRope) return N % 256 == 0 ? 256 : 0;
   const int mt = (M + kGemmBM - 1) / kGemmBM;
   int best = 0;
@@ -187,6 +191,7 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms) {
       case kEpiF32Resid: return run<256, kEpiF32Resid, 2>(g, st, num_sms);
       case kEpiF32: return run<256, kEpiF32, 2>(g, st, num_sms);
       case kEpiBf16Swiglu: return run<256, kEpiBf16Swiglu, 2>(g, st, num_sms);
+      case kEpiBf16GeluTanhGate: return run<256, kEpiBf16GeluTanhGate, 2>(g, st, num_sms);
       case kEpiBf16QkRope: return run<256, kEpiBf16QkRope, 2>(g, st, num_sms);
       default: break;
     }

@@ -38,6 +38,8 @@ enum GemmEpi : int {
   kEpiF32 = 4,         // out f32  = acc + bias
   kEpiBf16QkRope = 5,  // out bf16 = acc, with per-head RMSNorm + RoPE on the
                        // q/k heads (llama.lisp:244-253, 137-151), head dim 128
+  kEpiBf16GeluTanhGate = 6,  // out bf16 = gelu_tanh(gate) * up, N/2 wide
+                             // (gemma.lisp:277-283), SwiGLU's tile layout
 };
 
 // per-head q/k RMSNorm + rotate-half RoPE applied in the QKV epilogue
@@ -141,6 +143,12 @@ __device__ __forceinline__ float2 gelu_as2(float2 x) {
   const float2 se = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
   const float2 hx = __fmul2_rn(x, f2(0.5f));
   return __ffma2_rn(hx, se, hx);
+}
+
+// gelu_pytorch_tanh (gemma::gelu-tanh, gemma.lisp:85-89) in single precision
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float c = 0.7978845608028654f * (x + ((0.044715f * x) * x) * x);
+  return (0.5f * x) * (1.0f + tanhf(c));
 }
 
 // x * sigmoid(x) (llama::silu, llama.lisp:119-122)
@@ -324,7 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const int half = ew >> 2;  // the column part
     uint8_t* stage_base = smE + ew * 2 * Cfg::CHUNK_BYTES;
-    constexpr int NCH = EPI == kEpiBf16Swiglu ? BN / 64 : BN / 32;  // output chunks per tile
+    constexpr int NCH = (EPI == kEpiBf16Swiglu || EPI == kEpiBf16GeluTanhGate) ? BN / 64 : BN / 32;  // output chunks per tile
     static_assert(NCH >= PARTS, "every epilogue warp needs a chunk per tile");
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -348,7 +356,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // pass 2: scale by the norm weight, rotate pairs (i, i + 64), store
           const int gh = nb * 2 + half;
           const float* wn = gh < args.qk.q_heads ? args.qk.q_norm : args.qk.k_norm;
-          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+          if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
             report(args.status, kDevTimeoutEpilogue);
             *abort_flag = 1;
             break;
@@ -446,7 +454,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c0 = half; c0 < NCH; c0 += STEP) {
         const bool two = PAIR && c0 + 2 < NCH;
         if (c0 == half) {
-          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+          if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
             fine = false;
             break;
           }
@@ -519,7 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1
       for (int c = half; c < NCH; c += PARTS) {
-        const int col0 = (EPI == kEpiBf16Swiglu ? nb * (BN / 2) : nb * BN) + c * 32;
+        const int col0 = ((EPI == kEpiBf16Swiglu || EPI == kEpiBf16GeluTanhGate) ? nb * (BN / 2) : nb * BN) + c * 32;
         // residual rows row0 + 4k + lane/8, columns col0 + (lane%8)*4 .. +3:
         // coalesced 128-byte rows, issued before the TMEM wait
         float4 res[8];
@@ -534,7 +542,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (c == half) {
-          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+          if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
             report(args.status, kDevTimeoutEpilogue);
             *abort_flag = 1;
             tile = args.num_tiles;  // leave both loops
@@ -545,14 +553,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                static_cast<uint32_t>(acc * BN);
         float v[32];
-        if constexpr (EPI == kEpiBf16Swiglu) {
+        if constexpr ((EPI == kEpiBf16Swiglu || EPI == kEpiBf16GeluTanhGate)) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(t_row + c * 32, g);
           tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, u);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+          for (int j = 0; j < 32; ++j) {
+            if constexpr (EPI == kEpiBf16GeluTanhGate)
+              v[j] = gelu_tanh_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+            else
+              v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+          }
         } else {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);

@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ew == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::XS_TX);
       }
       __syncwarp();
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
         ok = false;
         break;
       }
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint8_t* buf = bufs + b * Cfg::BUF_BYTES;
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_row + cl, v);
-        if (!mbar_wait(&rb[b], (rbits >> b) & 1u, abort_flag)) {
+        if (!mbar_wait_warp(&rb[b], (rbits >> b) & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int r = 0; r < C; ++r)
           st_async_cluster_v2(cluster_map(dst, r), s_loc, m2_loc, cluster_map(bar, r));
       }
-      if (!mbar_wait_cluster(&xbar[par], static_cast<uint32_t>((tcount >> 1) & 1), abort_flag)) {
+      if (!mbar_wait_cluster_warp(&xbar[par], static_cast<uint32_t>((tcount >> 1) & 1), abort_flag)) {
         ok = false;
         break;
       }

@@ -76,6 +76,67 @@ struct PoolArgs {
   int H;
 };
 
+// ---- EmbeddingGemma rows (ec_gemma.cu) ---------------------------------------
+struct GemmaEmbedArgs {
+  const int* ids;
+  const void* table;
+  int dtype;
+  float scale;          // sqrt(hidden) as a single-float
+  float* h32;           // [T, H]
+  __nv_bfloat16* h0b;   // [T, H] bf16 copy
+  int T, H;
+};
+struct HeadNormRopeArgs {
+  __nv_bfloat16* qkv;   // [T, ld] packed q | k | v heads
+  int ld;
+  int q_heads, kv_heads, hd;
+  const float* q_norm;
+  const float* k_norm;
+  double eps;
+  const int* pos;
+  const float* cos_t;   // [max_pos, hd / 2]
+  const float* sin_t;
+  int T;
+};
+struct NormAddArgs {
+  const float* x;       // [T, H] sub-block output
+  const float* g1;      // its RMSNorm weight
+  float* h32;           // residual stream, updated in place
+  int scale_h;          // multiply h by `scalar` after the add
+  float scalar;
+  const float* g2;      // RMSNorm weight for hb, or nullptr (hb = bf16(h))
+  __nv_bfloat16* outb;  // [T, H] or nullptr
+  double eps;
+  int T, H;
+};
+struct PlePrepArgs {
+  float* x;             // [T, P], in place
+  float inv_sqrt_h;
+  const float* g;
+  double eps;
+  int T, P;
+};
+struct PleGateArgs {
+  const float* gate;    // [T, P]
+  const float* ple;     // [T, P]
+  __nv_bfloat16* outb;  // [T, P]
+  int T, P;
+};
+struct GemmaPoolArgs {
+  const float* h;       // [T, H] after the final RMSNorm
+  const int* cu;        // [nseq + 1]
+  const float* w_out;   // [out_dim, H]
+  float* out;
+  int out_stride;
+  int H, out_dim;
+};
+cudaError_t launch_gemma_embed(const GemmaEmbedArgs& a, cudaStream_t st);
+cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t st);
+cudaError_t launch_norm_add(const NormAddArgs& a, cudaStream_t st);
+cudaError_t launch_ple_prep(const PlePrepArgs& a, cudaStream_t st);
+cudaError_t launch_ple_gate(const PleGateArgs& a, cudaStream_t st);
+cudaError_t launch_gemma_pool(const GemmaPoolArgs& a, int nseq, cudaStream_t st);
+
 cudaError_t launch_embed_ln(const EmbedLnArgs& a, cudaStream_t st);
 cudaError_t launch_ln(const LnArgs& a, cudaStream_t st);
 cudaError_t launch_rmsnorm(const RmsArgs& a, cudaStream_t st);
@@ -179,6 +240,7 @@ struct AttnLaunch {
   int n_long;
   int nblocks128_long;
   int max_short_len;     // longest sequence in [n_long, nseq)
+  float scale = 0.f;     // logit scale; 0 = 1 / sqrt(head_dim) (Gemma uses 1.0)
 };
 // key capacity of the short-sequence attention kernel (ec_attn_short.cuh)
 constexpr int kAttnShortCap = 256;

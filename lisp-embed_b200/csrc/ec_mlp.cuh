@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
       const int row0 = tile * 128 + quad * 32;
       for (int f = 0; f < NF; ++f) {
-        if (!mbar_wait(u_full, u_phase, abort_flag)) {
+        if (!mbar_wait_warp(u_full, u_phase, abort_flag)) {
           ok = false;
           break;
         }
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(u_empty);
         const int pb = f % Cfg::PBUF;
-        if (!mbar_wait(&p_empty[pb], pe_phase[pb] ^ 1, abort_flag)) {
+        if (!mbar_wait_warp(&p_empty[pb], pe_phase[pb] ^ 1, abort_flag)) {
           ok = false;
           break;
         }
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       }
       if (!ok) break;
       // ------------------------------------------- bias + residual + LayerNorm
-      if (!mbar_wait(y_full, y_phase, abort_flag)) {
+      if (!mbar_wait_warp(y_full, y_phase, abort_flag)) {
         ok = false;
         break;
       }

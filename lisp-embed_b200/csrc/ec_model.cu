@@ -360,6 +360,146 @@ static int load_llama(Device& d, const JVal& cfg) {
   return EC_OK;
 }
 
+// RoPE table of gemma::init-rope / llama::init-rope: double, rounded to single
+static int rope_table(Device& d, double theta, int hd, int max_pos, float** cos_t, float** sin_t) {
+  const int half = hd / 2;
+  std::vector<float> cs(static_cast<size_t>(max_pos) * half), sn(cs.size());
+  for (int p = 0; p < max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double freq = 1.0 / std::pow(theta, (2.0 * i) / hd);
+      const double ang = p * freq;
+      cs[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(ang));
+      sn[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(ang));
+    }
+  void *dc, *ds;
+  int rc;
+  if ((rc = model_alloc(d, &dc, cs.size() * 4, "rope cos")) ||
+      (rc = model_alloc(d, &ds, sn.size() * 4, "rope sin")))
+    return rc;
+  if ((rc = check_cuda(cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope")) ||
+      (rc = check_cuda(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope")))
+    return rc;
+  *cos_t = static_cast<float*>(dc);
+  *sin_t = static_cast<float*>(ds);
+  return EC_OK;
+}
+
+// gemma:load-model (gemma.lisp:140-212): text_config fields, weights under
+// language_model., per-layer head dim from q_norm and kv heads from k_proj;
+// RoPE theta 1e6 on full_attention layers, 1e4 otherwise (:173-175).
+static int load_gemma(Device& d, const JVal& tc) {
+  ModelW& m = d.model;
+  int rc;
+  if ((rc = cfg_int(tc, "hidden_size", &m.H)) || (rc = cfg_int(tc, "num_hidden_layers", &m.layers)) ||
+      (rc = cfg_int(tc, "num_attention_heads", &m.heads)) ||
+      (rc = cfg_int(tc, "intermediate_size", &m.F)))
+    return rc;
+  if ((rc = cfg_int(tc, "hidden_size_per_layer_input", &m.ple_dim, false, m.H)) ||
+      (rc = cfg_int(tc, "embedding_dim", &m.out_dim, false, 768)))
+    return rc;
+  const JVal* ep = tc.get("rms_norm_eps");
+  m.eps = (ep && ep->is_num()) ? ep->num() : 1e-6;
+  m.family = EC_FAMILY_GEMMA;
+  m.pooling = 1;      // gemma::*pooling* :mean
+  m.max_pos = 2048;   // gemma::*max-pos*
+  const int H = m.H, F = m.F, P = m.ple_dim, NL = m.layers;
+  const std::string pre = "language_model.";
+  const Tensor *emb = nullptr, *pp = nullptr, *ppn = nullptr, *nw = nullptr, *wo = nullptr;
+  if ((rc = need_t(d, pre + "embed_tokens.weight", &emb, {})) ||
+      (rc = need_t(d, pre + "ple.per_layer_model_projection.weight", &pp,
+                   {static_cast<int64_t>(NL) * P, H})) ||
+      (rc = need_t(d, pre + "ple.per_layer_projection_norm.weight", &ppn, {P})) ||
+      (rc = need_t(d, pre + "norm.weight", &nw, {H})) ||
+      (rc = need_t(d, pre + "embedding_projection.weight", &wo, {m.out_dim, H})))
+    return rc;
+  if (emb->shape.size() != 2 || emb->shape[1] != H)
+    return set_error(EC_EINVAL, "embed_tokens must be [*, %d]", H);
+  // head dim / kv heads of layer 0; every layer must agree (one workspace)
+  const Tensor *qn0 = nullptr, *k0 = nullptr;
+  if ((rc = need_t(d, pre + "layers.0.self_attn.q_norm.weight", &qn0, {})) ||
+      (rc = need_t(d, pre + "layers.0.self_attn.k_proj.weight", &k0, {})))
+    return rc;
+  m.hd = static_cast<int>(qn0->numel);
+  m.kv_heads = m.hd ? static_cast<int>(k0->shape[0] / m.hd) : 0;
+  if (m.hd != 32 && m.hd != 64 && m.hd != 128)
+    return set_error(EC_EUNSUPPORTED, "gemma head_dim %d (attention kernels: 32, 64, 128)", m.hd);
+  if (m.kv_heads <= 0 || m.heads % m.kv_heads)
+    return set_error(EC_EINVAL, "heads %d not a multiple of kv heads %d", m.heads, m.kv_heads);
+  if (H % 128 || P % 64 || F % 128 || ((m.heads + 2 * m.kv_heads) * m.hd) % 64 || H > 2048 ||
+      H + m.out_dim > 12288)
+    return set_error(EC_EUNSUPPORTED, "gemma widths H %d P %d F %d outside this build", H, P, F);
+  m.word = emb->p;
+  m.word_dt = emb->dtype;
+  m.vocab = static_cast<int>(emb->shape[0]);
+  if ((rc = as_f32(d, nw, &m.final_norm)) || (rc = as_f32(d, ppn, &m.ple_norm)) ||
+      (rc = as_f32(d, wo, &m.w_out)))
+    return rc;
+  if ((rc = rope_table(d, 10000.0, m.hd, m.max_pos, &m.cos_t, &m.sin_t)) ||
+      (rc = rope_table(d, 1e6, m.hd, m.max_pos, &m.cos2_t, &m.sin2_t)))
+    return rc;
+  const JVal* types = tc.get("layer_types");
+  const int qd = m.heads * m.hd, kvd = m.kv_heads * m.hd;
+  m.gl.resize(NL);
+  for (int li = 0; li < NL; ++li) {
+    const std::string pf = pre + "layers." + std::to_string(li) + ".";
+    GemmaLayerW& L = m.gl[li];
+    const Tensor *in, *post, *pre_ff, *post_ff, *qw, *kw, *vw, *ow, *qn, *kn, *gw, *uw, *dw, *pg, *pj,
+        *pn, *sc;
+    if ((rc = need_t(d, pf + "input_layernorm.weight", &in, {H})) ||
+        (rc = need_t(d, pf + "post_attention_layernorm.weight", &post, {H})) ||
+        (rc = need_t(d, pf + "pre_feedforward_layernorm.weight", &pre_ff, {H})) ||
+        (rc = need_t(d, pf + "post_feedforward_layernorm.weight", &post_ff, {H})) ||
+        (rc = need_t(d, pf + "self_attn.q_proj.weight", &qw, {qd, H})) ||
+        (rc = need_t(d, pf + "self_attn.k_proj.weight", &kw, {kvd, H})) ||
+        (rc = need_t(d, pf + "self_attn.v_proj.weight", &vw, {kvd, H})) ||
+        (rc = need_t(d, pf + "self_attn.o_proj.weight", &ow, {H, qd})) ||
+        (rc = need_t(d, pf + "self_attn.q_norm.weight", &qn, {m.hd})) ||
+        (rc = need_t(d, pf + "self_attn.k_norm.weight", &kn, {m.hd})) ||
+        (rc = need_t(d, pf + "mlp.gate_proj.weight", &gw, {F, H})) ||
+        (rc = need_t(d, pf + "mlp.up_proj.weight", &uw, {F, H})) ||
+        (rc = need_t(d, pf + "mlp.down_proj.weight", &dw, {H, F})) ||
+        (rc = need_t(d, pf + "ple_block.per_layer_input_gate.weight", &pg, {P, H})) ||
+        (rc = need_t(d, pf + "ple_block.per_layer_projection.weight", &pj, {H, P})) ||
+        (rc = need_t(d, pf + "ple_block.post_per_layer_input_norm.weight", &pn, {H})) ||
+        (rc = need_t(d, pf + "layer_scalar", &sc, {})))
+      return rc;
+    if (sc->numel < 1) return set_error(EC_EINVAL, "%slayer_scalar is empty", pf.c_str());
+    if ((rc = as_f32(d, in, &L.in_ln)) || (rc = as_f32(d, post, &L.post_ln)) ||
+        (rc = as_f32(d, pre_ff, &L.pre_ff_ln)) || (rc = as_f32(d, post_ff, &L.post_ff_ln)) ||
+        (rc = as_f32(d, qn, &L.q_norm)) || (rc = as_f32(d, kn, &L.k_norm)) ||
+        (rc = as_f32(d, pn, &L.ple_norm)) ||
+        (rc = concat_bf16(d, {qw, kw, vw}, H, &L.wqkv)) || (rc = concat_bf16(d, {ow}, qd, &L.wo)) ||
+        (rc = concat_bf16(d, {dw}, F, &L.wdown)) || (rc = concat_bf16(d, {pg}, H, &L.wple_gate)) ||
+        (rc = concat_bf16(d, {pj}, P, &L.wple_proj)))
+      return rc;
+    // this layer's P rows of the per-layer-embedding projection
+    void* p;
+    if ((rc = model_alloc(d, &p, static_cast<size_t>(P) * H * 2, "ple rows"))) return rc;
+    if ((rc = rows_to_bf16(d, pp, static_cast<int64_t>(li) * P, P, H, static_cast<bf16*>(p))))
+      return rc;
+    L.wpp = static_cast<bf16*>(p);
+    // gate/up interleaved by 128 rows for the gated epilogue
+    if ((rc = model_alloc(d, &p, static_cast<size_t>(2) * F * H * 2, "gate/up"))) return rc;
+    bf16* gu = static_cast<bf16*>(p);
+    for (int b = 0; b < F / 128; ++b) {
+      if ((rc = rows_to_bf16(d, gw, b * 128, 128, H, gu + static_cast<size_t>(2 * b) * 128 * H)) ||
+          (rc = rows_to_bf16(d, uw, b * 128, 128, H, gu + static_cast<size_t>(2 * b + 1) * 128 * H)))
+        return rc;
+    }
+    L.wgu = gu;
+    // the layer scalar, read back once (a [1] tensor of the upload dtype)
+    float* scd;
+    if ((rc = as_f32(d, sc, &scd))) return rc;
+    if ((rc = check_cuda(cudaMemcpy(&L.scalar, scd, 4, cudaMemcpyDeviceToHost), "layer scalar")))
+      return rc;
+    const JVal* ty = (types && types->kind == JVal::Arr && li < static_cast<int>(types->a.size()))
+                         ? &types->a[li]
+                         : nullptr;
+    L.rope = (ty && ty->kind == JVal::Str && ty->s == "full_attention") ? 1 : 0;
+  }
+  return EC_OK;
+}
+
 int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
   free_model(d);
   // the workspace is laid out for a model; a new model starts from scratch
@@ -389,10 +529,11 @@ int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
              mt == "gemma2") {
     rc = load_llama(d, cfg);
   } else if (mt == "embedding_gemma2" || mt == "embedding_gemma2_text") {
-    rc = set_error(EC_EUNSUPPORTED, "model_type %s is not built in this library", mt.c_str());
+    rc = load_gemma(d, tc && tc->kind == JVal::Obj ? *tc : cfg);  // model.lisp:41-43
   } else {
     rc = set_error(EC_EUNSUPPORTED, "unsupported model_type %s", mt.c_str());
   }
+  if (rc == EC_OK && d.model.out_dim == 0) d.model.out_dim = d.model.H;
   if (rc == EC_OK) rc = sync_and_check(d, "model assembly");
   if (rc != EC_OK) free_model(d);
   return rc;
@@ -401,6 +542,7 @@ int load_model_on(Device& d, const JVal& cfg, const JVal* pool) {
 // --------------------------------------------------------------- forward --
 struct WsLayout {
   size_t ids, pos, cu, blocks, blocks128, seqs, h32, tmp, hb, qkv, ctx, ff, out, total;
+  size_t h0b = 0, ple = 0, pg = 0, pgb = 0;  // Gemma per-layer-embedding buffers
 };
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -423,7 +565,14 @@ static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
   L.qkv = o; o += al256(T * nqkv * 2);
   L.ctx = o; o += al256(T * nctx * 2);
   L.ff = o; o += al256(T * m.F * 2);
-  L.out = o; o += al256(nseq * m.H * 4);
+  L.out = o; o += al256(nseq * std::max(m.H, m.out_dim) * 4);
+  if (m.family == EC_FAMILY_GEMMA) {
+    const size_t P = m.ple_dim;
+    L.h0b = o; o += al256(T * m.H * 2);
+    L.ple = o; o += al256(T * P * 4);
+    L.pg = o; o += al256(T * P * 4);
+    L.pgb = o; o += al256(T * P * 2);
+  }
   L.total = o;
   return L;
 }
@@ -436,7 +585,7 @@ static int ensure_ws(Device& d, int T, int nseq) {
   const size_t pin = static_cast<size_t>(t2) * 4 + (static_cast<size_t>(s2) + 1) * 4 +
                      (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
                      (static_cast<size_t>(t2) / 128 + s2 + 1) * 16 + static_cast<size_t>(s2) * 8 + 768 +
-                     static_cast<size_t>(s2) * d.model.H * 4 + 1024;
+                     static_cast<size_t>(s2) * std::max(d.model.H, d.model.out_dim) * 4 + 1024;
   if (!d.ws || L.total > d.ws_bytes) {
     if (d.ws) {
       cudaStreamSynchronize(d.stream);
@@ -505,6 +654,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   // profiling): class 0 gemm, 1 attention, 2 row kernels
   auto rows = [&](cudaError_t e, const char* what, double bytes, int e0) -> int {
     prof_end(d, 2, 0.0, bytes, e0);
+    trace_launch(d, what);
     return check_cuda(e, what);
   };
   const double TH = static_cast<double>(T) * H;
@@ -540,6 +690,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_gemm(g, st, d.num_sms);
     prof_end(d, 0, 2.0 * T * N * K, bytes, e0);
+    trace_launch(d, "gemm");
     return check_cuda(e, "gemm");
   };
   // h32 = LayerNorm(A . W^T + bias + h32), hb = bf16(h32) in one kernel
@@ -552,6 +703,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_gemm_ln(g, st, d.num_sms);
     prof_end(d, 0, 2.0 * T * H * K, bytes, e0);
+    trace_launch(d, "gemm+layernorm");
     return check_cuda(e, "gemm+layernorm");
   };
   AttnLaunch at;
@@ -585,6 +737,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_attention(at, st);
     prof_end(d, 1, attn_pairs * 4.0 * m.heads * m.hd, 2.0 * T * (nqkv + nctx), e0);
+    trace_launch(d, "attention");
     return check_cuda(e, "attention");
   };
 
@@ -659,6 +812,61 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
       EC_TRY(rows(launch_pool_l2(pa, nseq, st), "pool",
                   (m.pooling == 1 ? TH : static_cast<double>(nseq) * H) * 4.0, e0));
     }
+    return EC_OK;
+  }
+  if (m.family == EC_FAMILY_GEMMA) {
+    // gemma::embed / layer-forward (gemma.lisp:216-376)
+    const int P = m.ple_dim;
+    bf16* h0b = reinterpret_cast<bf16*>(ws + L.h0b);
+    float* ple = reinterpret_cast<float*>(ws + L.ple);
+    float* pg = reinterpret_cast<float*>(ws + L.pg);
+    bf16* pgb = reinterpret_cast<bf16*>(ws + L.pgb);
+    at.scale = 1.0f;  // bidirectional attention with scale 1.0 (gemma.lisp:250-265)
+    at.causal = 0;
+    auto row = [&](cudaError_t e, const char* what, double bytes) -> int {
+      const int e0 = prof_begin(d);
+      return rows(e, what, bytes, e0);
+    };
+    {
+      GemmaEmbedArgs ea{ids, m.word, m.word_dt, sqrtf(static_cast<float>(H)), h32, h0b, T, H};
+      EC_TRY(row(launch_gemma_embed(ea, st), "gemma embed", TH * 10.0));
+    }
+    const float inv_sqrt_h = 1.0f / sqrtf(static_cast<float>(H));
+    for (int li = 0; li < m.layers; ++li) {
+      const GemmaLayerW& w = m.gl[li];
+      // attention sub-block
+      RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};
+      EC_TRY(row(launch_rmsnorm(r1, st), "rmsnorm", TH * 6.0));
+      EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16));
+      HeadNormRopeArgs hr{qkv, nqkv, m.heads, m.kv_heads, m.hd, w.q_norm, w.k_norm, m.eps, pos,
+                          w.rope ? m.cos2_t : m.cos_t, w.rope ? m.sin2_t : m.sin_t, T};
+      EC_TRY(row(launch_head_norm_rope(hr, st), "head norm rope", 4.0 * T * nqkv));
+      EC_TRY(attention());
+      EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, nullptr, tmp, H, kEpiF32));
+      NormAddArgs na1{tmp, w.post_ln, h32, 0, 1.f, w.pre_ff_ln, hb, m.eps, T, H};
+      EC_TRY(row(launch_norm_add(na1, st), "norm add", TH * 14.0));
+      // gated GELU-tanh MLP
+      EC_TRY(gemm(hb, H, w.wgu, 2 * F, H, nullptr, nullptr, ff, F, kEpiBf16GeluTanhGate));
+      EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, nullptr, tmp, H, kEpiF32));
+      NormAddArgs na2{tmp, w.post_ff_ln, h32, 0, 1.f, nullptr, hb, m.eps, T, H};
+      EC_TRY(row(launch_norm_add(na2, st), "norm add", TH * 14.0));
+      // per-layer embedding of this layer from the scaled token embedding
+      EC_TRY(gemm(h0b, H, w.wpp, P, H, nullptr, nullptr, ple, P, kEpiF32));
+      PlePrepArgs pa{ple, inv_sqrt_h, m.ple_norm, m.eps, T, P};
+      EC_TRY(row(launch_ple_prep(pa, st), "ple prep", 8.0 * T * P));
+      // PLE block: gate(h) -> GELU-tanh * ple -> projection -> norm -> residual
+      EC_TRY(gemm(hb, H, w.wple_gate, P, H, nullptr, nullptr, pg, P, kEpiF32));
+      PleGateArgs pga{pg, ple, pgb, T, P};
+      EC_TRY(row(launch_ple_gate(pga, st), "ple gate", 10.0 * T * P));
+      EC_TRY(gemm(pgb, P, w.wple_proj, H, P, nullptr, nullptr, tmp, H, kEpiF32));
+      NormAddArgs na3{tmp, w.ple_norm, h32, 1, w.scalar, nullptr, nullptr, m.eps, T, H};
+      EC_TRY(row(launch_norm_add(na3, st), "norm add scale", TH * 12.0));
+    }
+    // final RMSNorm per token, then mean pool + projection + L2
+    RmsArgs rf{h32, nullptr, m.final_norm, m.eps, nullptr, h32, T, H};
+    EC_TRY(row(launch_rmsnorm(rf, st), "final rmsnorm", TH * 8.0));
+    GemmaPoolArgs gp{h32, cu, m.w_out, out, out_stride, H, m.out_dim};
+    EC_TRY(row(launch_gemma_pool(gp, nseq, st), "pool project", TH * 4.0));
     return EC_OK;
   }
   // llama family: h = embed_tokens[ids] (llama.lisp:316-320)
@@ -853,14 +1061,14 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     }
     float* dout = out_dev ? out_dev + static_cast<size_t>(seqs[i]) * out_stride
                           : reinterpret_cast<float*>(ws + L.out);
-    const int ostride = out_dev ? out_stride : m.H;
+    const int ostride = out_dev ? out_stride : m.out_dim;
     double pairs = 0.0;  // (query, key) pairs that attention scores
     for (int k = 0; k < nseq; ++k)
       pairs += m.family == EC_FAMILY_LLAMA ? 0.5 * lens[k] * (lens[k] + 1.0)
                                            : static_cast<double>(lens[k]) * lens[k];
     EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
     if (!out_dev) {
-      std::vector<float> hout(static_cast<size_t>(nseq) * m.H);
+      std::vector<float> hout(static_cast<size_t>(nseq) * m.out_dim);
       EC_TRY(check_cuda(cudaMemcpyAsync(hout.data(), dout, hout.size() * 4,
                                         cudaMemcpyDeviceToHost, d.stream),
                         "output download"));
@@ -868,7 +1076,7 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
       prof_collect(d);
       for (int k = 0; k < nseq; ++k)
         std::memcpy(out_host + static_cast<size_t>(seqs[i + k]) * out_stride,
-                    hout.data() + static_cast<size_t>(k) * m.H, static_cast<size_t>(m.H) * 4);
+                    hout.data() + static_cast<size_t>(k) * m.out_dim, static_cast<size_t>(m.out_dim) * 4);
     } else {
       EC_TRY(sync_and_check(d, "forward"));
       prof_collect(d);

@@ -86,14 +86,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// mbar_wait for a whole warp that goes on to warp-collective (.sync.aligned)
+// tcgen05 loads / stores: every lane gets the same answer, so a lane whose
+// wait ran out can never leave the others inside an aligned instruction.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
 // Bounded rendezvous: every participating thread arrives on `bar` (initialised
 // with the participant count) and waits for the phase to complete.  `phase`
 // is the caller's parity bit for this barrier.  Returns false on timeout or
 // abort, so a partner that gave up can never leave the others blocked.
+// Called by whole warps only (the answer is warp-uniform).
 __device__ __forceinline__ bool mbar_sync(uint64_t* bar, uint32_t& phase,
                                           volatile int* abort_flag) {
   mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, phase, abort_flag);
+  const bool ok = mbar_wait_warp(bar, phase, abort_flag);
   phase ^= 1;
   return ok;
 }
@@ -154,6 +163,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     if (abort_flag && *abort_flag) return false;
     if (globaltimer_ns() - t0 > EC_WAIT_NS) return false;
   }
+}
+// warp-uniform mbar_wait_cluster (see mbar_wait_warp)
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity,
+                                                       volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, abort_flag));
 }
 // every thread of every CTA of the cluster (start: partners' barriers are
 // initialised before any remote access; end: no remote access is in flight

@@ -38,9 +38,26 @@ struct LlamaLayerW {
   bf16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
 };
 
+// EmbeddingGemma layer (gemma.lisp:149-212)
+struct GemmaLayerW {
+  float *in_ln = nullptr, *post_ln = nullptr, *pre_ff_ln = nullptr, *post_ff_ln = nullptr;
+  float *q_norm = nullptr, *k_norm = nullptr, *ple_norm = nullptr;
+  bf16 *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
+  bf16 *wpp = nullptr;        // this layer's rows of the per-layer projection [P, H]
+  bf16 *wple_gate = nullptr;  // [P, H]
+  bf16 *wple_proj = nullptr;  // [H, P]
+  float scalar = 1.f;
+  int rope = 0;               // 0: theta 1e4 table, 1: theta 1e6 (full_attention)
+};
+
 struct ModelW {
   int family = 0;  // EC_FAMILY_*
   int H = 0, layers = 0, heads = 0, kv_heads = 0, hd = 0, F = 0;
+  int out_dim = 0;            // embedding width (H except Gemma's projection)
+  int ple_dim = 0;            // Gemma per-layer-input width
+  std::vector<GemmaLayerW> gl;
+  float *ple_norm = nullptr, *w_out = nullptr;   // Gemma [P], [out_dim, H] fp32
+  float *cos2_t = nullptr, *sin2_t = nullptr;    // Gemma theta-1e6 RoPE tables
   int pooling = 0;  // 0 first token, 1 mean, 2 last token
   int pos_offset = 0, vocab = 0, max_pos = 0;
   double eps = 1e-6, theta = 10000.0;
@@ -111,6 +128,7 @@ struct Global {
   int max_tokens = 262144;
   // profiling of the forward (ecdbg_profile)
   bool profile = false;
+  bool sync_each = false;  // EC_SYNC_EACH_LAUNCH: wait for and report every forward launch
   ProfAcc prof[3];
   long long launches = 0;
   // multi-process communicator
@@ -144,6 +162,9 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
 // profiling helpers: bracket one launch with events (no-op unless profiling)
 int prof_begin(Device& d);
 void prof_end(Device& d, int cls, double flops, double bytes, int e0);
+// With EC_SYNC_EACH_LAUNCH set: wait (at most 60 s) for the launch just
+// enqueued and print its name, status and duration to stderr.
+void trace_launch(Device& d, const char* what);
 // fold finished events of d into G().prof (call after synchronising d.stream)
 void prof_collect(Device& d);
 

@@ -20,7 +20,7 @@ HEADER = os.path.join(REPO, "include", "embedcuda.h")
 EC_OK, EC_EINVAL, EC_ESTATE, EC_ECUDA, EC_ENOMEM, EC_ETIMEOUT, EC_ENCCL, EC_EUNSUPPORTED = \
     0, -1, -2, -3, -4, -5, -6, -7
 EC_F32, EC_BF16, EC_F16 = 0, 1, 2
-FAMILIES = {1: "bert", 2: "mpnet", 3: "llama"}
+FAMILIES = {1: "bert", 2: "mpnet", 3: "llama", 4: "gemma"}
 
 _lock = threading.Lock()
 _lib = None

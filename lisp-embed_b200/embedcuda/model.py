@@ -19,7 +19,7 @@ _state = {"family": None, "path": None, "dim": 0}
 
 def load_model(path, devices=None):
     """Load any supported model directory; returns the family keyword
-    ('bert' | 'mpnet' | 'llama')."""
+    ('bert' | 'mpnet' | 'llama' | 'gemma')."""
     _lib.init(devices)
     d = path if os.path.isdir(path) else os.path.dirname(path)
     with open(os.path.join(d, "config.json")) as f:

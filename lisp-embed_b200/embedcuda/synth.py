@@ -58,14 +58,25 @@ MPNET_BASE = ModelShape("mpnet-base", "mpnet", 768, 12, 12, 3072, 30527, 514, "F
 QWEN3_06B = ModelShape("qwen3-0.6b", "qwen3", 1024, 28, 16, 3072, 151669, 40960, "BF16",
                        "last", kv_heads=8, head_dim=128, rope_theta=1000000.0, rms_eps=1e-6)
 
-SHAPES = {s.name: s for s in (MINILM, BERT_BASE, MPNET_BASE, QWEN3_06B)}
-SEEDS = {"minilm-l6": 0, "bert-base": 1, "mpnet-base": 2, "qwen3-0.6b": 3}
+# EmbeddingGemma (Gemma-3n text) shape at gemma.lisp's own defaults (hidden
+# 512, 24 layers, 4 heads, FFN 2048, PLE 512, output 768; head dim 128 from
+# q_norm, one kv head); full_attention every fourth layer.
+GEMMA_EMB = ModelShape("embeddinggemma", "embedding_gemma2", 512, 24, 4, 2048, 32768, 2048, "F32",
+                       "mean", kv_heads=1, head_dim=128, rms_eps=1e-6,
+                       extra={"ple_dim": 512, "out_dim": 768,
+                              "layer_types": ["full_attention" if i % 4 == 3 else "sliding_attention"
+                                              for i in range(24)]})
+
+SHAPES = {s.name: s for s in (MINILM, BERT_BASE, MPNET_BASE, QWEN3_06B, GEMMA_EMB)}
+SEEDS = {"minilm-l6": 0, "bert-base": 1, "mpnet-base": 2, "qwen3-0.6b": 3, "embeddinggemma": 4}
 
 
 def with_layers(shape: ModelShape, layers: int, vocab: int | None = None) -> ModelShape:
     """Same widths, fewer layers (and optionally a smaller vocab) for tests."""
     d = dict(shape.__dict__)
     d["layers"] = layers
+    if "layer_types" in d.get("extra", {}):
+        d["extra"] = dict(d["extra"], layer_types=d["extra"]["layer_types"][:layers])
     d["name"] = f"{shape.name}-{layers}l"
     if vocab is not None:
         d["vocab"] = vocab
@@ -139,6 +150,34 @@ def tensor_specs(s: ModelShape):
                     (p + "mlp.up_proj.weight", (F, H), "normal"),
                     (p + "mlp.down_proj.weight", (H, F), "normal")]
         out += [("norm.weight", (H,), "ones")]
+    elif s.model_type == "embedding_gemma2":
+        hd, kv = s.head_dim, s.kv_heads
+        P, O = s.extra["ple_dim"], s.extra["out_dim"]
+        pre = "language_model."
+        out += [(pre + "embed_tokens.weight", (s.vocab, H), "normal"),
+                (pre + "ple.per_layer_model_projection.weight", (s.layers * P, H), "normal"),
+                (pre + "ple.per_layer_projection_norm.weight", (P,), "ones"),
+                (pre + "norm.weight", (H,), "ones"),
+                (pre + "embedding_projection.weight", (O, H), "normal")]
+        for li in range(s.layers):
+            p = f"{pre}layers.{li}."
+            out += [(p + "input_layernorm.weight", (H,), "ones"),
+                    (p + "post_attention_layernorm.weight", (H,), "ones"),
+                    (p + "pre_feedforward_layernorm.weight", (H,), "ones"),
+                    (p + "post_feedforward_layernorm.weight", (H,), "ones"),
+                    (p + "self_attn.q_proj.weight", (s.heads * hd, H), "normal"),
+                    (p + "self_attn.k_proj.weight", (kv * hd, H), "normal"),
+                    (p + "self_attn.v_proj.weight", (kv * hd, H), "normal"),
+                    (p + "self_attn.o_proj.weight", (H, s.heads * hd), "normal"),
+                    (p + "self_attn.q_norm.weight", (hd,), "ones"),
+                    (p + "self_attn.k_norm.weight", (hd,), "ones"),
+                    (p + "mlp.gate_proj.weight", (F, H), "normal"),
+                    (p + "mlp.up_proj.weight", (F, H), "normal"),
+                    (p + "mlp.down_proj.weight", (H, F), "normal"),
+                    (p + "ple_block.per_layer_input_gate.weight", (P, H), "normal"),
+                    (p + "ple_block.per_layer_projection.weight", (H, P), "normal"),
+                    (p + "ple_block.post_per_layer_input_norm.weight", (H,), "ones"),
+                    (p + "layer_scalar", (1,), "scalar")]
     else:
         raise ValueError(f"unknown model_type {s.model_type}")
     return out
@@ -164,6 +203,8 @@ def make_weights(s: ModelShape, seed: int):
             a = rng.normal(0.0, 0.02, size=shape).astype(np.float32)
         elif init == "ones":
             a = np.ones(shape, np.float32)
+        elif init == "scalar":  # a layer scalar near 1
+            a = np.full(shape, 0.5 + rng.random(), np.float32)
         else:
             a = np.zeros(shape, np.float32)
         if s.dtype == "BF16":
@@ -207,6 +248,16 @@ def config_json(s: ModelShape) -> dict:
             cfg["relative_attention_num_buckets"] = 32
         return cfg
     hd = s.head_dim or s.hidden // s.heads
+    if s.model_type == "embedding_gemma2":
+        return {"model_type": "embedding_gemma2",
+                "text_config": {"model_type": "embedding_gemma2_text", "hidden_size": s.hidden,
+                                "num_hidden_layers": s.layers, "num_attention_heads": s.heads,
+                                "num_key_value_heads": s.kv_heads, "head_dim": hd,
+                                "intermediate_size": s.inter, "vocab_size": s.vocab,
+                                "hidden_size_per_layer_input": s.extra["ple_dim"],
+                                "embedding_dim": s.extra["out_dim"], "rms_norm_eps": s.rms_eps,
+                                "layer_types": s.extra["layer_types"],
+                                "hidden_activation": "gelu_pytorch_tanh"}}
     return {"model_type": s.model_type, "hidden_size": s.hidden,
             "num_hidden_layers": s.layers, "num_attention_heads": s.heads,
             "num_key_value_heads": s.kv_heads or s.heads, "head_dim": hd,
@@ -249,6 +300,7 @@ def make_inputs(workload: str, nseq: int, seed: int, vocab: int | None = None):
     U{16..256} (minilm) or floor(exp(U[ln 32, ln 512])) (bert-base).
     mpnet: <s>=0 + U[1000, vocab-1] + </s>=2, total length U{64..384}.
     qwen3: body U{128..512} of U[0, 151643) then EOS 151643.
+    gemma: <bos>=2 + U[1000, vocab-1] + <eos>=1, total length U{16..512}.
     """
     rng = np.random.default_rng((seed, 1))
     if workload.startswith("minilm"):
@@ -264,6 +316,9 @@ def make_inputs(workload: str, nseq: int, seed: int, vocab: int | None = None):
         body = rng.integers(128, 512, size=nseq, endpoint=True)
         lens = body + 1
         lo, hi, pre, post = 0, min(151642, (vocab or 151669) - 1), [], [151643]
+    elif "gemma" in workload:
+        lens = rng.integers(16, 512, size=nseq, endpoint=True)
+        lo, hi, pre, post = 1000, (vocab or 32768) - 1, [2], [1]
     else:
         raise ValueError(workload)
     lens = np.asarray(lens, np.int64)
@@ -284,6 +339,8 @@ def make_short_inputs(workload: str, lengths, seed: int, vocab: int):
         pre, post, lo, hi = [], [min(151643, vocab - 1)], 0, min(151642, vocab - 2)
     elif workload.startswith("mpnet"):
         pre, post, lo, hi = [0], [2], min(1000, vocab - 2), vocab - 1
+    elif "gemma" in workload:
+        pre, post, lo, hi = [2], [1], min(1000, vocab - 2), vocab - 1
     else:
         pre, post, lo, hi = [101], [102], min(1000, vocab - 2), vocab - 1
     offs = [0]

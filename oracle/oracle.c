@@ -370,6 +370,170 @@ int or_llama_embed(const or_llama *m, const int32_t *ids, int seq, float *out) {
   return 0;
 }
 
+/* ---- gemma.lisp ------------------------------------------------------------ */
+
+/* gemma::rmsnorm-noscale (gemma.lisp:74-83): the v-norm, no learned scale. */
+static void rmsnorm_noscale(float *x, int n, double eps) {
+  double ss = 0.0;
+  for (int i = 0; i < n; ++i) ss += (double)(x[i] * x[i]);
+  float inv = (float)(1.0 / sqrt(ss / (double)n + eps));
+  for (int i = 0; i < n; ++i) x[i] = x[i] * inv;
+}
+
+/* gemma::gelu-tanh (gemma.lisp:85-89): gelu_pytorch_tanh evaluated in double. */
+static float gelu_tanh(float x) {
+  double xd = (double)x;
+  double c = 0.7978845608028654 * (xd + ((0.044715 * xd) * xd) * xd);
+  return (float)((0.5 * xd) * (1.0 + tanh(c)));
+}
+
+/* gemma::embed + layer-forward (gemma.lisp:216-376). */
+int or_gemma_embed(const or_gemma *m, const int32_t *ids, int seq, float *out) {
+  const int H = m->hidden, heads = m->heads, F = m->inter, P = m->ple_dim, NL = m->layers;
+  if (seq > m->max_pos) return -2;
+  int maxq = 0, maxkv = 0, maxhalf = 0;
+  for (int li = 0; li < NL; ++li) {
+    const int hd = m->L[li].head_dim;
+    if (heads * hd > maxq) maxq = heads * hd;
+    if (m->L[li].kv_heads * hd > maxkv) maxkv = m->L[li].kv_heads * hd;
+    if (hd / 2 > maxhalf) maxhalf = hd / 2;
+  }
+  int tw = H > F ? H : F;
+  if (P > tw) tw = P;
+  int ow = F > P ? F : P;
+  float *h = malloc((size_t)seq * H * sizeof(float));
+  float *ple = malloc((size_t)seq * NL * P * sizeof(float));
+  float *qb = malloc((size_t)seq * maxq * sizeof(float));
+  float *kb = malloc((size_t)seq * maxkv * sizeof(float));
+  float *vb = malloc((size_t)seq * maxkv * sizeof(float));
+  float *ctx = malloc((size_t)seq * maxq * sizeof(float));
+  float *scores = malloc((size_t)seq * sizeof(float));
+  float *tmp = malloc((size_t)seq * tw * sizeof(float));
+  float *o = malloc((size_t)seq * ow * sizeof(float));
+  float *normed = malloc((size_t)seq * H * sizeof(float));
+  float *cs = malloc((size_t)m->max_pos * maxhalf * sizeof(float));
+  float *sn = malloc((size_t)m->max_pos * maxhalf * sizeof(float));
+  float *pooled = malloc((size_t)H * sizeof(float));
+  int rc = 0;
+  if (!h || !ple || !qb || !kb || !vb || !ctx || !scores || !tmp || !o || !normed || !cs || !sn ||
+      !pooled) {
+    rc = -1;
+    goto done;
+  }
+  /* token embeddings scaled by sqrt(hidden) (gemma.lisp:326-330) */
+  const float scale = ssqrt((float)H);
+  for (int t = 0; t < seq; ++t)
+    for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = scale * m->w_embed[(size_t)ids[t] * H + i];
+  /* per-layer embeddings: projection, * 1/sqrt(hidden), RMSNorm per layer
+   * slice (gemma.lisp:331-343) */
+  for (int t = 0; t < seq; ++t)
+    linear_nb(h + (size_t)t * H, m->w_ple_proj, ple + (size_t)t * NL * P, H, NL * P);
+  {
+    const float inv = 1.0f / ssqrt((float)H);
+    for (size_t i = 0; i < (size_t)seq * NL * P; ++i) ple[i] = ple[i] * inv;
+    for (int t = 0; t < seq; ++t)
+      for (int li = 0; li < NL; ++li)
+        rmsnorm(ple + (size_t)t * NL * P + (size_t)li * P, P, m->w_ple_norm, m->eps);
+  }
+  for (int li = 0; li < NL; ++li) {
+    const or_gemma_layer *lw = &m->L[li];
+    const int hd = lw->head_dim, kv = lw->kv_heads, half = hd / 2;
+    const int qd = heads * hd, kvd = kv * hd, group = heads / kv;
+    /* gemma::init-rope (gemma.lisp:91-103) with this layer's theta */
+    for (int p = 0; p < m->max_pos; ++p)
+      for (int i = 0; i < half; ++i) {
+        double freq = 1.0 / pow(lw->rope_theta, (2.0 * i) / (double)hd);
+        double ang = p * freq;
+        cs[(size_t)p * half + i] = (float)cos(ang);
+        sn[(size_t)p * half + i] = (float)sin(ang);
+      }
+    /* attention sub-block (gemma.lisp:228-274) */
+    for (int t = 0; t < seq; ++t) {
+      memcpy(normed + (size_t)t * H, h + (size_t)t * H, H * sizeof(float));
+      rmsnorm(normed + (size_t)t * H, H, lw->in_ln, m->eps);
+    }
+    for (int t = 0; t < seq; ++t) {
+      linear_nb(normed + (size_t)t * H, lw->q_w, qb + (size_t)t * qd, H, qd);
+      linear_nb(normed + (size_t)t * H, lw->k_w, kb + (size_t)t * kvd, H, kvd);
+      linear_nb(normed + (size_t)t * H, lw->v_w, vb + (size_t)t * kvd, H, kvd);
+    }
+    for (int t = 0; t < seq; ++t) {
+      for (int hh = 0; hh < heads; ++hh) rmsnorm(qb + (size_t)t * qd + hh * hd, hd, lw->q_norm, m->eps);
+      for (int hh = 0; hh < kv; ++hh) {
+        rmsnorm(kb + (size_t)t * kvd + hh * hd, hd, lw->k_norm, m->eps);
+        rmsnorm_noscale(vb + (size_t)t * kvd + hh * hd, hd, m->eps);
+      }
+      rope(qb + (size_t)t * qd, t, heads, hd, cs, sn);
+      rope(kb + (size_t)t * kvd, t, kv, hd, cs, sn);
+    }
+    /* bidirectional attention, scale 1.0 (gemma.lisp:250-265) */
+    for (int hh = 0; hh < heads; ++hh) {
+      int kvh = hh / group;
+      for (int t1 = 0; t1 < seq; ++t1) {
+        for (int t2 = 0; t2 < seq; ++t2)
+          scores[t2] = or_dot(qb + (size_t)t1 * qd + hh * hd, kb + (size_t)t2 * kvd + kvh * hd, hd);
+        softmax(scores, seq);
+        for (int i = 0; i < hd; ++i) {
+          float acc = 0.0f;
+          for (int t2 = 0; t2 < seq; ++t2)
+            acc = acc + scores[t2] * vb[(size_t)t2 * kvd + kvh * hd + i];
+          ctx[(size_t)t1 * qd + hh * hd + i] = acc;
+        }
+      }
+    }
+    for (int t = 0; t < seq; ++t) {
+      float *tr = tmp + (size_t)t * H;
+      linear_nb(ctx + (size_t)t * qd, lw->o_w, tr, qd, H);
+      rmsnorm(tr, H, lw->post_ln, m->eps);
+      for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = h[(size_t)t * H + i] + tr[i];
+    }
+    /* FFN sub-block: GELU-tanh gated MLP between pre/post norms (:275-287) */
+    for (int t = 0; t < seq; ++t) {
+      memcpy(normed + (size_t)t * H, h + (size_t)t * H, H * sizeof(float));
+      rmsnorm(normed + (size_t)t * H, H, lw->pre_ff_ln, m->eps);
+    }
+    for (int t = 0; t < seq; ++t) {
+      float *orow = o + (size_t)t * ow, *trow = tmp + (size_t)t * tw;
+      linear_nb(normed + (size_t)t * H, lw->gate, orow, H, F);
+      linear_nb(normed + (size_t)t * H, lw->up, trow, H, F);
+      for (int i = 0; i < F; ++i) orow[i] = gelu_tanh(orow[i]) * trow[i];
+      linear_nb(orow, lw->down, trow, F, H);
+      rmsnorm(trow, H, lw->post_ff_ln, m->eps);
+      for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = h[(size_t)t * H + i] + trow[i];
+    }
+    /* PLE sub-block: gate(h) -> GELU-tanh * ple -> proj -> norm -> residual
+     * (:288-298) */
+    for (int t = 0; t < seq; ++t) {
+      float *orow = o + (size_t)t * ow, *trow = tmp + (size_t)t * tw;
+      const float *prow = ple + (size_t)t * NL * P + (size_t)li * P;
+      linear_nb(h + (size_t)t * H, lw->ple_gate, orow, H, P);
+      for (int i = 0; i < P; ++i) orow[i] = gelu_tanh(orow[i]) * prow[i];
+      linear_nb(orow, lw->ple_proj, trow, P, H);
+      rmsnorm(trow, H, lw->ple_norm, m->eps);
+      for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = h[(size_t)t * H + i] + trow[i];
+    }
+    /* layer scalar (:300-302) */
+    for (size_t i = 0; i < (size_t)seq * H; ++i) h[i] = h[i] * lw->scalar;
+  }
+  /* final norm, mean pool, projection, L2 (:359-376) */
+  for (int t = 0; t < seq; ++t) rmsnorm(h + (size_t)t * H, H, m->w_norm, m->eps);
+  for (int i = 0; i < H; ++i) pooled[i] = 0.0f;
+  for (int t = 0; t < seq; ++t)
+    for (int i = 0; i < H; ++i) pooled[i] = pooled[i] + h[(size_t)t * H + i];
+  for (int i = 0; i < H; ++i) pooled[i] = pooled[i] / (float)seq;
+  linear_nb(pooled, m->w_out, out, H, m->out_dim);
+  {
+    float norm = 0.0f;
+    for (int i = 0; i < m->out_dim; ++i) norm = norm + out[i] * out[i];
+    norm = ssqrt(norm);
+    for (int i = 0; i < m->out_dim; ++i) out[i] = out[i] / norm;
+  }
+done:
+  free(h); free(ple); free(qb); free(kb); free(vb); free(ctx); free(scores); free(tmp);
+  free(o); free(normed); free(cs); free(sn); free(pooled);
+  return rc;
+}
+
 /* ---- embed.lisp batch driver ---------------------------------------------- */
 typedef struct {
   int kind;
@@ -382,8 +546,9 @@ typedef struct {
 
 static void *embed_thread(void *arg) {
   embed_job *j = (embed_job *)arg;
-  j->rc = j->kind == 0 ? or_bert_embed((const or_bert *)j->model, j->ids, j->seq, j->out)
-                       : or_llama_embed((const or_llama *)j->model, j->ids, j->seq, j->out);
+  j->rc = j->kind == 0   ? or_bert_embed((const or_bert *)j->model, j->ids, j->seq, j->out)
+          : j->kind == 1 ? or_llama_embed((const or_llama *)j->model, j->ids, j->seq, j->out)
+                         : or_gemma_embed((const or_gemma *)j->model, j->ids, j->seq, j->out);
   return NULL;
 }
 

@@ -70,8 +70,30 @@ typedef struct {
 
 int or_llama_embed(const or_llama *m, const int32_t *ids, int seq, float *out);
 
+/* ---- EmbeddingGemma / Gemma-3n text (gemma.lisp) ------------------------- */
+typedef struct {
+  int head_dim, kv_heads;
+  double rope_theta;   /* 1e6 for full_attention layers, 1e4 otherwise */
+  const float *in_ln, *post_ln, *pre_ff_ln, *post_ff_ln;
+  const float *q_w, *k_w, *v_w, *o_w, *q_norm, *k_norm;
+  const float *gate, *up, *down;
+  const float *ple_gate, *ple_proj, *ple_norm;
+  float scalar;
+} or_gemma_layer;
+
+typedef struct {
+  int hidden, layers, heads, inter, ple_dim, out_dim;
+  int max_pos;         /* gemma::*max-pos* (2048) */
+  double eps;
+  const float *w_embed, *w_ple_proj, *w_ple_norm, *w_norm, *w_out;
+  const or_gemma_layer *L;
+} or_gemma;
+
+int or_gemma_embed(const or_gemma *m, const int32_t *ids, int seq, float *out);
+
 /* Batch driver mirroring embed.lisp:88-105: batches of `threads` sequences,
- * one thread per sequence, joined in input order.  kind 0 = bert, 1 = llama. */
+ * one thread per sequence, joined in input order.  kind 0 = bert, 1 = llama,
+ * 2 = gemma. */
 int or_embed_batch(int kind, const void *model, const int32_t *ids,
                    const int64_t *offsets, int nseq, int dim, float *out,
                    int threads);

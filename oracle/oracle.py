@@ -43,6 +43,7 @@ def lib():
         L.or_top_k_ivf.restype = C.c_int
         L.or_top_k_brute.restype = C.c_int
         L.or_mpnet_bucket.restype = C.c_int
+        L.or_gemma_embed.restype = C.c_int
         _lib = L
     return _lib
 
@@ -70,6 +71,20 @@ class Llama(C.Structure):
                 ("kv_heads", C.c_int), ("head_dim", C.c_int), ("inter", C.c_int),
                 ("pooling", C.c_int), ("max_pos", C.c_int), ("rope_theta", C.c_double),
                 ("eps", C.c_double), ("w_embed", F), ("w_norm", F), ("L", C.POINTER(LlamaLayer))]
+
+
+class GemmaLayer(C.Structure):
+    _fields_ = [("head_dim", C.c_int), ("kv_heads", C.c_int), ("rope_theta", C.c_double)] + \
+        [(n, F) for n in ("in_ln", "post_ln", "pre_ff_ln", "post_ff_ln", "q_w", "k_w", "v_w", "o_w",
+                          "q_norm", "k_norm", "gate", "up", "down", "ple_gate", "ple_proj",
+                          "ple_norm")] + [("scalar", C.c_float)]
+
+
+class Gemma(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("inter", C.c_int),
+                ("ple_dim", C.c_int), ("out_dim", C.c_int), ("max_pos", C.c_int),
+                ("eps", C.c_double), ("w_embed", F), ("w_ple_proj", F), ("w_ple_norm", F),
+                ("w_norm", F), ("w_out", F), ("L", C.POINTER(GemmaLayer))]
 
 
 def _fp(a):
@@ -201,6 +216,54 @@ class OracleModel:
             self._keep.append(layers)
             self.m = m
             self.dim = H
+        elif mt in ("embedding_gemma2", "embedding_gemma2_text"):  # model.lisp:41
+            # gemma:load-model (gemma.lisp:140-212): text_config fields, weights
+            # under language_model., per-layer head dim from q_norm and kv heads
+            # from k_proj, RoPE theta 1e6 on full_attention layers
+            self.kind = 2
+            self.family = "gemma"
+            t = tc or cfg
+            m = Gemma()
+            m.hidden, m.layers = t["hidden_size"], t["num_hidden_layers"]
+            m.heads, m.inter = t["num_attention_heads"], t["intermediate_size"]
+            m.ple_dim = t.get("hidden_size_per_layer_input") or m.hidden
+            m.out_dim = t.get("embedding_dim") or 768
+            m.max_pos = 2048
+            m.eps = float(t.get("rms_norm_eps") or 1e-6)
+            g = self._get
+            pre = "language_model."
+            m.w_embed = g(pre + "embed_tokens.weight")
+            m.w_ple_proj = g(pre + "ple.per_layer_model_projection.weight")
+            m.w_ple_norm = g(pre + "ple.per_layer_projection_norm.weight")
+            m.w_norm = g(pre + "norm.weight")
+            m.w_out = g(pre + "embedding_projection.weight")
+            types = t.get("layer_types") or []
+            layers = (GemmaLayer * m.layers)()
+            for li in range(m.layers):
+                p = f"{pre}layers.{li}."
+                Lw = layers[li]
+                hd = self.w[p + "self_attn.q_norm.weight"].shape[0]
+                Lw.head_dim = hd
+                Lw.kv_heads = self.w[p + "self_attn.k_proj.weight"].shape[0] // hd
+                Lw.rope_theta = 1e6 if li < len(types) and types[li] == "full_attention" else 1e4
+                for field, nm in dict(
+                        in_ln="input_layernorm.weight", post_ln="post_attention_layernorm.weight",
+                        pre_ff_ln="pre_feedforward_layernorm.weight",
+                        post_ff_ln="post_feedforward_layernorm.weight",
+                        q_w="self_attn.q_proj.weight", k_w="self_attn.k_proj.weight",
+                        v_w="self_attn.v_proj.weight", o_w="self_attn.o_proj.weight",
+                        q_norm="self_attn.q_norm.weight", k_norm="self_attn.k_norm.weight",
+                        gate="mlp.gate_proj.weight", up="mlp.up_proj.weight",
+                        down="mlp.down_proj.weight",
+                        ple_gate="ple_block.per_layer_input_gate.weight",
+                        ple_proj="ple_block.per_layer_projection.weight",
+                        ple_norm="ple_block.post_per_layer_input_norm.weight").items():
+                    setattr(Lw, field, g(p + nm))
+                Lw.scalar = float(self.w[p + "layer_scalar"].reshape(-1)[0])
+            m.L = layers
+            self._keep.append(layers)
+            self.m = m
+            self.dim = m.out_dim
         else:
             raise ValueError(f"unsupported model_type {mt}")
 
@@ -217,7 +280,7 @@ class OracleModel:
     def embed(self, ids):
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.zeros(self.dim, np.float32)
-        fn = lib().or_bert_embed if self.kind == 0 else lib().or_llama_embed
+        fn = (lib().or_bert_embed, lib().or_llama_embed, lib().or_gemma_embed)[self.kind]
         rc = fn(C.byref(self.m), ids.ctypes.data_as(C.POINTER(C.c_int32)), C.c_int(ids.size),
                 _fp(out))
         if rc:

@@ -78,3 +78,15 @@ def test_errors(synth_root, ec):
         model.embed(np.arange(600, dtype=np.int32) + 1000)  # past 512 positions
     with pytest.raises(_lib.EcError):
         model.embed_batch(np.zeros(0, np.int32), np.array([0, 0], np.int64))  # empty sequence
+
+
+def test_gemma(synth_root, ec):
+    """EmbeddingGemma: one sliding (theta 1e4) and one full-attention (theta
+    1e6) layer, PLE, per-head q/k/v norms, mean pool + 512 -> 768 projection."""
+    import dataclasses
+    s = synth.with_layers(synth.GEMMA_EMB, 2, vocab=4096)
+    s = dataclasses.replace(s, name=s.name + "-sf", extra=dict(
+        s.extra, layer_types=["sliding_attention", "full_attention"]))
+    fam, _ = _check(s, 4, [1, 2, 40, 129, 300], synth_root, ec, "gemma")
+    assert fam == "gemma"
+    assert model.dim() == 768

@@ -132,3 +132,86 @@ def test_top_k_ivf_merge_order():
     assert list(ids) == [3, 0, 1] and list(sc) == [1.0, 1.0, 1.0]
     ids, sc = oracle.top_k_brute(x, np.array([1, 0], np.float32), 3)
     assert list(ids) == [0, 1, 3]
+
+
+def _gemma_numpy(w, t, ids):
+    """float64 numpy restatement of gemma::embed (gemma.lisp:306-380) used to
+    check the C oracle's Gemma path; same step order, wider arithmetic."""
+    H, P, NL = t["hidden_size"], t["hidden_size_per_layer_input"], t["num_hidden_layers"]
+    eps = t["rms_norm_eps"]
+    pre = "language_model."
+    W = {k: np.asarray(v, np.float64) for k, v in w.items()}
+
+    def rms(x, g=None):
+        y = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+        return y if g is None else y * g
+
+    def gelu(x):
+        return 0.5 * x * (1 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+    S = ids.size
+    h = np.sqrt(np.float32(H)).astype(np.float64) * W[pre + "embed_tokens.weight"][ids]
+    ple = (h @ W[pre + "ple.per_layer_model_projection.weight"].T) / np.sqrt(H)
+    ple = rms(ple.reshape(S, NL, P), W[pre + "ple.per_layer_projection_norm.weight"])
+    pos = np.arange(S)[:, None]
+    for li in range(NL):
+        p = f"{pre}layers.{li}."
+        hd = W[p + "self_attn.q_norm.weight"].size
+        theta = 1e6 if t["layer_types"][li] == "full_attention" else 1e4
+        ang = pos * (1.0 / theta ** (2.0 * np.arange(hd // 2) / hd))
+        cos, sin = np.cos(ang)[:, None], np.sin(ang)[:, None]
+
+        def rope(x):
+            a, b = x[..., :hd // 2], x[..., hd // 2:]
+            return np.concatenate([a * cos - b * sin, a * sin + b * cos], -1)
+
+        x = rms(h, W[p + "input_layernorm.weight"])
+        q = (x @ W[p + "self_attn.q_proj.weight"].T).reshape(S, -1, hd)
+        k = (x @ W[p + "self_attn.k_proj.weight"].T).reshape(S, -1, hd)
+        v = (x @ W[p + "self_attn.v_proj.weight"].T).reshape(S, -1, hd)
+        q = rope(rms(q, W[p + "self_attn.q_norm.weight"]))
+        k = rope(rms(k, W[p + "self_attn.k_norm.weight"]))
+        v = rms(v)
+        grp = q.shape[1] // k.shape[1]
+        k, v = np.repeat(k, grp, 1), np.repeat(v, grp, 1)
+        sc = np.einsum("shd,thd->hst", q, k)            # scale 1.0, bidirectional
+        sc = np.exp(sc - sc.max(-1, keepdims=True))
+        sc /= sc.sum(-1, keepdims=True)
+        ctx = np.einsum("hst,thd->shd", sc, v).reshape(S, -1)
+        h = h + rms(ctx @ W[p + "self_attn.o_proj.weight"].T, W[p + "post_attention_layernorm.weight"])
+        x = rms(h, W[p + "pre_feedforward_layernorm.weight"])
+        f = gelu(x @ W[p + "mlp.gate_proj.weight"].T) * (x @ W[p + "mlp.up_proj.weight"].T)
+        h = h + rms(f @ W[p + "mlp.down_proj.weight"].T, W[p + "post_feedforward_layernorm.weight"])
+        g = gelu(h @ W[p + "ple_block.per_layer_input_gate.weight"].T) * ple[:, li]
+        h = h + rms(g @ W[p + "ple_block.per_layer_projection.weight"].T,
+                    W[p + "ple_block.post_per_layer_input_norm.weight"])
+        h = h * W[p + "layer_scalar"].reshape(-1)[0]
+    h = rms(h, W[pre + "norm.weight"])
+    v = W[pre + "embedding_projection.weight"] @ h.mean(0)
+    return v / np.linalg.norm(v)
+
+
+def test_gemma_oracle_matches_float64_restatement(synth_root):
+    """The C oracle's gemma::embed (single precision, gemma.lisp's order of
+    operations) against a float64 numpy restatement on the same weights:
+    two layers, one sliding (theta 1e4) and one full-attention (theta 1e6)."""
+    import dataclasses
+    import json
+    s = synth.with_layers(synth.GEMMA_EMB, 2, vocab=4096)
+    s = dataclasses.replace(s, name=s.name + "-sf", extra=dict(
+        s.extra, layer_types=["sliding_attention", "full_attention"]))
+    d = synth.build_model_dir(s, 4, synth_root)
+    om = oracle.OracleModel(d)
+    with open(os.path.join(d, "config.json")) as f:
+        t = json.load(f)["text_config"]
+    ids, offs = synth.make_short_inputs("gemma", [1, 2, 37, 130], 4, s.vocab)
+    got = om.embed_batch(ids, offs, threads=4)
+    assert got.shape == (4, 768)
+    for i in range(4):
+        ref = _gemma_numpy(om.w, t, ids[offs[i]:offs[i + 1]])
+        cos = float(np.dot(got[i], ref) / np.linalg.norm(got[i]))
+        assert cos > 0.99999, (i, cos)
+        assert np.abs(got[i] - ref).max() < 1e-4
+    # one sequence alone equals the same sequence inside the batch
+    one = om.embed(ids[offs[2]:offs[3]])
+    assert np.array_equal(one, got[2])
