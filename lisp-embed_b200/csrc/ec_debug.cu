@@ -56,7 +56,7 @@ int ecdbg_gemm(const void* A, const void* W, int M, int N, int K, const float* b
   g.resid = resid;
   g.ldr = N;
   g.out = out;
-  g.ldo = epi == 3 ? N / 2 : N;
+  g.ldo = (epi == 3 || epi == 6) ? N / 2 : N;
   g.epi = epi;
   g.bn = bn;
   g.status = d.status;

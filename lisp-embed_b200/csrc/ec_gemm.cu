@@ -117,6 +117,11 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.num_tiles = ((g.M + kGemmBM * CG - 1) / (kGemmBM * CG)) * a.n_tiles_n;
   a.status = g.status;
   a.qk = QkRopeEpi{};
+  if constexpr (EPI == kEpiF32Resid || EPI == kEpiBf16GeluTanhMul) {
+    // the epilogue reads 16-byte pieces of the residual / multiplier rows
+    if (!g.resid || g.ldr % 4 || reinterpret_cast<uintptr_t>(g.resid) % 16)
+      return cudaErrorInvalidValue;
+  }
   if constexpr (EPI == kEpiBf16QkRope) {
     if (!g.qk) return cudaErrorInvalidValue;
     a.qk = *g.qk;
@@ -145,6 +150,9 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
     case kEpiBf16GeluTanhGate:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16GeluTanhGate>(g, st, num_sms);
       return cudaErrorInvalidValue;
+    case kEpiBf16GeluTanhMul:
+      if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16GeluTanhMul>(g, st, num_sms);
+      return cudaErrorInvalidValue;
     case kEpiBf16Swiglu:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
       return cudaErrorInvalidValue;
@@ -153,7 +161,7 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
 }
 
 int gemm_pick_bn(int M, int N, int epi, int num_sms) {
-  if (epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate)
+  if (epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate || epi == kEpiBf16GeluTanhMul)
     return N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
   if (epi == kEpiBf16QkRope) return N % 256 == 0 ? 256 : 0;
   const int mt = (M + kGemmBM - 1) / kGemmBM;

@@ -40,6 +40,8 @@ enum GemmEpi : int {
                        // q/k heads (llama.lisp:244-253, 137-151), head dim 128
   kEpiBf16GeluTanhGate = 6,  // out bf16 = gelu_tanh(gate) * up, N/2 wide
                              // (gemma.lisp:277-283), SwiGLU's tile layout
+  kEpiBf16GeluTanhMul = 7,   // out bf16 = gelu_tanh(acc) * resid, resid fp32
+                             // [M, ldr] (the PLE gate, gemma.lisp:290-293)
 };
 
 // per-head q/k RMSNorm + rotate-half RoPE applied in the QKV epilogue
@@ -51,12 +53,14 @@ struct QkRopeEpi {
   const int* pos;       // [M] position of each row
   const float* cos_t;   // [max_pos, 64]
   const float* sin_t;
+  int v_heads = 0;      // v heads after the k heads get the unweighted
+  int v_norm = 0;       // RMSNorm (gemma.lisp:244) when v_norm, no RoPE
 };
 
 struct GemmArgs {
   int M, N, K;
   const float* bias;   // [N] or nullptr
-  const float* resid;  // [M, ldr] fp32 (kEpiF32Resid); may alias out
+  const float* resid;  // [M, ldr] fp32 (kEpiF32Resid, kEpiBf16GeluTanhMul); may alias out
   int ldr;
   void* out;           // bf16 or fp32, row stride ldo elements
   int ldo;
@@ -81,7 +85,8 @@ struct GemmCfg {
   static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32;
   // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
   // rows of 64 B (64B swizzle); two per epilogue warp
-  static constexpr uint32_t CHUNK_BYTES = OUT_F32 ? 4096 : 2048;
+  // (kEpiBf16GeluTanhMul stages its fp32 multiplier chunk in the same slot)
+  static constexpr uint32_t CHUNK_BYTES = (OUT_F32 || EPI == kEpiBf16GeluTanhMul) ? 4096 : 2048;
   static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t B_BYTES = (BN / CG) * kGemmBK * 2;  // this CTA's rows of W
@@ -350,12 +355,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool fine = true;
       if constexpr (EPI == kEpiBf16QkRope) {
         static_assert(BN == 256 && EW == 8, "two 128-wide heads per tile, one per warp half");
-        if (nb * 2 < args.qk.q_heads + args.qk.k_heads) {
+        const int qk_heads = args.qk.q_heads + args.qk.k_heads;
+        if (nb * 2 < qk_heads + (args.qk.v_norm ? args.qk.v_heads : 0)) {
           // this warp half owns head gh = 2 nb + half (chunks 4 half .. 4 half + 3);
           // pass 1: the head's sum of squares (in double, as llama::rmsnorm),
-          // pass 2: scale by the norm weight, rotate pairs (i, i + 64), store
+          // pass 2: scale by the norm weight, rotate pairs (i, i + 64), store.
+          // A v head in such a tile gets the unweighted norm (v_norm) or
+          // nothing, and no rotation.
           const int gh = nb * 2 + half;
-          const float* wn = gh < args.qk.q_heads ? args.qk.q_norm : args.qk.k_norm;
+          const bool is_v = gh >= qk_heads;
+          const float* wn = gh < args.qk.q_heads ? args.qk.q_norm : (is_v ? nullptr : args.qk.k_norm);
+          const bool do_norm = is_v ? args.qk.v_norm != 0 : wn != nullptr;
           if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
             report(args.status, kDevTimeoutEpilogue);
             *abort_flag = 1;
@@ -364,7 +374,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t t_head = t_row + half * 128;
           float inv = 1.f;
-          if (wn) {
+          if (do_norm) {
             double ss = 0.0;
 #pragma unroll 1
             for (int c = 0; c < 4; c += 2) {
@@ -417,9 +427,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (wn) {
                   x = (x * inv) * gl[e];
                   y = (y * inv) * gh4[e];
+                } else if (do_norm) {
+                  x = x * inv;
+                  y = y * inv;
                 }
-                lo[j + e] = x * cc[e] - y * ssn[e];
-                hi[j + e] = x * ssn[e] + y * cc[e];
+                if (is_v) {
+                  lo[j + e] = x;
+                  hi[j + e] = y;
+                } else {
+                  lo[j + e] = x * cc[e] - y * ssn[e];
+                  hi[j + e] = x * ssn[e] + y * cc[e];
+                }
               }
             }
             auto emit = [&](const float (&v)[32], int col0) {
@@ -531,7 +549,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // residual rows row0 + 4k + lane/8, columns col0 + (lane%8)*4 .. +3:
         // coalesced 128-byte rows, issued before the TMEM wait
         float4 res[8];
-        if constexpr (EPI == kEpiF32Resid) {
+        if constexpr (EPI == kEpiF32Resid || EPI == kEpiBf16GeluTanhMul) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int r = row0 + 4 * k + (lane >> 3);
@@ -588,7 +606,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
         if (lane == 0) tma_store_wait_read<1>();
         __syncwarp();
-        if constexpr (EPI == kEpiF32Resid) {
+        if constexpr (EPI == kEpiF32Resid || EPI == kEpiBf16GeluTanhMul) {
           // transpose the residual to row-per-lane through the staging chunk
 #pragma unroll
           for (int k = 0; k < 8; ++k)
@@ -597,11 +615,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 q = *reinterpret_cast<const float4*>(st + stage_off<true>(lane, j));
-            v[4 * j] += q.x;
-            v[4 * j + 1] += q.y;
-            v[4 * j + 2] += q.z;
-            v[4 * j + 3] += q.w;
+            if constexpr (EPI == kEpiF32Resid) {
+              v[4 * j] += q.x;
+              v[4 * j + 1] += q.y;
+              v[4 * j + 2] += q.z;
+              v[4 * j + 3] += q.w;
+            } else {
+              v[4 * j] = gelu_tanh_f(v[4 * j]) * q.x;
+              v[4 * j + 1] = gelu_tanh_f(v[4 * j + 1]) * q.y;
+              v[4 * j + 2] = gelu_tanh_f(v[4 * j + 2]) * q.z;
+              v[4 * j + 3] = gelu_tanh_f(v[4 * j + 3]) * q.w;
+            }
           }
+          // the bf16 rows below overlap other lanes' fp32 rows of this chunk
+          if constexpr (EPI == kEpiBf16GeluTanhMul) __syncwarp();
         }
         if constexpr (F32) {
 #pragma unroll

@@ -29,103 +29,140 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   return (0.5f * x) * (1.0f + tanhf(c));
 }
 
-__device__ __forceinline__ float ld_elem(const void* base, int dtype, size_t i) {
-  if (dtype == kDtBf16) return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
-  return static_cast<const float*>(base)[i];
+__device__ __forceinline__ double sq4(float4 v) {
+  return static_cast<double>(v.x * v.x) + static_cast<double>(v.y * v.y) +
+         static_cast<double>(v.z * v.z) + static_cast<double>(v.w * v.w);
+}
+
+__device__ __forceinline__ uint2 bf16x4(float a, float b, float c, float d) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  return make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
 }
 
 // h = sqrt(hidden) * embed[id] (gemma.lisp:326-330); also the bf16 copy that
-// feeds every layer's per-layer-embedding projection (gemma.lisp:331-333)
+// feeds every layer's per-layer-embedding projection (gemma.lisp:331-333).
+// One warp per token, four columns per lane step (H % 128 == 0).
 __global__ void gemma_embed_kernel(GemmaEmbedArgs a) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= a.T) return;
   const size_t src = static_cast<size_t>(a.ids[t]) * a.H;
-  for (int i = lane; i < a.H; i += 32) {
-    const float v = a.scale * ld_elem(a.table, a.dtype, src + i);
-    a.h32[static_cast<size_t>(t) * a.H + i] = v;
-    a.h0b[static_cast<size_t>(t) * a.H + i] = __float2bfloat16_rn(v);
+  float4* h4 = reinterpret_cast<float4*>(a.h32 + static_cast<size_t>(t) * a.H);
+  uint2* hb4 = reinterpret_cast<uint2*>(a.h0b + static_cast<size_t>(t) * a.H);
+  for (int i = lane; i < a.H / 4; i += 32) {
+    float4 v;
+    if (a.dtype == kDtBf16) {
+      const uint2 r = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.table) + src)[i];
+      v = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u),
+                      __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u));
+    } else {
+      v = reinterpret_cast<const float4*>(static_cast<const float*>(a.table) + src)[i];
+    }
+    v = make_float4(a.scale * v.x, a.scale * v.y, a.scale * v.z, a.scale * v.w);
+    h4[i] = v;
+    hb4[i] = bf16x4(v.x, v.y, v.z, v.w);
   }
 }
 
 // One warp per (token, head): q heads get RMSNorm(q_norm) + RoPE, k heads
 // RMSNorm(k_norm) + RoPE, v heads the unscaled RMSNorm (gemma.lisp:236-247),
-// in place on the packed bf16 QKV rows.  Head dim <= 256.
+// in place on the packed bf16 QKV rows.  Lane l holds the element pairs
+// (i, i + hd/2) for i in [l * E, l * E + E), E = hd / 64 (head dim 64..256).
+template <int E>
 __global__ void head_norm_rope_kernel(HeadNormRopeArgs a) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nh = a.q_heads + 2 * a.kv_heads;
   if (w >= a.T * nh) return;
   const int t = w / nh, hh = w % nh;
-  const int hd = a.hd, half = hd / 2;
+  constexpr int HD = 64 * E, HALF = 32 * E;
   const int kind = hh < a.q_heads ? 0 : (hh < a.q_heads + a.kv_heads ? 1 : 2);
-  __nv_bfloat16* row = a.qkv + static_cast<size_t>(t) * a.ld + static_cast<size_t>(hh) * hd;
-  // lane holds pairs (i, i + half) for i = lane + 32 j < half
-  float lo[4], hi[4];
+  __nv_bfloat16* row = a.qkv + static_cast<size_t>(t) * a.ld + static_cast<size_t>(hh) * HD;
+  float lo[E], hi[E];
   double ss = 0.0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int i = lane + 32 * j;
-    lo[j] = hi[j] = 0.f;
-    if (i < half) {
-      lo[j] = __bfloat162float(row[i]);
-      hi[j] = __bfloat162float(row[i + half]);
-      ss += static_cast<double>(lo[j] * lo[j]) + static_cast<double>(hi[j] * hi[j]);
-    }
+  for (int e = 0; e < E; ++e) {
+    lo[e] = __bfloat162float(row[lane * E + e]);
+    hi[e] = __bfloat162float(row[HALF + lane * E + e]);
+    ss += static_cast<double>(lo[e] * lo[e]) + static_cast<double>(hi[e] * hi[e]);
   }
   ss = warp_sum_dd(ss);
-  const float inv = rms_inv(ss, hd, a.eps);
+  const float inv = rms_inv(ss, HD, a.eps);
   const float* g = kind == 0 ? a.q_norm : (kind == 1 ? a.k_norm : nullptr);
   const int p = a.pos[t];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int i = lane + 32 * j;
-    if (i >= half) continue;
-    float x = lo[j] * inv, y = hi[j] * inv;
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    float x = lo[e] * inv, y = hi[e] * inv;
     if (g) {
       x = x * g[i];
-      y = y * g[i + half];
+      y = y * g[i + HALF];
     }
     if (kind < 2) {
       // rotate-half RoPE at the token's position (gemma.lisp:105-119)
-      const float c = a.cos_t[static_cast<size_t>(p) * half + i];
-      const float s = a.sin_t[static_cast<size_t>(p) * half + i];
+      const float c = a.cos_t[static_cast<size_t>(p) * HALF + i];
+      const float s = a.sin_t[static_cast<size_t>(p) * HALF + i];
       const float nx = x * c - y * s, ny = x * s + y * c;
       x = nx;
       y = ny;
     }
-    row[i] = __float2bfloat16_rn(x);
-    row[i + half] = __float2bfloat16_rn(y);
+    lo[e] = x;
+    hi[e] = y;
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    row[lane * E + e] = __float2bfloat16_rn(lo[e]);
+    row[HALF + lane * E + e] = __float2bfloat16_rn(hi[e]);
   }
 }
 
 // h = (h + RMSNorm(x, g1)) [* scalar]; then hb = bf16(RMSNorm(h, g2)) or
-// bf16(h) when g2 is null (gemma.lisp:268-302)
+// bf16(h) when g2 is null (gemma.lisp:268-302).  One warp per token, four
+// columns per lane step; the second and third passes re-read this warp's
+// own rows, which are still in L1 / L2.
 __global__ void norm_add_kernel(NormAddArgs a) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= a.T) return;
-  const float* x = a.x + static_cast<size_t>(t) * a.H;
-  float* h = a.h32 + static_cast<size_t>(t) * a.H;
+  const int n4 = a.H / 4;
+  const float4* x = reinterpret_cast<const float4*>(a.x + static_cast<size_t>(t) * a.H);
+  float4* h = reinterpret_cast<float4*>(a.h32 + static_cast<size_t>(t) * a.H);
+  const float4* g1 = reinterpret_cast<const float4*>(a.g1);
   double ss = 0.0;
-  for (int i = lane; i < a.H; i += 32) ss += static_cast<double>(x[i] * x[i]);
+#pragma unroll 4
+  for (int i = lane; i < n4; i += 32) ss += sq4(x[i]);
   const float inv = rms_inv(warp_sum_dd(ss), a.H, a.eps);
   double ss2 = 0.0;
-  for (int i = lane; i < a.H; i += 32) {
-    float v = h[i] + (x[i] * inv) * a.g1[i];
-    if (a.scale_h) v = v * a.scalar;
+#pragma unroll 4
+  for (int i = lane; i < n4; i += 32) {
+    const float4 xv = x[i], gv = g1[i];
+    float4 v = h[i];
+    v.x = v.x + (xv.x * inv) * gv.x;
+    v.y = v.y + (xv.y * inv) * gv.y;
+    v.z = v.z + (xv.z * inv) * gv.z;
+    v.w = v.w + (xv.w * inv) * gv.w;
+    if (a.scale_h) v = make_float4(v.x * a.scalar, v.y * a.scalar, v.z * a.scalar, v.w * a.scalar);
     h[i] = v;
-    ss2 += static_cast<double>(v * v);
+    ss2 += sq4(v);
   }
   if (!a.outb) return;
+  uint2* ob = reinterpret_cast<uint2*>(a.outb + static_cast<size_t>(t) * a.H);
   if (!a.g2) {
-    for (int i = lane; i < a.H; i += 32)
-      a.outb[static_cast<size_t>(t) * a.H + i] = __float2bfloat16_rn(h[i]);
+#pragma unroll 4
+    for (int i = lane; i < n4; i += 32) {
+      const float4 v = h[i];
+      ob[i] = bf16x4(v.x, v.y, v.z, v.w);
+    }
     return;
   }
   const float inv2 = rms_inv(warp_sum_dd(ss2), a.H, a.eps);
-  for (int i = lane; i < a.H; i += 32)
-    a.outb[static_cast<size_t>(t) * a.H + i] = __float2bfloat16_rn((h[i] * inv2) * a.g2[i]);
+  const float4* g2 = reinterpret_cast<const float4*>(a.g2);
+#pragma unroll 4
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = h[i], gv = g2[i];
+    ob[i] = bf16x4((v.x * inv2) * gv.x, (v.y * inv2) * gv.y, (v.z * inv2) * gv.z,
+                   (v.w * inv2) * gv.w);
+  }
 }
 
 // this layer's per-layer embedding: x = x * (1 / sqrt(hidden)), then
@@ -134,24 +171,41 @@ __global__ void ple_prep_kernel(PlePrepArgs a) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= a.T) return;
-  float* x = a.x + static_cast<size_t>(t) * a.P;
+  const int n4 = a.P / 4;
+  float4* x = reinterpret_cast<float4*>(a.x + static_cast<size_t>(t) * a.P);
+  const float4* g = reinterpret_cast<const float4*>(a.g);
+  const float s = a.inv_sqrt_h;
   double ss = 0.0;
-  for (int i = lane; i < a.P; i += 32) {
-    const float v = x[i] * a.inv_sqrt_h;
-    x[i] = v;
-    ss += static_cast<double>(v * v);
+#pragma unroll 4
+  for (int i = lane; i < n4; i += 32) {
+    float4 v = x[i];
+    v = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+    ss += sq4(v);
   }
   const float inv = rms_inv(warp_sum_dd(ss), a.P, a.eps);
-  for (int i = lane; i < a.P; i += 32) x[i] = (x[i] * inv) * a.g[i];
+#pragma unroll 4
+  for (int i = lane; i < n4; i += 32) {
+    float4 v = x[i];
+    const float4 gv = g[i];
+    v = make_float4(((v.x * s) * inv) * gv.x, ((v.y * s) * inv) * gv.y, ((v.z * s) * inv) * gv.z,
+                    ((v.w * s) * inv) * gv.w);
+    x[i] = v;
+  }
 }
 
 // gelu-tanh(gate(h)) * per-layer embedding, to bf16 for the PLE projection
-// (gemma.lisp:290-293)
+// (gemma.lisp:290-293); four elements per thread step
 __global__ void ple_gate_kernel(PleGateArgs a) {
-  const size_t n = static_cast<size_t>(a.T) * a.P;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    a.outb[i] = __float2bfloat16_rn(gelu_tanh_f(a.gate[i]) * a.ple[i]);
+  const size_t n4 = static_cast<size_t>(a.T) * a.P / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(a.gate);
+  const float4* p4 = reinterpret_cast<const float4*>(a.ple);
+  uint2* o4 = reinterpret_cast<uint2*>(a.outb);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 g = g4[i], p = p4[i];
+    o4[i] = bf16x4(gelu_tanh_f(g.x) * p.x, gelu_tanh_f(g.y) * p.y, gelu_tanh_f(g.z) * p.z,
+                   gelu_tanh_f(g.w) * p.w);
+  }
 }
 
 // One CTA per sequence: mean over tokens in order (gemma.lisp:366-370),
@@ -197,9 +251,13 @@ cudaError_t launch_gemma_embed(const GemmaEmbedArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t st) {
-  if (a.hd > 256 || a.hd % 2) return cudaErrorInvalidValue;
   const size_t rows = static_cast<size_t>(a.T) * (a.q_heads + 2 * a.kv_heads);
-  head_norm_rope_kernel<<<warps_grid(rows), 256, 0, st>>>(a);
+  switch (a.hd) {
+    case 64: head_norm_rope_kernel<1><<<warps_grid(rows), 256, 0, st>>>(a); break;
+    case 128: head_norm_rope_kernel<2><<<warps_grid(rows), 256, 0, st>>>(a); break;
+    case 256: head_norm_rope_kernel<4><<<warps_grid(rows), 256, 0, st>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
@@ -214,7 +272,8 @@ cudaError_t launch_ple_prep(const PlePrepArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_ple_gate(const PleGateArgs& a, cudaStream_t st) {
-  const size_t n = static_cast<size_t>(a.T) * a.P;
+  if (a.P % 4) return cudaErrorInvalidValue;
+  const size_t n = static_cast<size_t>(a.T) * a.P / 4;
   size_t blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   ple_gate_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(a);

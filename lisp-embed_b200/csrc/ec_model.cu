@@ -421,11 +421,11 @@ static int load_gemma(Device& d, const JVal& tc) {
     return rc;
   m.hd = static_cast<int>(qn0->numel);
   m.kv_heads = m.hd ? static_cast<int>(k0->shape[0] / m.hd) : 0;
-  if (m.hd != 32 && m.hd != 64 && m.hd != 128)
-    return set_error(EC_EUNSUPPORTED, "gemma head_dim %d (attention kernels: 32, 64, 128)", m.hd);
+  if (m.hd != 64 && m.hd != 128)
+    return set_error(EC_EUNSUPPORTED, "gemma head_dim %d (this build: 64, 128)", m.hd);
   if (m.kv_heads <= 0 || m.heads % m.kv_heads)
     return set_error(EC_EINVAL, "heads %d not a multiple of kv heads %d", m.heads, m.kv_heads);
-  if (H % 128 || P % 64 || F % 128 || ((m.heads + 2 * m.kv_heads) * m.hd) % 64 || H > 2048 ||
+  if (H % 128 || P % 128 || F % 128 || ((m.heads + 2 * m.kv_heads) * m.hd) % 64 || H > 2048 ||
       H + m.out_dim > 12288)
     return set_error(EC_EUNSUPPORTED, "gemma widths H %d P %d F %d outside this build", H, P, F);
   m.word = emb->p;
@@ -665,7 +665,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
 
   auto gemm = [&](const bf16* A, int lda, const bf16* W, int N, int K, const float* bias,
                   const float* resid, void* o, int ldo, int epi,
-                  const QkRopeEpi* qk = nullptr) -> int {
+                  const QkRopeEpi* qk = nullptr, int ldr = 0) -> int {
     GemmLaunch g;
     g.qk = qk;
     g.A = A;
@@ -677,15 +677,15 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     g.K = K;
     g.bias = bias;
     g.resid = resid;
-    g.ldr = H;
+    g.ldr = ldr ? ldr : H;
     g.out = o;
     g.ldo = ldo;
     g.epi = epi;
     g.bn = 0;
     g.status = d.status;
     const double out_b = epi == kEpiF32Resid || epi == kEpiF32 ? 4.0 * T * N
-                         : epi == kEpiBf16Swiglu              ? 1.0 * T * N
-                                                              : 2.0 * T * N;
+                         : epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate ? 1.0 * T * N
+                                                                                : 2.0 * T * N;
     const double bytes = 2.0 * T * K + 2.0 * N * K + out_b + (resid ? 4.0 * T * N : 0.0);
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_gemm(g, st, d.num_sms);
@@ -823,50 +823,80 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     bf16* pgb = reinterpret_cast<bf16*>(ws + L.pgb);
     at.scale = 1.0f;  // bidirectional attention with scale 1.0 (gemma.lisp:250-265)
     at.causal = 0;
-    auto row = [&](cudaError_t e, const char* what, double bytes) -> int {
+    // the start event is recorded before the launch (the launcher is
+    // called inside)
+    auto row = [&](auto&& launch, const char* what, double bytes) -> int {
       const int e0 = prof_begin(d);
+      const cudaError_t e = launch();
       return rows(e, what, bytes, e0);
     };
     {
       GemmaEmbedArgs ea{ids, m.word, m.word_dt, sqrtf(static_cast<float>(H)), h32, h0b, T, H};
-      EC_TRY(row(launch_gemma_embed(ea, st), "gemma embed", TH * 10.0));
+      EC_TRY(row([&] { return launch_gemma_embed(ea, st); }, "gemma embed", TH * 10.0));
     }
     const float inv_sqrt_h = 1.0f / sqrtf(static_cast<float>(H));
+    const bool fuse_qkv_norm = m.hd == 128 && nqkv % 256 == 0 && getenv("EC_NO_FUSED_ROPE") == nullptr;
     for (int li = 0; li < m.layers; ++li) {
       const GemmaLayerW& w = m.gl[li];
-      // attention sub-block
-      RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};
-      EC_TRY(row(launch_rmsnorm(r1, st), "rmsnorm", TH * 6.0));
-      EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16));
-      HeadNormRopeArgs hr{qkv, nqkv, m.heads, m.kv_heads, m.hd, w.q_norm, w.k_norm, m.eps, pos,
-                          w.rope ? m.cos2_t : m.cos_t, w.rope ? m.sin2_t : m.sin_t, T};
-      EC_TRY(row(launch_head_norm_rope(hr, st), "head norm rope", 4.0 * T * nqkv));
+      // attention sub-block; the input RMSNorm of layers after the first
+      // came out of the previous layer's last residual add
+      if (li == 0) {
+        RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};
+        EC_TRY(row([&] { return launch_rmsnorm(r1, st); }, "rmsnorm", TH * 6.0));
+      }
+      const float* cos_l = w.rope ? m.cos2_t : m.cos_t;
+      const float* sin_l = w.rope ? m.sin2_t : m.sin_t;
+      if (fuse_qkv_norm) {
+        // q/k RMSNorm + RoPE and the v RMSNorm in the QKV GEMM's epilogue
+        QkRopeEpi qe{w.q_norm, w.k_norm, m.heads, m.kv_heads, m.eps, pos, cos_l, sin_l};
+        qe.v_heads = m.kv_heads;
+        qe.v_norm = 1;
+        EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16QkRope, &qe));
+      } else {
+        EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, nullptr, nullptr, qkv, nqkv, kEpiBf16));
+        HeadNormRopeArgs hr{qkv, nqkv, m.heads, m.kv_heads, m.hd, w.q_norm, w.k_norm, m.eps, pos,
+                            cos_l, sin_l, T};
+        EC_TRY(row([&] { return launch_head_norm_rope(hr, st); }, "head norm rope",
+                   4.0 * T * nqkv));
+      }
       EC_TRY(attention());
       EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, nullptr, tmp, H, kEpiF32));
       NormAddArgs na1{tmp, w.post_ln, h32, 0, 1.f, w.pre_ff_ln, hb, m.eps, T, H};
-      EC_TRY(row(launch_norm_add(na1, st), "norm add", TH * 14.0));
+      EC_TRY(row([&] { return launch_norm_add(na1, st); }, "norm add", TH * 14.0));
       // gated GELU-tanh MLP
       EC_TRY(gemm(hb, H, w.wgu, 2 * F, H, nullptr, nullptr, ff, F, kEpiBf16GeluTanhGate));
       EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, nullptr, tmp, H, kEpiF32));
       NormAddArgs na2{tmp, w.post_ff_ln, h32, 0, 1.f, nullptr, hb, m.eps, T, H};
-      EC_TRY(row(launch_norm_add(na2, st), "norm add", TH * 14.0));
+      EC_TRY(row([&] { return launch_norm_add(na2, st); }, "norm add", TH * 14.0));
       // per-layer embedding of this layer from the scaled token embedding
       EC_TRY(gemm(h0b, H, w.wpp, P, H, nullptr, nullptr, ple, P, kEpiF32));
       PlePrepArgs pa{ple, inv_sqrt_h, m.ple_norm, m.eps, T, P};
-      EC_TRY(row(launch_ple_prep(pa, st), "ple prep", 8.0 * T * P));
+      EC_TRY(row([&] { return launch_ple_prep(pa, st); }, "ple prep", 8.0 * T * P));
       // PLE block: gate(h) -> GELU-tanh * ple -> projection -> norm -> residual
-      EC_TRY(gemm(hb, H, w.wple_gate, P, H, nullptr, nullptr, pg, P, kEpiF32));
-      PleGateArgs pga{pg, ple, pgb, T, P};
-      EC_TRY(row(launch_ple_gate(pga, st), "ple gate", 10.0 * T * P));
+      // gelu-tanh(gate(h)) * ple straight out of the gate GEMM's epilogue
+      // (EC_NO_FUSED_PLE_GATE: fp32 gate, then the row kernel)
+      if (getenv("EC_NO_FUSED_PLE_GATE") == nullptr) {
+        EC_TRY(gemm(hb, H, w.wple_gate, P, H, nullptr, ple, pgb, P, kEpiBf16GeluTanhMul, nullptr,
+                    P));
+      } else {
+        EC_TRY(gemm(hb, H, w.wple_gate, P, H, nullptr, nullptr, pg, P, kEpiF32));
+        PleGateArgs pga{pg, ple, pgb, T, P};
+        EC_TRY(row([&] { return launch_ple_gate(pga, st); }, "ple gate", 10.0 * T * P));
+      }
       EC_TRY(gemm(pgb, P, w.wple_proj, H, P, nullptr, nullptr, tmp, H, kEpiF32));
-      NormAddArgs na3{tmp, w.ple_norm, h32, 1, w.scalar, nullptr, nullptr, m.eps, T, H};
-      EC_TRY(row(launch_norm_add(na3, st), "norm add scale", TH * 12.0));
+      // h = (h + RMSNorm(ple)) * layer_scalar, and hb = the next layer's
+      // input RMSNorm of it
+      const bool more = li + 1 < m.layers;
+      NormAddArgs na3{tmp, w.ple_norm, h32, 1, w.scalar, more ? m.gl[li + 1].in_ln : nullptr,
+                      more ? hb : nullptr, m.eps, T, H};
+      EC_TRY(row([&] { return launch_norm_add(na3, st); }, "norm add scale",
+                 TH * (more ? 14.0 : 12.0)));
     }
     // final RMSNorm per token, then mean pool + projection + L2
     RmsArgs rf{h32, nullptr, m.final_norm, m.eps, nullptr, h32, T, H};
-    EC_TRY(row(launch_rmsnorm(rf, st), "final rmsnorm", TH * 8.0));
+    EC_TRY(row([&] { return launch_rmsnorm(rf, st); }, "final rmsnorm", TH * 8.0));
     GemmaPoolArgs gp{h32, cu, m.w_out, out, out_stride, H, m.out_dim};
-    EC_TRY(row(launch_gemma_pool(gp, nseq, st), "pool project", TH * 4.0));
+    EC_TRY(row([&] { return launch_gemma_pool(gp, nseq, st); }, "pool project", TH * 4.0));
     return EC_OK;
   }
   // llama family: h = embed_tokens[ids] (llama.lisp:316-320)
@@ -877,8 +907,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   }
   // q/k norm + RoPE fused into the QKV GEMM (head dim 128, heads in 256-wide
   // tiles); EC_NO_FUSED_ROPE keeps the separate row kernel
-  const bool fuse_rope = m.hd == 128 && nqkv % 256 == 0 && (m.heads + m.kv_heads) % 2 == 0 &&
-                         m.heads % 2 == 0 && getenv("EC_NO_FUSED_ROPE") == nullptr;
+  const bool fuse_rope = m.hd == 128 && nqkv % 256 == 0 && getenv("EC_NO_FUSED_ROPE") == nullptr;
   for (int li = 0; li < m.layers; ++li) {
     const LlamaLayerW& w = m.ll[li];
     RmsArgs r1{h32, nullptr, w.in_ln, m.eps, hb, nullptr, T, H};

@@ -80,13 +80,28 @@ def test_errors(synth_root, ec):
         model.embed_batch(np.zeros(0, np.int32), np.array([0, 0], np.int64))  # empty sequence
 
 
-def test_gemma(synth_root, ec):
+@pytest.mark.parametrize("unfused", [0, 1])
+def test_gemma(synth_root, ec, monkeypatch, unfused):
     """EmbeddingGemma: one sliding (theta 1e4) and one full-attention (theta
-    1e6) layer, PLE, per-head q/k/v norms, mean pool + 512 -> 768 projection."""
+    1e6) layer, PLE, per-head q/k/v norms, mean pool + 512 -> 768 projection;
+    with the norms / PLE gate fused into GEMM epilogues and without."""
     import dataclasses
+    if unfused:
+        monkeypatch.setenv("EC_NO_FUSED_ROPE", "1")
+        monkeypatch.setenv("EC_NO_FUSED_PLE_GATE", "1")
     s = synth.with_layers(synth.GEMMA_EMB, 2, vocab=4096)
     s = dataclasses.replace(s, name=s.name + "-sf", extra=dict(
         s.extra, layer_types=["sliding_attention", "full_attention"]))
     fam, _ = _check(s, 4, [1, 2, 40, 129, 300], synth_root, ec, "gemma")
     assert fam == "gemma"
     assert model.dim() == 768
+
+
+def test_qwen3_odd_head_count(synth_root, ec):
+    """16 q heads + 1 kv head: one 256-wide QKV tile holds the k head and the
+    v head, so the fused epilogue rotates one half and leaves the other."""
+    import dataclasses
+    s = synth.with_layers(synth.QWEN3_06B, 1, vocab=4096)
+    s = dataclasses.replace(s, name=s.name + "-kv1", kv_heads=1)
+    fam, _ = _check(s, 3, [1, 7, 200, 333], synth_root, ec, "qwen3")
+    assert fam == "llama"

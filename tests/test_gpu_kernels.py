@@ -54,6 +54,34 @@ def test_gemm_epilogues(ec, M, N, K, bn, epi):
     assert err < tol, f"rel err {err}"
 
 
+def _gelu_tanh(x):
+    # gemma::gelu-tanh (gemma.lisp:85-89)
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+
+# EmbeddingGemma epilogues: gelu_tanh(gate) * up on SwiGLU's 128-row
+# interleave (6), and gelu_tanh(acc) * an fp32 multiplier (7, the PLE gate)
+@pytest.mark.parametrize("M,N,K", [(1, 512, 512), (300, 4096, 512), (1029, 512, 512)])
+@pytest.mark.parametrize("epi", [6, 7])
+def test_gemm_gelu_tanh_epilogues(ec, M, N, K, epi):
+    g = torch.Generator(device="cuda").manual_seed(M + N + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    if epi == 6:
+        F = N // 2
+        Wg = (0.05 * torch.randn(F, K, device="cuda", generator=g)).bfloat16()
+        Wu = (0.05 * torch.randn(F, K, device="cuda", generator=g)).bfloat16()
+        W = torch.stack([Wg.view(F // 128, 128, K), Wu.view(F // 128, 128, K)], 1).reshape(N, K)
+        out = _gemm(ec, A, W.contiguous(), None, None, 6, 0, F, torch.bfloat16).float()
+        ref = _gelu_tanh(A.float() @ Wg.float().t()) * (A.float() @ Wu.float().t())
+    else:
+        W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+        mul = torch.randn(M, N, device="cuda", generator=g)
+        out = _gemm(ec, A, W, None, mul, 7, 0, N, torch.bfloat16).float()
+        ref = _gelu_tanh(A.float() @ W.float().t()) * mul
+    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
 # CTA-pair GEMM (cta_group::2, 256 x 256 tiles): ragged M (one or both
 # halves of the last tile past M), K down to one k-block
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (129, 512, 384), (300, 1536, 384),
