@@ -68,7 +68,8 @@ int ec_upload_tensor(const char *name, int dtype, const int64_t *shape, int ndim
 /* Build the model from the uploaded tensors.  `config_json` is config.json,
  * `pooling_json` is 1_Pooling/config.json or NULL.  Replaces
  * model:load-model's dispatch (model.lisp:28-46) plus bert:load-model
- * (bert.lisp:55-129, 343-389) and llama:load-model (llama.lisp:172-220).
+ * (bert.lisp:55-129, 343-389), llama:load-model (llama.lisp:172-220) and
+ * gemma:load-model (gemma.lisp:140-212).
  * Writes the family (EC_FAMILY_*) and the embedding dimension. */
 int ec_load_model(const char *config_json, const char *pooling_json, int *family,
                   int *dim);
@@ -81,8 +82,9 @@ int ec_dim(void);
  * offsets[s+1]); `out` receives nseq rows of ec_dim() floats at a stride of
  * `out_stride` floats, L2-normalised, in input order.  Replaces model:embed
  * (model.lisp:48-54) -> bert::embed-bert (bert.lisp:275-320),
- * bert::embed-mpnet (:455-499) and llama:embed (llama.lisp:296-344) for a
- * whole batch, the way embed:run batches chunks (embed.lisp:88-105). */
+ * bert::embed-mpnet (:455-499), llama:embed (llama.lisp:296-344) and
+ * gemma:embed (gemma.lisp:306-380) for a whole batch, the way embed:run
+ * batches chunks (embed.lisp:88-105). */
 int ec_embed_batch(const int32_t *ids, const int64_t *offsets, int nseq, float *out,
                    int out_stride);
 

@@ -149,7 +149,8 @@ cudaError_t launch_convert(int kind, const void* src, void* dst, size_t n, cudaS
 
 // ---- GEMM (ec_gemm.cu) -------------------------------------------------------
 // C[M, N] = A[M, K] . W[N, K]^T with epilogue `epi` (GemmEpi in ec_gemm.cuh:
-// 0 bf16, 1 bf16+gelu, 2 f32+resid, 3 bf16 swiglu, 4 f32).  A and W bf16,
+// 0 bf16, 1 bf16+gelu, 2 f32+resid, 3 bf16 swiglu, 4 f32, 5 bf16 with head
+// norms + RoPE, 6 bf16 gelu-tanh gate, 7 bf16 gelu-tanh * multiplier).  A and W bf16,
 // K-major; K % 64 == 0; N % bn == 0.  `bn` 0 = pick automatically.
 struct QkRopeEpi;  // ec_gemm.cuh
 struct GemmLaunch {

@@ -139,7 +139,7 @@ family keyword as model:load-model does (model.lisp:28-46)."
     (with-saps ((fp fam) (dp dm))
       (check (%load-model cfg pool fp dp) "ec_load_model"))
     (setf *dim* (aref dm 0))
-    (ecase (aref fam 0) (1 :bert) (2 :mpnet) (3 :llama))))
+    (ecase (aref fam 0) (1 :bert) (2 :mpnet) (3 :llama) (4 :gemma))))
 
 (defun dim () *dim*)
 
