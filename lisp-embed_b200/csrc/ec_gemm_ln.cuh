@@ -5,7 +5,10 @@
 //
 //   x = A . W^T + bias + resid        (fp32, one full row of N = hidden)
 //   y = (x - mean(x)) / (sqrt(var(x)) + 1e-12) * g + b
-//   out32 = y (fp32 residual stream), outb = bf16(y) (next GEMM's input)
+//   outb = bf16(y) (next GEMM's input), out32 = y (fp32, optional)
+//
+// The residual is either the fp32 stream or (RB) the previous LayerNorm's
+// bf16 output -- the same rounded row the next GEMM already reads.
 //
 // A LayerNorm needs whole rows, wider than one CTA's accumulator, so a
 // thread-block cluster of C CTAs shares each 128-row tile: CTA r computes
@@ -30,14 +33,16 @@ namespace ec {
 struct GemmLnArgs {
   int M, N, K;
   const float* bias;   // [N] or nullptr
-  const float* resid;  // [M, N] fp32, may alias the fp32 output
   const float* ln_g;   // [N]
   const float* ln_b;   // [N]
   int m_tiles;
+  int out32;           // 1: also store the fp32 row
   unsigned* status;
 };
 
-template <int BN, int C>
+// RB: the residual arrives as bf16 (the previous LayerNorm's bf16 output,
+// which is also the next GEMM's input) instead of fp32
+template <int BN, int C, bool RB = false>
 struct GemmLnCfg {
   static constexpr int NCH = BN / 32;                      // 32-column chunks per CTA
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
@@ -46,6 +51,7 @@ struct GemmLnCfg {
   // per epilogue warp: two fp32 32 x 32 buffers (residual in by TMA, then
   // fp32 out) and one bf16 32 x 32 staging chunk
   static constexpr uint32_t BUF_BYTES = 4096;
+  static constexpr uint32_t RES_BYTES = RB ? 2048 : 4096;  // one residual chunk
   static constexpr uint32_t WARP_BYTES = 2 * BUF_BYTES + 2048;
   static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * WARP_BYTES;
   // exchange slots: float2 (sum, M2) [2 tile parities][C ranks][2 halves][128 rows]
@@ -64,14 +70,14 @@ struct GemmLnCfg {
   static_assert(NCH % 2 == 0, "both epilogue halves take whole chunks");
 };
 
-template <int BN, int C>
+template <int BN, int C, bool RB>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO32,
                    const __grid_constant__ CUtensorMap tmOb,
                    const __grid_constant__ CUtensorMap tmR, const GemmLnArgs args) {
-  using Cfg = GemmLnCfg<BN, C>;
+  using Cfg = GemmLnCfg<BN, C, RB>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NCH = Cfg::NCH;
   constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
@@ -222,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // xs[par][r][hf][row]
     auto slot = [&](int par, int r, int hf) -> int { return ((par * C + r) * 2 + hf) * 128 + row; };
     auto load_res = [&](int b, int c, int row0) {
-      mbar_arrive_expect_tx(&rb[b], Cfg::BUF_BYTES);
+      mbar_arrive_expect_tx(&rb[b], Cfg::RES_BYTES);
       tma_load_2d(bufs + b * Cfg::BUF_BYTES, &tmR, &rb[b], rank * BN + c * 32, row0);
     };
     int acc = 0;
@@ -265,9 +271,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         rbits ^= 1u << b;
         tmem_wait_ld();
+        float rr[32];  // this lane's row of the residual chunk
+        if constexpr (RB) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(buf + stage_off<false>(lane, j));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              rr[8 * j + 2 * e] = __uint_as_float(w[e] << 16);
+              rr[8 * j + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 q = *reinterpret_cast<const float4*>(buf + stage_off<true>(lane, j));
+            rr[4 * j] = q.x;
+            rr[4 * j + 1] = q.y;
+            rr[4 * j + 2] = q.z;
+            rr[4 * j + 3] = q.w;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 q = *reinterpret_cast<const float4*>(buf + stage_off<true>(lane, j));
+          const float4 q = make_float4(rr[4 * j], rr[4 * j + 1], rr[4 * j + 2], rr[4 * j + 3]);
           const float4 bb = *reinterpret_cast<const float4*>(sVec + cl + 4 * j);
           const float x0 = (__uint_as_float(v[4 * j]) + bb.x) + q.x;
           const float x1 = (__uint_as_float(v[4 * j + 1]) + bb.y) + q.y;
@@ -352,9 +380,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int e = 0; e < 8; ++e)
             y[e] = ((__uint_as_float(v[8 * j + e]) - mean) * inv) * sVec[BN + cl + 8 * j + e] +
                    sVec[2 * BN + cl + 8 * j + e];
-          *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j)) = make_float4(y[0], y[1], y[2], y[3]);
-          *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j + 1)) =
-              make_float4(y[4], y[5], y[6], y[7]);
+          if (args.out32) {
+            *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j)) =
+                make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j + 1)) =
+                make_float4(y[4], y[5], y[6], y[7]);
+          }
           *reinterpret_cast<uint4*>(stb + stage_off<false>(lane, j)) =
               make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]),
                          pack_bf16(y[6], y[7]));
@@ -362,7 +393,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmO32, st32, rank * BN + cl, row0);
+          if (args.out32) tma_store_2d(&tmO32, st32, rank * BN + cl, row0);
           tma_store_2d(&tmOb, stb, rank * BN + cl, row0);
           tma_store_commit();
         }

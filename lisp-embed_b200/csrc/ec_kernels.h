@@ -183,12 +183,13 @@ struct GemmLnLaunch {
   const __nv_bfloat16* W;  // [N, K]
   int M, N, K;
   const float* bias;
-  const float* resid;      // [M, N]
+  const float* resid;      // [M, N] fp32 residual, or
   const float* ln_g;
   const float* ln_b;
-  float* out32;            // [M, N]
+  float* out32;            // [M, N] or nullptr (no fp32 output)
   __nv_bfloat16* outb;     // [M, N]
   unsigned* status;
+  const __nv_bfloat16* resid_b = nullptr;  // [M, N] bf16 residual (replaces resid)
 };
 bool gemm_ln_supported(int N);
 cudaError_t launch_gemm_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms);

@@ -696,10 +696,22 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   // h32 = LayerNorm(A . W^T + bias + h32), hb = bf16(h32) in one kernel
   // (EC_NO_GEMM_LN keeps the GEMM + separate LayerNorm pair)
   const bool fuse_ln = gemm_ln_supported(H) && getenv("EC_NO_GEMM_LN") == nullptr;
+  // post-LayerNorm models with the fused kernel carry the residual between
+  // sublayers as the LayerNorm's bf16 output (the row the next GEMM reads
+  // anyway); only the last LayerNorm also writes fp32 rows, for pooling.
+  // EC_F32_RESIDUAL keeps the fp32 stream everywhere.
+  const bool bf16_resid = fuse_ln && getenv("EC_F32_RESIDUAL") == nullptr &&
+                          getenv("EC_FUSED_MLP") == nullptr;
   auto gemm_ln = [&](const bf16* A, int K, const bf16* W, const float* bias, const float* lg,
-                     const float* lb) -> int {
+                     const float* lb, bool out32 = true) -> int {
     GemmLnLaunch g{A, K, W, T, H, K, bias, h32, lg, lb, h32, hb, d.status};
-    const double bytes = 2.0 * T * K + 2.0 * H * K + 4.0 * T * H + 6.0 * T * H;
+    if (bf16_resid) {
+      g.resid = nullptr;
+      g.resid_b = hb;
+      if (!out32) g.out32 = nullptr;
+    }
+    const double bytes = 2.0 * T * K + 2.0 * H * K + (bf16_resid ? 2.0 : 4.0) * T * H +
+                         (g.out32 ? 6.0 : 2.0) * T * H;
     const int e0 = prof_begin(d);
     const cudaError_t e = launch_gemm_ln(g, st, d.num_sms);
     prof_end(d, 0, 2.0 * T * H * K, bytes, e0);
@@ -754,7 +766,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     e.type_dtype = m.type_dt;
     e.g = m.emb_g;
     e.b = m.emb_b;
-    e.out32 = h32;
+    e.out32 = bf16_resid && m.layers > 0 ? nullptr : h32;
     e.outb = hb;
     e.T = T;
     e.H = H;
@@ -767,7 +779,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
       EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, w.bqkv, nullptr, qkv, nqkv, kEpiBf16));
       EC_TRY(attention());
       if (fuse_ln) {
-        EC_TRY(gemm_ln(ctx, nctx, w.wo, w.bo, w.ln1g, w.ln1b));
+        EC_TRY(gemm_ln(ctx, nctx, w.wo, w.bo, w.ln1g, w.ln1b, false));
       } else {
         EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, w.bo, h32, tmp, H, kEpiF32Resid));
         LnArgs l1{tmp, w.ln1g, w.ln1b, h32, hb, T, H};
@@ -788,7 +800,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
       } else {
         EC_TRY(gemm(hb, H, w.wff, F, H, w.bff, nullptr, ff, F, kEpiBf16Gelu));
         if (fuse_ln) {
-          EC_TRY(gemm_ln(ff, F, w.wout, w.bout, w.ln2g, w.ln2b));
+          EC_TRY(gemm_ln(ff, F, w.wout, w.bout, w.ln2g, w.ln2b, li + 1 == m.layers));
         } else {
           EC_TRY(gemm(ff, F, w.wout, H, F, w.bout, h32, tmp, H, kEpiF32Resid));
           LnArgs l2{tmp, w.ln2g, w.ln2b, h32, hb, T, H};

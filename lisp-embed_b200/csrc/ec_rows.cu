@@ -95,7 +95,7 @@ __global__ void embed_ln_kernel(EmbedLnArgs a) {
     }
     v[i] = s;
   }
-  ln_finish<NV>(v, a.H, a.g, a.b, a.out32 + static_cast<size_t>(warp) * a.H,
+  ln_finish<NV>(v, a.H, a.g, a.b, a.out32 ? a.out32 + static_cast<size_t>(warp) * a.H : nullptr,
                 a.outb + static_cast<size_t>(warp) * a.H, lane);
 }
 

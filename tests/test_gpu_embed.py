@@ -31,12 +31,20 @@ def _check(shape, seed, lengths, synth_root, ec, workload):
     return fam, cos
 
 
-def test_minilm_full_depth(synth_root, ec):
+# default: the residual between sublayers is the LayerNorm's bf16 output;
+# EC_F32_RESIDUAL keeps an fp32 residual stream
+@pytest.mark.parametrize("f32_resid", [0, 1])
+def test_minilm_full_depth(synth_root, ec, monkeypatch, f32_resid):
+    if f32_resid:
+        monkeypatch.setenv("EC_F32_RESIDUAL", "1")
     fam, cos = _check(synth.MINILM, 0, [1, 2, 16, 63, 64, 65, 130, 256], synth_root, ec, "minilm")
     assert fam == "bert"
 
 
-def test_bert_base_bf16(synth_root, ec):
+@pytest.mark.parametrize("f32_resid", [0, 1])
+def test_bert_base_bf16(synth_root, ec, monkeypatch, f32_resid):
+    if f32_resid:
+        monkeypatch.setenv("EC_F32_RESIDUAL", "1")
     s = synth.with_layers(synth.BERT_BASE, 2)
     fam, _ = _check(s, 1, [3, 32, 100, 129, 512], synth_root, ec, "bert")
     assert fam == "bert"
