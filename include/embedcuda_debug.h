@@ -50,6 +50,10 @@ int ecdbg_profile_read(const char *cls, double *ms, double *flops, double *bytes
                        long long *launches);
 /* Kernel launches issued by the library since the last ecdbg_profile(1). */
 long long ecdbg_launches(void);
+/* Rows assigned by the tensor-core path of ec_kmeans / ec_assign /
+ * ec_assign_all (scores re-checked exactly) and rows that took the exact
+ * single-float scan, since the last reset; reset != 0 clears them. */
+int ecdbg_assign_rows(long long *tc_rows, long long *exact_rows, int reset);
 
 /* Failure-path check of the bounded waits: launches one CTA that waits on an
  * mbarrier no thread arrives on, with a limit of `limit_ms` milliseconds.

@@ -61,6 +61,57 @@ int sync_and_check(Device& d, const char* what) {
   return EC_OK;
 }
 
+int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* what) {
+  constexpr size_t kChunk = size_t{64} << 20;
+  if (bytes < 2 * kChunk) {
+    int rc = check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d.stream), what);
+    if (rc) return rc;
+    return check_cuda(cudaStreamSynchronize(d.stream), what);
+  }
+  for (int i = 0; i < 2; ++i) {
+    if (!d.stage[i] && cudaHostAlloc(&d.stage[i], kChunk, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      d.stage[i] = nullptr;
+      // no pinned memory to spare: one pageable copy
+      int rc = check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d.stream), what);
+      if (rc) return rc;
+      return check_cuda(cudaStreamSynchronize(d.stream), what);
+    }
+    if (!d.stage_ev[i]) {
+      int rc = check_cuda(cudaEventCreateWithFlags(&d.stage_ev[i], cudaEventDisableTiming), what);
+      if (rc) return rc;
+    }
+  }
+  const unsigned hw = std::thread::hardware_concurrency();
+  const int nthr = static_cast<int>(std::min(8u, std::max(1u, hw / 2)));
+  const char* s = static_cast<const char*>(src);
+  char* t = static_cast<char*>(dst);
+  bool used[2] = {false, false};
+  int b = 0;
+  for (size_t off = 0; off < bytes; off += kChunk, b ^= 1) {
+    const size_t len = std::min(kChunk, bytes - off);
+    // the DMA that last read this buffer must be done
+    if (used[b]) {
+      int rc = check_cuda(cudaEventSynchronize(d.stage_ev[b]), what);
+      if (rc) return rc;
+    }
+    char* buf = static_cast<char*>(d.stage[b]);
+    const size_t per = (len + nthr - 1) / nthr;
+    std::vector<std::thread> th;
+    for (int k = 1; k < nthr; ++k) {
+      const size_t a0 = std::min(len, per * k), a1 = std::min(len, per * (k + 1));
+      if (a1 > a0) th.emplace_back([=] { std::memcpy(buf + a0, s + off + a0, a1 - a0); });
+    }
+    std::memcpy(buf, s + off, std::min(len, per));
+    for (auto& x : th) x.join();
+    int rc = check_cuda(cudaMemcpyAsync(t + off, buf, len, cudaMemcpyHostToDevice, d.stream), what);
+    if (!rc) rc = check_cuda(cudaEventRecord(d.stage_ev[b], d.stream), what);
+    if (rc) return rc;
+    used[b] = true;
+  }
+  return check_cuda(cudaStreamSynchronize(d.stream), what);
+}
+
 int dev_alloc(Device& d, void** p, size_t bytes, const char* what) {
   *p = nullptr;
   if (bytes == 0) bytes = 256;
@@ -104,6 +155,10 @@ static void destroy_device(Device* d) {
   free_uploads(*d);
   if (d->ws) cudaFree(d->ws);
   if (d->pin) cudaFreeHost(d->pin);
+  for (int i = 0; i < 2; ++i) {
+    if (d->stage[i]) cudaFreeHost(d->stage[i]);
+    if (d->stage_ev[i]) cudaEventDestroy(d->stage_ev[i]);
+  }
   if (d->status) cudaFree(d->status);
   if (d->stream) cudaStreamDestroy(d->stream);
   for (cudaEvent_t e : d->evpool) cudaEventDestroy(e);

@@ -234,4 +234,12 @@ long long ecdbg_launches(void) {
   return G().launches;
 }
 
+int ecdbg_assign_rows(long long* tc_rows, long long* exact_rows, int reset) {
+  std::lock_guard<std::mutex> lk(G().stat_mu);
+  if (tc_rows) *tc_rows = G().assign_tc_rows;
+  if (exact_rows) *exact_rows = G().assign_exact_rows;
+  if (reset) G().assign_tc_rows = G().assign_exact_rows = 0;
+  return EC_OK;
+}
+
 }  // extern "C"

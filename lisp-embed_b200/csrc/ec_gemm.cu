@@ -103,7 +103,12 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   if (!encode_2d_bf16(&ta, g.A, g.M, g.K, g.lda, kGemmBM)) return cudaErrorInvalidValue;
   if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.ldw, BN / CG)) return cudaErrorInvalidValue;
   const uint64_t out_cols = (EPI == kEpiBf16Swiglu || EPI == kEpiBf16GeluTanhGate) ? g.N / 2 : g.N;
-  if (!encode_2d_out(&tc, g.out, Cfg::OUT_F32, g.M, out_cols, g.ldo)) return cudaErrorInvalidValue;
+  if constexpr (EPI == kEpiArgCand) {
+    // no dense output: the map is never used (any valid encoding will do)
+    if (!g.ac || !encode_2d_out(&tc, g.ac->mloc, true, 32, 32, 32)) return cudaErrorInvalidValue;
+  } else if (!encode_2d_out(&tc, g.out, Cfg::OUT_F32, g.M, out_cols, g.ldo)) {
+    return cudaErrorInvalidValue;
+  }
   GemmArgs a;
   a.M = g.M;
   a.N = g.N;
@@ -117,6 +122,8 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.num_tiles = ((g.M + kGemmBM * CG - 1) / (kGemmBM * CG)) * a.n_tiles_n;
   a.status = g.status;
   a.qk = QkRopeEpi{};
+  a.ac = ArgCandEpi{};
+  if constexpr (EPI == kEpiArgCand) a.ac = *g.ac;
   if constexpr (EPI == kEpiF32Resid || EPI == kEpiBf16GeluTanhMul) {
     // the epilogue reads 16-byte pieces of the residual / multiplier rows
     if (!g.resid || g.ldr % 4 || reinterpret_cast<uintptr_t>(g.resid) % 16)
@@ -153,6 +160,9 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
     case kEpiBf16GeluTanhMul:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16GeluTanhMul>(g, st, num_sms);
       return cudaErrorInvalidValue;
+    case kEpiArgCand:
+      if constexpr (BN == 128 || BN == 256) return run<BN, kEpiArgCand>(g, st, num_sms);
+      return cudaErrorInvalidValue;
     case kEpiBf16Swiglu:
       if constexpr (BN == 128 || BN == 256) return run<BN, kEpiBf16Swiglu>(g, st, num_sms);
       return cudaErrorInvalidValue;
@@ -161,7 +171,8 @@ static cudaError_t dispatch_epi(const GemmLaunch& g, cudaStream_t st, int num_sm
 }
 
 int gemm_pick_bn(int M, int N, int epi, int num_sms) {
-  if (epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate || epi == kEpiBf16GeluTanhMul)
+  if (epi == kEpiBf16Swiglu || epi == kEpiBf16GeluTanhGate || epi == kEpiBf16GeluTanhMul ||
+      epi == kEpiArgCand)
     return N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
   if (epi == kEpiBf16QkRope) return N % 256 == 0 ? 256 : 0;
   const int mt = (M + kGemmBM - 1) / kGemmBM;

@@ -42,6 +42,28 @@ enum GemmEpi : int {
                              // (gemma.lisp:277-283), SwiGLU's tile layout
   kEpiBf16GeluTanhMul = 7,   // out bf16 = gelu_tanh(acc) * resid, resid fp32
                              // [M, ldr] (the PLE gate, gemma.lisp:290-293)
+  kEpiArgCand = 8,           // no dense output: per row and column part the
+                             // best approximate score and the candidates for
+                             // the exact argmax (ArgCandEpi)
+};
+
+// k-means assignment prefilter (kEpiArgCand).  For row r and column part t
+// (= 2 * column tile + epilogue half) of the approximate scores S~ = bf16(x)
+// . bf16(c)^T: mloc[t][r] = the largest S~, col1/col2 = the columns of the
+// largest two, meta bit 0 = the second lies within w_r of the first, bit 1 =
+// the third-largest does too (then two columns do not cover the part and the
+// row needs the exact scan).  w_r = wscale * xnorm[r] is twice the bound on
+// |S~ - S| for that row, so the exact argmax -- and every column exactly tied
+// with it -- has S~ >= max S~ - w_r.  Arrays are [parts][M].  (w_r =
+// rel2 * cmax * xnorm[r]; wscale below is rel2 * cmax.)
+struct ArgCandEpi {
+  const float* xnorm;   // [M] upper bounds of the row norms
+  const float* cmax;    // [1] upper bound of the largest centroid norm
+  float rel2;           // 2 * relative bound: w_r = rel2 * cmax * xnorm[r]
+  float* mloc;
+  int* meta;
+  int* col1;
+  int* col2;
 };
 
 // per-head q/k RMSNorm + rotate-half RoPE applied in the QKV epilogue
@@ -68,6 +90,7 @@ struct GemmArgs {
   int num_tiles;       // ceil(M / 128) * n_tiles_n
   unsigned* status;    // device status word
   QkRopeEpi qk;        // kEpiBf16QkRope only
+  ArgCandEpi ac;       // kEpiArgCand only
 };
 
 constexpr int kGemmBM = 128;
@@ -82,12 +105,13 @@ constexpr int gemm_threads(int ew) { return (2 + ew) * 32; }
 // output drops by a third -- the mainloop is bound by L2 -> SM bandwidth).
 template <int BN, int EPI, int CG = 1>
 struct GemmCfg {
-  static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32;
+  static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32 || EPI == kEpiArgCand;
   // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
   // rows of 64 B (64B swizzle); two per epilogue warp
   // (kEpiBf16GeluTanhMul stages its fp32 multiplier chunk in the same slot)
   static constexpr uint32_t CHUNK_BYTES = (OUT_F32 || EPI == kEpiBf16GeluTanhMul) ? 4096 : 2048;
-  static constexpr uint32_t EPI_BYTES = kGemmEpiWarps * 2 * CHUNK_BYTES;
+  // (kEpiArgCand stores nothing through shared memory)
+  static constexpr uint32_t EPI_BYTES = EPI == kEpiArgCand ? 0 : kGemmEpiWarps * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t B_BYTES = (BN / CG) * kGemmBK * 2;  // this CTA's rows of W
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -342,6 +366,76 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;
+    if constexpr (EPI == kEpiArgCand) {
+      // the three largest approximate scores of this thread's row over its
+      // chunks (one compare per score once the list has filled)
+      const float wscale = args.ac.rel2 * *args.ac.cmax;
+      for (int tile = tile0; tile < args.num_tiles; tile += tstep) {
+        const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+        const int grow = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32 + lane;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN);
+        const float w = grow < args.M ? wscale * args.ac.xnorm[grow] : 0.f;
+        if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
+          report(args.status, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        float t1 = -INFINITY, t2 = -INFINITY, t3 = -INFINITY;
+        int c1 = 0, c2 = 0;
+#pragma unroll 1
+        for (int c = half; c < NCH; c += PARTS) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_wait_ld();
+          if (c + PARTS >= NCH) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release_acc(acc);
+          }
+          const int col0 = nb * BN + c * 32;
+          // values below (running max - w) can never be within w of the
+          // row's final max and need no bookkeeping: groups of 8 columns
+          // whose max lies below the window are skipped; in the others the
+          // top-three update is branch-free (selects), so lanes do not
+          // diverge
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float gm = __uint_as_float(r[8 * g]);
+#pragma unroll
+            for (int e = 1; e < 8; ++e) gm = fmaxf(gm, __uint_as_float(r[8 * g + e]));
+            const float thr = fmaxf(t1, gm) - w;
+            if (gm >= thr) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float v = __uint_as_float(r[8 * g + e]);
+                const int col = col0 + 8 * g + e;
+                const bool in = v >= thr;
+                const bool g1 = in && v > t1, g2 = in && v > t2, g3 = in && v > t3;
+                t3 = g2 ? t2 : (g3 ? v : t3);
+                c2 = g1 ? c1 : (g2 ? col : c2);
+                t2 = g1 ? t1 : (g2 ? v : t2);
+                c1 = g1 ? col : c1;
+                t1 = g1 ? v : t1;
+              }
+            }
+          }
+        }
+        if (grow < args.M) {
+          const size_t o = static_cast<size_t>(nb * PARTS + half) * args.M + grow;
+          const float lo = t1 - w;
+          // a row whose window is not a finite number takes the exact scan
+          const bool bad = !(w >= 0.f && w < INFINITY) || !(t1 > -INFINITY && t1 < INFINITY);
+          args.ac.mloc[o] = bad ? INFINITY : t1;
+          args.ac.meta[o] = (t2 >= lo ? 1 : 0) | ((t3 >= lo || bad) ? 2 : 0);
+          args.ac.col1[o] = c1;
+          args.ac.col2[o] = c2;
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
     // bias / GELU / fp32 epilogues: two chunks per step (two TMEM loads, one
     // wait, 64 independent element chains), accumulator handed back as soon
     // as the last TMEM read lands
@@ -540,7 +634,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    for (int tile = tile0; !kPaired && tile < args.num_tiles; tile += tstep) {
+    for (int tile = tile0; !kPaired && EPI != kEpiArgCand && tile < args.num_tiles; tile += tstep) {
       const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
       const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1

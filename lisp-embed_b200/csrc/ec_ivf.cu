@@ -4,11 +4,15 @@
 // processes after ec_comm_init); only k-means exchanges data, with one NCCL
 // all-reduce of the centroid sums + counts per Lloyd iteration.
 #include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 #include <vector>
 
 #include "ec_comm.h"
+#include "ec_gemm.cuh"
 #include "ec_ivf.h"
 #include "ec_state.h"
 
@@ -63,6 +67,129 @@ static void split(int64_t n, int parts, int k, int64_t* b, int64_t* e) {
   *e = std::min<int64_t>(n, per * (k + 1));
 }
 
+// ------------------------------------------------- tensor-core assignment --
+// ann::nearest-centroid for n device-resident rows: bf16 tcgen05 scores with
+// a rigorous error window, candidates re-scored exactly, the rest of the rows
+// through the exact scan (ec_ivf_tc.cu).  Identical results to launch_assign.
+struct TcAssign {
+  DBuf xb, xnorm, cb, cmax, mloc, meta, col1, col2, fbr, fbn, tmp;
+  int64_t n = 0;
+  int d = 0, k = 0, parts = 0;
+  float rel2 = 0.f;
+  bool ready = false;
+};
+
+static bool tc_assign_eligible(int64_t n, int d, int k) {
+  return getenv("EC_EXACT_ASSIGN") == nullptr && n > 0 && n < (int64_t{1} << 31) - 1 && d > 0 &&
+         d % 64 == 0 && d <= 8192 && k > 0 && k % 128 == 0;
+}
+
+// buffers for n rows and the rows' bf16 copy; t.ready stays false (and no
+// error is left set) when they do not fit, so the caller scans exactly
+static int tc_assign_setup(Device& dv, TcAssign& t, const float* X, int64_t n, int d, int k,
+                           cudaStream_t st) {
+  t.ready = false;
+  if (!tc_assign_eligible(n, d, k)) return EC_OK;
+  const int bn = gemm_pick_bn(static_cast<int>(std::min<int64_t>(n, 1 << 30)), k, kEpiArgCand,
+                              dv.num_sms);
+  if (!bn) return EC_OK;
+  t.n = n;
+  t.d = d;
+  t.k = k;
+  t.parts = 2 * (k / bn);
+  t.rel2 = 2.0f * argcand_rel(d);
+  const size_t pn = static_cast<size_t>(t.parts) * n;
+  const bool fit = !t.xb.alloc(dv, static_cast<size_t>(n) * d * 2, "assign rows bf16") &&
+                   !t.xnorm.alloc(dv, static_cast<size_t>(n) * 4, "assign row norms") &&
+                   !t.cb.alloc(dv, static_cast<size_t>(k) * d * 2, "assign centroids bf16") &&
+                   !t.cmax.alloc(dv, 256, "assign centroid norm") &&
+                   !t.mloc.alloc(dv, pn * 4, "assign part maxima") &&
+                   !t.meta.alloc(dv, pn * 4, "assign part flags") &&
+                   !t.col1.alloc(dv, pn * 4, "assign candidates") &&
+                   !t.col2.alloc(dv, pn * 4, "assign candidates") &&
+                   !t.fbr.alloc(dv, static_cast<size_t>(n) * 8, "assign exact rows") &&
+                   !t.fbn.alloc(dv, 256, "assign exact count") &&
+                   !t.tmp.alloc(dv, static_cast<size_t>(n) * 4, "assign exact results");
+  if (!fit) {
+    clear_error();  // not enough memory: the exact scan needs none of it
+    return EC_OK;
+  }
+  EC_TRY(check_cuda(launch_round_rows(X, n, d, t.xb.as<__nv_bfloat16>(), t.xnorm.as<float>(),
+                                      nullptr, st),
+                    "round rows"));
+  t.ready = true;
+  return EC_OK;
+}
+
+static int tc_assign_run(Device& dv, TcAssign& t, const float* X, const float* C, int32_t* out,
+                         cudaStream_t st) {
+  const int64_t n = t.n;
+  const int d = t.d, k = t.k;
+  EC_TRY(check_cuda(cudaMemsetAsync(t.cmax.p, 0, 4, st), "centroid norm clear"));
+  EC_TRY(check_cuda(launch_round_rows(C, k, d, t.cb.as<__nv_bfloat16>(), nullptr,
+                                      t.cmax.as<unsigned>(), st),
+                    "round centroids"));
+  ArgCandEpi ac{t.xnorm.as<float>(), t.cmax.as<float>(), t.rel2, t.mloc.as<float>(),
+                t.meta.as<int>(), t.col1.as<int>(), t.col2.as<int>()};
+  GemmLaunch g;
+  g.A = t.xb.as<__nv_bfloat16>();
+  g.lda = d;
+  g.W = t.cb.as<__nv_bfloat16>();
+  g.ldw = d;
+  g.M = static_cast<int>(n);
+  g.N = k;
+  g.K = d;
+  g.bias = nullptr;
+  g.resid = nullptr;
+  g.ldr = 0;
+  g.out = nullptr;
+  g.ldo = 0;
+  g.epi = kEpiArgCand;
+  g.bn = 0;
+  g.status = dv.status;
+  g.ac = &ac;
+  {
+    // event-timed while profiling (class 0: tensor-core GEMMs)
+    const int e0 = prof_begin(dv);
+    const cudaError_t e = launch_gemm(g, st, dv.num_sms);
+    prof_end(dv, 0, 2.0 * static_cast<double>(n) * k * d,
+             2.0 * static_cast<double>(n) * d + 2.0 * k * d + 16.0 * t.parts * n, e0);
+    EC_TRY(check_cuda(e, "assign scores"));
+  }
+  EC_TRY(check_cuda(cudaMemsetAsync(t.fbn.p, 0, 8, st), "exact count clear"));
+  {
+    const int e0 = prof_begin(dv);
+    const cudaError_t e = launch_argcand_reduce(
+        X, n, d, C, t.xnorm.as<float>(), t.cmax.as<float>(), t.rel2, t.parts, t.mloc.as<float>(),
+        t.meta.as<int>(), t.col1.as<int>(), t.col2.as<int>(), out, t.fbr.as<int64_t>(),
+        t.fbn.as<unsigned long long>(), st);
+    prof_end(dv, 2, 0.0, 16.0 * t.parts * n + 4.0 * n * d, e0);
+    EC_TRY(check_cuda(e, "assign candidates"));
+  }
+  unsigned long long nfb = 0;
+  EC_TRY(check_cuda(cudaMemcpyAsync(&nfb, t.fbn.p, 8, cudaMemcpyDeviceToHost, st), "exact count"));
+  EC_TRY(sync_and_check(dv, "assign scores"));
+  {
+    std::lock_guard<std::mutex> lk(G().stat_mu);
+    prof_collect(dv);
+  }
+  if (nfb > static_cast<unsigned long long>(n)) return set_error(EC_ECUDA, "assign: bad exact count");
+  if (nfb) {
+    EC_TRY(check_cuda(launch_assign(X, t.fbr.as<int64_t>(), static_cast<int64_t>(nfb), C, k, d,
+                                    t.tmp.as<int32_t>(), st),
+                      "assign exact rows"));
+    EC_TRY(check_cuda(launch_scatter_assign(t.fbr.as<int64_t>(), static_cast<int64_t>(nfb),
+                                            t.tmp.as<int32_t>(), out, st),
+                      "assign scatter"));
+  }
+  {
+    std::lock_guard<std::mutex> lk(G().stat_mu);
+    G().assign_tc_rows += n - static_cast<int64_t>(nfb);
+    G().assign_exact_rows += static_cast<int64_t>(nfb);
+  }
+  return EC_OK;
+}
+
 // ------------------------------------------------------------------ kmeans --
 static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t* sample,
                          int64_t j0, int64_t j1, int k, int iters, const float* cent0,
@@ -70,14 +197,33 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   Device& dv = *G().devs[li];
   EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
   const int64_t ns = j1 - j0;
-  // training rows of this shard, in sample order (ann.lisp:99-103)
-  std::vector<float> xs(static_cast<size_t>(std::max<int64_t>(ns, 1)) * d);
-  for (int64_t j = 0; j < ns; ++j)
-    std::memcpy(&xs[static_cast<size_t>(j) * d], x + sample[j0 + j] * d, static_cast<size_t>(d) * 4);
+  const bool trace = getenv("EC_TRACE_IVF") != nullptr;
+  auto t_start = std::chrono::steady_clock::now();
+  auto phase = [&](const char* what) {
+    if (!trace) return;
+    cudaStreamSynchronize(dv.stream);
+    const auto now = std::chrono::steady_clock::now();
+    fprintf(stderr, "[ec kmeans dev %d] %s %.1f ms\n", dv.ordinal, what,
+            std::chrono::duration<double, std::milli>(now - t_start).count());
+    t_start = now;
+  };
+  // training rows of this shard, in sample order (ann.lisp:99-103); a
+  // contiguous run of rows is uploaded from the caller's array directly
+  bool run = ns > 0;
+  for (int64_t j = 1; run && j < ns; ++j) run = sample[j0 + j] == sample[j0] + j;
+  std::vector<float> xs;
+  const float* src = run ? x + sample[j0] * d : nullptr;
+  if (!run) {
+    xs.resize(static_cast<size_t>(std::max<int64_t>(ns, 1)) * d);
+    for (int64_t j = 0; j < ns; ++j)
+      std::memcpy(&xs[static_cast<size_t>(j) * d], x + sample[j0 + j] * d, static_cast<size_t>(d) * 4);
+    src = xs.data();
+  }
   (void)n;
+  phase("gather");
   DBuf bx, bc, ba, bh, bcnt, boffs, bl, bs;
   const int64_t nt = sort_tiles(ns);
-  EC_TRY(bx.alloc(dv, xs.size() * 4, "kmeans rows"));
+  EC_TRY(bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * d * 4, "kmeans rows"));
   EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
   EC_TRY(ba.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "assignments"));
   EC_TRY(bh.alloc(dv, static_cast<size_t>(std::max<int64_t>(nt, 1)) * k * 4, "sort scratch"));
@@ -86,13 +232,20 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   EC_TRY(bl.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "lists"));
   EC_TRY(bs.alloc(dv, static_cast<size_t>(k) * (d + 1) * 4, "sums"));
   cudaStream_t st = dv.stream;
-  EC_TRY(check_cuda(cudaMemcpyAsync(bx.p, xs.data(), static_cast<size_t>(ns) * d * 4,
-                                    cudaMemcpyHostToDevice, st), "rows upload"));
+  EC_TRY(upload_h2d(dv, bx.p, src, static_cast<size_t>(ns) * d * 4, "rows upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent0, static_cast<size_t>(k) * d * 4,
                                     cudaMemcpyHostToDevice, st), "centroid upload"));
+  phase("alloc + upload");
+  TcAssign tc;
+  if (ns > 0) EC_TRY(tc_assign_setup(dv, tc, bx.as<float>(), ns, d, k, st));
+  phase("assign setup");
   for (int it = 0; it < iters; ++it) {
-    EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, ns, bc.as<float>(), k, d,
-                                    ba.as<int32_t>(), st), "assign"));
+    if (tc.ready) {
+      EC_TRY(tc_assign_run(dv, tc, bx.as<float>(), bc.as<float>(), ba.as<int32_t>(), st));
+    } else {
+      EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, ns, bc.as<float>(), k, d,
+                                      ba.as<int32_t>(), st), "assign"));
+    }
     EC_TRY(check_cuda(launch_lists(ba.as<int32_t>(), ns, k, bh.as<uint32_t>(), bcnt.as<uint32_t>(),
                                    boffs.as<int64_t>(), 0u, bl.as<uint32_t>(), st), "lists"));
     EC_TRY(check_cuda(launch_segsum(bx.as<float>(), bl.as<uint32_t>(), boffs.as<int64_t>(), k, d,
@@ -100,6 +253,7 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
     if (reduce)
       EC_TRY(comm_allreduce_sum_f32(li, bs.as<float>(), static_cast<size_t>(k) * (d + 1), st));
     EC_TRY(check_cuda(launch_update(bs.as<float>(), k, d, bc.as<float>(), st), "update"));
+    if (it == 0 || it + 1 == iters) phase(it == 0 ? "iteration 1" : "remaining iterations");
   }
   if (cent_out)
     EC_TRY(check_cuda(cudaMemcpyAsync(cent_out, bc.p, static_cast<size_t>(k) * d * 4,
@@ -132,12 +286,20 @@ static int assign_device(int li, const float* x, int64_t r0, int64_t r1, int d, 
   EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
   EC_TRY(ba.alloc(dv, static_cast<size_t>(m) * 4, "assignments"));
   cudaStream_t st = dv.stream;
-  EC_TRY(check_cuda(cudaMemcpyAsync(bx.p, src, static_cast<size_t>(m) * d * 4, cudaMemcpyHostToDevice, st),
-                    "rows upload"));
+  EC_TRY(upload_h2d(dv, bx.p, src, static_cast<size_t>(m) * d * 4, "rows upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice, st),
                     "centroid upload"));
-  EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, m, bc.as<float>(), k, d, ba.as<int32_t>(), st),
-                    "assign"));
+  {
+    TcAssign tc;
+    EC_TRY(tc_assign_setup(dv, tc, bx.as<float>(), m, d, k, st));
+    if (tc.ready) {
+      EC_TRY(tc_assign_run(dv, tc, bx.as<float>(), bc.as<float>(), ba.as<int32_t>(), st));
+    } else {
+      EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, m, bc.as<float>(), k, d,
+                                      ba.as<int32_t>(), st),
+                        "assign"));
+    }
+  }
   if (assign_out)
     EC_TRY(check_cuda(cudaMemcpyAsync(assign_out + r0, ba.p, static_cast<size_t>(m) * 4,
                                       cudaMemcpyDeviceToHost, st), "assign download"));
@@ -357,8 +519,7 @@ int ec_index_load(const float* x, int64_t n, int d, const float* centroids, int 
       return rc;
     };
     EC_TRY(take(reinterpret_cast<void**>(&ix.x), static_cast<size_t>(n) * d * 4, "index vectors"));
-    EC_TRY(check_cuda(cudaMemcpy(ix.x, x, static_cast<size_t>(n) * d * 4, cudaMemcpyHostToDevice),
-                      "vectors upload"));
+    EC_TRY(upload_h2d(*dv, ix.x, x, static_cast<size_t>(n) * d * 4, "vectors upload"));
     if (k > 0) {
       EC_TRY(take(reinterpret_cast<void**>(&ix.cent), static_cast<size_t>(k) * d * 4, "centroids"));
       EC_TRY(take(reinterpret_cast<void**>(&ix.lists), static_cast<size_t>(n) * 4, "lists"));

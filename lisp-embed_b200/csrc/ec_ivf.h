@@ -1,6 +1,7 @@
 // ec_ivf.h -- launchers of the IVF kernels (ec_ivf_kernels.cu).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -32,5 +33,24 @@ cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, cons
                              int64_t nq, int topk, unsigned long long* cand, cudaStream_t st);
 cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk,
                          int64_t* ids, float* scores, cudaStream_t st);
+
+// ---- tensor-core assignment (ec_ivf_tc.cu) ----------------------------------
+// relative bound on |bf16 score - exact score| / (|x| max|c|) for head dim d
+float argcand_rel(int d);
+// Xb = bf16(X) [n, d]; norms[r] >= |X[r]| (nullptr: skip); *nmax >= the
+// largest (nullptr: skip; the caller zeroes it first)
+cudaError_t launch_round_rows(const float* X, int64_t n, int d, __nv_bfloat16* Xb, float* norms,
+                              unsigned* nmax, cudaStream_t st);
+// exact argmax over each row's candidate columns (the kEpiArgCand GEMM's
+// output, `parts` column parts); rows that need the exact scan are appended
+// to fb_rows / *fb_count instead
+cudaError_t launch_argcand_reduce(const float* X, int64_t n, int d, const float* C,
+                                  const float* xnorm, const float* cmax, float rel2, int parts,
+                                  const float* mloc, const int* meta, const int* col1,
+                                  const int* col2, int32_t* out, int64_t* fb_rows,
+                                  unsigned long long* fb_count, cudaStream_t st);
+// out[fb_rows[i]] = vals[i]
+cudaError_t launch_scatter_assign(const int64_t* fb_rows, int64_t nfb, const int32_t* vals,
+                                  int32_t* out, cudaStream_t st);
 
 }  // namespace ec

@@ -152,7 +152,8 @@ cudaError_t launch_convert(int kind, const void* src, void* dst, size_t n, cudaS
 // 0 bf16, 1 bf16+gelu, 2 f32+resid, 3 bf16 swiglu, 4 f32, 5 bf16 with head
 // norms + RoPE, 6 bf16 gelu-tanh gate, 7 bf16 gelu-tanh * multiplier).  A and W bf16,
 // K-major; K % 64 == 0; N % bn == 0.  `bn` 0 = pick automatically.
-struct QkRopeEpi;  // ec_gemm.cuh
+struct QkRopeEpi;   // ec_gemm.cuh
+struct ArgCandEpi;  // ec_gemm.cuh
 struct GemmLaunch {
   const __nv_bfloat16* A;
   int lda;              // elements
@@ -168,6 +169,7 @@ struct GemmLaunch {
   int bn;
   unsigned* status;
   const QkRopeEpi* qk = nullptr;  // kEpiBf16QkRope (5)
+  const ArgCandEpi* ac = nullptr; // kEpiArgCand (8)
 };
 int gemm_pick_bn(int M, int N, int epi, int num_sms);
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms);

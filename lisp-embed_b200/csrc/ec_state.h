@@ -118,10 +118,14 @@ struct Device {
   void* pin = nullptr;
   size_t pin_bytes = 0;
   size_t allocated = 0;
+  // double-buffered pinned staging of large uploads (upload_h2d)
+  void* stage[2] = {nullptr, nullptr};
+  cudaEvent_t stage_ev[2] = {nullptr, nullptr};
 };
 
 struct Global {
   std::mutex mu;
+  std::mutex stat_mu;  // counters updated from per-device worker threads
   std::vector<Device*> devs;
   bool inited = false;
   size_t max_bytes = 0;  // EC_MAX_BYTES (0 = unlimited), per device
@@ -131,6 +135,8 @@ struct Global {
   bool sync_each = false;  // EC_SYNC_EACH_LAUNCH: wait for and report every forward launch
   ProfAcc prof[3];
   long long launches = 0;
+  long long assign_tc_rows = 0;     // rows the tensor-core assignment settled
+  long long assign_exact_rows = 0;  // rows that took the exact scan
   // multi-process communicator
   void* comm = nullptr;
   int rank = 0, world = 1;
@@ -149,6 +155,11 @@ int check_cuda(cudaError_t e, const char* what);
 // synchronise d.stream and translate both CUDA errors and the device status
 // word (bounded-wait timeouts) into a status code
 int sync_and_check(Device& d, const char* what);
+// Copy `bytes` of pageable host memory to device memory, enqueued on the
+// device's stream after the work already there; returns once the source may
+// be reused.  Large copies go through double-buffered pinned staging filled
+// by several host threads, so the host copy and the DMA overlap.
+int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* what);
 
 struct JVal;
 // build the model of config.json (+ pooling config) from d.uploads

@@ -27,6 +27,62 @@ def test_assign_exact(ec, corpus):
     assert np.array_equal(ann.assign(x, cent, rows=rows), oracle.assign(x, cent, rows=rows))
 
 
+def _assign_rows(ec):
+    import ctypes as C
+    tc, ex = C.c_longlong(), C.c_longlong()
+    ec.check(ec.lib().ecdbg_assign_rows(C.byref(tc), C.byref(ex), 1), "assign rows")
+    return tc.value, ex.value
+
+
+# d % 64 == 0 and k % 128 == 0: bf16 tensor-core scores with an error window,
+# candidates re-scored exactly; results must equal the exact scan bit for bit
+@pytest.mark.parametrize("k", [128, 384, 512])
+def test_assign_tensor_core_exact(ec, corpus, k):
+    x = corpus
+    rng = np.random.default_rng(k)
+    cent = x[rng.choice(len(x), k, replace=False)].copy()
+    _assign_rows(ec)
+    got = ann.assign(x, cent)
+    tc, _ = _assign_rows(ec)
+    assert tc > 0  # the tensor-core path ran
+    assert np.array_equal(got, oracle.assign(x, cent))
+
+
+def test_assign_tensor_core_ties_and_near_ties(ec, corpus):
+    """Duplicated centroids (exact ties: lowest index wins), clusters of
+    near-identical centroids (more candidates than one part keeps: those rows
+    take the exact scan), rows equal to centroids, a row too large for a
+    finite norm."""
+    x = corpus[:4000].copy()
+    rng = np.random.default_rng(7)
+    cent = x[rng.choice(len(x), 256, replace=False)].copy()
+    cent[200] = cent[3]                      # exact duplicate, higher index
+    cent[201] = cent[3]
+    for j in range(10, 16):                  # six near-copies of centroid 9
+        cent[j] = cent[9] + 1e-4 * rng.standard_normal(cent.shape[1]).astype(np.float32)
+    x[:50] = cent[rng.integers(0, 256, 50)]  # rows sitting on centroids
+    x[50] = cent[3]
+    x[51] = cent[9]
+    x[52, :] = 3e19                          # |x|^2 overflows single-float
+    _assign_rows(ec)
+    got = ann.assign(x, cent)
+    tc, exact = _assign_rows(ec)
+    assert tc > 0 and exact > 0
+    ref = oracle.assign(x, cent)
+    assert np.array_equal(got, ref)
+    assert got[50] == 3
+
+
+def test_kmeans_tensor_core_bit_exact(ec, corpus):
+    x = corpus
+    sample = synth.make_ivf_sample(len(x), 4)
+    _assign_rows(ec)
+    got = ann.kmeans(x, sample, 256, 4)
+    tc, _ = _assign_rows(ec)
+    assert tc > 0
+    assert np.array_equal(got, oracle.kmeans(x, sample, 256, 4))
+
+
 def test_assign_ties_lowest_index(ec):
     x = np.zeros((8, 8), np.float32)
     x[:, 0] = 1.0
