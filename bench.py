@@ -511,7 +511,9 @@ def main():
                        "tokens_per_rank": T, "parallelism": f"dp{world} (sequence shards)",
                        "l2": "flushed (256 MB write) between timed steps",
                        "precision": "bf16 tensor-core GEMM/attention, fp32 accumulate, "
-                                    "fp32 norms and residual stream"},
+                                    "fp32 norms; residual between sublayers: the "
+                                    "LayerNorm's bf16 output (BERT/MPNet), fp32 (Qwen3, "
+                                    "Gemma)"},
             "e2e": {"value": world * nseq * args.steps / e2e_s, "unit": "embeddings/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "timing": "host wall clock around the synchronous ec_embed_batch call"},
