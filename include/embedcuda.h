@@ -161,6 +161,42 @@ int ec_flat_search(const float *q, int nq, int topk, int64_t *ids, float *scores
 int ec_flat_search_noalloc(const float *d_x, int64_t n, int d, const float *d_q, int nq,
                            int topk, int64_t *d_ids, float *d_scores, void *stream);
 
+/* ---- index files (no reference counterpart in C; the formats are the
+ * reference's, with the dimension passed in instead of the constant 384 of
+ * ann.lisp:19 / kb.lisp:23 / embed.lisp:83) --------------------------------- */
+
+/* Write ann.bin: u32 0x414E4E31, k, dim, n; k x dim f32 centroids; k u32
+ * counts; n u32 row ids grouped by centroid.  Same bytes as ann::save-ann
+ * (ann.lisp:165-187).  counts must sum to n.  Needs no ec_init. */
+int ec_ann_save(const char *path, const float *centroids, int k, int d, int64_t n,
+                const uint32_t *counts, const uint32_t *lists);
+
+/* Read ann.bin (kb::load-ann, kb.lisp:283-314): writes k, d and n; fills the
+ * arrays that are not NULL (k x d, k, n elements).  A wrong magic or size is
+ * EC_EINVAL.  Needs no ec_init. */
+int ec_ann_read(const char *path, int *k, int *d, int64_t *n, float *centroids,
+                uint32_t *counts, uint32_t *lists);
+
+/* Make index.bin (rows of d f32, n = file size / 4d) and, when ann_path is not
+ * NULL, ann.bin resident on every device, reading the vectors from a mapping
+ * of the file (no host copy).  Replaces the vector and ann parts of
+ * kb::load-index (kb.lisp:84-129) and kb::load-ann (kb.lisp:283-314); same
+ * state as ec_index_load afterwards.  Writes n (may be NULL). */
+int ec_index_load_files(const char *index_path, int d, const char *ann_path, int64_t *n);
+
+/* ann:run from index.bin to ann.bin (ann.lisp:189-200): k-means over the rows
+ * sample[0..nsample) (centroids start at the first k of them), then
+ * assign-all and ann.bin.  The sample is explicit: the reference draws it
+ * with SBCL's random state (ann.lisp:57-67). */
+int ec_ann_build_file(const char *index_path, int d, int k, int iters, const int64_t *sample,
+                      int64_t nsample, const char *ann_path);
+
+/* ec_embed_batch, then the rows appended to index.bin the way embed:run
+ * writes them (embed.lisp:47-57, 99-101): ec_dim() f32 per sequence, input
+ * order. */
+int ec_embed_batch_to_file(const int32_t *ids, const int64_t *offsets, int nseq,
+                           const char *index_path);
+
 /* ---- multi-process (one process per GPU) ------------------------------------ */
 
 /* Size of the opaque NCCL unique id (128 bytes). */

@@ -61,6 +61,13 @@ _SIGS = {
     "ec_ivf_search": (C.c_int, [FP, C.c_int, C.c_int, C.c_int, I64P, FP]),
     "ec_flat_search": (C.c_int, [FP, C.c_int, C.c_int, I64P, FP]),
     "ec_flat_search_noalloc": (C.c_int, [P, C.c_int64, C.c_int, P, C.c_int, C.c_int, P, P, P]),
+    "ec_ann_save": (C.c_int, [C.c_char_p, FP, C.c_int, C.c_int, C.c_int64, U32P, U32P]),
+    "ec_ann_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int), I64P, FP, U32P,
+                              U32P]),
+    "ec_index_load_files": (C.c_int, [C.c_char_p, C.c_int, C.c_char_p, I64P]),
+    "ec_ann_build_file": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, I64P, C.c_int64,
+                                    C.c_char_p]),
+    "ec_embed_batch_to_file": (C.c_int, [I32P, I64P, C.c_int, C.c_char_p]),
     "ec_comm_id_size": (C.c_int, []),
     "ec_comm_get_id": (C.c_int, [P]),
     "ec_comm_init": (C.c_int, [C.c_int, C.c_int, P]),

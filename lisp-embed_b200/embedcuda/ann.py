@@ -1,7 +1,8 @@
 """IVF index build -- the ann.lisp mirror (ann.lisp:1-200).
 
 ``kmeans`` (ann::kmeans), ``assign_all`` (ann::assign-all), ``save_ann`` /
-``load_ann`` (the ann.bin format of ann.lisp:4-6, 165-187) and ``run``.
+``load_ann`` (the ann.bin format of ann.lisp:4-6, 165-187), ``run`` and
+``build_file`` (ann:run from index.bin to ann.bin in the library).
 The arithmetic runs in libembedcuda.so; ``sample`` is the explicit list of
 training rows whose first k rows initialise the centroids (ann.lisp:83-86).
 """
@@ -68,26 +69,44 @@ def assign_all(vecs, centroids):
 
 
 def save_ann(path, centroids, counts, lists, n):
-    """ann.bin: u32 magic, k, dim, n; k*dim f32; k u32 counts; n u32 ids."""
-    k, d = centroids.shape
-    with open(path, "wb") as f:
-        f.write(struct.pack("<4I", MAGIC, k, d, n))
-        f.write(np.ascontiguousarray(centroids, "<f4").tobytes())
-        f.write(np.ascontiguousarray(counts, "<u4").tobytes())
-        f.write(np.ascontiguousarray(lists, "<u4").tobytes())
+    """ann.bin: u32 magic, k, dim, n; k*dim f32; k u32 counts; n u32 ids
+    (ann::save-ann, ann.lisp:165-187), written by ec_ann_save."""
+    cent = np.ascontiguousarray(centroids, np.float32)
+    counts = np.ascontiguousarray(counts, np.uint32)
+    lists = np.ascontiguousarray(lists, np.uint32)
+    k, d = cent.shape
+    _lib.check(_lib.lib().ec_ann_save(str(path).encode(), _lib.ptr(cent, C.c_float), k, d, n,
+                                      _lib.ptr(counts, C.c_uint32), _lib.ptr(lists, C.c_uint32)),
+               "ann_save")
 
 
 def load_ann(path):
     """(centroids, counts, lists) from ann.bin, or None when the magic differs
-    (kb::load-ann, kb.lisp:283-314)."""
+    (kb::load-ann, kb.lisp:283-314), read by ec_ann_read."""
     with open(path, "rb") as f:
-        magic, k, d, n = struct.unpack("<4I", f.read(16))
-        if magic != MAGIC:
-            return None
-        cent = np.frombuffer(f.read(4 * k * d), "<f4").reshape(k, d).copy()
-        counts = np.frombuffer(f.read(4 * k), "<u4").copy()
-        lists = np.frombuffer(f.read(4 * n), "<u4").copy()
+        head = f.read(4)
+    if len(head) < 4 or struct.unpack("<I", head)[0] != MAGIC:
+        return None
+    k, d, n = C.c_int(), C.c_int(), C.c_int64()
+    L = _lib.lib()
+    _lib.check(L.ec_ann_read(str(path).encode(), C.byref(k), C.byref(d), C.byref(n), None, None,
+                             None), "ann_read")
+    cent = np.empty((k.value, d.value), np.float32)
+    counts = np.empty(k.value, np.uint32)
+    lists = np.empty(n.value, np.uint32)
+    _lib.check(L.ec_ann_read(str(path).encode(), C.byref(k), C.byref(d), C.byref(n),
+                             _lib.ptr(cent, C.c_float), _lib.ptr(counts, C.c_uint32),
+                             _lib.ptr(lists, C.c_uint32)), "ann_read")
     return cent, counts, lists
+
+
+def build_file(index_path, dim, k, iters, sample, ann_path):
+    """ann:run from index.bin to ann.bin inside the library (the vectors are
+    read from a mapping of index.bin, never copied into a host array)."""
+    sample = np.ascontiguousarray(sample, np.int64)
+    _lib.check(_lib.lib().ec_ann_build_file(str(index_path).encode(), dim, k, iters,
+                                            _lib.ptr(sample, C.c_int64), sample.size,
+                                            str(ann_path).encode()), "ann_build_file")
 
 
 def run(vecs, k=1024, iters=10, sample=None, seed=None, out_path=None):

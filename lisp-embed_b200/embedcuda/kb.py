@@ -37,6 +37,19 @@ def load_index(vectors, ann=None):
     _state.update(ivf=True, dim=d)
 
 
+def load_index_files(index_path, dim, ann_path=None):
+    """index.bin (rows of `dim` f32) and optionally ann.bin straight from the
+    files into device memory (kb::load-index + kb::load-ann, kb.lisp:84-129,
+    283-314, with the dimension passed in).  Returns n."""
+    _lib.init()
+    n = C.c_int64()
+    _lib.check(_lib.lib().ec_index_load_files(str(index_path).encode(), dim,
+                                              str(ann_path).encode() if ann_path else None,
+                                              C.byref(n)), "index_load_files")
+    _state.update(ivf=ann_path is not None, dim=dim)
+    return n.value
+
+
 def search_ivf(q, k, nprobe=None):
     q = np.ascontiguousarray(np.atleast_2d(q), np.float32)
     nq = q.shape[0]

@@ -80,3 +80,14 @@ def embed_batch_device(d_ids_ptr, offsets, nseq, d_out_ptr, out_stride, stream=N
                                                 nseq, C.c_void_p(d_out_ptr), out_stride,
                                                 C.c_void_p(stream) if stream else None),
                "embed_batch_device")
+
+
+def embed_batch_to_file(ids, offsets, index_path):
+    """embed_batch, then the rows appended to index.bin as embed:run writes
+    them (embed.lisp:47-57, 99-101)."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    offsets = np.ascontiguousarray(offsets, np.int64)
+    _lib.check(_lib.lib().ec_embed_batch_to_file(ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                                                 offsets.ctypes.data_as(C.POINTER(C.c_int64)),
+                                                 offsets.size - 1, str(index_path).encode()),
+               "embed_batch_to_file")

@@ -10,6 +10,8 @@
 ;;;;   (cuda:kmeans vecs sample k iters)  ; ann::kmeans
 ;;;;   (cuda:assign-all vecs n centroids k)
 ;;;;   (cuda:index-load vecs n centroids counts lists)
+;;;;   (cuda:index-load-files "index.bin" :ann-path "ann.bin" :dim 384)
+;;;;   (cuda:ann-build-file "index.bin" "ann.bin" sample k iters)  ; ann:run
 ;;;;   (cuda:top-k q k)                   ; kb::top-k
 ;;;;
 ;;;; Every foreign call returns an int status; a negative status becomes a
@@ -20,7 +22,8 @@
 (defpackage :cuda
   (:use :cl)
   (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
-           #:kmeans #:assign-all #:index-load #:top-k #:top-k-brute #:*nprobe*))
+           #:kmeans #:assign-all #:index-load #:index-load-files #:ann-build-file
+           #:top-k #:top-k-brute #:*nprobe*))
 (in-package :cuda)
 
 (defparameter *library* (or (sb-ext:posix-getenv "EC_LIBRARY") "libembedcuda.so"))
@@ -63,6 +66,14 @@
 (sb-alien:define-alien-routine ("ec_flat_search" %flat-search) sb-alien:int
   (q sb-sys:system-area-pointer) (nq sb-alien:int) (topk sb-alien:int)
   (ids sb-sys:system-area-pointer) (scores sb-sys:system-area-pointer))
+
+(sb-alien:define-alien-routine ("ec_index_load_files" %index-load-files) sb-alien:int
+  (index-path sb-alien:c-string) (d sb-alien:int) (ann-path sb-alien:c-string)
+  (n sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_ann_build_file" %ann-build-file) sb-alien:int
+  (index-path sb-alien:c-string) (d sb-alien:int) (k sb-alien:int) (iters sb-alien:int)
+  (sample sb-sys:system-area-pointer) (nsample (sb-alien:signed 64))
+  (ann-path sb-alien:c-string))
 
 (defun check (rc what)
   (when (minusp rc)
@@ -194,6 +205,27 @@ training row indices; its first K rows initialise the centroids."
     (with-saps ((xp vecs) (cp centroids) (np counts) (lp lists))
       (check (%index-load xp n dim cp k np lp) "ec_index_load"))
     (setf *ivf* (plusp k))))
+
+(defun index-load-files (index-path &key ann-path (dim 384))
+  "kb::load-index's vectors + kb::load-ann straight from index.bin / ann.bin
+into device memory (no Lisp array of the vectors).  Returns n."
+  (let ((n (make-array 1 :element-type '(signed-byte 64))))
+    (with-saps ((np n))
+      (check (%index-load-files (namestring index-path) dim
+                                (and ann-path (namestring ann-path)) np)
+             "ec_index_load_files"))
+    (setf *ivf* (and ann-path t))
+    (aref n 0)))
+
+(defun ann-build-file (index-path ann-path sample k iters &key (dim 384))
+  "ann:run from index.bin to ann.bin in the library; SAMPLE is the vector of
+training row ids (ann::random-sample's result), its first K rows the initial
+centroids."
+  (let ((sv (coerce sample '(simple-array (signed-byte 64) (*)))))
+    (with-saps ((sp sv))
+      (check (%ann-build-file (namestring index-path) dim k iters sp (length sv)
+                              (namestring ann-path))
+             "ec_ann_build_file"))))
 
 (defun %search (q k ivf)
   (let ((ids (make-array k :element-type '(signed-byte 64)))

@@ -396,3 +396,20 @@ def top_k_brute(vecs, q, topk, threads=8):
 
 def mpnet_bucket(i, j):
     return lib().or_mpnet_bucket(C.c_int(i), C.c_int(j))
+
+
+def ann_bytes(cent, counts, lists, n):
+    """The bytes ann::save-ann writes (ann.lisp:165-187): u32 0x414E4E31, k,
+    dim, n (write-u32 of each), then the centroids' f32 bit patterns, the k
+    counts and the n row ids, all as little-endian (unsigned-byte 32)."""
+    import struct
+    cent = np.ascontiguousarray(cent, np.float32)
+    k, dim = cent.shape
+    return (struct.pack("<4I", 0x414E4E31, k, dim, n) + cent.astype("<f4").tobytes()
+            + np.asarray(counts, "<u4").tobytes() + np.asarray(lists, "<u4").tobytes())
+
+
+def index_bytes(rows):
+    """index.bin as embed::write-f32 appends it (embed.lisp:47-57): each row's
+    f32 bit patterns, little-endian, no header."""
+    return np.ascontiguousarray(rows, np.float32).astype("<f4").tobytes()
