@@ -53,7 +53,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["ivf", "query"], default="minilm")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["ivf", "query", "tokenize"], default="minilm")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -380,6 +380,68 @@ def run_reference(args, rank):
     return 0
 
 
+def run_tokenize(args, rank):
+    """tokenizer.lisp's tk-encode on the host: texts/s of ec_tokenize (C++,
+    all host threads) over 20,000 synthetic sentences of 16..256 words, with
+    the WordPiece tokenizer.json fixture (700-piece vocabulary, lowercase,
+    [CLS]/[SEP]).  cpu_baseline: the Python restatement of tokenizer.lisp on
+    one thread over a bounded sample (the Lisp itself needs SBCL)."""
+    if rank != 0:
+        return 0
+    import random
+    from embedcuda.tokenizer import Tokenizer
+    tok_json = os.path.join(REPO, "tests", "golden", "tok", "wordpiece.json")
+    rng = random.Random(11)
+    syl = ["ka", "to", "ri", "na", "mo", "se", "lu", "pe", "di", "ga", "vo", "stra", "ble",
+           "ing", "tion", "er", "ed", "ly", "pre", "un", "re", "ment", "ness"]
+    punct = [",", ".", "!", "?", ";", "(", ")"]
+
+    def sentence():
+        words = []
+        for _ in range(rng.randint(16, 256)):
+            r = rng.random()
+            words.append(rng.choice(punct) if r < 0.08 else str(rng.randint(0, 9999)) if r < 0.14
+                         else "".join(rng.choice(syl) for _ in range(rng.randint(1, 4))))
+        return " ".join(words)
+
+    texts = [sentence() for _ in range(20000)]
+    tk = Tokenizer.from_json(tok_json)
+    for _ in range(args.warmup):
+        tk.encode_batch(texts[:2000])
+    times = []
+    ntok = 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ids, offs = tk.encode_batch(texts)
+        times.append(time.perf_counter() - t0)
+        ntok = int(offs[-1])
+    el = sum(times)
+    threads = os.cpu_count() or 1
+    value = len(texts) * args.steps / el
+    out = {"metric": "texts/s", "value": value, "unit": "texts/s", "n_gpus": 0,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+           "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "utf-8",
+           "data": "synthetic", "config": {"workload": "tokenize (tk-encode, WordPiece)",
+                                           "texts_per_step": len(texts),
+                                           "tokens_per_step": ntok, "threads": threads},
+           "tokens_per_s": ntok * args.steps / el}
+    if not args.no_cpu_baseline:
+        from oracle import tokenizer_ref
+        r = tokenizer_ref.from_json(tok_json)
+        t0 = time.perf_counter()
+        done = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0) and done < len(texts):
+            r.encode(texts[done])
+            done += 1
+        rel = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": done / rel, "unit": "texts/s", "cores": 1, "kind": "port",
+                               "sample": f"{done} texts in {rel:.1f} s (Python restatement of "
+                                         "tokenizer.lisp, one thread)"}
+    print(json.dumps(out), flush=True)
+    tk.close()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.warmup < 3:
@@ -388,7 +450,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        if args.workload in ("ivf", "query"):
+        if args.workload in ("ivf", "query", "tokenize"):
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable":
                                   "reference arm is timed for the embedding workloads only"}))
@@ -400,6 +462,8 @@ def main():
         return run_ivf(args, rank, world, local_rank)
     if args.workload == "query":
         return run_query(args, rank, local_rank)
+    if args.workload == "tokenize":
+        return run_tokenize(args, rank)
 
     # NCCL's version banner goes to stdout; the benchmark prints one JSON line
     if not os.environ.get("EC_KEEP_NCCL_DEBUG"):

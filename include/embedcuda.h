@@ -197,6 +197,41 @@ int ec_ann_build_file(const char *index_path, int d, int k, int iters, const int
 int ec_embed_batch_to_file(const int32_t *ids, const int64_t *offsets, int nseq,
                            const char *index_path);
 
+/* ---- tokenizer (tokenizer.lisp) ----------------------------------------------
+ * Host-only (no GPU, no ec_init).  A tokenizer is a handle > 0; it is
+ * read-only after loading, so any number of threads may tokenize with it. */
+
+/* make-tokenizer-from-json (tokenizer.lisp:515-552): HF tokenizer.json with a
+ * WordPiece or BPE model; specials from the post-processor (json-specials,
+ * :465-498), pre-tokenizer family from its regex (pretok-mode, :500-513). */
+int ec_tokenizer_from_json(const char *path, int *handle);
+/* make-tokenizer :wordpiece (tokenizer.lisp:126-140, bert.lisp:45): vocab.txt,
+ * one token per line, id = line number. */
+int ec_tokenizer_wordpiece(const char *vocab_txt, int lowercase, int *handle);
+/* make-tokenizer :bpe (tokenizer.lisp:141-173; bert.lisp:47-53, llama.lisp:76-80):
+ * vocab.json + merges.txt.  NULL special-token names keep the defaults
+ * "[CLS]", "[SEP]", "[UNK]"; bos_id / eos_id < 0: none. */
+int ec_tokenizer_bpe(const char *vocab_json, const char *merges_txt, int lowercase,
+                     int byte_level, int llama3, const char *cls_token, const char *sep_token,
+                     const char *unk_token, int bos_id, int eos_id, int *handle);
+/* make-tokenizer :unigram (tokenizer.lisp:174-197): {token: log score}. */
+int ec_tokenizer_unigram(const char *scores_json, int lowercase, int *handle);
+int ec_tokenizer_free(int handle);
+/* Number of ids of the vocabulary (tk-vocab-size, tokenizer.lisp:254). */
+int ec_tokenizer_vocab_size(int handle);
+/* tk-encode (tokenizer.lisp:201-244) of ntexts UTF-8 texts (texts[i] of
+ * lengths[i] bytes, or NUL-terminated when lengths is NULL) on nthreads host
+ * threads (<= 0: all cores).  Ids are packed into ids[0..offsets[ntexts]) with
+ * text i at [offsets[i], offsets[i+1]) -- the layout ec_embed_batch takes.
+ * Each text yields at most 512 ids.  If they do not fit `cap`, the call fails
+ * with EC_EINVAL after filling offsets (offsets[ntexts] = the count needed). */
+int ec_tokenize(int handle, const char *const *texts, const int64_t *lengths, int ntexts,
+                int32_t *ids, int64_t cap, int64_t *offsets, int nthreads);
+/* tk-decode (tokenizer.lisp:246-252): the tokens of ids concatenated into
+ * out (UTF-8, not NUL-terminated); *len = the byte count. */
+int ec_tokenizer_decode(int handle, const int32_t *ids, int n, char *out, int64_t cap,
+                        int64_t *len);
+
 /* ---- multi-process (one process per GPU) ------------------------------------ */
 
 /* Size of the opaque NCCL unique id (128 bytes). */

@@ -1,4 +1,5 @@
-// ec_json.h -- minimal JSON reader for config.json / 1_Pooling/config.json.
+// ec_json.h -- minimal JSON reader for config.json / 1_Pooling/config.json /
+// tokenizer.json.
 //
 // Numbers with '.', 'e' or 'E' are converted exactly the way json.lisp's
 // parse-number does (json.lisp:79-113): integer digits accumulated in a
@@ -24,6 +25,7 @@ struct JVal {
   std::string s;
   std::vector<JVal> a;
   std::map<std::string, JVal> o;
+  std::vector<std::string> keys;  // object keys in file order (first occurrence)
 
   const JVal* get(const std::string& k) const {
     if (kind != Obj) return nullptr;
@@ -109,6 +111,7 @@ class JParser {
       if (next() != ':') throw std::string("json: expected ':'");
       JVal x;
       value(x);
+      if (v.o.find(k) == v.o.end()) v.keys.push_back(k);
       v.o[k] = std::move(x);
       ws();
       char c = next();
@@ -134,6 +137,18 @@ class JParser {
       if (c != ',') throw std::string("json: expected ',' or ']'");
     }
   }
+  unsigned hex4() {
+    unsigned cp = 0;
+    for (int k = 0; k < 4; ++k) {
+      char h = next();
+      cp <<= 4;
+      if (h >= '0' && h <= '9') cp |= h - '0';
+      else if (h >= 'a' && h <= 'f') cp |= h - 'a' + 10;
+      else if (h >= 'A' && h <= 'F') cp |= h - 'A' + 10;
+      else throw std::string("json: bad \\u escape");
+    }
+    return cp;
+  }
   void str(std::string& out) {
     if (next() != '"') throw std::string("json: expected string");
     while (true) {
@@ -148,21 +163,30 @@ class JParser {
           case 'b': out += '\b'; break;
           case 'f': out += '\f'; break;
           case 'u': {
-            unsigned cp = 0;
-            for (int k = 0; k < 4; ++k) {
-              char h = next();
-              cp <<= 4;
-              if (h >= '0' && h <= '9') cp |= h - '0';
-              else if (h >= 'a' && h <= 'f') cp |= h - 'a' + 10;
-              else if (h >= 'A' && h <= 'F') cp |= h - 'A' + 10;
-              else throw std::string("json: bad \\u escape");
+            unsigned cp = hex4();
+            // a high surrogate followed by an escaped low one is one
+            // supplementary character
+            if (cp >= 0xD800 && cp < 0xDC00 && p_ + 1 < s_.size() && s_[p_] == '\\' &&
+                s_[p_ + 1] == 'u') {
+              const size_t save = p_;
+              p_ += 2;
+              const unsigned lo = hex4();
+              if (lo >= 0xDC00 && lo < 0xE000)
+                cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+              else
+                p_ = save;
             }
             if (cp < 0x80) out += static_cast<char>(cp);
             else if (cp < 0x800) {
               out += static_cast<char>(0xC0 | (cp >> 6));
               out += static_cast<char>(0x80 | (cp & 0x3F));
-            } else {
+            } else if (cp < 0x10000) {
               out += static_cast<char>(0xE0 | (cp >> 12));
+              out += static_cast<char>(0x80 | ((cp >> 6) & 0x3F));
+              out += static_cast<char>(0x80 | (cp & 0x3F));
+            } else {
+              out += static_cast<char>(0xF0 | (cp >> 18));
+              out += static_cast<char>(0x80 | ((cp >> 12) & 0x3F));
               out += static_cast<char>(0x80 | ((cp >> 6) & 0x3F));
               out += static_cast<char>(0x80 | (cp & 0x3F));
             }

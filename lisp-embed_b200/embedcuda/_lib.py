@@ -68,6 +68,16 @@ _SIGS = {
     "ec_ann_build_file": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, I64P, C.c_int64,
                                     C.c_char_p]),
     "ec_embed_batch_to_file": (C.c_int, [I32P, I64P, C.c_int, C.c_char_p]),
+    "ec_tokenizer_from_json": (C.c_int, [C.c_char_p, C.POINTER(C.c_int)]),
+    "ec_tokenizer_wordpiece": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(C.c_int)]),
+    "ec_tokenizer_bpe": (C.c_int, [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_char_p,
+                                   C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "ec_tokenizer_unigram": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(C.c_int)]),
+    "ec_tokenizer_free": (C.c_int, [C.c_int]),
+    "ec_tokenizer_vocab_size": (C.c_int, [C.c_int]),
+    "ec_tokenize": (C.c_int, [C.c_int, C.POINTER(C.c_char_p), I64P, C.c_int, I32P, C.c_int64,
+                              I64P, C.c_int]),
+    "ec_tokenizer_decode": (C.c_int, [C.c_int, I32P, C.c_int, C.c_char_p, C.c_int64, I64P]),
     "ec_comm_id_size": (C.c_int, []),
     "ec_comm_get_id": (C.c_int, [P]),
     "ec_comm_init": (C.c_int, [C.c_int, C.c_int, P]),

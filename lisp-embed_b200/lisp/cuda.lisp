@@ -7,6 +7,7 @@
 ;;;;                                      ; bert:load-model / llama:load-model
 ;;;;   (cuda:embed-ids ids)               ; one sequence of token ids
 ;;;;   (cuda:embed-batch list-of-id-vectors)
+;;;;   (cuda:load-tokenizer "tokenizer.json") (cuda:embed-texts list-of-strings)
 ;;;;   (cuda:kmeans vecs sample k iters)  ; ann::kmeans
 ;;;;   (cuda:assign-all vecs n centroids k)
 ;;;;   (cuda:index-load vecs n centroids counts lists)
@@ -22,6 +23,7 @@
 (defpackage :cuda
   (:use :cl)
   (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
+           #:load-tokenizer #:embed-texts
            #:kmeans #:assign-all #:index-load #:index-load-files #:ann-build-file
            #:top-k #:top-k-brute #:*nprobe*))
 (in-package :cuda)
@@ -74,6 +76,13 @@
   (index-path sb-alien:c-string) (d sb-alien:int) (k sb-alien:int) (iters sb-alien:int)
   (sample sb-sys:system-area-pointer) (nsample (sb-alien:signed 64))
   (ann-path sb-alien:c-string))
+
+(sb-alien:define-alien-routine ("ec_tokenizer_from_json" %tokenizer-from-json) sb-alien:int
+  (path sb-alien:c-string) (handle sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_tokenize" %tokenize) sb-alien:int
+  (handle sb-alien:int) (texts sb-sys:system-area-pointer) (lengths sb-sys:system-area-pointer)
+  (ntexts sb-alien:int) (ids sb-sys:system-area-pointer) (cap (sb-alien:signed 64))
+  (offsets sb-sys:system-area-pointer) (nthreads sb-alien:int))
 
 (defun check (rc what)
   (when (minusp rc)
@@ -226,6 +235,43 @@ centroids."
       (check (%ann-build-file (namestring index-path) dim k iters sp (length sv)
                               (namestring ann-path))
              "ec_ann_build_file"))))
+
+(defvar *tokenizer* 0)
+
+(defun load-tokenizer (path)
+  "make-tokenizer-from-json in the library; later EMBED-TEXTS calls use it."
+  (let ((h (make-array 1 :element-type '(signed-byte 32))))
+    (with-saps ((hp h))
+      (check (%tokenizer-from-json (namestring path) hp) "ec_tokenizer_from_json"))
+    (setf *tokenizer* (aref h 0))))
+
+(defun embed-texts (texts)
+  "tk-encode of every text on the library's host threads, then one batched
+forward (model:embed for a list of texts, in input order)."
+  (let* ((n (length texts))
+         (octets (mapcar (lambda (s) (sb-ext:string-to-octets s :external-format :utf-8)) texts))
+         (total (reduce #'+ octets :key #'length))
+         (buf (make-array (max 1 total) :element-type '(unsigned-byte 8)))
+         (lens (make-array n :element-type '(signed-byte 64)))
+         (ptrs (make-array n :element-type '(unsigned-byte 64)))
+         (offs (make-array (1+ n) :element-type '(signed-byte 64)))
+         (ids (make-array (* 512 (max 1 n)) :element-type '(signed-byte 32))))
+    (let ((pos 0) (i 0))
+      (dolist (o octets)
+        (replace buf o :start1 pos)
+        (setf (aref lens i) (length o))
+        (incf pos (length o))
+        (incf i)))
+    (sb-sys:with-pinned-objects (buf lens ptrs offs ids)
+      (let ((base (sb-sys:sap-int (sb-sys:vector-sap buf))) (pos 0))
+        (dotimes (i n)
+          (setf (aref ptrs i) (+ base pos))
+          (incf pos (aref lens i))))
+      (check (%tokenize *tokenizer* (sb-sys:vector-sap ptrs) (sb-sys:vector-sap lens) n
+                        (sb-sys:vector-sap ids) (length ids) (sb-sys:vector-sap offs) 0)
+             "ec_tokenize"))
+    (embed-batch (loop for i below n
+                       collect (subseq ids (aref offs i) (aref offs (1+ i)))))))
 
 (defun %search (q k ivf)
   (let ((ids (make-array k :element-type '(signed-byte 64)))

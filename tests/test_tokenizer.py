@@ -1,0 +1,146 @@
+"""tokenizer.lisp in the library (ec_tokenizer.cu) against the committed
+golden ids of its Python restatement (oracle/tokenizer_ref.py) on tokenizers
+trained for the purpose (tests/golden/make_tokenizers.py): WordPiece and
+byte-level BPE from tokenizer.json, vocab.txt and vocab.json + merges.txt,
+GPT-2 and Llama-3 style pre-tokenizers, Unigram scores.  Host-only: no GPU."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from embedcuda import _lib
+from embedcuda.tokenizer import Tokenizer
+from oracle import tokenizer_ref as ref
+
+TOK = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tok")
+
+
+def _p(name):
+    return os.path.join(TOK, name)
+
+
+@pytest.fixture(scope="module")
+def texts():
+    with open(_p("texts.json"), encoding="utf-8") as f:
+        return json.load(f)
+
+
+@pytest.fixture(scope="module")
+def expected():
+    with open(_p("expected.json")) as f:
+        return json.load(f)
+
+
+def _bpe_ids():
+    with open(_p("bpe_gpt2.json"), encoding="utf-8") as f:
+        v = json.load(f)["model"]["vocab"]
+    return v["<s>"], v["</s>"]
+
+
+def _ours(name):
+    if name == "wordpiece_json":
+        return Tokenizer.from_json(_p("wordpiece.json"))
+    if name == "bpe_gpt2_json":
+        return Tokenizer.from_json(_p("bpe_gpt2.json"))
+    if name == "bpe_llama3_json":
+        return Tokenizer.from_json(_p("bpe_llama3.json"))
+    if name == "wordpiece_txt":
+        return Tokenizer.wordpiece(_p("vocab.txt"))
+    if name == "bpe_files":
+        bos, eos = _bpe_ids()
+        return Tokenizer.bpe(_p("vocab.json"), _p("merges.txt"), lowercase=False, byte_level=True,
+                             llama3=True, unk_token="<unk>", bos=bos, eos=eos)
+    if name == "unigram":
+        return Tokenizer.unigram(_p("unigram.json"))
+    raise KeyError(name)
+
+
+NAMES = ["wordpiece_json", "bpe_gpt2_json", "bpe_llama3_json", "wordpiece_txt", "bpe_files",
+         "unigram"]
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_library_matches_golden(texts, expected, name):
+    tk = _ours(name)
+    ids, offs = tk.encode_batch(texts)
+    got = [ids[offs[i]:offs[i + 1]].tolist() for i in range(len(texts))]
+    for i, (g, e) in enumerate(zip(got, expected[name])):
+        assert g == e, (name, i, texts[i][:60])
+    # one text at a time and a single thread give the same ids
+    ids1, offs1 = tk.encode_batch(texts, threads=1)
+    assert np.array_equal(ids1, ids) and np.array_equal(offs1, offs)
+    assert tk.encode(texts[3]).tolist() == expected[name][3]
+    tk.close()
+
+
+def test_restatement_matches_golden(texts, expected):
+    """The oracle itself, recomputed, against its committed output."""
+    tk = ref.from_json(_p("bpe_llama3.json"))
+    assert [tk.encode(t) for t in texts] == expected["bpe_llama3_json"]
+    tk = ref.from_json(_p("wordpiece.json"))
+    assert [tk.encode(t) for t in texts] == expected["wordpiece_json"]
+
+
+def test_restatement_pinned_to_hf_tokenizers(texts):
+    """Where tokenizer.lisp and Hugging Face tokenizers do the same thing --
+    ASCII text, single spaces, no apostrophes, WordPiece with the usual
+    advance (the Lisp's counts the "##") -- the restatement equals HF."""
+    hf = pytest.importorskip("tokenizers")
+    wp_hf = hf.Tokenizer.from_file(_p("wordpiece.json"))
+    bpe_hf = hf.Tokenizer.from_file(_p("bpe_gpt2.json"))
+    wp = ref.from_json(_p("wordpiece.json"))
+    wp.lisp_advance = False
+    bpe = ref.from_json(_p("bpe_gpt2.json"))
+    n = 0
+    for t in texts[160:240]:
+        if "'" in t:
+            continue
+        assert wp_hf.encode(t).ids == wp.encode(t)
+        assert bpe_hf.encode(t).ids == bpe.encode(t)
+        n += 1
+    assert n >= 30
+
+
+def test_lisp_quirks_reproduced():
+    tk = Tokenizer.from_json(_p("wordpiece.json"))
+    r = ref.from_json(_p("wordpiece.json"))
+    long_word = "x" * 101                       # > 100 characters -> [UNK]
+    assert tk.encode(long_word).tolist() == r.encode(long_word)
+    assert r.inv[r.encode(long_word)[1]] == "[UNK]"
+    u = Tokenizer.unigram(_p("unigram.json"))   # Viterbi ids looked up as strings -> [UNK]
+    ids = u.encode("kato rina").tolist()
+    assert len(ids) >= 2 and len(set(ids)) == 1
+    tk.close()
+    u.close()
+
+
+def test_truncation_and_decode(texts):
+    tk = Tokenizer.from_json(_p("bpe_gpt2.json"))
+    r = ref.from_json(_p("bpe_gpt2.json"))
+    long = texts[-1]
+    ids = tk.encode(long)
+    assert len(ids) == 512 and ids.tolist() == r.encode(long)   # BOS + 510 + EOS
+    assert tk.decode(ids[:20]) == r.decode(ids[:20].tolist())
+    tk.close()
+
+
+def test_errors():
+    tk = Tokenizer.from_json(_p("wordpiece.json"))
+    import ctypes as C
+    bad = (C.c_char_p * 1)(b"ok \xff\xfe")
+    offs = np.zeros(2, np.int64)
+    ids = np.zeros(16, np.int32)
+    rc = _lib.lib().ec_tokenize(tk.handle, bad, None, 1, _lib.ptr(ids, C.c_int32), 16,
+                                _lib.ptr(offs, C.c_int64), 1)
+    assert rc == _lib.EC_EINVAL                  # malformed UTF-8
+    good = (C.c_char_p * 1)(b"kato rina mose " * 20)
+    rc = _lib.lib().ec_tokenize(tk.handle, good, None, 1, _lib.ptr(ids, C.c_int32), 4,
+                                _lib.ptr(offs, C.c_int64), 1)
+    assert rc == _lib.EC_EINVAL and offs[1] > 4   # the count needed is reported
+    with pytest.raises(_lib.EcError):
+        Tokenizer.from_json(_p("texts.json"))    # not a tokenizer.json
+    tk.close()
+    with pytest.raises(_lib.EcError):
+        tk.handle = 12345
+        tk.vocab_size()
