@@ -33,6 +33,15 @@ int ecdbg_mlp(const void *A, const void *W1, const void *W2, const float *b1, co
 int ecdbg_gemm_ln(const void *A, const void *W, int M, int N, int K, const float *bias,
                   const float *resid, const float *ln_g, const float *ln_b, float *out32,
                   void *outb);
+/* The same cluster GEMM with an RMSNorm epilogue (x = A . W^T, fp32 rows):
+ * mode 1: out32 = x + resid, outb = RMSNorm(out32) * g1;
+ * mode 2: out32 = (resid + RMSNorm(x) * g1) [* scale when has_scale],
+ *         outb = RMSNorm(out32) * g2, or bf16(out32) when g2 is NULL;
+ * mode 3: out32 = RMSNorm(x * scale) * g1 (outb may be NULL).
+ * RMSNorm(v) = v / sqrt(mean(v^2) + eps).  N in {512, 768, 1024}. */
+int ecdbg_gemm_norm(const void *A, const void *W, int M, int N, int K, const float *resid,
+                    const float *g1, const float *g2, float *out32, void *outb, int mode,
+                    float eps, float scale, int has_scale);
 
 /* Varlen attention over packed bf16 rows qkv[T, ld]; cu[nseq + 1] (device,
  * int32) token offsets; lens on the host.  out[T, heads * head_dim] bf16. */

@@ -101,6 +101,29 @@ int ecdbg_gemm_ln(const void* A, const void* W, int M, int N, int K, const float
   return sync_and_check(d, "gemm+layernorm");
 }
 
+int ecdbg_gemm_norm(const void* A, const void* W, int M, int N, int K, const float* resid,
+                    const float* g1, const float* g2, float* out32, void* outb, int mode, float eps,
+                    float scale, int has_scale) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!gemm_rms_supported(N)) return set_error(EC_EUNSUPPORTED, "gemm+rmsnorm N %d", N);
+  if (!A || !W || !g1 || mode < 1 || mode > 3 || M <= 0 || K <= 0 || K % 64)
+    return set_error(EC_EINVAL, "bad gemm+rmsnorm arguments");
+  Device& d = *G().devs[0];
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  GemmLnLaunch g{static_cast<const bf16*>(A), K, static_cast<const bf16*>(W), M, N, K, nullptr,
+                 resid, g1, g2, out32, static_cast<bf16*>(outb), d.status};
+  g.mode = mode;
+  g.eps = eps;
+  g.scale = scale;
+  g.has_scale = has_scale;
+  rc = check_cuda(launch_gemm_ln(g, d.stream, d.num_sms), "gemm+rmsnorm");
+  if (rc) return rc;
+  return sync_and_check(d, "gemm+rmsnorm");
+}
+
 int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, void* out,
                     const int32_t* cu_dev, const int32_t* lens_host, int nseq, int heads,
                     int kv_heads, int head_dim, int causal) {

@@ -228,9 +228,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms) {
 
 // ---------------------------------------------------------------------------
 // GEMM + residual + LayerNorm on clusters of C CTAs (one column slice each)
-template <int BN, int C, bool RB>
+template <int BN, int C, bool RB, int NM = kNormLayer>
 static cudaError_t run_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
-  using Cfg = GemmLnCfg<BN, C, RB>;
+  using Cfg = GemmLnCfg<BN, C, RB, NM>;
   static std::mutex mu;
   static int max_clusters[64] = {};
   int dev = 0;
@@ -250,14 +250,14 @@ static cudaError_t run_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!max_clusters[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_ln_kernel<BN, C, RB>,
+      cudaError_t e = cudaFuncSetAttribute(gemm_ln_kernel<BN, C, RB, NM>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(Cfg::SMEM_BYTES));
       if (e != cudaSuccess) return e;
       // clusters that fit at once (GPC boundaries leave some SMs idle)
       cfg.gridDim = dim3((num_sms / C) * C, 1, 1);
       int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, gemm_ln_kernel<BN, C, RB>, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, gemm_ln_kernel<BN, C, RB, NM>, &cfg);
       if (e != cudaSuccess) return e;
       if (n <= 0) return cudaErrorInvalidConfiguration;
       max_clusters[dev] = n;
@@ -266,20 +266,21 @@ static cudaError_t run_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
   CUtensorMap ta, tb, t32, tbf, tr;
   if (!encode_2d_bf16(&ta, g.A, g.M, g.K, g.lda, kGemmBM)) return cudaErrorInvalidValue;
   if (!encode_2d_bf16(&tb, g.W, g.N, g.K, g.K, BN)) return cudaErrorInvalidValue;
-  if (!encode_2d_out(&tbf, g.outb, false, g.M, g.N, g.N)) return cudaErrorInvalidValue;
-  // without an fp32 output the map is never used: the bf16 one stands in
-  if (g.out32) {
-    if (!encode_2d_out(&t32, g.out32, true, g.M, g.N, g.N)) return cudaErrorInvalidValue;
-  } else {
-    t32 = tbf;
-  }
+  // a map that is never used (no such output / residual) borrows a valid one
+  if (g.outb && !encode_2d_out(&tbf, g.outb, false, g.M, g.N, g.N)) return cudaErrorInvalidValue;
+  if (g.out32 && !encode_2d_out(&t32, g.out32, true, g.M, g.N, g.N)) return cudaErrorInvalidValue;
+  if (!g.outb) tbf = t32;
+  if (!g.out32) t32 = tbf;
   // the residual is read with the matching output's box and swizzle (rows
   // past M read as zero)
   if (RB) {
     if (!encode_2d_out(&tr, const_cast<__nv_bfloat16*>(g.resid_b), false, g.M, g.N, g.N))
       return cudaErrorInvalidValue;
-  } else if (!encode_2d_out(&tr, const_cast<float*>(g.resid), true, g.M, g.N, g.N)) {
-    return cudaErrorInvalidValue;
+  } else if (g.resid) {
+    if (!encode_2d_out(&tr, const_cast<float*>(g.resid), true, g.M, g.N, g.N))
+      return cudaErrorInvalidValue;
+  } else {
+    tr = t32;
   }
   GemmLnArgs a;
   a.M = g.M;
@@ -287,20 +288,50 @@ static cudaError_t run_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
   a.K = g.K;
   a.bias = g.bias;
   a.out32 = g.out32 ? 1 : 0;
+  a.outb = g.outb ? 1 : 0;
+  a.eps = g.eps;
+  a.scale = g.scale;
+  a.has_scale = g.has_scale;
   a.ln_g = g.ln_g;
   a.ln_b = g.ln_b;
   a.m_tiles = (g.M + kGemmBM - 1) / kGemmBM;
   a.status = g.status;
   const int clusters = a.m_tiles < max_clusters[dev] ? a.m_tiles : max_clusters[dev];
   cfg.gridDim = dim3(clusters * C, 1, 1);
-  return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<BN, C, RB>, ta, tb, t32, tbf, tr, a);
+  return cudaLaunchKernelEx(&cfg, gemm_ln_kernel<BN, C, RB, NM>, ta, tb, t32, tbf, tr, a);
 }
 
 bool gemm_ln_supported(int N) { return N == 384 || N == 768 || N == 1024; }
+bool gemm_rms_supported(int N) { return N == 512 || N == 768 || N == 1024; }
+
+template <int NM>
+static cudaError_t launch_rms(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
+  switch (g.N) {
+    case 512: return run_ln<128, 4, false, NM>(g, st, num_sms);
+    case 768: return run_ln<192, 4, false, NM>(g, st, num_sms);
+    case 1024: return run_ln<256, 4, false, NM>(g, st, num_sms);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 cudaError_t launch_gemm_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
-  if (g.K % kGemmBK || g.M <= 0 || !(g.resid || g.resid_b) || !g.ln_g || !g.ln_b || !g.outb)
-    return cudaErrorInvalidValue;
+  if (g.K % kGemmBK || g.M <= 0 || !g.ln_g) return cudaErrorInvalidValue;
+  if (g.mode != kNormLayer) {
+    if (g.resid_b || !(g.out32 || g.outb)) return cudaErrorInvalidValue;
+    switch (g.mode) {
+      case kNormResRms:
+        if (!g.resid || !g.out32 || !g.outb) return cudaErrorInvalidValue;
+        return launch_rms<kNormResRms>(g, st, num_sms);
+      case kNormPostAdd:
+        if (!g.resid || !g.out32) return cudaErrorInvalidValue;
+        return launch_rms<kNormPostAdd>(g, st, num_sms);
+      case kNormScaled:
+        if (g.resid || !g.out32) return cudaErrorInvalidValue;
+        return launch_rms<kNormScaled>(g, st, num_sms);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (!(g.resid || g.resid_b) || !g.ln_b || !g.outb) return cudaErrorInvalidValue;
   const bool rb = g.resid_b != nullptr;
   switch (g.N) {
     case 384: return rb ? run_ln<192, 2, true>(g, st, num_sms) : run_ln<192, 2, false>(g, st, num_sms);

@@ -33,16 +33,30 @@ namespace ec {
 struct GemmLnArgs {
   int M, N, K;
   const float* bias;   // [N] or nullptr
-  const float* ln_g;   // [N]
-  const float* ln_b;   // [N]
+  const float* ln_g;   // [N] (RMS modes: the first gain)
+  const float* ln_b;   // [N] (kNormPostAdd: the second gain, or nullptr)
   int m_tiles;
   int out32;           // 1: also store the fp32 row
+  int outb;            // 1: store the bf16 row
+  float eps;           // RMS modes
+  float scale;         // kNormPostAdd: layer scalar (when has_scale); kNormScaled: input scale
+  int has_scale;
   unsigned* status;
+};
+
+// epilogue of gemm_ln_kernel (x = the accumulator row of N = hidden columns)
+enum GemmNorm : int {
+  kNormLayer = 0,    // LayerNorm(x + bias + resid) -> out32 / outb (bert.lisp)
+  kNormResRms = 1,   // h = x + resid -> out32, outb = RMSNorm(h) * g (llama.lisp
+                     // residual add + the next pre-norm)
+  kNormPostAdd = 2,  // h = (resid + RMSNorm(x) * g) [* scale] -> out32, outb =
+                     // RMSNorm(h) * g2 or h (gemma::layer-forward post-norms)
+  kNormScaled = 3,   // out32 = RMSNorm(x * scale) * g (gemma per-layer input)
 };
 
 // RB: the residual arrives as bf16 (the previous LayerNorm's bf16 output,
 // which is also the next GEMM's input) instead of fp32
-template <int BN, int C, bool RB = false>
+template <int BN, int C, bool RB = false, int NM = kNormLayer>
 struct GemmLnCfg {
   static constexpr int NCH = BN / 32;                      // 32-column chunks per CTA
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
@@ -70,15 +84,16 @@ struct GemmLnCfg {
   static_assert(NCH % 2 == 0, "both epilogue halves take whole chunks");
 };
 
-template <int BN, int C, bool RB>
+template <int BN, int C, bool RB, int NM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO32,
                    const __grid_constant__ CUtensorMap tmOb,
                    const __grid_constant__ CUtensorMap tmR, const GemmLnArgs args) {
-  using Cfg = GemmLnCfg<BN, C, RB>;
+  using Cfg = GemmLnCfg<BN, C, RB, NM>;
   constexpr int STAGES = Cfg::STAGES;
+  static_assert(NM == kNormLayer || !RB, "RMS modes take an fp32 residual");
   constexpr int NCH = Cfg::NCH;
   constexpr uint32_t IDESC = make_idesc(1, kGemmBM, BN);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
@@ -137,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = threadIdx.x - 64; i < BN; i += kGemmThreads - 64) {
       sVec[i] = args.bias ? args.bias[rk * BN + i] : 0.f;
       sVec[BN + i] = args.ln_g[rk * BN + i];
-      sVec[2 * BN + i] = args.ln_b[rk * BN + i];
+      sVec[2 * BN + i] = args.ln_b ? args.ln_b[rk * BN + i] : 0.f;
     }
   }
   tc_fence_before();
@@ -242,12 +257,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              static_cast<uint32_t>(acc * BN);
       // residual chunks by TMA into the two buffers, once the previous
       // tile's bulk stores have finished reading them
+      // kNormPostAdd with a second gain exchanges twice per tile, through
+      // fixed slots 0 / 1 (a partner can only overwrite slot e after every
+      // CTA has passed the other exchange); one exchange alternates slots
+      // with the tile parity
+      const bool two_ex = NM == kNormPostAdd && args.ln_b != nullptr;
       if (lane == 0) {
         tma_store_wait_read<0>();
-        load_res(0, half, row0);
-        if (NLOC > 1) load_res(1, half + 2, row0);
+        if constexpr (NM != kNormScaled) {
+          load_res(0, half, row0);
+          if (NLOC > 1) load_res(1, half + 2, row0);
+        }
         // this tile's exchange: C * 256 partners' 8-byte stores land here
-        if (ew == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::XS_TX);
+        if (ew == 0) {
+          if (two_ex) {
+            mbar_arrive_expect_tx(&xbar[0], Cfg::XS_TX);
+            mbar_arrive_expect_tx(&xbar[1], Cfg::XS_TX);
+          } else {
+            mbar_arrive_expect_tx(&xbar[par], Cfg::XS_TX);
+          }
+        }
       }
       __syncwarp();
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
@@ -255,6 +284,168 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
+      if constexpr (NM != kNormLayer) {
+        // ---------------------------------------------- RMS epilogues --
+        // this lane's fp32 residual row of chunk ci (buffer ci & 1), then
+        // the next load into the same buffer once every lane has read it
+        auto take_res = [&](int ci, float (&rr)[32]) -> bool {
+          const int b = ci & 1;
+          if (!mbar_wait_warp(&rb[b], (rbits >> b) & 1u, abort_flag)) return false;
+          rbits ^= 1u << b;
+          const uint8_t* buf = bufs + b * Cfg::BUF_BYTES;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 q = *reinterpret_cast<const float4*>(buf + stage_off<true>(lane, j));
+            rr[4 * j] = q.x;
+            rr[4 * j + 1] = q.y;
+            rr[4 * j + 2] = q.z;
+            rr[4 * j + 3] = q.w;
+          }
+          __syncwarp();
+          if (lane == 0 && ci + 2 < NLOC) load_res(b, half + 2 * (ci + 2), row0);
+          return true;
+        };
+        // one exchange of this warp's partial sum of squares; total over the row
+        auto exchange = [&](int sl, uint32_t parity, float val, float& total) -> bool {
+          const uint32_t dst = smem_u32(xs + slot(sl, rank, half));
+          const uint32_t bar = smem_u32(&xbar[sl]);
+#pragma unroll
+          for (int r = 0; r < C; ++r)
+            st_async_cluster_v2(cluster_map(dst, r), val, 0.f, cluster_map(bar, r));
+          if (!mbar_wait_cluster_warp(&xbar[sl], parity, abort_flag)) return false;
+          float t = 0.f;
+#pragma unroll
+          for (int r = 0; r < C; ++r) t += xs[slot(sl, r, 0)].x + xs[slot(sl, r, 1)].x;
+          total = t;
+          return true;
+        };
+        const int sl0 = two_ex ? 0 : par;
+        const uint32_t ph0 = two_ex ? static_cast<uint32_t>(tcount & 1)
+                                    : static_cast<uint32_t>((tcount >> 1) & 1);
+        // ---- pass A: x (+ resid / * scale) -> TMEM where it changes; sum x^2
+        float ss = 0.f;
+#pragma unroll 1
+        for (int ci = 0; ci < NLOC; ++ci) {
+          const int cl = (half + 2 * ci) * 32;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + cl, v);
+          float rr[32];
+          if constexpr (NM == kNormResRms) {
+            if (!take_res(ci, rr)) {
+              ok = false;
+              break;
+            }
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]);
+            if constexpr (NM == kNormResRms) x = x + rr[j];
+            if constexpr (NM == kNormScaled) x = x * args.scale;
+            ss += x * x;
+            v[j] = __float_as_uint(x);
+          }
+          if constexpr (NM != kNormPostAdd) tmem_st_32x32b_x32(t_row + cl, v);
+        }
+        if (!ok) break;
+        if constexpr (NM != kNormPostAdd) tmem_wait_st();
+        float tot = 0.f;
+        if (!exchange(sl0, ph0, ss, tot)) {
+          ok = false;
+          break;
+        }
+        const float inv1 = 1.0f / sqrtf(tot * inv_n + args.eps);
+        float inv2 = 1.f;
+        if constexpr (NM == kNormPostAdd) {
+          // ---- pass B: h = resid + RMSNorm(x) * g1 [* scale] -> TMEM; sum h^2
+          float ss2 = 0.f;
+#pragma unroll 1
+          for (int ci = 0; ci < NLOC; ++ci) {
+            const int cl = (half + 2 * ci) * 32;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_row + cl, v);
+            float rr[32];
+            if (!take_res(ci, rr)) {
+              ok = false;
+              break;
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float hv = rr[j] + (__uint_as_float(v[j]) * inv1) * sVec[BN + cl + j];
+              if (args.has_scale) hv = hv * args.scale;
+              ss2 += hv * hv;
+              v[j] = __float_as_uint(hv);
+            }
+            tmem_st_32x32b_x32(t_row + cl, v);
+          }
+          if (!ok) break;
+          tmem_wait_st();
+          if (two_ex) {
+            float tot2 = 0.f;
+            if (!exchange(1, static_cast<uint32_t>(tcount & 1), ss2, tot2)) {
+              ok = false;
+              break;
+            }
+            inv2 = 1.0f / sqrtf(tot2 * inv_n + args.eps);
+          }
+        }
+        // ---- pass C: stage and bulk-store the fp32 and / or bf16 rows
+#pragma unroll 1
+        for (int ci = 0; ci < NLOC; ++ci) {
+          const int cl = (half + 2 * ci) * 32;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + cl, v);
+          uint8_t* st32 = bufs + (ci & 1) * Cfg::BUF_BYTES;
+          if (lane == 0) tma_store_wait_read<0>();
+          __syncwarp();
+          tmem_wait_ld();
+          if (ci + 1 == NLOC) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float o32[8], ob[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int k = 8 * j + e;
+              const float x = __uint_as_float(v[k]);
+              if constexpr (NM == kNormResRms) {
+                o32[e] = x;
+                ob[e] = (x * inv1) * sVec[BN + cl + k];
+              } else if constexpr (NM == kNormPostAdd) {
+                o32[e] = x;
+                ob[e] = two_ex ? (x * inv2) * sVec[2 * BN + cl + k] : x;
+              } else {
+                o32[e] = (x * inv1) * sVec[BN + cl + k];
+                ob[e] = o32[e];
+              }
+            }
+            if (args.out32) {
+              *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j)) =
+                  make_float4(o32[0], o32[1], o32[2], o32[3]);
+              *reinterpret_cast<float4*>(st32 + stage_off<true>(lane, 2 * j + 1)) =
+                  make_float4(o32[4], o32[5], o32[6], o32[7]);
+            }
+            if (args.outb)
+              *reinterpret_cast<uint4*>(stb + stage_off<false>(lane, j)) =
+                  make_uint4(pack_bf16(ob[0], ob[1]), pack_bf16(ob[2], ob[3]),
+                             pack_bf16(ob[4], ob[5]), pack_bf16(ob[6], ob[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (args.out32) tma_store_2d(&tmO32, st32, rank * BN + cl, row0);
+            if (args.outb) tma_store_2d(&tmOb, stb, rank * BN + cl, row0);
+            tma_store_commit();
+          }
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+        continue;
+      }
       // ---- pass A: x = acc + bias + resid, back into TMEM; partial sum;
       // chunk ci's residual is in buffer ci & 1
       float s_loc = 0.f;

@@ -192,8 +192,18 @@ struct GemmLnLaunch {
   __nv_bfloat16* outb;     // [M, N]
   unsigned* status;
   const __nv_bfloat16* resid_b = nullptr;  // [M, N] bf16 residual (replaces resid)
+  // epilogue (GemmNorm in ec_gemm_ln.cuh): 0 LayerNorm (ln_g, ln_b); RMS
+  // modes with eps: 1 out32 = x + resid, outb = RMSNorm(out32) * ln_g;
+  // 2 out32 = (resid + RMSNorm(x) * ln_g) [* scale when has_scale], outb =
+  // RMSNorm(out32) * ln_b (ln_b nullptr: bf16(out32)); 3 out32 =
+  // RMSNorm(x * scale) * ln_g (outb may be nullptr)
+  int mode = 0;
+  float eps = 0.f;
+  float scale = 1.f;
+  int has_scale = 0;
 };
 bool gemm_ln_supported(int N);
+bool gemm_rms_supported(int N);
 cudaError_t launch_gemm_ln(const GemmLnLaunch& g, cudaStream_t st, int num_sms);
 
 // ---- fused feed-forward block (ec_mlp.cu) -------------------------------------

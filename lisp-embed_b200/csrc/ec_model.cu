@@ -718,6 +718,24 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     trace_launch(d, "gemm+layernorm");
     return check_cuda(e, "gemm+layernorm");
   };
+  // out32 / outb = an RMSNorm-family epilogue of A . W^T on N = H columns
+  // (GemmNorm modes 1-3, see GemmLnLaunch)
+  auto gemm_norm = [&](const bf16* A, int K, const bf16* W, int mode, const float* resid,
+                       const float* g1, const float* g2, float* o32, bf16* ob, float scale,
+                       int has_scale, int N) -> int {
+    GemmLnLaunch g{A, K, W, T, N, K, nullptr, resid, g1, g2, o32, ob, d.status};
+    g.mode = mode;
+    g.eps = static_cast<float>(m.eps);
+    g.scale = scale;
+    g.has_scale = has_scale;
+    const double bytes = 2.0 * T * K + 2.0 * N * K + (resid ? 4.0 * T * N : 0.0) +
+                         (o32 ? 4.0 * T * N : 0.0) + (ob ? 2.0 * T * N : 0.0);
+    const int e0 = prof_begin(d);
+    const cudaError_t e = launch_gemm_ln(g, st, d.num_sms);
+    prof_end(d, 0, 2.0 * T * N * K, bytes, e0);
+    trace_launch(d, "gemm+rmsnorm");
+    return check_cuda(e, "gemm+rmsnorm");
+  };
   AttnLaunch at;
   at.qkv = qkv;
   at.ld = nqkv;
@@ -848,6 +866,11 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
     }
     const float inv_sqrt_h = 1.0f / sqrtf(static_cast<float>(H));
     const bool fuse_qkv_norm = m.hd == 128 && nqkv % 256 == 0 && getenv("EC_NO_FUSED_ROPE") == nullptr;
+    // the post-norm residual adds and the per-layer-input norm in the
+    // epilogues of the GEMMs that produce them (clusters over the full row);
+    // EC_NO_GEMM_RMS keeps fp32 GEMM outputs + the row kernels
+    const bool fuse_rms = gemm_rms_supported(H) && gemm_rms_supported(P) &&
+                          getenv("EC_NO_GEMM_RMS") == nullptr;
     for (int li = 0; li < m.layers; ++li) {
       const GemmaLayerW& w = m.gl[li];
       // attention sub-block; the input RMSNorm of layers after the first
@@ -872,18 +895,33 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
                    4.0 * T * nqkv));
       }
       EC_TRY(attention());
-      EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, nullptr, tmp, H, kEpiF32));
-      NormAddArgs na1{tmp, w.post_ln, h32, 0, 1.f, w.pre_ff_ln, hb, m.eps, T, H};
-      EC_TRY(row([&] { return launch_norm_add(na1, st); }, "norm add", TH * 14.0));
+      if (fuse_rms) {
+        // h = h + RMSNorm(o) * g, hb = RMSNorm(h) * g' in the O GEMM
+        EC_TRY(gemm_norm(ctx, nctx, w.wo, 2, h32, w.post_ln, w.pre_ff_ln, h32, hb, 1.f, 0, H));
+      } else {
+        EC_TRY(gemm(ctx, nctx, w.wo, H, nctx, nullptr, nullptr, tmp, H, kEpiF32));
+        NormAddArgs na1{tmp, w.post_ln, h32, 0, 1.f, w.pre_ff_ln, hb, m.eps, T, H};
+        EC_TRY(row([&] { return launch_norm_add(na1, st); }, "norm add", TH * 14.0));
+      }
       // gated GELU-tanh MLP
       EC_TRY(gemm(hb, H, w.wgu, 2 * F, H, nullptr, nullptr, ff, F, kEpiBf16GeluTanhGate));
-      EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, nullptr, tmp, H, kEpiF32));
-      NormAddArgs na2{tmp, w.post_ff_ln, h32, 0, 1.f, nullptr, hb, m.eps, T, H};
-      EC_TRY(row([&] { return launch_norm_add(na2, st); }, "norm add", TH * 14.0));
+      if (fuse_rms) {
+        // h = h + RMSNorm(down) * g, hb = bf16(h) (the PLE gate's input)
+        EC_TRY(gemm_norm(ff, F, w.wdown, 2, h32, w.post_ff_ln, nullptr, h32, hb, 1.f, 0, H));
+      } else {
+        EC_TRY(gemm(ff, F, w.wdown, H, F, nullptr, nullptr, tmp, H, kEpiF32));
+        NormAddArgs na2{tmp, w.post_ff_ln, h32, 0, 1.f, nullptr, hb, m.eps, T, H};
+        EC_TRY(row([&] { return launch_norm_add(na2, st); }, "norm add", TH * 14.0));
+      }
       // per-layer embedding of this layer from the scaled token embedding
-      EC_TRY(gemm(h0b, H, w.wpp, P, H, nullptr, nullptr, ple, P, kEpiF32));
-      PlePrepArgs pa{ple, inv_sqrt_h, m.ple_norm, m.eps, T, P};
-      EC_TRY(row([&] { return launch_ple_prep(pa, st); }, "ple prep", 8.0 * T * P));
+      if (fuse_rms) {
+        EC_TRY(gemm_norm(h0b, H, w.wpp, 3, nullptr, m.ple_norm, nullptr, ple, nullptr, inv_sqrt_h,
+                         0, P));
+      } else {
+        EC_TRY(gemm(h0b, H, w.wpp, P, H, nullptr, nullptr, ple, P, kEpiF32));
+        PlePrepArgs pa{ple, inv_sqrt_h, m.ple_norm, m.eps, T, P};
+        EC_TRY(row([&] { return launch_ple_prep(pa, st); }, "ple prep", 8.0 * T * P));
+      }
       // PLE block: gate(h) -> GELU-tanh * ple -> projection -> norm -> residual
       // gelu-tanh(gate(h)) * ple straight out of the gate GEMM's epilogue
       // (EC_NO_FUSED_PLE_GATE: fp32 gate, then the row kernel)
@@ -895,14 +933,20 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
         PleGateArgs pga{pg, ple, pgb, T, P};
         EC_TRY(row([&] { return launch_ple_gate(pga, st); }, "ple gate", 10.0 * T * P));
       }
-      EC_TRY(gemm(pgb, P, w.wple_proj, H, P, nullptr, nullptr, tmp, H, kEpiF32));
       // h = (h + RMSNorm(ple)) * layer_scalar, and hb = the next layer's
       // input RMSNorm of it
       const bool more = li + 1 < m.layers;
-      NormAddArgs na3{tmp, w.ple_norm, h32, 1, w.scalar, more ? m.gl[li + 1].in_ln : nullptr,
-                      more ? hb : nullptr, m.eps, T, H};
-      EC_TRY(row([&] { return launch_norm_add(na3, st); }, "norm add scale",
-                 TH * (more ? 14.0 : 12.0)));
+      if (fuse_rms) {
+        EC_TRY(gemm_norm(pgb, P, w.wple_proj, 2, h32, w.ple_norm,
+                         more ? m.gl[li + 1].in_ln : nullptr, h32, more ? hb : nullptr, w.scalar,
+                         1, H));
+      } else {
+        EC_TRY(gemm(pgb, P, w.wple_proj, H, P, nullptr, nullptr, tmp, H, kEpiF32));
+        NormAddArgs na3{tmp, w.ple_norm, h32, 1, w.scalar, more ? m.gl[li + 1].in_ln : nullptr,
+                        more ? hb : nullptr, m.eps, T, H};
+        EC_TRY(row([&] { return launch_norm_add(na3, st); }, "norm add scale",
+                   TH * (more ? 14.0 : 12.0)));
+      }
     }
     // final RMSNorm per token, then mean pool + projection + L2
     RmsArgs rf{h32, nullptr, m.final_norm, m.eps, nullptr, h32, T, H};

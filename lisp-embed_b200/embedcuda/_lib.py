@@ -84,6 +84,8 @@ _SIGS = {
     "ecdbg_gemm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P, P, C.c_int, C.c_int]),
     "ecdbg_mlp": (C.c_int, [P, P, P, P, P, P, P, P, P, P, C.c_int, C.c_int, C.c_int]),
     "ecdbg_gemm_ln": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P]),
+    "ecdbg_gemm_norm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P, P, P, P, C.c_int,
+                                  C.c_float, C.c_float, C.c_int]),
     "ecdbg_profile": (C.c_int, [C.c_int]),
     "ecdbg_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                      C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),

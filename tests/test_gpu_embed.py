@@ -88,15 +88,18 @@ def test_errors(synth_root, ec):
         model.embed_batch(np.zeros(0, np.int32), np.array([0, 0], np.int64))  # empty sequence
 
 
-@pytest.mark.parametrize("unfused", [0, 1])
+@pytest.mark.parametrize("unfused", [0, 1, 2])
 def test_gemma(synth_root, ec, monkeypatch, unfused):
     """EmbeddingGemma: one sliding (theta 1e4) and one full-attention (theta
     1e6) layer, PLE, per-head q/k/v norms, mean pool + 512 -> 768 projection;
     with the norms / PLE gate fused into GEMM epilogues and without."""
     import dataclasses
-    if unfused:
+    if unfused == 1:      # every Gemma fusion off
         monkeypatch.setenv("EC_NO_FUSED_ROPE", "1")
         monkeypatch.setenv("EC_NO_FUSED_PLE_GATE", "1")
+        monkeypatch.setenv("EC_NO_GEMM_RMS", "1")
+    elif unfused == 2:    # only the GEMM + RMSNorm epilogues off
+        monkeypatch.setenv("EC_NO_GEMM_RMS", "1")
     s = synth.with_layers(synth.GEMMA_EMB, 2, vocab=4096)
     s = dataclasses.replace(s, name=s.name + "-sf", extra=dict(
         s.extra, layer_types=["sliding_attention", "full_attention"]))

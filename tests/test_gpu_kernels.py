@@ -82,6 +82,54 @@ def test_gemm_gelu_tanh_epilogues(ec, M, N, K, epi):
     assert err < 1e-2, err
 
 
+def _rms(x, eps):
+    return x / torch.sqrt((x * x).mean(-1, keepdim=True) + eps)
+
+
+# GEMM + RMSNorm epilogues on clusters (the Qwen3 residual add + pre-norm,
+# Gemma's post-norm residual adds with and without the layer scalar and the
+# second norm, Gemma's per-layer-input norm); in-place residual for mode 2
+@pytest.mark.parametrize("M,N,K", [(1, 512, 512), (300, 512, 2048), (1029, 1024, 512),
+                                   (777, 768, 768)])
+@pytest.mark.parametrize("mode,variant", [(1, 0), (2, 0), (2, 1), (3, 0)])
+def test_gemm_rms_epilogues(ec, M, N, K, mode, variant):
+    import ctypes as C
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + mode)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    g1 = 1 + 0.1 * torch.randn(N, device="cuda", generator=g)
+    g2 = 1 + 0.1 * torch.randn(N, device="cuda", generator=g)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    x = A.float() @ W.float().t()
+    eps, scale = 1e-6, 0.75
+    out32 = resid.clone() if mode == 2 else torch.empty(M, N, device="cuda")
+    outb = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    if mode == 1:
+        ref32 = x + resid
+        refb = _rms(ref32, eps) * g1
+        args = (resid.data_ptr(), g1.data_ptr(), None, 0, 1.0)
+    elif mode == 2:
+        ref32 = resid + _rms(x, eps) * g1
+        if variant:
+            ref32 = ref32 * scale
+        refb = _rms(ref32, eps) * g2 if variant else ref32
+        # in place: the residual is the fp32 output
+        args = (out32.data_ptr(), g1.data_ptr(), g2.data_ptr() if variant else None, variant, scale)
+    else:
+        ref32 = _rms(x * scale, eps) * g1
+        refb = ref32
+        args = (None, g1.data_ptr(), None, 0, scale)
+    resid_p, g1_p, g2_p, has_scale, sc = args
+    torch.cuda.synchronize()
+    ec.check(ec.lib().ecdbg_gemm_norm(A.data_ptr(), W.data_ptr(), M, N, K, resid_p, g1_p, g2_p,
+                                      out32.data_ptr(), outb.data_ptr(), mode, eps, sc,
+                                      has_scale), "gemm_norm")
+    e32 = (out32 - ref32).abs().max().item() / ref32.abs().max().item()
+    eb = (outb.float() - refb).abs().max().item() / refb.abs().max().item()
+    assert e32 < 1e-4, e32
+    assert eb < 1e-2, eb
+
+
 # CTA-pair GEMM (cta_group::2, 256 x 256 tiles): ragged M (one or both
 # halves of the last tile past M), K down to one k-block
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (129, 512, 384), (300, 1536, 384),
