@@ -307,7 +307,7 @@ bool gemm_rms_supported(int N) { return N == 512 || N == 768 || N == 1024; }
 template <int NM>
 static cudaError_t launch_rms(const GemmLnLaunch& g, cudaStream_t st, int num_sms) {
   switch (g.N) {
-    case 512: return run_ln<128, 4, false, NM>(g, st, num_sms);
+    case 512: return run_ln<256, 2, false, NM>(g, st, num_sms);
     case 768: return run_ln<192, 4, false, NM>(g, st, num_sms);
     case 1024: return run_ln<256, 4, false, NM>(g, st, num_sms);
     default: return cudaErrorInvalidValue;
