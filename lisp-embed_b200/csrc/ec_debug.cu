@@ -228,7 +228,7 @@ int ecdbg_profile_read(const char* cls, double* ms, double* flops, double* bytes
   clear_error();
   if (!cls) return set_error(EC_EINVAL, "class is NULL");
   const std::string c(cls);
-  const int i = c == "gemm" ? 0 : c == "attention" ? 1 : c == "rows" ? 2 : -1;
+  const int i = c == "gemm" ? 0 : c == "attention" ? 1 : c == "rows" ? 2 : c == "scan" ? 3 : -1;
   if (i < 0) return set_error(EC_EINVAL, "unknown class %s", cls);
   const ProfAcc& a = G().prof[i];
   if (ms) *ms = a.ms;

@@ -352,6 +352,31 @@ static int ensure_search_ws(Device& dv, size_t bytes, void** out) {
 
 static size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Rows the probes of one search batch cover (profiling only: reads the
+// probes back, so the stream is idle when the timed scan starts).
+static double probed_rows(Device& dv, const int32_t* dp, int64_t np) {
+  const IndexW& ix = dv.index;
+  std::vector<int32_t> h(static_cast<size_t>(np));
+  if (np <= 0 || ix.h_offs.size() < static_cast<size_t>(ix.k) + 1) return 0;
+  if (cudaMemcpyAsync(h.data(), dp, static_cast<size_t>(np) * 4, cudaMemcpyDeviceToHost, dv.stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(dv.stream) != cudaSuccess)
+    return 0;
+  double r = 0;
+  for (const int32_t c : h)
+    if (c >= 0 && c < ix.k) r += static_cast<double>(ix.h_offs[c + 1] - ix.h_offs[c]);
+  return r;
+}
+
+// Query-batched scan when each probed list gets 8 queries on average (IVF)
+// or there are 8 queries (flat); EC_SCAN_PER_QUERY keeps one CTA per
+// (query, list / chunk).  Search workspaces are 256-byte aligned, so Q is.
+static bool scan_batched_ok(const IndexW& ix, int64_t nq, int nprobe, int topk, bool ivf) {
+  static const bool off = getenv("EC_SCAN_PER_QUERY") != nullptr;
+  if (off || !batched_scan_supported(ix.x, ix.x, ix.d, topk)) return false;
+  return ivf ? nq * nprobe >= 8 * static_cast<int64_t>(ix.k) : nq >= 8;
+}
+
 static int search_device(int li, const float* q, int64_t q0, int64_t q1, int nprobe, int topk, bool ivf,
                          int64_t* ids, float* scores) {
   Device& dv = *G().devs[li];
@@ -370,8 +395,13 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     const size_t s_c = a256(static_cast<size_t>(nq) * ngroups * topk * 8);
     const size_t s_i = a256(static_cast<size_t>(nq) * topk * 8);
     const size_t s_f = a256(static_cast<size_t>(nq) * topk * 4);
+    // query-batched scans once a batch gives each list several queries
+    // (flat: once there are several queries); one CTA per (query, list)
+    // otherwise
+    const bool batched = scan_batched_ok(ix, nq, nprobe, topk, ivf);
+    const size_t s_b = batched && ivf ? a256(batched_list_scan_ws(ix.k, nq * nprobe)) : 0;
     void* ws;
-    EC_TRY(ensure_search_ws(dv, s_q + s_s + s_p + s_c + s_i + s_f, &ws));
+    EC_TRY(ensure_search_ws(dv, s_q + s_s + s_p + s_c + s_i + s_f + s_b, &ws));
     char* w = static_cast<char*>(ws);
     float* dq = reinterpret_cast<float*>(w);
     float* dS = reinterpret_cast<float*>(w + s_q);
@@ -384,10 +414,23 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     if (ivf) {
       EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st), "probe scores"));
       EC_TRY(check_cuda(launch_probe_select(dS, nq, ix.k, nprobe, dp, st), "probe select"));
-      EC_TRY(check_cuda(launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, dc, st),
-                        "list scan"));
+      // event-timed while profiling (class 3: scans; algorithmic work = the
+      // probed lists' rows, d multiply-adds and d * 4 bytes each)
+      double rows = 0;
+      if (G().profile) rows = probed_rows(dv, dp, nq * nprobe);
+      const int e0 = prof_begin(dv);
+      const cudaError_t e =
+          batched ? launch_list_scan_batched(ix.x, d, ix.lists, ix.offs, ix.k, dp, nprobe, dq, nq, topk,
+                                             w + s_q + s_s + s_p + s_c + s_i + s_f, dc, st)
+                  : launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, dc, st);
+      prof_end(dv, 3, 2.0 * rows * d, 4.0 * rows * d, e0);
+      EC_TRY(check_cuda(e, "list scan"));
     } else {
-      EC_TRY(check_cuda(launch_flat_scan(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st), "flat scan"));
+      const int e0 = prof_begin(dv);
+      const cudaError_t e = batched ? launch_flat_scan_batched(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st)
+                                    : launch_flat_scan(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st);
+      prof_end(dv, 3, 2.0 * static_cast<double>(nq) * ix.n * d, 4.0 * static_cast<double>(nq) * ix.n * d, e0);
+      EC_TRY(check_cuda(e, "flat scan"));
     }
     EC_TRY(check_cuda(launch_merge(dc, nq, ngroups, topk, di, df, st), "merge"));
     EC_TRY(check_cuda(cudaMemcpyAsync(ids + a * topk, di, static_cast<size_t>(nq) * topk * 8,
@@ -395,6 +438,10 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     EC_TRY(check_cuda(cudaMemcpyAsync(scores + a * topk, df, static_cast<size_t>(nq) * topk * 4,
                                       cudaMemcpyDeviceToHost, st), "scores download"));
     EC_TRY(sync_and_check(dv, "search"));
+    if (G().profile) {
+      std::lock_guard<std::mutex> lk(G().stat_mu);
+      prof_collect(dv);
+    }
   }
   return EC_OK;
 }

@@ -34,6 +34,20 @@ cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, cons
 cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk,
                          int64_t* ids, float* scores, cudaStream_t st);
 
+// ---- query-batched scans (ec_ivf_scan.cu): same candidates as
+// launch_list_scan / launch_flat_scan, one CTA per (list or row chunk, up to
+// 32 queries).  Needs d % 4 == 0, 16-byte aligned X and Q, topk <= 64.
+bool batched_scan_supported(const float* X, const float* Q, int d, int topk);
+// bytes of scratch launch_list_scan_batched needs
+size_t batched_list_scan_ws(int k, int64_t npairs);
+cudaError_t launch_list_scan_batched(const float* X, int d, const uint32_t* lists,
+                                     const int64_t* offs, int k, const int32_t* probes, int nprobe,
+                                     const float* Q, int64_t nq, int topk, void* ws,
+                                     unsigned long long* cand, cudaStream_t st);
+cudaError_t launch_flat_scan_batched(const float* X, int64_t n, int d, int nchunks,
+                                     const float* Q, int64_t nq, int topk,
+                                     unsigned long long* cand, cudaStream_t st);
+
 // ---- tensor-core assignment (ec_ivf_tc.cu) ----------------------------------
 // relative bound on |bf16 score - exact score| / (|x| max|c|) for head dim d
 float argcand_rel(int d);

@@ -133,7 +133,7 @@ struct Global {
   // profiling of the forward (ecdbg_profile)
   bool profile = false;
   bool sync_each = false;  // EC_SYNC_EACH_LAUNCH: wait for and report every forward launch
-  ProfAcc prof[3];
+  ProfAcc prof[4];  // gemm, attention, rows, scan
   long long launches = 0;
   long long assign_tc_rows = 0;     // rows the tensor-core assignment settled
   long long assign_exact_rows = 0;  // rows that took the exact scan

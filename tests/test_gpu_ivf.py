@@ -138,3 +138,53 @@ def test_ivf_and_flat_search(ec, corpus):
     # kb::top-k pairs
     pairs = kb.top_k(qs[0], 5)
     assert len(pairs) == 5 and all(pairs[j][1] >= pairs[j + 1][1] for j in range(4))
+
+
+def _check_ivf(x, cent, counts, lists, qs, nprobe, topk):
+    ids, sc = kb.search_ivf(qs, topk, nprobe=nprobe)
+    for i in range(len(qs)):
+        rid, rsc = oracle.top_k_ivf(x, cent, counts, lists, nprobe, qs[i], topk)
+        assert np.array_equal(ids[i][:len(rid)], rid), i
+        assert np.array_equal(sc[i][:len(rsc)], rsc), i
+        assert np.all(ids[i][len(rid):] == -1), i
+
+
+@pytest.mark.parametrize("topk", [1, 10, 64])
+def test_ivf_search_query_batched(ec, corpus, topk):
+    """Enough queries that every list gets several 32-query chunks: the
+    list-major scan (one CTA per list and query chunk) against kb::top-k-ivf."""
+    x = corpus
+    cent = x[synth.make_ivf_sample(len(x), 5)[:64]]
+    counts, lists = ann.assign_all(x, cent)
+    kb.load_index(x, (cent, counts, lists))
+    qs, _ = synth.make_ivf_corpus(400, 384, 64, seed=101)
+    _check_ivf(x, cent, counts, lists, qs, 8, topk)
+
+
+def test_ivf_search_batched_ties_empty_lists_odd_dim(ec):
+    """d = 100 (a partial 32-column chunk), every row duplicated (equal scores:
+    the earlier list position must win), and centroids that own no rows
+    (empty lists probed by many queries)."""
+    base, _ = synth.make_ivf_corpus(3000, 100, 16, seed=7)
+    x = np.repeat(base, 2, axis=0)
+    far = -np.ones((8, 100), np.float32) / 10.0  # attract no rows
+    cent = np.concatenate([x[::250][:24], far], axis=0).astype(np.float32)
+    counts, lists = ann.assign_all(x, cent)
+    assert (counts == 0).sum() >= 1
+    kb.load_index(x, (cent, counts, lists))
+    qs, _ = synth.make_ivf_corpus(300, 100, 16, seed=8)
+    qs = np.concatenate([qs, base[:20]], axis=0)  # exact duplicates of rows
+    _check_ivf(x, cent, counts, lists, qs, 32, 10)
+    _check_ivf(x, cent, counts, lists, qs, 5, 64)
+
+
+def test_flat_search_query_batched(ec, corpus):
+    x = corpus
+    kb.load_index(x, None)
+    qs, _ = synth.make_ivf_corpus(40, 384, 64, seed=11)
+    qs = np.concatenate([qs, x[100:104]], axis=0)
+    for topk in (10, 64):
+        fid, fsc = kb.search_brute(qs, topk)
+        for i in range(len(qs)):
+            rid, rsc = oracle.top_k_brute(x, qs[i], topk)
+            assert np.array_equal(fid[i], rid) and np.array_equal(fsc[i], rsc), (topk, i)
