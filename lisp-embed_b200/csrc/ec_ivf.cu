@@ -384,7 +384,22 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
   EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
   const int d = ix.d;
   cudaStream_t st = dv.stream;
-  const int64_t QB = 8192;
+  const int64_t QB = 16384;
+  // EC_TRACE_SEARCH: per-phase device time of each batch on stderr
+  static const bool trace = getenv("EC_TRACE_SEARCH") != nullptr;
+  struct Events {
+    cudaEvent_t e[7] = {};
+    ~Events() {
+      for (auto x : e)
+        if (x) cudaEventDestroy(x);
+    }
+  } tevs;
+  cudaEvent_t* tev = tevs.e;
+  if (trace)
+    for (int i = 0; i < 7; ++i) cudaEventCreate(&tev[i]);
+  auto mark = [&](int i) {
+    if (trace) cudaEventRecord(tev[i], st);
+  };
   for (int64_t a = q0; a < q1; a += QB) {
     const int64_t nq = std::min(QB, q1 - a);
     const int nchunks = ivf ? 0 : static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(1, (ix.n + 8191) / 8192)));
@@ -409,11 +424,15 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     unsigned long long* dc = reinterpret_cast<unsigned long long*>(w + s_q + s_s + s_p);
     int64_t* di = reinterpret_cast<int64_t*>(w + s_q + s_s + s_p + s_c);
     float* df = reinterpret_cast<float*>(w + s_q + s_s + s_p + s_c + s_i);
+    mark(0);
     EC_TRY(check_cuda(cudaMemcpyAsync(dq, q + a * d, static_cast<size_t>(nq) * d * 4,
                                       cudaMemcpyHostToDevice, st), "query upload"));
+    mark(1);
     if (ivf) {
       EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st), "probe scores"));
+      mark(2);
       EC_TRY(check_cuda(launch_probe_select(dS, nq, ix.k, nprobe, dp, st), "probe select"));
+      mark(3);
       // event-timed while profiling (class 3: scans; algorithmic work = the
       // probed lists' rows, d multiply-adds and d * 4 bytes each)
       double rows = 0;
@@ -426,18 +445,32 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
       prof_end(dv, 3, 2.0 * rows * d, 4.0 * rows * d, e0);
       EC_TRY(check_cuda(e, "list scan"));
     } else {
+      mark(2);
+      mark(3);
       const int e0 = prof_begin(dv);
       const cudaError_t e = batched ? launch_flat_scan_batched(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st)
                                     : launch_flat_scan(ix.x, ix.n, d, nchunks, dq, nq, topk, dc, st);
       prof_end(dv, 3, 2.0 * static_cast<double>(nq) * ix.n * d, 4.0 * static_cast<double>(nq) * ix.n * d, e0);
       EC_TRY(check_cuda(e, "flat scan"));
     }
+    mark(4);
     EC_TRY(check_cuda(launch_merge(dc, nq, ngroups, topk, di, df, st), "merge"));
+    mark(5);
     EC_TRY(check_cuda(cudaMemcpyAsync(ids + a * topk, di, static_cast<size_t>(nq) * topk * 8,
                                       cudaMemcpyDeviceToHost, st), "ids download"));
     EC_TRY(check_cuda(cudaMemcpyAsync(scores + a * topk, df, static_cast<size_t>(nq) * topk * 4,
                                       cudaMemcpyDeviceToHost, st), "scores download"));
+    mark(6);
     EC_TRY(sync_and_check(dv, "search"));
+    if (trace) {
+      float ms[6] = {};
+      for (int i = 0; i < 6; ++i)
+        cudaEventElapsedTime(&ms[i], tev[i], tev[i + 1]);
+      fprintf(stderr,
+              "[ec search dev %d] nq %lld: upload %.3f scores %.3f select %.3f scan %.3f merge %.3f "
+              "download %.3f ms\n",
+              dv.ordinal, static_cast<long long>(nq), ms[0], ms[1], ms[2], ms[3], ms[4], ms[5]);
+    }
     if (G().profile) {
       std::lock_guard<std::mutex> lk(G().stat_mu);
       prof_collect(dv);

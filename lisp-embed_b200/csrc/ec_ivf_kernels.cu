@@ -309,31 +309,134 @@ __device__ unsigned long long block_min_u64(unsigned long long v, unsigned long 
 
 // top nprobe centroids of each query: score desc, index asc (stable sort of
 // kb.lisp:353).  One block per query, bitonic sort of k <= 8192 keys.
-__global__ void probe_select_kernel(const float* S, int k, int nprobe, int32_t* probes) {
-  extern __shared__ unsigned long long keys[];
+// The nprobe best centroids of query q in (score desc, index asc) order --
+// the first nprobe of kb.lisp:352's sort -- without sorting all k: a radix
+// select finds the nprobe-th smallest key (8 bits per pass over the 32-bit
+// score key, then over the index among equal scores), the keys at or below
+// it are gathered and only those are sorted.  One block of 256 threads per
+// query, k <= 8192 (32 keys per thread in registers).
+constexpr int kSelThreads = 256;
+constexpr int kSelPer = 32;
+
+__device__ __forceinline__ uint32_t score_key32(float s) {
+  return static_cast<uint32_t>(desc_key(s, 0u) >> 32);
+}
+
+// bin of the 256-bin histogram where the running count reaches `need`;
+// warp 0 only; writes (bin, count before it)
+__device__ __forceinline__ void sel_find(const uint32_t* hist, uint32_t need, uint32_t* out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t c[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = hist[8 * lane + j];
+    sum += c[j];
+  }
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  const uint32_t excl = incl - sum;
+  if (excl < need && need <= incl) {
+    uint32_t run = excl;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (run + c[j] >= need) {
+        out[0] = 8 * lane + j;
+        out[1] = run;
+        break;
+      }
+      run += c[j];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSelThreads) probe_select_kernel(const float* S, int k, int nprobe,
+                                                                   int32_t* probes) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t found[2];
+  __shared__ int nsel;
+  extern __shared__ unsigned long long sel[];  // [P2], P2 = pow2 >= nprobe
   const int64_t q = blockIdx.x;
+  const float* sq = S + q * k;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nv = tid < k ? (k - tid + kSelThreads - 1) / kSelThreads : 0;  // keys of this thread
+  uint32_t key[kSelPer];
+#pragma unroll
+  for (int m = 0; m < kSelPer; ++m) key[m] = m < nv ? score_key32(sq[tid + kSelThreads * m]) : 0u;
+
+  // histogram pass over the keys with (field & mask) == prefix, one warp
+  // atomic per distinct bin
+  auto pass = [&](auto field, uint32_t mask, uint32_t prefix, int shift, uint32_t need) {
+    hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < kSelPer; ++m) {
+      const uint32_t f = field(m);
+      const bool on = m < nv && (f & mask) == prefix;
+      const uint32_t bin = on ? (f >> shift) & 255u : 256u;
+      const unsigned grp = __match_any_sync(0xffffffffu, bin);
+      if (on && lane == __ffs(grp) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(grp)));
+    }
+    __syncthreads();
+    if (tid < 32) sel_find(hist, need, found);
+    __syncthreads();
+    const uint32_t b = found[0], before = found[1];
+    __syncthreads();  // found[] is rewritten by the next pass
+    return make_uint2(b, before);
+  };
+
+  // 1) the 32-bit score key v of the nprobe-th smallest key
+  uint32_t prefix = 0, mask = 0, need = static_cast<uint32_t>(nprobe);
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    const uint2 r = pass([&](int m) { return key[m]; }, mask, prefix, shift, need);
+    prefix |= r.x << shift;
+    mask |= 0xffu << shift;
+    need -= r.y;
+  }
+  const uint32_t v = prefix;
+  // 2) among the keys equal to v, the `need` lowest indices: index <= ix
+  uint32_t ip = 0, imask = 0, need2 = need;
+  for (int shift = 8; shift >= 0; shift -= 8) {
+    const uint2 r = pass(
+        [&](int m) { return key[m] == v ? static_cast<uint32_t>(tid + kSelThreads * m) : 0xffffffffu; },
+        imask | 0xffff0000u, ip, shift, need2);
+    ip |= r.x << shift;
+    imask |= 0xffu << shift;
+    need2 -= r.y;
+  }
+  // 3) gather exactly nprobe keys, sort them, emit the indices
   int P = 1;
-  while (P < k) P <<= 1;
-  for (int i = threadIdx.x; i < P; i += blockDim.x)
-    keys[i] = i < k ? desc_key(S[q * k + i], static_cast<uint32_t>(i)) : ~0ull;
+  while (P < nprobe) P <<= 1;
+  if (tid == 0) nsel = 0;
+  for (int i = tid; i < P; i += kSelThreads) sel[i] = ~0ull;
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < kSelPer; ++m) {
+    const uint32_t idx = static_cast<uint32_t>(tid + kSelThreads * m);
+    if (m < nv && (key[m] < v || (key[m] == v && idx <= ip)))
+      sel[atomicAdd(&nsel, 1)] = (static_cast<unsigned long long>(key[m]) << 32) | idx;
+  }
   __syncthreads();
   for (int size = 2; size <= P; size <<= 1)
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+      for (int i = tid; i < P; i += kSelThreads) {
         const int j = i ^ stride;
         if (j > i) {
           const bool up = (i & size) == 0;
-          const unsigned long long a = keys[i], b = keys[j];
+          const unsigned long long a = sel[i], b = sel[j];
           if ((a > b) == up) {
-            keys[i] = b;
-            keys[j] = a;
+            sel[i] = b;
+            sel[j] = a;
           }
         }
       }
       __syncthreads();
     }
-  for (int i = threadIdx.x; i < nprobe; i += blockDim.x)
-    probes[q * nprobe + i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
+  for (int i = tid; i < nprobe; i += kSelThreads)
+    probes[q * nprobe + i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
 }
 
 // Exact scores of `cnt` rows against one query, top `topk` by (score desc,
@@ -521,12 +624,12 @@ cudaError_t launch_update(const float* sums, int k, int d, float* cent, cudaStre
 
 cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, int32_t* probes,
                                 cudaStream_t st) {
+  if (k > kSelThreads * kSelPer || nprobe < 1 || nprobe > k) return cudaErrorInvalidValue;
   int P = 1;
-  while (P < k) P <<= 1;
+  while (P < nprobe) P <<= 1;
   const size_t sm = static_cast<size_t>(P) * 8;
-  if (sm > 64 * 1024) return cudaErrorInvalidValue;
   cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-  probe_select_kernel<<<static_cast<unsigned>(nq), 512, sm, st>>>(S, k, nprobe, probes);
+  probe_select_kernel<<<static_cast<unsigned>(nq), kSelThreads, sm, st>>>(S, k, nprobe, probes);
   return cudaGetLastError();
 }
 
