@@ -26,15 +26,15 @@ namespace ec {
 namespace {
 
 constexpr int kTsLanes = 32;   // queries per CTA
-constexpr int kTsWarps = 8;
-constexpr int kTsThreads = kTsWarps * 32;
-// each thread: 4 queries x 4 rows.  lane = rg * 8 + qg: query group qg
-// (queries 4 qg .. 4 qg + 3), row group rg (rows 4 rg .. 4 rg + 3 of the
-// warp's 16); a warp covers all 32 queries x 16 rows, the CTA 128 rows.
-// Every shared-memory load feeds 16 multiply-adds per lane (2 bytes of
-// register writeback per multiply-add, about the fp32 pipe's rate).
-constexpr int kTsQW = 4, kTsRW = 4;
-constexpr int kTsRows = kTsWarps * 4 * kTsRW;  // 128 rows per tile
+// each thread: 4 queries x RW rows.  lane = rg * 8 + qg: query group qg
+// (queries 4 qg .. 4 qg + 3), row group rg (rows RW rg .. RW rg + RW - 1 of
+// the warp's 4 RW); a warp covers all 32 queries, the CTA WARPS x 4 x RW =
+// 128 rows.  Each 16-byte shared-memory load feeds 4 RW (query operand) or
+// 16 (row operand) multiply-adds per lane: (4 + RW) x 16 bytes of register
+// writeback per 16 RW multiply-adds.
+constexpr int kTsQW = 4;
+constexpr int kTsWarps = 8, kTsRW = 4;  // the configuration launched
+constexpr int kTsRows = 128;            // rows per tile
 constexpr int kTsChunk = 16;                   // columns per pipeline stage
 constexpr int kTsStages = 3;
 constexpr int kTsHalf = kTsRows / 2;           // candidates per query per round
@@ -98,8 +98,12 @@ size_t ts_smem(int d, int topk) {
          static_cast<size_t>(kTsLanes) * (8 + 4 + 4 + 4);            // thr, cnt, nb, slot
 }
 
-template <bool kIvf>
-__global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScanArgs a) {
+template <bool kIvf, int WARPS, int RW>
+__global__ void __launch_bounds__(WARPS * 32, 2) tile_scan_kernel(const TileScanArgs a) {
+  static_assert(WARPS * 4 * RW == kTsRows && RW % 2 == 0, "tile shape");
+  constexpr int kThreads = WARPS * 32;
+  constexpr int kNp = kTsRows * (kTsChunk / 4) / kThreads;  // 16-byte pieces per thread per stage
+  constexpr int kRowStep = kThreads / (kTsChunk / 4);
   extern __shared__ __align__(16) uint8_t ts_sm[];
   const int d = a.d, topk = a.topk;
   const int d4 = d >> 2;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
     thr[tid] = ~0ull;
   }
   __syncthreads();
-  for (int i = tid; i < kTsLanes * d4; i += kTsThreads) {
+  for (int i = tid; i < kTsLanes * d4; i += kThreads) {
     const int q = i / d4, c4 = i - q * d4;
     const int s = slot[q];
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -175,38 +179,37 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
   const int ntiles = static_cast<int>((nrows + kTsRows - 1) / kTsRows);
 
   // Issue side of the pipeline: stage = (tile ti, column chunk ci) into
-  // buffer bi.  Each thread copies two 16-byte pieces per stage: rows
-  // tid / 4 and tid / 4 + 64 of the tile, piece tid % 4.  The row ids of the
-  // next tile are fetched one tile ahead (nx*), so no cp.async waits on an
+  // buffer bi.  Each thread copies kNp 16-byte pieces per stage: rows
+  // tid / 4 + kRowStep h of the tile, piece tid % 4.  The row ids of the
+  // next tile are fetched one tile ahead (nx), so no cp.async waits on an
   // id load.
   const int piece = tid & 3;
   const int pr = tid >> 2;
   int ti = 0, ci = 0, bi = 0;
-  int64_t cur0 = 0, cur1 = 0, nx0 = 0, nx1 = 0;  // row ids (-1: past the rows)
+  int64_t cur[kNp], nx[kNp];  // row ids (-1: past the rows)
   auto row_of = [&](int t, int r) -> int64_t {
     const int64_t pos = static_cast<int64_t>(t) * kTsRows + r;
     if (pos >= nrows) return -1;
     return kIvf ? static_cast<int64_t>(lrows[pos]) : row0 + pos;
   };
-  if (ntiles > 0) {
-    nx0 = row_of(0, pr);
-    nx1 = row_of(0, pr + 64);
-  }
+#pragma unroll
+  for (int h = 0; h < kNp; ++h) nx[h] = ntiles > 0 ? row_of(0, pr + kRowStep * h) : -1;
   auto issue = [&]() {
     if (ti < ntiles) {
       if (ci == 0) {
-        cur0 = nx0;
-        cur1 = nx1;
-        if (ti + 1 < ntiles) {
-          nx0 = row_of(ti + 1, pr);
-          nx1 = row_of(ti + 1, pr + 64);
+#pragma unroll
+        for (int h = 0; h < kNp; ++h) {
+          cur[h] = nx[h];
+          if (ti + 1 < ntiles) nx[h] = row_of(ti + 1, pr + kRowStep * h);
         }
       }
       const int c = ci * kTsChunk + piece * 4;
       const bool cok = c < d;
       float* dst = rs + bi * (kTsRows * kTsChunk) + piece * 4;
-      ts_cp16(dst + pr * kTsChunk, a.X + (cur0 >= 0 && cok ? cur0 * d + c : 0), cur0 >= 0 && cok);
-      ts_cp16(dst + (pr + 64) * kTsChunk, a.X + (cur1 >= 0 && cok ? cur1 * d + c : 0), cur1 >= 0 && cok);
+#pragma unroll
+      for (int h = 0; h < kNp; ++h)
+        ts_cp16(dst + (pr + kRowStep * h) * kTsChunk, a.X + (cur[h] >= 0 && cok ? cur[h] * d + c : 0),
+                cur[h] >= 0 && cok);
       if (++ci == nchunks) {
         ci = 0;
         ++ti;
@@ -219,13 +222,13 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
 #pragma unroll
   for (int s = 0; s < kTsStages - 1; ++s) issue();
 
-  float acc[kTsRW][kTsQW];
+  float acc[RW][kTsQW];
 #pragma unroll
-  for (int j = 0; j < kTsRW; ++j)
+  for (int j = 0; j < RW; ++j)
 #pragma unroll
     for (int i = 0; i < kTsQW; ++i) acc[j][i] = 0.f;
 
-  const int myrow = warp * 16 + rg * kTsRW;  // first of this thread's 4 tile rows
+  const int myrow = warp * 4 * RW + rg * RW;  // first of this thread's RW tile rows
   int bc = 0;
   for (int t = 0; t < ntiles; ++t) {
     for (int kc = 0; kc < nchunks; ++kc) {
@@ -239,34 +242,34 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
       if (nq4 == kTsChunk / 4) {
 #pragma unroll
         for (int c4 = 0; c4 < kTsChunk / 4; ++c4) {
-          float4 qv[kTsQW], xv[kTsRW];
+          float4 qv[kTsQW], xv[RW];
 #pragma unroll
           for (int i = 0; i < kTsQW; ++i) qv[i] = qb[c4 * kTsLanes + i * 8];
 #pragma unroll
-          for (int j = 0; j < kTsRW; ++j) xv[j] = rb[j * (kTsChunk / 4) + c4];
+          for (int j = 0; j < RW; ++j) xv[j] = rb[j * (kTsChunk / 4) + c4];
 #pragma unroll
-          for (int j = 0; j < kTsRW; ++j)
+          for (int j = 0; j < RW; ++j)
 #pragma unroll
             for (int i = 0; i < kTsQW; ++i) acc[j][i] = ts_dot4(acc[j][i], xv[j], qv[i]);
         }
       } else {
         for (int c4 = 0; c4 < nq4; ++c4) {
-          float4 qv[kTsQW], xv[kTsRW];
+          float4 qv[kTsQW], xv[RW];
 #pragma unroll
           for (int i = 0; i < kTsQW; ++i) qv[i] = qb[c4 * kTsLanes + i * 8];
 #pragma unroll
-          for (int j = 0; j < kTsRW; ++j) xv[j] = rb[j * (kTsChunk / 4) + c4];
+          for (int j = 0; j < RW; ++j) xv[j] = rb[j * (kTsChunk / 4) + c4];
 #pragma unroll
-          for (int j = 0; j < kTsRW; ++j)
+          for (int j = 0; j < RW; ++j)
 #pragma unroll
             for (int i = 0; i < kTsQW; ++i) acc[j][i] = ts_dot4(acc[j][i], xv[j], qv[i]);
         }
       }
     }
 
-    // ---- tile t complete: two rounds (rows j = 0, 1 then 2, 3 of each
-    // thread, 64 rows per query per round) of candidates better than the
-    // query's k-th best, each followed by a rank merge
+    // ---- tile t complete: two rounds (the first then the second half of
+    // each thread's rows, 64 rows per query per round) of candidates better
+    // than the query's k-th best, each followed by a rank merge
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -275,8 +278,8 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
         if (q < npairs) {
           const unsigned long long th = thr[q];
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int j = 2 * h + jj;
+          for (int jj = 0; jj < RW / 2; ++jj) {
+            const int j = (RW / 2) * h + jj;
             const int64_t pos = static_cast<int64_t>(t) * kTsRows + myrow + j;
             if (pos < nrows) {
               const unsigned long long key = ts_key(acc[j][i], static_cast<uint32_t>(pos));
@@ -286,8 +289,8 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
         }
       }
       __syncthreads();
-      // warp w merges queries w, w + 8, w + 16, w + 24
-      for (int j = warp; j < npairs; j += kTsWarps) {
+      // warp w merges queries w, w + WARPS, ...
+      for (int j = warp; j < npairs; j += WARPS) {
         const int nc = cnt[j];
         if (nc == 0) continue;
         const int n0 = nb[j];
@@ -333,14 +336,14 @@ __global__ void __launch_bounds__(kTsThreads, 2) tile_scan_kernel(const TileScan
       __syncthreads();
     }
 #pragma unroll
-    for (int j = 0; j < kTsRW; ++j)
+    for (int j = 0; j < RW; ++j)
 #pragma unroll
       for (int i = 0; i < kTsQW; ++i) acc[j][i] = 0.f;
   }
   ts_wait<0>();
 
   // ---- output: positions -> row ids, empty slots ~0
-  for (int j = warp; j < npairs; j += kTsWarps) {
+  for (int j = warp; j < npairs; j += WARPS) {
     const int s = slot[j];
     const int m = nb[j];
     for (int r = lane; r < topk; r += 32) {
@@ -437,7 +440,7 @@ cudaError_t set_smem(size_t sm) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (done[dev] >= static_cast<int>(sm)) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(tile_scan_kernel<kIvf>,
+  const cudaError_t e = cudaFuncSetAttribute(tile_scan_kernel<kIvf, kTsWarps, kTsRW>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(sm));
   if (e == cudaSuccess) done[dev] = static_cast<int>(sm);
@@ -494,7 +497,7 @@ cudaError_t launch_list_scan_batched(const float* X, int d, const uint32_t* list
   const int64_t grid = std::min<int64_t>(k, np) + (np + kTsLanes - 1) / kTsLanes;
   if (grid <= 0) return cudaGetLastError();
   if (grid > INT32_MAX) return cudaErrorInvalidValue;
-  tile_scan_kernel<true><<<static_cast<unsigned>(grid), kTsThreads, sm, st>>>(a);
+  tile_scan_kernel<true, kTsWarps, kTsRW><<<static_cast<unsigned>(grid), kTsWarps * 32, sm, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -517,7 +520,7 @@ cudaError_t launch_flat_scan_batched(const float* X, int64_t n, int d, int nchun
   const int64_t grid = static_cast<int64_t>(nchunks) * a.nqc;
   if (grid <= 0) return cudaGetLastError();
   if (grid > INT32_MAX) return cudaErrorInvalidValue;
-  tile_scan_kernel<false><<<static_cast<unsigned>(grid), kTsThreads, sm, st>>>(a);
+  tile_scan_kernel<false, kTsWarps, kTsRW><<<static_cast<unsigned>(grid), kTsWarps * 32, sm, st>>>(a);
   return cudaGetLastError();
 }
 
