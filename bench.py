@@ -45,6 +45,7 @@ WORKLOADS = {
               "len U[16,512], mean pool + projection"),
 }
 IVF_N, IVF_D, IVF_K, IVF_ITERS, IVF_SEED = 3_270_000, 384, 4096, 20, 4
+SEARCH_NQ, SEARCH_NPROBE, SEARCH_TOPK = 10_000, 32, 10
 
 
 def parse_args():
@@ -57,6 +58,12 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--search-rows", type=int, default=IVF_N,
+                   help="search workload: index rows (a smaller index for profiling)")
+    p.add_argument("--search-k", type=int, default=IVF_K,
+                   help="search workload: centroids")
+    p.add_argument("--search-queries", type=int, default=SEARCH_NQ,
+                   help="search workload: queries per call")
     return p.parse_args()
 
 
@@ -334,7 +341,6 @@ def run_query(args, rank, local_rank):
     return 0
 
 
-SEARCH_NQ, SEARCH_NPROBE, SEARCH_TOPK = 10_000, 32, 10
 
 
 def run_search(args, rank, local_rank):
@@ -351,14 +357,15 @@ def run_search(args, rank, local_rank):
     from embedcuda import _lib, ann, kb
     from oracle import oracle
     torch.cuda.set_device(local_rank)
-    x_dev, perm, q_dev = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda", SEARCH_NQ)
+    n, k, nq = args.search_rows, args.search_k, args.search_queries
+    x_dev, perm, q_dev = ivf_corpus_torch(n, IVF_D, k, IVF_SEED, "cuda", nq)
     x = x_dev.cpu().numpy()
     qs = q_dev.cpu().numpy()
     del x_dev, q_dev
     torch.cuda.empty_cache()
     perm = perm.cpu().numpy().astype(np.int64)
     _lib.init([local_rank])
-    cent = ann.kmeans(x, perm, IVF_K, IVF_ITERS)
+    cent = ann.kmeans(x, perm, k, IVF_ITERS)
     counts, lists = ann.assign_all(x, cent)
     kb.load_index(x, (cent, counts, lists))
     L = _lib.lib()
@@ -382,14 +389,14 @@ def run_search(args, rank, local_rank):
     L.ecdbg_profile(0)
     scan_ms, scan_flops, scan_bytes = v[0].value, v[1].value, v[2].value
     # spot parity against the oracle (kb::top-k-ivf restated) on a few queries
-    for i in range(0, SEARCH_NQ, SEARCH_NQ // 4):
+    for i in range(0, nq, max(1, nq // 4)):
         rid, rsc = oracle.top_k_ivf(x, cent, counts, lists, SEARCH_NPROBE, qs[i], SEARCH_TOPK)
         if not (np.array_equal(ids[i][:len(rid)], rid) and np.array_equal(sc[i][:len(rsc)], rsc)):
             raise SystemExit(f"search parity failed on query {i}")
     # CPU baseline: the oracle's kb::top-k-ivf, one query at a time, one thread
     t0 = time.perf_counter()
     done = 0
-    while time.perf_counter() - t0 < 10.0 and done < SEARCH_NQ:
+    while not args.no_cpu_baseline and time.perf_counter() - t0 < 10.0 and done < nq:
         oracle.top_k_ivf(x, cent, counts, lists, SEARCH_NPROBE, qs[done], SEARCH_TOPK)
         done += 1
     cpu_el = time.perf_counter() - t0
@@ -400,17 +407,17 @@ def run_search(args, rank, local_rank):
     if sm_max:
         peak = props.multi_processor_count * 128 * sm_max * 1e6 / 1e12
     achieved = scan_flops / (scan_ms * 1e-3) / 1e12 if scan_ms > 0 else None
-    qps = SEARCH_NQ / el
+    qps = nq / el
     out = {"metric": "queries/s", "value": qps, "unit": "queries/s", "n_gpus": 1,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el,
            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic",
-           "config": {"workload": "ivf-search-3.27Mx384", "queries": SEARCH_NQ,
-                      "nprobe": SEARCH_NPROBE, "topk": SEARCH_TOPK, "k": IVF_K,
-                      "l2": "index 5.0 GB > L2",
+           "config": {"workload": f"ivf-search-{n / 1e6:g}Mx{IVF_D}", "queries": nq,
+                      "nprobe": SEARCH_NPROBE, "topk": SEARCH_TOPK, "k": k, "rows": n,
+                      "l2": f"index {n * IVF_D * 4 / 1e9:.1f} GB > L2",
                       "timing": "host wall clock around the synchronous ec_ivf_search call"},
            "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": int(qs.nbytes),
-                   "d2h_bytes_per_step": SEARCH_NQ * SEARCH_TOPK * 12},
+                   "d2h_bytes_per_step": nq * SEARCH_TOPK * 12},
            "roofline": {"bound": "fp32", "kernel": "tile_scan_kernel<true> (list scan)",
                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak if achieved and peak else None, "traffic": None,
@@ -421,7 +428,8 @@ def run_search(args, rank, local_rank):
                         "algorithmic_gb_per_step": scan_bytes / 1e9,
                         "algorithmic_note": "2 FLOP and 4 bytes per probed row and column"},
            "clocks": clocks,
-           "cpu_baseline": {"value": done / cpu_el, "unit": "queries/s", "cores": 1,
+           "cpu_baseline": None if args.no_cpu_baseline else {
+                            "value": done / cpu_el, "unit": "queries/s", "cores": 1,
                             "kind": "port",
                             "sample": f"{done} queries in {cpu_el:.1f} s (oracle kb::top-k-ivf, "
                                       "one thread; the reference runs one thread per probed "
