@@ -1,7 +1,9 @@
 """Two-GPU paths (run only when two GPUs are visible): the in-process
 multi-device split of ec_embed_batch must give the same embeddings as one
-device, and k-means over two devices (NCCL all-reduce of sums + counts)
-must agree with the single-device result up to float32 summation order."""
+device, k-means over two devices (NCCL all-reduce of sums + counts) must
+agree with the single-device result up to float32 summation order, and IVF /
+flat search with the queries split over the devices (each running the
+query-batched scan on its half) must equal kb::top-k-ivf / top-k-brute."""
 import os
 import subprocess
 import sys
@@ -17,7 +19,7 @@ CHILD = r"""
 import sys, os, json
 import numpy as np
 sys.path[:0] = [{repo!r}, os.path.join({repo!r}, "lisp-embed_b200")]
-from embedcuda import _lib, model, synth, ann
+from embedcuda import _lib, model, synth, ann, kb
 from oracle import oracle
 _lib.init([0, 1])
 d = synth.build_model_dir(synth.with_layers(synth.MINILM, 2), 0, {root!r})
@@ -31,7 +33,21 @@ counts, lists = ann.assign_all(x, cent2)
 rc, rl = oracle.assign_all(x, cent2)
 np.save({out!r} + "_emb.npy", two)
 np.save({out!r} + "_cent.npy", cent2)
-print(json.dumps({{"lists_equal": bool(np.array_equal(counts, rc) and np.array_equal(lists, rl))}}))
+kb.load_index(x, (cent2, counts, lists))
+qs, _ = synth.make_ivf_corpus(300, 384, 64, seed=21)
+ids_, sc_ = kb.search_ivf(qs, 10, nprobe=8)
+ivf_ok = True
+for i in range(len(qs)):
+    rid, rsc = oracle.top_k_ivf(x, cent2, counts, lists, 8, qs[i], 10)
+    ivf_ok &= bool(np.array_equal(ids_[i][:len(rid)], rid) and np.array_equal(sc_[i][:len(rsc)], rsc))
+kb.load_index(x, None)
+fid, fsc = kb.search_brute(qs[:24], 10)
+flat_ok = True
+for i in range(24):
+    rid, rsc = oracle.top_k_brute(x, qs[i], 10)
+    flat_ok &= bool(np.array_equal(fid[i], rid) and np.array_equal(fsc[i], rsc))
+print(json.dumps({{"lists_equal": bool(np.array_equal(counts, rc) and np.array_equal(lists, rl)),
+                  "ivf_search_equal": ivf_ok, "flat_search_equal": flat_ok}}))
 """
 
 
@@ -50,6 +66,7 @@ def test_two_device_embed_and_kmeans(tmp_path, synth_root):
                        capture_output=True, text=True, timeout=900)
     assert p.returncode == 0, p.stdout + p.stderr
     assert '"lists_equal": true' in p.stdout
+    assert '"ivf_search_equal": true' in p.stdout and '"flat_search_equal": true' in p.stdout
     from embedcuda import _lib, ann, model, synth
     from oracle import oracle
     _lib.init([0])
