@@ -25,7 +25,7 @@
   (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
            #:load-tokenizer #:embed-texts
            #:kmeans #:assign-all #:index-load #:index-load-files #:ann-build-file
-           #:top-k #:top-k-brute #:*nprobe*))
+           #:top-k #:top-k-brute #:top-k-batch #:*nprobe*))
 (in-package :cuda)
 
 (defparameter *library* (or (sb-ext:posix-getenv "EC_LIBRARY") "libembedcuda.so"))
@@ -291,3 +291,26 @@ forward (model:embed for a list of texts, in input order)."
 (defun top-k (q k)
   "kb::top-k (kb.lisp:366-368): list of (row . score), descending."
   (%search q k *ivf*))
+
+(defun top-k-batch (queries k)
+  "kb::top-k for a list of query vectors in one call (the library regroups a
+large batch by probed list): a list with one (row . score) list per query,
+each as top-k would return it."
+  (let* ((nq (length queries))
+         (d (if queries (length (first queries)) 0))
+         (qv (make-array (* nq d) :element-type 'single-float))
+         (ids (make-array (* nq k) :element-type '(signed-byte 64)))
+         (sc (make-array (* nq k) :element-type 'single-float)))
+    (loop for q in queries
+          for i from 0
+          do (replace qv (coerce q '(simple-array single-float (*))) :start1 (* i d)))
+    (when (plusp nq)
+      (with-saps ((qp qv) (ip ids) (sp sc))
+        (check (if *ivf*
+                   (%ivf-search qp nq *nprobe* k ip sp)
+                   (%flat-search qp nq k ip sp))
+               "search")))
+    (loop for i below nq
+          collect (loop for j from (* i k) below (* (1+ i) k)
+                        when (>= (aref ids j) 0)
+                          collect (cons (aref ids j) (aref sc j))))))
