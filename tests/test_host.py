@@ -75,3 +75,33 @@ def test_bench_flop_accounting():
     ids, offsets = synth.make_inputs("minilm", 1024, 0)
     total = bench.algorithmic_flops(synth.MINILM, offsets)
     assert 3.0e12 < total < 3.4e12  # the ~3.18e12 of the workload spec
+
+
+def test_bench_reference_arm_lines_for_other_workloads():
+    """--impl reference prints one JSON line and exits 0 for every workload
+    name (the reference arm times the embedding workloads only)."""
+    import json
+    import subprocess
+    import sys
+    from conftest import REPO
+    for wl in ("ivf", "query", "search", "tokenize"):
+        p = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", wl,
+                            "--steps", "1", "--warmup", "3"], cwd=REPO, capture_output=True,
+                           text=True, timeout=300)
+        assert p.returncode == 0, p.stderr
+        line = json.loads(p.stdout.strip().splitlines()[-1])
+        assert line["impl"] == "reference" and "unavailable" in line, wl
+
+
+def test_bench_search_options():
+    import bench
+    import sys
+    argv = sys.argv
+    try:
+        sys.argv = ["bench.py", "--workload", "search", "--search-rows", "800000", "--search-k", "1024",
+                    "--search-queries", "2500"]
+        a = bench.parse_args()
+    finally:
+        sys.argv = argv
+    assert (a.search_rows, a.search_k, a.search_queries) == (800000, 1024, 2500)
+    assert bench.SEARCH_NQ == 10_000 and bench.IVF_N == 3_270_000
