@@ -1153,15 +1153,19 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
                                            : static_cast<double>(lens[k]) * lens[k];
     EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
     if (!out_dev) {
-      std::vector<float> hout(static_cast<size_t>(nseq) * m.out_dim);
-      EC_TRY(check_cuda(cudaMemcpyAsync(hout.data(), dout, hout.size() * 4,
-                                        cudaMemcpyDeviceToHost, d.stream),
+      // pinned staging: the region reserved for the outputs sits just below
+      // the ids at the back (ensure_ws sizes it; the tables at the front end
+      // well before it)
+      const size_t obytes = static_cast<size_t>(nseq) * m.out_dim * 4;
+      float* hout = reinterpret_cast<float*>(static_cast<char*>(d.pin) + d.pin_bytes -
+                                             al256(static_cast<size_t>(T) * 4) - 256 - al256(obytes));
+      EC_TRY(check_cuda(cudaMemcpyAsync(hout, dout, obytes, cudaMemcpyDeviceToHost, d.stream),
                         "output download"));
       EC_TRY(sync_and_check(d, "forward"));
       prof_collect(d);
       for (int k = 0; k < nseq; ++k)
         std::memcpy(out_host + static_cast<size_t>(seqs[i + k]) * out_stride,
-                    hout.data() + static_cast<size_t>(k) * m.out_dim, static_cast<size_t>(m.out_dim) * 4);
+                    hout + static_cast<size_t>(k) * m.out_dim, static_cast<size_t>(m.out_dim) * 4);
     } else {
       EC_TRY(sync_and_check(d, "forward"));
       prof_collect(d);
