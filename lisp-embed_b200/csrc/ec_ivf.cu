@@ -368,6 +368,34 @@ static double probed_rows(Device& dv, const int32_t* dp, int64_t np) {
   return r;
 }
 
+// Tensor-core probe scores for a batch of at least 64 queries (d % 64 == 0,
+// k % 128 == 0, nprobe <= 128); EC_EXACT_PROBE keeps the exact SIMT scores.
+// Both give the same probes.
+static bool probe_tc_ok(const IndexW& ix, int64_t nq, int nprobe) {
+  static const bool off = getenv("EC_EXACT_PROBE") != nullptr;
+  return !off && nq >= 64 && nq < (int64_t{1} << 31) && ix.d % 64 == 0 && ix.d <= 8192 && ix.k % 128 == 0 &&
+         ix.k <= 8192 && nprobe <= 128;
+}
+
+// bf16 copy of the index centroids and their norm bound, made on first use
+static int ensure_cent_bf16(Device& dv, cudaStream_t st) {
+  IndexW& ix = dv.index;
+  if (ix.cent_b) return EC_OK;
+  void* cb = nullptr;
+  void* cm = nullptr;
+  EC_TRY(dev_alloc(dv, &cb, static_cast<size_t>(ix.k) * ix.d * 2, "probe centroids bf16"));
+  ix.owned.push_back(cb);
+  EC_TRY(dev_alloc(dv, &cm, 256, "probe centroid norm"));
+  ix.owned.push_back(cm);
+  EC_TRY(check_cuda(cudaMemsetAsync(cm, 0, 4, st), "centroid norm clear"));
+  EC_TRY(check_cuda(launch_round_rows(ix.cent, ix.k, ix.d, static_cast<__nv_bfloat16*>(cb), nullptr,
+                                      static_cast<unsigned*>(cm), st),
+                    "round centroids"));
+  ix.cent_b = cb;
+  ix.cent_max = static_cast<float*>(cm);
+  return EC_OK;
+}
+
 // Query-batched scan when each probed list gets 8 queries on average (IVF)
 // or there are 8 queries (flat); EC_SCAN_PER_QUERY keeps one CTA per
 // (query, list / chunk).  Search workspaces are 256-byte aligned, so Q is.
@@ -415,8 +443,12 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     // otherwise
     const bool batched = scan_batched_ok(ix, nq, nprobe, topk, ivf);
     const size_t s_b = batched && ivf ? a256(batched_list_scan_ws(ix.k, nq * nprobe)) : 0;
+    const bool tcp = ivf && probe_tc_ok(ix, nq, nprobe);
+    const size_t s_qb = tcp ? a256(static_cast<size_t>(nq) * d * 2) : 0;
+    const size_t s_qn = tcp ? a256(static_cast<size_t>(nq) * 4) : 0;
+    if (tcp) EC_TRY(ensure_cent_bf16(dv, st));
     void* ws;
-    EC_TRY(ensure_search_ws(dv, s_q + s_s + s_p + s_c + s_i + s_f + s_b, &ws));
+    EC_TRY(ensure_search_ws(dv, s_q + s_s + s_p + s_c + s_i + s_f + s_b + s_qb + s_qn, &ws));
     char* w = static_cast<char*>(ws);
     float* dq = reinterpret_cast<float*>(w);
     float* dS = reinterpret_cast<float*>(w + s_q);
@@ -428,11 +460,42 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     EC_TRY(check_cuda(cudaMemcpyAsync(dq, q + a * d, static_cast<size_t>(nq) * d * 4,
                                       cudaMemcpyHostToDevice, st), "query upload"));
     mark(1);
-    if (ivf) {
+    if (ivf && tcp) {
+      // bf16 queries (and norm bounds) x bf16 centroids on the tensor cores,
+      // then the window re-check against the exact scores
+      char* wq = w + s_q + s_s + s_p + s_c + s_i + s_f + s_b;
+      __nv_bfloat16* dqb = reinterpret_cast<__nv_bfloat16*>(wq);
+      float* dqn = reinterpret_cast<float*>(wq + s_qb);
+      EC_TRY(check_cuda(launch_round_rows(dq, nq, d, dqb, dqn, nullptr, st), "round queries"));
+      GemmLaunch g;
+      g.A = dqb;
+      g.lda = d;
+      g.W = static_cast<const __nv_bfloat16*>(ix.cent_b);
+      g.ldw = d;
+      g.M = static_cast<int>(nq);
+      g.N = ix.k;
+      g.K = d;
+      g.bias = nullptr;
+      g.resid = nullptr;
+      g.ldr = 0;
+      g.out = dS;
+      g.ldo = ix.k;
+      g.epi = kEpiF32;
+      g.bn = 0;
+      g.status = dv.status;
+      EC_TRY(check_cuda(launch_gemm(g, st, dv.num_sms), "probe scores"));
+      mark(2);
+      EC_TRY(check_cuda(launch_probe_select_tc(dS, dq, ix.cent, dqn, ix.cent_max, 2.0f * argcand_rel(d), nq,
+                                               ix.k, d, nprobe, dp, st),
+                        "probe select"));
+      mark(3);
+    } else if (ivf) {
       EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st), "probe scores"));
       mark(2);
       EC_TRY(check_cuda(launch_probe_select(dS, nq, ix.k, nprobe, dp, st), "probe select"));
       mark(3);
+    }
+    if (ivf) {
       // event-timed while profiling (class 3: scans; algorithmic work = the
       // probed lists' rows, d multiply-adds and d * 4 bytes each)
       double rows = 0;

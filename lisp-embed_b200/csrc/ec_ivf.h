@@ -26,6 +26,12 @@ cudaError_t launch_segsum(const float* X, const uint32_t* lists, const int64_t* 
 cudaError_t launch_update(const float* sums, int k, int d, float* cent, cudaStream_t st);
 cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, int32_t* probes,
                                 cudaStream_t st);
+// the same probes from tensor-core scores S (|S - exact| <= rel2 |q| max|c| / 2):
+// candidates within the window re-scored exactly; Q, C the fp32 queries and
+// centroids, qnorm / cmax upper bounds of their norms
+cudaError_t launch_probe_select_tc(const float* S, const float* Q, const float* C, const float* qnorm,
+                                   const float* cmax, float rel2, int64_t nq, int k, int d, int nprobe,
+                                   int32_t* probes, cudaStream_t st);
 cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
                              const int32_t* probes, int nprobe, const float* Q, int64_t nq,
                              int topk, unsigned long long* cand, cudaStream_t st);

@@ -353,73 +353,54 @@ __device__ __forceinline__ void sel_find(const uint32_t* hist, uint32_t need, ui
   }
 }
 
-__global__ void __launch_bounds__(kSelThreads) probe_select_kernel(const float* S, int k, int nprobe,
-                                                                   int32_t* probes) {
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t found[2];
-  __shared__ int nsel;
-  extern __shared__ unsigned long long sel[];  // [P2], P2 = pow2 >= nprobe
-  const int64_t q = blockIdx.x;
-  const float* sq = S + q * k;
+struct SelSmem {
+  uint32_t* hist;  // [256]
+  uint32_t* found; // [2]
+  int* nsel;
+};
+
+// One 8-bit radix pass over the fields f(m) (m < nv) with (f & mask) ==
+// prefix, one warp atomic per distinct bin; returns (bin, count below it).
+template <class F>
+__device__ __forceinline__ uint2 sel_pass(F field, int nv, uint32_t mask, uint32_t prefix, int shift,
+                                          uint32_t need, const SelSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31;
-  const int nv = tid < k ? (k - tid + kSelThreads - 1) / kSelThreads : 0;  // keys of this thread
-  uint32_t key[kSelPer];
+  sm.hist[tid] = 0;
+  __syncthreads();
 #pragma unroll
-  for (int m = 0; m < kSelPer; ++m) key[m] = m < nv ? score_key32(sq[tid + kSelThreads * m]) : 0u;
+  for (int m = 0; m < kSelPer; ++m) {
+    const uint32_t f = field(m);
+    const bool on = m < nv && (f & mask) == prefix;
+    const uint32_t bin = on ? (f >> shift) & 255u : 256u;
+    const unsigned grp = __match_any_sync(0xffffffffu, bin);
+    if (on && lane == __ffs(grp) - 1) atomicAdd(&sm.hist[bin], static_cast<uint32_t>(__popc(grp)));
+  }
+  __syncthreads();
+  if (tid < 32) sel_find(sm.hist, need, sm.found);
+  __syncthreads();
+  const uint2 r = make_uint2(sm.found[0], sm.found[1]);
+  __syncthreads();  // found[] is rewritten by the next pass
+  return r;
+}
 
-  // histogram pass over the keys with (field & mask) == prefix, one warp
-  // atomic per distinct bin
-  auto pass = [&](auto field, uint32_t mask, uint32_t prefix, int shift, uint32_t need) {
-    hist[tid] = 0;
-    __syncthreads();
-#pragma unroll
-    for (int m = 0; m < kSelPer; ++m) {
-      const uint32_t f = field(m);
-      const bool on = m < nv && (f & mask) == prefix;
-      const uint32_t bin = on ? (f >> shift) & 255u : 256u;
-      const unsigned grp = __match_any_sync(0xffffffffu, bin);
-      if (on && lane == __ffs(grp) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(grp)));
-    }
-    __syncthreads();
-    if (tid < 32) sel_find(hist, need, found);
-    __syncthreads();
-    const uint32_t b = found[0], before = found[1];
-    __syncthreads();  // found[] is rewritten by the next pass
-    return make_uint2(b, before);
-  };
-
-  // 1) the 32-bit score key v of the nprobe-th smallest key
-  uint32_t prefix = 0, mask = 0, need = static_cast<uint32_t>(nprobe);
+// The 32-bit key v of the need-th smallest of key[m] (m < nv); *left = how
+// many keys equal to v are among the need smallest.
+__device__ __forceinline__ uint32_t sel_kth(const uint32_t (&key)[kSelPer], int nv, uint32_t need,
+                                            const SelSmem& sm, uint32_t* left) {
+  uint32_t prefix = 0, mask = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    const uint2 r = pass([&](int m) { return key[m]; }, mask, prefix, shift, need);
+    const uint2 r = sel_pass([&](int m) { return key[m]; }, nv, mask, prefix, shift, need, sm);
     prefix |= r.x << shift;
     mask |= 0xffu << shift;
     need -= r.y;
   }
-  const uint32_t v = prefix;
-  // 2) among the keys equal to v, the `need` lowest indices: index <= ix
-  uint32_t ip = 0, imask = 0, need2 = need;
-  for (int shift = 8; shift >= 0; shift -= 8) {
-    const uint2 r = pass(
-        [&](int m) { return key[m] == v ? static_cast<uint32_t>(tid + kSelThreads * m) : 0xffffffffu; },
-        imask | 0xffff0000u, ip, shift, need2);
-    ip |= r.x << shift;
-    imask |= 0xffu << shift;
-    need2 -= r.y;
-  }
-  // 3) gather exactly nprobe keys, sort them, emit the indices
-  int P = 1;
-  while (P < nprobe) P <<= 1;
-  if (tid == 0) nsel = 0;
-  for (int i = tid; i < P; i += kSelThreads) sel[i] = ~0ull;
-  __syncthreads();
-#pragma unroll
-  for (int m = 0; m < kSelPer; ++m) {
-    const uint32_t idx = static_cast<uint32_t>(tid + kSelThreads * m);
-    if (m < nv && (key[m] < v || (key[m] == v && idx <= ip)))
-      sel[atomicAdd(&nsel, 1)] = (static_cast<unsigned long long>(key[m]) << 32) | idx;
-  }
-  __syncthreads();
+  *left = need;
+  return prefix;
+}
+
+// Ascending bitonic sort of sel[0, P) (P a power of two), whole block.
+__device__ __forceinline__ void sel_sort(unsigned long long* sel, int P) {
+  const int tid = threadIdx.x;
   for (int size = 2; size <= P; size <<= 1)
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = tid; i < P; i += kSelThreads) {
@@ -435,8 +416,151 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(const float* 
       }
       __syncthreads();
     }
-  for (int i = tid; i < nprobe; i += kSelThreads)
-    probes[q * nprobe + i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
+}
+
+// Writes the indices of the nprobe smallest (key[m], index tid + 256 m) to
+// out[0, nprobe) in order; sel needs pow2(nprobe) slots.
+__device__ void select_emit(const uint32_t (&key)[kSelPer], int nv, int nprobe, const SelSmem& sm,
+                            unsigned long long* sel, int32_t* out) {
+  const int tid = threadIdx.x;
+  uint32_t need;
+  const uint32_t v = sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &need);
+  // among the keys equal to v, the `need` lowest indices: index <= ip
+  uint32_t ip = 0, imask = 0;
+  for (int shift = 8; shift >= 0; shift -= 8) {
+    const uint2 r = sel_pass(
+        [&](int m) { return key[m] == v ? static_cast<uint32_t>(tid + kSelThreads * m) : 0xffffffffu; }, nv,
+        imask | 0xffff0000u, ip, shift, need, sm);
+    ip |= r.x << shift;
+    imask |= 0xffu << shift;
+    need -= r.y;
+  }
+  int P = 1;
+  while (P < nprobe) P <<= 1;
+  if (tid == 0) *sm.nsel = 0;
+  for (int i = tid; i < P; i += kSelThreads) sel[i] = ~0ull;
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < kSelPer; ++m) {
+    const uint32_t idx = static_cast<uint32_t>(tid + kSelThreads * m);
+    if (m < nv && (key[m] < v || (key[m] == v && idx <= ip)))
+      sel[atomicAdd(sm.nsel, 1)] = (static_cast<unsigned long long>(key[m]) << 32) | idx;
+  }
+  __syncthreads();
+  sel_sort(sel, P);
+  for (int i = tid; i < nprobe; i += kSelThreads) out[i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
+}
+
+__global__ void __launch_bounds__(kSelThreads) probe_select_kernel(const float* S, int k, int nprobe,
+                                                                   int32_t* probes) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t found[2];
+  __shared__ int nsel;
+  extern __shared__ unsigned long long sel[];  // [P2], P2 = pow2 >= nprobe
+  const int64_t q = blockIdx.x;
+  const float* sq = S + q * k;
+  const int tid = threadIdx.x;
+  const int nv = tid < k ? (k - tid + kSelThreads - 1) / kSelThreads : 0;  // keys of this thread
+  uint32_t key[kSelPer];
+#pragma unroll
+  for (int m = 0; m < kSelPer; ++m) key[m] = m < nv ? score_key32(sq[tid + kSelThreads * m]) : 0u;
+  select_emit(key, nv, nprobe, SelSmem{hist, found, &nsel}, sel, probes + q * nprobe);
+}
+
+// ---- probe selection from tensor-core scores --------------------------------
+// S holds bf16-operand tcgen05 scores (fp32 accumulation) of query q against
+// every centroid; |S - exact| <= w / 2 with w = rel2 |q| max|c| (the bound of
+// the k-means assignment window, qnorm and cmax upper bounds of the norms).
+// With t the approximate nprobe-th largest score, every centroid of the exact
+// first nprobe has S >= t - w, and every centroid below t - w has an exact
+// score below the exact nprobe-th.  So the candidates S >= t - w are
+// re-scored with the reference's sequential single-float dot, sorted by
+// (exact score desc, index asc), and the first nprobe are exactly
+// kb.lisp:352's.  A query with more than kTcCand candidates, or a window that
+// is not a finite number, scores every centroid exactly instead.
+constexpr int kTcCand = 256;
+
+__device__ __forceinline__ float key32_score(uint32_t v) {
+  return key_score(static_cast<unsigned long long>(v) << 32);
+}
+
+__device__ __forceinline__ float exact_dot(const float* qs, const float* c, int d) {
+  const float4* c4 = reinterpret_cast<const float4*>(c);
+  float acc = 0.f;
+  for (int j = 0; j < d; j += 4) {
+    const float4 x = __ldg(c4 + (j >> 2));
+    acc = __fadd_rn(acc, __fmul_rn(qs[j], x.x));
+    acc = __fadd_rn(acc, __fmul_rn(qs[j + 1], x.y));
+    acc = __fadd_rn(acc, __fmul_rn(qs[j + 2], x.z));
+    acc = __fadd_rn(acc, __fmul_rn(qs[j + 3], x.w));
+  }
+  return acc;
+}
+
+__global__ void __launch_bounds__(kSelThreads) probe_select_tc_kernel(
+    const float* S, const float* Q, const float* C, const float* qnorm, const float* cmax, float rel2, int k,
+    int d, int nprobe, int32_t* probes) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t found[2];
+  __shared__ int nsel, ncand;
+  extern __shared__ __align__(16) unsigned char tc_sm[];
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(tc_sm);  // [max(kTcCand, pow2(nprobe))]
+  int P2 = 1;
+  while (P2 < nprobe) P2 <<= 1;
+  const int nsel_slots = P2 > kTcCand ? P2 : kTcCand;
+  int* cand = reinterpret_cast<int*>(sel + nsel_slots);  // [kTcCand]
+  float* qs = reinterpret_cast<float*>(cand + kTcCand);  // [d]
+  const SelSmem sm{hist, found, &nsel};
+  const int64_t q = blockIdx.x;
+  const float* sq = S + q * k;
+  const int tid = threadIdx.x;
+  for (int j = tid; j < d; j += kSelThreads) qs[j] = Q[q * d + j];
+  const int nv = tid < k ? (k - tid + kSelThreads - 1) / kSelThreads : 0;
+  uint32_t key[kSelPer];
+#pragma unroll
+  for (int m = 0; m < kSelPer; ++m) key[m] = m < nv ? score_key32(sq[tid + kSelThreads * m]) : 0u;
+  uint32_t left;
+  const float t = key32_score(sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &left));
+  const float w = __fmul_ru(__fmul_ru(rel2, qnorm[q]), *cmax);
+  const float lo = __fsub_rd(t, w);
+  bool ok = w >= 0.f && w < INFINITY && lo > -INFINITY && lo < INFINITY;  // block-uniform
+  if (tid == 0) ncand = 0;
+  __syncthreads();
+  if (ok) {
+#pragma unroll
+    for (int m = 0; m < kSelPer; ++m)
+      if (m < nv && key32_score(key[m]) >= lo) {
+        const int p = atomicAdd(&ncand, 1);
+        if (p < kTcCand) cand[p] = tid + kSelThreads * m;
+      }
+  }
+  __syncthreads();
+  const int n = ncand;
+  ok = ok && n <= kTcCand && n >= nprobe;
+  if (ok) {
+    int P = 1;
+    while (P < n) P <<= 1;
+    for (int i = tid; i < P; i += kSelThreads) {
+      unsigned long long v = ~0ull;
+      if (i < n) {
+        const int c = cand[i];
+        v = (static_cast<unsigned long long>(score_key32(exact_dot(qs, C + static_cast<int64_t>(c) * d, d)))
+             << 32) |
+            static_cast<uint32_t>(c);
+      }
+      sel[i] = v;
+    }
+    __syncthreads();
+    sel_sort(sel, P);
+    for (int i = tid; i < nprobe; i += kSelThreads)
+      probes[q * nprobe + i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
+  } else {
+#pragma unroll
+    for (int m = 0; m < kSelPer; ++m)
+      if (m < nv)
+        key[m] = score_key32(exact_dot(qs, C + static_cast<int64_t>(tid + kSelThreads * m) * d, d));
+    select_emit(key, nv, nprobe, sm, sel, probes + q * nprobe);
+  }
 }
 
 // Exact scores of `cnt` rows against one query, top `topk` by (score desc,
@@ -630,6 +754,20 @@ cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, i
   const size_t sm = static_cast<size_t>(P) * 8;
   cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   probe_select_kernel<<<static_cast<unsigned>(nq), kSelThreads, sm, st>>>(S, k, nprobe, probes);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_probe_select_tc(const float* S, const float* Q, const float* C, const float* qnorm,
+                                   const float* cmax, float rel2, int64_t nq, int k, int d, int nprobe,
+                                   int32_t* probes, cudaStream_t st) {
+  if (k > kSelThreads * kSelPer || nprobe < 1 || nprobe > k || d % 4) return cudaErrorInvalidValue;
+  int P = 1;
+  while (P < nprobe) P <<= 1;
+  const size_t sm = static_cast<size_t>(P > kTcCand ? P : kTcCand) * 8 + kTcCand * 4 + static_cast<size_t>(d) * 4;
+  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  cudaFuncSetAttribute(probe_select_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  probe_select_tc_kernel<<<static_cast<unsigned>(nq), kSelThreads, sm, st>>>(S, Q, C, qnorm, cmax, rel2, k, d,
+                                                                            nprobe, probes);
   return cudaGetLastError();
 }
 

@@ -87,6 +87,8 @@ struct IndexW {
   std::vector<void*> owned;
   void* sws = nullptr;         // search workspace
   size_t sws_bytes = 0;
+  void* cent_b = nullptr;      // bf16 centroids for tensor-core probe scores (lazy, owned)
+  float* cent_max = nullptr;   // upper bound of the centroid norms
 };
 
 struct ProfAcc {

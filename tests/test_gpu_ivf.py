@@ -188,3 +188,35 @@ def test_flat_search_query_batched(ec, corpus):
         for i in range(len(qs)):
             rid, rsc = oracle.top_k_brute(x, qs[i], topk)
             assert np.array_equal(fid[i], rid) and np.array_equal(fsc[i], rsc), (topk, i)
+
+
+@pytest.mark.parametrize("nprobe", [16, 32, 128])
+def test_ivf_search_tensor_core_probes(ec, corpus, nprobe):
+    """Batches of >= 64 queries with k % 128 == 0 score the probes on the
+    tensor cores and re-score the centroids inside the error window exactly:
+    the probe order (and so every result) must equal kb::top-k-ivf's."""
+    x = corpus
+    cent = x[synth.make_ivf_sample(len(x), 6)[:256]]
+    counts, lists = ann.assign_all(x, cent)
+    kb.load_index(x, (cent, counts, lists))
+    qs, _ = synth.make_ivf_corpus(160, 384, 64, seed=102)
+    qs = np.concatenate([qs, x[:16]], axis=0)
+    _check_ivf(x, cent, counts, lists, qs, nprobe, 10)
+
+
+def test_ivf_search_tensor_core_probe_ties_and_fallback(ec, corpus):
+    """300 identical centroids (exact ties, decided by the lower index) out
+    of 384: queries next to them have more window candidates than the fast
+    path keeps and take the exact scoring of every centroid; the others stay
+    on the fast path.  Both must give kb::top-k-ivf's results."""
+    x = corpus
+    rest = x[synth.make_ivf_sample(len(x), 7)[:84]]
+    cent = np.concatenate([rest[:40], np.repeat(x[5:6], 300, axis=0), rest[40:]], axis=0).astype(np.float32)
+    assert cent.shape[0] == 384
+    counts, lists = ann.assign_all(x, cent)
+    kb.load_index(x, (cent, counts, lists))
+    near = x[5:6] + 0.01 * np.random.default_rng(3).standard_normal((40, 384)).astype(np.float32)
+    far, _ = synth.make_ivf_corpus(60, 384, 64, seed=103)
+    qs = np.concatenate([near / np.linalg.norm(near, axis=1, keepdims=True), far], axis=0).astype(np.float32)
+    _check_ivf(x, cent, counts, lists, qs, 32, 10)
+    _check_ivf(x, cent, counts, lists, qs, 128, 10)
