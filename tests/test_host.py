@@ -105,3 +105,31 @@ def test_bench_search_options():
         sys.argv = argv
     assert (a.search_rows, a.search_k, a.search_queries) == (800000, 1024, 2500)
     assert bench.SEARCH_NQ == 10_000 and bench.IVF_N == 3_270_000
+
+
+def test_search_cpu_baseline_threads():
+    """The search workload's CPU baseline runs the oracle's kb::top-k-ivf on
+    several threads at once; the C restatement is re-entrant, so concurrent
+    calls give the single-threaded results."""
+    import threading
+    import bench
+    from oracle import oracle
+    x, _ = synth.make_ivf_corpus(4000, 64, 16, seed=4)
+    cent = x[:32].copy()
+    counts, lists = oracle.assign_all(x, cent)
+    qs, _ = synth.make_ivf_corpus(24, 64, 16, seed=5)
+    done, el, threads = bench.search_cpu_baseline(x, cent, counts, lists, qs, 8, 10, 5.0, threads=4)
+    assert threads == 4 and done == len(qs) and el > 0
+    ref = [oracle.top_k_ivf(x, cent, counts, lists, 8, q, 10) for q in qs]
+    got = [None] * len(qs)
+
+    def run(i):
+        got[i] = oracle.top_k_ivf(x, cent, counts, lists, 8, qs[i], 10)
+
+    th = [threading.Thread(target=run, args=(i,)) for i in range(len(qs))]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    for (ri, rs), (gi, gs) in zip(ref, got):
+        assert np.array_equal(ri, gi) and np.array_equal(rs, gs)
