@@ -201,10 +201,23 @@ struct Tokenizer {
 
   // WordPiece: byte tries of every token (root 0: the candidates of a word's
   // first piece are matched as they are) and of the "##" tokens without the
-  // "##" (root 1: continuation candidates); edge (node << 8 | byte) -> child,
-  // node -> id of the token ending there (-1: none)
+  // "##" (root 1: continuation candidates); edge (node << 8 | byte) -> child
+  // while building, node -> id of the token ending there (-1: none).  For
+  // matching, the two roots get direct 256-entry child tables and every other
+  // node its children as a byte-sorted run (few children each).
   std::unordered_map<uint64_t, int> edge;
   std::vector<int> node_id;
+  std::vector<int> root_child;            // [2 * 256]
+  std::vector<uint32_t> kid_off;          // [nodes + 1]
+  std::vector<unsigned char> kid_byte;
+  std::vector<int> kid_node;
+  int child(int node, unsigned char b) const {
+    if (node < 2) return root_child[static_cast<size_t>(node) * 256 + b];
+    const uint32_t e = kid_off[static_cast<size_t>(node) + 1];
+    for (uint32_t i = kid_off[static_cast<size_t>(node)]; i < e; ++i)
+      if (kid_byte[i] >= b) return kid_byte[i] == b ? kid_node[i] : -1;
+    return -1;
+  }
   void trie_insert(int root, const std::string& t, size_t from, int id) {
     int node = root;
     for (size_t b = from; b < t.size(); ++b) {
@@ -228,6 +241,27 @@ struct Tokenizer {
       if (kv.first.size() > 2 && kv.first[0] == '#' && kv.first[1] == '#')
         trie_insert(1, kv.first, 2, kv.second);
     }
+    // flatten: (parent, byte, child) sorted by parent then byte
+    std::vector<std::pair<uint64_t, int>> es(edge.begin(), edge.end());
+    std::sort(es.begin(), es.end());
+    const size_t nn = node_id.size();
+    root_child.assign(2 * 256, -1);
+    kid_off.assign(nn + 1, 0);
+    kid_byte.clear();
+    kid_node.clear();
+    for (const auto& e : es) {
+      const size_t parent = static_cast<size_t>(e.first >> 8);
+      const unsigned char b = static_cast<unsigned char>(e.first & 0xff);
+      if (parent < 2) {
+        root_child[parent * 256 + b] = e.second;
+      } else {
+        ++kid_off[parent + 1];
+        kid_byte.push_back(b);
+        kid_node.push_back(e.second);
+      }
+    }
+    for (size_t i = 0; i < nn; ++i) kid_off[i + 1] += kid_off[i];
+    edge.clear();
   }
 };
 
@@ -249,21 +283,6 @@ std::vector<U32> split_spaces(const U32& s) {
       start = i + 1;
     }
   if (s.size() > start) out.emplace_back(s, start, s.size() - start);
-  return out;
-}
-
-std::vector<U32> pretokenize_wordpiece(const U32& s) {
-  std::vector<U32> out;
-  for (const U32& w : split_spaces(s)) {
-    size_t start = 0;
-    for (size_t i = 0; i < w.size(); ++i)
-      if (punctuation_p(w[i])) {
-        if (i > start) out.emplace_back(w, start, i - start);
-        out.emplace_back(1, w[i]);
-        start = i + 1;
-      }
-    if (start < w.size()) out.emplace_back(w, start, w.size() - start);
-  }
   return out;
 }
 
@@ -364,9 +383,8 @@ void wordpiece_word(const Tokenizer& tk, const char32_t* w, size_t len, std::vec
     size_t best_end = start;
     size_t c = start;
     for (size_t b = bo[start]; b < u8.size(); ++b) {
-      auto it = tk.edge.find((static_cast<uint64_t>(node) << 8) | static_cast<unsigned char>(u8[b]));
-      if (it == tk.edge.end()) break;
-      node = it->second;
+      node = tk.child(node, static_cast<unsigned char>(u8[b]));
+      if (node < 0) break;
       if (b + 1 == bo[c + 1]) {  // a character boundary: a piece may end here
         ++c;
         const int id = tk.node_id[static_cast<size_t>(node)];
@@ -465,10 +483,30 @@ bool encode(const Tokenizer& tk, const char* text, size_t n, std::vector<int32_t
   thread_local std::vector<int> pid;
   pid.clear();
   if (tk.kind == kWordPiece) {
-    for (const U32& w : pretokenize_wordpiece(s)) {
-      if (pid.size() >= keep) break;
-      wordpiece_word(tk, w.data(), w.size(), pid);
+    // pretokenize-wordpiece's pieces, in order, as spans of s: runs between
+    // whitespace, each punctuation character a piece of its own
+    const char32_t* p = s.data();
+    const size_t n = s.size();
+    size_t start = 0;
+    bool full = false;
+    auto piece = [&](size_t b, size_t len) {
+      if (pid.size() >= keep) {
+        full = true;
+        return;
+      }
+      wordpiece_word(tk, p + b, len, pid);
+    };
+    for (size_t i = 0; i < n && !full; ++i) {
+      if (whitespace_p(p[i])) {
+        if (i > start) piece(start, i - start);
+        start = i + 1;
+      } else if (punctuation_p(p[i])) {
+        if (i > start) piece(start, i - start);
+        if (!full) piece(i, 1);
+        start = i + 1;
+      }
     }
+    if (!full && n > start) piece(start, n - start);
   } else if (tk.kind == kBpe) {
     for (const U32& w : pretokenize_bytelevel(s, tk.llama3)) {
       if (pid.size() >= keep) break;
