@@ -406,6 +406,36 @@ void wordpiece_word(const Tokenizer& tk, const char32_t* w, size_t len, std::vec
   }
 }
 
+// wordpiece_word for an ASCII word (every byte a character)
+void wordpiece_word_ascii(const Tokenizer& tk, const unsigned char* w, size_t len, std::vector<int>& out) {
+  if (len > 100) {
+    out.push_back(-1);
+    return;
+  }
+  size_t start = 0;
+  while (start < len) {
+    int node = start == 0 ? 0 : 1;
+    int best_id = -1;
+    size_t best_end = start;
+    for (size_t b = start; b < len; ++b) {
+      node = tk.child(node, w[b]);
+      if (node < 0) break;
+      const int id = tk.node_id[static_cast<size_t>(node)];
+      if (id >= 0) {
+        best_id = id;
+        best_end = b + 1;
+      }
+    }
+    if (best_id >= 0) {
+      start += (best_end - start) + (start > 0 ? 2 : 0);
+      out.push_back(best_id);
+    } else {
+      out.push_back(-1);
+      start = len;
+    }
+  }
+}
+
 // ids of the merged parts (-1: not in the vocabulary)
 void bpe_word(const Tokenizer& tk, const U32& word, std::vector<int>& out) {
   std::vector<std::string> parts;
@@ -470,17 +500,53 @@ bool unigram_word(const Tokenizer& tk, const U32& s, std::vector<int>& ids) {
 }
 
 // tk-encode; false when a token has no id and there is no unknown token
+bool finish(const Tokenizer& tk, const std::vector<int>& pid, size_t keep, std::vector<int32_t>& out);
+
 bool encode(const Tokenizer& tk, const char* text, size_t n, std::vector<int32_t>& out) {
   thread_local U32 raw, s;
+  thread_local std::vector<int> pid;
+  const size_t keep = static_cast<size_t>(std::max(0, tk.max_len - 2));
+  bool ascii = tk.kind == kWordPiece;
+  for (size_t i = 0; ascii && i < n; ++i) ascii = static_cast<unsigned char>(text[i]) < 0x80;
+  if (ascii) {
+    // the same pieces as below for a pure-ASCII text, on its bytes: ASCII
+    // lowering, whitespace runs split, punctuation single pieces
+    thread_local std::string low;
+    low.assign(text, n);
+    if (tk.lowercase)
+      for (char& c : low)
+        if (c >= 'A' && c <= 'Z') c = static_cast<char>(c + 32);
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(low.data());
+    pid.clear();
+    size_t start = 0;
+    bool full = false;
+    auto piece = [&](size_t b, size_t len) {
+      if (pid.size() >= keep) {
+        full = true;
+        return;
+      }
+      wordpiece_word_ascii(tk, p + b, len, pid);
+    };
+    for (size_t i = 0; i < n && !full; ++i) {
+      if (whitespace_p(p[i])) {
+        if (i > start) piece(start, i - start);
+        start = i + 1;
+      } else if (punctuation_p(p[i])) {
+        if (i > start) piece(start, i - start);
+        if (!full) piece(i, 1);
+        start = i + 1;
+      }
+    }
+    if (!full && n > start) piece(start, n - start);
+    return finish(tk, pid, keep, out);
+  }
   if (!utf8_decode(text, n, raw)) return false;
   if (tk.lowercase) s = lowercase(raw);
   else s.swap(raw);
-  const size_t keep = static_cast<size_t>(std::max(0, tk.max_len - 2));
   // piece ids before the unknown-token substitution (-1: no id); pieces past
   // the truncation point cannot change the result for WordPiece and BPE, so
   // their words are skipped (unigram words are all scanned: the Lisp signals
   // on a word it cannot segment anywhere in the text)
-  thread_local std::vector<int> pid;
   pid.clear();
   if (tk.kind == kWordPiece) {
     // pretokenize-wordpiece's pieces, in order, as spans of s: runs between
@@ -529,6 +595,12 @@ bool encode(const Tokenizer& tk, const char* text, size_t n, std::vector<int32_t
       if (!unigram_word(tk, w, uni)) return false;
     pid.assign(uni.size(), -1);
   }
+  return finish(tk, pid, keep, out);
+}
+
+// specials around the first `keep` piece ids, unknown pieces -> the unknown
+// token (false: an unknown piece and no unknown token)
+bool finish(const Tokenizer& tk, const std::vector<int>& pid, size_t keep, std::vector<int32_t>& out) {
   const size_t nb = std::min(pid.size(), keep);
   const int unk = tk.id_of(tk.unk), cls = tk.id_of(tk.cls), sep = tk.id_of(tk.sep);
   out.clear();

@@ -173,6 +173,9 @@ def test_random_texts_match_restatement(texts):
         ("bpe_llama3_json", ref.from_json(_p("bpe_llama3.json")), full),
         ("wordpiece_txt", ref.from_vocab_txt(_p("vocab.txt")), full),
         ("unigram", ref.from_unigram_scores(_p("unigram.json")), golden_chars),
+        # pure-ASCII texts take the library's byte-level WordPiece path
+        ("wordpiece_json", ref.from_json(_p("wordpiece.json")), ascii_ + list("\t\n\r\x0b\x0c\x00\x07")),
+        ("wordpiece_txt", ref.from_vocab_txt(_p("vocab.txt")), ascii_ + list("\t\n\r\x0b\x0c\x00\x07")),
     ]
     for name, theirs, alpha in cases:
         ours = _ours(name)
@@ -187,3 +190,10 @@ def test_random_texts_match_restatement(texts):
                 want = None
             assert got == want, (name, t)
         ours.close()
+    # words of exactly 100 and 101 characters (the limit past which a word is
+    # one unknown piece), ASCII and not
+    wp = ref.from_json(_p("wordpiece.json"))
+    ours = _ours("wordpiece_json")
+    for t in ["ka" * 50 + " x", "ka" * 50 + "k y", "é" + "ka" * 49 + "k z", "é" + "ka" * 50 + " w"]:
+        assert ours.encode(t).tolist() == wp.encode(t), t
+    ours.close()
