@@ -6,6 +6,7 @@ make-tokenizer (:119-197), ``encode`` is tk-encode (:201-244) for one text and
 from __future__ import annotations
 
 import ctypes as C
+import threading
 
 import numpy as np
 
@@ -15,6 +16,7 @@ from . import _lib
 class Tokenizer:
     def __init__(self, handle):
         self.handle = handle
+        self._tls = threading.local()  # per-thread output buffer, reused across calls
 
     @classmethod
     def from_json(cls, path):
@@ -61,17 +63,24 @@ class Tokenizer:
     def encode_batch(self, texts, threads=0):
         """(ids int32[total], offsets int64[n + 1]) for a list of str.  The
         texts go over as one UTF-8 buffer with a pointer per text."""
-        raw = [t.encode("utf-8") for t in texts]
-        n = len(raw)
-        lens = np.fromiter((len(b) for b in raw), np.int64, count=n)
-        buf = np.frombuffer(b"".join(raw) + b"\0", np.uint8)
+        n = len(texts)
+        if all(t.isascii() for t in texts):
+            # one encode for the whole batch: ASCII characters are bytes
+            lens = np.fromiter((len(t) for t in texts), np.int64, count=n)
+            buf = np.frombuffer(("".join(texts) + "\0").encode("ascii"), np.uint8)
+        else:
+            raw = [t.encode("utf-8") for t in texts]
+            lens = np.fromiter((len(b) for b in raw), np.int64, count=n)
+            buf = np.frombuffer(b"".join(raw) + b"\0", np.uint8)
         starts = np.zeros(max(n, 1), np.int64)
         if n:
             starts[1:] = np.cumsum(lens)[:-1]
         ptrs = (buf.ctypes.data + starts).astype(np.uint64)
         offs = np.zeros(n + 1, np.int64)
         cap = 512 * n
-        ids = np.empty(max(cap, 1), np.int32)
+        ids = getattr(self._tls, "ids", None)
+        if ids is None or ids.size < max(cap, 1):
+            ids = self._tls.ids = np.empty(max(cap, 1), np.int32)
         _lib.check(_lib.lib().ec_tokenize(self.handle, ptrs.ctypes.data_as(C.POINTER(C.c_char_p)),
                                           _lib.ptr(lens, C.c_int64) if n else None, n,
                                           _lib.ptr(ids, C.c_int32), cap, _lib.ptr(offs, C.c_int64),

@@ -197,3 +197,25 @@ def test_random_texts_match_restatement(texts):
     for t in ["ka" * 50 + " x", "ka" * 50 + "k y", "é" + "ka" * 49 + "k z", "é" + "ka" * 50 + " w"]:
         assert ours.encode(t).tolist() == wp.encode(t), t
     ours.close()
+
+
+def test_encode_batch_from_threads(texts):
+    """encode_batch on one tokenizer from several Python threads at once
+    (the library call runs without the GIL) gives each caller its own ids."""
+    import threading
+    tk = _ours("wordpiece_json")
+    want = [tk.encode_batch(texts[i::4]) for i in range(4)]
+    got = [None] * 4
+
+    def run(i):
+        for _ in range(5):
+            got[i] = tk.encode_batch(texts[i::4])
+
+    th = [threading.Thread(target=run, args=(i,)) for i in range(4)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    for (wi, wo), (gi, go) in zip(want, got):
+        assert np.array_equal(wi, gi) and np.array_equal(wo, go)
+    tk.close()
