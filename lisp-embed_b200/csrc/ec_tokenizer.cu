@@ -186,6 +186,7 @@ struct Tokenizer {
   std::unordered_map<std::string, int> vocab;
   std::vector<std::string> inv;
   std::unordered_map<std::string, int> merges;  // "a\x01b" -> rank
+  std::vector<std::pair<std::string, std::string>> merge_list;  // (a, b) in file order
   std::unordered_map<std::string, double> scores;
   bool lowercase = true;
   int max_len = 512;
@@ -211,6 +212,26 @@ struct Tokenizer {
   std::vector<uint32_t> kid_off;          // [nodes + 1]
   std::vector<unsigned char> kid_byte;
   std::vector<int> kid_node;
+  // BPE on integers: every vocabulary and merge string interned as a symbol;
+  // (left, right) -> (rank, merged symbol) with the rank merges[] gives the
+  // pair's string key; characters without a symbol take part in no merge and
+  // have no id
+  std::unordered_map<std::string, int> sym;
+  std::vector<int> sym_id;                                 // vocab id or -1
+  std::unordered_map<uint64_t, std::pair<int, int>> pair_rank;
+  std::vector<int> char_sym;                               // code points < 0x10000
+  int intern(const std::string& str) {
+    auto it = sym.find(str);
+    if (it != sym.end()) return it->second;
+    const int s = static_cast<int>(sym_id.size());
+    sym.emplace(str, s);
+    auto v = vocab.find(str);
+    sym_id.push_back(v == vocab.end() ? -1 : v->second);
+    return s;
+  }
+  void add_merge(const std::string& a, const std::string& b, int rank);
+  void build_bpe();
+  int symbol_of(char32_t c) const;
   int child(int node, unsigned char b) const {
     if (node < 2) return root_child[static_cast<size_t>(node) * 256 + b];
     const uint32_t e = kid_off[static_cast<size_t>(node) + 1];
@@ -272,6 +293,40 @@ std::string merge_key(const std::string& a, const std::string& b) {
   k += '\x01';
   k += b;
   return k;
+}
+
+void Tokenizer::add_merge(const std::string& a, const std::string& b, int rank) {
+  merges[merge_key(a, b)] = rank;
+  merge_list.emplace_back(a, b);
+}
+
+void Tokenizer::build_bpe() {
+  sym.clear();
+  sym_id.clear();
+  pair_rank.clear();
+  for (const auto& kv : vocab) intern(kv.first);
+  for (const auto& m : merge_list) {
+    const int a = intern(m.first), b = intern(m.second);
+    const int ab = intern(m.first + m.second);
+    pair_rank[(static_cast<uint64_t>(a) << 32) | static_cast<uint32_t>(b)] =
+        std::make_pair(merges.at(merge_key(m.first, m.second)), ab);
+  }
+  char_sym.assign(0x10000, -1);
+  std::string u;
+  for (uint32_t c = 0; c < 0x10000; ++c) {
+    u.clear();
+    utf8_append(static_cast<char32_t>(c), u);
+    auto it = sym.find(u);
+    if (it != sym.end()) char_sym[c] = it->second;
+  }
+}
+
+int Tokenizer::symbol_of(char32_t c) const {
+  if (c < 0x10000) return char_sym[c];
+  std::string u;
+  utf8_append(c, u);
+  auto it = sym.find(u);
+  return it == sym.end() ? -1 : it->second;
 }
 
 std::vector<U32> split_spaces(const U32& s) {
@@ -438,20 +493,26 @@ void wordpiece_word_ascii(const Tokenizer& tk, const unsigned char* w, size_t le
 
 // ids of the merged parts (-1: not in the vocabulary)
 void bpe_word(const Tokenizer& tk, const U32& word, std::vector<int>& out) {
-  std::vector<std::string> parts;
-  parts.reserve(word.size());
-  for (char32_t c : word) {
-    std::string p;
-    utf8_append(c, p);
-    parts.push_back(std::move(p));
-  }
-  // rank of each adjacent pair, recomputed only next to a merge
-  std::vector<int> rank(parts.empty() ? 0 : parts.size() - 1);
+  // the parts as symbols (-1: a character with no symbol)
+  thread_local std::vector<int> parts;
+  thread_local std::vector<int> rank;
+  parts.clear();
+  for (char32_t c : word) parts.push_back(tk.symbol_of(c));
+  // rank of each adjacent pair (-1: none), recomputed only next to a merge;
+  // merged[i]: the symbol a merge of pair i makes
+  thread_local std::vector<int> merged;
   auto rank_of = [&](size_t i) {
-    auto it = tk.merges.find(merge_key(parts[i], parts[i + 1]));
-    return it == tk.merges.end() ? -1 : it->second;
+    merged[i] = -1;
+    if (parts[i] < 0 || parts[i + 1] < 0) return -1;
+    auto it = tk.pair_rank.find((static_cast<uint64_t>(parts[i]) << 32) | static_cast<uint32_t>(parts[i + 1]));
+    if (it == tk.pair_rank.end()) return -1;
+    merged[i] = it->second.second;
+    return it->second.first;
   };
-  for (size_t i = 0; i + 1 < parts.size(); ++i) rank[i] = rank_of(i);
+  const size_t np = parts.empty() ? 0 : parts.size() - 1;
+  rank.assign(np, -1);
+  merged.assign(np, -1);
+  for (size_t i = 0; i < np; ++i) rank[i] = rank_of(i);
   while (parts.size() > 1) {
     int best = -1;
     size_t bi = 0;
@@ -461,13 +522,14 @@ void bpe_word(const Tokenizer& tk, const U32& word, std::vector<int>& out) {
         bi = i;
       }
     if (best < 0) break;
-    parts[bi] += parts[bi + 1];
+    parts[bi] = merged[bi];
     parts.erase(parts.begin() + static_cast<long>(bi) + 1);
     rank.erase(rank.begin() + static_cast<long>(bi));
+    merged.erase(merged.begin() + static_cast<long>(bi));
     if (bi < rank.size()) rank[bi] = rank_of(bi);
     if (bi > 0) rank[bi - 1] = rank_of(bi - 1);
   }
-  for (const auto& p : parts) out.push_back(tk.id_of(p));
+  for (const int p : parts) out.push_back(p >= 0 ? tk.sym_id[static_cast<size_t>(p)] : -1);
 }
 
 bool unigram_word(const Tokenizer& tk, const U32& s, std::vector<int>& ids) {
@@ -577,10 +639,13 @@ bool encode(const Tokenizer& tk, const char* text, size_t n, std::vector<int32_t
     for (const U32& w : pretokenize_bytelevel(s, tk.llama3)) {
       if (pid.size() >= keep) break;
       if (tk.byte_level) {
-        const std::string b = utf8(w);
-        U32 mapped;
-        mapped.reserve(b.size());
-        for (unsigned char ch : b) mapped.push_back(byte_map().to[ch]);
+        thread_local std::string b;
+        thread_local U32 mapped;
+        b.clear();
+        for (char32_t c : w) utf8_append(c, b);
+        mapped.clear();
+        const ByteMap& bm = byte_map();
+        for (unsigned char ch : b) mapped.push_back(bm.to[ch]);
         bpe_word(tk, mapped, pid);
       } else {
         bpe_word(tk, w, pid);
@@ -786,10 +851,10 @@ int from_json(const char* path, Tokenizer& t) {
         for (const JVal& m : ms->a) {
           if (m.kind == JVal::Arr && m.a.size() >= 2 && m.a[0].kind == JVal::Str &&
               m.a[1].kind == JVal::Str) {
-            t.merges[merge_key(m.a[0].s, m.a[1].s)] = rank++;
+            t.add_merge(m.a[0].s, m.a[1].s, rank++);
           } else if (m.kind == JVal::Str) {
             const size_t sp = m.s.find(' ');
-            if (sp != std::string::npos) t.merges[merge_key(m.s.substr(0, sp), m.s.substr(sp + 1))] = rank++;
+            if (sp != std::string::npos) t.add_merge(m.s.substr(0, sp), m.s.substr(sp + 1), rank++);
           }
         }
     return EC_OK;
@@ -802,6 +867,7 @@ std::mutex g_mu;
 std::vector<std::unique_ptr<Tokenizer>> g_tok;
 
 int add(std::unique_ptr<Tokenizer> t, int* handle) {
+  if (t->kind == kBpe) t->build_bpe();
   std::lock_guard<std::mutex> lk(g_mu);
   for (size_t i = 0; i < g_tok.size(); ++i)
     if (!g_tok[i]) {
@@ -876,7 +942,7 @@ int ec_tokenizer_bpe(const char* vocab_json, const char* merges_txt, int lowerca
     if (l.empty() || l[0] == '#') continue;
     const size_t sp = l.find(' ');
     if (sp == std::string::npos) continue;
-    t->merges[merge_key(l.substr(0, sp), l.substr(sp + 1))] = rank++;
+    t->add_merge(l.substr(0, sp), l.substr(sp + 1), rank++);
   }
   t->lowercase = lowercase != 0;
   t->byte_level = byte_level != 0;
