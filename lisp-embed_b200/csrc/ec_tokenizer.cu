@@ -342,9 +342,11 @@ std::vector<U32> split_spaces(const U32& s) {
 }
 
 // pretokenize-gpt2 / pretokenize-llama3: same branches, same order
-std::vector<U32> pretokenize_bytelevel(const U32& s, bool llama3) {
+// the pieces as (start, length) spans of s, in order
+using Spans = std::vector<std::pair<size_t, size_t>>;
+void pretokenize_bytelevel(const U32& s, bool llama3, Spans& out) {
   static const char* kContr[] = {"s", "t", "m", "d", "re", "ve", "ll"};
-  std::vector<U32> out;
+  out.clear();
   const size_t n = s.size();
   auto alpha_at = [&](size_t j) { return j < n && alpha_p(s[j]); };
   auto digit_at = [&](size_t j) { return j < n && digit_p(s[j]); };
@@ -366,10 +368,10 @@ std::vector<U32> pretokenize_bytelevel(const U32& s, bool llama3) {
       }
       if (m >= 0) {
         const size_t L = std::strlen(kContr[m]);
-        out.emplace_back(s, i, 1 + L);
+        out.emplace_back(i, 1 + L);
         i += 1 + L;
       } else {
-        out.emplace_back(1, c);
+        out.emplace_back(i, 1);
         i += 1;
       }
       continue;
@@ -378,35 +380,34 @@ std::vector<U32> pretokenize_bytelevel(const U32& s, bool llama3) {
                 : (alpha_at(i) || (c != '\r' && c != '\n' && !digit_at(i) && alpha_at(i + 1)))) {
       size_t k = !llama3 ? (c == ' ' ? i + 1 : i) : (alpha_at(i) ? i : i + 1);
       while (alpha_at(k)) ++k;
-      out.emplace_back(s, i, k - i);
+      out.emplace_back(i, k - i);
       i = k;
       continue;
     }
     if (!llama3 && (digit_at(i) || (c == ' ' && digit_at(i + 1)))) {
       size_t k = c == ' ' ? i + 1 : i;
       while (digit_at(k)) ++k;
-      out.emplace_back(s, i, k - i);
+      out.emplace_back(i, k - i);
       i = k;
       continue;
     }
     if (llama3 && digit_at(i)) {
-      out.emplace_back(1, c);
+      out.emplace_back(i, 1);
       i += 1;
       continue;
     }
     if (punct_at(i) || (c == ' ' && punct_at(i + 1))) {
       size_t k = c == ' ' ? i + 1 : i;
       while (punct_at(k)) ++k;
-      out.emplace_back(s, i, k - i);
+      out.emplace_back(i, k - i);
       i = k;
       continue;
     }
     size_t k = i;
     while (k < n && whitespace_p(s[k])) ++k;
-    out.emplace_back(s, i, k - i);
+    out.emplace_back(i, k - i);
     i = k;
   }
-  return out;
 }
 
 std::vector<U32> pretokenize_metaspace(const U32& s) {
@@ -492,12 +493,12 @@ void wordpiece_word_ascii(const Tokenizer& tk, const unsigned char* w, size_t le
 }
 
 // ids of the merged parts (-1: not in the vocabulary)
-void bpe_word(const Tokenizer& tk, const U32& word, std::vector<int>& out) {
+void bpe_word(const Tokenizer& tk, const char32_t* word, size_t len, std::vector<int>& out) {
   // the parts as symbols (-1: a character with no symbol)
   thread_local std::vector<int> parts;
   thread_local std::vector<int> rank;
   parts.clear();
-  for (char32_t c : word) parts.push_back(tk.symbol_of(c));
+  for (size_t i = 0; i < len; ++i) parts.push_back(tk.symbol_of(word[i]));
   // rank of each adjacent pair (-1: none), recomputed only next to a merge;
   // merged[i]: the symbol a merge of pair i makes
   thread_local std::vector<int> merged;
@@ -636,19 +637,22 @@ bool encode(const Tokenizer& tk, const char* text, size_t n, std::vector<int32_t
     }
     if (!full && n > start) piece(start, n - start);
   } else if (tk.kind == kBpe) {
-    for (const U32& w : pretokenize_bytelevel(s, tk.llama3)) {
+    thread_local Spans spans;
+    pretokenize_bytelevel(s, tk.llama3, spans);
+    for (const auto& sp : spans) {
       if (pid.size() >= keep) break;
+      const char32_t* w = s.data() + sp.first;
       if (tk.byte_level) {
         thread_local std::string b;
         thread_local U32 mapped;
         b.clear();
-        for (char32_t c : w) utf8_append(c, b);
+        for (size_t i = 0; i < sp.second; ++i) utf8_append(w[i], b);
         mapped.clear();
         const ByteMap& bm = byte_map();
         for (unsigned char ch : b) mapped.push_back(bm.to[ch]);
-        bpe_word(tk, mapped, pid);
+        bpe_word(tk, mapped.data(), mapped.size(), pid);
       } else {
-        bpe_word(tk, w, pid);
+        bpe_word(tk, w, sp.second, pid);
       }
     }
   } else {
