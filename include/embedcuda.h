@@ -104,9 +104,18 @@ int ec_embed_batch_device(const int32_t *d_ids, const int64_t *offsets, int nseq
  * x[sample[c]] (ann.lisp:83-86), or as init[c] when `init` is not NULL.  Each iteration assigns every training row
  * to its nearest centroid by inner product (ties -> lowest index,
  * ann.lisp:69-77) and replaces each non-empty centroid by the mean of its
- * rows (ann.lisp:107-122).  Rows are sharded across the library's devices and
- * the per-device sums and counts are combined with an NCCL all-reduce.
- * `centroids` receives k x d floats.  Replaces ann::kmeans (ann.lisp:79-125). */
+ * rows (ann.lisp:107-122).  The training set is split into contiguous
+ * shards, one per device (or per process after ec_comm_init, where rank r
+ * passes the r-th contiguous piece of the sample).  Each rank assigns its
+ * shard; the per-cluster sums then pass down the ranks in sample order over
+ * NCCL (rank r continues rank r-1's accumulators with its own rows) and the
+ * last rank divides and broadcasts the centroids, so every float add follows
+ * the reference's serial loop and the result does not depend on the number
+ * of devices.  EC_KMEANS_ALLREDUCE=1 instead all-reduces per-rank sums (one
+ * ncclAllReduce per iteration; the cross-rank sums then take another order).
+ * A failed exchange aborts the communicators (process mode: call
+ * ec_comm_init again).  `centroids` receives k x d floats.  Replaces
+ * ann::kmeans (ann.lisp:79-125). */
 int ec_kmeans(const float *x, int64_t n, int d, const int64_t *sample, int64_t nsample,
               int k, int iters, const float *init, float *centroids);
 
@@ -155,8 +164,13 @@ int ec_flat_search(const float *q, int nq, int topk, int64_t *ids, float *scores
  * nq x min(256, ceil(n / 8192)) x topk x 8 bytes of it (nq <= 65535) and
  * larger calls fail with EC_EINVAL before any launch.  Every call on a device
  * shares that array, so calls whose kernels overlap in time race; calls in
- * order on one stream do not.  The first call on each device looks up the
- * array's address, so make it before any stream capture begins.  Needs no
+ * order on one stream do not.  The array is placed in device memory when
+ * the library's module holding it loads on a device: at ec_init for the
+ * library's devices, otherwise at the first call with nq > 0 (CUDA loads
+ * modules lazily), so a host that reserves its device arena up front should
+ * call ec_init, or make one search, before it takes the arena.  The first
+ * call in each CUDA context looks up the array's address (cached per device
+ * and context), so make it before any stream capture begins.  Needs no
  * ec_init. */
 int ec_flat_search_noalloc(const float *d_x, int64_t n, int d, const float *d_q, int nq,
                            int topk, int64_t *d_ids, float *d_scores, void *stream);
@@ -239,8 +253,9 @@ int ec_comm_id_size(void);
 /* Rank 0 creates the id; the caller ships it to the other ranks. */
 int ec_comm_get_id(void *id_out);
 /* Join a `world`-rank communicator as `rank` (after ec_init on one device).
- * ec_kmeans then all-reduces across processes instead of local devices: each
- * rank passes its own shard of training rows and the same `init`. */
+ * ec_kmeans then exchanges across processes instead of local devices: rank r
+ * passes the r-th contiguous piece of the training sample (in sample order)
+ * and every rank the same `init`. */
 int ec_comm_init(int rank, int world, const void *id);
 
 #ifdef __cplusplus

@@ -7,6 +7,7 @@
 #ifndef EMBEDCUDA_DEBUG_H
 #define EMBEDCUDA_DEBUG_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -63,6 +64,16 @@ long long ecdbg_launches(void);
  * ec_assign_all (scores re-checked exactly) and rows that took the exact
  * single-float scan, since the last reset; reset != 0 clears them. */
 int ecdbg_assign_rows(long long *tc_rows, long long *exact_rows, int reset);
+
+/* binaryVersion / ptxVersion (major * 10 + minor) of the library's device
+ * code as the CUDA runtime loaded it on the current device: 100 for sm_100. */
+int ecdbg_kernel_arch(int *binary_version, int *ptx_version);
+
+/* Copy the device copy of an uploaded tensor (device 0) to host memory, as
+ * stored after ec_upload_tensor: F32 and F16 uploads as f32 (F16 widened on
+ * the device), BF16 as bf16.  nbytes must equal the stored size; *dtype
+ * receives EC_F32 or EC_BF16. */
+int ecdbg_tensor_read(const char *name, void *host, size_t nbytes, int *dtype);
 
 /* Failure-path check of the bounded waits: launches one CTA that waits on an
  * mbarrier no thread arrives on, with a limit of `limit_ms` milliseconds.

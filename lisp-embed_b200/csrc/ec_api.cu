@@ -292,6 +292,10 @@ int ec_init(const int* devices, int ndev) {
     if (!rc) rc = check_cuda(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "stream");
     if (!rc) rc = dev_alloc(*d, reinterpret_cast<void**>(&d->status), 256, "status word");
     if (!rc) rc = check_cuda(cudaMemset(d->status, 0, 256), "status clear");
+    // place ec_flat_search_noalloc's static scratch array now, with the
+    // library's other device memory, rather than at its first call
+    void* scratch = nullptr;
+    if (!rc) rc = noalloc_scratch_current(&scratch);
     if (rc) break;
   }
   if (rc) {

@@ -1,16 +1,30 @@
 // ec_comm.cu -- NCCL loaded at run time (dlopen), so the library links no
 // NCCL and shares the one already in the process (PyTorch's) when there is
-// one.  Used only by k-means: one all-reduce (f32 sum) of the per-device
-// centroid sums + counts per Lloyd iteration.
+// one.  Used only by k-means, whose centroid update is the path's one real
+// exchange step:
 //
-// Two modes: several local devices in one process (ncclCommInitAll, one host
-// thread per device) and one process per GPU (ec_comm_get_id / ec_comm_init
-// with ncclCommInitRank).  Collective failures are detected with a bounded
-// host-side wait on ncclCommGetAsyncError and end in ncclCommAbort, never a
-// hang.
+//  * exact mode (default): the per-cluster accumulators travel down a chain
+//    of ranks in sample order (ncclSend / ncclRecv): rank r continues the
+//    sums of ranks 0..r-1 with its own rows, so every float add happens in
+//    the order of ann.lisp's serial loop; the last rank divides and
+//    broadcasts the centroids (ncclBroadcast);
+//  * all-reduce mode (EC_KMEANS_ALLREDUCE=1): one ncclAllReduce (f32 sum) of
+//    the per-rank sums + counts, faster for many ranks but the cross-rank
+//    float sums take a different order from the serial loop.
+//
+// Two ways to form the ranks: several local devices in one process
+// (ncclCommInitAll, one host thread per device) and one process per GPU
+// (ec_comm_get_id / ec_comm_init with ncclCommInitRank).  Every wait on a
+// collective is a bounded host loop on the stream and ncclCommGetAsyncError.
+// A rank that fails (error, timeout, or failure before its collective)
+// raises a shared flag so the other local ranks stop waiting at once; the
+// caller then aborts every communicator of the clique (comm_abort_all) and
+// forgets them before any device memory is freed, so no handle is used or
+// destroyed after its abort and no cudaFree waits behind a stuck collective.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
@@ -27,19 +41,27 @@ struct NcclApi {
   decltype(&ncclCommInitRank) commInitRank = nullptr;
   decltype(&ncclCommInitAll) commInitAll = nullptr;
   decltype(&ncclAllReduce) allReduce = nullptr;
+  decltype(&ncclBroadcast) broadcast = nullptr;
+  decltype(&ncclSend) send = nullptr;
+  decltype(&ncclRecv) recv = nullptr;
   decltype(&ncclCommDestroy) commDestroy = nullptr;
   decltype(&ncclCommAbort) commAbort = nullptr;
   decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
-  decltype(&ncclGroupStart) groupStart = nullptr;
-  decltype(&ncclGroupEnd) groupEnd = nullptr;
   decltype(&ncclGetErrorString) errStr = nullptr;
 };
 
 static NcclApi g_nccl;
 static std::vector<ncclComm_t> g_comms;  // one per local device, or one (process mode)
 static bool g_process_mode = false;
+static bool g_process_dead = false;      // process-mode communicator aborted
+static std::atomic<bool> g_failed{false};
 
-// test hook: EC_FAKE_NCCL_FAIL=1 makes loading fail as if NCCL were absent
+static std::atomic<int> g_arrived{0};
+
+// test hooks: EC_FAKE_NCCL_FAIL=1 makes loading fail as if NCCL were absent;
+// EC_FAKE_COMM_FAIL=<local index> makes that device's thread fail at the
+// rendezvous before the first exchange (the failure-before-the-collective
+// path, as after a failed allocation)
 static int load_nccl() {
   if (g_nccl.h) return EC_OK;
   if (const char* f = getenv("EC_FAKE_NCCL_FAIL"))
@@ -52,24 +74,27 @@ static int load_nccl() {
     if (h) break;
   }
   if (!h) return set_error(EC_ENCCL, "cannot load NCCL (libnccl.so.2): %s", dlerror());
-#define EC_SYM(field, name)                                                  \
-  g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(h, name));  \
-  if (!g_nccl.field) {                                                       \
-    dlclose(h);                                                              \
-    return set_error(EC_ENCCL, "NCCL lacks %s", name);                       \
+  NcclApi api;
+#define EC_SYM(field, name)                                            \
+  api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name));  \
+  if (!api.field) {                                                    \
+    dlclose(h);                                                        \
+    return set_error(EC_ENCCL, "NCCL lacks %s", name);                 \
   }
   EC_SYM(getUniqueId, "ncclGetUniqueId");
   EC_SYM(commInitRank, "ncclCommInitRank");
   EC_SYM(commInitAll, "ncclCommInitAll");
   EC_SYM(allReduce, "ncclAllReduce");
+  EC_SYM(broadcast, "ncclBroadcast");
+  EC_SYM(send, "ncclSend");
+  EC_SYM(recv, "ncclRecv");
   EC_SYM(commDestroy, "ncclCommDestroy");
   EC_SYM(commAbort, "ncclCommAbort");
   EC_SYM(getAsyncError, "ncclCommGetAsyncError");
-  EC_SYM(groupStart, "ncclGroupStart");
-  EC_SYM(groupEnd, "ncclGroupEnd");
   EC_SYM(errStr, "ncclGetErrorString");
 #undef EC_SYM
-  g_nccl.h = h;
+  api.h = h;
+  g_nccl = api;
   return EC_OK;
 }
 
@@ -83,12 +108,29 @@ void comm_destroy() {
     if (c && g_nccl.commDestroy) g_nccl.commDestroy(c);
   g_comms.clear();
   g_process_mode = false;
+  g_process_dead = false;
+  g_failed = false;
   G().comm = nullptr;
   G().rank = 0;
   G().world = 1;
 }
 
+void comm_abort_all() {
+  for (ncclComm_t c : g_comms)
+    if (c && g_nccl.commAbort) g_nccl.commAbort(c);
+  g_comms.clear();
+  if (g_process_mode) g_process_dead = true;
+  g_failed = false;
+}
+
 bool comm_process_mode() { return g_process_mode; }
+
+void comm_begin() {
+  g_failed = false;
+  g_arrived = 0;
+}
+
+void comm_mark_failed() { g_failed = true; }
 
 int comm_ensure_local() {
   if (g_process_mode) return EC_OK;
@@ -105,28 +147,12 @@ int comm_ensure_local() {
   return rc;
 }
 
-// Wait for the collective on `st` with a bounded host loop; abort the
-// communicator on an asynchronous NCCL error or timeout.
-static int wait_collective(ncclComm_t c, cudaStream_t st, double timeout_s) {
-  const auto t0 = std::chrono::steady_clock::now();
-  while (true) {
-    cudaError_t q = cudaStreamQuery(st);
-    if (q == cudaSuccess) return EC_OK;
-    if (q != cudaErrorNotReady) return check_cuda(q, "all-reduce");
-    ncclResult_t ae = ncclSuccess;
-    g_nccl.getAsyncError(c, &ae);
-    if (ae != ncclSuccess && ae != ncclInProgress) {
-      g_nccl.commAbort(c);
-      return nccl_err(ae, "all-reduce (communicator aborted)");
-    }
-    const double el =
-        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (el > timeout_s) {
-      g_nccl.commAbort(c);
-      return set_error(EC_ENCCL, "all-reduce timed out after %.0f s (communicator aborted)", el);
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
+int comm_check_ready() {
+  if (!g_process_mode) return EC_OK;
+  if (g_process_dead || g_comms.size() != 1)
+    return set_error(EC_ESTATE, "the communicator was aborted after a failed collective; "
+                                "call ec_comm_init again");
+  return EC_OK;
 }
 
 static double comm_timeout() {
@@ -135,15 +161,107 @@ static double comm_timeout() {
   return t > 0 ? t : 120.0;
 }
 
+// Wait for the collective on `st` with a bounded host loop.  On an
+// asynchronous NCCL error, a timeout or another rank's failure it raises the
+// shared flag and returns an error; the communicators are aborted by the
+// caller once every local rank has returned (comm_abort_all).
+static int wait_collective(ncclComm_t c, cudaStream_t st, const char* what) {
+  const double timeout_s = comm_timeout();
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return EC_OK;
+    if (q != cudaErrorNotReady) {
+      g_failed = true;
+      return check_cuda(q, what);
+    }
+    ncclResult_t ae = ncclSuccess;
+    g_nccl.getAsyncError(c, &ae);
+    if (ae != ncclSuccess && ae != ncclInProgress) {
+      g_failed = true;
+      return nccl_err(ae, what);
+    }
+    if (g_failed) return set_error(EC_ENCCL, "%s: another rank failed", what);
+    const double el =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) {
+      g_failed = true;
+      return set_error(EC_ENCCL, "%s timed out after %.0f s", what, el);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+static ncclComm_t comm_of(int local_index) {
+  return g_process_mode ? g_comms[0] : g_comms[local_index];
+}
+
+int comm_rendezvous(int local_index, int nlocal) {
+  const char* v = getenv("EC_FAKE_COMM_FAIL");
+  if (v && *v && atoi(v) == local_index) {
+    g_failed = true;
+    return set_error(EC_ENCCL, "injected failure before the first exchange (EC_FAKE_COMM_FAIL)");
+  }
+  ++g_arrived;
+  const double timeout_s = comm_timeout();
+  const auto t0 = std::chrono::steady_clock::now();
+  while (g_arrived.load() < nlocal) {
+    if (g_failed) return set_error(EC_ENCCL, "another rank failed before the first exchange");
+    const double el =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) {
+      g_failed = true;
+      return set_error(EC_ENCCL, "ranks did not reach the first exchange within %.0f s", el);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  return g_failed ? set_error(EC_ENCCL, "another rank failed before the first exchange") : EC_OK;
+}
+
 int comm_allreduce_sum_f32(int local_index, float* buf, size_t count, cudaStream_t st) {
-  ncclComm_t c = g_process_mode ? g_comms[0] : g_comms[local_index];
+  ncclComm_t c = comm_of(local_index);
   int rc = nccl_err(g_nccl.allReduce(buf, buf, count, ncclFloat32, ncclSum, c, st),
                     "ncclAllReduce");
-  if (rc) return rc;
-  return wait_collective(c, st, comm_timeout());
+  if (rc) {
+    g_failed = true;
+    return rc;
+  }
+  return wait_collective(c, st, "all-reduce");
+}
+
+int comm_send_f32(int local_index, const float* buf, size_t count, int peer, cudaStream_t st) {
+  ncclComm_t c = comm_of(local_index);
+  int rc = nccl_err(g_nccl.send(buf, count, ncclFloat32, peer, c, st), "ncclSend");
+  if (rc) {
+    g_failed = true;
+    return rc;
+  }
+  return wait_collective(c, st, "send");
+}
+
+int comm_recv_f32(int local_index, float* buf, size_t count, int peer, cudaStream_t st) {
+  ncclComm_t c = comm_of(local_index);
+  int rc = nccl_err(g_nccl.recv(buf, count, ncclFloat32, peer, c, st), "ncclRecv");
+  if (rc) {
+    g_failed = true;
+    return rc;
+  }
+  return wait_collective(c, st, "receive");
+}
+
+int comm_bcast_f32(int local_index, float* buf, size_t count, int root, cudaStream_t st) {
+  ncclComm_t c = comm_of(local_index);
+  int rc = nccl_err(g_nccl.broadcast(buf, buf, count, ncclFloat32, root, c, st), "ncclBroadcast");
+  if (rc) {
+    g_failed = true;
+    return rc;
+  }
+  return wait_collective(c, st, "broadcast");
 }
 
 int comm_world() { return g_process_mode ? G().world : static_cast<int>(G().devs.size()); }
+
+int comm_rank(int local_index) { return g_process_mode ? G().rank : local_index; }
 
 }  // namespace ec
 

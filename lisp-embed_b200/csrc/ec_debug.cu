@@ -257,6 +257,33 @@ long long ecdbg_launches(void) {
   return G().launches;
 }
 
+int ecdbg_kernel_arch(int* binary_version, int* ptx_version) {
+  clear_error();
+  cudaFuncAttributes a{};
+  int rc = check_cuda(cudaFuncGetAttributes(&a, wait_timeout_kernel), "cudaFuncGetAttributes");
+  if (rc) return rc;
+  if (binary_version) *binary_version = a.binaryVersion;
+  if (ptx_version) *ptx_version = a.ptxVersion;
+  return EC_OK;
+}
+
+int ecdbg_tensor_read(const char* name, void* host, size_t nbytes, int* dtype) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
+  if (!name || !host) return set_error(EC_EINVAL, "name and host must not be NULL");
+  Device& d = *G().devs[0];
+  auto it = d.uploads.find(name);
+  if (it == d.uploads.end()) return set_error(EC_EINVAL, "no uploaded tensor '%s'", name);
+  const Tensor& t = it->second;
+  const size_t bytes = t.numel * (t.dtype == kDtBf16 ? 2 : 4);
+  if (nbytes != bytes) return set_error(EC_EINVAL, "tensor '%s' holds %zu bytes, not %zu", name, bytes, nbytes);
+  if (dtype) *dtype = t.dtype == kDtBf16 ? EC_BF16 : EC_F32;
+  int rc = check_cuda(cudaSetDevice(d.ordinal), "cudaSetDevice");
+  if (rc) return rc;
+  return check_cuda(cudaMemcpy(host, t.p, bytes, cudaMemcpyDeviceToHost), "tensor download");
+}
+
 int ecdbg_assign_rows(long long* tc_rows, long long* exact_rows, int reset) {
   std::lock_guard<std::mutex> lk(G().stat_mu);
   if (tc_rows) *tc_rows = G().assign_tc_rows;

@@ -191,9 +191,23 @@ static int tc_assign_run(Device& dv, TcAssign& t, const float* X, const float* C
 }
 
 // ------------------------------------------------------------------ kmeans --
+// Device buffers of one rank's k-means; owned by ec_kmeans so that, after a
+// failed exchange, the communicators are aborted before any of this memory
+// is freed (cudaFree would wait behind a collective that never completes).
+struct KmeansDev {
+  DBuf bx, bc, ba, bh, bcnt, boffs, bl, bs, bprev;
+  TcAssign tc;
+};
+
+enum KmeansExchange { kKmSingle = 0, kKmChain = 1, kKmAllReduce = 2 };
+
+// One rank's Lloyd iterations over its contiguous shard sample[j0, j1).
+// kKmChain: the per-cluster sums continue from the previous rank's (rank
+// order = sample order), so every add follows ann.lisp:107-122's serial
+// loop; the last rank divides and broadcasts the centroids.
 static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t* sample,
                          int64_t j0, int64_t j1, int k, int iters, const float* cent0,
-                         float* cent_out, bool reduce) {
+                         float* cent_out, KmeansExchange mode, KmeansDev& w) {
   Device& dv = *G().devs[li];
   EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
   const int64_t ns = j1 - j0;
@@ -221,42 +235,61 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   }
   (void)n;
   phase("gather");
-  DBuf bx, bc, ba, bh, bcnt, boffs, bl, bs;
   const int64_t nt = sort_tiles(ns);
-  EC_TRY(bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * d * 4, "kmeans rows"));
-  EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
-  EC_TRY(ba.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "assignments"));
-  EC_TRY(bh.alloc(dv, static_cast<size_t>(std::max<int64_t>(nt, 1)) * k * 4, "sort scratch"));
-  EC_TRY(bcnt.alloc(dv, static_cast<size_t>(k) * 4, "counts"));
-  EC_TRY(boffs.alloc(dv, static_cast<size_t>(k + 1) * 8, "offsets"));
-  EC_TRY(bl.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "lists"));
-  EC_TRY(bs.alloc(dv, static_cast<size_t>(k) * (d + 1) * 4, "sums"));
+  const size_t nsum = static_cast<size_t>(k) * (d + 1);
+  EC_TRY(w.bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * d * 4, "kmeans rows"));
+  EC_TRY(w.bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
+  EC_TRY(w.ba.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "assignments"));
+  EC_TRY(w.bh.alloc(dv, static_cast<size_t>(std::max<int64_t>(nt, 1)) * k * 4, "sort scratch"));
+  EC_TRY(w.bcnt.alloc(dv, static_cast<size_t>(k) * 4, "counts"));
+  EC_TRY(w.boffs.alloc(dv, static_cast<size_t>(k + 1) * 8, "offsets"));
+  EC_TRY(w.bl.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "lists"));
+  EC_TRY(w.bs.alloc(dv, nsum * 4, "sums"));
+  if (mode == kKmChain) EC_TRY(w.bprev.alloc(dv, nsum * 4, "previous ranks' sums"));
   cudaStream_t st = dv.stream;
-  EC_TRY(upload_h2d(dv, bx.p, src, static_cast<size_t>(ns) * d * 4, "rows upload"));
-  EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent0, static_cast<size_t>(k) * d * 4,
+  if (ns > 0) EC_TRY(upload_h2d(dv, w.bx.p, src, static_cast<size_t>(ns) * d * 4, "rows upload"));
+  EC_TRY(check_cuda(cudaMemcpyAsync(w.bc.p, cent0, static_cast<size_t>(k) * d * 4,
                                     cudaMemcpyHostToDevice, st), "centroid upload"));
   phase("alloc + upload");
-  TcAssign tc;
-  if (ns > 0) EC_TRY(tc_assign_setup(dv, tc, bx.as<float>(), ns, d, k, st));
+  if (ns > 0) EC_TRY(tc_assign_setup(dv, w.tc, w.bx.as<float>(), ns, d, k, st));
   phase("assign setup");
+  const int rank = comm_rank(li), world = comm_world();
+  if (mode != kKmSingle) EC_TRY(comm_rendezvous(li, static_cast<int>(G().devs.size())));
   for (int it = 0; it < iters; ++it) {
-    if (tc.ready) {
-      EC_TRY(tc_assign_run(dv, tc, bx.as<float>(), bc.as<float>(), ba.as<int32_t>(), st));
-    } else {
-      EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, ns, bc.as<float>(), k, d,
-                                      ba.as<int32_t>(), st), "assign"));
+    if (ns > 0) {
+      if (w.tc.ready) {
+        EC_TRY(tc_assign_run(dv, w.tc, w.bx.as<float>(), w.bc.as<float>(), w.ba.as<int32_t>(), st));
+      } else {
+        EC_TRY(check_cuda(launch_assign(w.bx.as<float>(), nullptr, ns, w.bc.as<float>(), k, d,
+                                        w.ba.as<int32_t>(), st), "assign"));
+      }
     }
-    EC_TRY(check_cuda(launch_lists(ba.as<int32_t>(), ns, k, bh.as<uint32_t>(), bcnt.as<uint32_t>(),
-                                   boffs.as<int64_t>(), 0u, bl.as<uint32_t>(), st), "lists"));
-    EC_TRY(check_cuda(launch_segsum(bx.as<float>(), bl.as<uint32_t>(), boffs.as<int64_t>(), k, d,
-                                    bs.as<float>(), st), "sums"));
-    if (reduce)
-      EC_TRY(comm_allreduce_sum_f32(li, bs.as<float>(), static_cast<size_t>(k) * (d + 1), st));
-    EC_TRY(check_cuda(launch_update(bs.as<float>(), k, d, bc.as<float>(), st), "update"));
+    EC_TRY(check_cuda(launch_lists(w.ba.as<int32_t>(), ns, k, w.bh.as<uint32_t>(), w.bcnt.as<uint32_t>(),
+                                   w.boffs.as<int64_t>(), 0u, w.bl.as<uint32_t>(), st), "lists"));
+    if (mode == kKmChain) {
+      // sums of ranks 0..rank-1 arrive from rank-1; this shard's rows
+      // continue them; the next rank continues from here
+      if (rank > 0) EC_TRY(comm_recv_f32(li, w.bprev.as<float>(), nsum, rank - 1, st));
+      EC_TRY(check_cuda(launch_segsum(w.bx.as<float>(), w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
+                                      rank > 0 ? w.bprev.as<float>() : nullptr, w.bs.as<float>(), st),
+                        "sums"));
+      if (rank + 1 < world) {
+        EC_TRY(comm_send_f32(li, w.bs.as<float>(), nsum, rank + 1, st));
+      } else {
+        EC_TRY(check_cuda(launch_update(w.bs.as<float>(), k, d, w.bc.as<float>(), st), "update"));
+      }
+      EC_TRY(comm_bcast_f32(li, w.bc.as<float>(), static_cast<size_t>(k) * d, world - 1, st));
+    } else {
+      EC_TRY(check_cuda(launch_segsum(w.bx.as<float>(), w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
+                                      nullptr, w.bs.as<float>(), st),
+                        "sums"));
+      if (mode == kKmAllReduce) EC_TRY(comm_allreduce_sum_f32(li, w.bs.as<float>(), nsum, st));
+      EC_TRY(check_cuda(launch_update(w.bs.as<float>(), k, d, w.bc.as<float>(), st), "update"));
+    }
     if (it == 0 || it + 1 == iters) phase(it == 0 ? "iteration 1" : "remaining iterations");
   }
   if (cent_out)
-    EC_TRY(check_cuda(cudaMemcpyAsync(cent_out, bc.p, static_cast<size_t>(k) * d * 4,
+    EC_TRY(check_cuda(cudaMemcpyAsync(cent_out, w.bc.p, static_cast<size_t>(k) * d * 4,
                                       cudaMemcpyDeviceToHost, st), "centroid download"));
   return sync_and_check(dv, "kmeans");
 }
@@ -568,14 +601,28 @@ int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t n
   }
   const bool proc = comm_process_mode();
   const int nd = static_cast<int>(G().devs.size());
+  if (proc) EC_TRY(comm_check_ready());
   if (!proc && nd > 1) EC_TRY(comm_ensure_local());
-  const bool reduce = proc ? G().world > 1 : nd > 1;
-  return on_devices(nd, [&](int li) {
+  const bool multi = proc ? G().world > 1 : nd > 1;
+  const char* ar = getenv("EC_KMEANS_ALLREDUCE");
+  const KmeansExchange mode = !multi ? kKmSingle : (ar && *ar && *ar != '0') ? kKmAllReduce : kKmChain;
+  std::vector<KmeansDev> work(nd);
+  comm_begin();
+  const int rc = on_devices(nd, [&](int li) {
     int64_t j0, j1;
     split(nsample, nd, li, &j0, &j1);
-    return kmeans_device(li, x, n, d, sample, j0, j1, k, iters, c0.data(), li == 0 ? centroids : nullptr,
-                         reduce);
+    const int r = kmeans_device(li, x, n, d, sample, j0, j1, k, iters, c0.data(),
+                                li == 0 ? centroids : nullptr, mode, work[li]);
+    if (r && multi) comm_mark_failed();  // the other ranks stop waiting on this one
+    return r;
   });
+  if (rc && multi) {
+    // abort the whole clique before `work` frees device memory
+    const std::string msg = ec_last_error();
+    comm_abort_all();
+    return set_error(rc, "%s", msg.c_str());
+  }
+  return rc;
 }
 
 int ec_assign(const float* x, int64_t n, int d, const int64_t* rows, int64_t nrows,
@@ -642,6 +689,8 @@ int ec_index_load(const float* x, int64_t n, int d, const float* centroids, int 
   clear_error();
   if (!G().inited) return set_error(EC_ESTATE, "ec_init first");
   if (!x || n <= 0 || d <= 0 || d % 4 || d > 8192) return set_error(EC_EINVAL, "bad index arguments");
+  // the scans keep row ids in the low 32 bits of each candidate key
+  if (n > 0xffffffffLL) return set_error(EC_EINVAL, "more than 2^32 rows");
   if (k < 0 || (k > 0 && (!centroids || !counts || !lists)) || k > 8192)
     return set_error(EC_EINVAL, "bad ivf arguments (k <= 8192)");
   std::vector<int64_t> offs(k + 1, 0);

@@ -20,9 +20,10 @@ int64_t sort_tiles(int64_t n);
 cudaError_t launch_lists(const int32_t* a, int64_t n, int k, uint32_t* tile_hist,
                          uint32_t* counts, int64_t* offs, uint32_t base, uint32_t* lists,
                          cudaStream_t st);
-// out[c * (d + 1) + j] = sum of X[list c][j] in list order; [.. + d] = count
+// out[c * (d + 1) + j] = sum of X[list c][j] in list order; [.. + d] = count;
+// with `init` (same layout) the sums and counts continue from init's values
 cudaError_t launch_segsum(const float* X, const uint32_t* lists, const int64_t* offs, int k,
-                          int d, float* out, cudaStream_t st);
+                          int d, const float* init, float* out, cudaStream_t st);
 cudaError_t launch_update(const float* sums, int k, int d, float* cent, cudaStream_t st);
 cudaError_t launch_probe_select(const float* S, int64_t nq, int k, int nprobe, int32_t* probes,
                                 cudaStream_t st);

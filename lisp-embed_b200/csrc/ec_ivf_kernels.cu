@@ -249,12 +249,16 @@ __global__ void scatter_kernel(const int32_t* a, int64_t n, int k, const uint32_
 // sums[c] = x[rows of list c] summed in list order (ann.lisp:109-115) as
 // float4 columns; out[c * (d + 1) + d] = count.
 __global__ void segsum_kernel(const float* X, const uint32_t* lists, const int64_t* offs, int k,
-                              int d, float* out) {
+                              int d, const float* init, float* out) {
   const int c = blockIdx.x;
   if (c >= k) return;
   const int64_t b = offs[c], e = offs[c + 1];
+  const float* in = init ? init + static_cast<int64_t>(c) * (d + 1) : nullptr;
   for (int c4 = threadIdx.x; c4 < d / 4; c4 += blockDim.x) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    // continue the accumulators of the rows before this shard (exact
+    // multi-rank update) or start from zero
+    float4 s = in ? make_float4(in[c4 * 4], in[c4 * 4 + 1], in[c4 * 4 + 2], in[c4 * 4 + 3])
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int64_t j = b; j < e; ++j) {
       const float4 v = *reinterpret_cast<const float4*>(X + static_cast<int64_t>(lists[j]) * d + c4 * 4);
       s.x = __fadd_rn(s.x, v.x);
@@ -268,7 +272,10 @@ __global__ void segsum_kernel(const float* X, const uint32_t* lists, const int64
     o[2] = s.z;
     o[3] = s.w;
   }
-  if (threadIdx.x == 0) out[static_cast<int64_t>(c) * (d + 1) + d] = static_cast<float>(e - b);
+  // the count continues in float: exact while a cluster holds fewer than
+  // 2^24 rows of the sample
+  if (threadIdx.x == 0)
+    out[static_cast<int64_t>(c) * (d + 1) + d] = (in ? in[d] : 0.f) + static_cast<float>(e - b);
 }
 
 // centroid = sum / count for non-empty clusters (ann.lisp:116-122)
@@ -734,10 +741,10 @@ cudaError_t launch_lists(const int32_t* a, int64_t n, int k, uint32_t* tile_hist
 }
 
 cudaError_t launch_segsum(const float* X, const uint32_t* lists, const int64_t* offs, int k, int d,
-                          float* out, cudaStream_t st) {
+                          const float* init, float* out, cudaStream_t st) {
   int th = d / 4;
   th = th < 32 ? 32 : (th > 256 ? 256 : ((th + 31) / 32) * 32);
-  segsum_kernel<<<k, th, 0, st>>>(X, lists, offs, k, d, out);
+  segsum_kernel<<<k, th, 0, st>>>(X, lists, offs, k, d, init, out);
   return cudaGetLastError();
 }
 

@@ -19,9 +19,18 @@
 //     in order on one stream do not;
 //   * nothing in the scratch has to start at zero: the scan kernel writes
 //     every candidate slot (or its empty marker) before the merge reads it;
-//   * the first call on each device looks up the array's address with
-//     cudaGetSymbolAddress (with that device current) and caches it, so that
-//     first call should be made before any stream capture begins.
+//   * the array is placed in device memory when this file's module is
+//     loaded on a device: at ec_init for the library's devices, otherwise at
+//     the first call with nq > 0 on that device (CUDA loads modules lazily).
+//     A host that reserves its device arena up front should therefore call
+//     ec_init (or make one search) before it takes the arena;
+//   * the array's address is looked up with cudaGetSymbolAddress, with the
+//     device current, on the first call in each CUDA context and cached per
+//     (device, context); a new context (after cudaDeviceReset, or a caller's
+//     own non-primary context) gets a fresh lookup.  Make that first call
+//     before any stream capture begins.
+#include <cuda.h>
+
 #include <cstdint>
 #include <mutex>
 
@@ -38,24 +47,56 @@ constexpr int kMaxOrdinals = 64;
 static __device__ __align__(256) unsigned char g_search_scratch[kScratchBytes];
 
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[kMaxOrdinals] = {};
+struct ScratchSlot {
+  void* ctx = nullptr;  // CUcontext the address belongs to
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxOrdinals];
 
-// address of this device's scratch array; looked up once per device
-int scratch_for_current_device(void** out) {
+// cuCtxGetCurrent through the runtime's driver entry point (the library
+// links no libcuda); nullptr when the driver does not offer it
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    }
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+// address of the current device's scratch array in the current context;
+// looked up once per (device, context)
+int noalloc_scratch_current(void** out) {
   int dev = -1;
   if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (dev < 0 || dev >= kMaxOrdinals) return set_error(EC_EINVAL, "device ordinal %d out of range", dev);
+  CUcontext ctx = nullptr;
+  if (CtxGetCurrentFn f = ctx_get_current()) f(&ctx);
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  ScratchSlot& s = g_scratch[dev];
+  if (!s.ptr || s.ctx != static_cast<void*>(ctx)) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_search_scratch);
-    if (e != cudaSuccess || !p)
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
       return set_error(EC_ECUDA, "scratch address on device %d: %s", dev, cudaGetErrorString(e));
-    g_scratch_ptr[dev] = p;
+    }
+    s.ptr = p;
+    s.ctx = ctx;
   }
-  *out = g_scratch_ptr[dev];
+  *out = s.ptr;
   return EC_OK;
 }
+
+namespace {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -85,7 +126,7 @@ extern "C" int ec_flat_search_noalloc(const float* d_x, int64_t n, int d, const 
                      need, kScratchBytes, kScratchBytes / (static_cast<size_t>(nchunks) * topk * 8),
                      static_cast<long long>(n), topk);
   void* scratch = nullptr;
-  if (int rc = scratch_for_current_device(&scratch)) return rc;
+  if (int rc = noalloc_scratch_current(&scratch)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* cand = static_cast<unsigned long long*>(scratch);
   if (int rc = check_cuda(launch_flat_scan(d_x, n, d, nchunks, d_q, nq, topk, cand, st), "flat scan")) return rc;

@@ -184,5 +184,8 @@ void prof_collect(Device& d);
 // model teardown
 void free_model(Device& d);
 void free_index(Device& d);
+// address of ec_flat_search_noalloc's static scratch array on the current
+// device and context (ec_noalloc.cu); placing it loads that module
+int noalloc_scratch_current(void** out);
 
 }  // namespace ec

@@ -92,6 +92,8 @@ _SIGS = {
     "ecdbg_launches": (C.c_longlong, []),
     "ecdbg_assign_rows": (C.c_int, [C.POINTER(C.c_longlong), C.POINTER(C.c_longlong), C.c_int]),
     "ecdbg_wait_timeout": (C.c_int, [C.c_int]),
+    "ecdbg_kernel_arch": (C.c_int, [C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "ecdbg_tensor_read": (C.c_int, [C.c_char_p, P, C.c_size_t, C.POINTER(C.c_int)]),
     "ecdbg_attention": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P, I32P, C.c_int,
                                   C.c_int, C.c_int, C.c_int, C.c_int]),
 }

@@ -1,13 +1,16 @@
-"""Multi-rank host logic on CPU (gloo, world size 2).
+"""Multi-rank host logic on CPU (gloo, world size 2 and 3).
 
-ec_kmeans shards the training sample into contiguous ranges, computes each
-shard's per-cluster sums and counts, all-reduces them and updates every
-centroid identically (NCCL on the GPUs).  Here two gloo ranks run the same
-decomposition with the oracle's arithmetic and must reproduce the
-single-process Lloyd iteration: centroids within float32 summation-order
-noise, assignments identical except near-ties.  A second test kills one rank
-between steps and checks that the survivor's next collective fails with an
-error instead of hanging (host-side failure detection).
+ec_kmeans shards the training sample into contiguous ranges, one per rank.
+Its default exchange passes the per-cluster accumulators down the ranks in
+sample order (rank r continues rank r-1's sums with its own rows; the last
+rank divides and broadcasts the centroids; NCCL send / recv / broadcast on
+the GPUs): here gloo ranks run that decomposition with the oracle's
+arithmetic and must reproduce the single-process Lloyd iterations bit for
+bit.  The all-reduce exchange (EC_KMEANS_ALLREDUCE) sums per-rank partial
+sums instead: centroids within float32 summation-order noise, assignments
+identical except near-ties.  A third test kills one rank between steps and
+checks that the survivor's next collective fails with an error instead of
+hanging (host-side failure detection).
 """
 import os
 import socket
@@ -31,6 +34,58 @@ def _free_port():
 def _split(n, parts, k):
     per = (n + parts - 1) // parts
     return min(n, per * k), min(n, per * (k + 1))
+
+
+def _kmeans_chain_rank(rank, world, port, x, sample, k, iters, out):
+    import sys
+    sys.path[:0] = [os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                    os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                 "lisp-embed_b200")]
+    from oracle import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    d = x.shape[1]
+    cent = x[sample[:k]].copy()
+    j0, j1 = _split(len(sample), world, rank)
+    mine = sample[j0:j1]
+    for _ in range(iters):
+        a = oracle.assign(x, cent, rows=mine)
+        # the accumulators of ranks 0..rank-1, continued in sample order
+        buf = np.zeros((k, d + 1), np.float32)
+        if rank > 0:
+            t = torch.zeros(k, d + 1)
+            dist.recv(t, src=rank - 1)
+            buf = t.numpy().copy()
+        for j, r in enumerate(mine):
+            c = a[j]
+            buf[c, :d] = (buf[c, :d] + x[r]).astype(np.float32)
+            buf[c, d] += 1
+        t_cent = torch.from_numpy(cent.copy())
+        if rank + 1 < world:
+            dist.send(torch.from_numpy(buf), dst=rank + 1)
+        else:
+            nz = buf[:, d] > 0
+            cent[nz] = buf[nz, :d] / buf[nz, d:d + 1]
+            t_cent = torch.from_numpy(cent.copy())
+        dist.broadcast(t_cent, src=world - 1)
+        cent = t_cent.numpy().copy()
+    if rank == 0:
+        np.save(out, cent)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_chained_lloyd_is_bit_identical(tmp_path, world):
+    from embedcuda import synth
+    from oracle import oracle
+    x, _ = synth.make_ivf_corpus(3000, 32, 16, seed=4, sigma=0.2)
+    sample = synth.make_ivf_sample(len(x), 4)
+    k, iters = 16, 3
+    out = str(tmp_path / "cent.npy")
+    mp.start_processes(_kmeans_chain_rank, args=(world, _free_port(), x, sample, k, iters, out),
+                       nprocs=world, join=True, start_method="spawn")
+    assert np.array_equal(np.load(out), oracle.kmeans(x, sample, k, iters))
 
 
 def _kmeans_rank(rank, world, port, x, sample, k, iters, out):

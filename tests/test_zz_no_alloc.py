@@ -2,15 +2,17 @@
 its candidate scratch in the library's static device array.  Results must
 equal ec_flat_search (kb::top-k-brute, kb.lisp:186-200) on the same vectors
 and queries -- ids exactly, scores exactly (tolerance 0: both run the same
-scan and merge kernels) -- on two calls in a row, which share the scratch.
+scan and merge kernels) -- on two calls in a row, which share the scratch,
+and the oracle's restatement of kb::top-k-brute on a subset of the queries
+(also exact: the scan keeps the reference's sequential single-float sums).
 The file name sorts last so it also runs after every other GPU test."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
-from conftest import gpu_available
 from embedcuda import _lib
+from oracle import oracle
 
 SCRATCH_BYTES = 16 << 20
 
@@ -36,8 +38,15 @@ def _check_against_flat_search(ec, x, q, topk):
         rc = _call(ec.lib(), dx.data_ptr(), n, d, dq.data_ptr(), nq, topk, ids.data_ptr(), sc.data_ptr(), st)
         assert rc == 0, ec.last_error()
         torch.cuda.synchronize()
-        assert np.array_equal(ids.cpu().numpy(), ref_ids)
-        np.testing.assert_allclose(sc.cpu().numpy(), ref_sc, rtol=0, atol=0)
+        got_ids, got_sc = ids.cpu().numpy(), sc.cpu().numpy()
+        assert np.array_equal(got_ids, ref_ids)
+        np.testing.assert_allclose(got_sc, ref_sc, rtol=0, atol=0)
+    for i in range(0, nq, max(1, nq // 16)):
+        o_ids, o_sc = oracle.top_k_brute(x, q[i], topk)
+        r = len(o_ids)
+        assert np.array_equal(got_ids[i, :r], o_ids), i
+        assert np.array_equal(got_sc[i, :r], o_sc), i
+        assert np.all(got_ids[i, r:] == -1)
 
 
 @pytest.mark.gpu
@@ -69,7 +78,6 @@ def test_noalloc_at_scratch_limit(ec):
     _check_against_flat_search(ec, x, q, 64)
 
 
-@pytest.mark.skipif(gpu_available(), reason="argument checks only, no device")
 def test_noalloc_rejects_oversize_without_launching():
     lib = _lib.lib()
     fake = 4096  # never dereferenced: every case below is rejected before any launch
