@@ -1,21 +1,36 @@
 #!/usr/bin/env python
 """Benchmark of the B200 embedding hot path (one JSON line on rank 0).
 
-Default workload: corpus embedding with the all-MiniLM-L6-v2 shape (6 layers,
-hidden 384, 12 heads x 32, FFN 1536, seed-0 random F32 weights run on the
-BF16 tensor-core path), 1024 sequences of uniform length 16..256 with
-[CLS]/[SEP], mean pooling + L2.  A step is one forward over the whole batch.
+Default run: the headline is corpus embedding with the all-MiniLM-L6-v2
+shape (6 layers, hidden 384, 12 heads x 32, FFN 1536, seed-0 random F32
+weights run on the BF16 tensor-core path), 1024 sequences per rank of uniform
+length 16..256 with [CLS]/[SEP], mean pooling + L2.  A step is one forward
+over the whole batch.  The same line then carries the other metrics the
+benchmark names, each measured in the same run:
+
+  * "qwen3": embeddings/s of the Qwen3-Embedding-0.6B shape (28 layers, GQA
+    16:8, BF16), 2048 sequences per rank of 128..512 tokens + EOS;
+  * "ivf_build": seconds to build the IVF index over 3.27M x 384 rows
+    (k 4096, 20 Lloyd iterations + assign-all), rows sharded over the ranks;
+  * "query": p50 ms of one short MiniLM query (10 ids) + IVF top-10 over
+    that index, end to end through the host API (rank 0);
+  * "inproc_split" (N > 1): rank 0 drives all N devices through one
+    ec_embed_batch call (the library's length-balanced split, the path an
+    SBCL host takes) while the other ranks wait on the host.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload minilm|bert-base|mpnet|qwen3|gemma]
+                    [--workload minilm|bert-base|mpnet|qwen3|gemma|ivf|query|search|tokenize]
+                    [--headline-only]
 
 N > 1 is launched by torch.distributed.run, one process per GPU: every rank
-embeds its own 1024-sequence shard (weak scaling, no data-path collective);
-`value` is all ranks' sequences / the slowest rank's time.
+embeds its own shard (weak scaling, no data-path collective; the shards are
+dealt from one seeded pool so every rank gets the same token count), and
+`value` is all ranks' sequences / the slowest rank's device time.
 
 --impl reference times the reference algorithm on the host cores (the Lisp
 cannot run here, so its CPU restatement in oracle/ stands in, threads = all
-host cores, one sequence per thread as embed.lisp does).
+host cores, one sequence per thread as embed.lisp does) on the headline
+workload.
 """
 from __future__ import annotations
 
@@ -46,6 +61,8 @@ WORKLOADS = {
 }
 IVF_N, IVF_D, IVF_K, IVF_ITERS, IVF_SEED = 3_270_000, 384, 4096, 20, 4
 SEARCH_NQ, SEARCH_NPROBE, SEARCH_TOPK = 10_000, 32, 10
+PRECISION = ("bf16 tensor-core GEMM/attention, fp32 accumulate, fp32 norms; residual between "
+             "sublayers: the LayerNorm's bf16 output (BERT/MPNet), fp32 (Qwen3, Gemma)")
 
 
 def parse_args():
@@ -64,6 +81,8 @@ def parse_args():
                    help="search workload: centroids")
     p.add_argument("--search-queries", type=int, default=SEARCH_NQ,
                    help="search workload: queries per call")
+    p.add_argument("--headline-only", action="store_true",
+                   help="default workload: the MiniLM headline alone")
     return p.parse_args()
 
 
@@ -210,52 +229,303 @@ def ivf_corpus_torch(n, d, k, seed, device, nqueries=0):
     return x, perm, q / q.norm(dim=1, keepdim=True)
 
 
-def run_ivf(args, rank, world, local_rank):
-    """IVF build seconds: 20 Lloyd iterations over all 3.27M rows (k 4096,
-    init = first k rows of a seeded permutation, ann.lisp:83-86), rows
-    sharded over the ranks with one NCCL all-reduce of sums + counts per
-    iteration, then the inverted lists of each shard (ann::assign-all).
-    Inputs start in host memory; the timed region includes their upload."""
+class Ranks:
+    """Rank layout of one run.  Host-side exchanges (barriers, the max of
+    device times, the NCCL id of the library's k-means communicator) go
+    through a gloo group, so a rank waiting on another runs no GPU kernel."""
+
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.gloo = None
+
+    def setup(self):
+        import torch
+        torch.cuda.set_device(self.local_rank)
+        if self.world > 1:
+            import torch.distributed as dist
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=900))
+        phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+        self.smi_index = (phys[self.local_rank] if len(phys) > self.local_rank and phys[self.local_rank]
+                          else self.local_rank)
+        return self
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=self.gloo)
+
+    def max(self, *vals):
+        if self.world == 1:
+            return vals if len(vals) > 1 else vals[0]
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor(vals, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.gloo)
+        out = tuple(float(v) for v in t)
+        return out if len(out) > 1 else out[0]
+
+    def sum(self, val):
+        if self.world == 1:
+            return val
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([val], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.gloo)
+        return float(t[0])
+
+    def bcast_bytes(self, data, n):
+        if self.world == 1:
+            return data
+        import torch
+        import torch.distributed as dist
+        t = torch.zeros(n, dtype=torch.uint8)
+        if self.rank == 0:
+            t[:] = torch.frombuffer(bytearray(data), dtype=torch.uint8)
+        dist.broadcast(t, 0, group=self.gloo)
+        return bytes(t.numpy())
+
+    def finish(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            self.barrier()
+            dist.destroy_process_group()
+
+
+def synth_root():
+    return os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth")
+
+
+def shared_model_dir(shape, seed, R):
+    """The seeded model directory, written once per host (local rank 0) and
+    read by every rank."""
+    from embedcuda import synth
+    if R.local_rank == 0:
+        d = synth.build_model_dir(shape, seed, synth_root())
+    R.barrier()
+    if R.local_rank != 0:
+        d = synth.build_model_dir(shape, seed, synth_root())
+    return d
+
+
+def workload_config(workload, world, tokens_rank0):
+    """The `config` object of a line: the workload alone (both arms)."""
+    shape_name, _, nseq, desc = WORKLOADS[workload]
+    return {"workload": shape_name, "description": desc, "sequences_per_rank": nseq,
+            "tokens_per_rank": tokens_rank0, "parallelism": f"dp{world} (sequence shards)"}
+
+
+def rank_inputs(shape_name, nseq, seed, rank, world):
+    """This rank's sequences.  One rank: the workload's `nseq` sequences.
+    N ranks: a pool of N * nseq sequences from the same seed, sorted by
+    length and dealt in a snake order, so every rank gets nseq sequences and
+    (nearly) the same token count."""
+    from embedcuda import synth
+    if world == 1:
+        return synth.make_inputs(shape_name, nseq, seed)
+    ids, offs = synth.make_inputs(shape_name, nseq * world, seed)
+    lens = np.diff(offs)
+    order = np.argsort(-lens, kind="stable")
+    pos = np.arange(order.size)
+    blk, r = pos // world, pos % world
+    owner = np.where(blk % 2 == 0, r, world - 1 - r)
+    mine = np.sort(order[owner == rank])
+    chunks = [ids[offs[i]:offs[i + 1]] for i in mine]
+    o = np.zeros(len(mine) + 1, np.int64)
+    o[1:] = np.cumsum([len(c) for c in chunks])
+    return np.concatenate(chunks).astype(np.int32), o
+
+
+def embed_measure(R, workload, steps, warmup, profile=True, e2e_steps=None):
+    """Device-timed forward steps of one embedding workload on this rank's
+    shard (inputs resident in HBM, L2 flushed between steps), then the same
+    batch end to end through ec_embed_batch with host buffers.  Returns
+    rank 0's dict (None elsewhere)."""
     import ctypes as C
     import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-    from embedcuda import _lib, ann
-    torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+    from embedcuda import _lib, model, synth
+    shape_name, seed, nseq, desc = WORKLOADS[workload]
+    shape = synth.SHAPES[shape_name]
+    mdir = shared_model_dir(shape, seed, R)
+    _lib.init([R.local_rank])
+    model.load_model(mdir)
+    dim = model.dim()
+    ids, offsets = rank_inputs(shape_name, nseq, seed, R.rank, R.world)
+    T = int(offsets[-1])
+    flops_step = algorithmic_flops(shape, offsets)
+    d_ids = torch.from_numpy(ids).cuda()
+    d_out = torch.empty((nseq, dim), dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    L = _lib.lib()
+
+    def step_device():
+        model.embed_batch_device(d_ids.data_ptr(), offsets, nseq, d_out.data_ptr(), dim, sptr)
+
+    for _ in range(warmup):
+        flush.zero_()
+        step_device()
+    torch.cuda.synchronize()
+    R.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    if profile:
+        L.ecdbg_profile(1)
+    with ClockSampler(R.smi_index) as clk:
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step_device()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    R.barrier()
+    launches = int(L.ecdbg_launches()) if profile else None
+    prof = {}
+    if profile:
+        L.ecdbg_profile(0)
+        for cls in ("gemm", "attention", "rows"):
+            v = [C.c_double(), C.c_double(), C.c_double(), C.c_longlong()]
+            L.ecdbg_profile_read(cls.encode(), *[C.byref(x) for x in v])
+            prof[cls] = {"ms": v[0].value, "flops": v[1].value, "bytes": v[2].value,
+                         "launches": v[3].value}
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    clocks = clk.summary()
+    # end to end through the host API: ids from pinned host memory in,
+    # embeddings back to host memory, each step
+    h_ids = torch.from_numpy(ids).pin_memory().numpy()
+    h_out = np.empty((nseq, dim), np.float32)
+    for _ in range(2):
+        model.embed_batch(h_ids, offsets, out=h_out)
+    e2e_s = 0.0
+    ne2e = e2e_steps or steps
+    for _ in range(ne2e):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.embed_batch(h_ids, offsets, out=h_out)
+        e2e_s += time.perf_counter() - t0
+    nblk = int(np.sum((np.diff(offsets) + 63) // 64))
+    h2d = T * 4 + (nseq + 1) * 4 + nblk * 8
+    d2h = nseq * dim * 4
+    ms, e2e_per = R.max(ms, e2e_s / ne2e)
+    tokens_all = R.sum(float(T))
+    if R.rank != 0:
+        return None
+    peaks, src = measured_peaks()
+    peak = peaks.get("bf16_tflops")
+    out = {
+        "value": R.world * nseq * steps / (ms * 1e-3), "unit": "embeddings/s",
+        "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
+        "config": workload_config(workload, R.world, T),
+        "tokens_all_ranks": int(tokens_all),
+        "l2": "flushed (256 MB write) between timed steps",
+        "e2e": {"value": R.world * nseq / e2e_per, "unit": "embeddings/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "timing": "host wall clock around the synchronous ec_embed_batch call"},
+        "clocks": clocks,
+        "step_tflops": flops_step * steps / (ms * 1e-3) / 1e12,
+        "model_dir": mdir, "ids": ids, "offsets": offsets,
+    }
+    out["step_frac_of_peak"] = out["step_tflops"] / peak if peak else None
+    if profile:
+        g = prof["gemm"]
+        achieved = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else None
+        out["roofline"] = {
+            "bound": "tensor", "kernel": "gemm_tn_bf16 / gemm_ln (all GEMM launches)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": (achieved / peak) if achieved and peak else None,
+            "traffic": profile_traffic(f"gemm_{workload}"),
+            "peak_source": f"{src} bf16_tflops (burst: GEMM launches of 0.1-1 ms)",
+            "step_tflops": out["step_tflops"], "step_frac_of_peak": out["step_frac_of_peak"]}
+        out["kernel_classes"] = prof
+        out["gpu_launches"] = launches
+    return out
+
+
+def qwen3_cpu_baseline(model_dir, ids, offsets, seconds):
+    """The oracle's llama.lisp forward on all host cores, one sequence per
+    thread, over the first 2 of the 28 layers; the time is scaled by 28 / 2
+    (every layer does the same work; the embedding gather and final norm are
+    negligible)."""
+    from oracle import oracle
+    om = oracle.OracleModel(model_dir)
+    full = om.m.layers
+    om.m.layers = 2
+    threads = os.cpu_count() or 1
+    nseq = len(offsets) - 1
+    done, el, s = 0, 0.0, 0
+    while el < seconds and s < nseq:
+        b1 = min(nseq, s + threads)
+        sub = offsets[s:b1 + 1] - offsets[s]
+        t0 = time.perf_counter()
+        om.embed_batch(ids[offsets[s]:offsets[b1]], sub, threads=threads)
+        el += time.perf_counter() - t0
+        done += b1 - s
+        s = b1
+    om.m.layers = full
+    scale = full / 2.0
+    return {"value": done / (el * scale), "unit": "embeddings/s", "cores": threads, "kind": "port",
+            "sample": f"{done} of the workload's sequences through 2 of {full} layers in {el:.1f} s "
+                      f"({threads} threads, one sequence per thread), time scaled by {scale:g}"}
+
+
+def ivf_corpus_host(R):
+    """The IVF workload (generated on this rank's GPU with a fixed seed, the
+    same on every rank) copied to host memory, and its training permutation."""
+    import torch
     x_dev, perm = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda")
-    j0 = (IVF_N + world - 1) // world * rank
-    j1 = min(IVF_N, j0 + (IVF_N + world - 1) // world)
-    mine = perm[j0:j1]
-    x_local = x_dev[mine].cpu().numpy()            # this rank's training rows, sample order
-    init = x_dev[perm[:IVF_K]].cpu().numpy()        # same on every rank
+    x = x_dev.cpu().numpy()
+    perm = perm.cpu().numpy().astype(np.int64)
     del x_dev
     torch.cuda.empty_cache()
-    _lib.init([local_rank])
+    return x, perm
+
+
+def ivf_build_measure(R, x, perm):
+    """IVF build seconds: 20 Lloyd iterations over all 3.27M rows (k 4096,
+    init = the first k rows of a seeded permutation, ann.lisp:83-86) with the
+    rows sharded over the ranks in sample order (the sums chained from rank
+    to rank over NCCL, so the centroids equal one device's bit for bit), then
+    the inverted lists of each shard (ann::assign-all).  Inputs start in host
+    memory; the timed region includes their upload.  Returns (rank 0's dict,
+    centroids)."""
+    import ctypes as C
+    import torch
+    from embedcuda import _lib, ann
+    per = (IVF_N + R.world - 1) // R.world
+    j0, j1 = per * R.rank, min(IVF_N, per * (R.rank + 1))
+    mine = perm[j0:j1]
+    x_local = np.ascontiguousarray(x[mine])  # this rank's training rows, in sample order
+    init = np.ascontiguousarray(x[perm[:IVF_K]])
+    _lib.init([R.local_rank])
     L = _lib.lib()
-    if world > 1:
-        idbuf = C.create_string_buffer(L.ec_comm_id_size())
-        if rank == 0:
+    if R.world > 1 and not getattr(R, "comm_ready", False):
+        n = L.ec_comm_id_size()
+        idbuf = C.create_string_buffer(n)
+        if R.rank == 0:
             _lib.check(L.ec_comm_get_id(idbuf), "comm id")
-        t = torch.frombuffer(bytearray(idbuf.raw), dtype=torch.uint8).cuda()
-        dist.broadcast(t, 0)
-        idbuf = C.create_string_buffer(bytes(t.cpu().numpy()), len(idbuf.raw))
-        _lib.check(L.ec_comm_init(rank, world, idbuf), "comm init")
+        raw = R.bcast_bytes(idbuf.raw, n)
+        _lib.check(L.ec_comm_init(R.rank, R.world, C.create_string_buffer(raw, n)), "comm init")
+        R.comm_ready = True
     local_sample = np.arange(len(x_local), dtype=np.int64)
-    # warm-up: one iteration (module load, NCCL channels)
+    # warm-up: one iteration on a slice (module load, NCCL channels)
     ann.kmeans(x_local[:200000], local_sample[:200000], IVF_K, 1, init=init)
-    if world > 1:
-        dist.barrier()
     torch.cuda.synchronize()
+    R.barrier()
     L.ecdbg_profile(1)
     L.ecdbg_assign_rows(None, None, 1)
-    t0 = time.perf_counter()
-    cent = ann.kmeans(x_local, local_sample, IVF_K, IVF_ITERS, init=init)
-    t_km = time.perf_counter() - t0
-    counts, lists = ann.assign_all(x_local, cent)
-    t_all = time.perf_counter() - t0
+    with ClockSampler(R.smi_index) as clk:
+        t0 = time.perf_counter()
+        cent = ann.kmeans(x_local, local_sample, IVF_K, IVF_ITERS, init=init)
+        t_km = time.perf_counter() - t0
+        counts, lists = ann.assign_all(x_local, cent)
+        t_all = time.perf_counter() - t0
     v = [C.c_double(), C.c_double(), C.c_double(), C.c_longlong()]
     L.ecdbg_profile_read(b"gemm", *[C.byref(z) for z in v])
     g_ms, g_flops, g_launches = v[0].value, v[1].value, v[3].value
@@ -264,83 +534,282 @@ def run_ivf(args, rank, world, local_rank):
     L.ecdbg_profile(0)
     tc_rows, ex_rows = C.c_longlong(), C.c_longlong()
     L.ecdbg_assign_rows(C.byref(tc_rows), C.byref(ex_rows), 0)
-    if world > 1:
-        tt = torch.tensor([t_km, t_all], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_km, t_all = float(tt[0]), float(tt[1])
-    if rank == 0:
-        flops = 2.0 * IVF_N * IVF_K * IVF_D * (IVF_ITERS + 1)
-        out = {"metric": "IVF build s", "value": t_all, "unit": "s", "n_gpus": world,
-               "steps": 1, "warmup": 1, "ms_per_step": 1000 * t_all, "higher_is_better": False,
-               "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-               "config": {"workload": "ivf-3.27Mx384", "n": IVF_N, "dim": IVF_D, "k": IVF_K,
-                          "iters": IVF_ITERS, "sample": "all rows, seeded permutation",
-                          "kmeans_s": t_km, "assign_all_s": t_all - t_km,
-                          "parallelism": f"rows sharded over {world} GPU(s), NCCL all-reduce"},
-               "achieved_tflops": flops / t_all / 1e12,
-               "note": "assignments bit-exact to ann.lisp's sequential single-float scores on "
-                       "one GPU: bf16 tensor-core scores with a rigorous error window, "
-                       "candidates re-scored exactly, the rest of the rows scanned exactly"}
-        peaks, src = measured_peaks()
-        achieved = g_flops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None
-        peak = peaks.get("bf16_tflops")
-        out["roofline"] = {"bound": "tensor", "kernel": "gemm_tn_bf16_kernel<256, kEpiArgCand> "
-                                                       "(assignment scores)",
-                           "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                           "frac": achieved / peak if achieved and peak else None,
-                           "traffic": None, "launches": g_launches,
-                           "peak_source": f"{src} bf16_tflops (burst: each launch ~10 ms)"}
-        out["kernel_classes"] = {"assign_gemm_ms": g_ms, "assign_reduce_ms": r_ms}
-        out["assign_rows"] = {"tensor_core": tc_rows.value, "exact_scan": ex_rows.value}
-        print(json.dumps(out), flush=True)
-    _lib.shutdown()
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    t_km, t_all = R.max(t_km, t_all)
+    if R.rank != 0:
+        return None, cent
+    peaks, src = measured_peaks()
+    achieved = g_flops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None
+    peak = peaks.get("bf16_tflops")
+    flops = 2.0 * IVF_N * IVF_K * IVF_D * (IVF_ITERS + 1)
+    out = {"value": t_all, "unit": "s", "higher_is_better": False, "scaling": "strong",
+           "n_gpus": R.world, "dtype": "f32 (bf16 tensor-core scores, exact re-check)",
+           "config": {"workload": "ivf-3.27Mx384", "n": IVF_N, "dim": IVF_D, "k": IVF_K,
+                      "iters": IVF_ITERS, "sample": "all rows, seeded permutation",
+                      "parallelism": f"rows sharded over {R.world} GPU(s) in sample order",
+                      "exchange": "per-cluster sums chained rank to rank (NCCL send/recv), "
+                                  "centroids broadcast" if R.world > 1 else "none"},
+           "kmeans_s": t_km, "assign_all_s": t_all - t_km,
+           "achieved_tflops": flops / t_all / 1e12,
+           "roofline": {"bound": "tensor",
+                        "kernel": "gemm_tn_bf16_kernel<256, kEpiArgCand> (assignment scores, rank 0)",
+                        "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak if achieved and peak else None, "traffic": None,
+                        "launches": g_launches, "assign_gemm_ms": g_ms, "assign_reduce_ms": r_ms,
+                        "peak_source": f"{src} bf16_tflops (burst)"},
+           "assign_rows": {"tensor_core": tc_rows.value, "exact_scan": ex_rows.value},
+           "clocks": clk.summary(),
+           "note": "assignments and centroids bit-identical to ann.lisp's sequential "
+                   "single-float arithmetic at any rank count"}
+    return out, cent
 
 
-def run_query(args, rank, local_rank):
-    """p50 ms of one short MiniLM query end to end through the host API:
-    ec_embed_batch of ~10 token ids, then ec_ivf_search top-10 with nprobe 32
-    over the 3.27M x 384 IVF index (kb:kb-search without the text part)."""
-    if rank != 0:
-        return 0
-    import torch
-    from embedcuda import _lib, ann, kb, model, synth
-    torch.cuda.set_device(local_rank)
-    x_dev, perm = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda")
-    x = x_dev.cpu().numpy()
-    del x_dev
-    torch.cuda.empty_cache()
-    perm = perm.cpu().numpy().astype(np.int64)
-    _lib.init([local_rank])
-    cent = ann.kmeans(x, perm, IVF_K, IVF_ITERS)
+def ivf_cpu_baseline(x, perm, seconds):
+    """ann::kmeans on the host cores, timed on a sample and extrapolated: the
+    assignment pass one row and one centroid at a time on all threads
+    (ann.lisp:90-105) over a slice of rows, and the serial update
+    (ann.lisp:107-122) over a slice; build = 21 assignment passes + 20
+    updates over all 3.27M rows."""
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    init = np.ascontiguousarray(x[perm[:IVF_K]])
+    rows = 2048
+    el_a, done_a = 0.0, 0
+    while el_a < 0.6 * seconds and done_a < 64 * rows:
+        sl = perm[done_a:done_a + rows]
+        t0 = time.perf_counter()
+        a = oracle.assign_scalar(x, init, rows=sl, threads=threads)
+        el_a += time.perf_counter() - t0
+        done_a += rows
+    sl = perm[:200000]
+    # the serial update's cost does not depend on which cluster a row joins
+    a = np.random.default_rng(0).integers(0, IVF_K, len(sl)).astype(np.int32)
+    t0 = time.perf_counter()
+    oracle.kmeans_update(x, sl, a, init)
+    el_u = time.perf_counter() - t0
+    t_assign = IVF_N * el_a / done_a
+    t_update = IVF_N * el_u / len(sl)
+    total = (IVF_ITERS + 1) * t_assign + IVF_ITERS * t_update
+    return {"value": total, "unit": "s", "cores": threads, "kind": "port",
+            "sample": f"assignment of {done_a} rows on {threads} threads in {el_a:.1f} s and the "
+                      f"serial update of {len(sl)} rows in {el_u:.2f} s, extrapolated to "
+                      f"{IVF_ITERS + 1} passes and {IVF_ITERS} updates of {IVF_N} rows"}
+
+
+def query_measure(R, x, cent, nq, warmup):
+    """p50 ms of one short MiniLM query end to end through the host API
+    (rank 0, one GPU): ec_embed_batch of 10 token ids, then ec_ivf_search
+    top-10 with nprobe 32 over the 3.27M x 384 IVF index (kb:kb-search after
+    the text part)."""
+    from embedcuda import ann, kb, model, synth
     counts, lists = ann.assign_all(x, cent)
     kb.load_index(x, (cent, counts, lists))
-    d = synth.build_model_dir(synth.MINILM, 0, os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth"))
-    model.load_model(d)
+    model.load_model(synth.build_model_dir(synth.MINILM, 0, synth_root()))
     rng = np.random.default_rng(7)
     times = []
-    for i in range(101 + args.warmup):
+    for i in range(nq + warmup):
         ids = np.concatenate([[101], rng.integers(1000, 30522, 8), [102]]).astype(np.int32)
         t0 = time.perf_counter()
         q = model.embed(ids)
-        ids_, sc = kb.search_ivf(q, 10, nprobe=32)
+        kb.search_ivf(q, SEARCH_TOPK, nprobe=SEARCH_NPROBE)
         el = time.perf_counter() - t0
-        if i >= args.warmup:
+        if i >= warmup:
             times.append(el)
-    p50 = 1000 * float(np.median(times))
-    out = {"metric": "p50 query ms", "value": p50, "unit": "ms", "n_gpus": 1, "steps": 101,
-           "warmup": args.warmup, "ms_per_step": p50, "higher_is_better": False,
-           "scaling": "none", "vs_baseline": None, "dtype": "bf16+f32", "data": "synthetic",
-           "config": {"workload": "minilm-l6 query (10 ids) + ivf top-10 nprobe 32 over 3.27Mx384",
-                      "p90_ms": 1000 * float(np.percentile(times, 90)),
-                      "min_ms": 1000 * float(np.min(times))}}
-    print(json.dumps(out), flush=True)
+    return {"value": 1000 * float(np.median(times)), "unit": "ms", "higher_is_better": False,
+            "n_gpus": 1, "queries": nq,
+            "p90_ms": 1000 * float(np.percentile(times, 90)),
+            "min_ms": 1000 * float(np.min(times)),
+            "config": {"workload": "minilm-l6 query (10 ids) + ivf top-10 nprobe 32 over 3.27Mx384"},
+            "counts": counts, "lists": lists}
+
+
+def query_cpu_baseline(x, cent, counts, lists, nq=11):
+    """The oracle on the host: bert.lisp's forward of the same 10-id queries
+    on one thread, then kb::top-k-ivf (nprobe 32, top-10); p50 of nq."""
+    from embedcuda import synth
+    from oracle import oracle
+    om = oracle.OracleModel(synth.build_model_dir(synth.MINILM, 0, synth_root()))
+    rng = np.random.default_rng(7)
+    times = []
+    for _ in range(nq):
+        ids = np.concatenate([[101], rng.integers(1000, 30522, 8), [102]]).astype(np.int32)
+        t0 = time.perf_counter()
+        q = om.embed(ids)
+        oracle.top_k_ivf(x, cent, counts, lists, SEARCH_NPROBE, q, SEARCH_TOPK)
+        times.append(time.perf_counter() - t0)
+    return {"value": 1000 * float(np.median(times)), "unit": "ms", "cores": 1, "kind": "port",
+            "sample": f"p50 of {nq} queries (oracle embed on one thread + kb::top-k-ivf scan)"}
+
+
+def inproc_split_measure(R, steps):
+    """N > 1, rank 0 only: ec_init on all N devices and one ec_embed_batch
+    per step over N x 1024 MiniLM sequences from host buffers (the library
+    sorts them by length, deals them to the least-loaded device and scatters
+    the rows back in input order).  Host wall clock per call."""
+    import torch
+    from embedcuda import _lib, model, synth
+    if torch.cuda.device_count() < R.world:
+        return {"skipped": f"{torch.cuda.device_count()} devices visible to rank 0"}
+    shape_name, seed, nseq, _ = WORKLOADS["minilm"]
+    _lib.init(list(range(R.world)))
+    model.load_model(synth.build_model_dir(synth.SHAPES[shape_name], seed, synth_root()))
+    ids, offs = synth.make_inputs(shape_name, nseq * R.world, seed)
+    h_ids = torch.from_numpy(ids).pin_memory().numpy()
+    out = np.empty((len(offs) - 1, model.dim()), np.float32)
+    for _ in range(3):
+        model.embed_batch(h_ids, offs, out=out)
+    t = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        model.embed_batch(h_ids, offs, out=out)
+        t.append(time.perf_counter() - t0)
+    el = sum(t) / len(t)
     _lib.shutdown()
+    return {"value": (len(offs) - 1) / el, "unit": "embeddings/s", "n_gpus": R.world,
+            "ms_per_step": 1000 * el, "steps": steps, "sequences": len(offs) - 1,
+            "tokens": int(offs[-1]),
+            "timing": "host wall clock around one ec_embed_batch call over all devices "
+                      "(host ids in, host embeddings out)"}
+
+
+def run_default(args):
+    """The headline (MiniLM) line with the other metrics as sub-results."""
+    R = Ranks().setup()
+    from embedcuda import _lib
+    head = embed_measure(R, "minilm", args.steps, args.warmup)
+    out = None
+    if R.rank == 0:
+        out = {"metric": "embeddings/sec", "value": head["value"], "unit": "embeddings/s",
+               "n_gpus": R.world, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (seeded ids and N(0,0.02) weights of the named shape)",
+               "config": head["config"], "precision": PRECISION, "l2": head["l2"],
+               "tokens_all_ranks": head["tokens_all_ranks"],
+               "e2e": head["e2e"], "roofline": head["roofline"],
+               "kernel_classes": head["kernel_classes"], "gpu_launches": head["gpu_launches"],
+               "clocks": head["clocks"]}
+    extras = not args.headline_only
+    if extras:
+        q = embed_measure(R, "qwen3", 3, 3, profile=True, e2e_steps=2)
+        if R.rank == 0:
+            q.pop("ids"), q.pop("offsets"), q.pop("model_dir")
+            q.pop("kernel_classes", None), q.pop("gpu_launches", None)
+            out["qwen3"] = q
+        x, perm = ivf_corpus_host(R)
+        ivf, cent = ivf_build_measure(R, x, perm)
+        if R.rank == 0:
+            out["ivf_build"] = ivf
+            qm = query_measure(R, x, cent, 101, 5)
+            counts, lists = qm.pop("counts"), qm.pop("lists")
+            out["query"] = qm
+        # every rank closes the library (and the k-means communicator) together
+        R.barrier()
+        _lib.shutdown()
+        R.barrier()
+        if R.world > 1:
+            if R.rank == 0:
+                out["inproc_split"] = inproc_split_measure(R, args.steps)
+            R.barrier()
+    if R.rank == 0 and R.world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline(head["model_dir"], head["ids"], head["offsets"],
+                                               args.cpu_seconds)
+        except Exception as e:  # the baseline must not sink the GPU number
+            out["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        if extras:
+            for key, fn in (
+                    ("qwen3", lambda: qwen3_cpu_baseline(
+                        _qwen_dir(), *_qwen_inputs(), args.cpu_seconds)),
+                    ("ivf_build", lambda: ivf_cpu_baseline(x, perm, args.cpu_seconds)),
+                    ("query", lambda: query_cpu_baseline(x, cent, counts, lists))):
+                try:
+                    out[key]["cpu_baseline"] = fn()
+                except Exception as e:
+                    out[key]["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if R.rank == 0:
+        print(json.dumps(out), flush=True)
+    _lib.shutdown()
+    R.finish()
     return 0
 
 
+def _qwen_dir():
+    from embedcuda import synth
+    shape_name, seed, _, _ = WORKLOADS["qwen3"]
+    return synth.build_model_dir(synth.SHAPES[shape_name], seed, synth_root())
+
+
+def _qwen_inputs():
+    from embedcuda import synth
+    shape_name, seed, nseq, _ = WORKLOADS["qwen3"]
+    return synth.make_inputs(shape_name, nseq, seed)
+
+
+def run_single_embed(args):
+    """--workload bert-base | mpnet | qwen3 | gemma: that workload alone."""
+    R = Ranks().setup()
+    from embedcuda import _lib
+    r = embed_measure(R, args.workload, args.steps, args.warmup)
+    if R.rank == 0:
+        out = {"metric": "embeddings/sec", "value": r["value"], "unit": "embeddings/s",
+               "n_gpus": R.world, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (seeded ids and N(0,0.02) weights of the named shape)",
+               "config": r["config"], "precision": PRECISION, "l2": r["l2"], "e2e": r["e2e"],
+               "roofline": r["roofline"], "kernel_classes": r["kernel_classes"],
+               "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]}
+        if R.world == 1 and not args.no_cpu_baseline:
+            try:
+                if args.workload == "qwen3":
+                    out["cpu_baseline"] = qwen3_cpu_baseline(r["model_dir"], r["ids"], r["offsets"],
+                                                             args.cpu_seconds)
+                else:
+                    out["cpu_baseline"] = cpu_baseline(r["model_dir"], r["ids"], r["offsets"],
+                                                       args.cpu_seconds)
+            except Exception as e:
+                out["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        print(json.dumps(out), flush=True)
+    _lib.shutdown()
+    R.finish()
+    return 0
+
+
+def run_ivf(args):
+    """--workload ivf: the IVF build alone (its own line)."""
+    R = Ranks().setup()
+    from embedcuda import _lib
+    x, perm = ivf_corpus_host(R)
+    ivf, _ = ivf_build_measure(R, x, perm)
+    if R.rank == 0:
+        ivf.update(metric="IVF build s", steps=1, warmup=1, ms_per_step=1000 * ivf["value"],
+                   vs_baseline=None, data="synthetic")
+        if R.world == 1 and not args.no_cpu_baseline:
+            ivf["cpu_baseline"] = ivf_cpu_baseline(x, perm, args.cpu_seconds)
+        print(json.dumps(ivf), flush=True)
+    _lib.shutdown()
+    R.finish()
+    return 0
+
+
+def run_query(args):
+    """--workload query: the p50 query alone (rank 0)."""
+    R = Ranks().setup()
+    from embedcuda import _lib, ann
+    if R.rank == 0:
+        x, perm = ivf_corpus_host(R)
+        _lib.init([R.local_rank])
+        cent = ann.kmeans(x, perm, IVF_K, IVF_ITERS)
+        qm = query_measure(R, x, cent, 101, args.warmup)
+        counts, lists = qm.pop("counts"), qm.pop("lists")
+        qm.update(metric="p50 query ms", steps=101, warmup=args.warmup, ms_per_step=qm["value"],
+                  vs_baseline=None, data="synthetic", dtype="bf16+f32", scaling="none")
+        if not args.no_cpu_baseline:
+            qm["cpu_baseline"] = query_cpu_baseline(x, cent, counts, lists)
+        print(json.dumps(qm), flush=True)
+    _lib.shutdown()
+    R.finish()
+    return 0
 
 
 def search_cpu_baseline(x, cent, counts, lists, qs, nprobe, topk, seconds, threads=None):
@@ -466,16 +935,18 @@ def run_search(args, rank, local_rank):
     return 0
 
 
-def run_reference(args, rank):
-    """--impl reference: the oracle port of the reference's CPU path."""
+def run_reference(args, rank, world):
+    """--impl reference: the oracle port of the reference's CPU path on the
+    host cores, on the headline workload (rank 0's shard), one sequence per
+    thread in batches of `threads` (embed.lisp:88-105); rank 0 alone."""
     if rank != 0:
         return 0
     from embedcuda import synth
-    shape_name, seed, nseq, desc = WORKLOADS[args.workload]
+    workload = args.workload if args.workload in WORKLOADS else "minilm"
+    shape_name, seed, nseq, desc = WORKLOADS[workload]
     shape = synth.SHAPES[shape_name]
-    root = os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth")
-    d = synth.build_model_dir(shape, seed, root)
-    ids, offsets = synth.make_inputs(shape_name, nseq, seed)
+    d = synth.build_model_dir(shape, seed, synth_root())
+    ids, offsets = rank_inputs(shape_name, nseq, seed, 0, world)
     from oracle import oracle
     om = oracle.OracleModel(d)
     threads = os.cpu_count() or 1
@@ -506,11 +977,11 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": shape_name, "description": desc, "sequences_per_step": threads,
-                   "note": "each step embeds `threads` sequences of the workload"},
+        "config": workload_config(workload, world, int(offsets[-1])),
         "cpu_baseline": {"value": value, "unit": "embeddings/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps x {threads} sequences; SBCL absent, the "
-                                   "C restatement of bert.lisp/llama.lisp stands in"},
+                         "sample": f"{args.steps} steps x {threads} sequences of the workload "
+                                   "(one sequence per thread); SBCL absent, the C restatement "
+                                   "of bert.lisp / llama.lisp stands in"},
         "e2e": {"value": value, "unit": "embeddings/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -593,157 +1064,21 @@ def main():
                 print(json.dumps({"impl": "reference", "unavailable":
                                   "reference arm is timed for the embedding workloads only"}))
             return 0
-        return run_reference(args, rank)
-    if not os.environ.get("EC_KEEP_NCCL_DEBUG"):
-        os.environ["NCCL_DEBUG"] = "WARN"
-    if args.workload == "ivf":
-        return run_ivf(args, rank, world, local_rank)
-    if args.workload == "query":
-        return run_query(args, rank, local_rank)
-    if args.workload == "search":
-        return run_search(args, rank, local_rank)
-    if args.workload == "tokenize":
-        return run_tokenize(args, rank)
-
+        return run_reference(args, rank, world)
     # NCCL's version banner goes to stdout; the benchmark prints one JSON line
     if not os.environ.get("EC_KEEP_NCCL_DEBUG"):
         os.environ["NCCL_DEBUG"] = "WARN"
-    import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-
-    torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-
-    from embedcuda import _lib, model, synth
-    shape_name, seed, nseq, desc = WORKLOADS[args.workload]
-    shape = synth.SHAPES[shape_name]
-    root = os.path.join(os.environ.get("EC_SYNTH_DIR", "/tmp/ec_synth"), f"r{rank}")
-    mdir = synth.build_model_dir(shape, seed, root)
-    _lib.init([local_rank])
-    model.load_model(mdir)
-    dim = model.dim()
-    rseed = seed if rank == 0 else seed * 100003 + 7919 * rank
-    ids, offsets = synth.make_inputs(shape_name, nseq, rseed)
-    T = int(offsets[-1])
-    flops_step = algorithmic_flops(shape, offsets)
-
-    d_ids = torch.from_numpy(ids).cuda()
-    d_out = torch.empty((nseq, dim), dtype=torch.float32, device="cuda")
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
-    sptr = stream.cuda_stream
-    L = _lib.lib()
-
-    def step_device():
-        model.embed_batch_device(d_ids.data_ptr(), offsets, nseq, d_out.data_ptr(), dim, sptr)
-
-    for _ in range(args.warmup):
-        flush.zero_()
-        step_device()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    # timed region: K steps, L2 flushed (256 MB write) between them, CUDA
-    # events around each step on the stream the library launches on
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
-    smi_index = phys[local_rank] if len(phys) > local_rank and phys[local_rank] else local_rank
-    L.ecdbg_profile(1)
-    with ClockSampler(smi_index) as clk:
-        for i in range(args.steps):
-            flush.zero_()
-            ev[i][0].record(stream)
-            step_device()
-            ev[i][1].record(stream)
-        torch.cuda.synchronize()
-    launches = int(L.ecdbg_launches())
-    L.ecdbg_profile(0)
-    ms = sum(a.elapsed_time(b) for a, b in ev)
-    prof = {}
-    import ctypes as C
-    for cls in ("gemm", "attention", "rows"):
-        v = [C.c_double(), C.c_double(), C.c_double(), C.c_longlong()]
-        L.ecdbg_profile_read(cls.encode(), *[C.byref(x) for x in v])
-        prof[cls] = {"ms": v[0].value, "flops": v[1].value, "bytes": v[2].value,
-                     "launches": v[3].value}
-    clocks = clk.summary()
-
-    # end to end through the host API (ec_embed_batch): ids from pinned host
-    # memory in, embeddings back to host memory, each step
-    h_ids = torch.from_numpy(ids).pin_memory().numpy()
-    h_out = np.empty((nseq, dim), np.float32)
-    for _ in range(2):
-        model.embed_batch(h_ids, offsets, out=h_out)
-    e2e_s = 0.0
-    for _ in range(args.steps):
-        flush.zero_()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        model.embed_batch(h_ids, offsets, out=h_out)
-        e2e_s += time.perf_counter() - t0
-    nblk = int(np.sum((np.diff(offsets) + 63) // 64))
-    h2d = T * 4 + (nseq + 1) * 4 + nblk * 8
-    d2h = nseq * dim * 4
-
-    if world > 1:
-        t = torch.tensor([ms, e2e_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_s = float(t[0]), float(t[1])
-        dist.barrier()
-
-    out = None
-    if rank == 0:
-        peaks, src = measured_peaks()
-        g = prof["gemm"]
-        achieved = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else None
-        peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
-        traffic = profile_traffic(f"gemm_{args.workload}")
-        value = world * nseq * args.steps / (ms * 1e-3)
-        step_tflops = flops_step * args.steps / (ms * 1e-3) / 1e12
-        out = {
-            "metric": "embeddings/sec", "value": value, "unit": "embeddings/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded ids and N(0,0.02) weights of the named shape)",
-            "config": {"workload": shape_name, "description": desc, "sequences_per_rank": nseq,
-                       "tokens_per_rank": T, "parallelism": f"dp{world} (sequence shards)",
-                       "l2": "flushed (256 MB write) between timed steps",
-                       "precision": "bf16 tensor-core GEMM/attention, fp32 accumulate, "
-                                    "fp32 norms; residual between sublayers: the "
-                                    "LayerNorm's bf16 output (BERT/MPNet), fp32 (Qwen3, "
-                                    "Gemma)"},
-            "e2e": {"value": world * nseq * args.steps / e2e_s, "unit": "embeddings/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "timing": "host wall clock around the synchronous ec_embed_batch call"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_tn_bf16 (all GEMM launches)",
-                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": (achieved / peak) if achieved and peak else None,
-                         "traffic": traffic,
-                         "peak_source": f"{src} bf16_tflops_sustained (dense cuBLAS, "
-                                        "seconds-long loop)",
-                         "step_tflops": step_tflops,
-                         "step_frac_of_peak": step_tflops / peak if peak else None},
-            "kernel_classes": prof,
-            "gpu_launches": launches,
-            "clocks": clocks,
-        }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            out["cpu_baseline"] = cpu_baseline(mdir, ids, offsets, args.cpu_seconds)
-        except Exception as e:  # the baseline must not sink the GPU number
-            out["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(out), flush=True)
-    _lib.shutdown()
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    if args.workload == "minilm":
+        return run_default(args)
+    if args.workload in WORKLOADS:
+        return run_single_embed(args)
+    if args.workload == "ivf":
+        return run_ivf(args)
+    if args.workload == "query":
+        return run_query(args)
+    if args.workload == "search":
+        return run_search(args, rank, local_rank)
+    return run_tokenize(args, rank)
 
 
 if __name__ == "__main__":

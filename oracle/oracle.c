@@ -18,6 +18,53 @@ static inline float sexp(float x) { return (float)exp((double)x); }
 static inline float slog(float x) { return (float)log((double)x); }
 static inline float ssqrt(float x) { return (float)sqrt((double)x); }
 
+/* ---- intra-sequence parallel loops --------------------------------------
+ * or_set_seq_threads(n) lets one sequence's forward split its loops over
+ * tokens and over heads between n threads.  Every value is still computed
+ * by the same sequential code (each token row or head is one task), so the
+ * results do not depend on n; 1, the default, keeps the reference's one
+ * thread per sequence. */
+static int g_seq_threads = 1;
+void or_set_seq_threads(int n) { g_seq_threads = n < 1 ? 1 : n; }
+
+typedef void (*par_body)(void *ctx, int i);
+typedef struct {
+  par_body fn;
+  void *ctx;
+  int n;
+  int next;
+  pthread_mutex_t mu;
+} par_job;
+
+static void *par_worker(void *arg) {
+  par_job *j = (par_job *)arg;
+  for (;;) {
+    pthread_mutex_lock(&j->mu);
+    const int i = j->next++;
+    pthread_mutex_unlock(&j->mu);
+    if (i >= j->n) return NULL;
+    j->fn(j->ctx, i);
+  }
+}
+
+/* fn(ctx, i) for i in [0, n): on the calling thread alone, or on up to
+ * g_seq_threads threads taking indices in turn */
+static void par_for(int n, par_body fn, void *ctx) {
+  int nt = g_seq_threads < n ? g_seq_threads : n;
+  if (nt <= 1) {
+    for (int i = 0; i < n; ++i) fn(ctx, i);
+    return;
+  }
+  par_job j = {fn, ctx, n, 0, PTHREAD_MUTEX_INITIALIZER};
+  pthread_t tid[256];
+  if (nt > 256) nt = 256;
+  int started = 0;
+  for (int t = 1; t < nt; ++t)
+    if (pthread_create(&tid[started], NULL, par_worker, &j) == 0) ++started;
+  par_worker(&j);
+  for (int t = 0; t < started; ++t) pthread_join(tid[t], NULL);
+}
+
 /* %dot (bert.lisp:133-143, llama.lisp:86-95, ann.lisp:25-35, kb.lisp:153-162):
  * sequential single-float sum of products. */
 float or_dot(const float *a, const float *b, int n) {
@@ -96,40 +143,109 @@ int or_mpnet_bucket(int i, int j) {
   return ret + (f < 15 ? f : 15);
 }
 
+/* Shared state of one BERT / MPNet forward, for the parallel loop bodies. */
+typedef struct {
+  const or_bert *m;
+  const or_bert_layer *lw;
+  int seq;
+  float *h, *tmp, *ctx, *qb, *kb, *vb, *normed, *scores, *ff;
+} bert_state;
+
 /* Shared attention body for bert::encoder-layer (bert.lisp:226-248) and
- * bert::mpnet-layer (bert.lisp:408-423). */
-static void bert_attention(const or_bert *m, const float *q, const float *k,
-                           const float *v, float *ctx, float *scores, int seq) {
-  const int H = m->hidden, hd = m->head_dim;
+ * bert::mpnet-layer (bert.lisp:408-423): one head per task, each with its
+ * own seq x seq score block. */
+static void bert_attention_head(void *arg, int hh) {
+  const bert_state *S = (const bert_state *)arg;
+  const or_bert *m = S->m;
+  const int H = m->hidden, hd = m->head_dim, seq = S->seq;
+  const float *q = S->qb, *k = S->kb, *v = S->vb;
+  float *ctx = S->ctx, *scores = S->scores + (size_t)hh * seq * seq;
   const float sqrt_hd = ssqrt((float)hd);
-  for (int hh = 0; hh < m->heads; ++hh) {
-    for (int t1 = 0; t1 < seq; ++t1) {
-      for (int t2 = 0; t2 < seq; ++t2) {
-        float s;
-        if (m->mpnet) {
-          s = or_dot(q + (size_t)t1 * H + hh * hd, k + (size_t)t2 * H + hh * hd, hd) /
-                  sqrt_hd +
-              m->rel_bias[or_mpnet_bucket(t1, t2) * m->heads + hh];
-        } else if (m->causal && t2 > t1) {
-          s = -1e9f;
-        } else {
-          s = or_dot(q + (size_t)t1 * H + hh * hd, k + (size_t)t2 * H + hh * hd, hd) /
-              sqrt_hd;
-        }
-        scores[(size_t)t1 * seq + t2] = s;
+  for (int t1 = 0; t1 < seq; ++t1) {
+    for (int t2 = 0; t2 < seq; ++t2) {
+      float s;
+      if (m->mpnet) {
+        s = or_dot(q + (size_t)t1 * H + hh * hd, k + (size_t)t2 * H + hh * hd, hd) / sqrt_hd +
+            m->rel_bias[or_mpnet_bucket(t1, t2) * m->heads + hh];
+      } else if (m->causal && t2 > t1) {
+        s = -1e9f;
+      } else {
+        s = or_dot(q + (size_t)t1 * H + hh * hd, k + (size_t)t2 * H + hh * hd, hd) / sqrt_hd;
       }
-      if (m->mpnet) softmax(scores + (size_t)t1 * seq, seq);
+      scores[(size_t)t1 * seq + t2] = s;
     }
-    if (!m->mpnet)
-      for (int t1 = 0; t1 < seq; ++t1) softmax(scores + (size_t)t1 * seq, seq);
-    for (int t1 = 0; t1 < seq; ++t1)
-      for (int i = 0; i < hd; ++i) {
-        float acc = 0.0f;
-        for (int t2 = 0; t2 < seq; ++t2)
-          acc = acc + scores[(size_t)t1 * seq + t2] * v[(size_t)t2 * H + hh * hd + i];
-        ctx[(size_t)t1 * H + hh * hd + i] = acc;
-      }
+    if (m->mpnet) softmax(scores + (size_t)t1 * seq, seq);
   }
+  if (!m->mpnet)
+    for (int t1 = 0; t1 < seq; ++t1) softmax(scores + (size_t)t1 * seq, seq);
+  for (int t1 = 0; t1 < seq; ++t1)
+    for (int i = 0; i < hd; ++i) {
+      float acc = 0.0f;
+      for (int t2 = 0; t2 < seq; ++t2)
+        acc = acc + scores[(size_t)t1 * seq + t2] * v[(size_t)t2 * H + hh * hd + i];
+      ctx[(size_t)t1 * H + hh * hd + i] = acc;
+    }
+}
+
+/* q, k, v projections of token t (bert.lisp:220-225) */
+static void bert_qkv_tok(void *arg, int t) {
+  const bert_state *S = (const bert_state *)arg;
+  const int H = S->m->hidden;
+  const or_bert_layer *lw = S->lw;
+  linear_b(S->h + (size_t)t * H, lw->q_w, lw->q_b, S->qb + (size_t)t * H, H, H);
+  linear_b(S->h + (size_t)t * H, lw->k_w, lw->k_b, S->kb + (size_t)t * H, H, H);
+  linear_b(S->h + (size_t)t * H, lw->v_w, lw->v_b, S->vb + (size_t)t * H, H, H);
+}
+
+/* encoder-layer (bert.lisp:250-258): output projection + residual + LN */
+static void bert_ao_tok(void *arg, int t) {
+  const bert_state *S = (const bert_state *)arg;
+  const int H = S->m->hidden;
+  const or_bert_layer *lw = S->lw;
+  float *tr = S->tmp + (size_t)t * H;
+  linear_b(S->ctx + (size_t)t * H, lw->ao_w, lw->ao_b, tr, H, H);
+  for (int i = 0; i < H; ++i) tr[i] = tr[i] + S->h[(size_t)t * H + i];
+  layernorm(tr, H, lw->ao_g, lw->ao_b2);
+}
+
+/* encoder-layer (bert.lisp:259-271): GELU FFN + residual + LN into h */
+static void bert_ffn_tok(void *arg, int t) {
+  const bert_state *S = (const bert_state *)arg;
+  const int H = S->m->hidden, F = S->m->inter;
+  const or_bert_layer *lw = S->lw;
+  float *f = S->ff + (size_t)t * F; /* a fresh per-token array in the Lisp */
+  float *hr = S->h + (size_t)t * H;
+  linear_b(S->tmp + (size_t)t * H, lw->ff_w, lw->ff_b, f, H, F);
+  for (int i = 0; i < F; ++i) f[i] = gelu(f[i]);
+  linear_b(f, lw->o_w, lw->o_b, hr, F, H);
+  for (int i = 0; i < H; ++i) hr[i] = hr[i] + S->tmp[(size_t)t * H + i];
+  layernorm(hr, H, lw->o_g, lw->o_b2);
+}
+
+/* mpnet-layer (bert.lisp:424-437): output projection, residual + LN, FFN in */
+static void mpnet_ao_ff1_tok(void *arg, int t) {
+  const bert_state *S = (const bert_state *)arg;
+  const int H = S->m->hidden, F = S->m->inter;
+  const or_bert_layer *lw = S->lw;
+  linear_b(S->ctx + (size_t)t * H, lw->ao_w, lw->ao_b, S->tmp + (size_t)t * H, H, H);
+  float *nr = S->normed + (size_t)t * H;
+  for (int i = 0; i < H; ++i) nr[i] = S->tmp[(size_t)t * H + i] + S->h[(size_t)t * H + i];
+  layernorm(nr, H, lw->ao_g, lw->ao_b2);
+  float *f = S->ff + (size_t)t * F;
+  linear_b(nr, lw->ff_w, lw->ff_b, f, H, F);
+  for (int i = 0; i < F; ++i) f[i] = gelu(f[i]);
+}
+
+/* mpnet-layer (bert.lisp:438-452): FFN out, residual + LN into h */
+static void mpnet_ff2_tok(void *arg, int t) {
+  const bert_state *S = (const bert_state *)arg;
+  const int H = S->m->hidden, F = S->m->inter;
+  const or_bert_layer *lw = S->lw;
+  float *tr = S->tmp + (size_t)t * H;
+  linear_b(S->ff + (size_t)t * F, lw->o_w, lw->o_b, tr, F, H);
+  for (int i = 0; i < H; ++i) tr[i] = tr[i] + S->normed[(size_t)t * H + i];
+  layernorm(tr, H, lw->o_g, lw->o_b2);
+  memcpy(S->h + (size_t)t * H, tr, H * sizeof(float));
 }
 
 /* bert::embed-bert (bert.lisp:275-320) and bert::embed-mpnet (:455-499). */
@@ -143,7 +259,7 @@ int or_bert_embed(const or_bert *m, const int32_t *ids, int seq, float *out) {
   float *kb = malloc(sh * sizeof(float));
   float *vb = malloc(sh * sizeof(float));
   float *normed = malloc(sh * sizeof(float));
-  float *scores = malloc((size_t)seq * seq * sizeof(float));
+  float *scores = malloc((size_t)m->heads * seq * seq * sizeof(float));
   float *ff = malloc((size_t)seq * F * sizeof(float));
   if (!h || !tmp || !ctx || !qb || !kb || !vb || !normed || !scores || !ff) {
     free(h); free(tmp); free(ctx); free(qb); free(kb); free(vb);
@@ -166,52 +282,17 @@ int or_bert_embed(const or_bert *m, const int32_t *ids, int seq, float *out) {
   }
   for (int t = 0; t < seq; ++t) layernorm(h + (size_t)t * H, H, m->emb_g, m->emb_b);
 
+  bert_state S = {m, NULL, seq, h, tmp, ctx, qb, kb, vb, normed, scores, ff};
   for (int li = 0; li < m->layers; ++li) {
-    const or_bert_layer *lw = &m->L[li];
-    for (int t = 0; t < seq; ++t) {
-      linear_b(h + (size_t)t * H, lw->q_w, lw->q_b, qb + (size_t)t * H, H, H);
-      linear_b(h + (size_t)t * H, lw->k_w, lw->k_b, kb + (size_t)t * H, H, H);
-      linear_b(h + (size_t)t * H, lw->v_w, lw->v_b, vb + (size_t)t * H, H, H);
-    }
-    bert_attention(m, qb, kb, vb, ctx, scores, seq);
+    S.lw = &m->L[li];
+    par_for(seq, bert_qkv_tok, &S);
+    par_for(m->heads, bert_attention_head, &S);
     if (!m->mpnet) {
-      /* encoder-layer (bert.lisp:250-271) */
-      for (int t = 0; t < seq; ++t) {
-        float *tr = tmp + (size_t)t * H;
-        linear_b(ctx + (size_t)t * H, lw->ao_w, lw->ao_b, tr, H, H);
-        for (int i = 0; i < H; ++i) tr[i] = tr[i] + h[(size_t)t * H + i];
-        layernorm(tr, H, lw->ao_g, lw->ao_b2);
-      }
-      for (int t = 0; t < seq; ++t) {
-        float *f = ff; /* fresh per-token array in the Lisp; same values */
-        float *hr = h + (size_t)t * H;
-        linear_b(tmp + (size_t)t * H, lw->ff_w, lw->ff_b, f, H, F);
-        for (int i = 0; i < F; ++i) f[i] = gelu(f[i]);
-        linear_b(f, lw->o_w, lw->o_b, hr, F, H);
-        for (int i = 0; i < H; ++i) hr[i] = hr[i] + tmp[(size_t)t * H + i];
-        layernorm(hr, H, lw->o_g, lw->o_b2);
-      }
+      par_for(seq, bert_ao_tok, &S);
+      par_for(seq, bert_ffn_tok, &S);
     } else {
-      /* mpnet-layer (bert.lisp:424-452) */
-      for (int t = 0; t < seq; ++t)
-        linear_b(ctx + (size_t)t * H, lw->ao_w, lw->ao_b, tmp + (size_t)t * H, H, H);
-      for (int t = 0; t < seq; ++t) {
-        float *nr = normed + (size_t)t * H;
-        for (int i = 0; i < H; ++i) nr[i] = tmp[(size_t)t * H + i] + h[(size_t)t * H + i];
-        layernorm(nr, H, lw->ao_g, lw->ao_b2);
-      }
-      for (int t = 0; t < seq; ++t) {
-        float *f = ff + (size_t)t * F;
-        linear_b(normed + (size_t)t * H, lw->ff_w, lw->ff_b, f, H, F);
-        for (int i = 0; i < F; ++i) f[i] = gelu(f[i]);
-      }
-      for (int t = 0; t < seq; ++t) {
-        float *tr = tmp + (size_t)t * H;
-        linear_b(ff + (size_t)t * F, lw->o_w, lw->o_b, tr, F, H);
-        for (int i = 0; i < H; ++i) tr[i] = tr[i] + normed[(size_t)t * H + i];
-        layernorm(tr, H, lw->o_g, lw->o_b2);
-        memcpy(h + (size_t)t * H, tr, H * sizeof(float));
-      }
+      par_for(seq, mpnet_ao_ff1_tok, &S);
+      par_for(seq, mpnet_ff2_tok, &S);
     }
   }
   /* pooling + L2 (bert.lisp:302-319) */
@@ -263,10 +344,83 @@ static void rope(float *x, int pos, int heads, int hd, const float *cs,
   }
 }
 
+/* Shared state of one Llama / Qwen3 forward, for the parallel loop bodies. */
+typedef struct {
+  const or_llama *m;
+  const or_llama_layer *lw;
+  int seq, tw;
+  const float *cs, *sn;
+  float *h, *normed, *qb, *kb, *vb, *ctx, *scores, *tmp, *o;
+} llama_state;
+
+/* input RMSNorm, q/k/v projections, q/k RMSNorm and RoPE of token t
+ * (llama.lisp:296-312) */
+static void llama_qkv_tok(void *arg, int t) {
+  const llama_state *S = (const llama_state *)arg;
+  const or_llama *m = S->m;
+  const or_llama_layer *lw = S->lw;
+  const int H = m->hidden, hd = m->head_dim, heads = m->heads, kv = m->kv_heads;
+  const int qd = heads * hd, kvd = kv * hd;
+  float *nr = S->normed + (size_t)t * H;
+  memcpy(nr, S->h + (size_t)t * H, H * sizeof(float));
+  rmsnorm(nr, H, lw->in_ln, m->eps);
+  linear_nb(nr, lw->q_w, S->qb + (size_t)t * qd, H, qd);
+  linear_nb(nr, lw->k_w, S->kb + (size_t)t * kvd, H, kvd);
+  linear_nb(nr, lw->v_w, S->vb + (size_t)t * kvd, H, kvd);
+  if (lw->q_norm)
+    for (int hh = 0; hh < heads; ++hh) rmsnorm(S->qb + (size_t)t * qd + hh * hd, hd, lw->q_norm, m->eps);
+  if (lw->k_norm)
+    for (int hh = 0; hh < kv; ++hh) rmsnorm(S->kb + (size_t)t * kvd + hh * hd, hd, lw->k_norm, m->eps);
+  rope(S->qb + (size_t)t * qd, t, heads, hd, S->cs, S->sn);
+  rope(S->kb + (size_t)t * kvd, t, kv, hd, S->cs, S->sn);
+}
+
+/* causal GQA attention of one query head (llama.lisp:313-324) */
+static void llama_attention_head(void *arg, int hh) {
+  const llama_state *S = (const llama_state *)arg;
+  const or_llama *m = S->m;
+  const int hd = m->head_dim, heads = m->heads, kv = m->kv_heads, seq = S->seq;
+  const int qd = heads * hd, kvd = kv * hd, kvh = hh / (heads / kv);
+  const float sqrt_hd = ssqrt((float)hd);
+  float *scores = S->scores + (size_t)hh * seq;
+  for (int t1 = 0; t1 < seq; ++t1) {
+    for (int t2 = 0; t2 <= t1; ++t2)
+      scores[t2] = or_dot(S->qb + (size_t)t1 * qd + hh * hd, S->kb + (size_t)t2 * kvd + kvh * hd, hd) /
+                   sqrt_hd;
+    softmax(scores, t1 + 1);
+    for (int i = 0; i < hd; ++i) {
+      float acc = 0.0f;
+      for (int t2 = 0; t2 <= t1; ++t2) acc = acc + scores[t2] * S->vb[(size_t)t2 * kvd + kvh * hd + i];
+      S->ctx[(size_t)t1 * qd + hh * hd + i] = acc;
+    }
+  }
+}
+
+/* output projection + residual, post-attention RMSNorm, SwiGLU FFN +
+ * residual of token t (llama.lisp:325-343) */
+static void llama_out_ffn_tok(void *arg, int t) {
+  const llama_state *S = (const llama_state *)arg;
+  const or_llama *m = S->m;
+  const or_llama_layer *lw = S->lw;
+  const int H = m->hidden, F = m->inter, qd = m->heads * m->head_dim;
+  float *hr = S->h + (size_t)t * H;
+  float *trow = S->tmp + (size_t)t * S->tw, *orow = S->o + (size_t)t * F;
+  linear_nb(S->ctx + (size_t)t * qd, lw->o_w, trow, qd, H);
+  for (int i = 0; i < H; ++i) hr[i] = hr[i] + trow[i];
+  float *nr = S->normed + (size_t)t * H;
+  memcpy(nr, hr, H * sizeof(float));
+  rmsnorm(nr, H, lw->post_ln, m->eps);
+  linear_nb(nr, lw->gate, orow, H, F);
+  linear_nb(nr, lw->up, trow, H, F);
+  for (int i = 0; i < F; ++i) orow[i] = silu(orow[i]) * trow[i];
+  linear_nb(orow, lw->down, trow, F, H); /* the up row is consumed: reuse it */
+  for (int i = 0; i < H; ++i) hr[i] = hr[i] + trow[i];
+}
+
 /* llama::embed / layer-forward (llama.lisp:224-344). */
 int or_llama_embed(const or_llama *m, const int32_t *ids, int seq, float *out) {
   const int H = m->hidden, heads = m->heads, kv = m->kv_heads, hd = m->head_dim;
-  const int F = m->inter, kvd = kv * hd, qd = heads * hd, group = heads / kv;
+  const int F = m->inter, kvd = kv * hd, qd = heads * hd;
   const int half = hd / 2;
   if (seq > m->max_pos) return -2;
   /* init-rope (llama.lisp:124-135) */
@@ -278,7 +432,7 @@ int or_llama_embed(const or_llama *m, const int32_t *ids, int seq, float *out) {
   float *kb = malloc((size_t)seq * kvd * sizeof(float));
   float *vb = malloc((size_t)seq * kvd * sizeof(float));
   float *ctx = malloc((size_t)seq * qd * sizeof(float));
-  float *scores = malloc((size_t)seq * sizeof(float));
+  float *scores = malloc((size_t)heads * seq * sizeof(float));
   int tw = H > F ? H : F;
   float *tmp = malloc((size_t)seq * tw * sizeof(float));
   float *o = malloc((size_t)seq * F * sizeof(float));
@@ -296,61 +450,12 @@ int or_llama_embed(const or_llama *m, const int32_t *ids, int seq, float *out) {
     }
   for (int t = 0; t < seq; ++t)
     memcpy(h + (size_t)t * H, m->w_embed + (size_t)ids[t] * H, H * sizeof(float));
-  const float sqrt_hd = ssqrt((float)hd);
+  llama_state S = {m, NULL, seq, tw, cs, sn, h, normed, qb, kb, vb, ctx, scores, tmp, o};
   for (int li = 0; li < m->layers; ++li) {
-    const or_llama_layer *lw = &m->L[li];
-    for (int t = 0; t < seq; ++t) {
-      memcpy(normed + (size_t)t * H, h + (size_t)t * H, H * sizeof(float));
-      rmsnorm(normed + (size_t)t * H, H, lw->in_ln, m->eps);
-    }
-    for (int t = 0; t < seq; ++t) {
-      linear_nb(normed + (size_t)t * H, lw->q_w, qb + (size_t)t * qd, H, qd);
-      linear_nb(normed + (size_t)t * H, lw->k_w, kb + (size_t)t * kvd, H, kvd);
-      linear_nb(normed + (size_t)t * H, lw->v_w, vb + (size_t)t * kvd, H, kvd);
-    }
-    for (int t = 0; t < seq; ++t) {
-      if (lw->q_norm)
-        for (int hh = 0; hh < heads; ++hh)
-          rmsnorm(qb + (size_t)t * qd + hh * hd, hd, lw->q_norm, m->eps);
-      if (lw->k_norm)
-        for (int hh = 0; hh < kv; ++hh)
-          rmsnorm(kb + (size_t)t * kvd + hh * hd, hd, lw->k_norm, m->eps);
-      rope(qb + (size_t)t * qd, t, heads, hd, cs, sn);
-      rope(kb + (size_t)t * kvd, t, kv, hd, cs, sn);
-    }
-    for (int hh = 0; hh < heads; ++hh) {
-      int kvh = hh / group;
-      for (int t1 = 0; t1 < seq; ++t1) {
-        for (int t2 = 0; t2 <= t1; ++t2)
-          scores[t2] = or_dot(qb + (size_t)t1 * qd + hh * hd,
-                              kb + (size_t)t2 * kvd + kvh * hd, hd) / sqrt_hd;
-        softmax(scores, t1 + 1);
-        for (int i = 0; i < hd; ++i) {
-          float acc = 0.0f;
-          for (int t2 = 0; t2 <= t1; ++t2)
-            acc = acc + scores[t2] * vb[(size_t)t2 * kvd + kvh * hd + i];
-          ctx[(size_t)t1 * qd + hh * hd + i] = acc;
-        }
-      }
-    }
-    for (int t = 0; t < seq; ++t) {
-      float *tr = tmp + (size_t)t * H;
-      linear_nb(ctx + (size_t)t * qd, lw->o_w, tr, qd, H);
-      for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = h[(size_t)t * H + i] + tr[i];
-    }
-    for (int t = 0; t < seq; ++t) {
-      memcpy(normed + (size_t)t * H, h + (size_t)t * H, H * sizeof(float));
-      rmsnorm(normed + (size_t)t * H, H, lw->post_ln, m->eps);
-    }
-    for (int t = 0; t < seq; ++t) {
-      float *orow = o + (size_t)t * F, *trow = tmp + (size_t)t * F;
-      linear_nb(normed + (size_t)t * H, lw->gate, orow, H, F);
-      linear_nb(normed + (size_t)t * H, lw->up, trow, H, F);
-      for (int i = 0; i < F; ++i) orow[i] = silu(orow[i]) * trow[i];
-      float *dr = tmp + (size_t)t * H;
-      linear_nb(orow, lw->down, dr, F, H);
-      for (int i = 0; i < H; ++i) h[(size_t)t * H + i] = h[(size_t)t * H + i] + dr[i];
-    }
+    S.lw = &m->L[li];
+    par_for(seq, llama_qkv_tok, &S);
+    par_for(heads, llama_attention_head, &S);
+    par_for(seq, llama_out_ffn_tok, &S);
   }
   for (int t = 0; t < seq; ++t) rmsnorm(h + (size_t)t * H, H, m->w_norm, m->eps);
   for (int i = 0; i < H; ++i) out[i] = 0.0f;
@@ -627,18 +732,76 @@ typedef struct {
   int32_t *assign;
 } assign_job;
 
+/* Four rows at a time against four centroids at a time: sixteen independent
+ * %dot chains, each still the sequential single-float sum of or_dot, and the
+ * strict-> argmax visits the centroids of every row in index order, so the
+ * result equals or_nearest_centroid row by row (only faster). */
+static void nearest4(const float *const xr[4], int nr, const float *cent, int k, int dim,
+                     int32_t out[4]) {
+  float best_s[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+  int32_t best[4] = {0, 0, 0, 0};
+  int c = 0;
+  for (; c + 4 <= k; c += 4) {
+    const float *c0 = cent + (size_t)c * dim, *c1 = c0 + dim, *c2 = c1 + dim, *c3 = c2 + dim;
+    for (int r = 0; r < nr; ++r) {
+      const float *x = xr[r];
+      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+      for (int i = 0; i < dim; ++i) {
+        const float xi = x[i];
+        s0 = s0 + xi * c0[i];
+        s1 = s1 + xi * c1[i];
+        s2 = s2 + xi * c2[i];
+        s3 = s3 + xi * c3[i];
+      }
+      const float sc[4] = {s0, s1, s2, s3};
+      for (int j = 0; j < 4; ++j)
+        if (sc[j] > best_s[r]) {
+          best_s[r] = sc[j];
+          best[r] = c + j;
+        }
+    }
+  }
+  for (; c < k; ++c)
+    for (int r = 0; r < nr; ++r) {
+      const float sc = or_dot(xr[r], cent + (size_t)c * dim, dim);
+      if (sc > best_s[r]) {
+        best_s[r] = sc;
+        best[r] = c;
+      }
+    }
+  for (int r = 0; r < nr; ++r) out[r] = best[r];
+}
+
 static void *assign_thread(void *arg) {
   assign_job *j = (assign_job *)arg;
+  for (int64_t i = j->s; i < j->e; i += 4) {
+    const int nr = j->e - i < 4 ? (int)(j->e - i) : 4;
+    const float *xr[4];
+    for (int r = 0; r < nr; ++r) {
+      const int64_t row = j->rows ? j->rows[i + r] : i + r;
+      xr[r] = j->vecs + (size_t)row * j->dim;
+    }
+    int32_t out[4];
+    nearest4(xr, nr, j->cent, j->k, j->dim, out);
+    for (int r = 0; r < nr; ++r) j->assign[i + r] = out[r];
+  }
+  return NULL;
+}
+
+/* the reference's own loop shape: or_nearest_centroid per row, one
+ * centroid at a time (ann.lisp:69-77), for the timed CPU baseline */
+static void *assign_thread_scalar(void *arg) {
+  assign_job *j = (assign_job *)arg;
   for (int64_t i = j->s; i < j->e; ++i) {
-    int64_t row = j->rows ? j->rows[i] : i;
+    const int64_t row = j->rows ? j->rows[i] : i;
     j->assign[i] = or_nearest_centroid(j->vecs + (size_t)row * j->dim, j->cent, j->k, j->dim);
   }
   return NULL;
 }
 
-/* parallel assign over contiguous ranges (ann.lisp:90-105 / :131-144) */
-void or_assign(const float *vecs, const int64_t *rows, int64_t nrows,
-               const float *cent, int k, int dim, int32_t *assign, int threads) {
+static void assign_ranges(const float *vecs, const int64_t *rows, int64_t nrows,
+                          const float *cent, int k, int dim, int32_t *assign, int threads,
+                          void *(*body)(void *)) {
   if (threads < 1) threads = 1;
   int64_t per = (nrows + threads - 1) / threads;
   pthread_t *tid = calloc((size_t)threads, sizeof(pthread_t));
@@ -648,12 +811,24 @@ void or_assign(const float *vecs, const int64_t *rows, int64_t nrows,
     int64_t s = (int64_t)t * per, e = s + per < nrows ? s + per : nrows;
     if (s >= e) continue;
     jobs[started] = (assign_job){vecs, cent, rows, s, e, k, dim, assign};
-    pthread_create(&tid[started], NULL, assign_thread, &jobs[started]);
+    pthread_create(&tid[started], NULL, body, &jobs[started]);
     ++started;
   }
   for (int t = 0; t < started; ++t) pthread_join(tid[t], NULL);
   free(tid);
   free(jobs);
+}
+
+/* ann.lisp:90-105's parallel assign, one row and one centroid at a time */
+void or_assign_scalar(const float *vecs, const int64_t *rows, int64_t nrows,
+                      const float *cent, int k, int dim, int32_t *assign, int threads) {
+  assign_ranges(vecs, rows, nrows, cent, k, dim, assign, threads, assign_thread_scalar);
+}
+
+/* parallel assign over contiguous ranges (ann.lisp:90-105 / :131-144) */
+void or_assign(const float *vecs, const int64_t *rows, int64_t nrows,
+               const float *cent, int k, int dim, int32_t *assign, int threads) {
+  assign_ranges(vecs, rows, nrows, cent, k, dim, assign, threads, assign_thread);
 }
 
 /* Lloyd update (ann.lisp:107-122): serial sums in sample order; an empty

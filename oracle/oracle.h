@@ -91,6 +91,11 @@ typedef struct {
 
 int or_gemma_embed(const or_gemma *m, const int32_t *ids, int seq, float *out);
 
+/* Threads one sequence's forward may split its token and head loops over
+ * (default 1, the reference's one thread per sequence).  Results do not
+ * depend on it: each token row or head is computed by the same code. */
+void or_set_seq_threads(int n);
+
 /* Batch driver mirroring embed.lisp:88-105: batches of `threads` sequences,
  * one thread per sequence, joined in input order.  kind 0 = bert, 1 = llama,
  * 2 = gemma. */
@@ -107,6 +112,10 @@ float or_dot(const float *a, const float *b, int n);
 int32_t or_nearest_centroid(const float *x, const float *cent, int k, int dim);
 void or_assign(const float *vecs, const int64_t *rows, int64_t nrows,
                const float *cent, int k, int dim, int32_t *assign, int threads);
+/* the same results one row and one centroid at a time, as ann.lisp's loop
+ * runs (or_assign interleaves sixteen %dot chains for speed) */
+void or_assign_scalar(const float *vecs, const int64_t *rows, int64_t nrows,
+                      const float *cent, int k, int dim, int32_t *assign, int threads);
 /* one Lloyd update given assignments (ann.lisp:107-122); cent in/out */
 void or_kmeans_update(const float *vecs, const int64_t *sample, int64_t ns,
                       const int32_t *assign, int k, int dim, float *cent);

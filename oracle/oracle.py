@@ -287,16 +287,23 @@ class OracleModel:
             raise RuntimeError(f"oracle embed failed rc={rc}")
         return out
 
-    def embed_batch(self, ids, offsets, threads=None):
+    def embed_batch(self, ids, offsets, threads=None, seq_threads=1):
+        """One thread per sequence in batches of `threads` (embed.lisp's
+        scheme); seq_threads > 1 also splits each sequence's token and head
+        loops (for long test sequences; the results do not change)."""
         ids = np.ascontiguousarray(ids, np.int32)
         offsets = np.ascontiguousarray(offsets, np.int64)
         nseq = offsets.size - 1
         out = np.zeros((nseq, self.dim), np.float32)
         threads = threads or os.cpu_count() or 1
-        rc = lib().or_embed_batch(C.c_int(self.kind), C.byref(self.m),
-                                  ids.ctypes.data_as(C.POINTER(C.c_int32)),
-                                  offsets.ctypes.data_as(C.POINTER(C.c_int64)), C.c_int(nseq),
-                                  C.c_int(self.dim), _fp(out), C.c_int(threads))
+        lib().or_set_seq_threads(C.c_int(max(1, int(seq_threads))))
+        try:
+            rc = lib().or_embed_batch(C.c_int(self.kind), C.byref(self.m),
+                                      ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                                      offsets.ctypes.data_as(C.POINTER(C.c_int64)), C.c_int(nseq),
+                                      C.c_int(self.dim), _fp(out), C.c_int(threads))
+        finally:
+            lib().or_set_seq_threads(C.c_int(1))
         if rc:
             raise RuntimeError(f"oracle embed_batch failed rc={rc}")
         return out
@@ -334,6 +341,21 @@ def assign(vecs, cent, rows=None, threads=None):
     lib().or_assign(_fp(vecs), _i64(rows_a) if rows_a is not None else None,
                     C.c_int64(nrows), _fp(cent), C.c_int(k), C.c_int(dim), _i32(out),
                     C.c_int(threads or os.cpu_count() or 1))
+    return out
+
+
+def assign_scalar(vecs, cent, rows=None, threads=None):
+    """assign() computed one row and one centroid at a time (ann.lisp's loop
+    shape; the timed CPU baseline)."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    cent = np.ascontiguousarray(cent, np.float32)
+    k, dim = cent.shape
+    nrows = vecs.shape[0] if rows is None else len(rows)
+    rows_a = None if rows is None else np.ascontiguousarray(rows, np.int64)
+    out = np.empty(nrows, np.int32)
+    lib().or_assign_scalar(_fp(vecs), _i64(rows_a) if rows_a is not None else None,
+                           C.c_int64(nrows), _fp(cent), C.c_int(k), C.c_int(dim), _i32(out),
+                           C.c_int(threads or os.cpu_count() or 1))
     return out
 
 

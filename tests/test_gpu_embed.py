@@ -1,8 +1,17 @@
 """End-to-end parity of the encoder forwards against the CPU oracle
-(restatement of bert.lisp / llama.lisp) on the same seeded weights and ids.
+(restatement of bert.lisp / llama.lisp / gemma.lisp) on the same seeded
+weights and ids.
 
-Tolerance (BF16 tensor-core path): per-vector cosine >= 0.999.
+Tolerances (per-vector cosine against the oracle):
+  * F32 models (MiniLM, MPNet, and F16 weights, which st.lisp widens to
+    F32): >= 0.9999;
+  * BF16 models (BERT-base, Qwen3) and EmbeddingGemma: >= 0.999.
+Full-depth cases run every layer of the BASELINE shapes (12-layer BERT-base
+and MPNet, 28-layer Qwen3 with its full 151,669-row vocabulary) on a few
+sequences up to the longest length each workload draws.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -11,6 +20,7 @@ from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
+COS_F32 = 0.9999
 COS_BF16 = 0.999
 
 
@@ -18,16 +28,23 @@ def _cos(a, b):
     return np.sum(a * b, axis=1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
 
 
-def _check(shape, seed, lengths, synth_root, ec, workload):
-    d = synth.build_model_dir(shape, seed, synth_root)
+def _tol(shape):
+    return COS_BF16 if shape.dtype == "BF16" or shape.model_type == "embedding_gemma2" else COS_F32
+
+
+def _check(shape, seed, lengths, synth_root, ec, workload, d=None):
+    d = d or synth.build_model_dir(shape, seed, synth_root)
     fam = model.load_model(d)
     ids, offs = synth.make_short_inputs(workload, lengths, seed, shape.vocab)
     got = model.embed_batch(ids, offs)
-    ref = oracle.OracleModel(d).embed_batch(ids, offs)
+    # one host thread per sequence, each splitting its token / head loops
+    # over its share of the cores (same values as one thread)
+    per = max(1, (os.cpu_count() or 1) // len(lengths))
+    ref = oracle.OracleModel(d).embed_batch(ids, offs, threads=len(lengths), seq_threads=per)
     cos = _cos(got, ref)
     assert np.all(np.isfinite(got))
     assert np.allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-5)
-    assert cos.min() >= COS_BF16, (fam, cos)
+    assert cos.min() >= _tol(shape), (fam, cos)
     return fam, cos
 
 
@@ -60,6 +77,96 @@ def test_qwen3(synth_root, ec):
     s = synth.with_layers(synth.QWEN3_06B, 2, vocab=4096)
     fam, _ = _check(s, 3, [1, 2, 40, 129, 300], synth_root, ec, "qwen3")
     assert fam == "llama"
+
+
+# ---- full depth: every layer of the BASELINE shapes --------------------------
+
+def test_bert_base_full_depth(synth_root, ec):
+    """12 layers, BF16 weights, CLS pooling; lengths up to 512."""
+    fam, cos = _check(synth.BERT_BASE, 1, [32, 200, 512], synth_root, ec, "bert")
+    assert fam == "bert"
+
+
+def test_mpnet_full_depth(synth_root, ec):
+    """12 layers, F32 weights, relative-position buckets; lengths up to 384."""
+    fam, cos = _check(synth.MPNET_BASE, 2, [64, 230, 384], synth_root, ec, "mpnet")
+    assert fam == "mpnet"
+
+
+def test_qwen3_full_depth_full_vocab(synth_root, ec):
+    """28 layers, 151,669-row vocabulary, GQA 16:8, causal, last-token
+    pooling; the longest sequence is 512 body tokens + EOS."""
+    fam, cos = _check(synth.QWEN3_06B, 3, [129, 300, 513], synth_root, ec, "qwen3")
+    assert fam == "llama"
+
+
+# ---- F16 weights (st.lisp:22-30 widening on the device) ----------------------
+
+def _f16_patterns_widened(ec):
+    """Every binary16 bit pattern uploaded as an F16 tensor and read back from
+    the device as f32."""
+    import ctypes as C
+    from embedcuda import _lib
+    pats = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    shape = np.array([256, 256], np.int64)
+    L = ec.lib()
+    _lib.check(L.ec_upload_tensor(b"f16.probe", _lib.EC_F16, shape.ctypes.data_as(C.POINTER(C.c_int64)),
+                                  2, pats.ctypes.data, pats.nbytes), "upload probe")
+    got = np.empty(65536, np.float32)
+    dt = C.c_int()
+    _lib.check(L.ecdbg_tensor_read(b"f16.probe", got.ctypes.data, got.nbytes, C.byref(dt)), "read")
+    assert dt.value == _lib.EC_F32
+    ref = np.empty(65536, np.float32)
+    oracle.lib().or_f16_to_f32(pats.ctypes.data_as(C.POINTER(C.c_uint16)),
+                               ref.ctypes.data_as(C.POINTER(C.c_float)), C.c_int64(65536))
+    return pats, got, ref
+
+
+def test_f16_widening_every_pattern(ec):
+    """Subnormals, signed zeros, and exponent 31 (Inf / NaN patterns) ->
+    +-most-positive-single-float, bit for bit as st::half-to-float."""
+    pats, got, ref = _f16_patterns_widened(ec)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    assert got[0x7C00] == np.finfo(np.float32).max and got[0xFE00] == -np.finfo(np.float32).max
+    assert got[0x0001] == np.float32(2.0 ** -24)  # smallest subnormal
+
+
+def test_f16_model(synth_root, ec, tmp_path):
+    """A 2-layer MiniLM stored as F16, with subnormal halves planted in used
+    weights and exponent-31 halves in embedding rows the inputs never touch
+    (ids below 1000, positions past the longest sequence)."""
+    s = synth.with_layers(synth.MINILM, 2)
+    import dataclasses
+    s = dataclasses.replace(s, name=s.name + "-f16", dtype="F16")
+    w = synth.make_weights(s, 0)
+    rng = np.random.default_rng(5)
+    sub = np.array([0x0001, 0x0003, 0x03FF, 0x8001, 0x8200, 0x0200], np.uint16)
+    for nm in ("encoder.layer.0.attention.self.query.weight", "encoder.layer.1.output.dense.weight",
+               "embeddings.word_embeddings.weight"):
+        dt, shape, a = w[nm]
+        a = a.copy().reshape(-1)
+        idx = rng.choice(a.size, 200, replace=False)
+        a[idx] = sub[rng.integers(0, len(sub), 200)]
+        w[nm] = (dt, shape, a.reshape(shape))
+    big = np.array([0x7C00, 0xFC00, 0x7E00, 0xFFFF, 0x7C01], np.uint16)
+    dt, shape, a = w["embeddings.word_embeddings.weight"]
+    a = a.copy()
+    a[1:40] = big[rng.integers(0, len(big), (39, shape[1]))]
+    w["embeddings.word_embeddings.weight"] = (dt, shape, a)
+    dt, shape, a = w["embeddings.position_embeddings.weight"]
+    a = a.copy()
+    a[300:] = big[rng.integers(0, len(big), (shape[0] - 300, shape[1]))]
+    w["embeddings.position_embeddings.weight"] = (dt, shape, a)
+    d = str(tmp_path / "minilm-f16")
+    os.makedirs(os.path.join(d, "1_Pooling"))
+    import json
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(synth.config_json(s), f)
+    with open(os.path.join(d, "1_Pooling", "config.json"), "w") as f:
+        json.dump({"word_embedding_dimension": s.hidden, "pooling_mode_mean_tokens": True}, f)
+    synth.write_safetensors(os.path.join(d, "model.safetensors"), w)
+    fam, cos = _check(s, 0, [1, 5, 64, 130, 256], synth_root, ec, "minilm", d=d)
+    assert fam == "bert"
 
 
 def test_batch_invariance_and_order(synth_root, ec):

@@ -220,3 +220,39 @@ def test_ivf_search_tensor_core_probe_ties_and_fallback(ec, corpus):
     qs = np.concatenate([near / np.linalg.norm(near, axis=1, keepdims=True), far], axis=0).astype(np.float32)
     _check_ivf(x, cent, counts, lists, qs, 32, 10)
     _check_ivf(x, cent, counts, lists, qs, 128, 10)
+
+
+# ---- the IVF workload's own density: k 4096, d 384 ------------------------------
+
+@pytest.fixture(scope="module")
+def c5_subset():
+    """200,000 rows of the IVF workload's distribution (4096 Gaussian
+    clusters, centers uniform on the unit sphere, sigma 0.05, rows
+    L2-normalised, seed 4) and its seeded training permutation."""
+    x, _ = synth.make_ivf_corpus(200_000, 384, 4096, seed=4)
+    return x, synth.make_ivf_sample(len(x), 4)
+
+
+def test_c5_density_assign_kmeans_lists_exact(ec, c5_subset):
+    """At k = 4096, d = 384 the tensor-core window holds many near-tied
+    centroids per row: assignments from identical centroids, two Lloyd
+    iterations and the final inverted lists must still equal the oracle's
+    (ann.lisp:69-158) exactly -- no tie exceptions are needed."""
+    x, sample = c5_subset
+    k = 4096
+    init = x[sample[:k]].copy()
+    _assign_rows(ec)
+    got = ann.assign(x, init)
+    tc, exact = _assign_rows(ec)
+    assert tc > 0  # the tensor-core path ran at this density
+    assert np.array_equal(got, oracle.assign(x, init))
+    cent = ann.kmeans(x, sample, k, 2)
+    ref = oracle.kmeans(x, sample, k, 2)
+    assert np.array_equal(cent, ref)
+    counts, lists = ann.assign_all(x, cent)
+    rc, rl = oracle.assign_all(x, ref)
+    assert np.array_equal(counts, rc) and np.array_equal(lists, rl)
+    # IVF top-10 at nprobe 32 over the same index (kb.lisp:348-364)
+    kb.load_index(x, (cent, counts, lists))
+    qs, _ = synth.make_ivf_corpus(300, 384, 4096, seed=4)
+    _check_ivf(x, cent, counts, lists, qs[:200], 32, 10)

@@ -133,3 +133,33 @@ def test_search_cpu_baseline_threads():
         t.join()
     for (ri, rs), (gi, gs) in zip(ref, got):
         assert np.array_equal(ri, gi) and np.array_equal(rs, gs)
+
+
+def test_bench_rank_shards_balanced():
+    """N > 1: every rank gets the workload's sequence count from one seeded
+    pool, with (nearly) equal token counts, and the shards partition the pool."""
+    import bench
+    for world in (2, 4, 8):
+        tot = []
+        seen = 0
+        for r in range(world):
+            ids, offs = bench.rank_inputs("minilm-l6", 1024, 0, r, world)
+            assert len(offs) - 1 == 1024
+            tot.append(int(offs[-1]))
+            seen += int(offs[-1])
+        pool_ids, pool_offs = synth.make_inputs("minilm-l6", 1024 * world, 0)
+        assert seen == int(pool_offs[-1])
+        assert max(tot) - min(tot) <= 0.01 * max(tot), tot
+    ids1, offs1 = bench.rank_inputs("minilm-l6", 1024, 0, 0, 1)
+    ref_ids, ref_offs = synth.make_inputs("minilm-l6", 1024, 0)
+    assert np.array_equal(ids1, ref_ids) and np.array_equal(offs1, ref_offs)
+
+
+def test_bench_reference_config_matches_ours():
+    """Both arms print the same `config` object for the same run."""
+    import bench
+    for world in (1, 4):
+        ids, offs = bench.rank_inputs("minilm-l6", 1024, 0, 0, world)
+        a = bench.workload_config("minilm", world, int(offs[-1]))
+        assert a["workload"] == "minilm-l6" and a["parallelism"] == f"dp{world} (sequence shards)"
+        assert a["tokens_per_rank"] == int(offs[-1])
