@@ -130,21 +130,23 @@ static cudaError_t run_mode(const AttnLaunch& l, cudaStream_t st) {
   return run_attn<HD, 0>(l, st);
 }
 
-// sequences [n_long, nseq) of the launch, one CTA per (sequence, head)
-template <int HD, int MODE, int BK, int MINB>
+// sequences [n_long, nseq) of the launch, one CTA per (sequence, head);
+// F16P: the kernel with fp16 probabilities (attn_short_h_kernel)
+template <int HD, int MODE, int BK, int MINB, bool F16P>
 static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
   using S = ShortAttnSmem<HD, MODE>;
   static_assert(kShortAttnMaxLen == kAttnShortCap, "short-kernel capacity");
   static std::mutex mu;
   static bool set[64] = {};
+  const void* fn = F16P ? reinterpret_cast<const void*>(attn_short_h_kernel<HD, MODE, MINB>)
+                        : reinterpret_cast<const void*>(attn_short_kernel<HD, MODE, BK, MINB>);
   int dev = 0;
   cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(attn_short_kernel<HD, MODE, BK, MINB>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(S::MAX_BYTES));
       if (e != cudaSuccess) return e;
       set[dev] = true;
@@ -168,7 +170,10 @@ static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
   a.rel_max = l.rel_max;
   a.kcap = (l.max_short_len + 15) & ~15;
   dim3 grid(l.nseq - l.n_long, l.heads);
-  attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
+  if (F16P)
+    attn_short_h_kernel<HD, MODE, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
+  else
+    attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
   return cudaGetLastError();
 }
 
@@ -176,11 +181,18 @@ template <int HD>
 static cudaError_t run_short_mode(const AttnLaunch& l, cudaStream_t st) {
   // head dim 32 fits five CTAs per SM (94 registers, 40 KB of K/V); the
   // register budget for that measured fastest among 64/128-key blocks and
-  // 4..6 CTAs per SM on MiniLM batches
+  // 4..6 CTAs per SM on MiniLM batches.  EC_SHORT_ATTN_BF16 keeps the fp32
+  // exponentials with bf16 probabilities.
   constexpr int MINB = HD == 32 ? 5 : 1;
-  if (l.causal) return run_short<HD, 2, 64, MINB>(l, st);
-  if (l.relbias) return run_short<HD, 1, 64, MINB>(l, st);
-  return run_short<HD, 0, 64, MINB>(l, st);
+  const bool bf16p = getenv("EC_SHORT_ATTN_BF16") != nullptr;
+  if (bf16p) {
+    if (l.causal) return run_short<HD, 2, 64, MINB, false>(l, st);
+    if (l.relbias) return run_short<HD, 1, 64, MINB, false>(l, st);
+    return run_short<HD, 0, 64, MINB, false>(l, st);
+  }
+  if (l.causal) return run_short<HD, 2, 64, MINB, true>(l, st);
+  if (l.relbias) return run_short<HD, 1, 64, MINB, true>(l, st);
+  return run_short<HD, 0, 64, MINB, true>(l, st);
 }
 
 // Sequences longer than kAttnShortCap go to the tcgen05 kernel (their
