@@ -54,8 +54,8 @@ int sync_and_check(Device& d, const char* what) {
   rc = check_cuda(cudaMemcpy(&st, d.status, 4, cudaMemcpyDeviceToHost), "status read");
   if (rc) return rc;
   if (st) {
-    unsigned zero = 0;
-    cudaMemcpy(d.status, &zero, 4, cudaMemcpyHostToDevice);
+    cudaMemsetAsync(d.status, 0, 4, d.stream);
+    cudaStreamSynchronize(d.stream);
     return set_error(EC_ETIMEOUT, "%s: kernel wait timed out (device status %u)", what, st);
   }
   return EC_OK;
@@ -360,16 +360,22 @@ int ec_upload_tensor(const char* name, int dtype, const int64_t* shape, int ndim
     const size_t dev_bytes = numel * (t.dtype == kDtBf16 ? 2 : 4);
     rc = dev_alloc(*d, &t.p, dev_bytes, name);
     if (rc) return rc;
+    // Copies are issued on the library's (non-blocking) stream and waited
+    // for there: a plain cudaMemcpy from pageable memory may return before
+    // its DMA lands, and the legacy stream it runs on does not order work
+    // on a non-blocking stream.
     if (dtype == EC_F16) {
       // upload raw binary16, widen on the device (st.lisp:74-85)
       void* raw = nullptr;
       rc = dev_alloc(*d, &raw, nbytes, "f16 staging");
-      if (!rc) rc = check_cuda(cudaMemcpy(raw, data, nbytes, cudaMemcpyHostToDevice), "upload");
+      if (!rc)
+        rc = check_cuda(cudaMemcpyAsync(raw, data, nbytes, cudaMemcpyHostToDevice, d->stream), "upload");
       if (!rc) rc = check_cuda(launch_convert(kConvF16ToF32, raw, t.p, numel, d->stream), "f16 widen");
       if (!rc) rc = check_cuda(cudaStreamSynchronize(d->stream), "f16 widen");
-      dev_free(*d, raw, nbytes);
+      if (raw) dev_free(*d, raw, nbytes);
     } else {
-      rc = check_cuda(cudaMemcpy(t.p, data, nbytes, cudaMemcpyHostToDevice), "upload");
+      rc = check_cuda(cudaMemcpyAsync(t.p, data, nbytes, cudaMemcpyHostToDevice, d->stream), "upload");
+      if (!rc) rc = check_cuda(cudaStreamSynchronize(d->stream), "upload");
     }
     if (rc) {
       dev_free(*d, t.p, dev_bytes);

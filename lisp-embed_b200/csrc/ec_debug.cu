@@ -169,13 +169,14 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   void* dblk = nullptr;
   rc = dev_alloc(d, &dblk, tbytes, "blocks");
   if (rc) return rc;
-  rc = check_cuda(cudaMemcpy(dblk, blk.data(), n64 * 8, cudaMemcpyHostToDevice), "blocks");
+  rc = check_cuda(cudaMemcpyAsync(dblk, blk.data(), n64 * 8, cudaMemcpyHostToDevice, d.stream), "blocks");
   if (!rc)
-    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64, blk128.data(), b128, cudaMemcpyHostToDevice),
+    rc = check_cuda(cudaMemcpyAsync(static_cast<char*>(dblk) + b64, blk128.data(), b128,
+                                    cudaMemcpyHostToDevice, d.stream),
                     "blocks");
   if (!rc)
-    rc = check_cuda(cudaMemcpy(static_cast<char*>(dblk) + b64 + b128, seqs.data(), seqs.size() * 8,
-                               cudaMemcpyHostToDevice),
+    rc = check_cuda(cudaMemcpyAsync(static_cast<char*>(dblk) + b64 + b128, seqs.data(), seqs.size() * 8,
+                                    cudaMemcpyHostToDevice, d.stream),
                     "sequences");
   AttnLaunch a;
   a.qkv = static_cast<const bf16*>(qkv);

@@ -716,12 +716,18 @@ int ec_index_load(const float* x, int64_t n, int d, const float* centroids, int 
       EC_TRY(take(reinterpret_cast<void**>(&ix.cent), static_cast<size_t>(k) * d * 4, "centroids"));
       EC_TRY(take(reinterpret_cast<void**>(&ix.lists), static_cast<size_t>(n) * 4, "lists"));
       EC_TRY(take(reinterpret_cast<void**>(&ix.offs), static_cast<size_t>(k + 1) * 8, "offsets"));
-      EC_TRY(check_cuda(cudaMemcpy(ix.cent, centroids, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice),
+      // on the device's stream (searches run there), waited for before the
+      // host offsets go away
+      EC_TRY(check_cuda(cudaMemcpyAsync(ix.cent, centroids, static_cast<size_t>(k) * d * 4,
+                                        cudaMemcpyHostToDevice, dv->stream),
                         "centroids upload"));
-      EC_TRY(check_cuda(cudaMemcpy(ix.lists, lists, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice),
+      EC_TRY(check_cuda(cudaMemcpyAsync(ix.lists, lists, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice,
+                                        dv->stream),
                         "lists upload"));
-      EC_TRY(check_cuda(cudaMemcpy(ix.offs, offs.data(), static_cast<size_t>(k + 1) * 8, cudaMemcpyHostToDevice),
+      EC_TRY(check_cuda(cudaMemcpyAsync(ix.offs, offs.data(), static_cast<size_t>(k + 1) * 8,
+                                        cudaMemcpyHostToDevice, dv->stream),
                         "offsets upload"));
+      EC_TRY(check_cuda(cudaStreamSynchronize(dv->stream), "index upload"));
     }
     ix.n = n;
     ix.d = d;

@@ -316,8 +316,12 @@ static int load_llama(Device& d, const JVal& cfg) {
   if ((rc = model_alloc(d, &dc, cs.size() * 4, "rope cos")) ||
       (rc = model_alloc(d, &ds, sn.size() * 4, "rope sin")))
     return rc;
-  if ((rc = check_cuda(cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope")) ||
-      (rc = check_cuda(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope")))
+  // on the library's stream, waited for before the host tables go away
+  if ((rc = check_cuda(cudaMemcpyAsync(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, d.stream),
+                       "rope")) ||
+      (rc = check_cuda(cudaMemcpyAsync(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, d.stream),
+                       "rope")) ||
+      (rc = check_cuda(cudaStreamSynchronize(d.stream), "rope")))
     return rc;
   m.cos_t = static_cast<float*>(dc);
   m.sin_t = static_cast<float*>(ds);
@@ -376,8 +380,12 @@ static int rope_table(Device& d, double theta, int hd, int max_pos, float** cos_
   if ((rc = model_alloc(d, &dc, cs.size() * 4, "rope cos")) ||
       (rc = model_alloc(d, &ds, sn.size() * 4, "rope sin")))
     return rc;
-  if ((rc = check_cuda(cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope")) ||
-      (rc = check_cuda(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope")))
+  // on the library's stream, waited for before the host tables go away
+  if ((rc = check_cuda(cudaMemcpyAsync(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, d.stream),
+                       "rope")) ||
+      (rc = check_cuda(cudaMemcpyAsync(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, d.stream),
+                       "rope")) ||
+      (rc = check_cuda(cudaStreamSynchronize(d.stream), "rope")))
     return rc;
   *cos_t = static_cast<float*>(dc);
   *sin_t = static_cast<float*>(ds);
