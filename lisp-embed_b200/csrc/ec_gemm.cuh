@@ -89,6 +89,7 @@ struct GemmArgs {
   int n_tiles_n;       // N / BN
   int num_tiles;       // ceil(M / 128) * n_tiles_n
   unsigned* status;    // device status word
+  int gelu_as;         // kEpiBf16Gelu: 1 = Abramowitz-Stegun erf, 0 = FMA-only erf
   QkRopeEpi qk;        // kEpiBf16QkRope only
   ArgCandEpi ac;       // kEpiArgCand only
 };
@@ -172,6 +173,39 @@ __device__ __forceinline__ float2 gelu_as2(float2 x) {
   const float2 se = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
   const float2 hx = __fmul2_rn(x, f2(0.5f));
   return __ffma2_rn(hx, se, hx);
+}
+
+// GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from FMAs alone, so the epilogue
+// leaves the MUFU pipe free (gelu_as2 needs an approximate reciprocal and an
+// exp2 per element).  erf(z) ~ z P(z^2) for |z| <= 3 and erf(+-3) beyond,
+// P of degree 9 in u = z^2: coefficients from a weighted least-squares fit on
+// 6000 Chebyshev nodes of [0, 3] (Lawson reweighting toward the minimax
+// error), computed for this kernel.  |erf error| <= 1.5e-5 for |z| <= 3 and
+// <= 2.3e-5 beyond (erf(3) = 1 - 2.2e-5), evaluated in fp32 -- against the
+// 1.5e-7 of bert::erf-approx's Abramowitz-Stegun 7.1.26 a GELU difference of
+// at most 1.2e-5 |x|, far below the bf16 rounding the result then gets.
+__device__ __forceinline__ float2 gelu_poly2(float2 x) {
+  const float2 z = __fmul2_rn(x, f2(0.70710678118654752f));
+  const float2 zc = make_float2(fminf(fmaxf(z.x, -3.0f), 3.0f), fminf(fmaxf(z.y, -3.0f), 3.0f));
+  const float2 u = __fmul2_rn(zc, zc);
+  float2 p = __ffma2_rn(u, f2(-3.753065414e-09f), f2(1.995653207e-07f));
+  p = __ffma2_rn(u, p, f2(-4.770880878e-06f));
+  p = __ffma2_rn(u, p, f2(6.851473881e-05f));
+  p = __ffma2_rn(u, p, f2(-6.692105089e-04f));
+  p = __ffma2_rn(u, p, f2(4.784782883e-03f));
+  p = __ffma2_rn(u, p, f2(-2.621991932e-02f));
+  p = __ffma2_rn(u, p, f2(1.123043746e-01f));
+  p = __ffma2_rn(u, p, f2(-3.759220243e-01f));
+  p = __ffma2_rn(u, p, f2(1.128355980e+00f));
+  const float2 e = __fmul2_rn(zc, p);
+  const float2 hx = __fmul2_rn(x, f2(0.5f));
+  return __ffma2_rn(hx, e, hx);
+}
+
+// GELU of the bf16-output epilogue: the FMA-only erf unless EC_GELU_AS
+// selects the Abramowitz-Stegun form (kept for comparison)
+__device__ __forceinline__ float2 gelu_epi2(float2 x, bool as) {
+  return as ? gelu_as2(x) : gelu_poly2(x);
 }
 
 // gelu_pytorch_tanh (gemma::gelu-tanh, gemma.lisp:85-89) in single precision
@@ -610,7 +644,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 x[e] = __fadd2_rn(make_float2(__uint_as_float(r[h][8 * j + 2 * e]),
                                               __uint_as_float(r[h][8 * j + 2 * e + 1])),
                                   (e & 1) ? make_float2(b.z, b.w) : make_float2(b.x, b.y));
-                if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_as2(x[e]);
+                if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_epi2(x[e], args.gelu_as != 0);
               }
               *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
                   make_uint4(pack_bf16(x[0].x, x[0].y), pack_bf16(x[1].x, x[1].y),
@@ -736,7 +770,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
               float2 xx = make_float2(v[8 * j + e], v[8 * j + e + 1]);
-              if constexpr (EPI == kEpiBf16Gelu) xx = gelu_as2(xx);
+              if constexpr (EPI == kEpiBf16Gelu) xx = gelu_epi2(xx, args.gelu_as != 0);
               x[e] = xx.x;
               x[e + 1] = xx.y;
             }
