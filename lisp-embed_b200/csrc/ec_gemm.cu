@@ -61,9 +61,10 @@ static bool encode_2d_out(CUtensorMap* map, void* ptr, bool f32, uint64_t rows, 
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI, int CG = 1>
+template <int BN, int EPI, int CG = 1, bool WR = false>
 static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
-  using Cfg = GemmCfg<BN, EPI, CG>;
+  using Cfg = GemmCfg<BN, EPI, CG, WR>;
+  if (WR && g.K > kGemmWrMaxK) return cudaErrorInvalidValue;
   // the shared-memory opt-in is a per-device function attribute; pairs also
   // need the number of clusters that fit at once
   static std::mutex attr_mu;
@@ -85,14 +86,14 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
     std::lock_guard<std::mutex> lk(attr_mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!max_clusters[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI, CG>,
+      cudaError_t e = cudaFuncSetAttribute(gemm_tn_bf16_kernel<BN, EPI, CG, WR>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(Cfg::SMEM_BYTES));
       if (e != cudaSuccess) return e;
       int n = num_sms;
       if constexpr (CG == 2) {
         cfg.gridDim = dim3((num_sms / 2) * 2, 1, 1);
-        e = cudaOccupancyMaxActiveClusters(&n, gemm_tn_bf16_kernel<BN, EPI, CG>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_tn_bf16_kernel<BN, EPI, CG, WR>, &cfg);
         if (e != cudaSuccess) return e;
         if (n <= 0) return cudaErrorInvalidConfiguration;
       }
@@ -134,14 +135,27 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
     if (!g.qk) return cudaErrorInvalidValue;
     a.qk = *g.qk;
   }
+  if constexpr (WR) {
+    // every unit (CTA, or pair) keeps one W tile resident: all units run,
+    // in groups of n_tiles_n that share row blocks
+    const int units = CG == 2 ? max_clusters[dev] : num_sms;
+    if (units < a.n_tiles_n) return cudaErrorInvalidConfiguration;
+    if constexpr (CG == 1) {
+      gemm_tn_bf16_kernel<BN, EPI, CG, WR><<<units, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
+      return cudaGetLastError();
+    } else {
+      cfg.gridDim = dim3(units * 2, 1, 1);
+      return cudaLaunchKernelEx(&cfg, gemm_tn_bf16_kernel<BN, EPI, CG, WR>, ta, tb, tc, a);
+    }
+  }
   if constexpr (CG == 1) {
     const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
-    gemm_tn_bf16_kernel<BN, EPI, CG><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
+    gemm_tn_bf16_kernel<BN, EPI, CG, WR><<<grid, kGemmThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, a);
     return cudaGetLastError();
   } else {
     const int clusters = a.num_tiles < max_clusters[dev] ? a.num_tiles : max_clusters[dev];
     cfg.gridDim = dim3(clusters * 2, 1, 1);
-    return cudaLaunchKernelEx(&cfg, gemm_tn_bf16_kernel<BN, EPI, CG>, ta, tb, tc, a);
+    return cudaLaunchKernelEx(&cfg, gemm_tn_bf16_kernel<BN, EPI, CG, WR>, ta, tb, tc, a);
   }
 }
 
@@ -202,6 +216,21 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   // mainloop dominates: K >= 768 and epilogues lighter than GELU (measured:
   // 8-12% faster there, neutral or slower at K = 384 or with GELU).
   // EC_GEMM_PAIR forces pairs for every eligible shape, EC_NO_GEMM_PAIR none.
+  // K <= 384 with the plain / GELU epilogues (QKV, FFN-up of the small
+  // encoders): weight-resident CTA pairs (each pair keeps one W tile in
+  // shared memory and streams only A); EC_NO_GEMM_WR turns this off
+  if (!g.bn && g.K <= kGemmWrMaxK && (g.epi == kEpiBf16 || g.epi == kEpiBf16Gelu) &&
+      getenv("EC_NO_GEMM_WR") == nullptr) {
+    cudaError_t e = cudaErrorInvalidConfiguration;
+    if (g.N % 256 == 0)
+      e = g.epi == kEpiBf16 ? run<256, kEpiBf16, 2, true>(g, st, num_sms)
+                            : run<256, kEpiBf16Gelu, 2, true>(g, st, num_sms);
+    else if (g.N % 192 == 0)
+      e = g.epi == kEpiBf16 ? run<192, kEpiBf16, 2, true>(g, st, num_sms)
+                            : run<192, kEpiBf16Gelu, 2, true>(g, st, num_sms);
+    if (e != cudaErrorInvalidConfiguration) return e;
+    cudaGetLastError();  // fewer units than W tiles: the streaming schedule below
+  }
   const bool force_pair = getenv("EC_GEMM_PAIR") != nullptr;
   if (!g.bn && g.N % 256 == 0 && getenv("EC_NO_GEMM_PAIR") == nullptr &&
       (force_pair || (g.K >= 768 && g.epi != kEpiBf16Gelu))) {

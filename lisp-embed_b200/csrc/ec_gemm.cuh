@@ -104,7 +104,12 @@ constexpr int gemm_threads(int ew) { return (2 + ew) * 32; }
 // CG: CTAs per MMA (1, or 2 = a cluster pair issuing cta_group::2 MMAs of
 // M = 256: each CTA loads only half of the W tile, so the operand traffic per
 // output drops by a third -- the mainloop is bound by L2 -> SM bandwidth).
-template <int BN, int EPI, int CG = 1>
+// WR: weight-resident mode for K <= kGemmWrMaxK -- each CTA keeps its rows
+// of one W tile (all K) in shared memory for the whole launch and streams A
+// only (see the tile schedule in gemm_tn_bf16_kernel).
+constexpr int kGemmWrMaxK = 384;
+
+template <int BN, int EPI, int CG = 1, bool WR = false>
 struct GemmCfg {
   static constexpr bool OUT_F32 = EPI == kEpiF32Resid || EPI == kEpiF32 || EPI == kEpiArgCand;
   // one 32 x 32 output chunk: fp32 rows of 128 B (128B swizzle) or bf16
@@ -115,13 +120,16 @@ struct GemmCfg {
   static constexpr uint32_t EPI_BYTES = EPI == kEpiArgCand ? 0 : kGemmEpiWarps * 2 * CHUNK_BYTES;
   static constexpr uint32_t A_BYTES = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t B_BYTES = (BN / CG) * kGemmBK * 2;  // this CTA's rows of W
-  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int MAX_STAGES = (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES)) /
+  // WR: the resident W rows (kGemmWrMaxK / kGemmBK k-blocks), stages of A only
+  static constexpr uint32_t W_BYTES = WR ? (kGemmWrMaxK / kGemmBK) * B_BYTES : 0;
+  static constexpr uint32_t STAGE_BYTES = WR ? A_BYTES : A_BYTES + B_BYTES;
+  static constexpr int MAX_STAGES = (232448 - 1024 - 512 - static_cast<int>(EPI_BYTES) -
+                                     static_cast<int>(W_BYTES)) /
                                     static_cast<int>(STAGE_BYTES);
   static constexpr int STAGES = MAX_STAGES > 6 ? 6 : MAX_STAGES;
   static constexpr uint32_t TMEM_COLS =
       2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
-  static constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 512;
+  static constexpr size_t SMEM_BYTES = 1024 + W_BYTES + STAGES * STAGE_BYTES + EPI_BYTES + 512;
   static_assert(STAGES >= 2, "shared memory budget");
 };
 
@@ -228,12 +236,12 @@ __device__ __forceinline__ uint32_t stage_off(int r, int c) {
   return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-template <int BN, int EPI, int CG = 1>
+template <int BN, int EPI, int CG = 1, bool WR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tn_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, EPI, CG>;
+  using Cfg = GemmCfg<BN, EPI, CG, WR>;
   constexpr int EW = kGemmEpiWarps;
   static_assert(CG == 1 || CG == 2, "CTA group");
   constexpr int STAGES = Cfg::STAGES;
@@ -247,13 +255,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* smA = smem;
+  // WR: smB is the resident W (k-block kb at kb * B_BYTES); else B stages
   uint8_t* smB = smem + STAGES * Cfg::A_BYTES;
-  uint8_t* smE = smB + STAGES * Cfg::B_BYTES;  // epilogue staging, 2 chunks per warp
+  uint8_t* smE = smB + (WR ? Cfg::W_BYTES : STAGES * Cfg::B_BYTES);  // epilogue staging, 2 chunks per warp
   uint64_t* full = reinterpret_cast<uint64_t*>(smE + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* w_full = tempty + 2;  // WR: the resident W has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -261,8 +271,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // pair: CTA `rank` owns rows rank * 128.. of each 256-row tile; the even
   // CTA issues the MMAs; both walk the same tiles
   const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
-  const int tile0 = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
-  const int tstep = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+  const int unit = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int units = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+  // Tile schedule.  Default: tiles unit, unit + units, ... of the row-block
+  // major order (tile = mb * n_tiles_n + nb).  WR: units form groups of
+  // n_tiles_n; unit u keeps W tile nb = u % n_tiles_n resident and takes the
+  // rows blocks of its group's contiguous share (the launcher guarantees
+  // units >= n_tiles_n), so the units of a group read the same A tiles at
+  // about the same time (L2 hits) and W crosses to the SM once.  For WR a
+  // "tile" below is the row block mb itself.
+  int tile0, tstep, tend, wr_nb = 0;
+  if constexpr (WR) {
+    const int groups = units / args.n_tiles_n;
+    const int g = unit / args.n_tiles_n;
+    const int m_tiles = args.num_tiles / args.n_tiles_n;
+    const int per = (m_tiles + groups - 1) / groups;
+    wr_nb = unit % args.n_tiles_n;
+    tile0 = g < groups ? g * per : m_tiles;
+    tend = g < groups ? min(m_tiles, tile0 + per) : m_tiles;
+    tstep = 1;
+  } else {
+    tile0 = unit;
+    tstep = units;
+    tend = args.num_tiles;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -273,6 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EW * CG);  // the even CTA's counts both epilogues
     }
+    mbar_init(w_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -308,8 +341,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = tile0; ok && tile < args.num_tiles; tile += tstep) {
-        const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+      if constexpr (WR) {
+        // the resident W rows of this unit's tile, once for the launch
+        if (tile0 < tend) {
+          if constexpr (CG == 2) {
+            if (rank == 0) mbar_arrive_expect_tx(w_full, 2 * k_blocks * Cfg::B_BYTES);
+            const uint32_t fb = cluster_map(smem_u32(w_full), 0);
+            for (int kb = 0; kb < k_blocks; ++kb)
+              tma_load_2d_pair(smB + kb * Cfg::B_BYTES, &tmB, fb, kb * kGemmBK,
+                               wr_nb * BN + static_cast<int>(rank) * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(w_full, k_blocks * Cfg::B_BYTES);
+            for (int kb = 0; kb < k_blocks; ++kb)
+              tma_load_2d_hint(smB + kb * Cfg::B_BYTES, &tmB, w_full, kb * kGemmBK, wr_nb * BN, pol_w);
+          }
+        }
+      }
+      for (int tile = tile0; ok && tile < tend; tile += tstep) {
+        const int mb = WR ? tile : tile / args.n_tiles_n, nb = WR ? wr_nb : tile % args.n_tiles_n;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             report(args.status, kDevTimeoutProducer);
@@ -323,14 +372,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t fb = cluster_map(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(smA + stage * Cfg::A_BYTES, &tmA, fb, kb * kGemmBK,
                              mb * TM + static_cast<int>(rank) * kGemmBM);
-            tma_load_2d_pair(smB + stage * Cfg::B_BYTES, &tmB, fb, kb * kGemmBK,
-                             nb * BN + static_cast<int>(rank) * (BN / 2));
+            if constexpr (!WR)
+              tma_load_2d_pair(smB + stage * Cfg::B_BYTES, &tmB, fb, kb * kGemmBK,
+                               nb * BN + static_cast<int>(rank) * (BN / 2));
           } else {
             mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
             tma_load_2d(smA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * kGemmBK,
                         mb * kGemmBM);
-            tma_load_2d_hint(smB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * kGemmBK,
-                             nb * BN, pol_w);
+            if constexpr (!WR)
+              tma_load_2d_hint(smB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * kGemmBK,
+                               nb * BN, pol_w);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -346,7 +397,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = tile0; ok && tile < args.num_tiles; tile += tstep) {
+      if constexpr (WR) {
+        if (tile0 < tend && !mbar_wait(w_full, 0, abort_flag)) {
+          report(args.status, kDevTimeoutMma);
+          *abort_flag = 1;
+          ok = false;
+        }
+      }
+      for (int tile = tile0; ok && tile < tend; tile += tstep) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
           report(args.status, kDevTimeoutMma);
           *abort_flag = 1;
@@ -363,7 +421,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smA + stage * Cfg::A_BYTES);
-          const uint32_t b_addr = smem_u32(smB + stage * Cfg::B_BYTES);
+          const uint32_t b_addr = smem_u32(smB + (WR ? kb : stage) * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
             if constexpr (CG == 2)
@@ -404,8 +462,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // the three largest approximate scores of this thread's row over its
       // chunks (one compare per score once the list has filled)
       const float wscale = args.ac.rel2 * *args.ac.cmax;
-      for (int tile = tile0; tile < args.num_tiles; tile += tstep) {
-        const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+      for (int tile = tile0; tile < tend; tile += tstep) {
+        const int mb = WR ? tile : tile / args.n_tiles_n, nb = WR ? wr_nb : tile % args.n_tiles_n;
         const int grow = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32 + lane;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                static_cast<uint32_t>(acc * BN);
@@ -475,8 +533,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // as the last TMEM read lands
     constexpr bool kPaired =
         EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiBf16QkRope;
-    for (int tile = tile0; kPaired && tile < args.num_tiles; tile += tstep) {
-      const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+    for (int tile = tile0; kPaired && tile < tend; tile += tstep) {
+      const int mb = WR ? tile : tile / args.n_tiles_n, nb = WR ? wr_nb : tile % args.n_tiles_n;
       const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
@@ -668,8 +726,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    for (int tile = tile0; !kPaired && EPI != kEpiArgCand && tile < args.num_tiles; tile += tstep) {
-      const int mb = tile / args.n_tiles_n, nb = tile % args.n_tiles_n;
+    for (int tile = tile0; !kPaired && EPI != kEpiArgCand && tile < tend; tile += tstep) {
+      const int mb = WR ? tile : tile / args.n_tiles_n, nb = WR ? wr_nb : tile % args.n_tiles_n;
       const int row0 = mb * TM + static_cast<int>(rank) * kGemmBM + quad * 32;  // first row of this warp's 32
 #pragma unroll 1
       for (int c = half; c < NCH; c += PARTS) {

@@ -137,6 +137,7 @@ def test_gemm_rms_epilogues(ec, M, N, K, mode, variant):
 @pytest.mark.parametrize("epi", [0, 1, 2, 4])
 def test_gemm_cta_pair(ec, monkeypatch, M, N, K, epi):
     monkeypatch.setenv("EC_GEMM_PAIR", "1")
+    monkeypatch.setenv("EC_NO_GEMM_WR", "1")  # the streaming pair schedule, not weight-resident
     g = torch.Generator(device="cuda").manual_seed(M * 3 + N + K + epi)
     A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
@@ -155,6 +156,32 @@ def test_gemm_cta_pair(ec, monkeypatch, M, N, K, epi):
         tol = 1e-4
     err = (out - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
     assert err < tol, f"rel err {err}"
+
+
+# weight-resident CTA pairs (K <= 384, plain and GELU epilogues): each pair
+# keeps one W tile in shared memory for the launch; units are grouped by W
+# tile and share row blocks.  Ragged M (including fewer row blocks than
+# groups), K of one k-block up to 384, W-tile counts from 1 to 16 (BN 192 and
+# 256), and the equivalence with the streaming schedule.
+@pytest.mark.parametrize("M,N,K", [(1, 384, 384), (255, 1152, 384), (257, 1536, 384),
+                                   (4097, 1152, 384), (3001, 256, 64), (1000, 4096, 128),
+                                   (20011, 1536, 384), (700, 2304, 192)])
+@pytest.mark.parametrize("epi", [0, 1])
+def test_gemm_weight_resident(ec, monkeypatch, M, N, K, epi):
+    g = torch.Generator(device="cuda").manual_seed(M * 5 + N + K + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    ref = A.float() @ W.float().t() + bias
+    if epi == 1:
+        ref = _gelu_as(ref)
+    out = _gemm(ec, A, W, bias, None, epi, 0, N, torch.bfloat16).float()
+    err = (out - ref).abs().max().item() / max(ref.abs().max().item(), 1e-6)
+    assert err < 1e-2, f"rel err {err}"
+    monkeypatch.setenv("EC_NO_GEMM_WR", "1")
+    out2 = _gemm(ec, A, W, bias, None, epi, 0, N, torch.bfloat16).float()
+    err2 = (out - out2).abs().max().item() / max(ref.abs().max().item(), 1e-6)
+    assert err2 < 1e-2, f"weight-resident vs streaming rel diff {err2}"
 
 
 @pytest.mark.parametrize("M,F", [(1, 3072), (300, 3072), (1029, 1536)])
