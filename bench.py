@@ -61,6 +61,7 @@ WORKLOADS = {
 }
 IVF_N, IVF_D, IVF_K, IVF_ITERS, IVF_SEED = 3_270_000, 384, 4096, 20, 4
 SEARCH_NQ, SEARCH_NPROBE, SEARCH_TOPK = 10_000, 32, 10
+IVF_ROWS = [IVF_N]  # rows of the IVF workload (--ivf-rows: a smaller build for profiling)
 PRECISION = ("bf16 tensor-core GEMM/attention, fp32 accumulate, fp32 norms; residual between "
              "sublayers: the LayerNorm's bf16 output (BERT/MPNet), fp32 (Qwen3, Gemma)")
 
@@ -83,6 +84,8 @@ def parse_args():
                    help="search workload: queries per call")
     p.add_argument("--headline-only", action="store_true",
                    help="default workload: the MiniLM headline alone")
+    p.add_argument("--ivf-rows", type=int, default=IVF_N,
+                   help="ivf workload: rows of the corpus (a smaller build for profiling)")
     return p.parse_args()
 
 
@@ -479,7 +482,7 @@ def ivf_corpus_host(R):
     """The IVF workload (generated on this rank's GPU with a fixed seed, the
     same on every rank) copied to host memory, and its training permutation."""
     import torch
-    x_dev, perm = ivf_corpus_torch(IVF_N, IVF_D, IVF_K, IVF_SEED, "cuda")
+    x_dev, perm = ivf_corpus_torch(IVF_ROWS[0], IVF_D, IVF_K, IVF_SEED, "cuda")
     x = x_dev.cpu().numpy()
     perm = perm.cpu().numpy().astype(np.int64)
     del x_dev
@@ -498,8 +501,9 @@ def ivf_build_measure(R, x, perm):
     import ctypes as C
     import torch
     from embedcuda import _lib, ann
-    per = (IVF_N + R.world - 1) // R.world
-    j0, j1 = per * R.rank, min(IVF_N, per * (R.rank + 1))
+    n = len(x)
+    per = (n + R.world - 1) // R.world
+    j0, j1 = per * R.rank, min(n, per * (R.rank + 1))
     mine = perm[j0:j1]
     x_local = np.ascontiguousarray(x[mine])  # this rank's training rows, in sample order
     init = np.ascontiguousarray(x[perm[:IVF_K]])
@@ -540,10 +544,10 @@ def ivf_build_measure(R, x, perm):
     peaks, src = measured_peaks()
     achieved = g_flops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None
     peak = peaks.get("bf16_tflops")
-    flops = 2.0 * IVF_N * IVF_K * IVF_D * (IVF_ITERS + 1)
+    flops = 2.0 * n * IVF_K * IVF_D * (IVF_ITERS + 1)
     out = {"value": t_all, "unit": "s", "higher_is_better": False, "scaling": "strong",
            "n_gpus": R.world, "dtype": "f32 (bf16 tensor-core scores, exact re-check)",
-           "config": {"workload": "ivf-3.27Mx384", "n": IVF_N, "dim": IVF_D, "k": IVF_K,
+           "config": {"workload": f"ivf-{n / 1e6:g}Mx{IVF_D}", "n": n, "dim": IVF_D, "k": IVF_K,
                       "iters": IVF_ITERS, "sample": "all rows, seeded permutation",
                       "parallelism": f"rows sharded over {R.world} GPU(s) in sample order",
                       "exchange": "per-cluster sums chained rank to rank (NCCL send/recv), "
@@ -586,13 +590,14 @@ def ivf_cpu_baseline(x, perm, seconds):
     t0 = time.perf_counter()
     oracle.kmeans_update(x, sl, a, init)
     el_u = time.perf_counter() - t0
-    t_assign = IVF_N * el_a / done_a
-    t_update = IVF_N * el_u / len(sl)
+    n = len(x)
+    t_assign = n * el_a / done_a
+    t_update = n * el_u / len(sl)
     total = (IVF_ITERS + 1) * t_assign + IVF_ITERS * t_update
     return {"value": total, "unit": "s", "cores": threads, "kind": "port",
             "sample": f"assignment of {done_a} rows on {threads} threads in {el_a:.1f} s and the "
                       f"serial update of {len(sl)} rows in {el_u:.2f} s, extrapolated to "
-                      f"{IVF_ITERS + 1} passes and {IVF_ITERS} updates of {IVF_N} rows"}
+                      f"{IVF_ITERS + 1} passes and {IVF_ITERS} updates of {n} rows"}
 
 
 def query_measure(R, x, cent, nq, warmup):
@@ -1055,6 +1060,7 @@ def main():
     args = parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    IVF_ROWS[0] = args.ivf_rows
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

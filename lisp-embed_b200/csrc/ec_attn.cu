@@ -1,6 +1,7 @@
 // ec_attn.cu -- instantiations and host launcher of the varlen attention.
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include <cudaTypedefs.h>
 
@@ -130,15 +131,34 @@ static cudaError_t run_mode(const AttnLaunch& l, cudaStream_t st) {
   return run_attn<HD, 0>(l, st);
 }
 
+void attn_short_buckets(const int* lens_sorted, int n_long, int nseq, AttnLaunch* a) {
+  static const int cap[4] = {kAttnShortCap, 192, 128, 64};
+  a->nbuckets = 0;
+  int prev = -1;
+  for (int k = n_long; k < nseq; ++k) {
+    int b = 0;
+    while (b < 3 && lens_sorted[k] <= cap[b + 1]) ++b;
+    if (b != prev) {
+      a->bucket_first[a->nbuckets] = k;
+      a->bucket_max[a->nbuckets] = lens_sorted[k];
+      ++a->nbuckets;
+      prev = b;
+    }
+  }
+  a->bucket_first[a->nbuckets] = nseq;
+}
+
 // sequences [n_long, nseq) of the launch, one CTA per (sequence, head);
-// F16P: the kernel with fp16 probabilities (attn_short_h_kernel)
-template <int HD, int MODE, int BK, int MINB, bool F16P>
-static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
+// F16P: the kernel with fp16 probabilities (attn_short_h_kernel, key blocks
+// of BK, PV2 accumulator sets); bucketed: one launch per length bucket, each
+// sized for its longest sequence (less shared memory per CTA)
+template <int HD, int MODE, int BK, int MINB, bool F16P, bool PV2 = false>
+static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st, bool bucketed = false) {
   using S = ShortAttnSmem<HD, MODE>;
   static_assert(kShortAttnMaxLen == kAttnShortCap, "short-kernel capacity");
   static std::mutex mu;
   static bool set[64] = {};
-  const void* fn = F16P ? reinterpret_cast<const void*>(attn_short_h_kernel<HD, MODE, MINB>)
+  const void* fn = F16P ? reinterpret_cast<const void*>(attn_short_h_kernel<HD, MODE, MINB, BK, PV2>)
                         : reinterpret_cast<const void*>(attn_short_kernel<HD, MODE, BK, MINB>);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -168,13 +188,40 @@ static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st) {
   a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(static_cast<float>(HD)));
   a.relbias = l.relbias;
   a.rel_max = l.rel_max;
-  a.kcap = (l.max_short_len + 15) & ~15;
-  dim3 grid(l.nseq - l.n_long, l.heads);
-  if (F16P)
-    attn_short_h_kernel<HD, MODE, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
-  else
-    attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
-  return cudaGetLastError();
+  const int nb = bucketed && l.nbuckets > 0 ? l.nbuckets : 1;
+  for (int b = 0; b < nb; ++b) {
+    const int first = nb > 1 ? l.bucket_first[b] : l.n_long;
+    const int last = nb > 1 ? l.bucket_first[b + 1] : l.nseq;
+    const int maxlen = nb > 1 ? l.bucket_max[b] : l.max_short_len;
+    if (last <= first) continue;
+    a.first = first;
+    a.kcap = (maxlen + 15) & ~15;
+    dim3 grid(last - first, l.heads);
+    if (F16P)
+      attn_short_h_kernel<HD, MODE, MINB, BK, PV2><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
+    else
+      attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+template <int HD, int MODE>
+static cudaError_t run_short_h(const AttnLaunch& l, cudaStream_t st) {
+  // EC_SHORT_ATTN_CFG=<key block>,<two accumulator sets>,<CTAs per SM>[,b]
+  // picks a measured variant of the fp16-probability kernel for head dim
+  // 32 (default 64,0,5); a trailing ",b" launches per length bucket
+  constexpr int MINB = HD == 32 ? 5 : 1;
+  const char* cfg = getenv("EC_SHORT_ATTN_CFG");
+  const std::string c = cfg ? cfg : "";
+  const bool bk = c.find(",b") != std::string::npos;
+  if constexpr (HD == 32) {
+    if (c.rfind("32,0,6", 0) == 0) return run_short<HD, MODE, 32, 6, true, false>(l, st, bk);
+    if (c.rfind("64,1,4", 0) == 0) return run_short<HD, MODE, 64, 4, true, true>(l, st, bk);
+    if (c.rfind("32,1,5", 0) == 0) return run_short<HD, MODE, 32, 5, true, true>(l, st, bk);
+  }
+  return run_short<HD, MODE, 64, MINB, true, false>(l, st, bk);
 }
 
 template <int HD>
@@ -190,9 +237,9 @@ static cudaError_t run_short_mode(const AttnLaunch& l, cudaStream_t st) {
     if (l.relbias) return run_short<HD, 1, 64, MINB, false>(l, st);
     return run_short<HD, 0, 64, MINB, false>(l, st);
   }
-  if (l.causal) return run_short<HD, 2, 64, MINB, true>(l, st);
-  if (l.relbias) return run_short<HD, 1, 64, MINB, true>(l, st);
-  return run_short<HD, 0, 64, MINB, true>(l, st);
+  if (l.causal) return run_short_h<HD, 2>(l, st);
+  if (l.relbias) return run_short_h<HD, 1>(l, st);
+  return run_short_h<HD, 0>(l, st);
 }
 
 // Sequences longer than kAttnShortCap go to the tcgen05 kernel (their

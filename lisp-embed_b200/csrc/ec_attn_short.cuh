@@ -279,11 +279,15 @@ __device__ __forceinline__ uint32_t bf2_to_h2(uint32_t v) {
   return cvt_h2(lo, hi);
 }
 
-template <int HD, int MODE, int MINB>
+// BK: keys per online-softmax block (32 or 64); PV2: two independent P.V
+// accumulator sets (even / odd 16-key steps), summed at the end, so that
+// consecutive MMAs of the accumulation do not wait on each other
+template <int HD, int MODE, int MINB, int BK = 64, bool PV2 = false>
 __global__ void __launch_bounds__(kShortAttnThreads, MINB)
     attn_short_h_kernel(const ShortAttnArgs a) {
-  constexpr int BK = 64;
+  static_assert(BK == 32 || BK == 64, "key block");
   constexpr int NT = BK / 8;
+  constexpr int NS = PV2 ? 2 : 1;
   constexpr bool kBias = MODE == 1;
   constexpr bool kCausal = MODE == 2;
   constexpr int LDS = ShortAttnSmem<HD, MODE>::LDS;
@@ -361,9 +365,13 @@ __global__ void __launch_bounds__(kShortAttnThreads, MINB)
     if (tile + NW < ntiles) load_q(tile + NW, qn);
     const int q0 = tile * 16;
     const int row_a = q0 + (lane >> 2), row_b = row_a + 8;
-    float o[NT_D][4], osum[4] = {0.f, 0.f, 0.f, 0.f};
+    float o[NS][NT_D][4], osum[NS][4];
 #pragma unroll
-    for (int n = 0; n < NT_D; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int v = 0; v < NS; ++v) {
+      osum[v][0] = osum[v][1] = osum[v][2] = osum[v][3] = 0.f;
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) o[v][n][0] = o[v][n][1] = o[v][n][2] = o[v][n][3] = 0.f;
+    }
     float m_r[2] = {-INFINITY, -INFINITY};
     const int kv_end = kCausal ? min(L, q0 + 16) : L;
     for (int k0 = 0; k0 < kv_end; k0 += BK) {
@@ -409,12 +417,21 @@ __global__ void __launch_bounds__(kShortAttnThreads, MINB)
             if (key >= L || (kCausal && key > qr)) s[n][e] = -INFINITY;
           }
       }
-      float mx[2] = {-INFINITY, -INFINITY};
+      // row maxima by a pairwise tree (depth log2 NT + 1, not a chain of NT)
+      float mt[2][NT];
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
-        mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
+        mt[0][n] = fmaxf(s[n][0], s[n][1]);
+        mt[1][n] = fmaxf(s[n][2], s[n][3]);
       }
+#pragma unroll
+      for (int w = NT / 2; w >= 1; w /= 2)
+#pragma unroll
+        for (int n = 0; n < w; ++n) {
+          mt[0][n] = fmaxf(mt[0][n], mt[0][n + w]);
+          mt[1][n] = fmaxf(mt[1][n], mt[1][n + w]);
+        }
+      float mx[2] = {mt[0][0], mt[1][0]};
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
@@ -443,28 +460,30 @@ __global__ void __launch_bounds__(kShortAttnThreads, MINB)
       }
       const float2 c0 = make_float2(corr[0], corr[0]), c1 = make_float2(corr[1], corr[1]);
 #pragma unroll
-      for (int n = 0; n < NT_D; ++n) {
-        const float2 u = __fmul2_rn(make_float2(o[n][0], o[n][1]), c0);
-        const float2 w = __fmul2_rn(make_float2(o[n][2], o[n][3]), c1);
-        o[n][0] = u.x;
-        o[n][1] = u.y;
-        o[n][2] = w.x;
-        o[n][3] = w.y;
-      }
-      {
-        const float2 u = __fmul2_rn(make_float2(osum[0], osum[1]), c0);
-        const float2 w = __fmul2_rn(make_float2(osum[2], osum[3]), c1);
-        osum[0] = u.x;
-        osum[1] = u.y;
-        osum[2] = w.x;
-        osum[3] = w.y;
+      for (int v = 0; v < NS; ++v) {
+#pragma unroll
+        for (int n = 0; n < NT_D; ++n) {
+          const float2 u = __fmul2_rn(make_float2(o[v][n][0], o[v][n][1]), c0);
+          const float2 w = __fmul2_rn(make_float2(o[v][n][2], o[v][n][3]), c1);
+          o[v][n][0] = u.x;
+          o[v][n][1] = u.y;
+          o[v][n][2] = w.x;
+          o[v][n][3] = w.y;
+        }
+        const float2 u = __fmul2_rn(make_float2(osum[v][0], osum[v][1]), c0);
+        const float2 w = __fmul2_rn(make_float2(osum[v][2], osum[v][3]), c1);
+        osum[v][0] = u.x;
+        osum[v][1] = u.y;
+        osum[v][2] = w.x;
+        osum[v][3] = w.y;
       }
       // O += P V and the row sums += P . 1 over the live 16-key steps
 #pragma unroll
       for (int t = 0; t < NT / 2; ++t) {
         if (2 * t < nt_live) {
+          const int v = PV2 ? (t & 1) : 0;
           const uint32_t pa[4] = {ph[2 * t][0], ph[2 * t][1], ph[2 * t + 1][0], ph[2 * t + 1][1]};
-          mma_f16_16816(osum, pa, kOnes, kOnes);
+          mma_f16_16816(osum[v], pa, kOnes, kOnes);
 #pragma unroll
           for (int n = 0; n < NT_D; n += 2) {
             uint32_t b[4];
@@ -472,24 +491,32 @@ __global__ void __launch_bounds__(kShortAttnThreads, MINB)
             const int key = k0 + t * 16 + (mi & 1) * 8 + (lane & 7);
             const int d = (n + (mi >> 1)) * 8;
             ldsm_x4_t(b, sV + key * LDS + d);
-            mma_f16_16816(o[n], pa, b[0], b[1]);
-            mma_f16_16816(o[n + 1], pa, b[2], b[3]);
+            mma_f16_16816(o[v][n], pa, b[0], b[1]);
+            mma_f16_16816(o[v][n + 1], pa, b[2], b[3]);
           }
         }
       }
     }
-    const float inv0 = osum[0] > 0.f ? 1.f / osum[0] : 0.f;
-    const float inv1 = osum[2] > 0.f ? 1.f / osum[2] : 0.f;
+    if constexpr (PV2) {
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[0][n][e] += o[1][n][e];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) osum[0][e] += osum[1][e];
+    }
+    const float inv0 = osum[0][0] > 0.f ? 1.f / osum[0][0] : 0.f;
+    const float inv1 = osum[0][2] > 0.f ? 1.f / osum[0][2] : 0.f;
     __nv_bfloat16* out_h = a.out + h * HD;
 #pragma unroll
     for (int n = 0; n < NT_D; ++n) {
       const int d = n * 8 + (lane & 3) * 2;
       if (row_a < L)
         *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_a) * a.ldo + d) =
-            pack2_bf16(o[n][0] * inv0, o[n][1] * inv0);
+            pack2_bf16(o[0][n][0] * inv0, o[0][n][1] * inv0);
       if (row_b < L)
         *reinterpret_cast<uint32_t*>(out_h + static_cast<size_t>(base + row_b) * a.ldo + d) =
-            pack2_bf16(o[n][2] * inv1, o[n][3] * inv1);
+            pack2_bf16(o[0][n][2] * inv1, o[0][n][3] * inv1);
     }
   }
 }

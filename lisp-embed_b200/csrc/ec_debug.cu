@@ -199,6 +199,11 @@ int ecdbg_attention(const void* qkv, int ld, int q_off, int k_off, int v_off, vo
   a.n_long = n_long;
   a.nblocks128_long = nblk128_long;
   a.max_short_len = max_short;
+  {
+    std::vector<int> sl;
+    for (int s : order) sl.push_back(lens_host[s]);
+    attn_short_buckets(sl.data(), n_long, nseq, &a);
+  }
   a.heads = heads;
   a.kv_group = heads / kv_heads;
   a.head_dim = head_dim;

@@ -254,10 +254,19 @@ struct AttnLaunch {
   int n_long;
   int nblocks128_long;
   int max_short_len;     // longest sequence in [n_long, nseq)
+  // [n_long, nseq) cut where the length falls to 192 / 128 / 64 or below:
+  // bucket b is [bucket_first[b], bucket_first[b + 1]) with its longest
+  // sequence bucket_max[b] (nbuckets 0: one launch over the whole range)
+  int nbuckets = 0;
+  int bucket_first[5] = {0, 0, 0, 0, 0};
+  int bucket_max[4] = {0, 0, 0, 0};
   float scale = 0.f;     // logit scale; 0 = 1 / sqrt(head_dim) (Gemma uses 1.0)
 };
 // key capacity of the short-sequence attention kernel (ec_attn_short.cuh)
 constexpr int kAttnShortCap = 256;
+// fill AttnLaunch's length buckets from the sequence lengths in launch
+// order (descending), sequences [n_long, nseq)
+void attn_short_buckets(const int* lens_sorted, int n_long, int nseq, AttnLaunch* a);
 // tcgen05 kernel (ec_fa.cuh) for head_dim 32 / 64 / 128; the mma.sync kernel
 // (ec_attn.cuh) when EC_LEGACY_ATTN is set
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t st);

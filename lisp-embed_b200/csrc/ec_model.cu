@@ -637,6 +637,7 @@ struct AttnTables {
   int n_long = 0;                // sequences longer than kAttnShortCap (first in order)
   int nblk128_long = 0;          // their 128-row blocks (a prefix of blocks128)
   int max_short = 0;             // longest sequence of the rest
+  std::vector<int> sorted_lens;  // lengths in launch order (descending)
 };
 
 static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const AttnTables& tb,
@@ -768,6 +769,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   at.n_long = tb.n_long;
   at.nblocks128_long = tb.nblk128_long;
   at.max_short_len = tb.max_short;
+  if (!tb.sorted_lens.empty()) attn_short_buckets(tb.sorted_lens.data(), tb.n_long, nseq, &at);
   at.rows = T;
   at.status = d.status;
   at.num_sms = d.num_sms;
@@ -1069,6 +1071,8 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
   }
   int2* hseq = reinterpret_cast<int2*>(reinterpret_cast<char*>(hblk128) + al256(static_cast<size_t>(nb128) * 16));
   for (int k = 0; k < nseq; ++k) hseq[k] = make_int2(hcu[order[k]], lens[order[k]]);
+  tb->sorted_lens.resize(nseq);
+  for (int k = 0; k < nseq; ++k) tb->sorted_lens[k] = lens[order[k]];
   char* ws = static_cast<char*>(d.ws);
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.seqs, hseq, static_cast<size_t>(nseq) * 8,
                                     cudaMemcpyHostToDevice, d.stream),

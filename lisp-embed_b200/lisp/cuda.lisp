@@ -14,6 +14,7 @@
 ;;;;   (cuda:index-load-files "index.bin" :ann-path "ann.bin" :dim 384)
 ;;;;   (cuda:ann-build-file "index.bin" "ann.bin" sample k iters)  ; ann:run
 ;;;;   (cuda:top-k q k)                   ; kb::top-k
+;;;;   (cuda:kb-search "query" 8)         ; kb:kb-search, index resident on the GPU
 ;;;;
 ;;;; Every foreign call returns an int status; a negative status becomes a
 ;;;; Lisp ERROR carrying ec_last_error(), as st.lisp / model.lisp signal
@@ -25,7 +26,8 @@
   (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
            #:load-tokenizer #:embed-texts
            #:kmeans #:assign-all #:index-load #:index-load-files #:ann-build-file
-           #:top-k #:top-k-brute #:top-k-batch #:*nprobe*))
+           #:top-k #:top-k-brute #:top-k-batch #:*nprobe*
+           #:attach-kb #:kb-search))
 (in-package :cuda)
 
 (defparameter *library* (or (sb-ext:posix-getenv "EC_LIBRARY") "libembedcuda.so"))
@@ -237,12 +239,14 @@ centroids."
              "ec_ann_build_file"))))
 
 (defvar *tokenizer* 0)
+(defvar *have-tokenizer* nil)
 
 (defun load-tokenizer (path)
   "make-tokenizer-from-json in the library; later EMBED-TEXTS calls use it."
   (let ((h (make-array 1 :element-type '(signed-byte 32))))
     (with-saps ((hp h))
       (check (%tokenizer-from-json (namestring path) hp) "ec_tokenizer_from_json"))
+    (setf *have-tokenizer* t)
     (setf *tokenizer* (aref h 0))))
 
 (defun embed-texts (texts)
@@ -314,3 +318,39 @@ each as top-k would return it."
           collect (loop for j from (* i k) below (* (1+ i) k)
                         when (>= (aref ids j) 0)
                           collect (cons (aref ids j) (aref sc j))))))
+
+;;; ---- kb.lisp: kb-search with the index resident on the GPUs ---------------
+
+(defvar *kb-attached* nil)
+
+(defun attach-kb ()
+  "Load kb's index as kb::load-index does (meta.tsv, texts.tsv offsets,
+index.bin, ann.bin when present) and keep its vectors, centroids and lists
+resident on the GPUs; afterwards TOP-K answers kb::top-k's queries there.
+The model (CUDA:LOAD-MODEL or the patched model:load-model) is loaded here
+when no model is, replacing kb::start-encoder (whose *encoder* flag
+kb.lisp:205 reads but never binds)."
+  (unless kb::*vectors* (kb::load-index))
+  (when (zerop *dim*) (load-model (cfg:model-path)))
+  (let ((d kb::*dim*))
+    (if kb::*ann-centroids*
+        (index-load kb::*vectors* kb::*n* :dim d
+                    :centroids kb::*ann-centroids*
+                    :counts (coerce kb::*ann-counts* '(simple-array (unsigned-byte 32) (*)))
+                    :lists kb::*ann-lists*)
+        (index-load kb::*vectors* kb::*n* :dim d)))
+  (setf *nprobe* kb::*ann-nprobe*
+        *kb-attached* t))
+
+(defun kb-search (query &optional (k 8))
+  "kb:kb-search (kb.lisp:202-211) on the GPUs: the query is embedded by the
+library (its tokenizer when LOAD-TOKENIZER was called, else model:embed's
+token ids) and searched over the resident index; returns the same plists
+(:source :domain :score :text), best first."
+  (unless *kb-attached* (attach-kb))
+  (let ((q (if *have-tokenizer* (first (embed-texts (list query))) (model:embed query))))
+    (loop for (idx . score) in (top-k q k)
+          collect (list :source (aref kb::*sources* idx)
+                        :domain (aref kb::*domains* idx)
+                        :score score
+                        :text (kb::chunk-text idx)))))
