@@ -216,11 +216,12 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   // mainloop dominates: K >= 768 and epilogues lighter than GELU (measured:
   // 8-12% faster there, neutral or slower at K = 384 or with GELU).
   // EC_GEMM_PAIR forces pairs for every eligible shape, EC_NO_GEMM_PAIR none.
-  // K <= 384 with the plain / GELU epilogues (QKV, FFN-up of the small
-  // encoders): weight-resident CTA pairs (each pair keeps one W tile in
-  // shared memory and streams only A); EC_NO_GEMM_WR turns this off
+  // EC_GEMM_WR: K <= 384 with the plain / GELU epilogues (QKV, FFN-up of
+  // the small encoders) on weight-resident CTA pairs (each pair keeps one W
+  // tile in shared memory and streams only A).  Opt-in: on the MiniLM
+  // forward it measured 4% slower than the streaming schedule.
   if (!g.bn && g.K <= kGemmWrMaxK && (g.epi == kEpiBf16 || g.epi == kEpiBf16Gelu) &&
-      getenv("EC_NO_GEMM_WR") == nullptr) {
+      getenv("EC_GEMM_WR") != nullptr && getenv("EC_NO_GEMM_WR") == nullptr) {
     cudaError_t e = cudaErrorInvalidConfiguration;
     if (g.N % 256 == 0)
       e = g.epi == kEpiBf16 ? run<256, kEpiBf16, 2, true>(g, st, num_sms)

@@ -168,6 +168,7 @@ def test_gemm_cta_pair(ec, monkeypatch, M, N, K, epi):
                                    (20011, 1536, 384), (700, 2304, 192)])
 @pytest.mark.parametrize("epi", [0, 1])
 def test_gemm_weight_resident(ec, monkeypatch, M, N, K, epi):
+    monkeypatch.setenv("EC_GEMM_WR", "1")
     g = torch.Generator(device="cuda").manual_seed(M * 5 + N + K + epi)
     A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     W = (0.05 * torch.randn(N, K, device="cuda", generator=g)).bfloat16()
