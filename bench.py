@@ -510,12 +510,12 @@ def ivf_build_measure(R, x, perm):
     _lib.init([R.local_rank])
     L = _lib.lib()
     if R.world > 1 and not getattr(R, "comm_ready", False):
-        n = L.ec_comm_id_size()
-        idbuf = C.create_string_buffer(n)
+        idn = L.ec_comm_id_size()
+        idbuf = C.create_string_buffer(idn)
         if R.rank == 0:
             _lib.check(L.ec_comm_get_id(idbuf), "comm id")
-        raw = R.bcast_bytes(idbuf.raw, n)
-        _lib.check(L.ec_comm_init(R.rank, R.world, C.create_string_buffer(raw, n)), "comm init")
+        raw = R.bcast_bytes(idbuf.raw, idn)
+        _lib.check(L.ec_comm_init(R.rank, R.world, C.create_string_buffer(raw, idn)), "comm init")
         R.comm_ready = True
     local_sample = np.arange(len(x_local), dtype=np.int64)
     # warm-up: one iteration on a slice (module load, NCCL channels)

@@ -163,7 +163,9 @@ def test_two_device_failure_before_exchange_then_recovery():
     res = json.loads(p.stdout.strip().splitlines()[-1])
     from embedcuda import _lib
     assert res["first"] == _lib.EC_ENCCL, res
-    assert "injected" in res["msg"]
+    # the call reports the first device's error: the injected failure or the
+    # other device's prompt "another rank failed"
+    assert "injected" in res["msg"] or "another rank failed" in res["msg"], res
     assert res["second_exact"] and res["shutdown"] == "ok", res
 
 
