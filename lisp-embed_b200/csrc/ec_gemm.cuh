@@ -675,6 +675,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) release_acc(acc);
         }
+        if constexpr (!F32) {
+          // bf16 outputs: both chunks are computed into packed registers
+          // first (32 independent element pairs per chunk), then staged
+          // together behind one proxy fence and two TMA stores
+          uint32_t pk[PAIR ? 2 : 1][16];
+#pragma unroll
+          for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
+            if (h == 1 && !two) break;
+            const int col0 = nb * BN + (c0 + 2 * h) * 32;
+            const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 b = args.bias ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+              float2 x0 = __fadd2_rn(make_float2(__uint_as_float(r[h][4 * j]), __uint_as_float(r[h][4 * j + 1])),
+                                     make_float2(b.x, b.y));
+              float2 x1 = __fadd2_rn(make_float2(__uint_as_float(r[h][4 * j + 2]), __uint_as_float(r[h][4 * j + 3])),
+                                     make_float2(b.z, b.w));
+              if constexpr (EPI == kEpiBf16Gelu) {
+                x0 = gelu_epi2(x0, args.gelu_as != 0);
+                x1 = gelu_epi2(x1, args.gelu_as != 0);
+              }
+              pk[h][2 * j] = pack_bf16(x0.x, x0.y);
+              pk[h][2 * j + 1] = pack_bf16(x1.x, x1.y);
+            }
+          }
+          // both staging slots are free once every earlier store has read them
+          if (lane == 0) tma_store_wait_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
+            if (h == 1 && !two) break;
+            uint8_t* st = stage_base + (sbuf ^ h) * Cfg::CHUNK_BYTES;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
+                  make_uint4(pk[h][4 * j], pk[h][4 * j + 1], pk[h][4 * j + 2], pk[h][4 * j + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+#pragma unroll
+            for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
+              if (h == 1 && !two) break;
+              tma_store_2d(&tmC, stage_base + (sbuf ^ h) * Cfg::CHUNK_BYTES, nb * BN + (c0 + 2 * h) * 32, row0);
+            }
+            tma_store_commit();
+          }
+          // (the next step waits for these stores' reads before writing
+          // either slot, so the slot index needs no change)
+        } else {
 #pragma unroll
         for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
           if (h == 1 && !two) break;
@@ -686,29 +736,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
           if (lane == 0) tma_store_wait_read<1>();
           __syncwarp();
-          if constexpr (F32) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) = make_float4(
-                  __uint_as_float(r[h][4 * j]) + bq[j].x, __uint_as_float(r[h][4 * j + 1]) + bq[j].y,
-                  __uint_as_float(r[h][4 * j + 2]) + bq[j].z, __uint_as_float(r[h][4 * j + 3]) + bq[j].w);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float2 x[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float4 b = bq[2 * j + (e >> 1)];
-                x[e] = __fadd2_rn(make_float2(__uint_as_float(r[h][8 * j + 2 * e]),
-                                              __uint_as_float(r[h][8 * j + 2 * e + 1])),
-                                  (e & 1) ? make_float2(b.z, b.w) : make_float2(b.x, b.y));
-                if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_epi2(x[e], args.gelu_as != 0);
-              }
-              *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
-                  make_uint4(pack_bf16(x[0].x, x[0].y), pack_bf16(x[1].x, x[1].y),
-                             pack_bf16(x[2].x, x[2].y), pack_bf16(x[3].x, x[3].y));
-            }
-          }
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) = make_float4(
+                __uint_as_float(r[h][4 * j]) + bq[j].x, __uint_as_float(r[h][4 * j + 1]) + bq[j].y,
+                __uint_as_float(r[h][4 * j + 2]) + bq[j].z, __uint_as_float(r[h][4 * j + 3]) + bq[j].w);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -716,6 +748,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_store_commit();
           }
           sbuf ^= 1;
+        }
         }
       }
       if (!fine) {
