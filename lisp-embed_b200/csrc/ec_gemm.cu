@@ -122,7 +122,6 @@ static cudaError_t run(const GemmLaunch& g, cudaStream_t st, int num_sms) {
   a.n_tiles_n = g.N / BN;
   a.num_tiles = ((g.M + kGemmBM * CG - 1) / (kGemmBM * CG)) * a.n_tiles_n;
   a.status = g.status;
-  a.gelu_as = getenv("EC_GELU_AS") != nullptr ? 1 : 0;
   a.qk = QkRopeEpi{};
   a.ac = ArgCandEpi{};
   if constexpr (EPI == kEpiArgCand) a.ac = *g.ac;

@@ -89,7 +89,6 @@ struct GemmArgs {
   int n_tiles_n;       // N / BN
   int num_tiles;       // ceil(M / 128) * n_tiles_n
   unsigned* status;    // device status word
-  int gelu_as;         // kEpiBf16Gelu: 1 = Abramowitz-Stegun erf, 0 = FMA-only erf
   QkRopeEpi qk;        // kEpiBf16QkRope only
   ArgCandEpi ac;       // kEpiArgCand only
 };
@@ -183,39 +182,6 @@ __device__ __forceinline__ float2 gelu_as2(float2 x) {
   return __ffma2_rn(hx, se, hx);
 }
 
-// GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from FMAs alone, so the epilogue
-// leaves the MUFU pipe free (gelu_as2 needs an approximate reciprocal and an
-// exp2 per element).  erf(z) ~ z P(z^2) for |z| <= 3 and erf(+-3) beyond,
-// P of degree 9 in u = z^2: coefficients from a weighted least-squares fit on
-// 6000 Chebyshev nodes of [0, 3] (Lawson reweighting toward the minimax
-// error), computed for this kernel.  |erf error| <= 1.5e-5 for |z| <= 3 and
-// <= 2.3e-5 beyond (erf(3) = 1 - 2.2e-5), evaluated in fp32 -- against the
-// 1.5e-7 of bert::erf-approx's Abramowitz-Stegun 7.1.26 a GELU difference of
-// at most 1.2e-5 |x|, far below the bf16 rounding the result then gets.
-__device__ __forceinline__ float2 gelu_poly2(float2 x) {
-  const float2 z = __fmul2_rn(x, f2(0.70710678118654752f));
-  const float2 zc = make_float2(fminf(fmaxf(z.x, -3.0f), 3.0f), fminf(fmaxf(z.y, -3.0f), 3.0f));
-  const float2 u = __fmul2_rn(zc, zc);
-  float2 p = __ffma2_rn(u, f2(-3.753065414e-09f), f2(1.995653207e-07f));
-  p = __ffma2_rn(u, p, f2(-4.770880878e-06f));
-  p = __ffma2_rn(u, p, f2(6.851473881e-05f));
-  p = __ffma2_rn(u, p, f2(-6.692105089e-04f));
-  p = __ffma2_rn(u, p, f2(4.784782883e-03f));
-  p = __ffma2_rn(u, p, f2(-2.621991932e-02f));
-  p = __ffma2_rn(u, p, f2(1.123043746e-01f));
-  p = __ffma2_rn(u, p, f2(-3.759220243e-01f));
-  p = __ffma2_rn(u, p, f2(1.128355980e+00f));
-  const float2 e = __fmul2_rn(zc, p);
-  const float2 hx = __fmul2_rn(x, f2(0.5f));
-  return __ffma2_rn(hx, e, hx);
-}
-
-// GELU of the bf16-output epilogue: the FMA-only erf unless EC_GELU_AS
-// selects the Abramowitz-Stegun form (kept for comparison)
-__device__ __forceinline__ float2 gelu_epi2(float2 x, bool as) {
-  return as ? gelu_as2(x) : gelu_poly2(x);
-}
-
 // gelu_pytorch_tanh (gemma::gelu-tanh, gemma.lisp:85-89) in single precision
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float c = 0.7978845608028654f * (x + ((0.044715f * x) * x) * x);
@@ -276,7 +242,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Tile schedule.  Default: tiles unit, unit + units, ... of the row-block
   // major order (tile = mb * n_tiles_n + nb).  WR: units form groups of
   // n_tiles_n; unit u keeps W tile nb = u % n_tiles_n resident and takes the
-  // rows blocks of its group's contiguous share (the launcher guarantees
+  // row blocks of its group's contiguous share (the launcher guarantees
   // units >= n_tiles_n), so the units of a group read the same A tiles at
   // about the same time (L2 hits) and W crosses to the SM once.  For WR a
   // "tile" below is the row block mb itself.
@@ -675,56 +641,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
           if (lane == 0) release_acc(acc);
         }
-        if constexpr (!F32) {
-          // bf16 outputs: both chunks are computed into packed registers
-          // first (32 independent element pairs per chunk), then staged
-          // together behind one proxy fence and two TMA stores
-          uint32_t pk[PAIR ? 2 : 1][16];
-#pragma unroll
-          for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
-            if (h == 1 && !two) break;
-            const int col0 = nb * BN + (c0 + 2 * h) * 32;
-            const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 b = args.bias ? __ldg(b4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-              float2 x0 = __fadd2_rn(make_float2(__uint_as_float(r[h][4 * j]), __uint_as_float(r[h][4 * j + 1])),
-                                     make_float2(b.x, b.y));
-              float2 x1 = __fadd2_rn(make_float2(__uint_as_float(r[h][4 * j + 2]), __uint_as_float(r[h][4 * j + 3])),
-                                     make_float2(b.z, b.w));
-              if constexpr (EPI == kEpiBf16Gelu) {
-                x0 = gelu_epi2(x0, args.gelu_as != 0);
-                x1 = gelu_epi2(x1, args.gelu_as != 0);
-              }
-              pk[h][2 * j] = pack_bf16(x0.x, x0.y);
-              pk[h][2 * j + 1] = pack_bf16(x1.x, x1.y);
-            }
-          }
-          // both staging slots are free once every earlier store has read them
-          if (lane == 0) tma_store_wait_read<0>();
-          __syncwarp();
-#pragma unroll
-          for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
-            if (h == 1 && !two) break;
-            uint8_t* st = stage_base + (sbuf ^ h) * Cfg::CHUNK_BYTES;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
-                  make_uint4(pk[h][4 * j], pk[h][4 * j + 1], pk[h][4 * j + 2], pk[h][4 * j + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-#pragma unroll
-            for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
-              if (h == 1 && !two) break;
-              tma_store_2d(&tmC, stage_base + (sbuf ^ h) * Cfg::CHUNK_BYTES, nb * BN + (c0 + 2 * h) * 32, row0);
-            }
-            tma_store_commit();
-          }
-          // (the next step waits for these stores' reads before writing
-          // either slot, so the slot index needs no change)
-        } else {
 #pragma unroll
         for (int h = 0; h < (PAIR ? 2 : 1); ++h) {
           if (h == 1 && !two) break;
@@ -736,11 +652,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* st = stage_base + sbuf * Cfg::CHUNK_BYTES;
           if (lane == 0) tma_store_wait_read<1>();
           __syncwarp();
+          if constexpr (F32) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) = make_float4(
-                __uint_as_float(r[h][4 * j]) + bq[j].x, __uint_as_float(r[h][4 * j + 1]) + bq[j].y,
-                __uint_as_float(r[h][4 * j + 2]) + bq[j].z, __uint_as_float(r[h][4 * j + 3]) + bq[j].w);
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(st + stage_off<true>(lane, j)) = make_float4(
+                  __uint_as_float(r[h][4 * j]) + bq[j].x, __uint_as_float(r[h][4 * j + 1]) + bq[j].y,
+                  __uint_as_float(r[h][4 * j + 2]) + bq[j].z, __uint_as_float(r[h][4 * j + 3]) + bq[j].w);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float2 x[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float4 b = bq[2 * j + (e >> 1)];
+                x[e] = __fadd2_rn(make_float2(__uint_as_float(r[h][8 * j + 2 * e]),
+                                              __uint_as_float(r[h][8 * j + 2 * e + 1])),
+                                  (e & 1) ? make_float2(b.z, b.w) : make_float2(b.x, b.y));
+                if constexpr (EPI == kEpiBf16Gelu) x[e] = gelu_as2(x[e]);
+              }
+              *reinterpret_cast<uint4*>(st + stage_off<false>(lane, j)) =
+                  make_uint4(pack_bf16(x[0].x, x[0].y), pack_bf16(x[1].x, x[1].y),
+                             pack_bf16(x[2].x, x[2].y), pack_bf16(x[3].x, x[3].y));
+            }
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -748,7 +682,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_store_commit();
           }
           sbuf ^= 1;
-        }
         }
       }
       if (!fine) {
@@ -861,7 +794,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
               float2 xx = make_float2(v[8 * j + e], v[8 * j + e + 1]);
-              if constexpr (EPI == kEpiBf16Gelu) xx = gelu_epi2(xx, args.gelu_as != 0);
+              if constexpr (EPI == kEpiBf16Gelu) xx = gelu_as2(xx);
               x[e] = xx.x;
               x[e + 1] = xx.y;
             }
