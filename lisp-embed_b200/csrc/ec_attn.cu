@@ -7,6 +7,7 @@
 
 #include "ec_attn.cuh"
 #include "ec_attn_short.cuh"
+#include "ec_attn_tc.cuh"
 #include "ec_fa.cuh"
 #include "ec_kernels.h"
 
@@ -131,6 +132,55 @@ static cudaError_t run_mode(const AttnLaunch& l, cudaStream_t st) {
   return run_attn<HD, 0>(l, st);
 }
 
+// sequences [n_long, nseq) of head dim 32 without bias or mask on the
+// tcgen05 short-sequence kernel (ec_attn_tc.cuh): persistent, two CTAs per SM
+static cudaError_t run_short_tc(const AttnLaunch& l, cudaStream_t st) {
+  using Cfg = TcsCfg;
+  static std::mutex mu;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_tc_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(Cfg::SMEM_BYTES));
+      if (e != cudaSuccess) return e;
+      set[dev] = true;
+    }
+  }
+  if (l.max_short_len <= 0 || l.max_short_len > kAttnShortCap) return cudaErrorInvalidValue;
+  auto enc = gemm_encode_fn();
+  if (!enc) return cudaErrorInvalidValue;
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(l.ld), static_cast<cuuint64_t>(l.rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(l.ld) * 2};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t es[2] = {1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(l.qkv), dims, strides,
+          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  TcShortArgs a;
+  a.seqs = l.seqs;
+  a.first = l.n_long;
+  a.nseq = l.nseq - l.n_long;
+  a.heads = l.heads;
+  a.kv_group = l.kv_group;
+  a.q_off = l.q_off;
+  a.k_off = l.k_off;
+  a.v_off = l.v_off;
+  a.out = l.out;
+  a.ldo = l.ldo;
+  a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(32.f));
+  a.status = l.status;
+  const int items = a.nseq * a.heads;
+  const int grid = items < 2 * l.num_sms ? items : 2 * l.num_sms;
+  attn_tc_short_kernel<<<grid, kTcsThreads, Cfg::SMEM_BYTES, st>>>(tm, a);
+  return cudaGetLastError();
+}
+
 void attn_short_buckets(const int* lens_sorted, int n_long, int nseq, AttnLaunch* a) {
   static const int cap[4] = {kAttnShortCap, 192, 128, 64};
   a->nbuckets = 0;
@@ -239,6 +289,8 @@ static cudaError_t run_short_mode(const AttnLaunch& l, cudaStream_t st) {
   }
   if (l.causal) return run_short_h<HD, 2>(l, st);
   if (l.relbias) return run_short_h<HD, 1>(l, st);
+  // head dim 32, no bias or mask: the tcgen05 kernel when EC_SHORT_ATTN_TC
+  if (HD == 32 && getenv("EC_SHORT_ATTN_TC") != nullptr) return run_short_tc(l, st);
   return run_short_h<HD, 0>(l, st);
 }
 

@@ -49,11 +49,14 @@ def _check(shape, seed, lengths, synth_root, ec, workload, d=None):
 
 
 # default: the residual between sublayers is the LayerNorm's bf16 output;
-# EC_F32_RESIDUAL keeps an fp32 residual stream
-@pytest.mark.parametrize("f32_resid", [0, 1])
+# EC_F32_RESIDUAL keeps an fp32 residual stream; EC_SHORT_ATTN_TC runs the
+# attention of these short sequences on the tcgen05 short-sequence kernel
+@pytest.mark.parametrize("f32_resid", [0, 1, 2])
 def test_minilm_full_depth(synth_root, ec, monkeypatch, f32_resid):
-    if f32_resid:
+    if f32_resid == 1:
         monkeypatch.setenv("EC_F32_RESIDUAL", "1")
+    elif f32_resid == 2:
+        monkeypatch.setenv("EC_SHORT_ATTN_TC", "1")
     fam, cos = _check(synth.MINILM, 0, [1, 2, 16, 63, 64, 65, 130, 256], synth_root, ec, "minilm")
     assert fam == "bert"
 

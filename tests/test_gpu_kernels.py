@@ -271,8 +271,10 @@ def test_attention_rescale_mixed_rows(ec, hd, heads, kv, causal):
 # the short kernel's fp16 probabilities with large, uneven logits: keys from
 # position 128 on scaled by 4 (scores up to ~30 in log2 units, probabilities
 # down to f16 underflow) next to sequences that never reach them
-@pytest.mark.parametrize("hd,causal", [(32, 0), (64, 0), (32, 1)])
-def test_attention_short_large_logits(ec, hd, causal):
+@pytest.mark.parametrize("hd,causal,tc", [(32, 0, 0), (64, 0, 0), (32, 1, 0), (32, 0, 1)])
+def test_attention_short_large_logits(ec, monkeypatch, hd, causal, tc):
+    if tc:
+        monkeypatch.setenv("EC_SHORT_ATTN_TC", "1")
     _run_attention(ec, [256, 200, 129, 40, 130], hd, 4, 4 if not causal else 2, causal,
                    key_boost=4.0, tol=4e-2)
 
@@ -283,12 +285,15 @@ def test_attention_short_large_logits(ec, hd, causal):
 @pytest.mark.parametrize("hd,heads,kv,causal,tc", [(32, 12, 12, 0, 0), (32, 4, 2, 1, 0),
                                                     (64, 12, 12, 0, 0), (64, 4, 2, 1, 0),
                                                     (64, 12, 12, 0, 1), (32, 12, 12, 0, 1),
-                                                    (32, 12, 12, 0, 2), (64, 4, 2, 1, 2)])
+                                                    (32, 12, 12, 0, 2), (64, 4, 2, 1, 2),
+                                                    (32, 12, 12, 0, 3), (32, 4, 2, 0, 3)])
 def test_attention_short_sequences(ec, monkeypatch, hd, heads, kv, causal, tc):
     if tc == 1:
         monkeypatch.setenv("EC_NO_SHORT_ATTN", "1")
     elif tc == 2:
         monkeypatch.setenv("EC_SHORT_ATTN_BF16", "1")
+    elif tc == 3:  # the tcgen05 short-sequence kernel (head dim 32, no mask)
+        monkeypatch.setenv("EC_SHORT_ATTN_TC", "1")
     rng = np.random.default_rng(hd * 7 + heads)
     lens = [int(x) for x in rng.integers(1, 257, 40)] + [256, 255, 16, 1]
     _run_attention(ec, lens, hd, heads, kv, causal)
