@@ -166,6 +166,7 @@ static cudaError_t run_short_tc(const AttnLaunch& l, cudaStream_t st) {
   a.seqs = l.seqs;
   a.first = l.n_long;
   a.nseq = l.nseq - l.n_long;
+  a.n_two = l.n_gt128;
   a.heads = l.heads;
   a.kv_group = l.kv_group;
   a.q_off = l.q_off;
@@ -175,8 +176,9 @@ static cudaError_t run_short_tc(const AttnLaunch& l, cudaStream_t st) {
   a.ldo = l.ldo;
   a.scale_log2 = 1.4426950408889634f * (l.scale > 0.f ? l.scale : 1.f / sqrtf(32.f));
   a.status = l.status;
-  const int items = a.nseq * a.heads;
-  const int grid = items < 2 * l.num_sms ? items : 2 * l.num_sms;
+  const int units = (a.n_two * 2 + (a.nseq - a.n_two)) * a.heads;
+  const int grid = units < l.num_sms ? units : l.num_sms;
+  if (grid <= 0) return cudaSuccess;
   attn_tc_short_kernel<<<grid, kTcsThreads, Cfg::SMEM_BYTES, st>>>(tm, a);
   return cudaGetLastError();
 }
@@ -184,8 +186,10 @@ static cudaError_t run_short_tc(const AttnLaunch& l, cudaStream_t st) {
 void attn_short_buckets(const int* lens_sorted, int n_long, int nseq, AttnLaunch* a) {
   static const int cap[4] = {kAttnShortCap, 192, 128, 64};
   a->nbuckets = 0;
+  a->n_gt128 = 0;
   int prev = -1;
   for (int k = n_long; k < nseq; ++k) {
+    if (lens_sorted[k] > 128) ++a->n_gt128;
     int b = 0;
     while (b < 3 && lens_sorted[k] <= cap[b + 1]) ++b;
     if (b != prev) {

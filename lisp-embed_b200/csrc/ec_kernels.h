@@ -260,6 +260,7 @@ struct AttnLaunch {
   int nbuckets = 0;
   int bucket_first[5] = {0, 0, 0, 0, 0};
   int bucket_max[4] = {0, 0, 0, 0};
+  int n_gt128 = 0;       // sequences of [n_long, nseq) longer than 128 tokens
   float scale = 0.f;     // logit scale; 0 = 1 / sqrt(head_dim) (Gemma uses 1.0)
 };
 // key capacity of the short-sequence attention kernel (ec_attn_short.cuh)
