@@ -216,11 +216,11 @@ struct MlpLaunch {
   const __nv_bfloat16* W2;  // [H, F]
   const float* b1;
   const float* b2;
-  const float* resid;       // [M, H]
+  const float* resid;       // [M, H] fp32, or nullptr: the residual is A itself
   const float* ln_g;
   const float* ln_b;
-  float* out32;
-  __nv_bfloat16* outb;
+  float* out32;             // [M, H] or nullptr (no fp32 row)
+  __nv_bfloat16* outb;      // [M, H] (may alias A)
   int M, H, F;
   unsigned* status;
 };

@@ -27,28 +27,47 @@ static bool enc(CUtensorMap* m, CUtensorMapDataType dt, const void* p, uint64_t 
 template <int H>
 static cudaError_t run(const MlpLaunch& l, cudaStream_t st, int num_sms) {
   using Cfg = MlpCfg<H>;
+  // clusters of two CTAs (one CTA per SM): as many as fit at once
   static std::mutex mu;
-  static bool set[64] = {};
+  static int max_clusters[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kMlpThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(mlp_fused_kernel<H>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (!max_clusters[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(mlp_fused_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(Cfg::SMEM_BYTES));
       if (e != cudaSuccess) return e;
-      set[dev] = true;
+      int n = 0;
+      cfg.gridDim = dim3((num_sms / 2) * 2, 1, 1);
+      e = cudaOccupancyMaxActiveClusters(&n, mlp_fused_kernel<H>, &cfg);
+      if (e != cudaSuccess) return e;
+      if (n <= 0) return cudaErrorInvalidConfiguration;
+      max_clusters[dev] = n;
     }
   }
-  CUtensorMap ta, tw1, tw2, to32, tob;
+  CUtensorMap tx, tw1, tw2, to32, tob;
   const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (!enc(&ta, BF, l.A, l.M, H, H * 2ull, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !enc(&tw1, BF, l.W1, l.F, H, H * 2ull, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !enc(&tw2, BF, l.W2, H, l.F, l.F * 2ull, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !enc(&to32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, l.out32, l.M, H, H * 4ull, 32, 32,
-           CU_TENSOR_MAP_SWIZZLE_128B) ||
+  // X: 128-row boxes of 64 columns; W1: this CTA's 32 rows of a 64-row
+  // slice; W2: this CTA's half of a column part of H
+  float* o32 = l.out32 ? l.out32 : reinterpret_cast<float*>(l.outb);  // unused map when absent
+  if (!enc(&tx, BF, l.A, l.M, H, H * 2ull, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !enc(&tw1, BF, l.W1, l.F, H, H * 2ull, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !enc(&tw2, BF, l.W2, H, l.F, l.F * 2ull, 64, Cfg::NPW / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !enc(&to32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, o32, l.M, l.out32 ? H : H / 2, l.out32 ? H * 4ull : H * 2ull,
+           32, 32, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !enc(&tob, BF, l.outb, l.M, H, H * 2ull, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
   MlpArgs a;
@@ -57,19 +76,21 @@ static cudaError_t run(const MlpLaunch& l, cudaStream_t st, int num_sms) {
   a.b1 = l.b1;
   a.b2 = l.b2;
   a.resid = l.resid;
+  a.resid_b = l.A;
   a.ln_g = l.ln_g;
   a.ln_b = l.ln_b;
-  a.num_tiles = (l.M + 127) / 128;
+  a.out32 = l.out32 != nullptr;
+  a.num_tiles = (l.M + 255) / 256;
   a.status = l.status;
-  const int grid = a.num_tiles < num_sms ? a.num_tiles : num_sms;
-  mlp_fused_kernel<H><<<grid, kMlpThreads, Cfg::SMEM_BYTES, st>>>(ta, tw1, tw2, to32, tob, a);
-  return cudaGetLastError();
+  const int clusters = a.num_tiles < max_clusters[dev] ? a.num_tiles : max_clusters[dev];
+  cfg.gridDim = dim3(clusters * 2, 1, 1);
+  return cudaLaunchKernelEx(&cfg, mlp_fused_kernel<H>, tx, tw1, tw2, to32, tob, a);
 }
 
 bool mlp_supported(int H, int F) { return (H == 384 || H == 256 || H == 128) && F % 128 == 0; }
 
 cudaError_t launch_mlp(const MlpLaunch& l, cudaStream_t st, int num_sms) {
-  if (l.M <= 0 || l.F % 128) return cudaErrorInvalidValue;
+  if (l.M <= 0 || l.F % 128 || !l.A || !l.outb) return cudaErrorInvalidValue;
   switch (l.H) {
     case 384: return run<384>(l, st, num_sms);
     case 256: return run<256>(l, st, num_sms);

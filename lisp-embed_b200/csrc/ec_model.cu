@@ -709,8 +709,7 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
   // sublayers as the LayerNorm's bf16 output (the row the next GEMM reads
   // anyway); only the last LayerNorm also writes fp32 rows, for pooling.
   // EC_F32_RESIDUAL keeps the fp32 stream everywhere.
-  const bool bf16_resid = fuse_ln && getenv("EC_F32_RESIDUAL") == nullptr &&
-                          getenv("EC_FUSED_MLP") == nullptr;
+  const bool bf16_resid = fuse_ln && getenv("EC_F32_RESIDUAL") == nullptr;
   auto gemm_ln = [&](const bf16* A, int K, const bf16* W, const float* bias, const float* lg,
                      const float* lb, bool out32 = true) -> int {
     GemmLnLaunch g{A, K, W, T, H, K, bias, h32, lg, lb, h32, hb, d.status};
@@ -814,15 +813,18 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
         const int e0 = prof_begin(d);
         EC_TRY(rows(launch_ln(l1, st), "layernorm", TH * 10.0, e0));
       }
-      // the fused block is opt-in until it beats the unfused path (it is
-      // bound by streaming W1/W2 from L2 with 64 KB in flight per SM)
-      if (mlp_supported(H, F) && getenv("EC_FUSED_MLP")) {
-        // up + GELU + down + bias + residual + LayerNorm in one kernel
-        MlpLaunch ml{hb, w.wff, w.wout, w.bff, w.bout, h32, w.ln2g, w.ln2b, h32, hb, T, H, F,
-                     d.status};
+      // the fused block: opt-in (EC_FUSED_MLP) until it beats the unfused pair
+      if (mlp_supported(H, F) && fuse_ln && getenv("EC_FUSED_MLP")) {
+        // up + GELU + down + bias + residual + LayerNorm in one kernel; the
+        // residual is the bf16 input rows (or the fp32 stream), the fp32 row
+        // is stored where the unfused path stores it
+        const bool want32 = !bf16_resid || li + 1 == m.layers;
+        MlpLaunch ml{hb, w.wff, w.wout, w.bff, w.bout, bf16_resid ? nullptr : h32, w.ln2g, w.ln2b,
+                     want32 ? h32 : nullptr, hb, T, H, F, d.status};
         const int e0 = prof_begin(d);
         const cudaError_t e = launch_mlp(ml, st, d.num_sms);
-        prof_end(d, 0, 4.0 * T * H * F, 2.0 * T * H + 4.0 * H * F + 4.0 * T * H + 6.0 * T * H,
+        prof_end(d, 0, 4.0 * T * H * F,
+                 2.0 * T * H + 4.0 * H * F + (bf16_resid ? 2.0 : 4.0) * T * H + (want32 ? 6.0 : 2.0) * T * H,
                  e0);
         EC_TRY(check_cuda(e, "fused mlp"));
       } else {

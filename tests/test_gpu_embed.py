@@ -50,13 +50,17 @@ def _check(shape, seed, lengths, synth_root, ec, workload, d=None):
 
 # default: the residual between sublayers is the LayerNorm's bf16 output;
 # EC_F32_RESIDUAL keeps an fp32 residual stream; EC_SHORT_ATTN_TC runs the
-# attention of these short sequences on the tcgen05 short-sequence kernel
-@pytest.mark.parametrize("f32_resid", [0, 1, 2])
-def test_minilm_full_depth(synth_root, ec, monkeypatch, f32_resid):
-    if f32_resid == 1:
+# attention of these short sequences on the tcgen05 short-sequence kernel;
+# EC_FUSED_MLP runs each feed-forward block as one kernel (bf16 and fp32
+# residual)
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+def test_minilm_full_depth(synth_root, ec, monkeypatch, variant):
+    if variant in (1, 4):
         monkeypatch.setenv("EC_F32_RESIDUAL", "1")
-    elif f32_resid == 2:
+    if variant == 2:
         monkeypatch.setenv("EC_SHORT_ATTN_TC", "1")
+    if variant in (3, 4):
+        monkeypatch.setenv("EC_FUSED_MLP", "1")
     fam, cos = _check(synth.MINILM, 0, [1, 2, 16, 63, 64, 65, 130, 256], synth_root, ec, "minilm")
     assert fam == "bert"
 
