@@ -48,11 +48,20 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 int sync_and_check(Device& d, const char* what) {
-  int rc = check_cuda(cudaStreamSynchronize(d.stream), what);
+  // the status word travels with the stream's last copy: one wait
+  int rc = d.status_host ? check_cuda(cudaMemcpyAsync(d.status_host, d.status, 4, cudaMemcpyDeviceToHost,
+                                                      d.stream), "status read")
+                         : EC_OK;
+  if (rc) return rc;
+  rc = check_cuda(cudaStreamSynchronize(d.stream), what);
   if (rc) return rc;
   unsigned st = 0;
-  rc = check_cuda(cudaMemcpy(&st, d.status, 4, cudaMemcpyDeviceToHost), "status read");
-  if (rc) return rc;
+  if (d.status_host) {
+    st = *d.status_host;
+  } else {
+    rc = check_cuda(cudaMemcpy(&st, d.status, 4, cudaMemcpyDeviceToHost), "status read");
+    if (rc) return rc;
+  }
   if (st) {
     cudaMemsetAsync(d.status, 0, 4, d.stream);
     cudaStreamSynchronize(d.stream);
@@ -159,7 +168,9 @@ static void destroy_device(Device* d) {
     if (d->stage[i]) cudaFreeHost(d->stage[i]);
     if (d->stage_ev[i]) cudaEventDestroy(d->stage_ev[i]);
   }
+  graphs_clear(*d);
   if (d->status) cudaFree(d->status);
+  if (d->status_host) cudaFreeHost(d->status_host);
   if (d->stream) cudaStreamDestroy(d->stream);
   for (cudaEvent_t e : d->evpool) cudaEventDestroy(e);
   delete d;
@@ -292,6 +303,10 @@ int ec_init(const int* devices, int ndev) {
     if (!rc) rc = check_cuda(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "stream");
     if (!rc) rc = dev_alloc(*d, reinterpret_cast<void**>(&d->status), 256, "status word");
     if (!rc) rc = check_cuda(cudaMemset(d->status, 0, 256), "status clear");
+    if (!rc && cudaHostAlloc(reinterpret_cast<void**>(&d->status_host), 64, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      d->status_host = nullptr;  // sync_and_check falls back to a plain copy
+    }
     // place ec_flat_search_noalloc's static scratch array now, with the
     // library's other device memory, rather than at its first call
     void* scratch = nullptr;

@@ -121,7 +121,13 @@ static int concat_f32(Device& d, const std::vector<const Tensor*>& parts, float*
   return EC_OK;
 }
 
+void graphs_clear(Device& d) {
+  for (auto& g : d.graphs) cudaGraphExecDestroy(g.exec);
+  d.graphs.clear();
+}
+
 void free_model(Device& d) {
+  graphs_clear(d);
   for (void* p : d.model.owned) cudaFree(p);
   d.model = ModelW();
 }
@@ -585,6 +591,11 @@ static WsLayout layout_for(const ModelW& m, size_t T, size_t nseq) {
   return L;
 }
 
+// CUDA graphs of whole forwards: batches up to this many tokens, this many
+// distinct length sets per device
+constexpr int64_t kGraphMaxTokens = 8192;
+constexpr size_t kGraphCache = 64;
+
 static int ensure_ws(Device& d, int T, int nseq) {
   // the layout depends on the model (hidden, qkv, ffn widths), so size by
   // bytes, not only by token / sequence counts
@@ -594,6 +605,8 @@ static int ensure_ws(Device& d, int T, int nseq) {
                      (static_cast<size_t>(t2) / 64 + s2 + 1) * 8 +
                      (static_cast<size_t>(t2) / 128 + s2 + 1) * 16 + static_cast<size_t>(s2) * 8 + 768 +
                      static_cast<size_t>(s2) * std::max(d.model.H, d.model.out_dim) * 4 + 1024;
+  if (!d.ws || L.total > d.ws_bytes || t2 != d.ws_tokens || s2 != d.ws_seqs || pin > d.pin_bytes)
+    graphs_clear(d);  // the layout or the buffers change
   if (!d.ws || L.total > d.ws_bytes) {
     if (d.ws) {
       cudaStreamSynchronize(d.stream);
@@ -1046,8 +1059,9 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
 }
 
 // Build the per-chunk host tables (cu offsets, attention blocks sorted by
-// descending length) into pinned staging and upload them.
-static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& lens, AttnTables* tb) {
+// descending length) into pinned staging (fill_tables), and enqueue their
+// upload (copy_tables).  The staging layout depends only on the lengths.
+static void fill_tables(Device& d, const std::vector<int>& lens, AttnTables* tb) {
   const int nseq = static_cast<int>(lens.size());
   char* pin = static_cast<char*>(d.pin);
   int* hcu = reinterpret_cast<int*>(pin);
@@ -1075,6 +1089,17 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
   for (int k = 0; k < nseq; ++k) hseq[k] = make_int2(hcu[order[k]], lens[order[k]]);
   tb->sorted_lens.resize(nseq);
   for (int k = 0; k < nseq; ++k) tb->sorted_lens[k] = lens[order[k]];
+  tb->nblk = nb;
+  tb->nblk128 = nb128;
+}
+
+static int copy_tables(Device& d, const WsLayout& L, int nseq, const AttnTables& tb) {
+  char* pin = static_cast<char*>(d.pin);
+  const int nb = tb.nblk, nb128 = tb.nblk128;
+  const char* hcu = pin;
+  const char* hblk = pin + al256((nseq + 1) * 4);
+  const char* hblk128 = hblk + al256(static_cast<size_t>(nb) * 8);
+  const char* hseq = hblk128 + al256(static_cast<size_t>(nb128) * 16);
   char* ws = static_cast<char*>(d.ws);
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.seqs, hseq, static_cast<size_t>(nseq) * 8,
                                     cudaMemcpyHostToDevice, d.stream),
@@ -1082,15 +1107,14 @@ static int upload_tables(Device& d, const WsLayout& L, const std::vector<int>& l
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks128, hblk128, static_cast<size_t>(nb128) * 16,
                                     cudaMemcpyHostToDevice, d.stream),
                     "block upload"));
-  tb->nblk128 = nb128;
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.cu, hcu, (nseq + 1) * 4, cudaMemcpyHostToDevice, d.stream),
                     "cu upload"));
   EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.blocks, hblk, static_cast<size_t>(nb) * 8,
                                     cudaMemcpyHostToDevice, d.stream),
                     "block upload"));
-  tb->nblk = nb;
   return EC_OK;
 }
+
 
 int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
                     const std::vector<int>& seqs, const int64_t* offsets, float* out_host,
@@ -1137,26 +1161,20 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     for (int k = 0; k < nseq; ++k)
       lens[k] = static_cast<int>(offsets[seqs[i + k] + 1] - offsets[seqs[i + k]]);
     AttnTables tb;
-    EC_TRY(upload_tables(d, L, lens, &tb));
     char* ws = static_cast<char*>(d.ws);
-    if (ids_dev) {
-      EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, ids_dev + offsets[seqs[i]],
-                                        static_cast<size_t>(T) * 4, cudaMemcpyDeviceToDevice,
-                                        d.stream),
-                        "ids copy"));
-    } else {
-      int* hid = reinterpret_cast<int*>(static_cast<char*>(d.pin) + d.pin_bytes -
-                                        al256(static_cast<size_t>(T) * 4) - 256);
-      // pinned layout: tables at the front, ids at the back
+    // pinned layout: tables at the front, ids at the back, outputs below them
+    int* hid = reinterpret_cast<int*>(static_cast<char*>(d.pin) + d.pin_bytes -
+                                      al256(static_cast<size_t>(T) * 4) - 256);
+    const size_t obytes = static_cast<size_t>(nseq) * m.out_dim * 4;
+    float* hout = reinterpret_cast<float*>(static_cast<char*>(d.pin) + d.pin_bytes -
+                                           al256(static_cast<size_t>(T) * 4) - 256 - al256(obytes));
+    if (ids_host) {
       int64_t o = 0;
       for (int k = 0; k < nseq; ++k) {
         const int s = seqs[i + k];
         std::memcpy(hid + o, ids_host + offsets[s], static_cast<size_t>(lens[k]) * 4);
         o += lens[k];
       }
-      EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, hid, static_cast<size_t>(T) * 4,
-                                        cudaMemcpyHostToDevice, d.stream),
-                        "ids upload"));
     }
     float* dout = out_dev ? out_dev + static_cast<size_t>(seqs[i]) * out_stride
                           : reinterpret_cast<float*>(ws + L.out);
@@ -1165,25 +1183,76 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     for (int k = 0; k < nseq; ++k)
       pairs += m.family == EC_FAMILY_LLAMA ? 0.5 * lens[k] * (lens[k] + 1.0)
                                            : static_cast<double>(lens[k]) * lens[k];
-    EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
-    if (!out_dev) {
-      // pinned staging: the region reserved for the outputs sits just below
-      // the ids at the back (ensure_ws sizes it; the tables at the front end
-      // well before it)
-      const size_t obytes = static_cast<size_t>(nseq) * m.out_dim * 4;
-      float* hout = reinterpret_cast<float*>(static_cast<char*>(d.pin) + d.pin_bytes -
-                                             al256(static_cast<size_t>(T) * 4) - 256 - al256(obytes));
-      EC_TRY(check_cuda(cudaMemcpyAsync(hout, dout, obytes, cudaMemcpyDeviceToHost, d.stream),
-                        "output download"));
-      EC_TRY(sync_and_check(d, "forward"));
-      prof_collect(d);
+    // the stream work of this chunk: tables and ids up, forward, rows down
+    auto enqueue = [&]() -> int {
+      EC_TRY(copy_tables(d, L, nseq, tb));
+      if (ids_dev) {
+        EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, ids_dev + offsets[seqs[i]],
+                                          static_cast<size_t>(T) * 4, cudaMemcpyDeviceToDevice,
+                                          d.stream),
+                          "ids copy"));
+      } else {
+        EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, hid, static_cast<size_t>(T) * 4,
+                                          cudaMemcpyHostToDevice, d.stream),
+                          "ids upload"));
+      }
+      EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
+      if (!out_dev)
+        EC_TRY(check_cuda(cudaMemcpyAsync(hout, dout, obytes, cudaMemcpyDeviceToHost, d.stream),
+                          "output download"));
+      return EC_OK;
+    };
+    fill_tables(d, lens, &tb);
+    // Small host batches (query serving) replay a CUDA graph of the whole
+    // chunk, captured at the first batch with these lengths on this
+    // workspace: one launch in place of ~30, the host writes only the pinned
+    // tables and ids.  Not while profiling or checking every launch.
+    const bool graph = ids_host && !out_dev && j - i == seqs.size() && T <= kGraphMaxTokens &&
+                       !G().profile && !G().sync_each && getenv("EC_NO_GRAPH") == nullptr;
+    Device::FwdGraph* g = nullptr;
+    if (graph) {
+      for (auto& e : d.graphs)
+        if (e.lens == lens && e.ws == d.ws && e.ws_tokens == d.ws_tokens && e.ws_seqs == d.ws_seqs &&
+            e.pin == d.pin && e.pin_bytes == d.pin_bytes) {
+          g = &e;
+          break;
+        }
+      if (!g) {
+        cudaGraph_t cg = nullptr;
+        EC_TRY(check_cuda(cudaStreamBeginCapture(d.stream, cudaStreamCaptureModeRelaxed), "graph capture"));
+        const int rc = enqueue();
+        const cudaError_t ce = cudaStreamEndCapture(d.stream, &cg);
+        if (rc) {
+          if (cg) cudaGraphDestroy(cg);
+          return rc;
+        }
+        EC_TRY(check_cuda(ce, "graph capture"));
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&ex, cg, 0);
+        cudaGraphDestroy(cg);
+        EC_TRY(check_cuda(ie, "graph instantiate"));
+        if (d.graphs.size() >= kGraphCache) {
+          // drop the least recently used
+          size_t lru = 0;
+          for (size_t e = 1; e < d.graphs.size(); ++e)
+            if (d.graphs[e].used < d.graphs[lru].used) lru = e;
+          cudaGraphExecDestroy(d.graphs[lru].exec);
+          d.graphs.erase(d.graphs.begin() + static_cast<std::ptrdiff_t>(lru));
+        }
+        d.graphs.push_back({lens, d.ws, d.ws_tokens, d.ws_seqs, d.pin, d.pin_bytes, ex, 0});
+        g = &d.graphs.back();
+      }
+      g->used = ++d.graph_clock;
+      EC_TRY(check_cuda(cudaGraphLaunch(g->exec, d.stream), "graph launch"));
+    } else {
+      EC_TRY(enqueue());
+    }
+    EC_TRY(sync_and_check(d, "forward"));
+    prof_collect(d);
+    if (!out_dev)
       for (int k = 0; k < nseq; ++k)
         std::memcpy(out_host + static_cast<size_t>(seqs[i + k]) * out_stride,
                     hout + static_cast<size_t>(k) * m.out_dim, static_cast<size_t>(m.out_dim) * 4);
-    } else {
-      EC_TRY(sync_and_check(d, "forward"));
-      prof_collect(d);
-    }
     i = j;
   }
   return EC_OK;

@@ -123,7 +123,26 @@ struct Device {
   // double-buffered pinned staging of large uploads (upload_h2d)
   void* stage[2] = {nullptr, nullptr};
   cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+  // pinned mirror of the status word (read with the stream's last copy)
+  unsigned* status_host = nullptr;
+  // captured forwards of small host batches: the whole upload -> forward ->
+  // download sequence of one set of sequence lengths as a CUDA graph, valid
+  // for the workspace and staging it was captured on
+  struct FwdGraph {
+    std::vector<int> lens;
+    void* ws;
+    int ws_tokens, ws_seqs;
+    void* pin;
+    size_t pin_bytes;
+    cudaGraphExec_t exec;
+    uint64_t used;
+  };
+  std::vector<FwdGraph> graphs;
+  uint64_t graph_clock = 0;
 };
+
+// drop every captured forward of d (the workspace, staging or model changed)
+void graphs_clear(Device& d);
 
 struct Global {
   std::mutex mu;

@@ -189,6 +189,27 @@ def test_batch_invariance_and_order(synth_root, ec):
     assert np.array_equal(full, again)  # deterministic
 
 
+def test_graph_replay(synth_root, ec, monkeypatch):
+    """Small host batches replay a captured CUDA graph of the forward: the
+    replays (with other lengths captured in between, and new ids of the same
+    lengths) equal the launch-by-launch path bit for bit, and the oracle."""
+    d = synth.build_model_dir(synth.MINILM, 0, synth_root)
+    model.load_model(d)
+    ids, offs = synth.make_inputs("minilm", 8, 3)
+    rng = np.random.default_rng(5)
+    q = [np.concatenate([[101], rng.integers(1000, 30522, 8), [102]]).astype(np.int32) for _ in range(3)]
+    got = [model.embed_batch(ids, offs), model.embed(q[0]), model.embed_batch(ids, offs),
+           model.embed(q[1]), model.embed(q[2]), model.embed_batch(ids, offs)]
+    monkeypatch.setenv("EC_NO_GRAPH", "1")
+    ref = [model.embed_batch(ids, offs), model.embed(q[0]), model.embed_batch(ids, offs),
+           model.embed(q[1]), model.embed(q[2]), model.embed_batch(ids, offs)]
+    for a, b in zip(got, ref):
+        assert np.array_equal(a, b)
+    om = oracle.OracleModel(d)
+    for k, gi in enumerate((1, 3, 4)):
+        assert _cos(got[gi][None], om.embed(q[k])[None])[0] >= 0.9999
+
+
 def test_errors(synth_root, ec):
     from embedcuda import _lib
     d = synth.build_model_dir(synth.MINILM, 0, synth_root)
