@@ -464,17 +464,25 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
   for (int64_t a = q0; a < q1; a += QB) {
     const int64_t nq = std::min(QB, q1 - a);
     const int nchunks = ivf ? 0 : static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(1, (ix.n + 8191) / 8192)));
-    const int ngroups = ivf ? nprobe : nchunks;
+    // query-batched scans once a batch gives each list several queries
+    // (flat: once there are several queries); one CTA per (query, list)
+    // otherwise, each list split over up to 8 CTAs while the batch leaves
+    // the SMs idle (a single query probes only nprobe lists)
+    const bool batched = scan_batched_ok(ix, nq, nprobe, topk, ivf);
+    int parts = 1;
+    if (ivf && !batched) {
+      const int64_t ctas = nq * nprobe;
+      while (parts < 8 && ctas * parts < 4 * dv.num_sms &&
+             static_cast<int64_t>(nprobe) * parts * 2 * topk * 8 <= 150 * 1024)
+        parts *= 2;
+    }
+    const int ngroups = ivf ? nprobe * parts : nchunks;
     const size_t s_q = a256(static_cast<size_t>(nq) * d * 4);
     const size_t s_s = ivf ? a256(static_cast<size_t>(nq) * ix.k * 4) : 0;
     const size_t s_p = ivf ? a256(static_cast<size_t>(nq) * nprobe * 4) : 0;
     const size_t s_c = a256(static_cast<size_t>(nq) * ngroups * topk * 8);
     const size_t s_i = a256(static_cast<size_t>(nq) * topk * 8);
     const size_t s_f = a256(static_cast<size_t>(nq) * topk * 4);
-    // query-batched scans once a batch gives each list several queries
-    // (flat: once there are several queries); one CTA per (query, list)
-    // otherwise
-    const bool batched = scan_batched_ok(ix, nq, nprobe, topk, ivf);
     const size_t s_b = batched && ivf ? a256(batched_list_scan_ws(ix.k, nq * nprobe)) : 0;
     const bool tcp = ivf && probe_tc_ok(ix, nq, nprobe);
     const size_t s_qb = tcp ? a256(static_cast<size_t>(nq) * d * 2) : 0;
@@ -537,7 +545,7 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
       const cudaError_t e =
           batched ? launch_list_scan_batched(ix.x, d, ix.lists, ix.offs, ix.k, dp, nprobe, dq, nq, topk,
                                              w + s_q + s_s + s_p + s_c + s_i + s_f, dc, st)
-                  : launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, dc, st);
+                  : launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, parts, dc, st);
       prof_end(dv, 3, 2.0 * rows * d, 4.0 * rows * d, e0);
       EC_TRY(check_cuda(e, "list scan"));
     } else {

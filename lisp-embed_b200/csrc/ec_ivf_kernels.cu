@@ -159,6 +159,41 @@ __global__ void __launch_bounds__(256) scores_kernel(const float* Q, int64_t nq,
   }
 }
 
+// S[q, c] for a few queries (nq <= kSmallQ): one thread per centroid, the
+// sequential single-float sum of exact_tile (bit-identical scores); the
+// centroid row is read once for all the queries, several loads in flight.
+// (The 128 x 128 tiles of scores_kernel would be almost all padding.)
+constexpr int kSmallQ = 8;
+__global__ void __launch_bounds__(128) scores_small_kernel(const float* Q, int nq, const float* C, int k,
+                                                           int d, float* S) {
+  extern __shared__ float qs[];  // [nq][d]
+  for (int i = threadIdx.x; i < nq * d; i += blockDim.x) qs[i] = Q[i];
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= k) return;
+  float acc[kSmallQ];
+#pragma unroll
+  for (int j = 0; j < kSmallQ; ++j) acc[j] = 0.f;
+  const float4* cr = reinterpret_cast<const float4*>(C + static_cast<int64_t>(c) * d);
+#pragma unroll 8
+  for (int c4 = 0; c4 < d / 4; ++c4) {
+    const float4 v = cr[c4];
+#pragma unroll
+    for (int j = 0; j < kSmallQ; ++j) {
+      if (j < nq) {
+        const float* qj = qs + j * d + 4 * c4;
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qj[0], v.x));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qj[1], v.y));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qj[2], v.z));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qj[3], v.w));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kSmallQ; ++j)
+    if (j < nq) S[static_cast<int64_t>(j) * k + c] = acc[j];
+}
+
 // ---------------------------------------------------- stable counting sort --
 constexpr int kSortTile = 4096;
 
@@ -585,12 +620,23 @@ __device__ void scan_rows(const float* X, int d, const uint32_t* lists, int64_t 
       const int64_t row = kIndirect ? static_cast<int64_t>(lists[start + p]) : start + p;
       const float4* xr = reinterpret_cast<const float4*>(X + row * d);
       float s = 0.f;
-      for (int c4 = 0; c4 < d / 4; ++c4) {
-        const float4 v = xr[c4];
-        s = __fadd_rn(s, __fmul_rn(v.x, qs[4 * c4]));
-        s = __fadd_rn(s, __fmul_rn(v.y, qs[4 * c4 + 1]));
-        s = __fadd_rn(s, __fmul_rn(v.z, qs[4 * c4 + 2]));
-        s = __fadd_rn(s, __fmul_rn(v.w, qs[4 * c4 + 3]));
+      // the row in register chunks of 8 x 16 bytes, all loads of a chunk in
+      // flight before its adds (which stay one sequential chain)
+      const int d4 = d / 4;
+      for (int c0 = 0; c0 < d4; c0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = c0 + u < d4 ? xr[c0 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (c0 + u < d4) {
+            const float* qq = qs + 4 * (c0 + u);
+            s = __fadd_rn(s, __fmul_rn(v[u].x, qq[0]));
+            s = __fadd_rn(s, __fmul_rn(v[u].y, qq[1]));
+            s = __fadd_rn(s, __fmul_rn(v[u].z, qq[2]));
+            s = __fadd_rn(s, __fmul_rn(v[u].w, qq[3]));
+          }
+        }
       }
       tile[i] = desc_key(s, static_cast<uint32_t>(p));
     }
@@ -616,6 +662,9 @@ __device__ void scan_rows(const float* X, int d, const uint32_t* lists, int64_t 
 
 // grid (nprobe, nq): top-k of list probes[q][p] for query q.
 // cand[(q * nprobe + p) * topk + r] = key with tiebreak = position in list.
+// grid (nprobe, nq, parts): part z of the z-th probed list of query q; its
+// candidates are group p * parts + z, so the merge's (group, rank) order is
+// (probe rank, list position) as with one part per list
 __global__ void list_scan_kernel(const float* X, int d, const uint32_t* lists, const int64_t* offs,
                                  const int32_t* probes, int nprobe, const float* Q, int topk,
                                  unsigned long long* cand) {
@@ -630,14 +679,19 @@ __global__ void list_scan_kernel(const float* X, int d, const uint32_t* lists, c
   for (int i = threadIdx.x; i < topk; i += blockDim.x) best[i] = ~0ull;
   __syncthreads();
   const int c = probes[q * nprobe + p];
-  scan_rows<true>(X, d, lists, offs[c], offs[c + 1] - offs[c], qs, topk, best, tile, red);
+  const int parts = static_cast<int>(gridDim.z), z = static_cast<int>(blockIdx.z);
+  const int64_t len = offs[c + 1] - offs[c];
+  const int64_t per = (len + parts - 1) / parts;
+  const int64_t pb = per * z < len ? per * z : len;
+  const int64_t cnt = len - pb < per ? len - pb : per;
+  scan_rows<true>(X, d, lists, offs[c] + pb, cnt, qs, topk, best, tile, red);
   for (int i = threadIdx.x; i < topk; i += blockDim.x) {
     const unsigned long long kk = best[i];
-    // replace the list position by the row id (kept for the merge)
-    cand[(q * nprobe + p) * topk + i] =
+    // replace the position by the row id (kept for the merge)
+    cand[((q * nprobe + p) * parts + z) * topk + i] =
         kk == ~0ull ? ~0ull
                     : (kk & 0xffffffff00000000ull) |
-                          lists[offs[c] + static_cast<int64_t>(kk & 0xffffffffu)];
+                          lists[offs[c] + pb + static_cast<int64_t>(kk & 0xffffffffu)];
   }
 }
 
@@ -716,6 +770,12 @@ cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const 
 cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
                           cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
+  if (nq <= kSmallQ && d % 4 == 0 && static_cast<size_t>(nq) * d * sizeof(float) <= 48 * 1024 &&
+      (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+    scores_small_kernel<<<static_cast<unsigned>((k + 127) / 128), 128,
+                          static_cast<size_t>(nq) * d * sizeof(float), st>>>(Q, static_cast<int>(nq), C, k, d, S);
+    return cudaGetLastError();
+  }
   dim3 grid(static_cast<unsigned>((nq + SB - 1) / SB), static_cast<unsigned>((k + SB - 1) / SB));
   scores_kernel<<<grid, 256, 0, st>>>(Q, nq, C, k, d, S);
   return cudaGetLastError();
@@ -782,10 +842,11 @@ static size_t scan_smem(int d) { return (64 + 32 + 2048 + 64) * 8 + static_cast<
 
 cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
                              const int32_t* probes, int nprobe, const float* Q, int64_t nq, int topk,
-                             unsigned long long* cand, cudaStream_t st) {
+                             int parts, unsigned long long* cand, cudaStream_t st) {
+  if (parts < 1) return cudaErrorInvalidValue;
   const size_t sm = scan_smem(d);
   cudaFuncSetAttribute(list_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-  dim3 grid(nprobe, static_cast<unsigned>(nq));
+  dim3 grid(nprobe, static_cast<unsigned>(nq), static_cast<unsigned>(parts));
   list_scan_kernel<<<grid, 256, sm, st>>>(X, d, lists, offs, probes, nprobe, Q, topk, cand);
   return cudaGetLastError();
 }
