@@ -225,6 +225,29 @@ struct MlpLaunch {
   unsigned* status;
 };
 bool mlp_supported(int H, int F);
+
+// GEMMs of at most kSkinnyRows rows (ec_skinny.cu): out[m, n] =
+// epilogue(A[m, :] . W[n, :] + bias[n]), one warp per output column
+constexpr int kSkinnyRows = 16;
+enum SkinnyEpi : int {
+  kSkBf16 = 0,      // bf16 out = acc + bias
+  kSkGelu = 1,      // bf16 out = gelu(acc + bias)
+  kSkF32Resid = 2,  // fp32 out = (acc + bias) + resid (resid fp32, else resid_b bf16)
+};
+struct SkinnyLaunch {
+  const __nv_bfloat16* A;  // [M, lda]
+  int lda;
+  const __nv_bfloat16* W;  // [N, K]
+  int M, N, K;
+  const float* bias;              // [N] or nullptr
+  const float* resid;             // [M, ldr] or nullptr
+  const __nv_bfloat16* resid_b;   // [M, ldr] when resid is nullptr
+  int ldr;
+  void* out;                      // [M, ldo]
+  int ldo;
+  int epi;
+};
+cudaError_t launch_skinny_gemm(const SkinnyLaunch& s, cudaStream_t st);
 cudaError_t launch_mlp(const MlpLaunch& l, cudaStream_t st, int num_sms);
 
 // ---- attention (ec_attn.cu) --------------------------------------------------

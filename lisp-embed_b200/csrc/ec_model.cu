@@ -814,8 +814,36 @@ static int forward_packed(Device& d, const WsLayout& L, int T, int nseq, const A
       const int e0 = prof_begin(d);
       EC_TRY(rows(launch_embed_ln(e, st), "embed", TH * (8.0 + 6.0), e0));
     }
+    // a few rows (a query, a handful of short texts): the skinny GEMMs,
+    // weights spread over the whole GPU, and the LayerNorm row kernel
+    // (EC_NO_SKINNY: the tcgen05 GEMMs at every size)
+    const bool skinny = T <= kSkinnyRows && getenv("EC_NO_SKINNY") == nullptr;
+    auto sk = [&](const bf16* A, int lda, const bf16* W, int N, int K, const float* bias, int epi, void* o,
+                  int ldo) -> int {
+      SkinnyLaunch s{A, lda, W, T, N, K, bias, bf16_resid ? nullptr : h32, hb, H, o, ldo, epi};
+      const int e0 = prof_begin(d);
+      const cudaError_t e = launch_skinny_gemm(s, st);
+      prof_end(d, 0, 2.0 * T * N * K, 2.0 * T * K + 2.0 * N * K + (epi == kSkF32Resid ? 8.0 : 2.0) * T * N, e0);
+      trace_launch(d, "skinny gemm");
+      return check_cuda(e, "skinny gemm");
+    };
+    auto ln_rows = [&](const float* g, const float* b) -> int {
+      LnArgs l{tmp, g, b, h32, hb, T, H};
+      const int e0 = prof_begin(d);
+      return rows(launch_ln(l, st), "layernorm", TH * 10.0, e0);
+    };
     for (int li = 0; li < m.layers; ++li) {
       const BertLayerW& w = m.bl[li];
+      if (skinny) {
+        EC_TRY(sk(hb, H, w.wqkv, nqkv, H, w.bqkv, kSkBf16, qkv, nqkv));
+        EC_TRY(attention());
+        EC_TRY(sk(ctx, nctx, w.wo, H, nctx, w.bo, kSkF32Resid, tmp, H));
+        EC_TRY(ln_rows(w.ln1g, w.ln1b));
+        EC_TRY(sk(hb, H, w.wff, F, H, w.bff, kSkGelu, ff, F));
+        EC_TRY(sk(ff, F, w.wout, H, F, w.bout, kSkF32Resid, tmp, H));
+        EC_TRY(ln_rows(w.ln2g, w.ln2b));
+        continue;
+      }
       EC_TRY(gemm(hb, H, w.wqkv, nqkv, H, w.bqkv, nullptr, qkv, nqkv, kEpiBf16));
       EC_TRY(attention());
       if (fuse_ln) {

@@ -189,6 +189,26 @@ def test_batch_invariance_and_order(synth_root, ec):
     assert np.array_equal(full, again)  # deterministic
 
 
+# batches of at most 16 tokens run the skinny GEMMs + LayerNorm row kernel:
+# against the oracle, and against the tcgen05 path (EC_NO_SKINNY) on the
+# same batch; 16 tokens exactly, one token, several sequences
+@pytest.mark.parametrize("lengths", [[1], [10], [2, 3, 11], [16]])
+def test_skinny_small_batches(synth_root, ec, monkeypatch, lengths):
+    fam, cos = _check(synth.MINILM, 0, lengths, synth_root, ec, "minilm")
+    assert fam == "bert"
+    ids, offs = synth.make_short_inputs("minilm", lengths, 0, synth.MINILM.vocab)
+    got = model.embed_batch(ids, offs)
+    monkeypatch.setenv("EC_NO_SKINNY", "1")
+    tc = model.embed_batch(ids, offs)
+    assert _cos(got, tc).min() >= 0.9999
+
+
+def test_skinny_mpnet(synth_root, ec):
+    s = synth.with_layers(synth.MPNET_BASE, 2)
+    fam, _ = _check(s, 2, [4, 9], synth_root, ec, "mpnet")
+    assert fam == "mpnet"
+
+
 def test_graph_replay(synth_root, ec, monkeypatch):
     """Small host batches replay a captured CUDA graph of the forward: the
     replays (with other lengths captured in between, and new ids of the same
