@@ -13,6 +13,8 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cmath>
+#include <chrono>
+#include <climits>
 #include <cstring>
 #include <numeric>
 
@@ -1150,6 +1152,16 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
   ModelW& m = d.model;
   if (!m.family) return set_error(EC_ESTATE, "no model loaded");
   EC_TRY(check_cuda(cudaSetDevice(d.ordinal), "set device"));
+  // EC_TRACE_EMBED: host time of each phase of the call on stderr
+  static const bool trace = getenv("EC_TRACE_EMBED") != nullptr;
+  auto t_last = std::chrono::steady_clock::now();
+  auto tmark = [&](const char* what) {
+    if (!trace) return;
+    const auto now = std::chrono::steady_clock::now();
+    fprintf(stderr, "[ec embed dev %d] %s %.3f ms\n", d.ordinal, what,
+            std::chrono::duration<double, std::milli>(now - t_last).count());
+    t_last = now;
+  };
   // validate lengths and ids (host ids only; device ids are trusted)
   const int maxlen = m.family == EC_FAMILY_LLAMA ? m.max_pos : m.max_pos - m.pos_offset;
   for (int s : seqs) {
@@ -1160,12 +1172,22 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
                        s, static_cast<long long>(L), maxlen);
     if (m.family == EC_FAMILY_MPNET && L > 512)
       return set_error(EC_EUNSUPPORTED, "MPNet sequence %d longer than 512 tokens", s);
-    if (ids_host)
-      for (int64_t t = offsets[s]; t < offsets[s + 1]; ++t)
-        if (ids_host[t] < 0 || ids_host[t] >= m.vocab)
-          return set_error(EC_EINVAL, "token id %d of sequence %d outside vocab %d", ids_host[t],
-                           s, m.vocab);
+    if (ids_host) {
+      // min / max over the sequence's ids (a vectorisable pass); the slow
+      // search for the message only when one is out of range
+      int32_t lo = INT32_MAX, hi = INT32_MIN;
+      for (int64_t t = offsets[s]; t < offsets[s + 1]; ++t) {
+        lo = std::min(lo, ids_host[t]);
+        hi = std::max(hi, ids_host[t]);
+      }
+      if (lo < 0 || hi >= m.vocab)
+        for (int64_t t = offsets[s]; t < offsets[s + 1]; ++t)
+          if (ids_host[t] < 0 || ids_host[t] >= m.vocab)
+            return set_error(EC_EINVAL, "token id %d of sequence %d outside vocab %d", ids_host[t],
+                             s, m.vocab);
+    }
   }
+  tmark("validate");
   size_t i = 0;
   while (i < seqs.size()) {
     // chunk: as many sequences as fit the token budget (at least one)
@@ -1196,7 +1218,15 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     const size_t obytes = static_cast<size_t>(nseq) * m.out_dim * 4;
     float* hout = reinterpret_cast<float*>(static_cast<char*>(d.pin) + d.pin_bytes -
                                            al256(static_cast<size_t>(T) * 4) - 256 - al256(obytes));
-    if (ids_host) {
+    // consecutive sequences: their ids and output rows are contiguous in
+    // the caller's arrays, which the copies then use directly
+    bool contig = true;
+    for (int k = 1; k < nseq && contig; ++k) contig = seqs[i + k] == seqs[i + k - 1] + 1;
+    const bool graph = ids_host && !out_dev && j - i == seqs.size() && T <= kGraphMaxTokens &&
+                       !G().profile && !G().sync_each && getenv("EC_NO_GRAPH") == nullptr;
+    const bool direct = contig && !graph;
+    const bool direct_out = direct && !out_dev && out_stride == m.out_dim;
+    if (ids_host && !direct) {
       int64_t o = 0;
       for (int k = 0; k < nseq; ++k) {
         const int s = seqs[i + k];
@@ -1220,23 +1250,23 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
                                           d.stream),
                           "ids copy"));
       } else {
-        EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, hid, static_cast<size_t>(T) * 4,
-                                          cudaMemcpyHostToDevice, d.stream),
+        EC_TRY(check_cuda(cudaMemcpyAsync(ws + L.ids, direct ? ids_host + offsets[seqs[i]] : hid,
+                                          static_cast<size_t>(T) * 4, cudaMemcpyHostToDevice, d.stream),
                           "ids upload"));
       }
       EC_TRY(forward_packed(d, L, static_cast<int>(T), nseq, tb, pairs, dout, ostride));
       if (!out_dev)
-        EC_TRY(check_cuda(cudaMemcpyAsync(hout, dout, obytes, cudaMemcpyDeviceToHost, d.stream),
+        EC_TRY(check_cuda(cudaMemcpyAsync(direct_out ? out_host + static_cast<size_t>(seqs[i]) * out_stride : hout,
+                                          dout, obytes, cudaMemcpyDeviceToHost, d.stream),
                           "output download"));
       return EC_OK;
     };
     fill_tables(d, lens, &tb);
+    tmark("staging (ids, tables)");
     // Small host batches (query serving) replay a CUDA graph of the whole
     // chunk, captured at the first batch with these lengths on this
     // workspace: one launch in place of ~30, the host writes only the pinned
     // tables and ids.  Not while profiling or checking every launch.
-    const bool graph = ids_host && !out_dev && j - i == seqs.size() && T <= kGraphMaxTokens &&
-                       !G().profile && !G().sync_each && getenv("EC_NO_GRAPH") == nullptr;
     Device::FwdGraph* g = nullptr;
     if (graph) {
       for (auto& e : d.graphs)
@@ -1275,12 +1305,15 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
     } else {
       EC_TRY(enqueue());
     }
+    tmark(g ? "graph launch" : "enqueue");
     EC_TRY(sync_and_check(d, "forward"));
+    tmark("device (wait)");
     prof_collect(d);
-    if (!out_dev)
+    if (!out_dev && !direct_out)
       for (int k = 0; k < nseq; ++k)
         std::memcpy(out_host + static_cast<size_t>(seqs[i + k]) * out_stride,
                     hout + static_cast<size_t>(k) * m.out_dim, static_cast<size_t>(m.out_dim) * 4);
+    tmark("copy out");
     i = j;
   }
   return EC_OK;
