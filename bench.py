@@ -504,8 +504,9 @@ def ivf_build_measure(R, x, perm):
     init = the first k rows of a seeded permutation, ann.lisp:83-86) with the
     rows sharded over the ranks in sample order (the sums chained from rank
     to rank over NCCL, so the centroids equal one device's bit for bit), then
-    the inverted lists of each shard (ann::assign-all).  Inputs start in host
-    memory; the timed region includes their upload.  Returns (rank 0's dict,
+    the inverted lists of each shard (ann::assign-all), both in one
+    ec_ann_build call.  Inputs start in host memory; the timed region
+    includes their upload.  Returns (rank 0's dict,
     centroids)."""
     import ctypes as C
     import torch
@@ -527,17 +528,17 @@ def ivf_build_measure(R, x, perm):
         _lib.check(L.ec_comm_init(R.rank, R.world, C.create_string_buffer(raw, idn)), "comm init")
         R.comm_ready = True
     local_sample = np.arange(len(x_local), dtype=np.int64)
-    # warm-up: one iteration on a slice (module load, NCCL channels)
-    ann.kmeans(x_local[:200000], local_sample[:200000], IVF_K, 1, init=init)
+    # warm-up: the same build with one iteration (module load, NCCL channels,
+    # and the first device allocations of these sizes, whose cost varied from
+    # milliseconds to ~1 s between processes on the same box)
+    ann.build(x_local, local_sample, IVF_K, 1, init=init)
     torch.cuda.synchronize()
     R.barrier()
     L.ecdbg_profile(1)
     L.ecdbg_assign_rows(None, None, 1)
     with ClockSampler(R.smi_index) as clk:
         t0 = time.perf_counter()
-        cent = ann.kmeans(x_local, local_sample, IVF_K, IVF_ITERS, init=init)
-        t_km = time.perf_counter() - t0
-        counts, lists = ann.assign_all(x_local, cent)
+        cent, counts, lists = ann.build(x_local, local_sample, IVF_K, IVF_ITERS, init=init)
         t_all = time.perf_counter() - t0
     v = [C.c_double(), C.c_double(), C.c_double(), C.c_longlong()]
     L.ecdbg_profile_read(b"gemm", *[C.byref(z) for z in v])
@@ -547,7 +548,7 @@ def ivf_build_measure(R, x, perm):
     L.ecdbg_profile(0)
     tc_rows, ex_rows = C.c_longlong(), C.c_longlong()
     L.ecdbg_assign_rows(C.byref(tc_rows), C.byref(ex_rows), 0)
-    t_km, t_all = R.max(t_km, t_all)
+    t_all = R.max(t_all)
     if R.rank != 0:
         return None, cent
     peaks, src = measured_peaks()
@@ -561,7 +562,7 @@ def ivf_build_measure(R, x, perm):
                       "parallelism": f"rows sharded over {R.world} GPU(s) in sample order",
                       "exchange": "per-cluster sums chained rank to rank (NCCL send/recv), "
                                   "centroids broadcast" if R.world > 1 else "none"},
-           "kmeans_s": t_km, "assign_all_s": t_all - t_km,
+           "api": "ec_ann_build (kmeans + assign-all, rows uploaded once)",
            "achieved_tflops": flops / t_all / 1e12,
            "roofline": {"bound": "tensor",
                         "kernel": "gemm_tn_bf16_kernel<256, kEpiArgCand> (assignment scores, rank 0)",
@@ -878,8 +879,7 @@ def run_search(args, rank, local_rank):
     torch.cuda.empty_cache()
     perm = perm.cpu().numpy().astype(np.int64)
     _lib.init([local_rank])
-    cent = ann.kmeans(x, perm, k, IVF_ITERS)
-    counts, lists = ann.assign_all(x, cent)
+    cent, counts, lists = ann.build(x, perm, k, IVF_ITERS)
     kb.load_index(x, (cent, counts, lists))
     L = _lib.lib()
     for _ in range(args.warmup):

@@ -125,6 +125,16 @@ int ec_kmeans(const float *x, int64_t n, int d, const int64_t *sample, int64_t n
 int ec_assign_all(const float *x, int64_t n, int d, const float *centroids, int k,
                   uint32_t *counts, uint32_t *lists);
 
+/* ec_kmeans followed by ec_assign_all with its centroids, as ann:run does
+ * (ann.lisp:193-197): the same arguments and results as the two calls, but
+ * on one device the rows cross to it once (the sample's rows are gathered
+ * from that copy on the device, and the final assignment reuses it).  With
+ * several devices in the process it makes the two calls.  Replaces the
+ * kmeans + assign-all pair of ann:run (ann.lisp:189-200). */
+int ec_ann_build(const float *x, int64_t n, int d, const int64_t *sample, int64_t nsample,
+                 int k, int iters, const float *init, float *centroids, uint32_t *counts,
+                 uint32_t *lists);
+
 /* One assignment pass with explicit centroids: assign[i] = nearest centroid
  * of x[rows[i]] (rows NULL: row i).  Replaces the assign step of ann::kmeans
  * (ann.lisp:90-105). */

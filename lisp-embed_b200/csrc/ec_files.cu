@@ -169,9 +169,10 @@ int ec_ann_build_file(const char* index_path, int d, int k, int iters, const int
   if ((rc = index_rows(m, d, index_path, &n))) return rc;
   const float* x = static_cast<const float*>(m.p);
   std::vector<float> cent(static_cast<size_t>(k) * d);
-  if ((rc = ec_kmeans(x, n, d, sample, nsample, k, iters, nullptr, cent.data()))) return rc;
   std::vector<uint32_t> counts(k), lists(static_cast<size_t>(n));
-  if ((rc = ec_assign_all(x, n, d, cent.data(), k, counts.data(), lists.data()))) return rc;
+  rc = ec_ann_build(x, n, d, sample, nsample, k, iters, nullptr, cent.data(), counts.data(),
+                    lists.data());
+  if (rc) return rc;
   return ec_ann_save(ann_path, cent.data(), k, d, n, counts.data(), lists.data());
 }
 

@@ -205,9 +205,13 @@ enum KmeansExchange { kKmSingle = 0, kKmChain = 1, kKmAllReduce = 2 };
 // kKmChain: the per-cluster sums continue from the previous rank's (rank
 // order = sample order), so every add follows ann.lisp:107-122's serial
 // loop; the last rank divides and broadcasts the centroids.
+// x_dev: the caller's n rows already on this device (the one-upload build);
+// the training rows are then a slice of it or gathered from it on the device.
+// On return *rows_dev is the device copy of the training rows.
 static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t* sample,
                          int64_t j0, int64_t j1, int k, int iters, const float* cent0,
-                         float* cent_out, KmeansExchange mode, KmeansDev& w) {
+                         float* cent_out, KmeansExchange mode, KmeansDev& w,
+                         const float* x_dev = nullptr, const float** rows_dev = nullptr) {
   Device& dv = *G().devs[li];
   EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
   const int64_t ns = j1 - j0;
@@ -227,7 +231,7 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   for (int64_t j = 1; run && j < ns; ++j) run = sample[j0 + j] == sample[j0] + j;
   std::vector<float> xs;
   const float* src = run ? x + sample[j0] * d : nullptr;
-  if (!run) {
+  if (!run && !x_dev) {
     xs.resize(static_cast<size_t>(std::max<int64_t>(ns, 1)) * d);
     for (int64_t j = 0; j < ns; ++j)
       std::memcpy(&xs[static_cast<size_t>(j) * d], x + sample[j0 + j] * d, static_cast<size_t>(d) * 4);
@@ -237,7 +241,15 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   phase("gather");
   const int64_t nt = sort_tiles(ns);
   const size_t nsum = static_cast<size_t>(k) * (d + 1);
-  EC_TRY(w.bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * d * 4, "kmeans rows"));
+  // X: the training rows on the device, in sample order
+  const float* X = nullptr;
+  if (x_dev && run) {
+    X = x_dev + sample[j0] * d;
+  } else {
+    EC_TRY(w.bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * d * 4, "kmeans rows"));
+    X = w.bx.as<float>();
+  }
+  if (rows_dev) *rows_dev = X;
   EC_TRY(w.bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
   EC_TRY(w.ba.alloc(dv, static_cast<size_t>(std::max<int64_t>(ns, 1)) * 4, "assignments"));
   EC_TRY(w.bh.alloc(dv, static_cast<size_t>(std::max<int64_t>(nt, 1)) * k * 4, "sort scratch"));
@@ -247,20 +259,34 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
   EC_TRY(w.bs.alloc(dv, nsum * 4, "sums"));
   if (mode == kKmChain) EC_TRY(w.bprev.alloc(dv, nsum * 4, "previous ranks' sums"));
   cudaStream_t st = dv.stream;
-  if (ns > 0) EC_TRY(upload_h2d(dv, w.bx.p, src, static_cast<size_t>(ns) * d * 4, "rows upload"));
+  if (x_dev) {
+    if (ns > 0 && !run) {
+      // the sample's rows gathered from the resident copy (indices checked
+      // against n by the caller)
+      DBuf bi;
+      EC_TRY(bi.alloc(dv, static_cast<size_t>(ns) * 8, "sample indices"));
+      EC_TRY(check_cuda(cudaMemcpyAsync(bi.p, sample + j0, static_cast<size_t>(ns) * 8,
+                                        cudaMemcpyHostToDevice, st), "sample upload"));
+      EC_TRY(check_cuda(launch_gather_rows(x_dev, bi.as<int64_t>(), ns, d, w.bx.as<float>(),
+                                           dv.num_sms, st), "sample gather"));
+      EC_TRY(check_cuda(cudaStreamSynchronize(st), "sample gather"));
+    }
+  } else if (ns > 0) {
+    EC_TRY(upload_h2d(dv, w.bx.p, src, static_cast<size_t>(ns) * d * 4, "rows upload"));
+  }
   EC_TRY(check_cuda(cudaMemcpyAsync(w.bc.p, cent0, static_cast<size_t>(k) * d * 4,
                                     cudaMemcpyHostToDevice, st), "centroid upload"));
   phase("alloc + upload");
-  if (ns > 0) EC_TRY(tc_assign_setup(dv, w.tc, w.bx.as<float>(), ns, d, k, st));
+  if (ns > 0) EC_TRY(tc_assign_setup(dv, w.tc, X, ns, d, k, st));
   phase("assign setup");
   const int rank = comm_rank(li), world = comm_world();
   if (mode != kKmSingle) EC_TRY(comm_rendezvous(li, static_cast<int>(G().devs.size())));
   for (int it = 0; it < iters; ++it) {
     if (ns > 0) {
       if (w.tc.ready) {
-        EC_TRY(tc_assign_run(dv, w.tc, w.bx.as<float>(), w.bc.as<float>(), w.ba.as<int32_t>(), st));
+        EC_TRY(tc_assign_run(dv, w.tc, X, w.bc.as<float>(), w.ba.as<int32_t>(), st));
       } else {
-        EC_TRY(check_cuda(launch_assign(w.bx.as<float>(), nullptr, ns, w.bc.as<float>(), k, d,
+        EC_TRY(check_cuda(launch_assign(X, nullptr, ns, w.bc.as<float>(), k, d,
                                         w.ba.as<int32_t>(), st), "assign"));
       }
     }
@@ -270,7 +296,7 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
       // sums of ranks 0..rank-1 arrive from rank-1; this shard's rows
       // continue them; the next rank continues from here
       if (rank > 0) EC_TRY(comm_recv_f32(li, w.bprev.as<float>(), nsum, rank - 1, st));
-      EC_TRY(check_cuda(launch_segsum(w.bx.as<float>(), w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
+      EC_TRY(check_cuda(launch_segsum(X, w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
                                       rank > 0 ? w.bprev.as<float>() : nullptr, w.bs.as<float>(), st),
                         "sums"));
       if (rank + 1 < world) {
@@ -280,7 +306,7 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
       }
       EC_TRY(comm_bcast_f32(li, w.bc.as<float>(), static_cast<size_t>(k) * d, world - 1, st));
     } else {
-      EC_TRY(check_cuda(launch_segsum(w.bx.as<float>(), w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
+      EC_TRY(check_cuda(launch_segsum(X, w.bl.as<uint32_t>(), w.boffs.as<int64_t>(), k, d,
                                       nullptr, w.bs.as<float>(), st),
                         "sums"));
       if (mode == kKmAllReduce) EC_TRY(comm_allreduce_sum_f32(li, w.bs.as<float>(), nsum, st));
@@ -295,6 +321,10 @@ static int kmeans_device(int li, const float* x, int64_t n, int d, const int64_t
 }
 
 // ---------------------------------------------------------------- assign --
+static int assign_resident(Device& dv, const float* X, int64_t m, int64_t r0, int d, const float* C,
+                           int k, TcAssign* tc, int32_t* assign_out, uint32_t* counts_out,
+                           int64_t* offs_out, uint32_t* lists_out);
+
 static int assign_device(int li, const float* x, int64_t r0, int64_t r1, int d, const int64_t* rows,
                          const float* cent, int k, int32_t* assign_out, uint32_t* counts_out,
                          int64_t* offs_out, uint32_t* lists_out) {
@@ -314,23 +344,36 @@ static int assign_device(int li, const float* x, int64_t r0, int64_t r1, int d, 
       std::memcpy(&xs[static_cast<size_t>(j) * d], x + rows[r0 + j] * d, static_cast<size_t>(d) * 4);
     src = xs.data();
   }
-  DBuf bx, bc, ba;
+  DBuf bx, bc;
   EC_TRY(bx.alloc(dv, static_cast<size_t>(m) * d * 4, "rows"));
   EC_TRY(bc.alloc(dv, static_cast<size_t>(k) * d * 4, "centroids"));
-  EC_TRY(ba.alloc(dv, static_cast<size_t>(m) * 4, "assignments"));
-  cudaStream_t st = dv.stream;
   EC_TRY(upload_h2d(dv, bx.p, src, static_cast<size_t>(m) * d * 4, "rows upload"));
-  EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice, st),
+  EC_TRY(check_cuda(cudaMemcpyAsync(bc.p, cent, static_cast<size_t>(k) * d * 4, cudaMemcpyHostToDevice,
+                                    dv.stream),
                     "centroid upload"));
+  return assign_resident(dv, bx.as<float>(), m, r0, d, bc.as<float>(), k, nullptr, assign_out,
+                         counts_out, offs_out, lists_out);
+}
+
+// ann::nearest-centroid of m rows already on the device (X; row j is the
+// caller's row r0 + j) against centroids C on the device: assignments
+// downloaded to assign_out + r0 and/or inverted lists (ann::assign-all,
+// ids r0 + j) to counts_out / offs_out / lists_out.  tc: the tensor-core
+// state of an earlier pass over the same X (k-means), reused when ready.
+static int assign_resident(Device& dv, const float* X, int64_t m, int64_t r0, int d, const float* C,
+                           int k, TcAssign* tc, int32_t* assign_out, uint32_t* counts_out,
+                           int64_t* offs_out, uint32_t* lists_out) {
+  cudaStream_t st = dv.stream;
+  DBuf ba;
+  EC_TRY(ba.alloc(dv, static_cast<size_t>(m) * 4, "assignments"));
   {
-    TcAssign tc;
-    EC_TRY(tc_assign_setup(dv, tc, bx.as<float>(), m, d, k, st));
-    if (tc.ready) {
-      EC_TRY(tc_assign_run(dv, tc, bx.as<float>(), bc.as<float>(), ba.as<int32_t>(), st));
+    TcAssign own;
+    TcAssign* t = (tc && tc->ready && tc->n == m && tc->d == d && tc->k == k) ? tc : &own;
+    if (t == &own) EC_TRY(tc_assign_setup(dv, own, X, m, d, k, st));
+    if (t->ready) {
+      EC_TRY(tc_assign_run(dv, *t, X, C, ba.as<int32_t>(), st));
     } else {
-      EC_TRY(check_cuda(launch_assign(bx.as<float>(), nullptr, m, bc.as<float>(), k, d,
-                                      ba.as<int32_t>(), st),
-                        "assign"));
+      EC_TRY(check_cuda(launch_assign(X, nullptr, m, C, k, d, ba.as<int32_t>(), st), "assign"));
     }
   }
   if (assign_out)
@@ -587,13 +630,14 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
 
 using namespace ec;
 
-extern "C" {
-
-int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t nsample, int k,
-              int iters, const float* init, float* centroids) {
-  std::lock_guard<std::mutex> lk(G().mu);
-  clear_error();
-  EC_TRY(check_common(n, d, k));
+// ec_kmeans without the lock.  x_dev: the caller's rows already on the one
+// device (then the training rows are a slice of it or gathered from it);
+// post(li, w, X) runs on each device after its iterations, with the k-means
+// buffers still alive (X = the device's training rows, w.bc = the final
+// centroids).
+template <class Post>
+static int kmeans_impl(const float* x, int64_t n, int d, const int64_t* sample, int64_t nsample, int k,
+                       int iters, const float* init, float* centroids, const float* x_dev, Post post) {
   if (!x || !sample || !centroids || iters < 0 || nsample < 0)
     return set_error(EC_EINVAL, "bad kmeans arguments");
   for (int64_t j = 0; j < nsample; ++j)
@@ -619,8 +663,10 @@ int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t n
   const int rc = on_devices(nd, [&](int li) {
     int64_t j0, j1;
     split(nsample, nd, li, &j0, &j1);
-    const int r = kmeans_device(li, x, n, d, sample, j0, j1, k, iters, c0.data(),
-                                li == 0 ? centroids : nullptr, mode, work[li]);
+    const float* X = nullptr;
+    int r = kmeans_device(li, x, n, d, sample, j0, j1, k, iters, c0.data(),
+                          li == 0 ? centroids : nullptr, mode, work[li], x_dev, &X);
+    if (!r) r = post(li, work[li], X);
     if (r && multi) comm_mark_failed();  // the other ranks stop waiting on this one
     return r;
   });
@@ -631,6 +677,17 @@ int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t n
     return set_error(rc, "%s", msg.c_str());
   }
   return rc;
+}
+
+extern "C" {
+
+int ec_kmeans(const float* x, int64_t n, int d, const int64_t* sample, int64_t nsample, int k,
+              int iters, const float* init, float* centroids) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  return kmeans_impl(x, n, d, sample, nsample, k, iters, init, centroids, nullptr,
+                     [](int, KmeansDev&, const float*) { return EC_OK; });
 }
 
 int ec_assign(const float* x, int64_t n, int d, const int64_t* rows, int64_t nrows,
@@ -651,11 +708,9 @@ int ec_assign(const float* x, int64_t n, int d, const int64_t* rows, int64_t nro
   });
 }
 
-int ec_assign_all(const float* x, int64_t n, int d, const float* centroids, int k, uint32_t* counts,
-                  uint32_t* lists) {
-  std::lock_guard<std::mutex> lk(G().mu);
-  clear_error();
-  EC_TRY(check_common(n, d, k));
+// ec_assign_all without the lock
+static int assign_all_impl(const float* x, int64_t n, int d, const float* centroids, int k,
+                           uint32_t* counts, uint32_t* lists) {
   if (!x || !centroids || !counts || !lists) return set_error(EC_EINVAL, "bad assign-all arguments");
   const int nd = static_cast<int>(G().devs.size());
   if (nd == 1) {
@@ -689,6 +744,62 @@ int ec_assign_all(const float* x, int64_t n, int d, const float* centroids, int 
     counts[c] = tot;
   }
   return EC_OK;
+}
+
+int ec_assign_all(const float* x, int64_t n, int d, const float* centroids, int k, uint32_t* counts,
+                  uint32_t* lists) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  return assign_all_impl(x, n, d, centroids, k, counts, lists);
+}
+
+int ec_ann_build(const float* x, int64_t n, int d, const int64_t* sample, int64_t nsample, int k,
+                 int iters, const float* init, float* centroids, uint32_t* counts, uint32_t* lists) {
+  std::lock_guard<std::mutex> lk(G().mu);
+  clear_error();
+  EC_TRY(check_common(n, d, k));
+  if (!x || !centroids || !counts || !lists) return set_error(EC_EINVAL, "bad ann build arguments");
+  const int nd = static_cast<int>(G().devs.size());
+  if (nd > 1) {
+    // several devices in this process: the two passes, each split over them
+    EC_TRY(kmeans_impl(x, n, d, sample, nsample, k, iters, init, centroids, nullptr,
+                       [](int, KmeansDev&, const float*) { return EC_OK; }));
+    return assign_all_impl(x, n, d, centroids, k, counts, lists);
+  }
+  // one device: the rows go up once; k-means trains on them (a slice, or
+  // the sample gathered on the device) and the final assignment reads the
+  // same copy, with the k-means pass's bf16 rows when it covered them all
+  Device& dv = *G().devs[0];
+  EC_TRY(check_cuda(cudaSetDevice(dv.ordinal), "cudaSetDevice"));
+  const bool trace = getenv("EC_TRACE_IVF") != nullptr;
+  auto t_last = std::chrono::steady_clock::now();
+  auto phase = [&](const char* what) {
+    if (!trace) return;
+    const auto now = std::chrono::steady_clock::now();
+    fprintf(stderr, "[ec ann build dev %d] %s %.1f ms\n", dv.ordinal, what,
+            std::chrono::duration<double, std::milli>(now - t_last).count());
+    t_last = now;
+  };
+  DBuf bx;
+  EC_TRY(bx.alloc(dv, static_cast<size_t>(std::max<int64_t>(n, 1)) * d * 4, "rows"));
+  phase("alloc");
+  if (n > 0) EC_TRY(upload_h2d(dv, bx.p, x, static_cast<size_t>(n) * d * 4, "rows upload"));
+  phase("rows upload");
+  std::vector<int64_t> offs(static_cast<size_t>(k) + 1);
+  return kmeans_impl(x, n, d, sample, nsample, k, iters, init, centroids, bx.as<float>(),
+                     [&](int, KmeansDev& w, const float* X) {
+                       phase("k-means");
+                       if (n == 0) {
+                         std::fill(counts, counts + k, 0u);
+                         return static_cast<int>(EC_OK);
+                       }
+                       TcAssign* tc = X == bx.as<float>() ? &w.tc : nullptr;
+                       const int r = assign_resident(dv, bx.as<float>(), n, 0, d, w.bc.as<float>(), k,
+                                                     tc, nullptr, counts, offs.data(), lists);
+                       phase("assign-all");
+                       return r;
+                     });
 }
 
 int ec_index_load(const float* x, int64_t n, int d, const float* centroids, int k,

@@ -72,6 +72,10 @@ cudaError_t launch_argcand_reduce(const float* X, int64_t n, int d, const float*
                                   const float* mloc, const int* meta, const int* col1,
                                   const int* col2, int32_t* out, int64_t* fb_rows,
                                   unsigned long long* fb_count, cudaStream_t st);
+// out[j] = X[rows[j]] for j < m (rows of d floats, d % 4 == 0; the caller
+// checks every index against X's rows)
+cudaError_t launch_gather_rows(const float* X, const int64_t* rows, int64_t m, int d, float* out,
+                               int num_sms, cudaStream_t st);
 // out[fb_rows[i]] = vals[i]
 cudaError_t launch_scatter_assign(const int64_t* fb_rows, int64_t nfb, const int32_t* vals,
                                   int32_t* out, cudaStream_t st);

@@ -177,6 +177,20 @@ __global__ void scatter_assign_kernel(const int64_t* fb_rows, int64_t nfb, const
   if (i < nfb) out[fb_rows[i]] = vals[i];
 }
 
+// out[j] = X[rows[j]] for j < m, one warp per row in 16-byte pieces; grid
+// stride over the rows
+__global__ void gather_rows_kernel(const float* __restrict__ X, const int64_t* __restrict__ rows,
+                                   int64_t m, int d4, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); j < m;
+       j += warps) {
+    const float4* src = reinterpret_cast<const float4*>(X) + rows[j] * d4;
+    float4* dst = reinterpret_cast<float4*>(out) + j * d4;
+    for (int c = lane; c < d4; c += 32) dst[c] = __ldcs(src + c);
+  }
+}
+
 }  // namespace
 
 float argcand_rel(int d) {
@@ -202,6 +216,17 @@ cudaError_t launch_argcand_reduce(const float* X, int64_t n, int d,
   const int64_t blocks = (n + kRedRows - 1) / kRedRows;
   argcand_reduce_kernel<<<static_cast<unsigned>(blocks), kRedRows, 0, st>>>(
       X, n, d, C, xnorm, cmax, rel2, parts, mloc, meta, col1, col2, out, fb_rows, fb_count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const float* X, const int64_t* rows, int64_t m, int d, float* out,
+                               int num_sms, cudaStream_t st) {
+  if (m <= 0) return cudaSuccess;
+  if (d % 4) return cudaErrorInvalidValue;
+  const int64_t want = (m + 7) / 8;  // eight warps per CTA, one row each
+  const int64_t cap = static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * 8;
+  gather_rows_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, st>>>(X, rows, m, d / 4,
+                                                                                      out);
   return cudaGetLastError();
 }
 

@@ -179,7 +179,7 @@ static int load_bert(Device& d, const JVal& cfg, const std::string& mt, int pool
   if (m.H % 128 || m.H > 1024 || m.F % 64)
     return set_error(EC_EUNSUPPORTED, "hidden %d / ffn %d outside this build", m.H, m.F);
   const int H = m.H, F = m.F;
-  const Tensor *w, *p, *ty = nullptr, *g, *b;
+  const Tensor *w = nullptr, *p = nullptr, *ty = nullptr, *g = nullptr, *b = nullptr;
   if ((rc = need_t(d, "embeddings.word_embeddings.weight", &w, {})) ||
       (rc = need_t(d, "embeddings.position_embeddings.weight", &p, {})) ||
       (rc = need_t(d, "embeddings.LayerNorm.weight", &g, {H})) ||
@@ -202,8 +202,9 @@ static int load_bert(Device& d, const JVal& cfg, const std::string& mt, int pool
   }
   if ((rc = as_f32(d, g, &m.emb_g)) || (rc = as_f32(d, b, &m.emb_b))) return rc;
   if (mpnet) {
-    const Tensor* rb;
-    if ((rc = need_t(d, "encoder.relative_attention_bias.weight", &rb, {32, m.heads}))) return rc;
+    const Tensor* rb = nullptr;
+    rc = need_t(d, "encoder.relative_attention_bias.weight", &rb, {32, m.heads});
+    if (rc) return rc;
     // table over i - j in [-(rel_max-1), rel_max-1], pre-multiplied by log2(e)
     m.rel_max = 1024;
     const int nb = 2 * m.rel_max - 1;

@@ -56,6 +56,8 @@ _SIGS = {
     "ec_embed_batch_device": (C.c_int, [P, I64P, C.c_int, P, C.c_int, P]),
     "ec_kmeans": (C.c_int, [FP, C.c_int64, C.c_int, I64P, C.c_int64, C.c_int, C.c_int, FP, FP]),
     "ec_assign_all": (C.c_int, [FP, C.c_int64, C.c_int, FP, C.c_int, U32P, U32P]),
+    "ec_ann_build": (C.c_int, [FP, C.c_int64, C.c_int, I64P, C.c_int64, C.c_int, C.c_int, FP, FP,
+                               U32P, U32P]),
     "ec_assign": (C.c_int, [FP, C.c_int64, C.c_int, I64P, C.c_int64, FP, C.c_int, I32P]),
     "ec_index_load": (C.c_int, [FP, C.c_int64, C.c_int, FP, C.c_int, U32P, U32P]),
     "ec_ivf_search": (C.c_int, [FP, C.c_int, C.c_int, C.c_int, I64P, FP]),

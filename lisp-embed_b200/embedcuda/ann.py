@@ -1,8 +1,9 @@
 """IVF index build -- the ann.lisp mirror (ann.lisp:1-200).
 
-``kmeans`` (ann::kmeans), ``assign_all`` (ann::assign-all), ``save_ann`` /
-``load_ann`` (the ann.bin format of ann.lisp:4-6, 165-187), ``run`` and
-``build_file`` (ann:run from index.bin to ann.bin in the library).
+``kmeans`` (ann::kmeans), ``assign_all`` (ann::assign-all), ``build`` (both
+in one call), ``save_ann`` / ``load_ann`` (the ann.bin format of
+ann.lisp:4-6, 165-187), ``run`` and ``build_file`` (ann:run from index.bin
+to ann.bin in the library).
 The arithmetic runs in libembedcuda.so; ``sample`` is the explicit list of
 training rows whose first k rows initialise the centroids (ann.lisp:83-86).
 """
@@ -68,6 +69,27 @@ def assign_all(vecs, centroids):
     return counts, lists
 
 
+def build(vecs, sample, k, iters, init=None):
+    """kmeans(vecs, sample, k, iters, init) then assign_all with its
+    centroids, in one library call (ec_ann_build: on one device the rows
+    cross to it once).  Returns (centroids, counts, lists)."""
+    vecs = np.ascontiguousarray(vecs, np.float32)
+    sample = np.ascontiguousarray(sample, np.int64)
+    n, d = vecs.shape
+    cent = np.empty((k, d), np.float32)
+    counts = np.empty(k, np.uint32)
+    lists = np.empty(n, np.uint32)
+    init_p = None
+    if init is not None:
+        init = np.ascontiguousarray(init, np.float32)
+        init_p = _lib.ptr(init, C.c_float)
+    _lib.check(_lib.lib().ec_ann_build(_lib.ptr(vecs, C.c_float), n, d, _lib.ptr(sample, C.c_int64),
+                                       sample.size, k, iters, init_p, _lib.ptr(cent, C.c_float),
+                                       _lib.ptr(counts, C.c_uint32), _lib.ptr(lists, C.c_uint32)),
+               "ann_build")
+    return cent, counts, lists
+
+
 def save_ann(path, centroids, counts, lists, n):
     """ann.bin: u32 magic, k, dim, n; k*dim f32; k u32 counts; n u32 ids
     (ann::save-ann, ann.lisp:165-187), written by ec_ann_save."""
@@ -118,8 +140,7 @@ def run(vecs, k=1024, iters=10, sample=None, seed=None, out_path=None):
     if sample is None:
         rng = np.random.default_rng(seed)
         sample = rng.choice(n, size=min(100000, n), replace=False)
-    cent = kmeans(vecs, sample, k, iters)
-    counts, lists = assign_all(vecs, cent)
+    cent, counts, lists = build(vecs, sample, k, iters)
     if out_path:
         save_ann(out_path, cent, counts, lists, n)
     return cent, counts, lists

@@ -10,6 +10,7 @@
 ;;;;   (cuda:load-tokenizer "tokenizer.json") (cuda:embed-texts list-of-strings)
 ;;;;   (cuda:kmeans vecs sample k iters)  ; ann::kmeans
 ;;;;   (cuda:assign-all vecs n centroids k)
+;;;;   (cuda:ann-build vecs sample k iters) ; kmeans + assign-all, rows sent once
 ;;;;   (cuda:index-load vecs n centroids counts lists)
 ;;;;   (cuda:index-load-files "index.bin" :ann-path "ann.bin" :dim 384)
 ;;;;   (cuda:ann-build-file "index.bin" "ann.bin" sample k iters)  ; ann:run
@@ -25,7 +26,7 @@
   (:use :cl)
   (:export #:init #:available-p #:load-model #:dim #:embed-ids #:embed-batch
            #:load-tokenizer #:embed-texts
-           #:kmeans #:assign-all #:index-load #:index-load-files #:ann-build-file
+           #:kmeans #:assign-all #:ann-build #:index-load #:index-load-files #:ann-build-file
            #:top-k #:top-k-brute #:top-k-batch #:*nprobe*
            #:attach-kb #:kb-search))
 (in-package :cuda)
@@ -59,6 +60,11 @@
 (sb-alien:define-alien-routine ("ec_assign_all" %assign-all) sb-alien:int
   (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
   (centroids sb-sys:system-area-pointer) (k sb-alien:int)
+  (counts sb-sys:system-area-pointer) (lists sb-sys:system-area-pointer))
+(sb-alien:define-alien-routine ("ec_ann_build" %ann-build) sb-alien:int
+  (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
+  (sample sb-sys:system-area-pointer) (nsample (sb-alien:signed 64)) (k sb-alien:int)
+  (iters sb-alien:int) (init sb-sys:system-area-pointer) (centroids sb-sys:system-area-pointer)
   (counts sb-sys:system-area-pointer) (lists sb-sys:system-area-pointer))
 (sb-alien:define-alien-routine ("ec_index_load" %index-load) sb-alien:int
   (x sb-sys:system-area-pointer) (n (sb-alien:signed 64)) (d sb-alien:int)
@@ -207,6 +213,18 @@ training row indices; its first K rows initialise the centroids."
     (with-saps ((xp vecs) (cp centroids) (np counts) (lp lists))
       (check (%assign-all xp n dim cp k np lp) "ec_assign_all"))
     (values counts lists)))
+
+(defun ann-build (vecs sample k iters &key (dim 384))
+  "The kmeans + assign-all pair of ann:run (ann.lisp:193-197) in one call:
+(values centroids counts lists), the rows sent to the GPU once."
+  (let* ((n (floor (length vecs) dim))
+         (s (coerce sample '(simple-array (signed-byte 64) (*))))
+         (cent (make-array (* k dim) :element-type 'single-float))
+         (counts (make-array k :element-type '(unsigned-byte 32)))
+         (lists (make-array n :element-type '(unsigned-byte 32))))
+    (with-saps ((xp vecs) (sp s) (cp cent) (np nil) (kp counts) (lp lists))
+      (check (%ann-build xp n dim sp (length s) k iters np cp kp lp) "ec_ann_build"))
+    (values cent counts lists)))
 
 ;;; ---- kb.lisp -------------------------------------------------------------------
 

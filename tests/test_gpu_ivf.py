@@ -119,6 +119,40 @@ def test_assign_all_lists(ec, corpus):
     assert np.array_equal(counts, rc) and np.array_equal(lists, rl)
 
 
+# ann:run in one call (ec_ann_build): the rows go up once; the sample is the
+# whole corpus in order (k-means rows = the resident copy, its bf16 rows
+# reused by the final assignment), a contiguous slice of it, a permutation
+# of it or a random subset (both gathered on the device)
+@pytest.mark.parametrize("kind", ["all", "slice", "perm", "subset"])
+def test_ann_build_one_upload(ec, corpus, kind):
+    x = corpus
+    n = len(x)
+    rng = np.random.default_rng(11)
+    sample = {"all": np.arange(n), "slice": np.arange(1000, 15000), "perm": rng.permutation(n),
+              "subset": rng.choice(n, 6000, replace=False)}[kind].astype(np.int64)
+    k, iters = 256, 3
+    cent, counts, lists = ann.build(x, sample, k, iters)
+    ref_cent = oracle.kmeans(x, sample, k, iters)
+    assert np.array_equal(cent, ref_cent)
+    rc, rl = oracle.assign_all(x, ref_cent)
+    assert np.array_equal(counts, rc) and np.array_equal(lists, rl)
+    # the same as the two calls
+    c2 = ann.kmeans(x, sample, k, iters)
+    assert np.array_equal(cent, c2)
+
+
+def test_ann_build_init_and_small_k(ec, corpus):
+    # given initial centroids, k below the tensor-core granule (exact scan)
+    x = corpus[:3000]
+    sample = np.arange(len(x), dtype=np.int64)
+    init = np.ascontiguousarray(x[[5, 900, 1700, 2999, 42]])
+    cent, counts, lists = ann.build(x, sample, 5, 2, init=init)
+    assert np.array_equal(cent, ann.kmeans(x, sample, 5, 2, init=init))
+    rc, rl = ann.assign_all(x, cent)
+    assert np.array_equal(counts, rc) and np.array_equal(lists, rl)
+    assert int(counts.sum()) == len(x)
+
+
 def test_ivf_and_flat_search(ec, corpus):
     x = corpus
     sample = synth.make_ivf_sample(len(x), 4)
