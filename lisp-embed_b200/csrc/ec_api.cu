@@ -121,6 +121,20 @@ int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* 
   return check_cuda(cudaStreamSynchronize(d.stream), what);
 }
 
+// Large blocks are cached on free and handed to the next allocation of the
+// same size: repeated builds and searches of one shape then make no
+// cudaMalloc / cudaFree calls, whose cost varied from milliseconds to ~1 s
+// for the same multi-GB request.
+constexpr size_t kCacheMinBytes = size_t{16} << 20;
+
+static void cache_release(Device& d, size_t keep) {
+  while (d.free_bytes > keep && !d.free_blocks.empty()) {
+    cudaFree(d.free_blocks.front().first);
+    d.free_bytes -= d.free_blocks.front().second;
+    d.free_blocks.erase(d.free_blocks.begin());
+  }
+}
+
 int dev_alloc(Device& d, void** p, size_t bytes, const char* what) {
   *p = nullptr;
   if (bytes == 0) bytes = 256;
@@ -128,7 +142,23 @@ int dev_alloc(Device& d, void** p, size_t bytes, const char* what) {
   if (lim && d.allocated + bytes > lim)
     return set_error(EC_ENOMEM, "%s: %zu bytes would exceed EC_MAX_BYTES=%zu (in use %zu)", what,
                      bytes, lim, d.allocated);
+  if (bytes >= kCacheMinBytes) {
+    for (size_t i = d.free_blocks.size(); i-- > 0;) {
+      if (d.free_blocks[i].second != bytes) continue;
+      *p = d.free_blocks[i].first;
+      d.free_blocks.erase(d.free_blocks.begin() + static_cast<std::ptrdiff_t>(i));
+      d.free_bytes -= bytes;
+      d.allocated += bytes;
+      return EC_OK;
+    }
+  }
   cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess && !d.free_blocks.empty()) {
+    // the cached blocks go back to the driver and the request is retried
+    cudaGetLastError();
+    cache_release(d, 0);
+    e = cudaMalloc(p, bytes);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     *p = nullptr;
@@ -141,8 +171,16 @@ int dev_alloc(Device& d, void** p, size_t bytes, const char* what) {
 
 void dev_free(Device& d, void* p, size_t bytes) {
   if (!p) return;
-  cudaFree(p);
+  if (bytes == 0) bytes = 256;
   d.allocated = d.allocated >= bytes ? d.allocated - bytes : 0;
+  const size_t cap = G().cache_bytes;
+  if (bytes >= kCacheMinBytes && bytes <= cap) {
+    d.free_blocks.emplace_back(p, bytes);
+    d.free_bytes += bytes;
+    cache_release(d, cap);  // oldest blocks first
+    return;
+  }
+  cudaFree(p);
 }
 
 static void free_uploads(Device& d) {
@@ -163,6 +201,7 @@ static void destroy_device(Device* d) {
   free_index(*d);
   free_uploads(*d);
   if (d->ws) cudaFree(d->ws);
+  cache_release(*d, 0);
   if (d->pin) cudaFreeHost(d->pin);
   for (int i = 0; i < 2; ++i) {
     if (d->stage[i]) cudaFreeHost(d->stage[i]);
@@ -283,6 +322,11 @@ int ec_init(const int* devices, int ndev) {
   for (int o : list)
     if (o < 0 || o >= count) return set_error(EC_EINVAL, "device %d not visible (%d devices)", o, count);
   G().max_bytes = env_size("EC_MAX_BYTES", 0);
+  {
+    // EC_ALLOC_CACHE_MB: freed large blocks kept per device (0: none)
+    const char* cm = getenv("EC_ALLOC_CACHE_MB");
+    G().cache_bytes = (cm && *cm) ? static_cast<size_t>(strtoull(cm, nullptr, 10)) << 20 : size_t{24} << 30;
+  }
   G().max_tokens = static_cast<int>(env_size("EC_MAX_TOKENS_PER_BATCH", 262144));
   G().sync_each = getenv("EC_SYNC_EACH_LAUNCH") != nullptr;
   if (G().max_tokens < 1024) G().max_tokens = 1024;

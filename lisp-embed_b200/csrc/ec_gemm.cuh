@@ -49,10 +49,11 @@ enum GemmEpi : int {
 
 // k-means assignment prefilter (kEpiArgCand).  For row r and column part t
 // (= 2 * column tile + epilogue half) of the approximate scores S~ = bf16(x)
-// . bf16(c)^T: mloc[t][r] = the largest S~, col1/col2 = the columns of the
-// largest two, meta bit 0 = the second lies within w_r of the first, bit 1 =
-// the third-largest does too (then two columns do not cover the part and the
-// row needs the exact scan).  w_r = wscale * xnorm[r] is twice the bound on
+// . bf16(c)^T: mloc[t][r] = the largest S~; the part's window is the columns
+// with S~ >= mloc - w_r; col1/col2 = its first two columns in column order
+// (with one, col1 is the argmax), meta bit 0 = it holds at least two, bit 1
+// = at least three (then two columns do not cover the part and the row
+// needs the exact scan).  w_r = wscale * xnorm[r] is twice the bound on
 // |S~ - S| for that row, so the exact argmax -- and every column exactly tied
 // with it -- has S~ >= max S~ - w_r.  Arrays are [parts][M].  (w_r =
 // rel2 * cmax * xnorm[r]; wscale below is rel2 * cmax.)
@@ -140,6 +141,18 @@ __device__ __forceinline__ float rcp_approx(float x) {
 __device__ __forceinline__ float ex2_approx(float x) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// max(a, b, c) in one instruction (sm_100); a NaN operand is ignored, as by fmaxf
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// all ones when a >= b, else 0 (false for NaN)
+__device__ __forceinline__ uint32_t ge_mask(float a, float b) {
+  uint32_t r;
+  asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r) : "f"(a), "f"(b));
   return r;
 }
 
@@ -425,8 +438,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     int sbuf = 0;
     if constexpr (EPI == kEpiArgCand) {
-      // the three largest approximate scores of this thread's row over its
-      // chunks (one compare per score once the list has filled)
+      // All NCH / PARTS chunks of this thread's row part are read from TMEM
+      // at once (one wait; the accumulator goes back straight away).  Pass 1:
+      // the part's largest approximate score m (three-input max).  Pass 2:
+      // one bit per column with S~ >= m - w (a set + a lop3 per score), the
+      // first two such columns and their count.  The window holds the
+      // part's argmax, so count 1 means col1 is the argmax; count 2 means
+      // col1 / col2 are the two columns that need the exact re-score; count
+      // >= 3 sends the row to the exact scan.
+      constexpr int NCP = NCH / PARTS;
+      static_assert(NCH % PARTS == 0 && NCP <= 4, "ArgCand chunks per part");
       const float wscale = args.ac.rel2 * *args.ac.cmax;
       for (int tile = tile0; tile < tend; tile += tstep) {
         const int mb = WR ? tile : tile / args.n_tiles_n, nb = WR ? wr_nb : tile % args.n_tiles_n;
@@ -440,53 +461,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        float t1 = -INFINITY, t2 = -INFINITY, t3 = -INFINITY;
-        int c1 = 0, c2 = 0;
-#pragma unroll 1
-        for (int c = half; c < NCH; c += PARTS) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tmem_wait_ld();
-          if (c + PARTS >= NCH) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) release_acc(acc);
-          }
-          const int col0 = nb * BN + c * 32;
-          // values below (running max - w) can never be within w of the
-          // row's final max and need no bookkeeping: groups of 8 columns
-          // whose max lies below the window are skipped; in the others the
-          // top-three update is branch-free (selects), so lanes do not
-          // diverge
+        uint32_t r[NCP][32];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float gm = __uint_as_float(r[8 * g]);
+        for (int j = 0; j < NCP; ++j) tmem_ld_32x32b_x32(t_row + (half + j * PARTS) * 32, r[j]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release_acc(acc);
+        float m = -INFINITY;
 #pragma unroll
-            for (int e = 1; e < 8; ++e) gm = fmaxf(gm, __uint_as_float(r[8 * g + e]));
-            const float thr = fmaxf(t1, gm) - w;
-            if (gm >= thr) {
+        for (int j = 0; j < NCP; ++j) {
+          float cm[11];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float v = __uint_as_float(r[8 * g + e]);
-                const int col = col0 + 8 * g + e;
-                const bool in = v >= thr;
-                const bool g1 = in && v > t1, g2 = in && v > t2, g3 = in && v > t3;
-                t3 = g2 ? t2 : (g3 ? v : t3);
-                c2 = g1 ? c1 : (g2 ? col : c2);
-                t2 = g1 ? t1 : (g2 ? v : t2);
-                c1 = g1 ? col : c1;
-                t1 = g1 ? v : t1;
-              }
-            }
-          }
+          for (int q = 0; q < 10; ++q)
+            cm[q] = fmax3(__uint_as_float(r[j][3 * q]), __uint_as_float(r[j][3 * q + 1]),
+                          __uint_as_float(r[j][3 * q + 2]));
+          cm[10] = fmaxf(__uint_as_float(r[j][30]), __uint_as_float(r[j][31]));
+          const float a = fmax3(cm[0], cm[1], cm[2]), b = fmax3(cm[3], cm[4], cm[5]),
+                      c = fmax3(cm[6], cm[7], cm[8]);
+          m = fmax3(m, fmax3(a, b, c), fmaxf(cm[9], cm[10]));
+        }
+        const float lo = m - w;
+        int cnt = 0, c1 = 0, c2 = 0;
+#pragma unroll
+        for (int j = 0; j < NCP; ++j) {
+          uint32_t bits = 0;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) bits |= ge_mask(__uint_as_float(r[j][e]), lo) & (1u << e);
+          const int col0 = nb * BN + (half + j * PARTS) * 32;
+          const int f1 = __ffs(bits) - 1;                // -1 when empty
+          const int f2 = __ffs(bits & (bits - 1u)) - 1;  // the second set bit
+          c2 = cnt == 1 && f1 >= 0 ? col0 + f1 : (cnt == 0 && f2 >= 0 ? col0 + f2 : c2);
+          c1 = cnt == 0 && f1 >= 0 ? col0 + f1 : c1;
+          cnt += __popc(bits);
         }
         if (grow < args.M) {
           const size_t o = static_cast<size_t>(nb * PARTS + half) * args.M + grow;
-          const float lo = t1 - w;
           // a row whose window is not a finite number takes the exact scan
-          const bool bad = !(w >= 0.f && w < INFINITY) || !(t1 > -INFINITY && t1 < INFINITY);
-          args.ac.mloc[o] = bad ? INFINITY : t1;
-          args.ac.meta[o] = (t2 >= lo ? 1 : 0) | ((t3 >= lo || bad) ? 2 : 0);
+          const bool bad = !(w >= 0.f && w < INFINITY) || !(m > -INFINITY && m < INFINITY);
+          args.ac.mloc[o] = bad ? INFINITY : m;
+          args.ac.meta[o] = (cnt >= 2 ? 1 : 0) | ((cnt >= 3 || bad) ? 2 : 0);
           args.ac.col1[o] = c1;
           args.ac.col2[o] = c2;
         }

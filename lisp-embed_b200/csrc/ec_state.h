@@ -120,6 +120,11 @@ struct Device {
   void* pin = nullptr;
   size_t pin_bytes = 0;
   size_t allocated = 0;
+  // freed blocks of at least kCacheMinBytes kept for an allocation of the
+  // same size (dev_alloc / dev_free), oldest first; every use of them is on
+  // `stream`, so stream order makes the reuse safe
+  std::vector<std::pair<void*, size_t>> free_blocks;
+  size_t free_bytes = 0;
   // double-buffered pinned staging of large uploads (upload_h2d)
   void* stage[2] = {nullptr, nullptr};
   cudaEvent_t stage_ev[2] = {nullptr, nullptr};
@@ -150,6 +155,7 @@ struct Global {
   std::vector<Device*> devs;
   bool inited = false;
   size_t max_bytes = 0;  // EC_MAX_BYTES (0 = unlimited), per device
+  size_t cache_bytes = size_t{24} << 30;  // EC_ALLOC_CACHE_MB: freed blocks kept per device
   int max_tokens = 262144;
   // profiling of the forward (ecdbg_profile)
   bool profile = false;
