@@ -2,9 +2,11 @@
 // upload, model load and batched embedding across the library's devices.
 #include <algorithm>
 #include <chrono>
+#include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <numeric>
 #include <string>
 #include <thread>
@@ -70,14 +72,83 @@ int sync_and_check(Device& d, const char* what) {
   return EC_OK;
 }
 
+// Host threads that copy the pieces of one staging chunk in parallel: one
+// pool for the process, created on first use and kept (its threads wait on a
+// condition variable between jobs), so a multi-GB upload spawns no threads.
+class CopyPool {
+ public:
+  explicit CopyPool(int workers) : n_(workers) {
+    for (int i = 0; i < n_; ++i) std::thread([this, i] { loop(i + 1); }).detach();
+  }
+  // dst[0, len) = src[0, len), split over the workers and the calling thread
+  void copy(char* dst, const char* src, size_t len) {
+    const size_t per = (len + n_) / (n_ + 1);
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      dst_ = dst;
+      src_ = src;
+      len_ = len;
+      per_ = per;
+      left_ = n_;
+      ++gen_;
+    }
+    cv_.notify_all();
+    std::memcpy(dst, src, std::min(len, per));
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [this] { return left_ == 0; });
+  }
+
+ private:
+  void loop(int part) {
+    uint64_t seen = 0;
+    for (;;) {
+      char* dst;
+      const char* src;
+      size_t a0, a1;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return gen_ != seen; });
+        seen = gen_;
+        a0 = std::min(len_, per_ * part);
+        a1 = std::min(len_, per_ * (part + 1));
+        dst = dst_;
+        src = src_;
+      }
+      if (a1 > a0) std::memcpy(dst + a0, src + a0, a1 - a0);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--left_ == 0) done_.notify_one();
+    }
+  }
+  const int n_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_;
+  char* dst_ = nullptr;
+  const char* src_ = nullptr;
+  size_t len_ = 0, per_ = 0;
+  int left_ = 0;
+  uint64_t gen_ = 0;
+};
+
+static CopyPool& copy_pool() {
+  // never destroyed: its detached threads outlive static destruction
+  static CopyPool* pool = new CopyPool(static_cast<int>(
+      std::min(15u, std::max(1u, std::thread::hardware_concurrency()) - 1u)));
+  return *pool;
+}
+
+// Host-to-device copy of a large pageable array: 64 MB pieces go through a
+// ring of pinned staging buffers, each filled by the copy pool while earlier
+// pieces are in flight to the device.  Concurrent calls (one thread per
+// device) share the pool, one piece at a time.
 int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* what) {
   constexpr size_t kChunk = size_t{64} << 20;
+  constexpr int S = Device::kStages;
   if (bytes < 2 * kChunk) {
     int rc = check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d.stream), what);
     if (rc) return rc;
     return check_cuda(cudaStreamSynchronize(d.stream), what);
   }
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < S; ++i) {
     if (!d.stage[i] && cudaHostAlloc(&d.stage[i], kChunk, cudaHostAllocPortable) != cudaSuccess) {
       cudaGetLastError();
       d.stage[i] = nullptr;
@@ -91,13 +162,12 @@ int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* 
       if (rc) return rc;
     }
   }
-  const unsigned hw = std::thread::hardware_concurrency();
-  const int nthr = static_cast<int>(std::min(8u, std::max(1u, hw / 2)));
+  static std::mutex pool_mu;  // one job at a time in the shared pool
   const char* s = static_cast<const char*>(src);
   char* t = static_cast<char*>(dst);
-  bool used[2] = {false, false};
+  bool used[S] = {};
   int b = 0;
-  for (size_t off = 0; off < bytes; off += kChunk, b ^= 1) {
+  for (size_t off = 0; off < bytes; off += kChunk, b = (b + 1) % S) {
     const size_t len = std::min(kChunk, bytes - off);
     // the DMA that last read this buffer must be done
     if (used[b]) {
@@ -105,14 +175,10 @@ int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* 
       if (rc) return rc;
     }
     char* buf = static_cast<char*>(d.stage[b]);
-    const size_t per = (len + nthr - 1) / nthr;
-    std::vector<std::thread> th;
-    for (int k = 1; k < nthr; ++k) {
-      const size_t a0 = std::min(len, per * k), a1 = std::min(len, per * (k + 1));
-      if (a1 > a0) th.emplace_back([=] { std::memcpy(buf + a0, s + off + a0, a1 - a0); });
+    {
+      std::lock_guard<std::mutex> lk(pool_mu);
+      copy_pool().copy(buf, s + off, len);
     }
-    std::memcpy(buf, s + off, std::min(len, per));
-    for (auto& x : th) x.join();
     int rc = check_cuda(cudaMemcpyAsync(t + off, buf, len, cudaMemcpyHostToDevice, d.stream), what);
     if (!rc) rc = check_cuda(cudaEventRecord(d.stage_ev[b], d.stream), what);
     if (rc) return rc;
@@ -203,7 +269,7 @@ static void destroy_device(Device* d) {
   if (d->ws) cudaFree(d->ws);
   cache_release(*d, 0);
   if (d->pin) cudaFreeHost(d->pin);
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < Device::kStages; ++i) {
     if (d->stage[i]) cudaFreeHost(d->stage[i]);
     if (d->stage_ev[i]) cudaEventDestroy(d->stage_ev[i]);
   }

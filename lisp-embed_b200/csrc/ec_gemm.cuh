@@ -53,8 +53,8 @@ enum GemmEpi : int {
 // with S~ >= mloc - w_r; col1/col2 = its first two columns in column order
 // (with one, col1 is the argmax), meta bit 0 = it holds at least two, bit 1
 // = at least three (then two columns do not cover the part and the row
-// needs the exact scan).  w_r = wscale * xnorm[r] is twice the bound on
-// |S~ - S| for that row, so the exact argmax -- and every column exactly tied
+// needs the exact scan); the three are packed in pk[t][r].  w_r = wscale *
+// xnorm[r] is twice the bound on |S~ - S| for that row, so the exact argmax -- and every column exactly tied
 // with it -- has S~ >= max S~ - w_r.  Arrays are [parts][M].  (w_r =
 // rel2 * cmax * xnorm[r]; wscale below is rel2 * cmax.)
 struct ArgCandEpi {
@@ -62,9 +62,7 @@ struct ArgCandEpi {
   const float* cmax;    // [1] upper bound of the largest centroid norm
   float rel2;           // 2 * relative bound: w_r = rel2 * cmax * xnorm[r]
   float* mloc;
-  int* meta;
-  int* col1;
-  int* col2;
+  uint32_t* pk;         // col1 | col2 << 15 | meta << 30 (k <= 32768)
 };
 
 // per-head q/k RMSNorm + rotate-half RoPE applied in the QKV epilogue
@@ -500,9 +498,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // a row whose window is not a finite number takes the exact scan
           const bool bad = !(w >= 0.f && w < INFINITY) || !(m > -INFINITY && m < INFINITY);
           args.ac.mloc[o] = bad ? INFINITY : m;
-          args.ac.meta[o] = (cnt >= 2 ? 1 : 0) | ((cnt >= 3 || bad) ? 2 : 0);
-          args.ac.col1[o] = c1;
-          args.ac.col2[o] = c2;
+          const uint32_t meta = (cnt >= 2 ? 1u : 0u) | ((cnt >= 3 || bad) ? 2u : 0u);
+          args.ac.pk[o] = static_cast<uint32_t>(c1) | (static_cast<uint32_t>(c2) << 15) | (meta << 30);
         }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;

@@ -72,7 +72,7 @@ static void split(int64_t n, int parts, int k, int64_t* b, int64_t* e) {
 // a rigorous error window, candidates re-scored exactly, the rest of the rows
 // through the exact scan (ec_ivf_tc.cu).  Identical results to launch_assign.
 struct TcAssign {
-  DBuf xb, xnorm, cb, cmax, mloc, meta, col1, col2, fbr, fbn, tmp;
+  DBuf xb, xnorm, cb, cmax, mloc, pk, fbr, fbn, tmp;
   int64_t n = 0;
   int d = 0, k = 0, parts = 0;
   float rel2 = 0.f;
@@ -104,9 +104,7 @@ static int tc_assign_setup(Device& dv, TcAssign& t, const float* X, int64_t n, i
                    !t.cb.alloc(dv, static_cast<size_t>(k) * d * 2, "assign centroids bf16") &&
                    !t.cmax.alloc(dv, 256, "assign centroid norm") &&
                    !t.mloc.alloc(dv, pn * 4, "assign part maxima") &&
-                   !t.meta.alloc(dv, pn * 4, "assign part flags") &&
-                   !t.col1.alloc(dv, pn * 4, "assign candidates") &&
-                   !t.col2.alloc(dv, pn * 4, "assign candidates") &&
+                   !t.pk.alloc(dv, pn * 4, "assign candidates") &&
                    !t.fbr.alloc(dv, static_cast<size_t>(n) * 8, "assign exact rows") &&
                    !t.fbn.alloc(dv, 256, "assign exact count") &&
                    !t.tmp.alloc(dv, static_cast<size_t>(n) * 4, "assign exact results");
@@ -130,7 +128,7 @@ static int tc_assign_run(Device& dv, TcAssign& t, const float* X, const float* C
                                       t.cmax.as<unsigned>(), st),
                     "round centroids"));
   ArgCandEpi ac{t.xnorm.as<float>(), t.cmax.as<float>(), t.rel2, t.mloc.as<float>(),
-                t.meta.as<int>(), t.col1.as<int>(), t.col2.as<int>()};
+                t.pk.as<uint32_t>()};
   GemmLaunch g;
   g.A = t.xb.as<__nv_bfloat16>();
   g.lda = d;
@@ -153,7 +151,7 @@ static int tc_assign_run(Device& dv, TcAssign& t, const float* X, const float* C
     const int e0 = prof_begin(dv);
     const cudaError_t e = launch_gemm(g, st, dv.num_sms);
     prof_end(dv, 0, 2.0 * static_cast<double>(n) * k * d,
-             2.0 * static_cast<double>(n) * d + 2.0 * k * d + 16.0 * t.parts * n, e0);
+             2.0 * static_cast<double>(n) * d + 2.0 * k * d + 8.0 * t.parts * n, e0);
     EC_TRY(check_cuda(e, "assign scores"));
   }
   EC_TRY(check_cuda(cudaMemsetAsync(t.fbn.p, 0, 8, st), "exact count clear"));
@@ -161,9 +159,9 @@ static int tc_assign_run(Device& dv, TcAssign& t, const float* X, const float* C
     const int e0 = prof_begin(dv);
     const cudaError_t e = launch_argcand_reduce(
         X, n, d, C, t.xnorm.as<float>(), t.cmax.as<float>(), t.rel2, t.parts, t.mloc.as<float>(),
-        t.meta.as<int>(), t.col1.as<int>(), t.col2.as<int>(), out, t.fbr.as<int64_t>(),
+        t.pk.as<uint32_t>(), out, t.fbr.as<int64_t>(),
         t.fbn.as<unsigned long long>(), st);
-    prof_end(dv, 2, 0.0, 16.0 * t.parts * n + 4.0 * n * d, e0);
+    prof_end(dv, 2, 0.0, 8.0 * t.parts * n + 4.0 * n * d, e0);
     EC_TRY(check_cuda(e, "assign candidates"));
   }
   unsigned long long nfb = 0;

@@ -69,8 +69,8 @@ cudaError_t launch_round_rows(const float* X, int64_t n, int d, __nv_bfloat16* X
 // to fb_rows / *fb_count instead
 cudaError_t launch_argcand_reduce(const float* X, int64_t n, int d, const float* C,
                                   const float* xnorm, const float* cmax, float rel2, int parts,
-                                  const float* mloc, const int* meta, const int* col1,
-                                  const int* col2, int32_t* out, int64_t* fb_rows,
+                                  const float* mloc, const uint32_t* pk, int32_t* out,
+                                  int64_t* fb_rows,
                                   unsigned long long* fb_count, cudaStream_t st);
 // out[j] = X[rows[j]] for j < m (rows of d floats, d % 4 == 0; the caller
 // checks every index against X's rows)

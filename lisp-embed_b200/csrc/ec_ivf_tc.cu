@@ -61,28 +61,34 @@ __global__ void round_rows_kernel(const float* X, int64_t n, int d, float slack,
   }
 }
 
-// One thread per row: the exact argmax over the window's columns.  The
-// block's 128 rows pass through shared memory in 32-column slices (coalesced
-// loads, padded rows: thread t reads bank (t + k) % 32), and each thread keeps
-// up to kMaxCand running sequential sums -- the same single-float order as
-// the reference's %dot.  Rows with more candidates take the exact scan.
+// One thread per row: the exact argmax over the window's columns.  A row
+// whose window holds a single column is decided without reading it (that
+// column is the exact argmax: every column tied with or above it would lie
+// in the window too).  Rows with two to kMaxCand candidates pass through
+// shared memory in 32-column slices (coalesced loads of those rows only,
+// padded rows: thread t reads bank (t + k) % 32), each thread keeping up to
+// kMaxCand running sequential sums -- the same single-float order as the
+// reference's %dot; a block with no such row reads no rows at all.  Rows
+// with more candidates take the exact scan.
 constexpr int kRedRows = 128;
 constexpr int kMaxCand = 8;
 
 __global__ void __launch_bounds__(kRedRows)
     argcand_reduce_kernel(const float* X, int64_t n, int d, const float* C, const float* xnorm,
                           const float* cmax, float rel2, int parts, const float* mloc,
-                          const int* meta, const int* col1, const int* col2, int32_t* out,
-                          int64_t* fb_rows, unsigned long long* fb_count) {
+                          const uint32_t* pk, int32_t* out, int64_t* fb_rows,
+                          unsigned long long* fb_count) {
   // rows padded to 36 floats: 16-byte aligned, and the eight threads of a
   // 128-bit shared-memory phase land on distinct banks
   __shared__ __align__(16) float xs[kRedRows][36];
+  __shared__ int need[kRedRows];
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kRedRows;
   const int64_t r = r0 + threadIdx.x;
   const bool live = r < n;
   int cand[kMaxCand];
   int nc = 0;
   bool exact = false;
+  bool rescore = false;
   if (live) {
     const float w = rel2 * *cmax * xnorm[r];
     float m = -INFINITY;
@@ -92,25 +98,38 @@ __global__ void __launch_bounds__(kRedRows)
     for (int t = 0; !exact && t < parts; ++t) {
       const size_t o = static_cast<size_t>(t) * n + r;
       if (!(mloc[o] >= lo)) continue;
-      const int mt = meta[o];
-      const int need = (mt & 1) ? 2 : 1;
-      if ((mt & 2) || nc + need > kMaxCand) {
+      const uint32_t p = pk[o];
+      const uint32_t mt = p >> 30;
+      const int need_c = (mt & 1u) ? 2 : 1;
+      if ((mt & 2u) || nc + need_c > kMaxCand) {
         exact = true;
         break;
       }
 #pragma unroll
       for (int q = 0; q < kMaxCand; ++q)
-        if (q == nc) cand[q] = col1[o];
+        if (q == nc) cand[q] = static_cast<int>(p & 0x7fffu);
       ++nc;
-      if (mt & 1) {
+      if (mt & 1u) {
 #pragma unroll
         for (int q = 0; q < kMaxCand; ++q)
-          if (q == nc) cand[q] = col2[o];
+          if (q == nc) cand[q] = static_cast<int>((p >> 15) & 0x7fffu);
         ++nc;
       }
     }
+    if (exact) {
+      nc = 0;
+      fb_rows[atomicAdd(fb_count, 1ull)] = r;
+    } else if (nc == 1 && lo > -FLT_MAX) {
+      // the exact score is at least m - w / 2 > -FLT_MAX: the Lisp's strict
+      // comparison against most-negative-single-float picks this column
+      out[r] = cand[0];
+      nc = 0;
+    } else {
+      rescore = nc > 0;
+    }
   }
-  if (exact) nc = 0;
+  need[threadIdx.x] = rescore ? 1 : 0;
+  if (!__syncthreads_or(rescore)) return;
   float acc[kMaxCand];
 #pragma unroll
   for (int q = 0; q < kMaxCand; ++q) acc[q] = 0.f;
@@ -118,9 +137,9 @@ __global__ void __launch_bounds__(kRedRows)
     __syncthreads();
     for (int i = threadIdx.x; i < kRedRows * 8; i += kRedRows) {
       const int rr = i >> 3, c4 = i & 7;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r0 + rr < n) v = *reinterpret_cast<const float4*>(X + (r0 + rr) * d + k0 + c4 * 4);
-      *reinterpret_cast<float4*>(&xs[rr][c4 * 4]) = v;
+      if (need[rr])
+        *reinterpret_cast<float4*>(&xs[rr][c4 * 4]) =
+            *reinterpret_cast<const float4*>(X + (r0 + rr) * d + k0 + c4 * 4);
     }
     __syncthreads();
     // d % 32 == 0 on this path: whole 32-column slices
@@ -150,11 +169,7 @@ __global__ void __launch_bounds__(kRedRows)
         if (u == q) acc[u] = s;
     }
   }
-  if (!live) return;
-  if (exact) {
-    fb_rows[atomicAdd(fb_count, 1ull)] = r;
-    return;
-  }
+  if (!rescore) return;
   float best = -FLT_MAX;
   int bidx = 0x7fffffff;
 #pragma unroll
@@ -208,14 +223,13 @@ cudaError_t launch_round_rows(const float* X, int64_t n, int d, __nv_bfloat16* X
 
 cudaError_t launch_argcand_reduce(const float* X, int64_t n, int d,
                                   const float* C, const float* xnorm, const float* cmax, float rel2,
-                                  int parts, const float* mloc, const int* meta, const int* col1,
-                                  const int* col2, int32_t* out, int64_t* fb_rows,
-                                  unsigned long long* fb_count, cudaStream_t st) {
+                                  int parts, const float* mloc, const uint32_t* pk, int32_t* out,
+                                  int64_t* fb_rows, unsigned long long* fb_count, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   if (d % 32) return cudaErrorInvalidValue;
   const int64_t blocks = (n + kRedRows - 1) / kRedRows;
   argcand_reduce_kernel<<<static_cast<unsigned>(blocks), kRedRows, 0, st>>>(
-      X, n, d, C, xnorm, cmax, rel2, parts, mloc, meta, col1, col2, out, fb_rows, fb_count);
+      X, n, d, C, xnorm, cmax, rel2, parts, mloc, pk, out, fb_rows, fb_count);
   return cudaGetLastError();
 }
 

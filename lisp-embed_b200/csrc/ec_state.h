@@ -125,9 +125,10 @@ struct Device {
   // `stream`, so stream order makes the reuse safe
   std::vector<std::pair<void*, size_t>> free_blocks;
   size_t free_bytes = 0;
-  // double-buffered pinned staging of large uploads (upload_h2d)
-  void* stage[2] = {nullptr, nullptr};
-  cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+  // pinned staging ring of large uploads (upload_h2d)
+  static constexpr int kStages = 4;
+  void* stage[kStages] = {};
+  cudaEvent_t stage_ev[kStages] = {};
   // pinned mirror of the status word (read with the stream's last copy)
   unsigned* status_host = nullptr;
   // captured forwards of small host batches: the whole upload -> forward ->
