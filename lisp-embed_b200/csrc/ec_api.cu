@@ -187,6 +187,13 @@ int upload_h2d(Device& d, void* dst, const void* src, size_t bytes, const char* 
   return check_cuda(cudaStreamSynchronize(d.stream), what);
 }
 
+static thread_local bool t_pdl = true;
+bool pdl_enabled() {
+  static const bool on = getenv("EC_NO_PDL") == nullptr;
+  return on && t_pdl;
+}
+void pdl_set_thread(bool on) { t_pdl = on; }
+
 // Large blocks are cached on free and handed to the next allocation of the
 // same size: repeated builds and searches of one shape then make no
 // cudaMalloc / cudaFree calls, whose cost varied from milliseconds to ~1 s
@@ -276,6 +283,7 @@ static void destroy_device(Device* d) {
   graphs_clear(*d);
   if (d->status) cudaFree(d->status);
   if (d->status_host) cudaFreeHost(d->status_host);
+  if (d->res_host) cudaFreeHost(d->res_host);
   if (d->stream) cudaStreamDestroy(d->stream);
   for (cudaEvent_t e : d->evpool) cudaEventDestroy(e);
   delete d;

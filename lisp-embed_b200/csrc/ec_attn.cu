@@ -251,11 +251,14 @@ static cudaError_t run_short(const AttnLaunch& l, cudaStream_t st, bool bucketed
     a.first = first;
     a.kcap = (maxlen + 15) & ~15;
     dim3 grid(last - first, l.heads);
-    if (F16P)
-      attn_short_h_kernel<HD, MODE, MINB, BK, PV2><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
-    else
+    cudaError_t e;
+    if (F16P) {
+      e = launch_pdl(attn_short_h_kernel<HD, MODE, MINB, BK, PV2>, grid, dim3(kShortAttnThreads),
+                     S::bytes(a.kcap), st, a);
+    } else {
       attn_short_kernel<HD, MODE, BK, MINB><<<grid, kShortAttnThreads, S::bytes(a.kcap), st>>>(a);
-    const cudaError_t e = cudaGetLastError();
+      e = cudaGetLastError();
+    }
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -14,6 +14,7 @@
 #pragma once
 
 #include "ec_attn.cuh"
+#include "ec_kernels.h"
 
 namespace ec {
 
@@ -286,6 +287,8 @@ template <int HD, int MODE, int MINB, int BK = 64, bool PV2 = false>
 __global__ void __launch_bounds__(kShortAttnThreads, MINB)
     attn_short_h_kernel(const ShortAttnArgs a) {
   static_assert(BK == 32 || BK == 64, "key block");
+  pdl_trigger();
+  pdl_wait();
   constexpr int NT = BK / 8;
   constexpr int NS = PV2 ? 2 : 1;
   constexpr bool kBias = MODE == 1;

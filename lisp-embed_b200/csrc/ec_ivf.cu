@@ -601,12 +601,32 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
     mark(4);
     EC_TRY(check_cuda(launch_merge(dc, nq, ngroups, topk, di, df, st), "merge"));
     mark(5);
-    EC_TRY(check_cuda(cudaMemcpyAsync(ids + a * topk, di, static_cast<size_t>(nq) * topk * 8,
-                                      cudaMemcpyDeviceToHost, st), "ids download"));
-    EC_TRY(check_cuda(cudaMemcpyAsync(scores + a * topk, df, static_cast<size_t>(nq) * topk * 4,
-                                      cudaMemcpyDeviceToHost, st), "scores download"));
+    // small results (one query, say) land in pinned memory with one copy
+    // (ids and scores are adjacent in the workspace); larger ones go
+    // straight to the caller's arrays
+    const size_t res_bytes = s_i + static_cast<size_t>(nq) * topk * 4;
+    if (res_bytes <= Device::kResHostBytes && !dv.res_host &&
+        cudaHostAlloc(&dv.res_host, Device::kResHostBytes, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      dv.res_host = nullptr;
+    }
+    const bool pinned = res_bytes <= Device::kResHostBytes && dv.res_host;
+    if (pinned) {
+      EC_TRY(check_cuda(cudaMemcpyAsync(dv.res_host, di, res_bytes, cudaMemcpyDeviceToHost, st),
+                        "results download"));
+    } else {
+      EC_TRY(check_cuda(cudaMemcpyAsync(ids + a * topk, di, static_cast<size_t>(nq) * topk * 8,
+                                        cudaMemcpyDeviceToHost, st), "ids download"));
+      EC_TRY(check_cuda(cudaMemcpyAsync(scores + a * topk, df, static_cast<size_t>(nq) * topk * 4,
+                                        cudaMemcpyDeviceToHost, st), "scores download"));
+    }
     mark(6);
     EC_TRY(sync_and_check(dv, "search"));
+    if (pinned) {
+      const char* rh = static_cast<const char*>(dv.res_host);
+      std::memcpy(ids + a * topk, rh, static_cast<size_t>(nq) * topk * 8);
+      std::memcpy(scores + a * topk, rh + s_i, static_cast<size_t>(nq) * topk * 4);
+    }
     if (trace) {
       float ms[6] = {};
       for (int i = 0; i < 6; ++i)

@@ -194,6 +194,61 @@ __global__ void __launch_bounds__(128) scores_small_kernel(const float* Q, int n
     if (j < nq) S[static_cast<int64_t>(j) * k + c] = acc[j];
 }
 
+// The same scores with the centroid rows staged whole in shared memory: one
+// warp per 32 centroids issues every 16-byte piece of its 32 rows (one
+// contiguous block of C) and of the queries as cp.async at once, waits once,
+// and each lane then runs its centroid's sequential sum from shared memory
+// (rows padded to an odd number of 16-byte pieces: the eight lanes of a
+// 128-bit phase hit distinct banks).  One memory latency per warp instead of one per few
+// loads; bit-identical to scores_small_kernel.
+constexpr int kScoreRows = 32;
+
+__device__ __forceinline__ void ivf_cp16(float* smem, const float* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem));
+}
+
+__global__ void __launch_bounds__(32) scores_rows_kernel(const float* Q, int nq, const float* C, int k,
+                                                         int d, float* S) {
+  extern __shared__ __align__(16) float srow[];
+  const int ld = 4 * ((d >> 2) | 1);     // odd count of 16-byte pieces per row
+  float* cs = srow;                     // [kScoreRows][ld]
+  float* qs = srow + kScoreRows * ld;   // [nq][d]
+  const int lane = threadIdx.x;
+  const int c0 = blockIdx.x * kScoreRows;
+  const int rows = min(kScoreRows, k - c0);
+  const int d4 = d >> 2;
+  for (int r = 0; r < rows; ++r)
+    for (int c = lane; c < d4; c += 32) ivf_cp16(cs + r * ld + c * 4, C + static_cast<int64_t>(c0 + r) * d + c * 4);
+  for (int i = lane; i < nq * d4; i += 32) ivf_cp16(qs + i * 4, Q + static_cast<int64_t>(i) * 4);
+  asm volatile("cp.async.commit_group;\n" ::);
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncwarp();
+  if (lane >= rows) return;
+  float acc[kSmallQ];
+#pragma unroll
+  for (int j = 0; j < kSmallQ; ++j) acc[j] = 0.f;
+  const float4* cr = reinterpret_cast<const float4*>(cs + lane * ld);
+#pragma unroll 4
+  for (int c4 = 0; c4 < d4; ++c4) {
+    const float4 v = cr[c4];
+#pragma unroll
+    for (int j = 0; j < kSmallQ; ++j) {
+      if (j < nq) {
+        const float4 qv = reinterpret_cast<const float4*>(qs + j * d)[c4];
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.x, v.x));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.y, v.y));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.z, v.z));
+        acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.w, v.w));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kSmallQ; ++j)
+    if (j < nq) S[static_cast<int64_t>(j) * k + c0 + lane] = acc[j];
+}
+
 // ---------------------------------------------------- stable counting sort --
 constexpr int kSortTile = 4096;
 
@@ -365,7 +420,7 @@ __device__ __forceinline__ uint32_t score_key32(float s) {
 }
 
 // bin of the 256-bin histogram where the running count reaches `need`;
-// warp 0 only; writes (bin, count before it)
+// warp 0 only; writes (bin, count before it, count in it)
 __device__ __forceinline__ void sel_find(const uint32_t* hist, uint32_t need, uint32_t* out) {
   const int lane = threadIdx.x & 31;
   uint32_t c[8], sum = 0;
@@ -388,6 +443,7 @@ __device__ __forceinline__ void sel_find(const uint32_t* hist, uint32_t need, ui
       if (run + c[j] >= need) {
         out[0] = 8 * lane + j;
         out[1] = run;
+        out[2] = c[j];
         break;
       }
       run += c[j];
@@ -397,7 +453,7 @@ __device__ __forceinline__ void sel_find(const uint32_t* hist, uint32_t need, ui
 
 struct SelSmem {
   uint32_t* hist;  // [256]
-  uint32_t* found; // [2]
+  uint32_t* found; // [3]
   int* nsel;
 };
 
@@ -405,7 +461,7 @@ struct SelSmem {
 // prefix, one warp atomic per distinct bin; returns (bin, count below it).
 template <class F>
 __device__ __forceinline__ uint2 sel_pass(F field, int nv, uint32_t mask, uint32_t prefix, int shift,
-                                          uint32_t need, const SelSmem& sm) {
+                                          uint32_t need, const SelSmem& sm, uint32_t* in_bin = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31;
   sm.hist[tid] = 0;
   __syncthreads();
@@ -421,17 +477,19 @@ __device__ __forceinline__ uint2 sel_pass(F field, int nv, uint32_t mask, uint32
   if (tid < 32) sel_find(sm.hist, need, sm.found);
   __syncthreads();
   const uint2 r = make_uint2(sm.found[0], sm.found[1]);
+  if (in_bin) *in_bin = sm.found[2];
   __syncthreads();  // found[] is rewritten by the next pass
   return r;
 }
 
 // The 32-bit key v of the need-th smallest of key[m] (m < nv); *left = how
-// many keys equal to v are among the need smallest.
+// many keys equal to v are among the need smallest, *equal = how many keys
+// equal v in all.
 __device__ __forceinline__ uint32_t sel_kth(const uint32_t (&key)[kSelPer], int nv, uint32_t need,
-                                            const SelSmem& sm, uint32_t* left) {
+                                            const SelSmem& sm, uint32_t* left, uint32_t* equal) {
   uint32_t prefix = 0, mask = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    const uint2 r = sel_pass([&](int m) { return key[m]; }, nv, mask, prefix, shift, need, sm);
+    const uint2 r = sel_pass([&](int m) { return key[m]; }, nv, mask, prefix, shift, need, sm, equal);
     prefix |= r.x << shift;
     mask |= 0xffu << shift;
     need -= r.y;
@@ -465,11 +523,13 @@ __device__ __forceinline__ void sel_sort(unsigned long long* sel, int P) {
 __device__ void select_emit(const uint32_t (&key)[kSelPer], int nv, int nprobe, const SelSmem& sm,
                             unsigned long long* sel, int32_t* out) {
   const int tid = threadIdx.x;
-  uint32_t need;
-  const uint32_t v = sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &need);
-  // among the keys equal to v, the `need` lowest indices: index <= ip
+  uint32_t need, equal;
+  const uint32_t v = sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &need, &equal);
+  // among the keys equal to v, the `need` lowest indices: index <= ip (all
+  // of them, without the index passes, when every key equal to v is kept)
   uint32_t ip = 0, imask = 0;
-  for (int shift = 8; shift >= 0; shift -= 8) {
+  if (need == equal) ip = 0xffffffffu;
+  for (int shift = 8; need != equal && shift >= 0; shift -= 8) {
     const uint2 r = sel_pass(
         [&](int m) { return key[m] == v ? static_cast<uint32_t>(tid + kSelThreads * m) : 0xffffffffu; }, nv,
         imask | 0xffff0000u, ip, shift, need, sm);
@@ -496,7 +556,7 @@ __device__ void select_emit(const uint32_t (&key)[kSelPer], int nv, int nprobe, 
 __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(const float* S, int k, int nprobe,
                                                                    int32_t* probes) {
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t found[2];
+  __shared__ uint32_t found[3];
   __shared__ int nsel;
   extern __shared__ unsigned long long sel[];  // [P2], P2 = pow2 >= nprobe
   const int64_t q = blockIdx.x;
@@ -543,7 +603,7 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_tc_kernel(
     const float* S, const float* Q, const float* C, const float* qnorm, const float* cmax, float rel2, int k,
     int d, int nprobe, int32_t* probes) {
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t found[2];
+  __shared__ uint32_t found[3];
   __shared__ int nsel, ncand;
   extern __shared__ __align__(16) unsigned char tc_sm[];
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(tc_sm);  // [max(kTcCand, pow2(nprobe))]
@@ -561,8 +621,8 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_tc_kernel(
   uint32_t key[kSelPer];
 #pragma unroll
   for (int m = 0; m < kSelPer; ++m) key[m] = m < nv ? score_key32(sq[tid + kSelThreads * m]) : 0u;
-  uint32_t left;
-  const float t = key32_score(sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &left));
+  uint32_t left, equal;
+  const float t = key32_score(sel_kth(key, nv, static_cast<uint32_t>(nprobe), sm, &left, &equal));
   const float w = __fmul_ru(__fmul_ru(rel2, qnorm[q]), *cmax);
   const float lo = __fsub_rd(t, w);
   bool ok = w >= 0.f && w < INFINITY && lo > -INFINITY && lo < INFINITY;  // block-uniform
@@ -724,7 +784,6 @@ __global__ void flat_scan_kernel(const float* X, int64_t n, int d, int64_t rows_
 __global__ void merge_kernel(const unsigned long long* cand, int ngroups, int topk, int64_t* ids,
                              float* scores) {
   extern __shared__ unsigned long long mk[];
-  unsigned long long* red = mk;
   unsigned long long* keys = mk + 32;
   const int64_t q = blockIdx.x;
   const int tot = ngroups * topk;
@@ -734,17 +793,40 @@ __global__ void merge_kernel(const unsigned long long* cand, int ngroups, int to
     keys[i] = c == ~0ull ? ~0ull : ((c & 0xffffffff00000000ull) | static_cast<uint32_t>(i));
   }
   __syncthreads();
+  // each warp takes the topk smallest keys of its slice (no block barrier
+  // per round), then warp 0 takes the topk smallest of the warps' lists;
+  // keys are unique, so the result is the same as one pass over all keys
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = (tot + nw - 1) / nw;
+  const int b = min(tot, wid * per), e = min(tot, b + per);
+  unsigned long long* wtop = keys + tot;  // [nw][topk]
   for (int r = 0; r < topk; ++r) {
     unsigned long long mine = ~0ull;
     int at = -1;
-    for (int i = threadIdx.x; i < tot; i += blockDim.x)
+    for (int i = b + lane; i < e; i += 32)
       if (keys[i] < mine) {
         mine = keys[i];
         at = i;
       }
-    const unsigned long long w = block_min_u64(mine, red);
+    const unsigned long long w = warp_min_u64(mine);
     if (w == mine && at >= 0 && w != ~0ull) keys[at] = ~0ull;
-    if (threadIdx.x == 0) {
+    if (lane == 0) wtop[wid * topk + r] = w;
+    __syncwarp();
+  }
+  __syncthreads();
+  if (wid != 0) return;
+  const int tw = nw * topk;
+  for (int r = 0; r < topk; ++r) {
+    unsigned long long mine = ~0ull;
+    int at = -1;
+    for (int i = lane; i < tw; i += 32)
+      if (wtop[i] < mine) {
+        mine = wtop[i];
+        at = i;
+      }
+    const unsigned long long w = warp_min_u64(mine);
+    if (w == mine && at >= 0 && w != ~0ull) wtop[at] = ~0ull;
+    if (lane == 0) {
       if (w == ~0ull) {
         ids[q * topk + r] = -1;
         scores[q * topk + r] = -FLT_MAX;
@@ -754,7 +836,7 @@ __global__ void merge_kernel(const unsigned long long* cand, int ngroups, int to
         scores[q * topk + r] = key_score(c);
       }
     }
-    __syncthreads();
+    __syncwarp();
   }
 }
 
@@ -770,6 +852,20 @@ cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const 
 cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
                           cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
+  if (nq <= kSmallQ && d % 4 == 0 && ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(Q)) & 15) == 0) {
+    const size_t sm = (static_cast<size_t>(kScoreRows) * 4 * ((d / 4) | 1) + static_cast<size_t>(nq) * d) * 4;
+    constexpr size_t kMaxSm = 160 * 1024;
+    if (sm <= kMaxSm) {
+      // (set on every call: the attribute belongs to the current device)
+      if (cudaFuncSetAttribute(scores_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kMaxSm)) == cudaSuccess) {
+        scores_rows_kernel<<<static_cast<unsigned>((k + kScoreRows - 1) / kScoreRows), 32, sm, st>>>(
+            Q, static_cast<int>(nq), C, k, d, S);
+        return cudaGetLastError();
+      }
+      cudaGetLastError();
+    }
+  }
   if (nq <= kSmallQ && d % 4 == 0 && static_cast<size_t>(nq) * d * sizeof(float) <= 48 * 1024 &&
       (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
     scores_small_kernel<<<static_cast<unsigned>((k + 127) / 128), 128,
@@ -863,7 +959,8 @@ cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, cons
 
 cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk, int64_t* ids,
                          float* scores, cudaStream_t st) {
-  const size_t sm = (32 + static_cast<size_t>(ngroups) * topk) * 8;
+  // keys, then the eight warps' lists
+  const size_t sm = (32 + static_cast<size_t>(ngroups) * topk + 8 * static_cast<size_t>(topk)) * 8;
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
   cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   merge_kernel<<<static_cast<unsigned>(nq), 256, sm, st>>>(cand, ngroups, topk, ids, scores);

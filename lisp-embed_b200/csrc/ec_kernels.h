@@ -11,6 +11,36 @@
 
 namespace ec {
 
+// Programmatic dependent launch for the chains of small row / skinny /
+// attention kernels: a kernel launched by launch_pdl may be scheduled while
+// its predecessor in the stream drains, so it calls pdl_wait() before it
+// reads or writes anything that kernel touches (the wait returns once the
+// predecessor grid has completed and its writes are visible; without the
+// launch attribute it returns at once), and pdl_trigger() early so that its
+// own successor can be scheduled.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
+bool pdl_enabled();            // EC_NO_PDL turns it off; per thread, see pdl_set_thread
+void pdl_set_thread(bool on);  // this thread's launches (a graph capture turns it off)
+
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<A&&>(args)...);
+}
+
 enum DtKind : int { kDtF32 = 0, kDtBf16 = 1 };
 enum ConvKind : int { kConvF16ToF32 = 0, kConvBf16ToF32 = 1, kConvF32ToBf16 = 2 };
 

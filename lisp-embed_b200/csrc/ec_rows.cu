@@ -76,6 +76,8 @@ __device__ __forceinline__ void ln_finish(float4 (&v)[NV], int H, const float* g
 // bert.lisp:290-298 (type row 0), bert.lisp:473-479 (MPNet, no type).
 template <int NV>
 __global__ void embed_ln_kernel(EmbedLnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= a.T) return;
@@ -102,6 +104,8 @@ __global__ void embed_ln_kernel(EmbedLnArgs a) {
 // Plain LayerNorm of an fp32 row (residual already added by the GEMM).
 template <int NV>
 __global__ void ln_kernel(LnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= a.T) return;
@@ -194,6 +198,8 @@ __global__ void qk_norm_rope_kernel(QkRopeArgs a) {
 // With final_norm (llama), each pooled token is RMS-normalised first
 // (llama.lisp:325-326).
 __global__ void pool_l2_kernel(PoolArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   __shared__ double redd[32];
   const int s = blockIdx.x;
@@ -276,6 +282,8 @@ __global__ void gather_rows_kernel(const void* table, int dtype, const int* ids,
 
 // position of every packed token within its sequence
 __global__ void positions_kernel(const int* cu, int nseq, int* pos) {
+  pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.x;
   if (s >= nseq) return;
   const int b = cu[s], e = cu[s + 1];
@@ -318,30 +326,28 @@ cudaError_t launch_embed_ln(const EmbedLnArgs& a, cudaStream_t st) {
   const int nv = a.H / 128;
   const int blocks = grid_for(static_cast<size_t>(a.T), 8);
   switch (nv) {
-    case 3: embed_ln_kernel<3><<<blocks, 256, 0, st>>>(a); break;
-    case 6: embed_ln_kernel<6><<<blocks, 256, 0, st>>>(a); break;
-    case 8: embed_ln_kernel<8><<<blocks, 256, 0, st>>>(a); break;
-    case 4: embed_ln_kernel<4><<<blocks, 256, 0, st>>>(a); break;
-    case 2: embed_ln_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 1: embed_ln_kernel<1><<<blocks, 256, 0, st>>>(a); break;
+    case 3: return launch_pdl(embed_ln_kernel<3>, dim3(blocks), dim3(256), 0, st, a);
+    case 6: return launch_pdl(embed_ln_kernel<6>, dim3(blocks), dim3(256), 0, st, a);
+    case 8: return launch_pdl(embed_ln_kernel<8>, dim3(blocks), dim3(256), 0, st, a);
+    case 4: return launch_pdl(embed_ln_kernel<4>, dim3(blocks), dim3(256), 0, st, a);
+    case 2: return launch_pdl(embed_ln_kernel<2>, dim3(blocks), dim3(256), 0, st, a);
+    case 1: return launch_pdl(embed_ln_kernel<1>, dim3(blocks), dim3(256), 0, st, a);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_ln(const LnArgs& a, cudaStream_t st) {
   const int nv = a.H / 128;
   const int blocks = grid_for(static_cast<size_t>(a.T), 8);
   switch (nv) {
-    case 3: ln_kernel<3><<<blocks, 256, 0, st>>>(a); break;
-    case 6: ln_kernel<6><<<blocks, 256, 0, st>>>(a); break;
-    case 8: ln_kernel<8><<<blocks, 256, 0, st>>>(a); break;
-    case 4: ln_kernel<4><<<blocks, 256, 0, st>>>(a); break;
-    case 2: ln_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 1: ln_kernel<1><<<blocks, 256, 0, st>>>(a); break;
+    case 3: return launch_pdl(ln_kernel<3>, dim3(blocks), dim3(256), 0, st, a);
+    case 6: return launch_pdl(ln_kernel<6>, dim3(blocks), dim3(256), 0, st, a);
+    case 8: return launch_pdl(ln_kernel<8>, dim3(blocks), dim3(256), 0, st, a);
+    case 4: return launch_pdl(ln_kernel<4>, dim3(blocks), dim3(256), 0, st, a);
+    case 2: return launch_pdl(ln_kernel<2>, dim3(blocks), dim3(256), 0, st, a);
+    case 1: return launch_pdl(ln_kernel<1>, dim3(blocks), dim3(256), 0, st, a);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm(const RmsArgs& a, cudaStream_t st) {
@@ -369,8 +375,7 @@ cudaError_t launch_qk_norm_rope(const QkRopeArgs& a, cudaStream_t st) {
 cudaError_t launch_pool_l2(const PoolArgs& a, int nseq, cudaStream_t st) {
   const int threads = a.H <= 512 ? 128 : 256;
   if (a.H > 4 * threads) return cudaErrorInvalidValue;
-  pool_l2_kernel<<<nseq, threads, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(pool_l2_kernel, dim3(nseq), dim3(threads), 0, st, a);
 }
 
 cudaError_t launch_gather_rows(const void* table, int dtype, const int* ids, float* out, int T,
@@ -381,8 +386,7 @@ cudaError_t launch_gather_rows(const void* table, int dtype, const int* ids, flo
 }
 
 cudaError_t launch_positions(const int* cu, int nseq, int* pos, cudaStream_t st) {
-  positions_kernel<<<nseq, 128, 0, st>>>(cu, nseq, pos);
-  return cudaGetLastError();
+  return launch_pdl(positions_kernel, dim3(nseq), dim3(128), 0, st, cu, nseq, pos);
 }
 
 cudaError_t launch_convert(int kind, const void* src, void* dst, size_t n, cudaStream_t st) {

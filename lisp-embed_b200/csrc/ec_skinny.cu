@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkinnyLaunch a) 
   extern __shared__ __align__(16) uint8_t sk_smem[];
   uint4* sA = reinterpret_cast<uint4*>(sk_smem);  // [M][K / 8]
   const int M = a.M, k8 = a.K / 8;
+  pdl_trigger();
+  pdl_wait();
   for (int i = threadIdx.x; i < M * k8; i += blockDim.x) {
     const int m = i / k8, c = i - m * k8;
     sA[i] = *reinterpret_cast<const uint4*>(a.A + static_cast<size_t>(m) * a.lda + c * 8);
@@ -89,8 +91,8 @@ cudaError_t run_skinny(const SkinnyLaunch& s, size_t smem, cudaStream_t st) {
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  skinny_gemm_kernel<EPI><<<static_cast<unsigned>((s.N + 7) / 8), 256, smem, st>>>(s);
-  return cudaGetLastError();
+  return launch_pdl(skinny_gemm_kernel<EPI>, dim3(static_cast<unsigned>((s.N + 7) / 8)), dim3(256), smem, st,
+                    s);
 }
 
 }  // namespace

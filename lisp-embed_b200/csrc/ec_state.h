@@ -131,6 +131,9 @@ struct Device {
   cudaEvent_t stage_ev[kStages] = {};
   // pinned mirror of the status word (read with the stream's last copy)
   unsigned* status_host = nullptr;
+  // pinned landing area of small search results (kResHostBytes)
+  static constexpr size_t kResHostBytes = size_t{64} << 10;
+  void* res_host = nullptr;
   // captured forwards of small host batches: the whole upload -> forward ->
   // download sequence of one set of sequence lengths as a CUDA graph, valid
   // for the workspace and staging it was captured on

@@ -212,6 +212,23 @@ def test_ivf_search_batched_ties_empty_lists_odd_dim(ec):
     _check_ivf(x, cent, counts, lists, qs, 5, 64)
 
 
+@pytest.mark.parametrize("nq", [1, 3])
+def test_ivf_search_few_queries_tied_probes(ec, corpus, nq):
+    """A few queries (the staged-row probe scores, the warp-level merge):
+    every centroid duplicated, so probe scores tie in pairs and the nprobe-th
+    place falls inside a tie (the radix select's index passes); nprobe 33
+    splits a pair, nprobe 32 keeps whole pairs (no index pass)."""
+    x = corpus
+    base = x[synth.make_ivf_sample(len(x), 9)[:48]]
+    cent = np.ascontiguousarray(np.repeat(base, 2, axis=0))
+    counts, lists = ann.assign_all(x, cent)
+    kb.load_index(x, (cent, counts, lists))
+    rng = np.random.default_rng(nq)
+    qs = np.ascontiguousarray(x[rng.choice(len(x), nq, replace=False)])
+    for nprobe, topk in [(33, 10), (32, 10), (5, 64), (1, 1)]:
+        _check_ivf(x, cent, counts, lists, qs, nprobe, topk)
+
+
 def test_flat_search_query_batched(ec, corpus):
     x = corpus
     kb.load_index(x, None)
