@@ -194,11 +194,11 @@ bool pdl_enabled() {
 }
 void pdl_set_thread(bool on) { t_pdl = on; }
 
-// Large blocks are cached on free and handed to the next allocation of the
-// same size: repeated builds and searches of one shape then make no
-// cudaMalloc / cudaFree calls, whose cost varied from milliseconds to ~1 s
-// for the same multi-GB request.
-constexpr size_t kCacheMinBytes = size_t{16} << 20;
+// Freed blocks are cached and handed to the next allocation of the same
+// size: repeated builds and searches of one shape then make no cudaMalloc /
+// cudaFree calls, whose cost varied from milliseconds to ~1 s for the same
+// request (and every cudaFree waits for the whole device).
+constexpr size_t kCacheMinBytes = 256;
 
 static void cache_release(Device& d, size_t keep) {
   while (d.free_bytes > keep && !d.free_blocks.empty()) {

@@ -264,15 +264,6 @@ __global__ void hist_kernel(const int32_t* a, int64_t n, int k, uint32_t* tile_h
     tile_hist[static_cast<int64_t>(blockIdx.x) * k + c] = h[c];
 }
 
-// counts[c] = sum over tiles
-__global__ void colsum_kernel(const uint32_t* tile_hist, int ntiles, int k, uint32_t* counts) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= k) return;
-  uint32_t s = 0;
-  for (int t = 0; t < ntiles; ++t) s += tile_hist[static_cast<int64_t>(t) * k + c];
-  counts[c] = s;
-}
-
 // single-block exclusive scan of counts -> offs[0..k], k <= 32 * 1024
 __global__ void scan_kernel(const uint32_t* counts, int k, int64_t* offs) {
   __shared__ int64_t part[1024];
@@ -299,19 +290,8 @@ __global__ void scan_kernel(const uint32_t* counts, int k, int64_t* offs) {
   }
 }
 
-// tile_hist[t][c] <- start of tile t's run inside list c
-__global__ void tile_offsets_kernel(uint32_t* tile_hist, int ntiles, int k, const int64_t* offs) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= k) return;
-  uint32_t run = static_cast<uint32_t>(offs[c]);
-  for (int t = 0; t < ntiles; ++t) {
-    const uint32_t v = tile_hist[static_cast<int64_t>(t) * k + c];
-    tile_hist[static_cast<int64_t>(t) * k + c] = run;
-    run += v;
-  }
-}
-
-// one warp per tile, rows in ascending order: lists[pos] = base + row
+// one warp per tile, rows in ascending order: lists[pos] = base + row (for
+// k too large for scatter_cta_kernel's per-warp histograms)
 __global__ void scatter_kernel(const int32_t* a, int64_t n, int k, const uint32_t* tile_off,
                                uint32_t base, uint32_t* lists) {
   extern __shared__ uint32_t cur[];
@@ -331,6 +311,101 @@ __global__ void scatter_kernel(const int32_t* a, int64_t n, int k, const uint32_
       lists[pos] = base + static_cast<uint32_t>(i);
       __syncwarp(peers);
       if (lower == 0) cur[c] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+// Column sums and tile offsets of tile_hist with the tiles of each column
+// split over the eight warps of a block (32 columns per block, lane =
+// column): coalesced rows of tile_hist, eight segments in flight per column.
+constexpr int kSegWarps = 8;
+
+// counts[c] = sum over tiles
+__global__ void __launch_bounds__(256) colsum_seg_kernel(const uint32_t* tile_hist, int ntiles, int k,
+                                                         uint32_t* counts) {
+  __shared__ uint32_t part[kSegWarps][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int per = (ntiles + kSegWarps - 1) / kSegWarps;
+  const int t0 = min(ntiles, seg * per), t1 = min(ntiles, t0 + per);
+  uint32_t s = 0;
+  if (c < k)
+    for (int t = t0; t < t1; ++t) s += tile_hist[static_cast<int64_t>(t) * k + c];
+  part[seg][lane] = s;
+  __syncthreads();
+  if (seg == 0 && c < k) {
+    uint32_t tot = 0;
+#pragma unroll
+    for (int w = 0; w < kSegWarps; ++w) tot += part[w][lane];
+    counts[c] = tot;
+  }
+}
+
+// tile_hist[t][c] <- start of tile t's run inside list c
+__global__ void __launch_bounds__(256) tile_offsets_seg_kernel(uint32_t* tile_hist, int ntiles, int k,
+                                                               const int64_t* offs) {
+  __shared__ uint32_t part[kSegWarps][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int per = (ntiles + kSegWarps - 1) / kSegWarps;
+  const int t0 = min(ntiles, seg * per), t1 = min(ntiles, t0 + per);
+  uint32_t s = 0;
+  if (c < k)
+    for (int t = t0; t < t1; ++t) s += tile_hist[static_cast<int64_t>(t) * k + c];
+  part[seg][lane] = s;
+  __syncthreads();
+  if (c >= k) return;
+  uint32_t run = static_cast<uint32_t>(offs[c]);
+  for (int w = 0; w < seg; ++w) run += part[w][lane];
+  for (int t = t0; t < t1; ++t) {
+    const uint32_t v = tile_hist[static_cast<int64_t>(t) * k + c];
+    tile_hist[static_cast<int64_t>(t) * k + c] = run;
+    run += v;
+  }
+}
+
+// lists[pos] = base + row with one block of eight warps per tile: warp w
+// owns rows [w * 512, w * 512 + 512) of the tile, so its run inside each
+// list starts after the tile's earlier warps' rows (per-warp histograms in
+// shared memory, prefixed in warp order); each warp then scatters its rows
+// in ascending order (match_any groups equal lists within a step).
+constexpr int kScatWarps = 8;
+constexpr int kScatRows = kSortTile / kScatWarps;
+
+__global__ void __launch_bounds__(256) scatter_cta_kernel(const int32_t* a, int64_t n, int k,
+                                                          const uint32_t* tile_off, uint32_t base,
+                                                          uint32_t* lists) {
+  extern __shared__ uint32_t wh[];  // [kScatWarps][k]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < kScatWarps * k; i += blockDim.x) wh[i] = 0;
+  __syncthreads();
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSortTile + static_cast<int64_t>(w) * kScatRows;
+  const int64_t t1 = min(n, t0 + kScatRows);
+  uint32_t* mine = wh + static_cast<size_t>(w) * k;
+  for (int64_t i = t0 + lane; i < t1; i += 32) atomicAdd(&mine[a[i]], 1u);
+  __syncthreads();
+  for (int c = threadIdx.x; c < k; c += blockDim.x) {
+    uint32_t run = tile_off[static_cast<int64_t>(blockIdx.x) * k + c];
+#pragma unroll
+    for (int v = 0; v < kScatWarps; ++v) {
+      const uint32_t cnt = wh[static_cast<size_t>(v) * k + c];
+      wh[static_cast<size_t>(v) * k + c] = run;
+      run += cnt;
+    }
+  }
+  __syncthreads();
+  for (int64_t i0 = t0; i0 < t1; i0 += 32) {
+    const int64_t i = i0 + lane;
+    const bool valid = i < t1;
+    const int c = valid ? a[i] : -1 - lane;  // invalid lanes never match
+    const unsigned peers = __match_any_sync(0xffffffffu, c);
+    if (valid) {
+      const unsigned lower = peers & ((1u << lane) - 1u);
+      const uint32_t pos = mine[c] + __popc(lower);
+      lists[pos] = base + static_cast<uint32_t>(i);
+      __syncwarp(peers);
+      if (lower == 0) mine[c] += __popc(peers);
     }
     __syncwarp();
   }
@@ -889,10 +964,18 @@ cudaError_t launch_lists(const int32_t* a, int64_t n, int k, uint32_t* tile_hist
     cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(hsm));
   }
   if (nt > 0) hist_kernel<<<static_cast<unsigned>(nt), 256, hsm, st>>>(a, n, k, tile_hist);
-  colsum_kernel<<<(k + 255) / 256, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, counts);
+  colsum_seg_kernel<<<(k + 31) / 32, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, counts);
   scan_kernel<<<1, 1024, 0, st>>>(counts, k, offs);
-  tile_offsets_kernel<<<(k + 255) / 256, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, offs);
-  if (nt > 0) scatter_kernel<<<static_cast<unsigned>(nt), 32, hsm, st>>>(a, n, k, tile_hist, base, lists);
+  tile_offsets_seg_kernel<<<(k + 31) / 32, 256, 0, st>>>(tile_hist, static_cast<int>(nt), k, offs);
+  // eight warps per tile while their histograms fit in shared memory
+  const size_t wsm = static_cast<size_t>(kScatWarps) * k * 4;
+  if (nt > 0 && wsm <= 200 * 1024) {
+    if (wsm > 48 * 1024)
+      cudaFuncSetAttribute(scatter_cta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(wsm));
+    scatter_cta_kernel<<<static_cast<unsigned>(nt), 256, wsm, st>>>(a, n, k, tile_hist, base, lists);
+  } else if (nt > 0) {
+    scatter_kernel<<<static_cast<unsigned>(nt), 32, hsm, st>>>(a, n, k, tile_hist, base, lists);
+  }
   return cudaGetLastError();
 }
 

@@ -91,8 +91,18 @@ __global__ void __launch_bounds__(kRedRows)
   bool rescore = false;
   if (live) {
     const float w = rel2 * *cmax * xnorm[r];
-    float m = -INFINITY;
-    for (int t = 0; t < parts; ++t) m = fmaxf(m, mloc[static_cast<size_t>(t) * n + r]);
+    // the part maxima, four independent chains (several loads in flight)
+    float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+    int t = 0;
+#pragma unroll 2
+    for (; t + 4 <= parts; t += 4) {
+      m0 = fmaxf(m0, mloc[static_cast<size_t>(t) * n + r]);
+      m1 = fmaxf(m1, mloc[static_cast<size_t>(t + 1) * n + r]);
+      m2 = fmaxf(m2, mloc[static_cast<size_t>(t + 2) * n + r]);
+      m3 = fmaxf(m3, mloc[static_cast<size_t>(t + 3) * n + r]);
+    }
+    for (; t < parts; ++t) m0 = fmaxf(m0, mloc[static_cast<size_t>(t) * n + r]);
+    const float m = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
     exact = !(w >= 0.f && w < INFINITY) || !(m > -INFINITY && m < INFINITY);
     const float lo = m - w;
     for (int t = 0; !exact && t < parts; ++t) {

@@ -120,9 +120,9 @@ struct Device {
   void* pin = nullptr;
   size_t pin_bytes = 0;
   size_t allocated = 0;
-  // freed blocks of at least kCacheMinBytes kept for an allocation of the
-  // same size (dev_alloc / dev_free), oldest first; every use of them is on
-  // `stream`, so stream order makes the reuse safe
+  // freed blocks kept for an allocation of the same size (dev_alloc /
+  // dev_free), oldest first; every use of them is on `stream`, so stream
+  // order makes the reuse safe
   std::vector<std::pair<void*, size_t>> free_blocks;
   size_t free_bytes = 0;
   // pinned staging ring of large uploads (upload_h2d)
