@@ -572,7 +572,7 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
                         "probe select"));
       mark(3);
     } else if (ivf) {
-      EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st), "probe scores"));
+      EC_TRY(check_cuda(launch_scores(dq, nq, ix.cent, ix.k, d, dS, st, dv.status), "probe scores"));
       mark(2);
       EC_TRY(check_cuda(launch_probe_select(dS, nq, ix.k, nprobe, dp, st), "probe select"));
       mark(3);

@@ -12,7 +12,7 @@ cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const 
                           int d, int32_t* out, cudaStream_t st);
 // S[q, c] = <Q[q], C[c]> (sequential single-float order)
 cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
-                          cudaStream_t st);
+                          cudaStream_t st, unsigned* status = nullptr);
 // stable counting sort of assignments into inverted lists:
 // counts[k], offs[k + 1], lists[n] (base + row id, ascending within a list);
 // tile_hist needs sort_tiles(n) * k words of scratch

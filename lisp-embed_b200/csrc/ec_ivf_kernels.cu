@@ -14,6 +14,7 @@
 #include <cstdint>
 
 #include "ec_ivf.h"
+#include "ec_ptx.cuh"
 
 namespace ec {
 
@@ -195,41 +196,46 @@ __global__ void __launch_bounds__(128) scores_small_kernel(const float* Q, int n
 }
 
 // The same scores with the centroid rows staged whole in shared memory: one
-// warp per 32 centroids issues every 16-byte piece of its 32 rows (one
-// contiguous block of C) and of the queries as cp.async at once, waits once,
-// and each lane then runs its centroid's sequential sum from shared memory
-// (rows padded to an odd number of 16-byte pieces: the eight lanes of a
-// 128-bit phase hit distinct banks).  One memory latency per warp instead of one per few
-// loads; bit-identical to scores_small_kernel.
+// warp per 32 centroids copies its 32 rows and the queries with one untiled
+// bulk copy per row (lane r copies row r), all completing on one mbarrier,
+// waits once, and each lane then runs its centroid's sequential sum from
+// shared memory (rows padded to an odd number of 16-byte pieces: the eight
+// lanes of a 128-bit phase hit distinct banks).  One memory latency per warp
+// and a few copy instructions; bit-identical to scores_small_kernel.  The
+// wait is bounded: on a timeout the status word is set and the copies in
+// flight are waited for (bounded again) before the CTA exits.
 constexpr int kScoreRows = 32;
 
-__device__ __forceinline__ void ivf_cp16(float* smem, const float* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem));
-}
-
 __global__ void __launch_bounds__(32) scores_rows_kernel(const float* Q, int nq, const float* C, int k,
-                                                         int d, float* S) {
+                                                         int d, float* S, unsigned* status) {
   extern __shared__ __align__(16) float srow[];
+  __shared__ uint64_t bar;
   const int ld = 4 * ((d >> 2) | 1);     // odd count of 16-byte pieces per row
   float* cs = srow;                     // [kScoreRows][ld]
   float* qs = srow + kScoreRows * ld;   // [nq][d]
   const int lane = threadIdx.x;
   const int c0 = blockIdx.x * kScoreRows;
   const int rows = min(kScoreRows, k - c0);
-  const int d4 = d >> 2;
-  for (int r = 0; r < rows; ++r)
-    for (int c = lane; c < d4; c += 32) ivf_cp16(cs + r * ld + c * 4, C + static_cast<int64_t>(c0 + r) * d + c * 4);
-  for (int i = lane; i < nq * d4; i += 32) ivf_cp16(qs + i * 4, Q + static_cast<int64_t>(i) * 4);
-  asm volatile("cp.async.commit_group;\n" ::);
-  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 4u;
+  if (lane == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&bar, row_bytes * static_cast<uint32_t>(rows + nq));
+  }
   __syncwarp();
+  if (lane < rows) bulk_load(cs + lane * ld, C + static_cast<int64_t>(c0 + lane) * d, row_bytes, &bar);
+  for (int j = lane; j < nq; j += 32) bulk_load(qs + j * d, Q + static_cast<int64_t>(j) * d, row_bytes, &bar);
+  if (!mbar_wait(&bar, 0, nullptr)) {
+    report(status, kDevTimeoutOther);
+    mbar_wait(&bar, 0, nullptr);
+    return;
+  }
   if (lane >= rows) return;
   float acc[kSmallQ];
 #pragma unroll
   for (int j = 0; j < kSmallQ; ++j) acc[j] = 0.f;
   const float4* cr = reinterpret_cast<const float4*>(cs + lane * ld);
+  const int d4 = d >> 2;
 #pragma unroll 4
   for (int c4 = 0; c4 < d4; ++c4) {
     const float4 v = cr[c4];
@@ -862,16 +868,21 @@ __global__ void merge_kernel(const unsigned long long* cand, int ngroups, int to
   unsigned long long* keys = mk + 32;
   const int64_t q = blockIdx.x;
   const int tot = ngroups * topk;
+  const int nw = blockDim.x >> 5;
+  // the candidates' row ids, so the final picks read no global memory
+  uint32_t* rid = reinterpret_cast<uint32_t*>(keys + tot + nw * topk);
+#pragma unroll 4
   for (int i = threadIdx.x; i < tot; i += blockDim.x) {
     const unsigned long long c = cand[q * tot + i];
     // re-key: score bits high, then flat index (group * topk + rank) low
     keys[i] = c == ~0ull ? ~0ull : ((c & 0xffffffff00000000ull) | static_cast<uint32_t>(i));
+    rid[i] = static_cast<uint32_t>(c & 0xffffffffu);
   }
   __syncthreads();
   // each warp takes the topk smallest keys of its slice (no block barrier
   // per round), then warp 0 takes the topk smallest of the warps' lists;
   // keys are unique, so the result is the same as one pass over all keys
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int per = (tot + nw - 1) / nw;
   const int b = min(tot, wid * per), e = min(tot, b + per);
   unsigned long long* wtop = keys + tot;  // [nw][topk]
@@ -906,9 +917,9 @@ __global__ void merge_kernel(const unsigned long long* cand, int ngroups, int to
         ids[q * topk + r] = -1;
         scores[q * topk + r] = -FLT_MAX;
       } else {
-        const unsigned long long c = cand[q * tot + static_cast<int>(w & 0xffffffffu)];
-        ids[q * topk + r] = static_cast<int64_t>(c & 0xffffffffu);
-        scores[q * topk + r] = key_score(c);
+        // the key keeps the candidate's score bits above its flat index
+        ids[q * topk + r] = static_cast<int64_t>(rid[static_cast<int>(w & 0xffffffffu)]);
+        scores[q * topk + r] = key_score(w);
       }
     }
     __syncwarp();
@@ -925,7 +936,7 @@ cudaError_t launch_assign(const float* X, const int64_t* rows, int64_t n, const 
 }
 
 cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int d, float* S,
-                          cudaStream_t st) {
+                          cudaStream_t st, unsigned* status) {
   if (nq <= 0) return cudaSuccess;
   if (nq <= kSmallQ && d % 4 == 0 && ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(Q)) & 15) == 0) {
     const size_t sm = (static_cast<size_t>(kScoreRows) * 4 * ((d / 4) | 1) + static_cast<size_t>(nq) * d) * 4;
@@ -935,7 +946,7 @@ cudaError_t launch_scores(const float* Q, int64_t nq, const float* C, int k, int
       if (cudaFuncSetAttribute(scores_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kMaxSm)) == cudaSuccess) {
         scores_rows_kernel<<<static_cast<unsigned>((k + kScoreRows - 1) / kScoreRows), 32, sm, st>>>(
-            Q, static_cast<int>(nq), C, k, d, S);
+            Q, static_cast<int>(nq), C, k, d, S, status);
         return cudaGetLastError();
       }
       cudaGetLastError();
@@ -1042,8 +1053,9 @@ cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, cons
 
 cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk, int64_t* ids,
                          float* scores, cudaStream_t st) {
-  // keys, then the eight warps' lists
-  const size_t sm = (32 + static_cast<size_t>(ngroups) * topk + 8 * static_cast<size_t>(topk)) * 8;
+  // keys, the eight warps' lists, then the row ids
+  const size_t sm = (32 + static_cast<size_t>(ngroups) * topk + 8 * static_cast<size_t>(topk)) * 8 +
+                    static_cast<size_t>(ngroups) * topk * 4;
   if (sm > 200 * 1024) return cudaErrorInvalidValue;
   cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   merge_kernel<<<static_cast<unsigned>(nq), 256, sm, st>>>(cand, ngroups, topk, ids, scores);

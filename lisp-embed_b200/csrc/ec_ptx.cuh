@@ -251,6 +251,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
 }
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
+// (both addresses 16-byte aligned, bytes a multiple of 16; no multicast)
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
