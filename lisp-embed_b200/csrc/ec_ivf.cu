@@ -586,7 +586,8 @@ static int search_device(int li, const float* q, int64_t q0, int64_t q1, int npr
       const cudaError_t e =
           batched ? launch_list_scan_batched(ix.x, d, ix.lists, ix.offs, ix.k, dp, nprobe, dq, nq, topk,
                                              w + s_q + s_s + s_p + s_c + s_i + s_f, dc, st)
-                  : launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, parts, dc, st);
+                  : launch_list_scan(ix.x, d, ix.lists, ix.offs, dp, nprobe, dq, nq, topk, parts, dc, st,
+                                     dv.status);
       prof_end(dv, 3, 2.0 * rows * d, 4.0 * rows * d, e0);
       EC_TRY(check_cuda(e, "list scan"));
     } else {

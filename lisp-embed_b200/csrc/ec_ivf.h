@@ -37,7 +37,8 @@ cudaError_t launch_probe_select_tc(const float* S, const float* Q, const float* 
 // contiguous pieces, candidates [nq][nprobe][parts][topk]
 cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
                              const int32_t* probes, int nprobe, const float* Q, int64_t nq,
-                             int topk, int parts, unsigned long long* cand, cudaStream_t st);
+                             int topk, int parts, unsigned long long* cand, cudaStream_t st,
+                             unsigned* status = nullptr);
 cudaError_t launch_flat_scan(const float* X, int64_t n, int d, int nchunks, const float* Q,
                              int64_t nq, int topk, unsigned long long* cand, cudaStream_t st);
 cudaError_t launch_merge(const unsigned long long* cand, int64_t nq, int ngroups, int topk,

@@ -801,6 +801,111 @@ __device__ void scan_rows(const float* X, int d, const uint32_t* lists, int64_t 
   }
 }
 
+// scan_rows with the rows staged in shared memory: per pass of up to kStageRows
+// rows, thread i copies row i with one untiled bulk copy (all on one
+// mbarrier), the block waits once (bounded), then thread i runs row i's
+// sequential sum from shared memory -- one memory latency per pass instead
+// of one per 128 bytes of every row.  Rows padded to an odd number of
+// 16-byte pieces.  Same keys, same top-k as scan_rows.
+constexpr int kStageRows = 64;
+
+template <bool kIndirect>
+__device__ void scan_rows_staged(const float* X, int d, const uint32_t* lists, int64_t start, int64_t cnt,
+                                 const float* qs, int topk, unsigned long long* best,
+                                 unsigned long long* tile, unsigned long long* red, float* stage,
+                                 uint64_t* bar, unsigned* status) {
+  const int ld = 4 * ((d >> 2) | 1);
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 4u;
+  uint32_t phase = 0;
+  for (int64_t t0 = 0; t0 < cnt; t0 += kStageRows) {
+    const int m = static_cast<int>(cnt - t0 < kStageRows ? cnt - t0 : kStageRows);
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, row_bytes * static_cast<uint32_t>(m));
+    // the previous pass's reads of the staging rows are done (the barrier
+    // ending its top-k round) before the copies overwrite them
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x < m) {
+      const int64_t p = t0 + threadIdx.x;
+      const int64_t row = kIndirect ? static_cast<int64_t>(lists[start + p]) : start + p;
+      bulk_load(stage + threadIdx.x * ld, X + row * d, row_bytes, bar);
+    }
+    if (!__syncthreads_and(mbar_wait(bar, phase, nullptr))) {
+      if (threadIdx.x == 0) report(status, kDevTimeoutOther);
+      mbar_wait(bar, phase, nullptr);  // the copies in flight land first
+      return;
+    }
+    phase ^= 1u;
+    if (threadIdx.x < m) {
+      const float4* xr = reinterpret_cast<const float4*>(stage + threadIdx.x * ld);
+      float s = 0.f;
+      const int d4 = d / 4;
+#pragma unroll 4
+      for (int c4 = 0; c4 < d4; ++c4) {
+        const float4 v = xr[c4];
+        const float* qq = qs + 4 * c4;
+        s = __fadd_rn(s, __fmul_rn(v.x, qq[0]));
+        s = __fadd_rn(s, __fmul_rn(v.y, qq[1]));
+        s = __fadd_rn(s, __fmul_rn(v.z, qq[2]));
+        s = __fadd_rn(s, __fmul_rn(v.w, qq[3]));
+      }
+      tile[threadIdx.x] = desc_key(s, static_cast<uint32_t>(t0 + threadIdx.x));
+    }
+    // append the running best as candidates (their positions are smaller)
+    for (int i = threadIdx.x; i < topk; i += blockDim.x) tile[m + i] = best[i];
+    __syncthreads();
+    const int tot = m + topk;
+    for (int r = 0; r < topk; ++r) {
+      unsigned long long mine = ~0ull;
+      int at = -1;
+      for (int i = threadIdx.x; i < tot; i += blockDim.x)
+        if (tile[i] < mine) {
+          mine = tile[i];
+          at = i;
+        }
+      const unsigned long long w = block_min_u64(mine, red);
+      if (w == mine && at >= 0 && w != ~0ull) tile[at] = ~0ull;  // keys are unique
+      if (threadIdx.x == 0) best[r] = w;
+      __syncthreads();
+    }
+  }
+}
+
+// list_scan_kernel with the staged row loads (d % 4 == 0, 16-byte aligned X)
+__global__ void list_scan_staged_kernel(const float* X, int d, const uint32_t* lists, const int64_t* offs,
+                                        const int32_t* probes, int nprobe, const float* Q, int topk,
+                                        unsigned long long* cand, unsigned* status) {
+  extern __shared__ __align__(16) unsigned long long sm[];
+  unsigned long long* best = sm;              // [64]
+  unsigned long long* red = best + 64;        // [32]
+  unsigned long long* tile = red + 32;        // [kStageRows + 64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(tile + kStageRows + 64);  // [2] (16-byte slot)
+  float* qs = reinterpret_cast<float*>(bar + 2);
+  float* stage = qs + ((d + 3) & ~3);         // 16-byte aligned
+  const int p = blockIdx.x;
+  const int64_t q = blockIdx.y;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) qs[i] = Q[q * d + i];
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) best[i] = ~0ull;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int c = probes[q * nprobe + p];
+  const int parts = static_cast<int>(gridDim.z), z = static_cast<int>(blockIdx.z);
+  const int64_t len = offs[c + 1] - offs[c];
+  const int64_t per = (len + parts - 1) / parts;
+  const int64_t pb = per * z < len ? per * z : len;
+  const int64_t cnt = len - pb < per ? len - pb : per;
+  scan_rows_staged<true>(X, d, lists, offs[c] + pb, cnt, qs, topk, best, tile, red, stage, bar, status);
+  for (int i = threadIdx.x; i < topk; i += blockDim.x) {
+    const unsigned long long kk = best[i];
+    cand[((q * nprobe + p) * parts + z) * topk + i] =
+        kk == ~0ull ? ~0ull
+                    : (kk & 0xffffffff00000000ull) |
+                          lists[offs[c] + pb + static_cast<int64_t>(kk & 0xffffffffu)];
+  }
+}
+
 // grid (nprobe, nq): top-k of list probes[q][p] for query q.
 // cand[(q * nprobe + p) * topk + r] = key with tiebreak = position in list.
 // grid (nprobe, nq, parts): part z of the z-th probed list of query q; its
@@ -1032,8 +1137,20 @@ static size_t scan_smem(int d) { return (64 + 32 + 2048 + 64) * 8 + static_cast<
 
 cudaError_t launch_list_scan(const float* X, int d, const uint32_t* lists, const int64_t* offs,
                              const int32_t* probes, int nprobe, const float* Q, int64_t nq, int topk,
-                             int parts, unsigned long long* cand, cudaStream_t st) {
+                             int parts, unsigned long long* cand, cudaStream_t st, unsigned* status) {
   if (parts < 1) return cudaErrorInvalidValue;
+  if (d % 4 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && topk <= 64) {
+    const size_t sm = (64 + 32 + kStageRows + 64 + 2) * 8 + static_cast<size_t>((d + 3) & ~3) * 4 +
+                      static_cast<size_t>(kStageRows) * 4 * ((d / 4) | 1) * 4;
+    if (sm <= 160 * 1024 &&
+        cudaFuncSetAttribute(list_scan_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sm)) == cudaSuccess) {
+      dim3 grid(nprobe, static_cast<unsigned>(nq), static_cast<unsigned>(parts));
+      list_scan_staged_kernel<<<grid, 256, sm, st>>>(X, d, lists, offs, probes, nprobe, Q, topk, cand, status);
+      return cudaGetLastError();
+    }
+    cudaGetLastError();
+  }
   const size_t sm = scan_smem(d);
   cudaFuncSetAttribute(list_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   dim3 grid(nprobe, static_cast<unsigned>(nq), static_cast<unsigned>(parts));
