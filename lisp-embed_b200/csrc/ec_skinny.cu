@@ -28,11 +28,27 @@ __device__ __forceinline__ void bf8_to_f32(const uint4 v, float (&f)[8]) {
   }
 }
 
+// weight pieces (16 bytes) each lane loads ahead: K <= 32 * 8 * kSkChunks
+// (1536) is covered by the prefetch
+constexpr int kSkChunks = 6;
+
 template <int EPI>
 __global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkinnyLaunch a) {
   extern __shared__ __align__(16) uint8_t sk_smem[];
   uint4* sA = reinterpret_cast<uint4*>(sk_smem);  // [M][K / 8]
   const int M = a.M, k8 = a.K / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const bool col = n < a.N;
+  // this lane's first kSkChunks weight pieces, requested before the rows of
+  // A (the previous kernel's output) are waited for and staged
+  const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(col ? n : 0) * a.K);
+  uint4 wv[kSkChunks];
+#pragma unroll
+  for (int j = 0; j < kSkChunks; ++j) {
+    const int c = lane + 32 * j;
+    wv[j] = (col && c < k8) ? __ldg(wr + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
   pdl_trigger();
   pdl_wait();
   for (int i = threadIdx.x; i < M * k8; i += blockDim.x) {
@@ -40,16 +56,15 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkinnyLaunch a) 
     sA[i] = *reinterpret_cast<const uint4*>(a.A + static_cast<size_t>(m) * a.lda + c * 8);
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
-  if (n >= a.N) return;
+  if (!col) return;
   float acc[kSkinnyRows];
 #pragma unroll
   for (int m = 0; m < kSkinnyRows; ++m) acc[m] = 0.f;
-  const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(n) * a.K);
-  for (int c = lane; c < k8; c += 32) {
+  // the same order as one loop over c = lane, lane + 32, ...: the prefetched
+  // pieces first, then the rest of the row
+  auto piece = [&](const uint4 wq, int c) {
     float w[8];
-    bf8_to_f32(wr[c], w);
+    bf8_to_f32(wq, w);
 #pragma unroll
     for (int m = 0; m < kSkinnyRows; ++m) {
       if (m < M) {
@@ -59,7 +74,11 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkinnyLaunch a) 
         for (int e = 0; e < 8; ++e) acc[m] = fmaf(x[e], w[e], acc[m]);
       }
     }
-  }
+  };
+#pragma unroll
+  for (int j = 0; j < kSkChunks; ++j)
+    if (lane + 32 * j < k8) piece(wv[j], lane + 32 * j);
+  for (int c = lane + 32 * kSkChunks; c < k8; c += 32) piece(wr[c], c);
   // every lane gets every row's total; lane m keeps row m
   float mine = 0.f;
 #pragma unroll
