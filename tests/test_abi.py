@@ -57,6 +57,11 @@ def test_calls_fail_cleanly_without_device():
     assert "ec_init" in _lib.last_error()
     shape = (C.c_int64 * 1)(4)
     assert lib.ec_upload_tensor(b"x", _lib.EC_F32, shape, 1, None, 16) == _lib.EC_ESTATE
+    # the IVF entry points check the context before their arguments
+    assert lib.ec_kmeans(None, 0, 8, None, 0, 4, 1, None, None) == _lib.EC_ESTATE
+    assert lib.ec_assign_all(None, 0, 8, None, 4, None, None) == _lib.EC_ESTATE
+    assert lib.ec_ann_build(None, 0, 8, None, 0, 4, 1, None, None, None, None) == _lib.EC_ESTATE
+    assert "ec_init" in _lib.last_error()
     assert lib.ec_comm_id_size() == 128
 
 
