@@ -12,6 +12,8 @@
 #include <thread>
 #include <vector>
 
+#include <unistd.h>
+
 #include "ec_json.h"
 #include "ec_state.h"
 
@@ -130,9 +132,14 @@ class CopyPool {
 };
 
 static CopyPool& copy_pool() {
-  // never destroyed: its detached threads outlive static destruction
-  static CopyPool* pool = new CopyPool(static_cast<int>(
-      std::min(15u, std::max(1u, std::thread::hardware_concurrency()) - 1u)));
+  // never destroyed: its detached threads outlive static destruction.  A
+  // forked child has none of its parent's threads, so it builds its own.
+  static CopyPool* pool = nullptr;
+  static pid_t owner = 0;
+  if (!pool || owner != getpid()) {
+    pool = new CopyPool(static_cast<int>(std::min(15u, std::max(1u, std::thread::hardware_concurrency()) - 1u)));
+    owner = getpid();
+  }
   return *pool;
 }
 
