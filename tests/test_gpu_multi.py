@@ -1,4 +1,4 @@
-"""Two-GPU paths (run only when two GPUs are visible).
+"""Multi-GPU paths (run only when two or more GPUs are visible).
 
 * The in-process multi-device split of ec_embed_batch gives the same
   embeddings as one device (no collective: per-sequence work).
@@ -7,7 +7,9 @@
   device 1 in sample order (NCCL send / recv) and device 1 broadcasts the
   centroids.  The all-reduce exchange (EC_KMEANS_ALLREDUCE=1) agrees up to
   float32 summation order.  The same holds with one process per GPU
-  (ec_comm_init, each rank passing its contiguous shard of the sample).
+  (ec_comm_init, each rank passing its contiguous shard of the sample) and,
+  with three or four GPUs visible, for the middle ranks of the chain (in
+  process and one process per GPU).
 * IVF / flat search with the queries split over the devices equals
   kb::top-k-ivf / top-k-brute.
 * A device that fails before the first exchange (host-side injection,
@@ -92,7 +94,7 @@ PROC_CHILD = PRE + r"""
 import ctypes as C
 import torch.distributed as tdist
 from datetime import timedelta
-rank, world = int(sys.argv[1]), 2
+rank, world = int(sys.argv[1]), {world}
 store = tdist.TCPStore("127.0.0.1", {port}, world, rank == 0, timeout=timedelta(seconds=120))
 _lib.init([rank])
 L = _lib.lib()
@@ -112,7 +114,7 @@ cent = ann.kmeans(x, mine, 64, 4, init=init)
 if rank == 0:
     np.save({out!r}, cent)
 store.set("done%d" % rank, "1")
-store.wait(["done0", "done1"])
+store.wait(["done%d" % r for r in range(world)])
 _lib.shutdown()
 print("rank", rank, "ok")
 """
@@ -169,17 +171,38 @@ def test_two_device_failure_before_exchange_then_recovery():
     assert res["second_exact"] and res["shutdown"] == "ok", res
 
 
+@pytest.mark.skipif(_gpus() < 3, reason="needs three GPUs")
+def test_in_process_kmeans_middle_devices_bit_identical():
+    """Three or four devices in one process: the middle devices both receive
+    the running sums and pass them on."""
+    nd = min(_gpus(), 4)
+    src = PRE.format(repo=REPO) + f"""
+_lib.init(list(range({nd})))
+x, _ = synth.make_ivf_corpus(40000, 384, 64, seed=4)
+sample = synth.make_ivf_sample(len(x), 4)
+cent = ann.kmeans(x, sample, 64, 4)
+print(json.dumps({{"exact": bool(np.array_equal(cent, oracle.kmeans(x, sample, 64, 4)))}}))
+"""
+    p = subprocess.run([sys.executable, "-c", src], capture_output=True, text=True, timeout=600,
+                       env=_env())
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert '"exact": true' in p.stdout, p.stdout
+
+
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-def test_two_process_kmeans_bit_identical(tmp_path):
+def test_process_kmeans_bit_identical(tmp_path):
+    """One process per GPU on every visible GPU up to four (two ranks: the
+    first and last; more: the middle ranks of the chain too)."""
     import socket
+    world = min(_gpus(), 4)
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     out = str(tmp_path / "cent.npy")
-    src = PROC_CHILD.format(repo=REPO, port=port, out=out)
+    src = PROC_CHILD.format(repo=REPO, port=port, out=out, world=world)
     ps = [subprocess.Popen([sys.executable, "-c", src, str(r)], stdout=subprocess.PIPE,
-                           stderr=subprocess.STDOUT, text=True, env=_env()) for r in range(2)]
+                           stderr=subprocess.STDOUT, text=True, env=_env()) for r in range(world)]
     outs = []
     for p in ps:
         try:
