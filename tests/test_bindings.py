@@ -170,6 +170,32 @@ def test_lisp_routines_match_header():
                 assert c_t == ("ptr", "char"), (name, i, c_t)
 
 
+def _calls(form, heads, out):
+    if isinstance(form, list):
+        if form and isinstance(form[0], str) and form[0] in heads:
+            out.append(form)
+        for f in form:
+            _calls(f, heads, out)
+    return out
+
+
+def test_lisp_call_sites_pass_every_parameter():
+    """Each (%routine ...) call in cuda.lisp passes as many arguments as the
+    routine declares (SBCL would only notice when compiling the file)."""
+    with open(LISP) as f:
+        forms = _read_sexps(f.read())
+    arity = {}
+    for form in forms:
+        if isinstance(form, list) and form and form[0] == "sb-alien:define-alien-routine":
+            arity[form[1][1]] = len(form) - 3
+    calls = _calls([f for f in forms if not (isinstance(f, list) and f and
+                                             f[0] == "sb-alien:define-alien-routine")], arity, [])
+    called = {c[0] for c in calls}
+    assert {"%init", "%embed-batch", "%kmeans", "%ann-build", "%ivf-search"} <= called, called
+    for c in calls:
+        assert len(c) - 1 == arity[c[0]], (c[0], len(c) - 1, arity[c[0]])
+
+
 def test_reader_and_parser_catch_a_mismatch():
     """The comparisons above fail on a planted mismatch: an int where the
     header takes an int64_t, and a missing parameter."""
