@@ -1,4 +1,4 @@
-"""Multi-rank host logic on CPU (gloo, world size 2 and 3).
+"""Multi-rank host logic on CPU (gloo, world size 2 to 4).
 
 ec_kmeans shards the training sample into contiguous ranges, one per rank.
 Its default exchange passes the per-cluster accumulators down the ranks in
@@ -75,7 +75,7 @@ def _kmeans_chain_rank(rank, world, port, x, sample, k, iters, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_chained_lloyd_is_bit_identical(tmp_path, world):
     from embedcuda import synth
     from oracle import oracle
