@@ -244,7 +244,9 @@ int ec_tokenizer_free(int handle);
 /* Number of ids of the vocabulary (tk-vocab-size, tokenizer.lisp:254). */
 int ec_tokenizer_vocab_size(int handle);
 /* tk-encode (tokenizer.lisp:201-244) of ntexts UTF-8 texts (texts[i] of
- * lengths[i] bytes, or NUL-terminated when lengths is NULL) on nthreads host
+ * lengths[i] bytes, or NUL-terminated when lengths is NULL; a NULL texts[i]
+ * only with lengths[i] == 0, an empty text; a NULL text otherwise or a
+ * negative length is EC_EINVAL) on nthreads host
  * threads (<= 0: all cores).  Ids are packed into ids[0..offsets[ntexts]) with
  * text i at [offsets[i], offsets[i+1]) -- the layout ec_embed_batch takes.
  * Each text yields at most 512 ids.  If they do not fit `cap`, the call fails

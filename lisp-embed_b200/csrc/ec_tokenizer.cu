@@ -1007,8 +1007,15 @@ int ec_tokenize(int handle, const char* const* texts, const int64_t* lengths, in
   nt = std::max(1, std::min(nt, std::max(1, ntexts / 4)));
   auto work = [&](int w) {
     for (int i = w; i < ntexts; i += nt) {
-      const size_t n = lengths ? static_cast<size_t>(lengths[i]) : std::strlen(texts[i]);
-      if (!texts[i] || !encode(*t, texts[i], n, res[static_cast<size_t>(i)])) bad[static_cast<size_t>(i)] = 1;
+      // a NULL text is only accepted as an empty one (length given as 0)
+      const char* s = texts[i];
+      const int64_t n = lengths ? lengths[i] : (s ? static_cast<int64_t>(std::strlen(s)) : -1);
+      if (n < 0 || (!s && n > 0)) {
+        bad[static_cast<size_t>(i)] = 2;
+        continue;
+      }
+      if (!encode(*t, s ? s : "", static_cast<size_t>(n), res[static_cast<size_t>(i)]))
+        bad[static_cast<size_t>(i)] = 1;
     }
   };
   std::vector<std::thread> th;
@@ -1017,6 +1024,8 @@ int ec_tokenize(int handle, const char* const* texts, const int64_t* lengths, in
   for (auto& x : th) x.join();
   offsets[0] = 0;
   for (int i = 0; i < ntexts; ++i) {
+    if (bad[static_cast<size_t>(i)] == 2)
+      return set_error(EC_EINVAL, "text %d: NULL pointer or negative length", i);
     if (bad[static_cast<size_t>(i)])
       return set_error(EC_EINVAL, "text %d: invalid UTF-8, or a piece with no id and no unknown token", i);
     offsets[i + 1] = offsets[i] + static_cast<int64_t>(res[static_cast<size_t>(i)].size());
@@ -1033,6 +1042,7 @@ int ec_tokenizer_decode(int handle, const int32_t* ids, int n, char* out, int64_
   clear_error();
   const Tokenizer* t = get(handle);
   if (!t) return set_error(EC_EINVAL, "no tokenizer %d", handle);
+  if (n < 0 || (n > 0 && !ids)) return set_error(EC_EINVAL, "bad decode arguments");
   std::string s;
   for (int i = 0; i < n; ++i)
     if (ids[i] >= 0 && ids[i] < static_cast<int>(t->inv.size())) s += t->inv[static_cast<size_t>(ids[i])];

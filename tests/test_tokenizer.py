@@ -138,6 +138,24 @@ def test_errors():
     rc = _lib.lib().ec_tokenize(tk.handle, good, None, 1, _lib.ptr(ids, C.c_int32), 4,
                                 _lib.ptr(offs, C.c_int64), 1)
     assert rc == _lib.EC_EINVAL and offs[1] > 4   # the count needed is reported
+    # a NULL text: an error unless its length is given as 0 (an empty text);
+    # a negative length: an error (neither is read)
+    two = (C.c_char_p * 2)(b"kato", None)
+    offs3 = np.zeros(3, np.int64)
+    rc = _lib.lib().ec_tokenize(tk.handle, two, None, 2, _lib.ptr(ids, C.c_int32), 16,
+                                _lib.ptr(offs3, C.c_int64), 1)
+    assert rc == _lib.EC_EINVAL and "text 1: NULL" in _lib.last_error()
+    for lens, want in (([4, 0], _lib.EC_OK), ([4, 3], _lib.EC_EINVAL), ([-1, 0], _lib.EC_EINVAL)):
+        la = np.array(lens, np.int64)
+        rc = _lib.lib().ec_tokenize(tk.handle, two, _lib.ptr(la, C.c_int64), 2,
+                                    _lib.ptr(ids, C.c_int32), 16, _lib.ptr(offs3, C.c_int64), 1)
+        assert rc == want, (lens, _lib.last_error())
+    # the empty text yields what encoding "" yields
+    assert offs3[2] - offs3[1] == len(tk.encode(""))
+    out = C.create_string_buffer(8)
+    n = C.c_int64()
+    assert _lib.lib().ec_tokenizer_decode(tk.handle, None, 3, out, 8, C.byref(n)) == _lib.EC_EINVAL
+    assert _lib.lib().ec_tokenizer_decode(tk.handle, None, -1, out, 8, C.byref(n)) == _lib.EC_EINVAL
     with pytest.raises(_lib.EcError):
         Tokenizer.from_json(_p("texts.json"))    # not a tokenizer.json
     tk.close()
