@@ -119,9 +119,13 @@ int ec_ann_read(const char* path, int* k, int* d, int64_t* n, float* centroids, 
   const unsigned char* b = static_cast<const unsigned char*>(m.p);
   if (m.n < 16 || get_u32(b) != kAnnMagic) return set_error(EC_EINVAL, "%s: not an ann.bin (magic)", path);
   const uint32_t kk = get_u32(b + 4), dd = get_u32(b + 8), nn = get_u32(b + 12);
+  // k x d is checked against the file before the total is formed, so a
+  // header with huge sizes cannot wrap the total around to the file's size
+  if (kk == 0 || dd == 0 || kk > 0x7fffffffu || dd > 0x7fffffffu ||
+      static_cast<uint64_t>(kk) * dd > m.n / 4)
+    return set_error(EC_EINVAL, "%s: %zu bytes, header says k %u x dim %u", path, m.n, kk, dd);
   const size_t need = 16 + (static_cast<size_t>(kk) * dd + kk + nn) * 4;
-  if (kk == 0 || dd == 0 || kk > 0x7fffffffu || dd > 0x7fffffffu || m.n != need)
-    return set_error(EC_EINVAL, "%s: %zu bytes, header says %zu", path, m.n, need);
+  if (m.n != need) return set_error(EC_EINVAL, "%s: %zu bytes, header says %zu", path, m.n, need);
   *k = static_cast<int>(kk);
   *d = static_cast<int>(dd);
   *n = nn;

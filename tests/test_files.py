@@ -4,6 +4,8 @@ kb.lisp:283-314) and index.bin (embed.lisp:47-57, kb.lisp:84-129).
 
 The host-only entry points (ec_ann_save / ec_ann_read) run on the CPU; the
 rest need a GPU and are marked."""
+import struct
+
 import numpy as np
 import pytest
 
@@ -53,6 +55,13 @@ def test_ann_file_errors(tmp_path):
     rc = _lib.lib().ec_ann_read(str(short).encode(), C.byref(k), C.byref(d), C.byref(nn),
                                 None, None, None)
     assert rc == _lib.EC_EINVAL
+    # k = d = 2^31 - 1 and n = 2^31 + 16: 16 + (k*d + k + n) * 4 wraps around
+    # 2^64 to exactly this file's 80 bytes; the header must still be refused
+    wrap = tmp_path / "w.bin"
+    wrap.write_bytes(struct.pack("<4I", 0x414E4E31, 0x7FFFFFFF, 0x7FFFFFFF, 0x80000010) + bytes(64))
+    rc = _lib.lib().ec_ann_read(str(wrap).encode(), C.byref(k), C.byref(d), C.byref(nn),
+                                None, None, None)
+    assert rc == _lib.EC_EINVAL and "header says k" in _lib.last_error()
     with pytest.raises(_lib.EcError):                 # counts do not sum to n
         ann.save_ann(tmp_path / "c.bin", cent, counts, lists, n + 1)
 
