@@ -10,6 +10,7 @@
 #pragma once
 
 #include <cstdint>
+#include <exception>
 #include <map>
 #include <memory>
 #include <string>
@@ -50,12 +51,19 @@ class JParser {
     } catch (const std::string& e) {
       err = e;
       return false;
+    } catch (const std::exception& e) {  // e.g. std::bad_alloc: no exception leaves the C ABI
+      err = std::string("json: ") + e.what();
+      return false;
     }
   }
 
  private:
+  // nesting limit: a deeper file is refused before the recursion can
+  // exhaust the calling thread's stack
+  static constexpr int kMaxDepth = 256;
   const std::string& s_;
   size_t p_ = 0;
+  int depth_ = 0;
 
   char peek() const { return p_ < s_.size() ? s_[p_] : '\0'; }
   char next() {
@@ -69,10 +77,13 @@ class JParser {
   void value(JVal& v) {
     ws();
     char c = peek();
-    if (c == '{') {
-      obj(v);
-    } else if (c == '[') {
-      arr(v);
+    if (c == '{' || c == '[') {
+      if (++depth_ > kMaxDepth) throw std::string("json: nested too deeply");
+      if (c == '{')
+        obj(v);
+      else
+        arr(v);
+      --depth_;
     } else if (c == '"') {
       v.kind = JVal::Str;
       str(v.s);
@@ -211,8 +222,21 @@ class JParser {
     std::string t = s_.substr(st, p_ - st);
     if (t.empty()) throw std::string("json: bad value");
     if (t.find_first_of(".eE") == std::string::npos) {
+      // an optional '-' and digits; a value outside int64 is an error
+      const bool neg = t[0] == '-';
+      size_t i = neg ? 1 : 0;
+      if (i == t.size()) throw std::string("json: bad number");
+      uint64_t mag = 0;
+      for (; i < t.size(); ++i) {
+        if (t[i] < '0' || t[i] > '9') throw std::string("json: bad number");
+        const uint64_t dg = static_cast<uint64_t>(t[i] - '0');
+        if (mag > (UINT64_MAX - dg) / 10) throw std::string("json: integer out of range");
+        mag = mag * 10 + dg;
+      }
+      const uint64_t lim = neg ? (uint64_t{1} << 63) : static_cast<uint64_t>(INT64_MAX);
+      if (mag > lim) throw std::string("json: integer out of range");
       v.kind = JVal::Int;
-      v.i = std::stoll(t);
+      v.i = neg ? static_cast<int64_t>(0 - mag) : static_cast<int64_t>(mag);
       return;
     }
     // json.lisp:85-113

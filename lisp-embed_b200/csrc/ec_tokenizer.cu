@@ -34,8 +34,11 @@
 #include <fstream>
 #include <memory>
 #include <mutex>
+#include <new>
 #include <sstream>
+#include <stdexcept>
 #include <string>
+#include <system_error>
 #include <thread>
 #include <unordered_map>
 #include <vector>
@@ -726,6 +729,8 @@ std::string trim_cr_space(const std::string& s) {
   return s.substr(a, b - a);
 }
 
+constexpr int kMaxVocabId = 1 << 24;
+
 void build_inv(Tokenizer& t) {
   int maxid = -1;
   for (auto& kv : t.vocab) maxid = std::max(maxid, kv.second);
@@ -738,6 +743,10 @@ int vocab_from(const JVal& v, Tokenizer& t, const char* what) {
   if (v.kind != JVal::Obj) return set_error(EC_EINVAL, "%s: vocab is not an object", what);
   for (const auto& kv : v.o) {
     if (kv.second.kind != JVal::Int) return set_error(EC_EINVAL, "%s: non-integer id", what);
+    // ids index the decode table: bounded well above any real vocabulary
+    if (kv.second.i < 0 || kv.second.i >= kMaxVocabId)
+      return set_error(EC_EINVAL, "%s: id %lld of %s outside [0, %d)", what,
+                       static_cast<long long>(kv.second.i), kv.first.c_str(), kMaxVocabId);
     t.vocab[kv.first] = static_cast<int>(kv.second.i);
   }
   build_inv(t);
@@ -867,27 +876,43 @@ int from_json(const char* path, Tokenizer& t) {
 }
 
 // ------------------------------------------------------------- registry --
+// Shared ownership: a call holds its tokenizer until it returns, so an
+// ec_tokenizer_free from another thread only drops the registry's share.
 std::mutex g_mu;
-std::vector<std::unique_ptr<Tokenizer>> g_tok;
+std::vector<std::shared_ptr<const Tokenizer>> g_tok;
 
 int add(std::unique_ptr<Tokenizer> t, int* handle) {
   if (t->kind == kBpe) t->build_bpe();
+  std::shared_ptr<const Tokenizer> s(std::move(t));
   std::lock_guard<std::mutex> lk(g_mu);
   for (size_t i = 0; i < g_tok.size(); ++i)
     if (!g_tok[i]) {
-      g_tok[i] = std::move(t);
+      g_tok[i] = std::move(s);
       *handle = static_cast<int>(i) + 1;
       return EC_OK;
     }
-  g_tok.push_back(std::move(t));
+  g_tok.push_back(std::move(s));
   *handle = static_cast<int>(g_tok.size());
   return EC_OK;
 }
 
-const Tokenizer* get(int handle) {
+std::shared_ptr<const Tokenizer> get(int handle) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (handle < 1 || handle > static_cast<int>(g_tok.size())) return nullptr;
-  return g_tok[static_cast<size_t>(handle) - 1].get();
+  return g_tok[static_cast<size_t>(handle) - 1];
+}
+
+// No C++ exception leaves the C ABI: allocation failures become EC_ENOMEM,
+// anything else from the standard library EC_EINVAL.
+template <class F>
+int guarded(const char* what, F&& f) {
+  try {
+    return f();
+  } catch (const std::bad_alloc&) {
+    return set_error(EC_ENOMEM, "%s: out of host memory", what);
+  } catch (const std::exception& e) {
+    return set_error(EC_EINVAL, "%s: %s", what, e.what());
+  }
 }
 
 }  // namespace
@@ -902,28 +927,32 @@ extern "C" {
 int ec_tokenizer_from_json(const char* path, int* handle) {
   clear_error();
   if (!path || !handle) return set_error(EC_EINVAL, "bad tokenizer arguments");
-  auto t = std::make_unique<Tokenizer>();
-  int rc = from_json(path, *t);
-  if (rc) return rc;
-  return add(std::move(t), handle);
+  return guarded(path, [&]() -> int {
+    auto t = std::make_unique<Tokenizer>();
+    int rc = from_json(path, *t);
+    if (rc) return rc;
+    return add(std::move(t), handle);
+  });
 }
 
 int ec_tokenizer_wordpiece(const char* vocab_txt, int lowercase, int* handle) {
   clear_error();
   if (!vocab_txt || !handle) return set_error(EC_EINVAL, "bad tokenizer arguments");
-  std::string text;
-  int rc = read_file(vocab_txt, text);
-  if (rc) return rc;
-  auto t = std::make_unique<Tokenizer>();
-  t->kind = kWordPiece;
-  t->lowercase = lowercase != 0;
-  for (const std::string& line : file_lines(text)) {
-    const std::string tokn = trim_cr_space(line);
-    t->vocab[tokn] = static_cast<int>(t->inv.size());
-    t->inv.push_back(tokn);
-  }
-  t->build_trie();
-  return add(std::move(t), handle);
+  return guarded(vocab_txt, [&]() -> int {
+    std::string text;
+    int rc = read_file(vocab_txt, text);
+    if (rc) return rc;
+    auto t = std::make_unique<Tokenizer>();
+    t->kind = kWordPiece;
+    t->lowercase = lowercase != 0;
+    for (const std::string& line : file_lines(text)) {
+      const std::string tokn = trim_cr_space(line);
+      t->vocab[tokn] = static_cast<int>(t->inv.size());
+      t->inv.push_back(tokn);
+    }
+    t->build_trie();
+    return add(std::move(t), handle);
+  });
 }
 
 int ec_tokenizer_bpe(const char* vocab_json, const char* merges_txt, int lowercase,
@@ -931,52 +960,56 @@ int ec_tokenizer_bpe(const char* vocab_json, const char* merges_txt, int lowerca
                      const char* unk_token, int bos_id, int eos_id, int* handle) {
   clear_error();
   if (!vocab_json || !merges_txt || !handle) return set_error(EC_EINVAL, "bad tokenizer arguments");
-  auto t = std::make_unique<Tokenizer>();
-  t->kind = kBpe;
-  JVal v;
-  int rc = parse_json(vocab_json, v);
-  if (rc) return rc;
-  if ((rc = vocab_from(v, *t, vocab_json))) return rc;
-  std::string text;
-  if ((rc = read_file(merges_txt, text))) return rc;
-  const std::vector<std::string> lines = file_lines(text);
-  int rank = 0;
-  for (size_t i = 1; i < lines.size(); ++i) {  // the first line is the version line
-    const std::string& l = lines[i];
-    if (l.empty() || l[0] == '#') continue;
-    const size_t sp = l.find(' ');
-    if (sp == std::string::npos) continue;
-    t->add_merge(l.substr(0, sp), l.substr(sp + 1), rank++);
-  }
-  t->lowercase = lowercase != 0;
-  t->byte_level = byte_level != 0;
-  t->llama3 = llama3 != 0;
-  if (cls_token) t->cls = cls_token;
-  if (sep_token) t->sep = sep_token;
-  if (unk_token) t->unk = unk_token;
-  t->bos = bos_id;
-  t->eos = eos_id;
-  return add(std::move(t), handle);
+  return guarded(vocab_json, [&]() -> int {
+    auto t = std::make_unique<Tokenizer>();
+    t->kind = kBpe;
+    JVal v;
+    int rc = parse_json(vocab_json, v);
+    if (rc) return rc;
+    if ((rc = vocab_from(v, *t, vocab_json))) return rc;
+    std::string text;
+    if ((rc = read_file(merges_txt, text))) return rc;
+    const std::vector<std::string> lines = file_lines(text);
+    int rank = 0;
+    for (size_t i = 1; i < lines.size(); ++i) {  // the first line is the version line
+      const std::string& l = lines[i];
+      if (l.empty() || l[0] == '#') continue;
+      const size_t sp = l.find(' ');
+      if (sp == std::string::npos) continue;
+      t->add_merge(l.substr(0, sp), l.substr(sp + 1), rank++);
+    }
+    t->lowercase = lowercase != 0;
+    t->byte_level = byte_level != 0;
+    t->llama3 = llama3 != 0;
+    if (cls_token) t->cls = cls_token;
+    if (sep_token) t->sep = sep_token;
+    if (unk_token) t->unk = unk_token;
+    t->bos = bos_id;
+    t->eos = eos_id;
+    return add(std::move(t), handle);
+  });
 }
 
 int ec_tokenizer_unigram(const char* scores_json, int lowercase, int* handle) {
   clear_error();
   if (!scores_json || !handle) return set_error(EC_EINVAL, "bad tokenizer arguments");
-  JVal v;
-  int rc = parse_json(scores_json, v);
-  if (rc) return rc;
-  if (v.kind != JVal::Obj) return set_error(EC_EINVAL, "%s: not an object", scores_json);
-  auto t = std::make_unique<Tokenizer>();
-  t->kind = kUnigram;
-  t->lowercase = lowercase != 0;
-  for (const std::string& k : v.keys) {
-    const JVal& sv = v.o.at(k);
-    if (!sv.is_num()) return set_error(EC_EINVAL, "%s: score of %s is not a number", scores_json, k.c_str());
-    t->vocab[k] = static_cast<int>(t->inv.size());
-    t->inv.push_back(k);
-    t->scores[k] = sv.num();
-  }
-  return add(std::move(t), handle);
+  return guarded(scores_json, [&]() -> int {
+    JVal v;
+    int rc = parse_json(scores_json, v);
+    if (rc) return rc;
+    if (v.kind != JVal::Obj) return set_error(EC_EINVAL, "%s: not an object", scores_json);
+    auto t = std::make_unique<Tokenizer>();
+    t->kind = kUnigram;
+    t->lowercase = lowercase != 0;
+    for (const std::string& k : v.keys) {
+      const JVal& sv = v.o.at(k);
+      if (!sv.is_num()) return set_error(EC_EINVAL, "%s: score of %s is not a number", scores_json, k.c_str());
+      t->vocab[k] = static_cast<int>(t->inv.size());
+      t->inv.push_back(k);
+      t->scores[k] = sv.num();
+    }
+    return add(std::move(t), handle);
+  });
 }
 
 int ec_tokenizer_free(int handle) {
@@ -990,7 +1023,7 @@ int ec_tokenizer_free(int handle) {
 
 int ec_tokenizer_vocab_size(int handle) {
   clear_error();
-  const Tokenizer* t = get(handle);
+  const auto t = get(handle);
   if (!t) return set_error(EC_EINVAL, "no tokenizer %d", handle);
   return static_cast<int>(t->inv.size());
 }
@@ -998,59 +1031,79 @@ int ec_tokenizer_vocab_size(int handle) {
 int ec_tokenize(int handle, const char* const* texts, const int64_t* lengths, int ntexts,
                 int32_t* ids, int64_t cap, int64_t* offsets, int nthreads) {
   clear_error();
-  const Tokenizer* t = get(handle);
+  const auto t = get(handle);
   if (!t) return set_error(EC_EINVAL, "no tokenizer %d", handle);
   if (ntexts < 0 || (ntexts > 0 && (!texts || !offsets))) return set_error(EC_EINVAL, "bad tokenize arguments");
-  std::vector<std::vector<int32_t>> res(static_cast<size_t>(ntexts));
-  std::vector<int> bad(static_cast<size_t>(std::max(ntexts, 1)), 0);
-  int nt = nthreads > 0 ? nthreads : static_cast<int>(std::thread::hardware_concurrency());
-  nt = std::max(1, std::min(nt, std::max(1, ntexts / 4)));
-  auto work = [&](int w) {
-    for (int i = w; i < ntexts; i += nt) {
-      // a NULL text is only accepted as an empty one (length given as 0)
-      const char* s = texts[i];
-      const int64_t n = lengths ? lengths[i] : (s ? static_cast<int64_t>(std::strlen(s)) : -1);
-      if (n < 0 || (!s && n > 0)) {
-        bad[static_cast<size_t>(i)] = 2;
-        continue;
+  return guarded("ec_tokenize", [&]() -> int {
+    std::vector<std::vector<int32_t>> res(static_cast<size_t>(ntexts));
+    std::vector<int> bad(static_cast<size_t>(std::max(ntexts, 1)), 0);
+    int nt = nthreads > 0 ? nthreads : static_cast<int>(std::thread::hardware_concurrency());
+    nt = std::max(1, std::min(nt, std::max(1, ntexts / 4)));
+    auto work = [&](int w) {
+      for (int i = w; i < ntexts; i += nt) {
+        // a NULL text is only accepted as an empty one (length given as 0)
+        const char* s = texts[i];
+        const int64_t n = lengths ? lengths[i] : (s ? static_cast<int64_t>(std::strlen(s)) : -1);
+        if (n < 0 || (!s && n > 0)) {
+          bad[static_cast<size_t>(i)] = 2;
+          continue;
+        }
+        try {  // an exception must not leave a worker thread
+          if (!encode(*t, s ? s : "", static_cast<size_t>(n), res[static_cast<size_t>(i)]))
+            bad[static_cast<size_t>(i)] = 1;
+        } catch (const std::exception&) {
+          bad[static_cast<size_t>(i)] = 3;
+        }
       }
-      if (!encode(*t, s ? s : "", static_cast<size_t>(n), res[static_cast<size_t>(i)]))
-        bad[static_cast<size_t>(i)] = 1;
+    };
+    // reserved up front, so that once a thread runs nothing here can throw
+    // before it is joined; a worker whose thread cannot start runs here
+    std::vector<std::thread> th;
+    std::vector<int> here;
+    th.reserve(static_cast<size_t>(nt));
+    here.reserve(static_cast<size_t>(nt));
+    for (int w = 1; w < nt; ++w) {
+      try {
+        th.emplace_back(work, w);
+      } catch (const std::system_error&) {
+        here.push_back(w);
+      }
     }
-  };
-  std::vector<std::thread> th;
-  for (int w = 1; w < nt; ++w) th.emplace_back(work, w);
-  work(0);
-  for (auto& x : th) x.join();
-  offsets[0] = 0;
-  for (int i = 0; i < ntexts; ++i) {
-    if (bad[static_cast<size_t>(i)] == 2)
-      return set_error(EC_EINVAL, "text %d: NULL pointer or negative length", i);
-    if (bad[static_cast<size_t>(i)])
-      return set_error(EC_EINVAL, "text %d: invalid UTF-8, or a piece with no id and no unknown token", i);
-    offsets[i + 1] = offsets[i] + static_cast<int64_t>(res[static_cast<size_t>(i)].size());
-  }
-  if (offsets[ntexts] > cap || (offsets[ntexts] > 0 && !ids))
-    return set_error(EC_EINVAL, "%lld ids do not fit the buffer of %lld", static_cast<long long>(offsets[ntexts]),
-                     static_cast<long long>(cap));
-  for (int i = 0; i < ntexts; ++i)
-    std::memcpy(ids + offsets[i], res[static_cast<size_t>(i)].data(), res[static_cast<size_t>(i)].size() * 4);
-  return EC_OK;
+    work(0);
+    for (int w : here) work(w);
+    for (auto& x : th) x.join();
+    offsets[0] = 0;
+    for (int i = 0; i < ntexts; ++i) {
+      const int b = bad[static_cast<size_t>(i)];
+      if (b == 2) return set_error(EC_EINVAL, "text %d: NULL pointer or negative length", i);
+      if (b == 3) return set_error(EC_ENOMEM, "text %d: out of host memory", i);
+      if (b) return set_error(EC_EINVAL, "text %d: invalid UTF-8, or a piece with no id and no unknown token", i);
+      offsets[i + 1] = offsets[i] + static_cast<int64_t>(res[static_cast<size_t>(i)].size());
+    }
+    if (offsets[ntexts] > cap || (offsets[ntexts] > 0 && !ids))
+      return set_error(EC_EINVAL, "%lld ids do not fit the buffer of %lld", static_cast<long long>(offsets[ntexts]),
+                       static_cast<long long>(cap));
+    for (int i = 0; i < ntexts; ++i)
+      std::memcpy(ids + offsets[i], res[static_cast<size_t>(i)].data(), res[static_cast<size_t>(i)].size() * 4);
+    return EC_OK;
+  });
 }
 
 int ec_tokenizer_decode(int handle, const int32_t* ids, int n, char* out, int64_t cap, int64_t* len) {
   clear_error();
-  const Tokenizer* t = get(handle);
+  const auto t = get(handle);
   if (!t) return set_error(EC_EINVAL, "no tokenizer %d", handle);
   if (n < 0 || (n > 0 && !ids)) return set_error(EC_EINVAL, "bad decode arguments");
-  std::string s;
-  for (int i = 0; i < n; ++i)
-    if (ids[i] >= 0 && ids[i] < static_cast<int>(t->inv.size())) s += t->inv[static_cast<size_t>(ids[i])];
-  if (len) *len = static_cast<int64_t>(s.size());
-  if (static_cast<int64_t>(s.size()) > cap || (!out && !s.empty()))
-    return set_error(EC_EINVAL, "%zu bytes do not fit the buffer of %lld", s.size(), static_cast<long long>(cap));
-  if (!s.empty()) std::memcpy(out, s.data(), s.size());
-  return EC_OK;
+  return guarded("ec_tokenizer_decode", [&]() -> int {
+    std::string s;
+    for (int i = 0; i < n; ++i)
+      if (ids[i] >= 0 && ids[i] < static_cast<int>(t->inv.size())) s += t->inv[static_cast<size_t>(ids[i])];
+    if (len) *len = static_cast<int64_t>(s.size());
+    if (static_cast<int64_t>(s.size()) > cap || (!out && !s.empty()))
+      return set_error(EC_EINVAL, "%zu bytes do not fit the buffer of %lld", s.size(), static_cast<long long>(cap));
+    if (!s.empty()) std::memcpy(out, s.data(), s.size());
+    return EC_OK;
+  });
 }
 
 }  // extern "C"

@@ -164,6 +164,39 @@ def test_errors():
         tk.vocab_size()
 
 
+def test_malformed_files_are_refused(tmp_path):
+    """Damaged tokenizer files end in EC_EINVAL with a message, never in an
+    exception through the C ABI: an integer that is only a sign or does not
+    fit int64, nesting deeper than the reader's limit, a vocabulary id
+    outside [0, 2^24) (ids index the decode table)."""
+    import ctypes as C
+
+    def load(text, kind="json"):
+        p = tmp_path / "t.json"
+        p.write_text(text)
+        h = C.c_int()
+        if kind == "json":
+            return _lib.lib().ec_tokenizer_from_json(str(p).encode(), C.byref(h)), h.value
+        return _lib.lib().ec_tokenizer_unigram(str(p).encode(), 0, C.byref(h)), h.value
+
+    wp = '{"model": {"type": "WordPiece", "unk_token": "a", "vocab": {"a": 0, "b": %s}}}'
+    for bad, msg in (("-", "bad number"), ("+1", "bad number"),
+                     ("9223372036854775808", "out of range"), ("99999999999999999999", "out of range"),
+                     ("-1", "outside"), ("16777216", "outside"), ("2147483647", "outside")):
+        rc, _ = load(wp % bad)
+        assert rc == _lib.EC_EINVAL and msg in _lib.last_error(), (bad, _lib.last_error())
+    rc, _ = load("[" * 100000)
+    assert rc == _lib.EC_EINVAL and "nested too deeply" in _lib.last_error()
+    rc, _ = load('{"a": -}', "unigram")
+    assert rc == _lib.EC_EINVAL and "bad number" in _lib.last_error()
+    # the edges that are valid still load
+    rc, h = load(wp % "151668")
+    assert rc == _lib.EC_OK and _lib.lib().ec_tokenizer_vocab_size(h) == 151669
+    assert _lib.lib().ec_tokenizer_free(h) == _lib.EC_OK
+    rc, h = load('{"a": -9223372036854775808, "b": 9223372036854775807}', "unigram")
+    assert rc == _lib.EC_OK and _lib.lib().ec_tokenizer_free(h) == _lib.EC_OK
+
+
 def test_random_texts_match_restatement(texts):
     """Seeded random texts -- ASCII, whitespace runs and Unicode spaces,
     controls, accents, case pairs with special lowering (dotted I, title-case
