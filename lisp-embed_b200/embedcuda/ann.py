@@ -19,6 +19,20 @@ from . import _lib
 MAGIC = 0x414E4E31  # "ANN1"
 
 
+def _init_rows(init, k, d):
+    """The library reads k x dim initial centroids."""
+    init = np.ascontiguousarray(init, np.float32)
+    if init.shape != (k, d):
+        raise ValueError(f"init of shape {init.shape}, need ({k}, {d})")
+    return init
+
+
+def _check_centroids(centroids, d):
+    """The library reads k x dim centroids, dim taken from the vectors."""
+    if centroids.ndim != 2 or centroids.shape[1] != d:
+        raise ValueError(f"centroids of shape {centroids.shape}, need (k, {d})")
+
+
 def kmeans(vecs, sample, k, iters, init=None):
     """Train k centroids on vecs[sample] (float32[k, dim])."""
     vecs = np.ascontiguousarray(vecs, np.float32)
@@ -27,7 +41,7 @@ def kmeans(vecs, sample, k, iters, init=None):
     cent = np.empty((k, d), np.float32)
     init_p = None
     if init is not None:
-        init = np.ascontiguousarray(init, np.float32)
+        init = _init_rows(init, k, d)
         init_p = _lib.ptr(init, C.c_float)
     _lib.check(_lib.lib().ec_kmeans(_lib.ptr(vecs, C.c_float), n, d, _lib.ptr(sample, C.c_int64),
                                     sample.size, k, iters, init_p, _lib.ptr(cent, C.c_float)),
@@ -40,6 +54,7 @@ def assign(vecs, centroids, rows=None):
     vecs = np.ascontiguousarray(vecs, np.float32)
     centroids = np.ascontiguousarray(centroids, np.float32)
     n, d = vecs.shape
+    _check_centroids(centroids, d)
     k = centroids.shape[0]
     rp = None
     m = n
@@ -59,6 +74,7 @@ def assign_all(vecs, centroids):
     vecs = np.ascontiguousarray(vecs, np.float32)
     centroids = np.ascontiguousarray(centroids, np.float32)
     n, d = vecs.shape
+    _check_centroids(centroids, d)
     k = centroids.shape[0]
     counts = np.empty(k, np.uint32)
     lists = np.empty(n, np.uint32)
@@ -81,7 +97,7 @@ def build(vecs, sample, k, iters, init=None):
     lists = np.empty(n, np.uint32)
     init_p = None
     if init is not None:
-        init = np.ascontiguousarray(init, np.float32)
+        init = _init_rows(init, k, d)
         init_p = _lib.ptr(init, C.c_float)
     _lib.check(_lib.lib().ec_ann_build(_lib.ptr(vecs, C.c_float), n, d, _lib.ptr(sample, C.c_int64),
                                        sample.size, k, iters, init_p, _lib.ptr(cent, C.c_float),

@@ -19,9 +19,17 @@ _state = {"ivf": False, "dim": 0}
 
 def load_index(vectors, ann=None):
     """vectors float32[n, dim]; ann = (centroids, counts, lists) or None."""
-    _lib.init()
     x = np.ascontiguousarray(vectors, np.float32)
+    if x.ndim != 2:
+        raise ValueError("vectors must be float32[n, dim]")
     n, d = x.shape
+    if ann is not None:
+        # the library reads k x dim centroids, k counts and n list entries
+        c, cnt, lst = ann
+        c, cnt, lst = np.asarray(c), np.asarray(cnt), np.asarray(lst)
+        if c.ndim != 2 or c.shape[1] != d or cnt.size != c.shape[0] or lst.size != n:
+            raise ValueError(f"ann must be (centroids[k, {d}], counts[k], lists[{n}])")
+    _lib.init()
     if ann is None:
         _lib.check(_lib.lib().ec_index_load(_lib.ptr(x, C.c_float), n, d, None, 0, None, None),
                    "index_load")
@@ -50,8 +58,17 @@ def load_index_files(index_path, dim, ann_path=None):
     return n.value
 
 
-def search_ivf(q, k, nprobe=None):
+def _queries(q):
+    """float32[nq, dim] queries of the loaded index's width (the library
+    reads nq x dim floats and cannot see the array's own width)."""
     q = np.ascontiguousarray(np.atleast_2d(q), np.float32)
+    if q.ndim != 2 or (_state["dim"] and q.shape[1] != _state["dim"]):
+        raise ValueError(f"queries of shape {q.shape}, the index has dim {_state['dim']}")
+    return q
+
+
+def search_ivf(q, k, nprobe=None):
+    q = _queries(q)
     nq = q.shape[0]
     ids = np.empty((nq, k), np.int64)
     sc = np.empty((nq, k), np.float32)
@@ -62,7 +79,7 @@ def search_ivf(q, k, nprobe=None):
 
 
 def search_brute(q, k):
-    q = np.ascontiguousarray(np.atleast_2d(q), np.float32)
+    q = _queries(q)
     nq = q.shape[0]
     ids = np.empty((nq, k), np.int64)
     sc = np.empty((nq, k), np.float32)

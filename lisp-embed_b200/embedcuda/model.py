@@ -56,10 +56,21 @@ def embed_batch(ids, offsets, out=None):
     Returns float32[nseq, dim], L2-normalised, in input order."""
     ids = np.ascontiguousarray(ids, np.int32)
     offsets = np.ascontiguousarray(offsets, np.int64)
+    # the library reads ids[offsets[0] .. offsets[nseq]) and cannot see the
+    # length of ids, nor of out
+    if offsets.ndim != 1 or offsets.size < 1:
+        raise ValueError("offsets must be int64[nseq + 1]")
+    if offsets.size > 1 and (offsets[0] < 0 or offsets[-1] > ids.size or
+                             bool(np.any(offsets[1:] < offsets[:-1]))):
+        raise ValueError(f"offsets must be non-decreasing within [0, {ids.size}]")
     nseq = offsets.size - 1
     D = dim()
     if out is None:
         out = np.empty((nseq, D), np.float32)
+    elif (not isinstance(out, np.ndarray) or out.dtype != np.float32 or out.ndim != 2 or
+          not out.flags.c_contiguous or not out.flags.writeable or out.shape[0] < nseq or
+          out.shape[1] < D):
+        raise ValueError(f"out must be a writeable C-contiguous float32[>= {nseq}, >= {D}] array")
     _lib.check(_lib.lib().ec_embed_batch(_lib.ptr(ids, C.c_int32), _lib.ptr(offsets, C.c_int64),
                                          nseq, _lib.ptr(out, C.c_float), out.shape[1]),
                "embed_batch")

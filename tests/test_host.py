@@ -163,3 +163,45 @@ def test_bench_reference_config_matches_ours():
         a = bench.workload_config("minilm", world, int(offs[-1]))
         assert a["workload"] == "minilm-l6" and a["parallelism"] == f"dp{world} (sequence shards)"
         assert a["tokens_per_rank"] == int(offs[-1])
+
+
+def test_mirror_refuses_arrays_the_library_would_misread(monkeypatch):
+    """The C calls take raw pointers and counts, so the host mirror checks the
+    shapes it knows before any call: query width against the loaded index,
+    initial centroids against k x dim, centroid width, the ann arrays'
+    lengths, packed offsets within ids, and a caller's output buffer.  Each
+    case raises before the library is reached (no GPU needed)."""
+    import pytest
+    from embedcuda import kb, model
+
+    monkeypatch.setitem(kb._state, "dim", 8)
+    with pytest.raises(ValueError, match="index has dim 8"):
+        kb.search_brute(np.zeros((2, 7), np.float32), 3)
+    with pytest.raises(ValueError, match="index has dim 8"):
+        kb.search_ivf(np.zeros((2, 3, 8), np.float32), 3)
+    x = np.zeros((10, 8), np.float32)
+    with pytest.raises(ValueError, match="ann must be"):
+        kb.load_index(x, (np.zeros((4, 7), np.float32), np.zeros(4, np.uint32), np.zeros(10, np.uint32)))
+    with pytest.raises(ValueError, match="ann must be"):
+        kb.load_index(x, (np.zeros((4, 8), np.float32), np.zeros(3, np.uint32), np.zeros(10, np.uint32)))
+    with pytest.raises(ValueError, match="ann must be"):
+        kb.load_index(x, (np.zeros((4, 8), np.float32), np.zeros(4, np.uint32), np.zeros(9, np.uint32)))
+    sample = np.arange(10, dtype=np.int64)
+    with pytest.raises(ValueError, match=r"need \(4, 8\)"):
+        ann.kmeans(x, sample, 4, 1, init=np.zeros((3, 8), np.float32))
+    with pytest.raises(ValueError, match=r"need \(4, 8\)"):
+        ann.build(x, sample, 4, 1, init=np.zeros(32, np.float32))
+    with pytest.raises(ValueError, match=r"need \(k, 8\)"):
+        ann.assign(x, np.zeros((4, 16), np.float32))
+    with pytest.raises(ValueError, match=r"need \(k, 8\)"):
+        ann.assign_all(x, np.zeros(32, np.float32))
+    ids = np.arange(20, dtype=np.int32)
+    for offs in ([0, 5, 21], [0, 9, 5], [-1, 5], []):
+        with pytest.raises(ValueError, match="offsets"):
+            model.embed_batch(ids, np.array(offs, np.int64))
+    monkeypatch.setattr(model, "dim", lambda: 384)
+    offs = np.array([0, 5, 20], np.int64)
+    for out in (np.zeros((2, 384), np.float64), np.zeros((1, 384), np.float32),
+                np.zeros((2, 383), np.float32), np.zeros((384, 2), np.float32).T):
+        with pytest.raises(ValueError, match="out must be"):
+            model.embed_batch(ids, offs, out=out)
