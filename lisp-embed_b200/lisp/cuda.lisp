@@ -36,6 +36,7 @@
 (defvar *loaded* nil)
 (defvar *dim* 0)
 (defvar *ivf* nil)
+(defvar *index-dim* 0)   ; dimension of the resident index (0: none loaded)
 
 (defun available-p () *loaded*)
 
@@ -233,7 +234,8 @@ training row indices; its first K rows initialise the centroids."
   (let ((k (if centroids (floor (length centroids) dim) 0)))
     (with-saps ((xp vecs) (cp centroids) (np counts) (lp lists))
       (check (%index-load xp n dim cp k np lp) "ec_index_load"))
-    (setf *ivf* (plusp k))))
+    (setf *index-dim* dim
+          *ivf* (plusp k))))
 
 (defun index-load-files (index-path &key ann-path (dim 384))
   "kb::load-index's vectors + kb::load-ann straight from index.bin / ann.bin
@@ -243,7 +245,8 @@ into device memory (no Lisp array of the vectors).  Returns n."
       (check (%index-load-files (namestring index-path) dim
                                 (and ann-path (namestring ann-path)) np)
              "ec_index_load_files"))
-    (setf *ivf* (and ann-path t))
+    (setf *index-dim* dim
+          *ivf* (and ann-path t))
     (aref n 0)))
 
 (defun ann-build-file (index-path ann-path sample k iters &key (dim 384))
@@ -295,7 +298,13 @@ forward (model:embed for a list of texts, in input order)."
     (embed-batch (loop for i below n
                        collect (subseq ids (aref offs i) (aref offs (1+ i)))))))
 
+(defun check-query (q)
+  "The library reads *INDEX-DIM* floats per query and cannot see Q's length."
+  (unless (= (length q) *index-dim*)
+    (error "query of length ~D, the resident index has dim ~D" (length q) *index-dim*)))
+
 (defun %search (q k ivf)
+  (check-query q)
   (let ((ids (make-array k :element-type '(signed-byte 64)))
         (sc (make-array k :element-type 'single-float))
         (qv (coerce q '(simple-array single-float (*)))))
@@ -318,8 +327,9 @@ forward (model:embed for a list of texts, in input order)."
   "kb::top-k for a list of query vectors in one call (the library regroups a
 large batch by probed list): a list with one (row . score) list per query,
 each as top-k would return it."
+  (mapc #'check-query queries)
   (let* ((nq (length queries))
-         (d (if queries (length (first queries)) 0))
+         (d *index-dim*)
          (qv (make-array (* nq d) :element-type 'single-float))
          (ids (make-array (* nq k) :element-type '(signed-byte 64)))
          (sc (make-array (* nq k) :element-type 'single-float)))
