@@ -205,3 +205,21 @@ def test_mirror_refuses_arrays_the_library_would_misread(monkeypatch):
                 np.zeros((2, 383), np.float32), np.zeros((384, 2), np.float32).T):
         with pytest.raises(ValueError, match="out must be"):
             model.embed_batch(ids, offs, out=out)
+
+
+def test_model_configs_parse_with_the_library_json_reader(tmp_path):
+    """config.json of every model shape goes through the library's one JSON
+    reader (ec_json.h), shared with the tokenizer loader: loading it as a
+    tokenizer.json must fail only for the missing "model" key, after a clean
+    parse (integers, floats such as 1e-12, nested objects, null)."""
+    import ctypes as C
+    from embedcuda import _lib
+    for name in ("MINILM", "BERT_BASE", "MPNET_BASE", "QWEN3_06B", "GEMMA_EMB"):
+        cfg = synth.config_json(getattr(synth, name))
+        cfg["rope_scaling"] = None
+        cfg["eos_token_id"] = [1, -2, 9223372036854775807]
+        p = tmp_path / f"{name}.json"
+        p.write_text(json.dumps(cfg, indent=1))
+        h = C.c_int()
+        rc = _lib.lib().ec_tokenizer_from_json(str(p).encode(), C.byref(h))
+        assert rc == _lib.EC_EINVAL and _lib.last_error().endswith("no model"), (name, _lib.last_error())
