@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <chrono>
 #include <condition_variable>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -473,6 +474,8 @@ int ec_upload_tensor(const char* name, int dtype, const int64_t* shape, int ndim
   std::vector<int64_t> sh(shape, shape + ndim);
   for (int64_t v : sh) {
     if (v < 0) return set_error(EC_EINVAL, "tensor %s: negative dimension", name);
+    if (v && numel > SIZE_MAX / 4 / static_cast<size_t>(v))
+      return set_error(EC_EINVAL, "tensor %s: shape too large", name);
     numel *= static_cast<size_t>(v);
   }
   size_t esz;
