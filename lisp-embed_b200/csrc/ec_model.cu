@@ -1179,6 +1179,8 @@ int embed_on_device(Device& d, const int32_t* ids_host, const int32_t* ids_dev,
   const int maxlen = m.family == EC_FAMILY_LLAMA ? m.max_pos : m.max_pos - m.pos_offset;
   for (int s : seqs) {
     const int64_t L = offsets[s + 1] - offsets[s];
+    if (offsets[s] < 0)  // before the start of the ids (host or device)
+      return set_error(EC_EINVAL, "sequence %d starts at offset %lld", s, static_cast<long long>(offsets[s]));
     if (L <= 0) return set_error(EC_EINVAL, "sequence %d is empty", s);
     if (L > maxlen)
       return set_error(EC_EINVAL, "sequence %d has %lld tokens, above the %d positions of the model",

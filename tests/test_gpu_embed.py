@@ -241,6 +241,15 @@ def test_errors(synth_root, ec):
         model.embed(np.arange(600, dtype=np.int32) + 1000)  # past 512 positions
     with pytest.raises(_lib.EcError):
         model.embed_batch(np.zeros(0, np.int32), np.array([0, 0], np.int64))  # empty sequence
+    # a sequence that starts before the ids is refused before any id is read
+    # (raw call: the host mirror refuses it itself)
+    import ctypes as C
+    ids = np.arange(10, dtype=np.int32) + 1000
+    offs = np.array([-2, 5], np.int64)
+    out = np.zeros((1, model.dim()), np.float32)
+    rc = _lib.lib().ec_embed_batch(_lib.ptr(ids, C.c_int32), _lib.ptr(offs, C.c_int64), 1,
+                                   _lib.ptr(out, C.c_float), out.shape[1])
+    assert rc == _lib.EC_EINVAL and "starts at offset" in _lib.last_error()
 
 
 @pytest.mark.parametrize("unfused", [0, 1, 2])
