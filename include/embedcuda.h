@@ -84,7 +84,10 @@ int ec_dim(void);
  * (model.lisp:48-54) -> bert::embed-bert (bert.lisp:275-320),
  * bert::embed-mpnet (:455-499), llama:embed (llama.lisp:296-344) and
  * gemma:embed (gemma.lisp:306-380) for a whole batch, the way embed:run
- * batches chunks (embed.lisp:88-105). */
+ * batches chunks (embed.lisp:88-105).  offsets must ascend from >= 0, every
+ * sequence hold 1 .. the model's positions ids, every id lie in the
+ * vocabulary; otherwise EC_EINVAL before anything is computed.  The library
+ * cannot see the length of ids: offsets[nseq] must not pass it. */
 int ec_embed_batch(const int32_t *ids, const int64_t *offsets, int nseq, float *out,
                    int out_stride);
 
